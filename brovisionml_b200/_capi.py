@@ -1,0 +1,72 @@
+"""ctypes binding of libbvml_dsine.so (the C ABI in include/bvml_dsine.h).
+
+The library must have been built in-tree (``python -m brovisionml_b200.build``
+or ``__graft_entry__.build()``); a missing library is an ImportError, never a
+silent fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libbvml_dsine.so")
+
+BVML_F32 = 0
+BVML_F16 = 1
+BVML_OK = 0
+
+# Every symbol include/bvml_dsine.h declares (checked by the CPU test suite).
+EXPORTS = ("bvml_last_error", "bvml_abi_version", "bvml_ray_relu", "bvml_angmf_propagate",
+           "bvml_convex_upsample", "bvml_l2_normalize_nchw", "bvml_slice2d",
+           "bvml_refine_workspace_bytes", "bvml_refine", "bvml_probe_events")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(
+        f"brovisionml_b200: CUDA library not built ({LIB_PATH} missing); run "
+        "`python -m brovisionml_b200.build` (nvcc for sm_100a)")
+
+lib = ctypes.CDLL(LIB_PATH)
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_d = ctypes.c_double
+_sz = ctypes.c_size_t
+
+lib.bvml_last_error.restype = ctypes.c_char_p
+lib.bvml_last_error.argtypes = []
+lib.bvml_abi_version.restype = _i
+lib.bvml_abi_version.argtypes = []
+lib.bvml_ray_relu.restype = _i
+lib.bvml_ray_relu.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp]
+lib.bvml_angmf_propagate.restype = _i
+lib.bvml_angmf_propagate.argtypes = [_vp, _vp, _vp, _vp, _vp, _d, _d, _d, _d, _i, _i, _i, _i, _i,
+                                     _i, _vp, _vp]
+lib.bvml_convex_upsample.restype = _i
+lib.bvml_convex_upsample.argtypes = [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp]
+lib.bvml_l2_normalize_nchw.restype = _i
+lib.bvml_l2_normalize_nchw.argtypes = [_vp, _i, _i, _i, _i, ctypes.c_float, _i, _vp, _vp]
+lib.bvml_slice2d.restype = _i
+lib.bvml_slice2d.argtypes = [_vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp]
+lib.bvml_refine_workspace_bytes.restype = _sz
+lib.bvml_refine_workspace_bytes.argtypes = [_i, _i, _i]
+lib.bvml_refine.restype = _i
+lib.bvml_refine.argtypes = ([_vp, _vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
+                             ctypes.POINTER(_vp), _i, _vp] + [_i] * 5 + [_d] * 4 + [_i] * 6
+                            + [_vp, _sz, _vp, _vp])
+lib.bvml_probe_events.restype = _i
+lib.bvml_probe_events.argtypes = [ctypes.POINTER(_vp), _i]
+
+
+def abi_version() -> int:
+    return int(lib.bvml_abi_version())
+
+
+def loaded_library() -> str:
+    return LIB_PATH
+
+
+def check(rc: int) -> None:
+    if rc != BVML_OK:
+        msg = lib.bvml_last_error().decode("utf-8", "replace")
+        raise RuntimeError(msg or f"dsine ops: failed with status {rc}")

@@ -1,0 +1,77 @@
+// Shared device helpers for the DSINE refine-ops kernels (sm_100a only).
+//
+// Pixel pairs: the hot kernels give every thread two horizontally adjacent
+// pixels and carry their arithmetic in float2, issued as Blackwell's packed
+// f32x2 instructions (__ffma2_rn / __fadd2_rn / __fmul2_rn): one issue slot
+// does the work of two, which matters because these kernels sit close to the
+// issue-rate ridge.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "brovisionml_b200 kernels are written for sm_100a (B200) only"
+#endif
+
+namespace bvml {
+
+// ------------------------------------------------------------------ float2 ops
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+// a * b + c
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+// c - a * b
+__device__ __forceinline__ float2 fnma2(float2 a, float2 b, float2 c) {
+    return __ffma2_rn(make_float2(-a.x, -a.y), b, c);
+}
+__device__ __forceinline__ float2 max2(float2 a, float2 b) {
+    return make_float2(fmaxf(a.x, b.x), fmaxf(a.y, b.y));
+}
+__device__ __forceinline__ float2 rsqrt2(float2 a) { return make_float2(rsqrtf(a.x), rsqrtf(a.y)); }
+__device__ __forceinline__ float2 ex2_2(float2 a) { return make_float2(exp2f(a.x), exp2f(a.y)); }
+
+// -------------------------------------------------------------- storage types
+template <typename T> struct St;
+template <> struct St<float> {
+    __device__ __forceinline__ static float ld(const float* p) { return __ldg(p); }
+    // Two consecutive elements; p must be 8-byte aligned.
+    __device__ __forceinline__ static float2 ld2(const float* p) {
+        return __ldg(reinterpret_cast<const float2*>(p));
+    }
+    // Streaming (read-once) variant: evict-first in L1/L2.
+    __device__ __forceinline__ static float2 ld2s(const float* p) {
+        return __ldcs(reinterpret_cast<const float2*>(p));
+    }
+    __device__ __forceinline__ static float lds1(const float* p) { return __ldcs(p); }
+    __device__ __forceinline__ static void st(float* p, float v) { *p = v; }
+    __device__ __forceinline__ static void st2(float* p, float2 v) {
+        *reinterpret_cast<float2*>(p) = v;
+    }
+};
+template <> struct St<__half> {
+    __device__ __forceinline__ static float ld(const __half* p) { return __half2float(__ldg(p)); }
+    __device__ __forceinline__ static float2 ld2(const __half* p) {
+        return __half22float2(__ldg(reinterpret_cast<const __half2*>(p)));
+    }
+    __device__ __forceinline__ static float2 ld2s(const __half* p) {
+        return __half22float2(__ldcs(reinterpret_cast<const __half2*>(p)));
+    }
+    __device__ __forceinline__ static float lds1(const __half* p) {
+        return __half2float(__ldcs(p));
+    }
+    __device__ __forceinline__ static void st(__half* p, float v) { *p = __float2half_rn(v); }
+    __device__ __forceinline__ static void st2(__half* p, float2 v) {
+        *reinterpret_cast<__half2*>(p) = __float22half2_rn(v);
+    }
+};
+
+__device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+// RayReLU eps: the CPU twin's float constant 1e-2f (src/dsine_ops.cpp:27).
+constexpr float kRayEps = 1e-2f;
+
+}  // namespace bvml

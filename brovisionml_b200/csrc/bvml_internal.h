@@ -1,0 +1,47 @@
+// Internal launcher interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace bvml {
+
+enum class SType { F32 = 0, F16 = 1 };
+
+struct AngmfLaunch {
+    const void* pn;      // source normals (B,3,H,W); type pn_t
+    const void* prob;    // (B,P,H,W) storage type st
+    const void* xy;      // (B,2P,H,W)
+    const void* angle;   // (B,P,H,W)
+    const float* ray;    // (3,H,W)
+    void* out;           // (B,3,H,W); type out_t
+    SType st, pn_t, out_t;
+    bool fuse_ray_relu;  // apply RayReLU to the source normals while staging them
+    int B, H, W, ps, dil;
+    double fu, cu, fv, cv;
+};
+cudaError_t launch_angmf(const AngmfLaunch& L, cudaStream_t s);
+
+struct UpsampleLaunch {
+    const void* n;       // (B,3,h,w); type n_t
+    const void* mask;    // (B,576,h,w) storage type st
+    void* out;           // (B,3,out_h,out_w) storage type st
+    SType st, n_t;
+    bool normalize;      // channel L2-normalise (eps 1e-12) after the combine
+    bool ray_relu;       // full-resolution RayReLU after the normalise
+    int B, h, w;
+    int crop_t, crop_l, out_h, out_w;
+    double fu, cu, fv, cv;  // GRID intrinsics; the full-res ray uses 8x these
+};
+cudaError_t launch_upsample(const UpsampleLaunch& L, cudaStream_t s);
+
+cudaError_t launch_ray_relu(void* normal, SType t, const float* ray, int B, int H, int W,
+                            cudaStream_t s);
+cudaError_t launch_build_ray(float* ray, int H, int W, double fu, double cu, double fv,
+                             double cv, cudaStream_t s);
+cudaError_t launch_l2_normalize(const void* x, void* y, SType t, int N, int C, int H, int W,
+                                float eps, cudaStream_t s);
+cudaError_t launch_slice2d(const void* x, void* y, SType t, int N, int C, int H, int W, int h0,
+                           int w0, int Ho, int Wo, cudaStream_t s);
+
+}  // namespace bvml

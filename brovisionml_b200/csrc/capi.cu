@@ -1,0 +1,294 @@
+// extern "C" entry points of libbvml_dsine.so (declared in include/bvml_dsine.h).
+//
+// Argument checking and error reporting mirror the reference: argument
+// problems read "dsine ops: ..." (src/dsine_ops.cpp:18-22) and CUDA failures
+// "dsine cuda: <what>: <cudaGetErrorString>" (src/dsine_ops.cu:25-29), but
+// they are returned as status codes with the text in bvml_last_error(), since
+// no exception may cross a C ABI.
+#include "bvml_dsine.h"
+#include "bvml_internal.h"
+
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+namespace {
+
+thread_local std::string g_last_error;
+thread_local std::vector<cudaEvent_t> g_probe;
+
+cudaError_t probe(size_t k, cudaStream_t s) {
+    return k < g_probe.size() ? cudaEventRecord(g_probe[k], s) : cudaSuccess;
+}
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+int einval(const std::string& msg) { return fail(BVML_EINVAL, "dsine ops: " + msg); }
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(BVML_ECUDA, std::string("dsine cuda: ") + what + ": " + cudaGetErrorString(e));
+}
+int finish(cudaError_t e, const char* what) {
+    if (e == cudaErrorInvalidValue)
+        return fail(BVML_EUNSUPPORTED, std::string("dsine ops: ") + what +
+                                           ": unsupported type / option combination");
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    g_last_error.clear();
+    return BVML_OK;
+}
+
+bool dtype_ok(int dtype) { return dtype == BVML_F32 || dtype == BVML_F16; }
+bvml::SType st_of(int dtype) { return dtype == BVML_F16 ? bvml::SType::F16 : bvml::SType::F32; }
+bool window_ok(int ps, int dil) { return (ps == 3 || ps == 5 || ps == 7) && dil >= 1 && dil <= 4; }
+bool dims_ok(int B, int H, int W) {
+    if (B < 0 || H < 0 || W < 0) return false;
+    // every per-frame plane offset must fit the kernels' index arithmetic
+    return (int64_t)H * W * 2 * 49 < (int64_t)INT32_MAX;
+}
+bool intr_ok(double fu, double fv) { return fu != 0.0 && fv != 0.0 && fu == fu && fv == fv; }
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+}  // namespace
+
+extern "C" {
+
+const char* bvml_last_error(void) { return g_last_error.c_str(); }
+
+int bvml_abi_version(void) { return BVML_ABI_VERSION; }
+
+int bvml_probe_events(void* const* events, int n) {
+    if (n < 0 || (n > 0 && !events)) return einval("probe_events: bad event list");
+    g_probe.clear();
+    for (int i = 0; i < n; ++i) {
+        if (!events[i]) {
+            g_probe.clear();
+            return einval("probe_events: null event handle (create the events first)");
+        }
+        g_probe.push_back(static_cast<cudaEvent_t>(events[i]));
+    }
+    g_last_error.clear();
+    return BVML_OK;
+}
+
+int bvml_ray_relu(void* normal, const float* ray, int B, int H, int W, int dtype, void* stream) {
+    if (!dtype_ok(dtype)) return einval("ray_relu: unknown dtype");
+    if (!dims_ok(B, H, W)) return einval("ray_relu: bad shape");
+    if ((long)B * H * W == 0) return finish(cudaSuccess, "ray_relu");
+    if (!normal || !ray) return einval("ray_relu: null tensor");
+    return finish(bvml::launch_ray_relu(normal, st_of(dtype), ray, B, H, W,
+                                        static_cast<cudaStream_t>(stream)),
+                  "ray_relu launch");
+}
+
+int bvml_angmf_propagate(const void* pred_norm, const void* prob, const void* xy,
+                         const void* angle, const float* ray, double fu, double cu, double fv,
+                         double cv, int B, int H, int W, int ps, int dil, int dtype, void* out,
+                         void* stream) {
+    if (!dtype_ok(dtype)) return einval("angmf_propagate: unknown dtype");
+    if (!window_ok(ps, dil)) return einval("angmf_propagate: window must be 3/5/7, dilation 1..4");
+    if (!dims_ok(B, H, W)) return einval("angmf_propagate: bad shape");
+    if ((long)B * H * W == 0) return finish(cudaSuccess, "angmf_propagate");
+    if (!pred_norm || !prob || !xy || !angle || !ray || !out)
+        return einval("angmf_propagate: null tensor");
+    if (out == pred_norm) return einval("angmf_propagate: out must not alias pred_norm");
+    if (!intr_ok(fu, fv)) return einval("angmf_propagate: focal lengths must be nonzero");
+    bvml::AngmfLaunch L{};
+    L.pn = pred_norm;
+    L.prob = prob;
+    L.xy = xy;
+    L.angle = angle;
+    L.ray = ray;
+    L.out = out;
+    L.st = L.pn_t = L.out_t = st_of(dtype);
+    L.fuse_ray_relu = false;
+    L.B = B;
+    L.H = H;
+    L.W = W;
+    L.ps = ps;
+    L.dil = dil;
+    L.fu = fu;
+    L.cu = cu;
+    L.fv = fv;
+    L.cv = cv;
+    return finish(bvml::launch_angmf(L, static_cast<cudaStream_t>(stream)),
+                  "angmf_propagate launch");
+}
+
+int bvml_convex_upsample(const void* x, const void* mask, int N, int C, int H, int W, int scale,
+                         int dtype, void* y, void* stream) {
+    if (!dtype_ok(dtype)) return einval("convex_upsample: unknown dtype");
+    if (C != 3 || scale != 8)
+        return fail(BVML_EUNSUPPORTED, "dsine ops: convex_upsample: only C = 3, scale = 8");
+    if (!dims_ok(N, H, W)) return einval("convex_upsample: bad shape");
+    if ((long)N * H * W == 0) return finish(cudaSuccess, "convex_upsample");
+    if (!x || !mask || !y) return einval("convex_upsample: null tensor");
+    bvml::UpsampleLaunch L{};
+    L.n = x;
+    L.mask = mask;
+    L.out = y;
+    L.st = L.n_t = st_of(dtype);
+    L.normalize = false;
+    L.ray_relu = false;
+    L.B = N;
+    L.h = H;
+    L.w = W;
+    L.crop_t = 0;
+    L.crop_l = 0;
+    L.out_h = 8 * H;
+    L.out_w = 8 * W;
+    L.fu = L.fv = 1.0;
+    return finish(bvml::launch_upsample(L, static_cast<cudaStream_t>(stream)),
+                  "convex_upsample launch");
+}
+
+int bvml_l2_normalize_nchw(const void* x, int N, int C, int H, int W, float eps, int dtype,
+                           void* y, void* stream) {
+    if (!dtype_ok(dtype)) return einval("l2_normalize: unknown dtype");
+    if (C < 0 || C > 16) return fail(BVML_EUNSUPPORTED, "dsine ops: l2_normalize: C must be <= 16");
+    if (N < 0 || H < 0 || W < 0) return einval("l2_normalize: bad shape");
+    if ((long)N * C * H * W == 0) return finish(cudaSuccess, "l2_normalize");
+    if (!x || !y) return einval("l2_normalize: null tensor");
+    return finish(bvml::launch_l2_normalize(x, y, st_of(dtype), N, C, H, W, eps,
+                                            static_cast<cudaStream_t>(stream)),
+                  "l2_normalize launch");
+}
+
+int bvml_slice2d(const void* x, int N, int C, int H, int W, int h0, int w0, int Ho, int Wo,
+                 int dtype, void* y, void* stream) {
+    if (!dtype_ok(dtype)) return einval("slice2d: unknown dtype");
+    if (N < 0 || C < 0 || H < 0 || W < 0 || Ho < 0 || Wo < 0 || h0 < 0 || w0 < 0 ||
+        h0 + Ho > H || w0 + Wo > W)
+        return einval("slice2d: window outside the input");
+    if ((long)N * C * Ho * Wo == 0) return finish(cudaSuccess, "slice2d");
+    if (!x || !y) return einval("slice2d: null tensor");
+    return finish(bvml::launch_slice2d(x, y, st_of(dtype), N, C, H, W, h0, w0, Ho, Wo,
+                                       static_cast<cudaStream_t>(stream)),
+                  "slice2d launch");
+}
+
+size_t bvml_refine_workspace_bytes(int B, int h, int w) {
+    if (B < 0 || h < 0 || w < 0) return 0;
+    const size_t plane = (size_t)h * (size_t)w;
+    return 2 * align256(sizeof(float) * 3 * plane * (size_t)B) + align256(sizeof(float) * 3 * plane);
+}
+
+int bvml_refine(const void* normal0, const float* ray8, const void* const* prob,
+                const void* const* xy, const void* const* angle, int iters, const void* mask,
+                int B, int h, int w, int ps, int dil, double fu, double cu, double fv, double cv,
+                int full_res_ray_relu, int crop_t, int crop_l, int out_h, int out_w, int dtype,
+                void* workspace, size_t workspace_bytes, void* out, void* stream) {
+    if (!dtype_ok(dtype)) return einval("refine: unknown dtype");
+    if (!window_ok(ps, dil)) return einval("refine: window must be 3/5/7, dilation 1..4");
+    if (!dims_ok(B, h, w)) return einval("refine: bad shape");
+    if (iters < 0 || iters > 64) return einval("refine: iters must be in 0..64");
+    if (crop_t < 0 || crop_l < 0 || out_h < 0 || out_w < 0 || crop_t + out_h > 8 * h ||
+        crop_l + out_w > 8 * w)
+        return einval("refine: crop window outside the 8x output");
+    if ((long)B * h * w == 0 || (long)out_h * out_w == 0) return finish(cudaSuccess, "refine");
+    if (!normal0 || !mask || !out || !workspace) return einval("refine: null tensor");
+    if (iters > 0 && (!prob || !xy || !angle)) return einval("refine: null per-iteration arrays");
+    for (int i = 0; i < iters; ++i)
+        if (!prob[i] || !xy[i] || !angle[i]) return einval("refine: null per-iteration tensor");
+    if (!intr_ok(fu, fv)) return einval("refine: focal lengths must be nonzero");
+    if (workspace_bytes < bvml_refine_workspace_bytes(B, h, w))
+        return einval("refine: workspace too small");
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+        return einval("refine: workspace must be 256-byte aligned");
+
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    size_t launch_no = 0;
+    if (cudaError_t e = probe(launch_no++, s); e != cudaSuccess)
+        return cuda_fail(e, "refine: probe event record");
+    const size_t nbytes = align256(sizeof(float) * 3 * (size_t)h * w * (size_t)B);
+    float* bufa = static_cast<float*>(workspace);
+    float* bufb = reinterpret_cast<float*>(static_cast<char*>(workspace) + nbytes);
+    float* rayw = reinterpret_cast<float*>(static_cast<char*>(workspace) + 2 * nbytes);
+    const float* ray = ray8;
+    if (!ray) {
+        cudaError_t e = bvml::launch_build_ray(rayw, h, w, fu, cu, fv, cv, s);
+        if (e != cudaSuccess) return cuda_fail(e, "refine: ray launch");
+        if ((e = probe(launch_no++, s)) != cudaSuccess)
+            return cuda_fail(e, "refine: probe event record");
+        ray = rayw;
+    }
+    const bvml::SType st = st_of(dtype);
+    const float* cur = nullptr;
+    if (iters == 0) {
+        // only the initial RayReLU: copy to fp32 workspace then clamp in place
+        if (st == bvml::SType::F32) {
+            cudaError_t e = cudaMemcpyAsync(bufa, normal0, sizeof(float) * 3 * (size_t)h * w * B,
+                                            cudaMemcpyDeviceToDevice, s);
+            if (e != cudaSuccess) return cuda_fail(e, "refine: copy");
+        } else {
+            return fail(BVML_EUNSUPPORTED, "dsine ops: refine: iters = 0 needs fp32 storage");
+        }
+        cudaError_t e = bvml::launch_ray_relu(bufa, bvml::SType::F32, ray, B, h, w, s);
+        if (e != cudaSuccess) return cuda_fail(e, "refine: ray_relu launch");
+        if ((e = probe(launch_no++, s)) != cudaSuccess)
+            return cuda_fail(e, "refine: probe event record");
+        cur = bufa;
+    } else {
+        float* dst = bufa;
+        float* other = bufb;
+        for (int it = 0; it < iters; ++it) {
+            bvml::AngmfLaunch L{};
+            L.pn = it == 0 ? normal0 : static_cast<const void*>(cur);
+            L.prob = prob[it];
+            L.xy = xy[it];
+            L.angle = angle[it];
+            L.ray = ray;
+            L.out = dst;
+            L.st = st;
+            L.pn_t = it == 0 ? st : bvml::SType::F32;
+            L.out_t = bvml::SType::F32;
+            L.fuse_ray_relu = it == 0;
+            L.B = B;
+            L.H = h;
+            L.W = w;
+            L.ps = ps;
+            L.dil = dil;
+            L.fu = fu;
+            L.cu = cu;
+            L.fv = fv;
+            L.cv = cv;
+            cudaError_t e = bvml::launch_angmf(L, s);
+            if (e != cudaSuccess) return finish(e, "refine: angmf launch");
+            if ((e = probe(launch_no++, s)) != cudaSuccess)
+                return cuda_fail(e, "refine: probe event record");
+            cur = dst;
+            float* t = dst;
+            dst = other;
+            other = t;
+        }
+    }
+    bvml::UpsampleLaunch U{};
+    U.n = cur;
+    U.mask = mask;
+    U.out = out;
+    U.st = st;
+    U.n_t = bvml::SType::F32;
+    U.normalize = true;
+    U.ray_relu = full_res_ray_relu != 0;
+    U.B = B;
+    U.h = h;
+    U.w = w;
+    U.crop_t = crop_t;
+    U.crop_l = crop_l;
+    U.out_h = out_h;
+    U.out_w = out_w;
+    U.fu = fu;
+    U.cu = cu;
+    U.fv = fv;
+    U.cv = cv;
+    cudaError_t e = bvml::launch_upsample(U, s);
+    if (e != cudaSuccess) return finish(e, "refine: upsample launch");
+    if ((e = probe(launch_no++, s)) != cudaSuccess)
+        return cuda_fail(e, "refine: probe event record");
+    return finish(cudaSuccess, "refine");
+}
+
+}  // extern "C"

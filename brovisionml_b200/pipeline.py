@@ -1,0 +1,116 @@
+"""Host-buffer entry point: refine B frames whose inputs live in (pinned) host
+memory, overlapping the PCIe copies with the kernels.
+
+The reference uploads its inputs (src/dsine.cpp:87-89, the ray at
+src/dsine_refine.cpp:225-228), runs the ops, and downloads the result
+(src/dsine.cpp:99-101) one frame at a time on the default stream. Here the
+batch is cut into chunks of frames and three streams run a software
+pipeline: host->device copies of chunk i+1, the fused refine of chunk i and
+the device->host copy of chunk i-1 proceed together, double-buffered in
+device memory. Copies are plain cudaMemcpyAsync (torch ``copy_`` with
+``non_blocking``), one per tensor per chunk.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Sequence
+
+import torch
+
+from .ops import refine, refine_workspace_bytes
+
+
+@dataclass
+class HostBatch:
+    """Pinned host inputs of B frames (B,C,h,w) and the (3,h,w) fp32 ray."""
+    normal0: torch.Tensor
+    prob: Sequence[torch.Tensor]
+    xy: Sequence[torch.Tensor]
+    angle: Sequence[torch.Tensor]
+    mask: torch.Tensor
+    ray8: torch.Tensor | None = None
+
+
+class HostRefiner:
+    """Reusable device buffers + streams for ``refine_from_host`` on one GPU."""
+
+    def __init__(self, device: torch.device | int, B: int, h: int, w: int, iters: int,
+                 dtype: torch.dtype, *, ps: int = 5, chunk: int = 32):
+        self.dev = torch.device("cuda", device) if isinstance(device, int) else device
+        self.B, self.h, self.w, self.iters, self.dtype, self.ps = B, h, w, iters, dtype, ps
+        self.chunk = max(1, min(chunk, B))
+        P = ps * ps
+        c = self.chunk
+        mk = lambda *s: torch.empty(s, device=self.dev, dtype=dtype)  # noqa: E731
+        self.sets = []
+        for _ in range(2):
+            self.sets.append({
+                "normal0": mk(c, 3, h, w),
+                "prob": [mk(c, P, h, w) for _ in range(iters)],
+                "xy": [mk(c, 2 * P, h, w) for _ in range(iters)],
+                "angle": [mk(c, P, h, w) for _ in range(iters)],
+                "mask": mk(c, 576, h, w),
+                "out": mk(c, 3, 8 * h, 8 * w),
+            })
+        self.ray = torch.empty((3, h, w), device=self.dev, dtype=torch.float32)
+        self.ws = torch.empty(refine_workspace_bytes(c, h, w), device=self.dev, dtype=torch.uint8)
+        self.s_in = torch.cuda.Stream(self.dev)
+        self.s_run = torch.cuda.Stream(self.dev)
+        self.s_out = torch.cuda.Stream(self.dev)
+
+    def h2d_bytes(self, hb: HostBatch) -> int:
+        ts = [hb.normal0, hb.mask, *hb.prob, *hb.xy, *hb.angle]
+        n = sum(t.numel() * t.element_size() for t in ts)
+        return n + (hb.ray8.numel() * 4 if hb.ray8 is not None else 0)
+
+    def run(self, hb: HostBatch, out_host: torch.Tensor, fu: float, cu: float, fv: float,
+            cv: float, *, dil: int = 1, full_res_ray_relu: bool = False) -> None:
+        """Refine all B frames of ``hb`` into pinned ``out_host`` (B,3,8h,8w).
+        Returns when ``out_host`` is complete."""
+        B, c = hb.normal0.shape[0], self.chunk
+        with torch.cuda.device(self.dev):
+            if hb.ray8 is not None:
+                with torch.cuda.stream(self.s_in):
+                    self.ray.copy_(hb.ray8, non_blocking=True)
+            ray_ready = torch.cuda.Event()
+            ray_ready.record(self.s_in)
+            in_done, run_done, out_done = {}, {}, {}
+            chunks = [(b0, min(B, b0 + c)) for b0 in range(0, B, c)]
+            for i, (b0, b1) in enumerate(chunks):
+                st = self.sets[i % 2]
+                n = b1 - b0
+                with torch.cuda.stream(self.s_in):
+                    if i >= 2:  # the set is free once chunk i-2 is computed
+                        self.s_in.wait_event(run_done[i - 2])
+                    st["normal0"][:n].copy_(hb.normal0[b0:b1], non_blocking=True)
+                    for k in range(self.iters):
+                        st["prob"][k][:n].copy_(hb.prob[k][b0:b1], non_blocking=True)
+                        st["xy"][k][:n].copy_(hb.xy[k][b0:b1], non_blocking=True)
+                        st["angle"][k][:n].copy_(hb.angle[k][b0:b1], non_blocking=True)
+                    st["mask"][:n].copy_(hb.mask[b0:b1], non_blocking=True)
+                    in_done[i] = torch.cuda.Event()
+                    in_done[i].record(self.s_in)
+                with torch.cuda.stream(self.s_run):
+                    self.s_run.wait_event(in_done[i])
+                    self.s_run.wait_event(ray_ready)
+                    if i >= 2:  # out buffer of this set is free once copied out
+                        self.s_run.wait_event(out_done[i - 2])
+                    sl = lambda t: t[:n]  # noqa: E731
+                    refine(sl(st["normal0"]), [sl(t) for t in st["prob"]],
+                           [sl(t) for t in st["xy"]], [sl(t) for t in st["angle"]],
+                           sl(st["mask"]), fu, cu, fv, cv,
+                           ray8=self.ray if hb.ray8 is not None else None, ps=self.ps, dil=dil,
+                           full_res_ray_relu=full_res_ray_relu, out=sl(st["out"]),
+                           workspace=self.ws)
+                    run_done[i] = torch.cuda.Event()
+                    run_done[i].record(self.s_run)
+                with torch.cuda.stream(self.s_out):
+                    self.s_out.wait_event(run_done[i])
+                    out_host[b0:b1].copy_(st["out"][:n], non_blocking=True)
+                    out_done[i] = torch.cuda.Event()
+                    out_done[i].record(self.s_out)
+            self.s_out.synchronize()
+
+
+def pin(t: torch.Tensor) -> torch.Tensor:
+    return t.pin_memory() if not t.is_pinned() else t

@@ -1,0 +1,158 @@
+"""Work partitioning for the refine ops across the GPUs of one node.
+
+The path has no data exchange between pixels of different frames, and a
+frame's result at a pixel depends only on a bounded neighbourhood, so it
+shards without any collective:
+
+* frames   -- ``plan_frames``: contiguous, balanced frame ranges per rank
+  (image-parallel batches);
+* row-bands -- ``plan_bands``: one large frame cut into balanced bands of
+  owned grid rows, each computed with a halo of
+  ``halo_rows(iters, ps, dil) = iters * (ps // 2) * dil + 1`` extra rows per
+  side (each AngMF iteration widens the dependency cone by the window radius
+  times the dilation, the 3x3 upsample by one more row). Replicate padding is
+  applied only at true image edges; interior band edges see real halo rows,
+  and the rows the band edge contaminates are exactly the halo that is
+  cropped away, so the stitched result equals the whole-frame result (up to
+  fp32 rounding of the band-shifted principal point).
+* ``plan_tiles`` restates the reference's tile planner
+  (src/tile_runner.cpp:18-60) so a caller can report the reference's 2-D tile
+  plan for a frame; the balanced bands are what the GPUs run, since 25 tiles
+  of a 4096^2 frame cannot split evenly over 8 GPUs and tiles need
+  feathering, while exact bands need none.
+
+The only cross-GPU step is the final gather (``gather_frames`` /
+``gather_bands``): each rank's owned output goes to rank 0 (torch.distributed
+gather, NCCL over NVLink on GPUs, gloo on CPU) or is copied to host by each
+rank.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Sequence
+
+
+def plan_frames(B: int, world: int) -> list[tuple[int, int]]:
+    """Balanced contiguous (start, count) frame ranges, one per rank."""
+    if world <= 0:
+        raise ValueError("world must be positive")
+    base, extra = divmod(max(B, 0), world)
+    out, s = [], 0
+    for r in range(world):
+        n = base + (1 if r < extra else 0)
+        out.append((s, n))
+        s += n
+    return out
+
+
+def halo_rows(iters: int, ps: int, dil: int, upsample: bool = True) -> int:
+    """Grid rows of halo a band needs per side for an exact result."""
+    return iters * (ps // 2) * dil + (1 if upsample else 0)
+
+
+@dataclass(frozen=True)
+class Band:
+    own0: int    # first owned grid row
+    own1: int    # one past the last owned grid row
+    comp0: int   # first computed grid row (own0 - halo, clipped)
+    comp1: int   # one past the last computed grid row (own1 + halo, clipped)
+
+    @property
+    def rows(self) -> int:
+        return self.comp1 - self.comp0
+
+    @property
+    def crop_top(self) -> int:
+        """Owned rows start this many grid rows into the computed band."""
+        return self.own0 - self.comp0
+
+
+def plan_bands(h: int, world: int, halo: int) -> list[Band]:
+    """Balanced owned row-bands of an h-row grid, with halos clipped to the frame."""
+    bands = []
+    for own0, n in plan_frames(h, world):
+        own1 = own0 + n
+        bands.append(Band(own0, own1, max(0, own0 - halo), min(h, own1 + halo)))
+    return bands
+
+
+@dataclass(frozen=True)
+class TileRect:
+    x: int
+    y: int
+    w: int
+    h: int
+    ov_l: int = 0
+    ov_r: int = 0
+    ov_t: int = 0
+    ov_b: int = 0
+
+
+def _axis_starts(extent: int, tile: int, step: int) -> list[int]:
+    if extent <= tile:
+        return [0]
+    starts, p = [], 0
+    while True:
+        if p + tile >= extent:
+            starts.append(extent - tile)
+            return starts
+        starts.append(p)
+        p += step
+
+
+def plan_tiles(W: int, H: int, tile: int, overlap: int) -> list[TileRect]:
+    """The reference's overlapping-tile plan (src/tile_runner.cpp:33-60):
+    empty when tiling is off or the frame fits one tile; trailing tiles snap
+    to the edge at full size; feather overlap only toward a neighbour."""
+    if tile <= 0 or W <= 0 or H <= 0:
+        return []
+    if W <= tile and H <= tile:
+        return []
+    ov = min(max(overlap, 0), tile - 1)
+    step = max(1, tile - ov)
+    xs, ys = _axis_starts(W, tile, step), _axis_starts(H, tile, step)
+    out = []
+    for y in ys:
+        th = min(tile, H - y)
+        for x in xs:
+            tw = min(tile, W - x)
+            out.append(TileRect(x, y, tw, th, ov if x > 0 else 0, ov if x + tw < W else 0,
+                                ov if y > 0 else 0, ov if y + th < H else 0))
+    return out
+
+
+def band_intrinsics(cv: float, band: Band) -> float:
+    """Principal point v of a band: rows are re-indexed from comp0."""
+    return cv - band.comp0
+
+
+def gather_frames(local, counts: Sequence[int], group=None):
+    """Gather each rank's (count_r, ...) output to rank 0 (torch.distributed).
+
+    Returns the concatenated tensor on rank 0 and None elsewhere. Every rank
+    must call it (a collective)."""
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    mx = max(counts)
+    pad_shape = (mx,) + tuple(local.shape[1:])
+    send = torch.zeros(pad_shape, dtype=local.dtype, device=local.device)
+    if local.shape[0]:
+        send[: local.shape[0]].copy_(local)
+    recv = [torch.empty_like(send) for _ in range(world)] if rank == 0 else None
+    dist.gather(send, recv, dst=0, group=group)
+    if rank != 0:
+        return None
+    return torch.cat([recv[r][: counts[r]] for r in range(world)], dim=0)
+
+
+def gather_bands(local_rows, bands: Sequence[Band], group=None, row_dim: int = -2,
+                 scale: int = 8):
+    """Gather owned output rows (scale x grid rows) of every band to rank 0 and
+    stitch them along ``row_dim``. Returns the frame on rank 0, None elsewhere."""
+    counts = [scale * (b.own1 - b.own0) for b in bands]
+    moved = local_rows.movedim(row_dim, 0).contiguous()
+    full = gather_frames(moved, counts, group)
+    return None if full is None else full.movedim(0, row_dim).contiguous()

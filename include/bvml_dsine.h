@@ -1,0 +1,153 @@
+/*
+ * bvml_dsine.h -- C ABI of the B200 (sm_100a) DSINE refine-ops library
+ * (libbvml_dsine.so, built from brovisionml_b200/csrc/).
+ *
+ * It replaces the GPU half of wlejon/brovisionml's only repo-owned GPU path:
+ * the DSINE surface-normal refinement ops driven by Refiner::forward
+ * (src/dsine_refine.cpp:212-294). Each entry point names the reference
+ * interface it replaces.
+ *
+ * Conventions
+ *  - All pointers are DEVICE pointers of the current CUDA device, except the
+ *    pointer ARRAYS of bvml_refine (host arrays of device pointers).
+ *  - Tensors are planar NCHW and contiguous: (B, C, H, W), W fastest. B frames
+ *    of one camera share the intrinsics and the (3, H, W) fp32 ray map.
+ *  - `dtype` selects the storage type of the big tensors: BVML_F32 (float) or
+ *    BVML_F16 (IEEE binary16, fp32 arithmetic). Ray maps are always fp32.
+ *  - `stream` is a cudaStream_t (NULL = the legacy default stream, which is
+ *    where the reference launches). Calls are asynchronous; like the
+ *    reference, device faults surface at the caller's next synchronisation.
+ *  - Every call returns BVML_OK (0) or a BVML_E* code and never throws; the
+ *    text of the last failure on the calling thread is bvml_last_error(),
+ *    worded like the reference's exceptions: "dsine ops: ..." for argument
+ *    errors (src/dsine_ops.cpp:18-22) and "dsine cuda: <what>: <cuda error>"
+ *    for CUDA failures (src/dsine_ops.cu:25-29).
+ *  - Intrinsics fu, cu, fv, cv are the ones scaled to the (H, W) grid from
+ *    the "+0.5" principal point (src/dsine_refine.cpp:232-237).
+ */
+#ifndef BVML_DSINE_H
+#define BVML_DSINE_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BVML_ABI_VERSION 1
+
+enum bvml_dtype { BVML_F32 = 0, BVML_F16 = 1 };
+
+enum bvml_status {
+    BVML_OK = 0,
+    BVML_EINVAL = 1,      /* bad argument (null pointer, bad size, bad window) */
+    BVML_ECUDA = 2,       /* a CUDA call or kernel launch failed              */
+    BVML_EUNSUPPORTED = 3 /* valid request outside what this build implements  */
+};
+
+/* Text of the last failure on this thread ("" if none). */
+const char* bvml_last_error(void);
+
+/* BVML_ABI_VERSION of the loaded library. */
+int bvml_abi_version(void);
+
+/*
+ * RayReLU in place on B frames of (3, H, W) normals against one (3, H, W)
+ * ray: c = n.r / max(|n||r|, 1e-8); n <- normalise(n + r (max(c - eps, 0) + eps - c)),
+ * eps = 1e-2.
+ * Replaces brovisionml::dsine::detail::ray_relu_cuda
+ * (src/dsine_ops_cuda.h:13-14, src/dsine_ops.cu:159-168; CPU twin
+ * src/dsine_ops.cpp:55-76). B = 1 is the reference's call.
+ */
+int bvml_ray_relu(void* normal, const float* ray, int B, int H, int W, int dtype,
+                  void* stream);
+
+/*
+ * Fused AngMF propagate: for every pixel, rotate each of the ps*ps window
+ * neighbours' normals (dilation dil, replicate padding) by its predicted
+ * axis-angle, RayReLU it against the pixel's ray, take the prob-weighted sum
+ * and L2-normalise.
+ *   pred_norm (B,3,H,W)  prob (B,P,H,W)  xy (B,2P,H,W)  angle (B,P,H,W)
+ *   ray (3,H,W) fp32     out (B,3,H,W), caller-allocated, must not alias inputs
+ * with P = ps*ps, slot n = ky*ps + kx, xy channels [0,P) = x, [P,2P) = y.
+ * ps in {3, 5, 7}, dil in 1..4.
+ * Replaces brovisionml::dsine::detail::angmf_propagate_cuda
+ * (src/dsine_ops_cuda.h:16-23, src/dsine_ops.cu:170-191; CPU twin
+ * src/dsine_ops.cpp:78-172). The reference is ps = 5, dil = 1, B = 1, fp32
+ * and allocates `out` itself; the C++ bridge (brovisionml_b200/csrc/
+ * dsine_ops_b200.cpp) keeps that allocation contract.
+ */
+int bvml_angmf_propagate(const void* pred_norm, const void* prob, const void* xy,
+                         const void* angle, const float* ray, double fu, double cu,
+                         double fv, double cv, int B, int H, int W, int ps, int dil,
+                         int dtype, void* out, void* stream);
+
+/*
+ * Convex upsample: mask (N, 9*s*s, H, W) viewed (9, s, s), softmax over the 9
+ * taps, 3x3 replicate-padded unfold of x (N, C, H, W), output y (N, C, s*H, s*W)
+ * with row s*y+ky, col s*x+kx. This build implements C = 3, s = 8 (the path's
+ * only call); other shapes return BVML_EUNSUPPORTED.
+ * Replaces brotensor::convex_upsample_forward(X, mask, N, C, H, W, scale, Y)
+ * as called at src/dsine_refine.cpp:277-279 (semantics:
+ * include/brovisionml/dsine_refine.h:91-97).
+ */
+int bvml_convex_upsample(const void* x, const void* mask, int N, int C, int H, int W,
+                         int scale, int dtype, void* y, void* stream);
+
+/*
+ * Per-pixel channel L2-normalise y = x / max(|x|, eps), (N, C, H, W), C <= 16;
+ * y may alias x.
+ * Replaces brotensor::l2_normalize_nchw_forward(X, N, C, H, W, eps, Y)
+ * (src/dsine_refine.cpp:280-281).
+ */
+int bvml_l2_normalize_nchw(const void* x, int N, int C, int H, int W, float eps, int dtype,
+                           void* y, void* stream);
+
+/*
+ * Crop (N, C, H, W) at (h0, w0) to (N, C, Ho, Wo).
+ * Replaces brotensor::slice2d_forward(X, N, C, H, W, h0, w0, Ho, Wo, Y)
+ * (src/dsine_refine.cpp:288-292).
+ */
+int bvml_slice2d(const void* x, int N, int C, int H, int W, int h0, int w0, int Ho, int Wo,
+                 int dtype, void* y, void* stream);
+
+/* Bytes of device workspace bvml_refine needs for B frames of an (h, w) grid. */
+size_t bvml_refine_workspace_bytes(int B, int h, int w);
+
+/*
+ * The whole refine-ops unit of Refiner::forward (src/dsine_refine.cpp:241-292)
+ * for B frames, fused into iters + 1 kernel launches:
+ *   n = RayReLU(normal0, ray8)                      (fused into iteration 0)
+ *   repeat iters times: n = AngMF(n, prob[i], xy[i], angle[i], ray8)
+ *   up = L2normalise(ConvexUpsample8(n, mask))      (upsampled once: the
+ *        reference recomputes it every iteration but only keeps the last)
+ *   if full_res_ray_relu: up = RayReLU(up, full-res ray from 8x the intrinsics)
+ *   out = crop(up, crop_t, crop_l, out_h, out_w)
+ *   normal0 (B,3,h,w)  ray8 (3,h,w) fp32 or NULL (then computed from the
+ *   intrinsics exactly as get_ray_core, src/dsine_decoder.cpp:242-261)
+ *   prob/xy/angle: HOST arrays of `iters` device pointers, shapes as in
+ *   bvml_angmf_propagate   mask (B,576,h,w)   out (B,3,out_h,out_w)
+ * Intermediate normals stay fp32 in `workspace` (>= bvml_refine_workspace_bytes,
+ * 256-byte aligned); storage-typed tensors follow `dtype`.
+ */
+int bvml_refine(const void* normal0, const float* ray8, const void* const* prob,
+                const void* const* xy, const void* const* angle, int iters, const void* mask,
+                int B, int h, int w, int ps, int dil, double fu, double cu, double fv,
+                double cv, int full_res_ray_relu, int crop_t, int crop_l, int out_h,
+                int out_w, int dtype, void* workspace, size_t workspace_bytes, void* out,
+                void* stream);
+
+/*
+ * Profiling aid (no reference counterpart): arm `n` caller-created CUDA events
+ * (cudaEvent_t, cast to void*) for the calling thread. While armed,
+ * bvml_refine records events[0] on its stream before its first kernel and
+ * events[k] after its k-th kernel (k = 1 .. n-1), so the caller can time
+ * every launch of the fused unit on the stream it runs on. n = 0 disarms.
+ */
+int bvml_probe_events(void* const* events, int n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BVML_DSINE_H */
