@@ -4,7 +4,12 @@
 #include <cuda_runtime.h>
 #include <stddef.h>
 
+#include <string>
+
 namespace bvml {
+
+// Record `msg` as the calling thread's bvml_last_error() text; returns `code`.
+int report_error(int code, const std::string& msg);
 
 enum class SType { F32 = 0, F16 = 1 };
 

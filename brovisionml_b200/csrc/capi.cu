@@ -54,6 +54,8 @@ size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
 }  // namespace
 
+int bvml::report_error(int code, const std::string& msg) { return fail(code, msg); }
+
 extern "C" {
 
 const char* bvml_last_error(void) { return g_last_error.c_str(); }

@@ -137,6 +137,33 @@ int bvml_refine(const void* normal0, const float* ray8, const void* const* prob,
                 int out_w, int dtype, void* workspace, size_t workspace_bytes, void* out,
                 void* stream);
 
+/* Scratch bytes built into the library per device for bvml_refine_noalloc. */
+#define BVML_REFINE_NOALLOC_MAX_BYTES (32u * 1024u * 1024u)
+
+/*
+ * bvml_refine for callers that cannot allocate device memory (no counterpart
+ * in the reference, which allocates freely). Same arguments and results as
+ * bvml_refine, minus the workspace: the scratch is a fixed 32 MiB array built
+ * into this library, present on every GPU that loads it until the process
+ * exits. For hosts that own the GPU memory budget and forbid allocations after
+ * start-up (a plugin in another application's inference or render loop), or
+ * loops that cannot take cudaMalloc's implicit device synchronisation.
+ *  - The first call on each device looks the array's address up with that
+ *    device current; make that first call before any stream capture.
+ *  - Work needing more than BVML_REFINE_NOALLOC_MAX_BYTES of scratch
+ *    (bvml_refine_workspace_bytes(B, h, w); about 1.39 M grid pixels, e.g. 96
+ *    frames of 90x160) is rejected with BVML_EINVAL.
+ *  - All calls on a device share the array: calls that overlap on the GPU
+ *    (other streams or host threads) race and must be serialised by the
+ *    caller. Nothing in it needs clearing between calls.
+ *  - Allocates nothing: no cudaMalloc, cudaFree or allocating library call.
+ */
+int bvml_refine_noalloc(const void* normal0, const float* ray8, const void* const* prob,
+                        const void* const* xy, const void* const* angle, int iters,
+                        const void* mask, int B, int h, int w, int ps, int dil, double fu,
+                        double cu, double fv, double cv, int full_res_ray_relu, int crop_t,
+                        int crop_l, int out_h, int out_w, int dtype, void* out, void* stream);
+
 /*
  * Profiling aid (no reference counterpart): arm `n` caller-created CUDA events
  * (cudaEvent_t, cast to void*) for the calling thread. While armed,
