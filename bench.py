@@ -37,9 +37,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 import numpy as np
@@ -71,68 +69,75 @@ def hbm_peak():
 # ----------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi sampling (200 ms) of one GPU during the timed region."""
+    """SM clock and clock-event reasons of one GPU, polled through NVML every
+    ~5 ms in a background thread during the timed region (nvidia-smi's
+    fastest loop is too coarse for a region of tens of milliseconds)."""
 
-    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event-reason bits (nvml.h nvmlClocksEventReason*)
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40}
 
-    def __init__(self, uuid: str | None):
+    def __init__(self, device_index: int, uuid: str | None = None):
+        self.index = device_index
         self.uuid = uuid
-        self.proc = None
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.samples = []
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
+        self.error = None
 
     def __enter__(self):
+        import threading
+
         try:
-            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                   "-lms", "200"]
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = None
             if self.uuid:
-                cmd += ["-i", self.uuid]
-            self.proc = subprocess.Popen(cmd, stdout=self.f, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+                try:
+                    h = pynvml.nvmlDeviceGetHandleByUUID(self.uuid)
+                except Exception:
+                    h = None
+            if h is None:
+                h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # sampling is reported, never required
+            self.error = str(e)
+            return self
+        self._stop = threading.Event()
+
+        def poll():
+            while not self._stop.is_set():
+                try:
+                    mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    self.samples.append((mhz, rs, pw))
+                except Exception as e:
+                    self.error = str(e)
+                    return
+                self._stop.wait(0.005)
+
+        self._thread = threading.Thread(target=poll, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        self.f.flush()
-        rows = []
-        try:
-            with open(self.f.name) as f:
-                for line in f:
-                    parts = [x.strip() for x in line.split(",")]
-                    if len(parts) >= 10:
-                        rows.append(parts)
-        finally:
-            os.unlink(self.f.name)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-
-        def num(s):
-            try:
-                return float(s)
-            except ValueError:
-                return None
-
-        sm = [num(r[2]) for r in rows if num(r[2]) is not None]
-        mx = [num(r[3]) for r in rows if num(r[3]) is not None]
-        pw = [num(r[4]) for r in rows if num(r[4]) is not None]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i] == "Active"})
-        # "under load": samples within 20% of the top SM clock seen
-        top = max(sm) if sm else 0
-        load = [s for s in sm if s >= 0.5 * top] or sm
-        return {"sm_mhz": statistics.median(load) if load else None,
-                "sm_max_mhz": max(mx) if mx else None,
-                "power_w_max": max(pw) if pw else None,
-                "samples": len(rows), "reasons": reasons}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz,
+                    "reasons": ["unsampled" + (f": {self.error}" if self.error else "")]}
+        mhz = [m for m, _, _ in self.samples]
+        reasons = sorted({k for _, r, _ in self.samples for k, bit in self.REASONS.items()
+                          if r & bit})
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz,
+                "sm_mhz_min": min(mhz), "power_w_max": round(max(p for _, _, p in self.samples), 1),
+                "samples": len(self.samples), "reasons": reasons, "source": "nvml"}
 
 
 # ----------------------------------------------------------------- inputs
@@ -365,7 +370,7 @@ def main():
             uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
         except Exception:
             pass
-        with ClockSampler(uuid) as clk:
+        with ClockSampler(local, uuid) as clk:
             start.record(stream)
             for k in range(args.steps):
                 bv.check(bv.lib.bvml_probe_events(arrs[k], len(evs[k])))

@@ -212,227 +212,263 @@ constexpr float kMMin = 1e-2f;    // smallest tolerated |m|^2 after the RayReLU
 constexpr float kQMin = 1e-10f, kQMax = 1e30f;  // |xy|^2 range of the fast path
 constexpr float kThMax = 3.2f;    // |theta| range of the series
 
-template <int PS, typename TS, typename TNI, typename TNO, bool FUSE_RR>
-__global__ void __launch_bounds__(kThreads, 2)
-angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* __restrict__ xy,
-             const TS* __restrict__ ang, const float* __restrict__ ray, TNO* __restrict__ out,
-             const AngmfArgs a) {
-    constexpr int P = PS * PS;
-    using Mask = typename std::conditional<(P <= 32), uint32_t, unsigned long long>::type;
-    extern __shared__ float4 smem4[];
+template <typename Mask>
+struct PairAcc {
+    float2 x, y, z;   // prob-weighted sums of the clamped, rotated neighbours
+    Mask bad0, bad1;  // neighbours left to the exact fix-up, per pixel of the pair
+};
+
+// One neighbour slot n for a pixel pair: rotate the (unit) source normals,
+// RayReLU them against the pixels' (unit) rays, accumulate with weight w.
+// Sign conventions avoid negated packed operands: tun = -tu, nifu = -1/fu,
+// nifv = -1/fv are supplied by the caller.
+template <typename Mask>
+__device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 th, float2 wt,
+                                           float2 nx, float2 ny, float2 nz, float2 tu,
+                                           float2 tun, float2 tv, float2 ifu2, float2 ifv2,
+                                           float2 nifu2, float2 nifv2, float2 rx, float2 ry,
+                                           float2 rz, PairAcc<Mask>& A) {
+    const float2 q = fma2(xs, xs, mul2(ys, ys));
+    const float2 iq = rsqrt2_ftz(q);
+    const float2 X = mul2(xs, ifu2), Y = mul2(ys, ifv2);     // d (unnormalised)
+    const float2 Xn = mul2(xs, nifu2), Yn = mul2(ys, nifv2);
+    const float2 e = fma2(X, nx, mul2(Y, ny));               // d.n
+    const float2 as = fma2(tu, nx, fma2(tv, ny, nz));        // P.n
+    const float2 dd = fma2(iq, e, as);                       // (P + d).n, d normalised
+    // g = d x P = (Y, -X, gz); g_perp = g - n (g.n) = g + n ngn
+    const float2 gz = fma2(X, tv, mul2(Y, tun));
+    const float2 gzn = fma2(Xn, tv, mul2(Y, tu));
+    const float2 ngn = fma2(Yn, nx, fma2(X, ny, mul2(gzn, nz)));
+    const float2 gpx = fma2(nx, ngn, Y);
+    const float2 gpy = fma2(ny, ngn, Xn);
+    const float2 gpz = fma2(nz, ngn, gz);
+    const float2 gp2 = fma2(gpx, gpx, fma2(gpy, gpy, mul2(gpz, gpz)));
+    const float2 gg2 = fma2(Y, Y, fma2(X, X, mul2(gz, gz)));
+    const float2 gi = rsqrt2_ftz(max2(gp2, f2(1e-30f)));
+    // sin / cos of theta via the half angle
+    const float2 t2 = mul2(th, th);
+    float2 ps2 = fma2(t2, f2(kS6), f2(kS5));
+    ps2 = fma2(t2, ps2, f2(kS4));
+    ps2 = fma2(t2, ps2, f2(kS3));
+    ps2 = fma2(t2, ps2, f2(kS2));
+    ps2 = fma2(t2, ps2, f2(kS1));
+    ps2 = fma2(t2, ps2, f2(1.0f));
+    const float2 s2 = mul2(th, ps2);  // 2 sin(theta/2)
+    float2 ch = fma2(t2, f2(kC6), f2(kC5));
+    ch = fma2(t2, ch, f2(kC4));
+    ch = fma2(t2, ch, f2(kC3));
+    ch = fma2(t2, ch, f2(kC2));
+    ch = fma2(t2, ch, f2(kC1));
+    ch = fma2(t2, ch, f2(1.0f));      // cos(theta/2)
+    const float2 sn = mul2(s2, ch);   // sin(theta)
+    const float2 cs = fma2(s2, mul2(s2, f2(-0.5f)), f2(1.0f));  // cos(theta)
+    float2 kk = mul2(sn, gi);
+    kk.x = __uint_as_float(__float_as_uint(kk.x) ^ (__float_as_uint(dd.x) & 0x80000000u));
+    kk.y = __uint_as_float(__float_as_uint(kk.y) ^ (__float_as_uint(dd.y) & 0x80000000u));
+    const float2 qx = fma2(kk, gpx, mul2(cs, nx));
+    const float2 qy = fma2(kk, gpy, mul2(cs, ny));
+    const float2 qz = fma2(kk, gpz, mul2(cs, nz));
+    // RayReLU against the pixels' rays, then the weighted sum
+    const float2 c = fma2(qx, rx, fma2(qy, ry, mul2(qz, rz)));
+    const float2 dc = max2(fma2(c, f2(-1.0f), f2(kRayEps)), f2(0.0f));
+    const float2 mx = fma2(rx, dc, qx);
+    const float2 my = fma2(ry, dc, qy);
+    const float2 mz = fma2(rz, dc, qz);
+    const float2 l2 = fma2(mx, mx, fma2(my, my, mul2(mz, mz)));
+    const float2 wsg = mul2(mul2(wt, f2(kGCond)), sn);
+    const float2 gcond = mul2(mul2(wsg, wsg), gg2);
+    // bitwise | : every test is evaluated, no branches
+    const bool b0 = !(fabsf(dd.x) >= kTau) | !(gp2.x >= gcond.x) | !(l2.x >= kMMin) |
+                    !(q.x >= kQMin) | !(q.x <= kQMax) | !(fabsf(th.x) <= kThMax);
+    const bool b1 = !(fabsf(dd.y) >= kTau) | !(gp2.y >= gcond.y) | !(l2.y >= kMMin) |
+                    !(q.y >= kQMin) | !(q.y <= kQMax) | !(fabsf(th.y) <= kThMax);
+    float2 wm = mul2(wt, rsqrt2_ftz(l2));
+    if (b0 | b1) {  // rare: leave the neighbour to the exact fix-up
+        if (b0) {
+            wm.x = 0.0f;
+            A.bad0 |= Mask(1) << n;
+        }
+        if (b1) {
+            wm.y = 0.0f;
+            A.bad1 |= Mask(1) << n;
+        }
+    }
+    A.x = fma2(wm, mx, A.x);
+    A.y = fma2(wm, my, A.y);
+    A.z = fma2(wm, mz, A.z);
+}
+
+// The replicate-padded halo of unit source normals in shared memory. For each
+// component an "even" and an "odd" plane of float2 pairs,
+//   E[i][k] = (v[i][2k], v[i][2k+1]),  O[i][k] = (v[i][2k+1], v[i][2k+2]),
+// so the pair starting at column j is (j even ? E : O)[i][j >> 1]: a warp's
+// pairs for one neighbour slot are consecutive float2, conflict-free. tu0
+// (with its negation) and tv0 are tabulated the same way.
+struct NTile {
+    float2* e[3];
+    float2* o[3];
+    float4* tue;  // (tu0, tu1, -tu0, -tu1) of the pair starting at column 2k
+    float4* tuo;  // ... at column 2k + 1
+    float* tv;
+    int swh;      // pairs per plane row
+
+    static constexpr __host__ __device__ int pairs_per_row(int SW) { return SW / 2 + 1; }
+    static __host__ __device__ size_t bytes(int SW, int SH) {
+        const int h = pairs_per_row(SW);
+        return sizeof(float4) * 2 * h + sizeof(float2) * 6 * (size_t)SH * h + sizeof(float) * SH;
+    }
+    __device__ void carve(void* base, int SW, int SH) {
+        swh = pairs_per_row(SW);
+        tue = reinterpret_cast<float4*>(base);
+        tuo = tue + swh;
+        float2* p = reinterpret_cast<float2*>(tuo + swh);
+        for (int c = 0; c < 3; ++c) {
+            e[c] = p;
+            o[c] = p + SH * swh;
+            p += 2 * SH * swh;
+        }
+        tv = reinterpret_cast<float*>(p);
+    }
+};
+
+// Stage the tile's normal halo and tu0 / tv0 tables at (x0, y0).
+template <typename TNI, bool FUSE_RR>
+__device__ __forceinline__ void stage_normals(const TNI* __restrict__ pnb,
+                                              const float* __restrict__ ray, const NTile& T,
+                                              int x0, int y0, const AngmfArgs& a) {
     const int R = a.R;
     const int SW = kTW + 2 * R;
     const int SH = kTH + 2 * R;
-    float2* snx = reinterpret_cast<float2*>(smem4);   // [SH][SW] pair-duplicated planes:
-    float2* sny = snx + SH * SW;                      // element (i,j) = (v[i][j], v[i][j+1])
-    float2* snz = sny + SH * SW;
-    float2* stu = snz + SH * SW;                      // [SW] pairs of tu0
-    float* stv = reinterpret_cast<float*>(stu + SW);  // [SH] tv0
-
-    int t = blockIdx.x;
-    const int tix = t % a.tiles_x;
-    t /= a.tiles_x;
-    const int tiy = t % a.tiles_y;
-    const int b = t / a.tiles_y;
-    const int x0 = tix * kTW, y0 = tiy * kTH;
     const long HW = a.HW;
-    const TNI* pnb = pn + (long)b * 3 * HW;
-
-    // ---- stage the replicate-padded halo of unit source normals
     for (int idx = threadIdx.x; idx < SH * SW; idx += kThreads) {
         const int i = idx / SW, j = idx - i * SW;
         const int sy = clampi(y0 - R + i, 0, a.H - 1);
         const int sx = clampi(x0 - R + j, 0, a.W - 1);
         const long sp = (long)sy * a.W + sx;
-        float nx = St<TNI>::ld(pnb + sp), ny = St<TNI>::ld(pnb + HW + sp),
-              nz = St<TNI>::ld(pnb + 2 * HW + sp);
-        if (FUSE_RR) ray_relu_f32(nx, ny, nz, __ldg(ray + sp), __ldg(ray + HW + sp),
+        float v[3] = {St<TNI>::ld(pnb + sp), St<TNI>::ld(pnb + HW + sp),
+                      St<TNI>::ld(pnb + 2 * HW + sp)};
+        if (FUSE_RR) ray_relu_f32(v[0], v[1], v[2], __ldg(ray + sp), __ldg(ray + HW + sp),
                                   __ldg(ray + 2 * HW + sp));
-        const float inv = rsqrtf(fmaxf(fmaf(nx, nx, fmaf(ny, ny, nz * nz)), 1e-24f));
-        float* fx = reinterpret_cast<float*>(snx);
-        float* fy = reinterpret_cast<float*>(sny);
-        float* fz = reinterpret_cast<float*>(snz);
-        const int e = 2 * (i * SW + j);
-        fx[e] = nx * inv;
-        fy[e] = ny * inv;
-        fz[e] = nz * inv;
-        if (j > 0) {
-            fx[e - 1] = nx * inv;
-            fy[e - 1] = ny * inv;
-            fz[e - 1] = nz * inv;
+        const float inv = rsqrtf(fmaxf(fmaf(v[0], v[0], fmaf(v[1], v[1], v[2] * v[2])), 1e-24f));
+        const int k = j >> 1;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const float u = v[c] * inv;
+            float* ep = reinterpret_cast<float*>(T.e[c] + i * T.swh + k);
+            float* op = reinterpret_cast<float*>(T.o[c] + i * T.swh);
+            if (j & 1) {
+                ep[1] = u;
+                op[2 * k] = u;          // O[i][k].x
+            } else {
+                ep[0] = u;
+                if (k > 0) op[2 * (k - 1) + 1] = u;  // O[i][k-1].y
+            }
         }
     }
-    for (int j = threadIdx.x; j < SW; j += kThreads) {
-        const int s0 = clampi(x0 - R + j, 0, a.W - 1);
-        const int s1 = clampi(x0 - R + j + 1, 0, a.W - 1);
-        stu[j] = make_float2(fmaf((float)s0, a.ifu, a.tu_c), fmaf((float)s1, a.ifu, a.tu_c));
+    for (int k = threadIdx.x; k < T.swh; k += kThreads) {
+        float t[3];
+#pragma unroll
+        for (int d = 0; d < 3; ++d)
+            t[d] = fmaf((float)clampi(x0 - R + 2 * k + d, 0, a.W - 1), a.ifu, a.tu_c);
+        T.tue[k] = make_float4(t[0], t[1], -t[0], -t[1]);
+        T.tuo[k] = make_float4(t[1], t[2], -t[1], -t[2]);
     }
     for (int i = threadIdx.x; i < SH; i += kThreads) {
         const int s0 = clampi(y0 - R + i, 0, a.H - 1);
-        stv[i] = fmaf((float)s0, a.ifv, a.tv_c);
+        T.tv[i] = fmaf((float)s0, a.ifv, a.tv_c);
     }
-    __syncthreads();
+}
 
-    // ---- one pixel pair per thread
-    const int lx = 2 * (threadIdx.x % (kTW / 2));
-    const int ly = threadIdx.x / (kTW / 2);
-    const int x = x0 + lx, y = y0 + ly;
-    if (y >= a.H || x >= a.W) return;
-    const bool two = x + 1 < a.W;
-    const bool vec = (a.W & 1) == 0;  // pairs start at even offsets -> 8/4-byte aligned
-    const long p0 = (long)y * a.W + x;
-    const long p1 = two ? p0 + 1 : p0;
-
-    float2 rx = f2(__ldg(ray + p0), __ldg(ray + p1));
-    float2 ry = f2(__ldg(ray + HW + p0), __ldg(ray + HW + p1));
-    float2 rz = f2(__ldg(ray + 2 * HW + p0), __ldg(ray + 2 * HW + p1));
-    {
-        const float2 ri = rsqrt2(max2(fma2(rx, rx, fma2(ry, ry, mul2(rz, rz))), f2(1e-16f)));
-        rx = mul2(rx, ri);
-        ry = mul2(ry, ri);
-        rz = mul2(rz, ri);
+// The staged operands of the pair starting at column j of halo row i.
+struct NPair {
+    float2 nx, ny, nz, tu, tun, tv;
+};
+__device__ __forceinline__ NPair npair(const NTile& T, int i, int j) {
+    const int k = i * T.swh + (j >> 1);
+    NPair r;
+    if (j & 1) {
+        r.nx = T.o[0][k];
+        r.ny = T.o[1][k];
+        r.nz = T.o[2][k];
+        const float4 t = T.tuo[j >> 1];
+        r.tu = f2(t.x, t.y);
+        r.tun = f2(t.z, t.w);
+    } else {
+        r.nx = T.e[0][k];
+        r.ny = T.e[1][k];
+        r.nz = T.e[2][k];
+        const float4 t = T.tue[j >> 1];
+        r.tu = f2(t.x, t.y);
+        r.tun = f2(t.z, t.w);
     }
+    r.tv = f2(T.tv[i]);
+    return r;
+}
 
+// Exact fp64 fix-ups of the flagged neighbours of one pixel; returns the sum.
+template <int PS, typename TS, typename TNI, bool FUSE_RR, typename Mask>
+__device__ __noinline__ float3 fixups(Mask m, int b, int x, int y, const TNI* __restrict__ pn,
+                                      const TS* __restrict__ prob, const TS* __restrict__ xy,
+                                      const TS* __restrict__ ang, const float* __restrict__ ray,
+                                      const AngmfArgs a) {
+    constexpr int P = PS * PS;
+    const long HW = a.HW;
+    const long pp = (long)y * a.W + x;
+    const TNI* pnb = pn + (long)b * 3 * HW;
     const TS* xyb = xy + (long)b * 2 * P * HW;
     const TS* prb = prob + (long)b * P * HW;
     const TS* anb = ang + (long)b * P * HW;
-    auto ld = [&](const TS* base) -> float2 {
-        return vec ? St<TS>::ld2s(base + p0) : f2(St<TS>::lds1(base + p0), St<TS>::lds1(base + p1));
-    };
-
-    const float2 ifu2 = f2(a.ifu), ifv2 = f2(a.ifv);
-    float2 accx = f2(0.f), accy = f2(0.f), accz = f2(0.f);
-    Mask bad0 = 0, bad1 = 0;
-
-#pragma unroll 1
-    for (int ky = 0; ky < PS; ++ky) {
-        const int i = ly + ky * a.dil;
-        const float2 tv = f2(stv[i]);
-        const float2* rnx = snx + i * SW + lx;
-        const float2* rny = sny + i * SW + lx;
-        const float2* rnz = snz + i * SW + lx;
-        const float2* rtu = stu + lx;
-#pragma unroll
-        for (int kx = 0; kx < PS; ++kx) {
-            const int n = ky * PS + kx;
-            const int j = kx * a.dil;
-            const float2 nx = rnx[j], ny = rny[j], nz = rnz[j], tu = rtu[j];
-            const float2 xs = ld(xyb + (long)n * HW);
-            const float2 ys = ld(xyb + (long)(P + n) * HW);
-            const float2 th = ld(anb + (long)n * HW);
-            float2 wt = ld(prb + (long)n * HW);
-
-            const float2 q = fma2(xs, xs, mul2(ys, ys));
-            const float2 iq = rsqrt2(q);
-            const float2 xsf = mul2(xs, ifu2);
-            const float2 ysf = mul2(ys, ifv2);
-            const float2 e = fma2(xsf, nx, mul2(ysf, ny));
-            const float2 as = fma2(tu, nx, fma2(tv, ny, nz));
-            const float2 dd = fma2(iq, e, as);
-            // g = (ysf, -xsf, gz); carry gy' = -g_perp.y to avoid negations
-            const float2 gz = fnma2(ysf, tu, mul2(xsf, tv));
-            const float2 ng = fma2(gz, nz, fnma2(xsf, ny, mul2(ysf, nx)));
-            const float2 gpx = fnma2(nx, ng, ysf);
-            const float2 gpyn = fma2(ny, ng, xsf);
-            const float2 gpz = fnma2(nz, ng, gz);
-            const float2 gp2 = fma2(gpx, gpx, fma2(gpyn, gpyn, mul2(gpz, gpz)));
-            const float2 gg2 = fma2(ysf, ysf, fma2(xsf, xsf, mul2(gz, gz)));
-            const float2 gi = rsqrt2(max2(gp2, f2(1e-30f)));
-            // sin / cos of theta via the half angle
-            const float2 t2 = mul2(th, th);
-            float2 ps2 = fma2(t2, f2(kS6), f2(kS5));
-            ps2 = fma2(t2, ps2, f2(kS4));
-            ps2 = fma2(t2, ps2, f2(kS3));
-            ps2 = fma2(t2, ps2, f2(kS2));
-            ps2 = fma2(t2, ps2, f2(kS1));
-            ps2 = fma2(t2, ps2, f2(1.0f));
-            const float2 s2 = mul2(th, ps2);  // 2 sin(theta/2)
-            float2 ch = fma2(t2, f2(kC6), f2(kC5));
-            ch = fma2(t2, ch, f2(kC4));
-            ch = fma2(t2, ch, f2(kC3));
-            ch = fma2(t2, ch, f2(kC2));
-            ch = fma2(t2, ch, f2(kC1));
-            ch = fma2(t2, ch, f2(1.0f));      // cos(theta/2)
-            const float2 sn = mul2(s2, ch);   // sin(theta)
-            const float2 cs = fnma2(mul2(s2, f2(0.5f)), s2, f2(1.0f));  // cos(theta)
-            float2 kk = mul2(sn, gi);
-            kk.x = __uint_as_float(__float_as_uint(kk.x) ^ (__float_as_uint(dd.x) & 0x80000000u));
-            kk.y = __uint_as_float(__float_as_uint(kk.y) ^ (__float_as_uint(dd.y) & 0x80000000u));
-            const float2 qx = fma2(kk, gpx, mul2(cs, nx));
-            const float2 qy = fnma2(kk, gpyn, mul2(cs, ny));
-            const float2 qz = fma2(kk, gpz, mul2(cs, nz));
-            // RayReLU against this pixel's ray, then the weighted sum
-            const float2 c = fma2(qx, rx, fma2(qy, ry, mul2(qz, rz)));
-            const float2 dc = max2(fnma2(c, f2(1.0f), f2(kRayEps)), f2(0.0f));
-            const float2 mx = fma2(rx, dc, qx);
-            const float2 my = fma2(ry, dc, qy);
-            const float2 mz = fma2(rz, dc, qz);
-            const float2 l2 = fma2(mx, mx, fma2(my, my, mul2(mz, mz)));
-            const float2 wsg = mul2(mul2(wt, f2(kGCond)), sn);
-            const float2 gcond = mul2(mul2(wsg, wsg), gg2);
-            const bool b0 = !(fabsf(dd.x) >= kTau) || !(gp2.x >= gcond.x) || !(l2.x >= kMMin) ||
-                            !(q.x >= kQMin) || !(q.x <= kQMax) || !(fabsf(th.x) <= kThMax);
-            const bool b1 = !(fabsf(dd.y) >= kTau) || !(gp2.y >= gcond.y) || !(l2.y >= kMMin) ||
-                            !(q.y >= kQMin) || !(q.y <= kQMax) || !(fabsf(th.y) <= kThMax);
-            if (b0) { wt.x = 0.0f; bad0 |= Mask(1) << n; }
-            if (b1) { wt.y = 0.0f; bad1 |= Mask(1) << n; }
-            const float2 wm = mul2(wt, rsqrt2(l2));
-            accx = fma2(wm, mx, accx);
-            accy = fma2(wm, my, accy);
-            accz = fma2(wm, mz, accz);
-        }
+    const double orx = __ldg(ray + pp), ory = __ldg(ray + HW + pp), orz = __ldg(ray + 2 * HW + pp);
+    double ax = 0.0, ay = 0.0, az = 0.0;
+    while (m != 0) {
+        int n;
+        if constexpr (sizeof(Mask) == 4) n = __ffs(m) - 1;
+        else n = __ffsll((long long)m) - 1;
+        m &= m - 1;
+        const int ky = n / PS, kx = n - (n / PS) * PS;
+        const int sy = clampi(y - a.R + ky * a.dil, 0, a.H - 1);
+        const int sx = clampi(x - a.R + kx * a.dil, 0, a.W - 1);
+        const long sp = (long)sy * a.W + sx;
+        double nx = St<TNI>::ld(pnb + sp), ny = St<TNI>::ld(pnb + HW + sp),
+               nz = St<TNI>::ld(pnb + 2 * HW + sp);
+        if (FUSE_RR)
+            ray_relu_exact(nx, ny, nz, __ldg(ray + sp), __ldg(ray + HW + sp),
+                           __ldg(ray + 2 * HW + sp));
+        const double3 c3 = angmf_neighbor_exact(
+            nx, ny, nz, sx, sy, St<TS>::ld(xyb + (long)n * HW + pp),
+            St<TS>::ld(xyb + (long)(P + n) * HW + pp), St<TS>::ld(anb + (long)n * HW + pp),
+            St<TS>::ld(prb + (long)n * HW + pp), orx, ory, orz, a.fu, a.cu, a.fv, a.cv);
+        ax += c3.x;
+        ay += c3.y;
+        az += c3.z;
     }
+    return make_float3((float)ax, (float)ay, (float)az);
+}
 
-    // ---- rare exact fix-ups
-    if ((bad0 | bad1) != 0) {
-        const TNI* pnx = pnb;
-#pragma unroll 1
-        for (int e = 0; e < 2; ++e) {
-            Mask m = e == 0 ? bad0 : bad1;
-            if (e == 1 && !two) m = 0;
-            const long pp = e == 0 ? p0 : p1;
-            const int xx = x + e;
-            const double orx = __ldg(ray + pp), ory = __ldg(ray + HW + pp),
-                         orz = __ldg(ray + 2 * HW + pp);
-            double ax = 0.0, ay = 0.0, az = 0.0;
-            while (m != 0) {
-                int n;
-                if constexpr (sizeof(Mask) == 4) n = __ffs(m) - 1;
-                else n = __ffsll((long long)m) - 1;
-                m &= m - 1;
-                const int ky = n / PS, kx = n - (n / PS) * PS;
-                const int sy = clampi(y - R + ky * a.dil, 0, a.H - 1);
-                const int sx = clampi(xx - R + kx * a.dil, 0, a.W - 1);
-                const long sp = (long)sy * a.W + sx;
-                double nx = St<TNI>::ld(pnx + sp), ny = St<TNI>::ld(pnx + HW + sp),
-                       nz = St<TNI>::ld(pnx + 2 * HW + sp);
-                if (FUSE_RR)
-                    ray_relu_exact(nx, ny, nz, __ldg(ray + sp), __ldg(ray + HW + sp),
-                                   __ldg(ray + 2 * HW + sp));
-                const double3 c3 = angmf_neighbor_exact(
-                    nx, ny, nz, sx, sy, St<TS>::ld(xyb + (long)n * HW + pp),
-                    St<TS>::ld(xyb + (long)(P + n) * HW + pp), St<TS>::ld(anb + (long)n * HW + pp),
-                    St<TS>::ld(prb + (long)n * HW + pp), orx, ory, orz, a.fu, a.cu, a.fv, a.cv);
-                ax += c3.x;
-                ay += c3.y;
-                az += c3.z;
-            }
-            if (e == 0) {
-                accx.x += (float)ax;
-                accy.x += (float)ay;
-                accz.x += (float)az;
-            } else {
-                accx.y += (float)ax;
-                accy.y += (float)ay;
-                accz.y += (float)az;
-            }
-        }
+// Normalise the pair's sums (after fix-ups) and store.
+template <int PS, typename TS, typename TNI, typename TNO, bool FUSE_RR, typename Mask>
+__device__ __forceinline__ void finish_pair(PairAcc<Mask>& A, int b, int x, int y, bool two,
+                                            bool vec, const TNI* pn, const TS* prob,
+                                            const TS* xy, const TS* ang, const float* ray,
+                                            TNO* out, const AngmfArgs& a) {
+    if (A.bad0 != 0) {
+        const float3 f = fixups<PS, TS, TNI, FUSE_RR>(A.bad0, b, x, y, pn, prob, xy, ang, ray, a);
+        A.x.x += f.x;
+        A.y.x += f.y;
+        A.z.x += f.z;
     }
-
-    // ---- normalise and store
-    const float2 l = fma2(accx, accx, fma2(accy, accy, mul2(accz, accz)));
+    if (two && A.bad1 != 0) {
+        const float3 f =
+            fixups<PS, TS, TNI, FUSE_RR>(A.bad1, b, x + 1, y, pn, prob, xy, ang, ray, a);
+        A.x.y += f.x;
+        A.y.y += f.y;
+        A.z.y += f.z;
+    }
+    const float2 l = fma2(A.x, A.x, fma2(A.y, A.y, mul2(A.z, A.z)));
     const float2 inv = rsqrt2(max2(l, f2(1e-24f)));
-    const float2 ox = mul2(accx, inv), oy = mul2(accy, inv), oz = mul2(accz, inv);
+    const float2 ox = mul2(A.x, inv), oy = mul2(A.y, inv), oz = mul2(A.z, inv);
+    const long HW = a.HW;
+    const long p0 = (long)y * a.W + x;
     TNO* ob = out + (long)b * 3 * HW;
     if (vec) {
         St<TNO>::st2(ob + p0, ox);
@@ -443,11 +479,243 @@ angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* 
         St<TNO>::st(ob + HW + p0, oy.x);
         St<TNO>::st(ob + 2 * HW + p0, oz.x);
         if (two) {
-            St<TNO>::st(ob + p1, ox.y);
-            St<TNO>::st(ob + HW + p1, oy.y);
-            St<TNO>::st(ob + 2 * HW + p1, oz.y);
+            St<TNO>::st(ob + p0 + 1, ox.y);
+            St<TNO>::st(ob + HW + p0 + 1, oy.y);
+            St<TNO>::st(ob + 2 * HW + p0 + 1, oz.y);
         }
     }
+}
+
+__device__ __forceinline__ void pair_ray(const float* __restrict__ ray, long HW, long p0, long p1,
+                                         float2& rx, float2& ry, float2& rz) {
+    rx = f2(__ldg(ray + p0), __ldg(ray + p1));
+    ry = f2(__ldg(ray + HW + p0), __ldg(ray + HW + p1));
+    rz = f2(__ldg(ray + 2 * HW + p0), __ldg(ray + 2 * HW + p1));
+    const float2 ri = rsqrt2(max2(fma2(rx, rx, fma2(ry, ry, mul2(rz, rz))), f2(1e-16f)));
+    rx = mul2(rx, ri);
+    ry = mul2(ry, ri);
+    rz = mul2(rz, ri);
+}
+
+__device__ __forceinline__ void tile_of(const AngmfArgs& a, int& b, int& x0, int& y0) {
+    int t = blockIdx.x;
+    const int tix = t % a.tiles_x;
+    t /= a.tiles_x;
+    const int tiy = t % a.tiles_y;
+    b = t / a.tiles_y;
+    x0 = tix * kTW;
+    y0 = tiy * kTH;
+}
+
+// ---------------------------------------------------------------------------
+// General kernel: per-neighbour channels read straight from global memory.
+// Any shape; used when the width does not allow 16-byte staged copies.
+template <int PS, typename TS, typename TNI, typename TNO, bool FUSE_RR>
+__global__ void __launch_bounds__(kThreads, 2)
+angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* __restrict__ xy,
+             const TS* __restrict__ ang, const float* __restrict__ ray, TNO* __restrict__ out,
+             const AngmfArgs a) {
+    constexpr int P = PS * PS;
+    using Mask = typename std::conditional<(P <= 32), uint32_t, unsigned long long>::type;
+    extern __shared__ float4 smem4[];
+    NTile T;
+    T.carve(smem4, kTW + 2 * a.R, kTH + 2 * a.R);
+    int b, x0, y0;
+    tile_of(a, b, x0, y0);
+    const long HW = a.HW;
+    stage_normals<TNI, FUSE_RR>(pn + (long)b * 3 * HW, ray, T, x0, y0, a);
+    __syncthreads();
+
+    const int lx = 2 * (threadIdx.x % (kTW / 2));
+    const int ly = threadIdx.x / (kTW / 2);
+    const int x = x0 + lx, y = y0 + ly;
+    if (y >= a.H || x >= a.W) return;
+    const bool two = x + 1 < a.W;
+    const bool vec = (a.W & 1) == 0;
+    const long p0 = (long)y * a.W + x;
+    const long p1 = two ? p0 + 1 : p0;
+    float2 rx, ry, rz;
+    pair_ray(ray, HW, p0, p1, rx, ry, rz);
+    const TS* xyb = xy + (long)b * 2 * P * HW;
+    const TS* prb = prob + (long)b * P * HW;
+    const TS* anb = ang + (long)b * P * HW;
+    auto ld = [&](const TS* base) -> float2 {
+        return vec ? St<TS>::ld2s(base + p0) : f2(St<TS>::lds1(base + p0), St<TS>::lds1(base + p1));
+    };
+    const float2 ifu2 = f2(a.ifu), ifv2 = f2(a.ifv), nifu2 = f2(-a.ifu), nifv2 = f2(-a.ifv);
+    PairAcc<Mask> A{f2(0.f), f2(0.f), f2(0.f), 0, 0};
+#pragma unroll 1
+    for (int ky = 0; ky < PS; ++ky) {
+        const int i = ly + ky * a.dil;
+#pragma unroll
+        for (int kx = 0; kx < PS; ++kx) {
+            const int n = ky * PS + kx;
+            const NPair q = npair(T, i, lx + kx * a.dil);
+            angmf_pair<Mask>(n, ld(xyb + (long)n * HW), ld(xyb + (long)(P + n) * HW),
+                             ld(anb + (long)n * HW), ld(prb + (long)n * HW), q.nx, q.ny, q.nz,
+                             q.tu, q.tun, q.tv, ifu2, ifv2, nifu2, nifv2, rx, ry, rz, A);
+        }
+    }
+    finish_pair<PS, TS, TNI, TNO, FUSE_RR>(A, b, x, y, two, vec, pn, prob, xy, ang, ray, out, a);
+}
+
+// ---------------------------------------------------------------------------
+// Staged kernel (width a multiple of 16 bytes of storage, dilation 1 or 2).
+// Each warp owns two rows of the tile; for every neighbour slot n it copies
+// exactly the data its own lanes will consume -- the four channel strips
+// (prob, x offset, y offset, angle; 2 rows x 32 pixels each) -- global ->
+// shared with 16-byte cp.async into a warp-private ring of kN = kM * PS
+// slots, kN-1 slots ahead of the one being computed. Memory latency is covered
+// by the copies in flight instead of registers, and publishing a slot needs
+// only a warp barrier. With the window size, the dilation and the window
+// column compile-time constants, every shared-memory offset is an immediate.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+template <typename TS, int PS>
+struct Stages {
+    static constexpr int kEpc = 16 / (int)sizeof(TS);     // elements per 16-byte chunk
+    static constexpr int kCpr = kTW / kEpc;                // chunks per strip row
+    static constexpr int kRowsW = 2;                       // tile rows per warp
+    static constexpr int kChunksW = 4 * kRowsW * kCpr;     // per warp per slot
+    static constexpr int kPerLane = kChunksW / 32;         // 1 (fp16) or 2 (fp32)
+    static constexpr int kElemsW = 4 * kRowsW * kTW;       // per warp per slot
+    static constexpr int kM = (sizeof(TS) == 4 && PS == 7) ? 1 : 2;  // window rows per ring
+    static constexpr int kN = kM * PS;                     // ring depth
+    static constexpr size_t kBytes = (size_t)(kThreads / 32) * kN * kElemsW * sizeof(TS);
+};
+
+template <typename TS> __device__ __forceinline__ float2 lds2(const TS* p);
+template <> __device__ __forceinline__ float2 lds2<float>(const float* p) {
+    return *reinterpret_cast<const float2*>(p);
+}
+template <> __device__ __forceinline__ float2 lds2<__half>(const __half* p) {
+    return __half22float2(*reinterpret_cast<const __half2*>(p));
+}
+
+template <int PS, int DIL, typename TS, typename TNI, typename TNO, bool FUSE_RR>
+__global__ void __launch_bounds__(kThreads, 2)
+angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
+                    const TS* __restrict__ xy, const TS* __restrict__ ang,
+                    const float* __restrict__ ray, TNO* __restrict__ out, const AngmfArgs a) {
+    constexpr int P = PS * PS;
+    constexpr int R = (PS / 2) * DIL;
+    constexpr int SW = kTW + 2 * R, SH = kTH + 2 * R;
+    constexpr int SWH = NTile::pairs_per_row(SW);
+    using Mask = typename std::conditional<(P <= 32), uint32_t, unsigned long long>::type;
+    using S = Stages<TS, PS>;
+    extern __shared__ float4 smem4[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    TS* ring = reinterpret_cast<TS*>(smem4) + warp * S::kN * S::kElemsW;  // this warp's slots
+    NTile T;
+    T.carve(reinterpret_cast<char*>(smem4) + S::kBytes, SW, SH);
+    int b, x0, y0;
+    tile_of(a, b, x0, y0);
+    const long HW = a.HW;
+    const TS* xyb = xy + (long)b * 2 * P * HW;
+    const TS* prb = prob + (long)b * P * HW;
+    const TS* anb = ang + (long)b * P * HW;
+
+    // this lane's chunks: source of the next slot to issue, slot offset, validity
+    const TS* src[S::kPerLane];
+    int dst[S::kPerLane];
+    bool valid[S::kPerLane];
+#pragma unroll
+    for (int k = 0; k < S::kPerLane; ++k) {
+        const int q = lane + 32 * k;
+        const int c = q / (S::kRowsW * S::kCpr);
+        const int r = (q / S::kCpr) % S::kRowsW;
+        const int cc = q % S::kCpr;
+        const TS* base = c == 0 ? prb : c == 1 ? xyb : c == 2 ? xyb + (long)P * HW : anb;
+        const int gy = y0 + S::kRowsW * warp + r, gx = x0 + cc * S::kEpc;
+        valid[k] = gy < a.H && gx < a.W;
+        src[k] = valid[k] ? base + (long)gy * a.W + gx : base;
+        dst[k] = (c * S::kRowsW + r) * kTW + cc * S::kEpc;
+    }
+    auto issue = [&](int slot) {
+        TS* sl = ring + slot * S::kElemsW;
+#pragma unroll
+        for (int k = 0; k < S::kPerLane; ++k) {
+            cp_async16(sl + dst[k], src[k], valid[k]);
+            if (valid[k]) src[k] += HW;  // the same strip of the next neighbour slot
+        }
+    };
+
+    // prologue: the first kN-1 slots in flight while the normals are staged
+#pragma unroll
+    for (int sl = 0; sl < S::kN - 1; ++sl) {
+        if (sl < P) issue(sl);
+        cp_async_commit();
+    }
+    stage_normals<TNI, FUSE_RR>(pn + (long)b * 3 * HW, ray, T, x0, y0, a);
+    __syncthreads();  // the normal halo is shared by all warps
+
+    const int lx = 2 * (lane & 15);
+    const int ly = S::kRowsW * warp + (lane >> 4);
+    const int x = x0 + lx, y = y0 + ly;
+    const bool active = y < a.H && x < a.W;
+    const bool two = x + 1 < a.W;
+    const long p0 = (long)min(y, a.H - 1) * a.W + min(x, a.W - 1);
+    const long p1 = two ? p0 + 1 : p0;
+    float2 rx, ry, rz;
+    pair_ray(ray, HW, p0, p1, rx, ry, rz);
+    const float2 ifu2 = f2(a.ifu), ifv2 = f2(a.ifv), nifu2 = f2(-a.ifu), nifv2 = f2(-a.ifv);
+    PairAcc<Mask> A{f2(0.f), f2(0.f), f2(0.f), 0, 0};
+    constexpr int kStrip = S::kRowsW * kTW;
+    const TS* ring_lane = ring + (lane >> 4) * kTW + lx;   // this pair inside a slot
+    const int pbase = ly * SWH + (lx >> 1);                // this pair's first window pair
+
+#pragma unroll 1
+    for (int ky = 0; ky < PS; ++ky) {
+        const int grp = (S::kM == 2) ? (ky & 1) * PS : 0;  // slot group of this window row
+        const int prev_grp = (S::kM == 2) ? PS - grp : 0;  // ... of the previous row
+        const TS* st_row = ring_lane + grp * S::kElemsW;
+        const int prow = pbase + ky * DIL * SWH;
+        const float2 tv = f2(T.tv[ly + ky * DIL]);
+#pragma unroll
+        for (int kx = 0; kx < PS; ++kx) {
+            const int n = ky * PS + kx;
+            cp_async_wait<S::kN - 2>();
+            __syncwarp();  // slot n visible to the warp; every lane is done with slot n-1
+            if (n + S::kN - 1 < P) issue(kx > 0 ? grp + kx - 1 : prev_grp + PS - 1);
+            cp_async_commit();
+            if (active) {
+                const TS* st = st_row + kx * S::kElemsW;
+                // window column offset: a constant once the kx loop is unrolled
+                const int dj = kx * DIL;
+                const int pi = prow + (dj >> 1);
+                float2 nx, ny, nz, tu, tun;
+                if ((dj & 1) == 0) {
+                    nx = T.e[0][pi];
+                    ny = T.e[1][pi];
+                    nz = T.e[2][pi];
+                    const float4 t4 = T.tue[(lx >> 1) + (dj >> 1)];
+                    tu = f2(t4.x, t4.y);
+                    tun = f2(t4.z, t4.w);
+                } else {
+                    nx = T.o[0][pi];
+                    ny = T.o[1][pi];
+                    nz = T.o[2][pi];
+                    const float4 t4 = T.tuo[(lx >> 1) + (dj >> 1)];
+                    tu = f2(t4.x, t4.y);
+                    tun = f2(t4.z, t4.w);
+                }
+                angmf_pair<Mask>(n, lds2<TS>(st + 1 * kStrip), lds2<TS>(st + 2 * kStrip),
+                                 lds2<TS>(st + 3 * kStrip), lds2<TS>(st), nx, ny, nz, tu, tun,
+                                 tv, ifu2, ifv2, nifu2, nifv2, rx, ry, rz, A);
+            }
+        }
+    }
+    cp_async_wait<0>();
+    if (!active) return;
+    finish_pair<PS, TS, TNI, TNO, FUSE_RR>(A, b, x, y, two, true, pn, prob, xy, ang, ray, out, a);
 }
 
 template <int PS, typename TS, typename TNI, typename TNO, bool FUSE_RR>
@@ -469,17 +737,32 @@ cudaError_t launch_t(const AngmfLaunch& L, cudaStream_t s) {
     a.cu = L.cu;
     a.fv = L.fv;
     a.cv = L.cv;
-    const int SW = kTW + 2 * a.R, SH = kTH + 2 * a.R;
-    const size_t smem = sizeof(float2) * (3 * (size_t)SH * SW + SW) + sizeof(float) * SH;
-    auto kern = angmf_kernel<PS, TS, TNI, TNO, FUSE_RR>;
-    if (smem > 48 * 1024) {
+    const size_t nsmem = NTile::bytes(kTW + 2 * a.R, kTH + 2 * a.R);
+    const long blocks = (long)a.tiles_x * a.tiles_y * L.B;
+    if (blocks > 0x7fffffffL) return cudaErrorInvalidConfiguration;
+    // staged copies need every 16-byte chunk of a row to start on a 16-byte
+    // boundary (W a multiple of 16 bytes of storage); dilations 1 and 2 (the
+    // benchmark windows) have compile-time staged variants
+    if ((L.W % Stages<TS, PS>::kEpc) == 0 && (L.dil == 1 || L.dil == 2)) {
+        const size_t smem = Stages<TS, PS>::kBytes + nsmem;
+        auto kern = L.dil == 1 ? angmf_staged_kernel<PS, 1, TS, TNI, TNO, FUSE_RR>
+                               : angmf_staged_kernel<PS, 2, TS, TNI, TNO, FUSE_RR>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
         if (e != cudaSuccess) return e;
+        kern<<<(unsigned)blocks, kThreads, smem, s>>>(
+            static_cast<const TNI*>(L.pn), static_cast<const TS*>(L.prob),
+            static_cast<const TS*>(L.xy), static_cast<const TS*>(L.angle), L.ray,
+            static_cast<TNO*>(L.out), a);
+        return cudaGetLastError();
     }
-    const long blocks = (long)a.tiles_x * a.tiles_y * L.B;
-    if (blocks > 0x7fffffffL) return cudaErrorInvalidConfiguration;
-    kern<<<(unsigned)blocks, kThreads, smem, s>>>(
+    auto kern = angmf_kernel<PS, TS, TNI, TNO, FUSE_RR>;
+    if (nsmem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)nsmem);
+        if (e != cudaSuccess) return e;
+    }
+    kern<<<(unsigned)blocks, kThreads, nsmem, s>>>(
         static_cast<const TNI*>(L.pn), static_cast<const TS*>(L.prob),
         static_cast<const TS*>(L.xy), static_cast<const TS*>(L.angle), L.ray,
         static_cast<TNO*>(L.out), a);

@@ -32,7 +32,23 @@ __device__ __forceinline__ float2 max2(float2 a, float2 b) {
     return make_float2(fmaxf(a.x, b.x), fmaxf(a.y, b.y));
 }
 __device__ __forceinline__ float2 rsqrt2(float2 a) { return make_float2(rsqrtf(a.x), rsqrtf(a.y)); }
+// 1/sqrt(x) with the hardware approximation (PTX rsqrt.approx.ftz.f32, ~2 ulp):
+// for arguments known to be normal numbers (clamped or range-checked).
+__device__ __forceinline__ float rsqrt_ftz(float x) {
+    float y;
+    asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float2 rsqrt2_ftz(float2 a) { return make_float2(rsqrt_ftz(a.x), rsqrt_ftz(a.y)); }
 __device__ __forceinline__ float2 ex2_2(float2 a) { return make_float2(exp2f(a.x), exp2f(a.y)); }
+// 2^x with the hardware approximation (PTX ex2.approx.ftz.f32): results below
+// 2^-126 flush to zero, which is harmless where x <= 0 feeds a softmax.
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float2 ex2_ftz2(float2 a) { return make_float2(ex2_ftz(a.x), ex2_ftz(a.y)); }
 
 // -------------------------------------------------------------- storage types
 template <typename T> struct St;

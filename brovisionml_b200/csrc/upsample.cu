@@ -8,13 +8,20 @@
 // five iterations although only the last result is used. Here it runs once,
 // after the last AngMF iteration.
 //
-// Work split: a CTA owns a 2 x 32 grid-pixel tile; warp k (of 8) owns
-// sub-column kx = k of every 8x8 output cell, and each lane one grid pixel
-// pair of the tile. So every mask plane (tap t, sub-row ky, sub-column kx) is
-// read as 32-pixel coalesced rows, exactly once. The pair's 3x3 source
-// normals (27 float2) stay in registers for all 64 sub-pixels. Each sub-row
-// ky of results goes through a padded shared-memory row buffer (double
-// buffered) and leaves as coalesced row segments of the output.
+// Work split: a CTA owns an 8 x 64 tile of grid pixels; each warp one grid
+// row of it, each lane one grid-pixel pair (x, x+1). A thread walks the 8
+// sub-rows ky and, inside each, the 8 sub-columns kx: for every (ky, kx) it
+// takes the pair's 9 mask logits (planes t*64 + ky*8 + kx), so after the 8
+// sub-columns it holds output row 8y+ky, columns 8x .. 8x+15, contiguous, and
+// writes them with 16-byte stores. The pair's 3x3 source normals (27 float2)
+// stay in registers for all 64 sub-pixels.
+//
+// Logit staging: when the grid width is a multiple of 16 bytes of storage,
+// each warp copies, for every (ky, kx), the 9 logit strips of its own row
+// (9 planes x 64 columns) global -> shared with 16-byte cp.async into a
+// warp-private ring kN stages deep, kN-1 ahead of the stage being computed;
+// a warp barrier publishes each stage. The bytes in flight then do not cost
+// registers. Other widths read the logits straight from global memory.
 //
 // The softmax denominator is folded into the normalise: with e_t = exp(l_t -
 // max l), normalise(sum_t (e_t/S) n_t) = a / max(|a|, 1e-12 S) for
@@ -26,50 +33,145 @@
 namespace bvml {
 namespace {
 
-constexpr int kUTW = 32;               // grid columns per tile (16 pairs)
-constexpr int kUTH = 2;                // grid rows per tile
-constexpr int kUThreads = 256;         // 8 warps (kx) x 32 lanes (2 rows x 16 pairs)
-constexpr int kRowCols = 8 * kUTW;     // output columns per tile row
-constexpr int kRowPad = kRowCols + kRowCols / 16;  // one pad word per 16 columns
+constexpr int kUTW = 64;        // grid columns per tile (32 pairs = one warp)
+constexpr int kUTH = 8;         // grid rows per tile (one per warp)
+constexpr int kUThreads = 256;
+
+template <typename TS>
+struct UpStages {
+    static constexpr int kEpc = 16 / (int)sizeof(TS);             // elements per chunk
+    static constexpr int kCpr = kUTW / kEpc;                      // chunks per strip
+    static constexpr int kChunksW = 9 * kCpr;                     // per warp per stage
+    static constexpr int kElemsW = 9 * kUTW;                      // per warp per stage
+    static constexpr int kN = 4;                                  // ring depth
+    static constexpr size_t kBytes = (size_t)(kUThreads / 32) * kN * kElemsW * sizeof(TS);
+};
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+// Logits of a pixel pair in storage form: half2 for fp16 storage (their max is
+// taken packed, exactly, before any conversion), float2 for fp32.
+template <typename TS> struct Logit;
+template <> struct Logit<float> {
+    using T = float2;
+    __device__ __forceinline__ static T lds(const float* p) { return *reinterpret_cast<const float2*>(p); }
+    __device__ __forceinline__ static T ldg(const float* p, long d1, bool vec) {
+        return vec ? St<float>::ld2s(p) : f2(St<float>::lds1(p), St<float>::lds1(p + d1));
+    }
+    __device__ __forceinline__ static T mx(T a, T b) { return max2(a, b); }
+    __device__ __forceinline__ static float2 f(T v) { return v; }
+};
+template <> struct Logit<__half> {
+    using T = __half2;
+    __device__ __forceinline__ static T lds(const __half* p) { return *reinterpret_cast<const __half2*>(p); }
+    __device__ __forceinline__ static T ldg(const __half* p, long d1, bool vec) {
+        return vec ? __ldcs(reinterpret_cast<const __half2*>(p)) : __halves2half2(__ldcs(p), __ldcs(p + d1));
+    }
+    __device__ __forceinline__ static T mx(T a, T b) { return __hmax2(a, b); }
+    __device__ __forceinline__ static float2 f(T v) { return __half22float2(v); }
+};
+
+// A lane's share of one stage: chunks q = lane + 32 m (m < kPerLane) of the
+// 9 x kCpr chunk grid. Because 32 is a multiple of kCpr, a lane keeps one
+// column cc for all its chunks and its plane advances by 32 / kCpr per m, so
+// only a base offset, a column validity flag and a plane stride are kept.
+template <typename TS>
+struct LaneChunks {
+    using U = UpStages<TS>;
+    static constexpr int kPerLane = (U::kChunksW + 31) / 32;
+    static constexpr int kTStep = 32 / U::kCpr;   // planes between a lane's chunks
+    int off0;       // element offset of chunk m = 0 from the stage's plane-0 row
+    int doff0;      // its offset inside a warp slot
+    int tstep_hw;   // 64 * kTStep * hw: source distance between consecutive m
+    int nlast;      // chunks this lane has (kPerLane or kPerLane - 1)
+    bool col_ok;    // the lane's column lies inside the frame
+    __device__ void init(int lane, int ncols, long hw) {
+        const int t0 = lane / U::kCpr, cc = lane % U::kCpr;
+        off0 = t0 * 64 * (int)hw + cc * U::kEpc;
+        doff0 = t0 * kUTW + cc * U::kEpc;
+        tstep_hw = 64 * kTStep * (int)hw;
+        nlast = (lane + 32 * (kPerLane - 1) < U::kChunksW) ? kPerLane : kPerLane - 1;
+        col_ok = cc * U::kEpc < ncols;
+    }
+    // copy the lane's chunks of the stage whose plane-0 row starts at `src`
+    __device__ __forceinline__ void issue(TS* slot, const TS* src) const {
+        const TS* p = src + off0;
+#pragma unroll
+        for (int m = 0; m < kPerLane; ++m) {
+            if (m < nlast)
+                cp_async16(slot + doff0 + m * kTStep * kUTW, col_ok ? p : src, col_ok);
+            p += tstep_hw;
+        }
+    }
+};
 
 struct UpArgs {
     int B, h, w, tiles_x, tiles_y;
     long hw;
     int crop_t, crop_l, out_h, out_w;
-    float ifu8, ifv8, tu8_c, tv8_c;    // full-res ray: ((X+0.5)-8cu)/(8fu) = X*ifu8 + tu8_c
+    bool vec_out;                   // 16-byte aligned output runs
+    float ifu8, ifv8, tu8_c, tv8_c; // full-res ray: ((X+0.5)-8cu)/(8fu) = X*ifu8 + tu8_c
 };
 
-__device__ __forceinline__ int rb_index(int col) { return col + (col >> 4); }
+// Packs two fp32 results into one 32-bit storage word for TS = half; for
+// float the results are kept as they are.
+template <typename TS> struct OutRun;
+template <> struct OutRun<float> {
+    // 4 sub-columns x 2 pixels per channel, stored after every 4 sub-columns
+    float v[3][2][4];
+};
+template <> struct OutRun<__half> {
+    __half2 v[3][2][4];  // 8 sub-columns x 2 pixels per channel, as half pairs
+};
 
-template <typename TNI, typename TS, bool NORM, bool RR>
+template <typename TNI, typename TS, bool NORM, bool RR, bool STAGED>
 __global__ void __launch_bounds__(kUThreads, 2)
 upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __restrict__ out,
                 const UpArgs a) {
-    __shared__ float rowbuf[2][kUTH][3][kRowPad];
-
+    using U = UpStages<TS>;
+    extern __shared__ float4 up_smem[];
+    TS* ring = reinterpret_cast<TS*>(up_smem) + (threadIdx.x >> 5) * U::kN * U::kElemsW;
     int t = blockIdx.x;
     const int tix = t % a.tiles_x;
     t /= a.tiles_x;
     const int tiy = t % a.tiles_y;
     const int b = t / a.tiles_y;
-    const int x0 = tix * kUTW, y0 = tiy * kUTH;
-
     const int lane = threadIdx.x & 31;
-    const int kx = threadIdx.x >> 5;
-    const int lr = lane >> 4;            // tile row
-    const int lp = lane & 15;            // pair index
-    const int y = y0 + lr, x = x0 + 2 * lp;
-    const bool active = (y < a.h) && (x < a.w);
+    const int x0 = tix * kUTW, y0 = tiy * kUTH;
+    const int y = y0 + (threadIdx.x >> 5);
+    const int x = x0 + 2 * lane;
+    const bool active = y < a.h && x < a.w;
+    // only warp barriers below: a warp past the last row, or (unstaged) a
+    // lane past the last column, can leave now
+    if (y >= a.h || (!STAGED && !active)) return;
     const long hw = a.hw;
-    const bool vec = (a.w & 1) == 0;
-    // Lanes past the frame edge compute on clamped (valid) pixels and are not
-    // stored. With even w the clamp keeps the pair start even, so the paired
-    // loads below stay 8/4-byte aligned.
+    const TS* mframe = mask + (long)b * 576 * hw;
+    const TS* mrow = mframe + (long)y * a.w + x0;  // plane 0 of this warp's row
+    LaneChunks<TS> lc;
+    const TS* mnext = mrow;                         // plane-0 row of the next stage to copy
+    if (STAGED) {
+        lc.init(lane, a.w - x0, hw);
+#pragma unroll
+        for (int s = 0; s < U::kN - 1; ++s) {
+            lc.issue(ring + s * U::kElemsW, mnext);
+            mnext += hw;
+            cp_async_commit();
+        }
+    }
+    const bool vec = (a.w & 1) == 0;   // pairs start at even offsets: 8/4-byte aligned
     const int yc = min(y, a.h - 1);
-    const int xc0 = vec ? min(x, a.w - 2) : min(x, a.w - 1);
-    const int xc1 = min(xc0 + 1, a.w - 1);
+    const int xc = vec ? min(x, a.w - 2) : min(x, a.w - 1);
+    const int x1 = min(xc + 1, a.w - 1);
 
-    // 3x3 replicate-padded neighbourhood of the pair, per channel.
+    // 3x3 replicate-padded neighbourhood of the pair, per channel
     const TNI* nb = nrm + (long)b * 3 * hw;
     float2 N[9][3];
 #pragma unroll
@@ -77,121 +179,179 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
         const long row = (long)clampi(yc + ty - 1, 0, a.h - 1) * a.w;
 #pragma unroll
         for (int tx = 0; tx < 3; ++tx) {
-            const long c0 = row + clampi(xc0 + tx - 1, 0, a.w - 1);
-            const long c1 = row + clampi(xc1 + tx - 1, 0, a.w - 1);
+            const long c0 = row + clampi(xc + tx - 1, 0, a.w - 1);
+            const long c1 = row + clampi(x1 + tx - 1, 0, a.w - 1);
 #pragma unroll
             for (int c = 0; c < 3; ++c)
                 N[ty * 3 + tx][c] = f2(St<TNI>::ld(nb + c * hw + c0), St<TNI>::ld(nb + c * hw + c1));
         }
     }
 
-    const TS* mb = mask + (long)b * 576 * hw + (long)yc * a.w + xc0;
-    const long pofs1 = xc1 - xc0;
+    const TS* mb = mframe + (long)yc * a.w + xc;
+    const long d1 = x1 - xc;
     constexpr float kL2E = 1.4426950408889634f;
+    using L = Logit<TS>;
+    const int so = 2 * lane;  // pair offset in a staged strip
 
 #pragma unroll 1
     for (int ky = 0; ky < 8; ++ky) {
-        float2 l[9];
+        const int Yo = 8 * y + ky - a.crop_t;
+        const bool row_in = Yo >= 0 && Yo < a.out_h;
+        OutRun<TS> run;
 #pragma unroll
-        for (int tp = 0; tp < 9; ++tp) {
-            const TS* pch = mb + (long)(tp * 64 + ky * 8 + kx) * hw;
-            l[tp] = vec ? St<TS>::ld2s(pch) : f2(St<TS>::lds1(pch), St<TS>::lds1(pch + pofs1));
-        }
-        float2 m = l[0];
+        for (int kx = 0; kx < 8; ++kx) {
+            typename L::T l[9];
+            if (STAGED) {
+                const int k = ky * 8 + kx;
+                cp_async_wait<U::kN - 2>();
+                __syncwarp();  // stage k visible to the warp; every lane done with k-1
+                if (k + U::kN - 1 < 64) {
+                    lc.issue(ring + ((k + U::kN - 1) % U::kN) * U::kElemsW, mnext);
+                    mnext += hw;
+                }
+                cp_async_commit();
+                const TS* st = ring + (k % U::kN) * U::kElemsW + so;
 #pragma unroll
-        for (int tp = 1; tp < 9; ++tp) m = max2(m, l[tp]);
-        const float2 mo = mul2(m, f2(-kL2E));
-        float2 S = f2(0.f), ax = f2(0.f), ay = f2(0.f), az = f2(0.f);
-#pragma unroll
-        for (int tp = 0; tp < 9; ++tp) {
-            const float2 e = ex2_2(fma2(l[tp], f2(kL2E), mo));
-            S = add2(S, e);
-            ax = fma2(e, N[tp][0], ax);
-            ay = fma2(e, N[tp][1], ay);
-            az = fma2(e, N[tp][2], az);
-        }
-        float2 ox, oy, oz;
-        if (NORM) {
-            const float2 l2 = fma2(ax, ax, fma2(ay, ay, mul2(az, az)));
-            const float2 se = mul2(S, f2(1e-12f));
-            const float2 inv = rsqrt2(max2(l2, mul2(se, se)));
-            ox = mul2(ax, inv);
-            oy = mul2(ay, inv);
-            oz = mul2(az, inv);
-        } else {
-            const float2 inv = f2(1.0f / S.x, 1.0f / S.y);
-            ox = mul2(ax, inv);
-            oy = mul2(ay, inv);
-            oz = mul2(az, inv);
-        }
-        if (RR) {
-            // full-res ray at (8y+ky, 8x+kx) and (8y+ky, 8x+8+kx)
-            const float Yf = (float)(8 * y + ky);
-            const float X0 = (float)(8 * x + kx);
-            float2 rx = f2(fmaf(X0, a.ifu8, a.tu8_c), fmaf(X0 + 8.0f, a.ifu8, a.tu8_c));
-            float2 ry = f2(fmaf(Yf, a.ifv8, a.tv8_c));
-            const float2 ri = rsqrt2(fma2(rx, rx, fma2(ry, ry, f2(1.0f))));
-            rx = mul2(rx, ri);
-            ry = mul2(ry, ri);
-            const float2 rz = ri;
-            const float2 nn2 = fma2(ox, ox, fma2(oy, oy, mul2(oz, oz)));
-            const float2 c = mul2(fma2(ox, rx, fma2(oy, ry, mul2(oz, rz))),
-                                  rsqrt2(max2(nn2, f2(1e-16f))));
-            const float2 dc = max2(fnma2(c, f2(1.0f), f2(kRayEps)), f2(0.0f));
-            ox = fma2(rx, dc, ox);
-            oy = fma2(ry, dc, oy);
-            oz = fma2(rz, dc, oz);
-            const float2 inv = rsqrt2(max2(fma2(ox, ox, fma2(oy, oy, mul2(oz, oz))), f2(1e-24f)));
-            ox = mul2(ox, inv);
-            oy = mul2(oy, inv);
-            oz = mul2(oz, inv);
-        }
-        float(*rb)[3][kRowPad] = rowbuf[ky & 1];
-        const int c0 = rb_index(16 * lp + kx), c1 = rb_index(16 * lp + 8 + kx);
-        rb[lr][0][c0] = ox.x;
-        rb[lr][1][c0] = oy.x;
-        rb[lr][2][c0] = oz.x;
-        rb[lr][0][c1] = ox.y;
-        rb[lr][1][c1] = oy.y;
-        rb[lr][2][c1] = oz.y;
-        __syncthreads();
-
-        // write-out: kUTH rows x 3 channels x kRowCols columns, in column pairs
-        const int X0 = 8 * x0 - a.crop_l;
-        const bool vout = ((a.out_w & 1) == 0) && ((a.crop_l & 1) == 0);
-        constexpr int kChunks = kUTH * 3 * kRowCols / 2;
-#pragma unroll 1
-        for (int ch = threadIdx.x; ch < kChunks; ch += kUThreads) {
-            const int cp = ch % (kRowCols / 2);
-            const int rc = ch / (kRowCols / 2);
-            const int c = rc % 3;
-            const int r = rc / 3;
-            const int gy = y0 + r;
-            if (gy >= a.h) continue;
-            const int Yo = 8 * gy + ky - a.crop_t;
-            if (Yo < 0 || Yo >= a.out_h) continue;
-            const int col = 2 * cp;
-            const int Xo = X0 + col;
-            if (8 * (x0 + (col >> 3)) >= 8 * a.w) continue;  // beyond the grid's last column
-            const float v0 = rb[r][c][rb_index(col)], v1 = rb[r][c][rb_index(col + 1)];
-            TS* orow = out + (((long)b * 3 + c) * a.out_h + Yo) * (long)a.out_w;
-            if (vout && Xo >= 0 && Xo + 1 < a.out_w) {
-                St<TS>::st2(orow + Xo, f2(v0, v1));
+                for (int tp = 0; tp < 9; ++tp) l[tp] = L::lds(st + tp * kUTW);
             } else {
-                if (Xo >= 0 && Xo < a.out_w) St<TS>::st(orow + Xo, v0);
-                if (Xo + 1 >= 0 && Xo + 1 < a.out_w) St<TS>::st(orow + Xo + 1, v1);
+#pragma unroll
+                for (int tp = 0; tp < 9; ++tp)
+                    l[tp] = L::ldg(mb + (long)(tp * 64 + ky * 8 + kx) * hw, d1, vec);
+            }
+            if (!active) continue;  // staged mode: idle lanes only keep the warp barriers
+            const float2 m = L::f(L::mx(L::mx(L::mx(l[0], l[1]), L::mx(l[2], l[3])),
+                                        L::mx(L::mx(l[4], l[5]), L::mx(L::mx(l[6], l[7]), l[8]))));
+            const float2 mo = mul2(m, f2(-kL2E));
+            float2 S = f2(0.f), ax = f2(0.f), ay = f2(0.f), az = f2(0.f);
+#pragma unroll
+            for (int tp = 0; tp < 9; ++tp) {
+                const float2 e = ex2_ftz2(fma2(L::f(l[tp]), f2(kL2E), mo));
+                S = add2(S, e);
+                ax = fma2(e, N[tp][0], ax);
+                ay = fma2(e, N[tp][1], ay);
+                az = fma2(e, N[tp][2], az);
+            }
+            float2 ox, oy, oz;
+            if (NORM) {
+                const float2 l2 = fma2(ax, ax, fma2(ay, ay, mul2(az, az)));
+                const float2 se = mul2(S, f2(1e-12f));
+                const float2 inv = rsqrt2(max2(l2, mul2(se, se)));
+                ox = mul2(ax, inv);
+                oy = mul2(ay, inv);
+                oz = mul2(az, inv);
+            } else {
+                const float2 inv = f2(__frcp_rn(S.x), __frcp_rn(S.y));
+                ox = mul2(ax, inv);
+                oy = mul2(ay, inv);
+                oz = mul2(az, inv);
+            }
+            if (RR) {
+                // full-res ray at (8y+ky, 8x+kx) and (8y+ky, 8x+8+kx)
+                const float X0 = (float)(8 * x + kx);
+                float2 rx = f2(fmaf(X0, a.ifu8, a.tu8_c), fmaf(X0 + 8.0f, a.ifu8, a.tu8_c));
+                float2 ry = f2(fmaf((float)(8 * y + ky), a.ifv8, a.tv8_c));
+                const float2 ri = rsqrt2(fma2(rx, rx, fma2(ry, ry, f2(1.0f))));
+                rx = mul2(rx, ri);
+                ry = mul2(ry, ri);
+                const float2 rz = ri;
+                const float2 nn2 = fma2(ox, ox, fma2(oy, oy, mul2(oz, oz)));
+                const float2 c = mul2(fma2(ox, rx, fma2(oy, ry, mul2(oz, rz))),
+                                      rsqrt2(max2(nn2, f2(1e-16f))));
+                const float2 dc = max2(fma2(c, f2(-1.0f), f2(kRayEps)), f2(0.0f));
+                ox = fma2(rx, dc, ox);
+                oy = fma2(ry, dc, oy);
+                oz = fma2(rz, dc, oz);
+                const float2 inv =
+                    rsqrt2(max2(fma2(ox, ox, fma2(oy, oy, mul2(oz, oz))), f2(1e-24f)));
+                ox = mul2(ox, inv);
+                oy = mul2(oy, inv);
+                oz = mul2(oz, inv);
+            }
+            // collect; flush a 16-byte run per channel and pixel when complete
+            if constexpr (sizeof(TS) == 2) {
+                // half pairs (kx even, kx odd) per pixel
+                const float o[3][2] = {{ox.x, ox.y}, {oy.x, oy.y}, {oz.x, oz.y}};
+#pragma unroll
+                for (int c = 0; c < 3; ++c)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        if ((kx & 1) == 0)
+                            run.v[c][e][kx >> 1].x = __float2half_rn(o[c][e]);
+                        else
+                            run.v[c][e][kx >> 1].y = __float2half_rn(o[c][e]);
+                    }
+                if (kx == 7 && row_in && active) {
+                    TS* orow = out + (long)b * 3 * a.out_h * a.out_w + (long)Yo * a.out_w;
+#pragma unroll
+                    for (int c = 0; c < 3; ++c)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int X = 8 * (x + e) - a.crop_l;  // first column of the run
+                            TS* dst = orow + (long)c * a.out_h * a.out_w + X;
+                            if (e == 1 && x + 1 >= a.w) continue;
+                            if (a.vec_out && X >= 0 && X + 8 <= a.out_w) {
+                                *reinterpret_cast<uint4*>(dst) =
+                                    *reinterpret_cast<const uint4*>(&run.v[c][e][0]);
+                            } else {
+#pragma unroll
+                                for (int k = 0; k < 8; ++k) {
+                                    const __half hv = (k & 1) ? run.v[c][e][k >> 1].y
+                                                              : run.v[c][e][k >> 1].x;
+                                    if (X + k >= 0 && X + k < a.out_w) dst[k] = hv;
+                                }
+                            }
+                        }
+                }
+            } else {
+                const float o[3][2] = {{ox.x, ox.y}, {oy.x, oy.y}, {oz.x, oz.y}};
+#pragma unroll
+                for (int c = 0; c < 3; ++c)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) run.v[c][e][kx & 3] = o[c][e];
+                if ((kx & 3) == 3 && row_in && active) {
+                    TS* orow = out + (long)b * 3 * a.out_h * a.out_w + (long)Yo * a.out_w;
+#pragma unroll
+                    for (int c = 0; c < 3; ++c)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int X = 8 * (x + e) + (kx & 4) - a.crop_l;
+                            TS* dst = orow + (long)c * a.out_h * a.out_w + X;
+                            if (e == 1 && x + 1 >= a.w) continue;
+                            if (a.vec_out && X >= 0 && X + 4 <= a.out_w) {
+                                *reinterpret_cast<float4*>(dst) =
+                                    make_float4(run.v[c][e][0], run.v[c][e][1], run.v[c][e][2],
+                                                run.v[c][e][3]);
+                            } else {
+#pragma unroll
+                                for (int k = 0; k < 4; ++k)
+                                    if (X + k >= 0 && X + k < a.out_w) dst[k] = run.v[c][e][k];
+                            }
+                        }
+                }
             }
         }
     }
-    (void)active;
+    if (STAGED) cp_async_wait<0>();
 }
 
 template <typename TNI, typename TS, bool NORM, bool RR>
 cudaError_t launch_t(const UpsampleLaunch& L, const UpArgs& a, cudaStream_t s) {
     const long blocks = (long)a.tiles_x * a.tiles_y * a.B;
     if (blocks > 0x7fffffffL) return cudaErrorInvalidConfiguration;
-    upsample_kernel<TNI, TS, NORM, RR><<<(unsigned)blocks, kUThreads, 0, s>>>(
-        static_cast<const TNI*>(L.n), static_cast<const TS*>(L.mask), static_cast<TS*>(L.out), a);
+    if (a.w % UpStages<TS>::kEpc == 0) {
+        auto kern = upsample_kernel<TNI, TS, NORM, RR, true>;
+        const size_t smem = UpStages<TS>::kBytes;
+        cudaError_t e =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        kern<<<(unsigned)blocks, kUThreads, smem, s>>>(static_cast<const TNI*>(L.n),
+                                                      static_cast<const TS*>(L.mask),
+                                                      static_cast<TS*>(L.out), a);
+    } else {
+        upsample_kernel<TNI, TS, NORM, RR, false><<<(unsigned)blocks, kUThreads, 0, s>>>(
+            static_cast<const TNI*>(L.n), static_cast<const TS*>(L.mask),
+            static_cast<TS*>(L.out), a);
+    }
     return cudaGetLastError();
 }
 
@@ -218,6 +378,9 @@ cudaError_t launch_upsample(const UpsampleLaunch& L, cudaStream_t s) {
     a.crop_l = L.crop_l;
     a.out_h = L.out_h;
     a.out_w = L.out_w;
+    // 16-byte runs: 8 halves or 4 floats, every run start aligned
+    const int run = L.st == SType::F16 ? 8 : 4;
+    a.vec_out = (L.out_w % run == 0) && (L.crop_l % run == 0);
     // full-res intrinsics are 8x the grid ones (the /8 grid of a padded frame)
     a.ifu8 = (float)(1.0 / (8.0 * L.fu));
     a.ifv8 = (float)(1.0 / (8.0 * L.fv));
