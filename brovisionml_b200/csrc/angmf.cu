@@ -12,7 +12,7 @@
 //    coalesced pixel pairs, evict-first;
 //  * fp32 arithmetic carried two pixels at a time in packed f32x2 form, using
 //    a closed form of the reference's per-neighbour geometry (below) that
-//    needs no division, no fp64 and no transcendental beyond three rsqrt;
+//    needs no division and no fp64: three rsqrt and one sin / cos pair;
 //  * an exact fp64 fix-up, identical in arithmetic to the reference
 //    (src/dsine_ops.cpp:110-162), for the rare neighbours whose fp32
 //    evaluation would be ill-conditioned or out of range.
@@ -28,20 +28,21 @@
 // xy pair can be used for it: g ~ (ys/fv, -xs/fu, xs tv0/fu - ys tu0/fv);
 // only dd needs the normalised pair (one rsqrt). The quaternion route of
 // axis_angle_to_matrix (src/dsine_ops.cpp:31-51) computes the same rotation.
-// sin and cos come from the half-angle Taylor series (6 terms each, error
-// < 1e-8 on |theta| <= pi), not from library code.
+// sin and cos come from the hardware approximations (sin.approx / cos.approx,
+// absolute error ~5e-7 on |theta| <= pi).
 //
 // Fix-up criteria (per pixel, per neighbour), each a place where the fp32
 // evaluation can leave the reference's fp64 result by more than ~1e-6:
 //  * |dd| < 1e-5: the sign of dd (which flips the rotation) may be wrong in
 //    fp32, and the reference clamps |dd| < 1e-8;
-//  * w |sin(theta)| |g| > 10 |g_perp|: g nearly parallel to n, so the rotation
+//  * w |sin(theta)| |g| > 20 |g_perp|: g nearly parallel to n, so the rotation
 //    direction comes from a cancellation; its fp32 error (~2e-7 |g|/|g_perp|)
 //    is only tolerable while the neighbour's weighted sine is small;
-//  * |m|^2 < 1e-2 after the RayReLU: the rotated normal points almost straight
+//  * |m|^2 < 0.04 after the RayReLU: the rotated normal points almost straight
 //    away from the camera and the clamped vector is a cancellation too;
 //  * |xy|^2 outside [1e-10, 1e30] (the reference's 1e-12 clamp on |xy|, or
-//    fp32 overflow), |theta| > 3.2 (outside the series' range), or any NaN.
+//    fp32 overflow), |theta| > pi (outside the approximations' range), or any
+//    NaN.
 // Such neighbours are dropped from the fast sum, recorded in a bit mask and
 // recomputed after the loop in fp64 exactly as the reference does. On
 // camera-facing inputs this is about 1 neighbour evaluation in 10^5.
@@ -197,20 +198,11 @@ __device__ __noinline__ double3 angmf_neighbor_exact(double nx, double ny, doubl
                         __dmul_rn(w, __dmul_rn(m2, minv)));
 }
 
-// Half-angle Taylor coefficients: 2 sin(t/2) = t * sum_k (-1)^k t^2k / (4^k (2k+1)!),
-// cos(t/2) = sum_k (-1)^k t^2k / (4^k (2k)!).
-constexpr float kS1 = -1.0f / 24.0f, kS2 = 1.0f / 1920.0f, kS3 = -1.0f / 322560.0f,
-                kS4 = 1.0f / 92897280.0f, kS5 = -1.0f / 40874803200.0f,
-                kS6 = 1.0f / 25505877196800.0f;
-constexpr float kC1 = -1.0f / 8.0f, kC2 = 1.0f / 384.0f, kC3 = -1.0f / 46080.0f,
-                kC4 = 1.0f / 10321920.0f, kC5 = -1.0f / 3715891200.0f,
-                kC6 = 1.0f / 1961990553600.0f;
-
 constexpr float kTau = 1e-5f;     // |dd| fix-up threshold
-constexpr float kGCond = 0.1f;    // 1 / (largest tolerated w |sin| |g| / |g_perp|)
-constexpr float kMMin = 1e-2f;    // smallest tolerated |m|^2 after the RayReLU
+constexpr float kGCond = 0.05f;   // 1 / (largest tolerated w |sin| |g| / |g_perp|)
+constexpr float kMMin = 0.04f;    // smallest tolerated |m|^2 after the RayReLU
 constexpr float kQMin = 1e-10f, kQMax = 1e30f;  // |xy|^2 range of the fast path
-constexpr float kThMax = 3.2f;    // |theta| range of the series
+constexpr float kThMax = 3.1416f; // |theta| range of the sin / cos approximations
 
 template <typename Mask>
 struct PairAcc {
@@ -245,23 +237,10 @@ __device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 t
     const float2 gp2 = fma2(gpx, gpx, fma2(gpy, gpy, mul2(gpz, gpz)));
     const float2 gg2 = fma2(Y, Y, fma2(X, X, mul2(gz, gz)));
     const float2 gi = rsqrt2_ftz(max2(gp2, f2(1e-30f)));
-    // sin / cos of theta via the half angle
-    const float2 t2 = mul2(th, th);
-    float2 ps2 = fma2(t2, f2(kS6), f2(kS5));
-    ps2 = fma2(t2, ps2, f2(kS4));
-    ps2 = fma2(t2, ps2, f2(kS3));
-    ps2 = fma2(t2, ps2, f2(kS2));
-    ps2 = fma2(t2, ps2, f2(kS1));
-    ps2 = fma2(t2, ps2, f2(1.0f));
-    const float2 s2 = mul2(th, ps2);  // 2 sin(theta/2)
-    float2 ch = fma2(t2, f2(kC6), f2(kC5));
-    ch = fma2(t2, ch, f2(kC4));
-    ch = fma2(t2, ch, f2(kC3));
-    ch = fma2(t2, ch, f2(kC2));
-    ch = fma2(t2, ch, f2(kC1));
-    ch = fma2(t2, ch, f2(1.0f));      // cos(theta/2)
-    const float2 sn = mul2(s2, ch);   // sin(theta)
-    const float2 cs = fma2(s2, mul2(s2, f2(-0.5f)), f2(1.0f));  // cos(theta)
+    // sin / cos of theta with the hardware approximations (abs. error ~5e-7
+    // on |theta| <= pi; larger angles are left to the fix-up)
+    const float2 sn = sin2_approx(th);
+    const float2 cs = cos2_approx(th);
     float2 kk = mul2(sn, gi);
     kk.x = __uint_as_float(__float_as_uint(kk.x) ^ (__float_as_uint(dd.x) & 0x80000000u));
     kk.y = __uint_as_float(__float_as_uint(kk.y) ^ (__float_as_uint(dd.y) & 0x80000000u));

@@ -43,7 +43,7 @@ struct UpStages {
     static constexpr int kCpr = kUTW / kEpc;                      // chunks per strip
     static constexpr int kChunksW = 9 * kCpr;                     // per warp per stage
     static constexpr int kElemsW = 9 * kUTW;                      // per warp per stage
-    static constexpr int kN = 4;                                  // ring depth
+    static constexpr int kN = sizeof(TS) == 2 ? 6 : 4;            // ring depth
     static constexpr size_t kBytes = (size_t)(kUThreads / 32) * kN * kElemsW * sizeof(TS);
 };
 
@@ -192,6 +192,7 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
     constexpr float kL2E = 1.4426950408889634f;
     using L = Logit<TS>;
     const int so = 2 * lane;  // pair offset in a staged strip
+    int rslot = 0;            // ring slot of the stage being computed
 
 #pragma unroll 1
     for (int ky = 0; ky < 8; ++ky) {
@@ -205,12 +206,16 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
                 const int k = ky * 8 + kx;
                 cp_async_wait<U::kN - 2>();
                 __syncwarp();  // stage k visible to the warp; every lane done with k-1
+                // ring slots: stage k is in slot rslot, stage k+kN-1 goes to the
+                // slot of stage k-1 (counters wrap instead of taking k % kN)
+                const int islot = rslot == 0 ? U::kN - 1 : rslot - 1;
                 if (k + U::kN - 1 < 64) {
-                    lc.issue(ring + ((k + U::kN - 1) % U::kN) * U::kElemsW, mnext);
+                    lc.issue(ring + islot * U::kElemsW, mnext);
                     mnext += hw;
                 }
                 cp_async_commit();
-                const TS* st = ring + (k % U::kN) * U::kElemsW + so;
+                const TS* st = ring + rslot * U::kElemsW + so;
+                rslot = rslot == U::kN - 1 ? 0 : rslot + 1;
 #pragma unroll
                 for (int tp = 0; tp < 9; ++tp) l[tp] = L::lds(st + tp * kUTW);
             } else {
@@ -222,24 +227,35 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
             const float2 m = L::f(L::mx(L::mx(L::mx(l[0], l[1]), L::mx(l[2], l[3])),
                                         L::mx(L::mx(l[4], l[5]), L::mx(L::mx(l[6], l[7]), l[8]))));
             const float2 mo = mul2(m, f2(-kL2E));
-            float2 S = f2(0.f), ax = f2(0.f), ay = f2(0.f), az = f2(0.f);
+            float2 ax = f2(0.f), ay = f2(0.f), az = f2(0.f);
+            // softmax weights up to the factor 1/S (e_t = exp(l_t - max l))
+            auto ew = [&](int tp) { return ex2_ftz2(fma2(L::f(l[tp]), f2(kL2E), mo)); };
 #pragma unroll
             for (int tp = 0; tp < 9; ++tp) {
-                const float2 e = ex2_ftz2(fma2(L::f(l[tp]), f2(kL2E), mo));
-                S = add2(S, e);
+                const float2 e = ew(tp);
                 ax = fma2(e, N[tp][0], ax);
                 ay = fma2(e, N[tp][1], ay);
                 az = fma2(e, N[tp][2], az);
             }
             float2 ox, oy, oz;
             if (NORM) {
-                const float2 l2 = fma2(ax, ax, fma2(ay, ay, mul2(az, az)));
-                const float2 se = mul2(S, f2(1e-12f));
-                const float2 inv = rsqrt2(max2(l2, mul2(se, se)));
+                // x / max(|x|, 1e-12) for x = a / S; with 1 <= S <= 9 the clamp can
+                // only act when |a| < 9e-12, so S is summed only then.
+                float2 l2 = fma2(ax, ax, fma2(ay, ay, mul2(az, az)));
+                if ((l2.x < 8.1e-23f) | (l2.y < 8.1e-23f)) {
+                    float2 S = ew(0);
+                    for (int tp = 1; tp < 9; ++tp) S = add2(S, ew(tp));
+                    const float2 se = mul2(S, f2(1e-12f));
+                    l2 = max2(l2, mul2(se, se));
+                }
+                const float2 inv = rsqrt2(l2);
                 ox = mul2(ax, inv);
                 oy = mul2(ay, inv);
                 oz = mul2(az, inv);
             } else {
+                float2 S = ew(0);
+#pragma unroll
+                for (int tp = 1; tp < 9; ++tp) S = add2(S, ew(tp));
                 const float2 inv = f2(__frcp_rn(S.x), __frcp_rn(S.y));
                 ox = mul2(ax, inv);
                 oy = mul2(ay, inv);
