@@ -653,8 +653,8 @@ angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
 
 #pragma unroll 1
     for (int ky = 0; ky < PS; ++ky) {
-        const int grp = (S::kM == 2) ? (ky & 1) * PS : 0;  // slot group of this window row
-        const int prev_grp = (S::kM == 2) ? PS - grp : 0;  // ... of the previous row
+        const int grp = (ky % S::kM) * PS;                  // slot group of this window row
+        const int prev_grp = ((ky + S::kM - 1) % S::kM) * PS;  // ... of the previous row
         const TS* st_row = ring_lane + grp * S::kElemsW;
         const int prow = pbase + ky * DIL * SWH;
         const float2 tv = f2(T.tv[ly + ky * DIL]);
