@@ -1,0 +1,100 @@
+"""GPU tests at the benchmark configurations' full sizes, where the CPU
+oracle would take too long: size-independent properties instead.
+
+* every output is finite and unit length (fp32: 1e-5, fp16 storage: 2e-3);
+* the frame dimension is independent: a batch computed at once equals the
+  same frames computed in smaller batches, bit for bit;
+* row bands (config 3's multi-GPU split) stitched together equal the whole
+  frame (exact halo, see brovisionml_b200.sharding);
+* full-res RayReLU leaves every output facing the camera.
+"""
+import numpy as np
+import pytest
+import torch
+
+import bench
+from brovisionml_b200.sharding import band_intrinsics, halo_rows, plan_bands
+
+pytestmark = pytest.mark.gpu
+
+
+def run(inp, cfg, **kw):
+    import brovisionml_b200 as bv
+
+    return bv.refine(inp["normal0"], inp["prob"], inp["xy"], inp["angle"], inp["mask"],
+                     inp["fu"], inp["cu"], inp["fv"], inp["cv"], ray8=inp["ray8"], ps=cfg["ps"],
+                     dil=cfg["dil"], full_res_ray_relu=cfg["rr"], **kw)
+
+
+def check_unit(out, tol):
+    o = out.float()
+    assert torch.isfinite(o).all()
+    err = (o.norm(dim=1) - 1).abs().max().item()
+    assert err <= tol, err
+
+
+@pytest.mark.parametrize("name", ["cfg2", "cfg2h", "cfg4"])
+def test_fullsize_unit_norm_and_batch_split(name):
+    cfg = dict(bench.CONFIGS[name])
+    dev = torch.device("cuda", 0)
+    inp = bench.make_device_inputs(cfg, 5, dev, torch)
+    out = run(inp, cfg)
+    torch.cuda.synchronize()
+    check_unit(out, 2e-3 if cfg["f16"] else 1e-5)
+    # the same frames in two halves
+    B = cfg["B"]
+    half = B // 2
+    parts = []
+    for sl in (slice(0, half), slice(half, B)):
+        sub = dict(inp, normal0=inp["normal0"][sl].contiguous(),
+                   prob=[t[sl].contiguous() for t in inp["prob"]],
+                   xy=[t[sl].contiguous() for t in inp["xy"]],
+                   angle=[t[sl].contiguous() for t in inp["angle"]],
+                   mask=inp["mask"][sl].contiguous())
+        parts.append(run(sub, cfg))
+    torch.cuda.synchronize()
+    assert torch.equal(torch.cat(parts), out)
+
+
+def test_fullsize_cfg3_bands_match_whole_frame():
+    """Config 3: one 4096^2 frame (grid 512^2, 7x7, 5 iterations) computed whole
+    and as 8 exact halo bands (what 8 GPUs would each compute)."""
+    cfg = dict(bench.CONFIGS["cfg3"])
+    dev = torch.device("cuda", 0)
+    inp = bench.make_device_inputs(cfg, 9, dev, torch)
+    whole = run(inp, cfg)
+    check_unit(whole, 1e-5)
+    h = inp["h"]
+    bands = plan_bands(h, 8, halo_rows(cfg["iters"], cfg["ps"], cfg["dil"]))
+    rows = []
+    for b in bands:
+        sl = slice(b.comp0, b.comp1)
+        sub = dict(inp, normal0=inp["normal0"][:, :, sl].contiguous(),
+                   prob=[t[:, :, sl].contiguous() for t in inp["prob"]],
+                   xy=[t[:, :, sl].contiguous() for t in inp["xy"]],
+                   angle=[t[:, :, sl].contiguous() for t in inp["angle"]],
+                   mask=inp["mask"][:, :, sl].contiguous(),
+                   ray8=inp["ray8"][:, sl].contiguous(), cv=band_intrinsics(inp["cv"], b))
+        out = run(sub, cfg, crop=(8 * b.crop_top, 0, 8 * (b.own1 - b.own0), 8 * inp["w"]))
+        rows.append(out)
+    stitched = torch.cat(rows, dim=2)
+    torch.cuda.synchronize()
+    assert stitched.shape == whole.shape
+    err = (stitched - whole).abs().max().item()
+    assert err <= 1e-5, err
+
+
+def test_fullsize_cfg1_full_res_ray_relu_faces_camera():
+    cfg = dict(bench.CONFIGS["cfg1"])
+    dev = torch.device("cuda", 0)
+    inp = bench.make_device_inputs(cfg, 3, dev, torch)
+    out = run(inp, cfg)[0].double()
+    H, W = cfg["H"], cfg["W"]
+    fu, cu, fv, cv = 8 * inp["fu"], 8 * inp["cu"], 8 * inp["fv"], 8 * inp["cv"]
+    ys, xs = torch.meshgrid(torch.arange(H, device=dev, dtype=torch.float64),
+                            torch.arange(W, device=dev, dtype=torch.float64), indexing="ij")
+    r = torch.stack([((xs + 0.5) - cu) / fu, ((ys + 0.5) - cv) / fv, torch.ones_like(xs)])
+    r = r / r.norm(dim=0, keepdim=True)
+    c = (out * r).sum(0)
+    assert c.min().item() >= 0.01 - 1e-5
+    check_unit(out[None], 1e-5)
