@@ -292,7 +292,7 @@ struct NTile {
     int swh;      // pairs per plane row
 
     static constexpr __host__ __device__ int pairs_per_row(int SW) { return SW / 2 + 1; }
-    static __host__ __device__ size_t bytes(int SW, int SH) {
+    static constexpr __host__ __device__ size_t bytes(int SW, int SH) {
         const int h = pairs_per_row(SW);
         return sizeof(float4) * 2 * h + sizeof(float2) * 6 * (size_t)SH * h + sizeof(float) * SH;
     }
@@ -566,9 +566,20 @@ struct Stages {
     static constexpr int kChunksW = 4 * kRowsW * kCpr;     // per warp per slot
     static constexpr int kPerLane = kChunksW / 32;         // 1 (fp16) or 2 (fp32)
     static constexpr int kElemsW = 4 * kRowsW * kTW;       // per warp per slot
-    static constexpr int kM = (sizeof(TS) == 4 && PS == 7) ? 1 : 2;  // window rows per ring
+    static constexpr int kM = (sizeof(TS) == 2 && PS < 7) ? 2 : 1;  // window rows per ring
     static constexpr int kN = kM * PS;                     // ring depth
     static constexpr size_t kBytes = (size_t)(kThreads / 32) * kN * kElemsW * sizeof(TS);
+};
+
+// Shared memory of a staged variant and the CTAs per SM it is compiled for:
+// three when three fit (more warps to hide the dependency chains; the
+// register cap is then 80 and a few loop invariants spill to L1), else two.
+template <int PS, int DIL, typename TS>
+struct StagedCfg {
+    static constexpr int R = (PS / 2) * DIL;
+    static constexpr size_t kSmem =
+        Stages<TS, PS>::kBytes + NTile::bytes(kTW + 2 * R, kTH + 2 * R);
+    static constexpr int kMinBlocks = 3 * (kSmem + 1024) <= 228 * 1024 ? 3 : 2;
 };
 
 template <typename TS> __device__ __forceinline__ float2 lds2(const TS* p);
@@ -580,7 +591,7 @@ template <> __device__ __forceinline__ float2 lds2<__half>(const __half* p) {
 }
 
 template <int PS, int DIL, typename TS, typename TNI, typename TNO, bool FUSE_RR>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, (StagedCfg<PS, DIL, TS>::kMinBlocks))
 angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
                     const TS* __restrict__ xy, const TS* __restrict__ ang,
                     const float* __restrict__ ray, TNO* __restrict__ out, const AngmfArgs a) {
@@ -723,7 +734,7 @@ cudaError_t launch_t(const AngmfLaunch& L, cudaStream_t s) {
     // boundary (W a multiple of 16 bytes of storage); dilations 1 and 2 (the
     // benchmark windows) have compile-time staged variants
     if ((L.W % Stages<TS, PS>::kEpc) == 0 && (L.dil == 1 || L.dil == 2)) {
-        const size_t smem = Stages<TS, PS>::kBytes + nsmem;
+        const size_t smem = Stages<TS, PS>::kBytes + nsmem;  // = StagedCfg<...>::kSmem
         auto kern = L.dil == 1 ? angmf_staged_kernel<PS, 1, TS, TNI, TNO, FUSE_RR>
                                : angmf_staged_kernel<PS, 2, TS, TNI, TNO, FUSE_RR>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
