@@ -19,9 +19,12 @@
 // Logit staging: when the grid width is a multiple of 16 bytes of storage,
 // each warp copies, for every (ky, kx), the 9 logit strips of its own row
 // (9 planes x 64 columns) global -> shared with 16-byte cp.async into a
-// warp-private ring kN stages deep, kN-1 ahead of the stage being computed;
-// a warp barrier publishes each stage. The bytes in flight then do not cost
-// registers. Other widths read the logits straight from global memory.
+// warp-private ring kN stages deep. Stages go in groups of kSP: one warp
+// barrier publishes a group, and the kSP sub-pixels of a group are computed
+// together so that their independent dependency chains interleave (the kernel
+// is otherwise bound by fixed-latency waits at 4 warps per scheduler). The
+// bytes in flight do not cost registers. Other widths read the logits
+// straight from global memory.
 //
 // The softmax denominator is folded into the normalise: with e_t = exp(l_t -
 // max l), normalise(sum_t (e_t/S) n_t) = a / max(|a|, 1e-12 S) for
@@ -43,7 +46,10 @@ struct UpStages {
     static constexpr int kCpr = kUTW / kEpc;                      // chunks per strip
     static constexpr int kChunksW = 9 * kCpr;                     // per warp per stage
     static constexpr int kElemsW = 9 * kUTW;                      // per warp per stage
+    static constexpr int kSP = sizeof(TS) == 2 ? 2 : 1;           // stages per group
     static constexpr int kN = sizeof(TS) == 2 ? 6 : 4;            // ring depth
+    static constexpr int kG = kN / kSP;                           // groups in the ring
+    static_assert(kN % kSP == 0 && 8 % kSP == 0, "stage groups must tile the ring and a row");
     static constexpr size_t kBytes = (size_t)(kUThreads / 32) * kN * kElemsW * sizeof(TS);
 };
 
@@ -160,10 +166,10 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
     if (STAGED) {
         lc.init(lane, a.w - x0, hw);
 #pragma unroll
-        for (int s = 0; s < U::kN - 1; ++s) {
+        for (int s = 0; s < U::kN - U::kSP; ++s) {  // the first kG-1 groups
             lc.issue(ring + s * U::kElemsW, mnext);
             mnext += hw;
-            cp_async_commit();
+            if (s % U::kSP == U::kSP - 1) cp_async_commit();
         }
     }
     const bool vec = (a.w & 1) == 0;   // pairs start at even offsets: 8/4-byte aligned
@@ -192,7 +198,7 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
     constexpr float kL2E = 1.4426950408889634f;
     using L = Logit<TS>;
     const int so = 2 * lane;  // pair offset in a staged strip
-    int rslot = 0;            // ring slot of the stage being computed
+    int rslot = 0;            // ring slot of the first stage of the group being computed
 
 #pragma unroll 1
     for (int ky = 0; ky < 8; ++ky) {
@@ -200,149 +206,164 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
         const bool row_in = Yo >= 0 && Yo < a.out_h;
         OutRun<TS> run;
 #pragma unroll
-        for (int kx = 0; kx < 8; ++kx) {
-            typename L::T l[9];
+        for (int kg = 0; kg < 8 / U::kSP; ++kg) {
+            typename L::T lg[U::kSP][9];
             if (STAGED) {
-                const int k = ky * 8 + kx;
-                cp_async_wait<U::kN - 2>();
-                __syncwarp();  // stage k visible to the warp; every lane done with k-1
-                // ring slots: stage k is in slot rslot, stage k+kN-1 goes to the
-                // slot of stage k-1 (counters wrap instead of taking k % kN)
-                const int islot = rslot == 0 ? U::kN - 1 : rslot - 1;
-                if (k + U::kN - 1 < 64) {
-                    lc.issue(ring + islot * U::kElemsW, mnext);
-                    mnext += hw;
+                const int k = ky * 8 + kg * U::kSP;  // first stage of the group
+                cp_async_wait<U::kG - 2>();
+                __syncwarp();  // group visible to the warp; every lane done with the previous one
+                // the group kG-1 ahead goes to the slots of the previous group
+                // (slot counters wrap instead of taking k % kN)
+                const int islot = rslot == 0 ? U::kN - U::kSP : rslot - U::kSP;
+                if (k + U::kN - U::kSP < 64) {
+#pragma unroll
+                    for (int e = 0; e < U::kSP; ++e) {
+                        lc.issue(ring + (islot + e) * U::kElemsW, mnext);
+                        mnext += hw;
+                    }
                 }
                 cp_async_commit();
                 const TS* st = ring + rslot * U::kElemsW + so;
-                rslot = rslot == U::kN - 1 ? 0 : rslot + 1;
+                rslot = rslot == U::kN - U::kSP ? 0 : rslot + U::kSP;
 #pragma unroll
-                for (int tp = 0; tp < 9; ++tp) l[tp] = L::lds(st + tp * kUTW);
+                for (int e = 0; e < U::kSP; ++e)
+#pragma unroll
+                    for (int tp = 0; tp < 9; ++tp)
+                        lg[e][tp] = L::lds(st + e * U::kElemsW + tp * kUTW);
             } else {
 #pragma unroll
-                for (int tp = 0; tp < 9; ++tp)
-                    l[tp] = L::ldg(mb + (long)(tp * 64 + ky * 8 + kx) * hw, d1, vec);
+                for (int e = 0; e < U::kSP; ++e)
+#pragma unroll
+                    for (int tp = 0; tp < 9; ++tp)
+                        lg[e][tp] = L::ldg(mb + (long)(tp * 64 + ky * 8 + kg * U::kSP + e) * hw,
+                                           d1, vec);
             }
             if (!active) continue;  // staged mode: idle lanes only keep the warp barriers
-            const float2 m = L::f(L::mx(L::mx(L::mx(l[0], l[1]), L::mx(l[2], l[3])),
-                                        L::mx(L::mx(l[4], l[5]), L::mx(L::mx(l[6], l[7]), l[8]))));
-            const float2 mo = mul2(m, f2(-kL2E));
-            float2 ax = f2(0.f), ay = f2(0.f), az = f2(0.f);
-            // softmax weights up to the factor 1/S (e_t = exp(l_t - max l))
-            auto ew = [&](int tp) { return ex2_ftz2(fma2(L::f(l[tp]), f2(kL2E), mo)); };
 #pragma unroll
-            for (int tp = 0; tp < 9; ++tp) {
-                const float2 e = ew(tp);
-                ax = fma2(e, N[tp][0], ax);
-                ay = fma2(e, N[tp][1], ay);
-                az = fma2(e, N[tp][2], az);
-            }
-            float2 ox, oy, oz;
-            if (NORM) {
-                // x / max(|x|, 1e-12) for x = a / S; with 1 <= S <= 9 the clamp can
-                // only act when |a| < 9e-12, so S is summed only then.
-                float2 l2 = fma2(ax, ax, fma2(ay, ay, mul2(az, az)));
-                if ((l2.x < 8.1e-23f) | (l2.y < 8.1e-23f)) {
-                    float2 S = ew(0);
-                    for (int tp = 1; tp < 9; ++tp) S = add2(S, ew(tp));
-                    const float2 se = mul2(S, f2(1e-12f));
-                    l2 = max2(l2, mul2(se, se));
+            for (int sg = 0; sg < U::kSP; ++sg) {
+                const int kx = kg * U::kSP + sg;
+                const typename L::T* l = lg[sg];
+                const float2 m =
+                    L::f(L::mx(L::mx(L::mx(l[0], l[1]), L::mx(l[2], l[3])),
+                               L::mx(L::mx(l[4], l[5]), L::mx(L::mx(l[6], l[7]), l[8]))));
+                const float2 mo = mul2(m, f2(-kL2E));
+                float2 ax = f2(0.f), ay = f2(0.f), az = f2(0.f);
+                // softmax weights up to the factor 1/S (e_t = exp(l_t - max l))
+                auto ew = [&](int tp) { return ex2_ftz2(fma2(L::f(l[tp]), f2(kL2E), mo)); };
+#pragma unroll
+                for (int tp = 0; tp < 9; ++tp) {
+                    const float2 e = ew(tp);
+                    ax = fma2(e, N[tp][0], ax);
+                    ay = fma2(e, N[tp][1], ay);
+                    az = fma2(e, N[tp][2], az);
                 }
-                const float2 inv = rsqrt2(l2);
-                ox = mul2(ax, inv);
-                oy = mul2(ay, inv);
-                oz = mul2(az, inv);
-            } else {
-                float2 S = ew(0);
-#pragma unroll
-                for (int tp = 1; tp < 9; ++tp) S = add2(S, ew(tp));
-                const float2 inv = f2(__frcp_rn(S.x), __frcp_rn(S.y));
-                ox = mul2(ax, inv);
-                oy = mul2(ay, inv);
-                oz = mul2(az, inv);
-            }
-            if (RR) {
-                // full-res ray at (8y+ky, 8x+kx) and (8y+ky, 8x+8+kx)
-                const float X0 = (float)(8 * x + kx);
-                float2 rx = f2(fmaf(X0, a.ifu8, a.tu8_c), fmaf(X0 + 8.0f, a.ifu8, a.tu8_c));
-                float2 ry = f2(fmaf((float)(8 * y + ky), a.ifv8, a.tv8_c));
-                const float2 ri = rsqrt2(fma2(rx, rx, fma2(ry, ry, f2(1.0f))));
-                rx = mul2(rx, ri);
-                ry = mul2(ry, ri);
-                const float2 rz = ri;
-                const float2 nn2 = fma2(ox, ox, fma2(oy, oy, mul2(oz, oz)));
-                const float2 c = mul2(fma2(ox, rx, fma2(oy, ry, mul2(oz, rz))),
-                                      rsqrt2(max2(nn2, f2(1e-16f))));
-                const float2 dc = max2(fma2(c, f2(-1.0f), f2(kRayEps)), f2(0.0f));
-                ox = fma2(rx, dc, ox);
-                oy = fma2(ry, dc, oy);
-                oz = fma2(rz, dc, oz);
-                const float2 inv =
-                    rsqrt2(max2(fma2(ox, ox, fma2(oy, oy, mul2(oz, oz))), f2(1e-24f)));
-                ox = mul2(ox, inv);
-                oy = mul2(oy, inv);
-                oz = mul2(oz, inv);
-            }
-            // collect; flush a 16-byte run per channel and pixel when complete
-            if constexpr (sizeof(TS) == 2) {
-                // half pairs (kx even, kx odd) per pixel
-                const float o[3][2] = {{ox.x, ox.y}, {oy.x, oy.y}, {oz.x, oz.y}};
-#pragma unroll
-                for (int c = 0; c < 3; ++c)
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        if ((kx & 1) == 0)
-                            run.v[c][e][kx >> 1].x = __float2half_rn(o[c][e]);
-                        else
-                            run.v[c][e][kx >> 1].y = __float2half_rn(o[c][e]);
+                float2 ox, oy, oz;
+                if (NORM) {
+                    // x / max(|x|, 1e-12) for x = a / S; with 1 <= S <= 9 the clamp can
+                    // only act when |a| < 9e-12, so S is summed only then.
+                    float2 l2 = fma2(ax, ax, fma2(ay, ay, mul2(az, az)));
+                    if ((l2.x < 8.1e-23f) | (l2.y < 8.1e-23f)) {
+                        float2 S = ew(0);
+                        for (int tp = 1; tp < 9; ++tp) S = add2(S, ew(tp));
+                        const float2 se = mul2(S, f2(1e-12f));
+                        l2 = max2(l2, mul2(se, se));
                     }
-                if (kx == 7 && row_in && active) {
-                    TS* orow = out + (long)b * 3 * a.out_h * a.out_w + (long)Yo * a.out_w;
+                    const float2 inv = rsqrt2(l2);
+                    ox = mul2(ax, inv);
+                    oy = mul2(ay, inv);
+                    oz = mul2(az, inv);
+                } else {
+                    float2 S = ew(0);
+#pragma unroll
+                    for (int tp = 1; tp < 9; ++tp) S = add2(S, ew(tp));
+                    const float2 inv = f2(__frcp_rn(S.x), __frcp_rn(S.y));
+                    ox = mul2(ax, inv);
+                    oy = mul2(ay, inv);
+                    oz = mul2(az, inv);
+                }
+                if (RR) {
+                    // full-res ray at (8y+ky, 8x+kx) and (8y+ky, 8x+8+kx)
+                    const float X0 = (float)(8 * x + kx);
+                    float2 rx = f2(fmaf(X0, a.ifu8, a.tu8_c), fmaf(X0 + 8.0f, a.ifu8, a.tu8_c));
+                    float2 ry = f2(fmaf((float)(8 * y + ky), a.ifv8, a.tv8_c));
+                    const float2 ri = rsqrt2(fma2(rx, rx, fma2(ry, ry, f2(1.0f))));
+                    rx = mul2(rx, ri);
+                    ry = mul2(ry, ri);
+                    const float2 rz = ri;
+                    const float2 nn2 = fma2(ox, ox, fma2(oy, oy, mul2(oz, oz)));
+                    const float2 c = mul2(fma2(ox, rx, fma2(oy, ry, mul2(oz, rz))),
+                                          rsqrt2(max2(nn2, f2(1e-16f))));
+                    const float2 dc = max2(fma2(c, f2(-1.0f), f2(kRayEps)), f2(0.0f));
+                    ox = fma2(rx, dc, ox);
+                    oy = fma2(ry, dc, oy);
+                    oz = fma2(rz, dc, oz);
+                    const float2 inv =
+                        rsqrt2(max2(fma2(ox, ox, fma2(oy, oy, mul2(oz, oz))), f2(1e-24f)));
+                    ox = mul2(ox, inv);
+                    oy = mul2(oy, inv);
+                    oz = mul2(oz, inv);
+                }
+                // collect; flush a 16-byte run per channel and pixel when complete
+                if constexpr (sizeof(TS) == 2) {
+                    // half pairs (kx even, kx odd) per pixel
+                    const float o[3][2] = {{ox.x, ox.y}, {oy.x, oy.y}, {oz.x, oz.y}};
 #pragma unroll
                     for (int c = 0; c < 3; ++c)
 #pragma unroll
                         for (int e = 0; e < 2; ++e) {
-                            const int X = 8 * (x + e) - a.crop_l;  // first column of the run
-                            TS* dst = orow + (long)c * a.out_h * a.out_w + X;
-                            if (e == 1 && x + 1 >= a.w) continue;
-                            if (a.vec_out && X >= 0 && X + 8 <= a.out_w) {
-                                *reinterpret_cast<uint4*>(dst) =
-                                    *reinterpret_cast<const uint4*>(&run.v[c][e][0]);
-                            } else {
+                            if ((kx & 1) == 0)
+                                run.v[c][e][kx >> 1].x = __float2half_rn(o[c][e]);
+                            else
+                                run.v[c][e][kx >> 1].y = __float2half_rn(o[c][e]);
+                        }
+                    if (kx == 7 && row_in && active) {
+                        TS* orow = out + (long)b * 3 * a.out_h * a.out_w + (long)Yo * a.out_w;
 #pragma unroll
-                                for (int k = 0; k < 8; ++k) {
-                                    const __half hv = (k & 1) ? run.v[c][e][k >> 1].y
-                                                              : run.v[c][e][k >> 1].x;
-                                    if (X + k >= 0 && X + k < a.out_w) dst[k] = hv;
+                        for (int c = 0; c < 3; ++c)
+#pragma unroll
+                            for (int e = 0; e < 2; ++e) {
+                                const int X = 8 * (x + e) - a.crop_l;  // first column of the run
+                                TS* dst = orow + (long)c * a.out_h * a.out_w + X;
+                                if (e == 1 && x + 1 >= a.w) continue;
+                                if (a.vec_out && X >= 0 && X + 8 <= a.out_w) {
+                                    *reinterpret_cast<uint4*>(dst) =
+                                        *reinterpret_cast<const uint4*>(&run.v[c][e][0]);
+                                } else {
+#pragma unroll
+                                    for (int k = 0; k < 8; ++k) {
+                                        const __half hv = (k & 1) ? run.v[c][e][k >> 1].y
+                                                                  : run.v[c][e][k >> 1].x;
+                                        if (X + k >= 0 && X + k < a.out_w) dst[k] = hv;
+                                    }
                                 }
                             }
-                        }
-                }
-            } else {
-                const float o[3][2] = {{ox.x, ox.y}, {oy.x, oy.y}, {oz.x, oz.y}};
-#pragma unroll
-                for (int c = 0; c < 3; ++c)
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) run.v[c][e][kx & 3] = o[c][e];
-                if ((kx & 3) == 3 && row_in && active) {
-                    TS* orow = out + (long)b * 3 * a.out_h * a.out_w + (long)Yo * a.out_w;
+                    }
+                } else {
+                    const float o[3][2] = {{ox.x, ox.y}, {oy.x, oy.y}, {oz.x, oz.y}};
 #pragma unroll
                     for (int c = 0; c < 3; ++c)
 #pragma unroll
-                        for (int e = 0; e < 2; ++e) {
-                            const int X = 8 * (x + e) + (kx & 4) - a.crop_l;
-                            TS* dst = orow + (long)c * a.out_h * a.out_w + X;
-                            if (e == 1 && x + 1 >= a.w) continue;
-                            if (a.vec_out && X >= 0 && X + 4 <= a.out_w) {
-                                *reinterpret_cast<float4*>(dst) =
-                                    make_float4(run.v[c][e][0], run.v[c][e][1], run.v[c][e][2],
-                                                run.v[c][e][3]);
-                            } else {
+                        for (int e = 0; e < 2; ++e) run.v[c][e][kx & 3] = o[c][e];
+                    if ((kx & 3) == 3 && row_in && active) {
+                        TS* orow = out + (long)b * 3 * a.out_h * a.out_w + (long)Yo * a.out_w;
 #pragma unroll
-                                for (int k = 0; k < 4; ++k)
-                                    if (X + k >= 0 && X + k < a.out_w) dst[k] = run.v[c][e][k];
+                        for (int c = 0; c < 3; ++c)
+#pragma unroll
+                            for (int e = 0; e < 2; ++e) {
+                                const int X = 8 * (x + e) + (kx & 4) - a.crop_l;
+                                TS* dst = orow + (long)c * a.out_h * a.out_w + X;
+                                if (e == 1 && x + 1 >= a.w) continue;
+                                if (a.vec_out && X >= 0 && X + 4 <= a.out_w) {
+                                    *reinterpret_cast<float4*>(dst) =
+                                        make_float4(run.v[c][e][0], run.v[c][e][1], run.v[c][e][2],
+                                                    run.v[c][e][3]);
+                                } else {
+#pragma unroll
+                                    for (int k = 0; k < 4; ++k)
+                                        if (X + k >= 0 && X + k < a.out_w) dst[k] = run.v[c][e][k];
+                                }
                             }
-                        }
+                    }
                 }
             }
         }
