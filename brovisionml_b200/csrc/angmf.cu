@@ -212,40 +212,40 @@ struct PairAcc {
 
 // One neighbour slot n for a pixel pair: rotate the (unit) source normals,
 // RayReLU them against the pixels' (unit) rays, accumulate with weight w.
-// Sign conventions avoid negated packed operands: tun = -tu, nifu = -1/fu,
-// nifv = -1/fv are supplied by the caller.
+// tun = -tu is supplied by the caller (from the staged table).
 template <typename Mask>
 __device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 th, float2 wt,
                                            float2 nx, float2 ny, float2 nz, float2 tu,
                                            float2 tun, float2 tv, float2 ifu2, float2 ifv2,
-                                           float2 nifu2, float2 nifv2, float2 rx, float2 ry,
-                                           float2 rz, PairAcc<Mask>& A) {
+                                           float2 rx, float2 ry, float2 rz, PairAcc<Mask>& A) {
     const float2 q = fma2(xs, xs, mul2(ys, ys));
     const float2 iq = rsqrt2_ftz(q);
     const float2 X = mul2(xs, ifu2), Y = mul2(ys, ifv2);     // d (unnormalised)
-    const float2 Xn = mul2(xs, nifu2), Yn = mul2(ys, nifv2);
     const float2 e = fma2(X, nx, mul2(Y, ny));               // d.n
     const float2 as = fma2(tu, nx, fma2(tv, ny, nz));        // P.n
     const float2 dd = fma2(iq, e, as);                       // (P + d).n, d normalised
-    // g = d x P = (Y, -X, gz); g_perp = g - n (g.n) = g + n ngn
+    // g = d x P = (Y, -X, gz); g_perp = g - n (g.n) = (gpx, -gpyn, gpz)
     const float2 gz = fma2(X, tv, mul2(Y, tun));
-    const float2 gzn = fma2(Xn, tv, mul2(Y, tu));
-    const float2 ngn = fma2(Yn, nx, fma2(X, ny, mul2(gzn, nz)));
-    const float2 gpx = fma2(nx, ngn, Y);
-    const float2 gpy = fma2(ny, ngn, Xn);
-    const float2 gpz = fma2(nz, ngn, gz);
-    const float2 gp2 = fma2(gpx, gpx, fma2(gpy, gpy, mul2(gpz, gpz)));
-    const float2 gg2 = fma2(Y, Y, fma2(X, X, mul2(gz, gz)));
-    const float2 gi = rsqrt2_ftz(max2(gp2, f2(1e-30f)));
+    const float2 ng = fma2(Y, nx, fnma2(X, ny, mul2(gz, nz)));
+    const float2 gpx = fnma2(nx, ng, Y);
+    const float2 gpyn = fma2(ny, ng, X);
+    const float2 gpz = fnma2(nz, ng, gz);
+    const float2 gp2 = fma2(gpx, gpx, fma2(gpyn, gpyn, mul2(gpz, gpz)));
+    const float2 gg2 = fma2(ng, ng, gp2);                    // |g|^2 = |g_perp|^2 + (n.g)^2
+    // |g_perp| = 0 gives an infinite or NaN kk below, which the fix-up tests catch
+    const float2 gi = rsqrt2_ftz(gp2);
     // sin / cos of theta with the hardware approximations (abs. error ~5e-7
     // on |theta| <= pi; larger angles are left to the fix-up)
     const float2 sn = sin2_approx(th);
     const float2 cs = cos2_approx(th);
     float2 kk = mul2(sn, gi);
+    // w |sin| |g| > |g_perp| / kGCond  <=>  (w sin / |g_perp|)^2 |g|^2 > 1 / kGCond^2
+    const float2 wk = mul2(wt, kk);
+    const float2 gcond = mul2(mul2(wk, wk), gg2);
     kk.x = __uint_as_float(__float_as_uint(kk.x) ^ (__float_as_uint(dd.x) & 0x80000000u));
     kk.y = __uint_as_float(__float_as_uint(kk.y) ^ (__float_as_uint(dd.y) & 0x80000000u));
     const float2 qx = fma2(kk, gpx, mul2(cs, nx));
-    const float2 qy = fma2(kk, gpy, mul2(cs, ny));
+    const float2 qy = fnma2(kk, gpyn, mul2(cs, ny));
     const float2 qz = fma2(kk, gpz, mul2(cs, nz));
     // RayReLU against the pixels' rays, then the weighted sum
     const float2 c = fma2(qx, rx, fma2(qy, ry, mul2(qz, rz)));
@@ -254,27 +254,27 @@ __device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 t
     const float2 my = fma2(ry, dc, qy);
     const float2 mz = fma2(rz, dc, qz);
     const float2 l2 = fma2(mx, mx, fma2(my, my, mul2(mz, mz)));
-    const float2 wsg = mul2(mul2(wt, f2(kGCond)), sn);
-    const float2 gcond = mul2(mul2(wsg, wsg), gg2);
     // bitwise | : every test is evaluated, no branches
-    const bool b0 = !(fabsf(dd.x) >= kTau) | !(gp2.x >= gcond.x) | !(l2.x >= kMMin) |
+    const bool b0 = !(fabsf(dd.x) >= kTau) | !(gcond.x <= 1.0f / (kGCond * kGCond)) | !(l2.x >= kMMin) |
                     !(q.x >= kQMin) | !(q.x <= kQMax) | !(fabsf(th.x) <= kThMax);
-    const bool b1 = !(fabsf(dd.y) >= kTau) | !(gp2.y >= gcond.y) | !(l2.y >= kMMin) |
+    const bool b1 = !(fabsf(dd.y) >= kTau) | !(gcond.y <= 1.0f / (kGCond * kGCond)) | !(l2.y >= kMMin) |
                     !(q.y >= kQMin) | !(q.y <= kQMax) | !(fabsf(th.y) <= kThMax);
     float2 wm = mul2(wt, rsqrt2_ftz(l2));
+    float2 ux = mx, uy = my, uz = mz;
     if (b0 | b1) {  // rare: leave the neighbour to the exact fix-up
+        // weight and vector both zeroed: the vector may be infinite or NaN here
         if (b0) {
-            wm.x = 0.0f;
+            wm.x = ux.x = uy.x = uz.x = 0.0f;
             A.bad0 |= Mask(1) << n;
         }
         if (b1) {
-            wm.y = 0.0f;
+            wm.y = ux.y = uy.y = uz.y = 0.0f;
             A.bad1 |= Mask(1) << n;
         }
     }
-    A.x = fma2(wm, mx, A.x);
-    A.y = fma2(wm, my, A.y);
-    A.z = fma2(wm, mz, A.z);
+    A.x = fma2(wm, ux, A.x);
+    A.y = fma2(wm, uy, A.y);
+    A.z = fma2(wm, uz, A.z);
 }
 
 // The replicate-padded halo of unit source normals in shared memory. For each
@@ -356,6 +356,62 @@ __device__ __forceinline__ void stage_normals(const TNI* __restrict__ pnb,
         const int s0 = clampi(y0 - R + i, 0, a.H - 1);
         T.tv[i] = fmaf((float)s0, a.ifv, a.tv_c);
     }
+}
+
+// Stage the same halo and tables with compile-time geometry (the staged
+// kernel): one item per two source columns, so each channel of an item is
+// one 8-byte store to the even plane and two 4-byte stores to the odd plane,
+// and the item index splits with a constant divisor.
+template <int R, typename TNI, bool FUSE_RR>
+__device__ __forceinline__ void stage_normals_ct(const TNI* __restrict__ pnb,
+                                                 const float* __restrict__ ray, const NTile& T,
+                                                 int x0, int y0, const AngmfArgs& a) {
+    constexpr int SW = kTW + 2 * R, SH = kTH + 2 * R;
+    constexpr int NP = SW / 2;  // column pairs per halo row (SW is even)
+    constexpr int SWH = NTile::pairs_per_row(SW);
+    static_assert(SW % 2 == 0, "halo width must be even");
+    const long HW = a.HW;
+    for (int it = threadIdx.x; it < SH * NP; it += kThreads) {
+        const int i = it / NP, k = it - (it / NP) * NP;
+        const long row = (long)clampi(y0 - R + i, 0, a.H - 1) * a.W;
+        const int sx = x0 - R + 2 * k;
+        const long q0 = row + clampi(sx, 0, a.W - 1);
+        const long q1 = row + clampi(sx + 1, 0, a.W - 1);
+        float v0[3], v1[3];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            v0[c] = St<TNI>::ld(pnb + c * HW + q0);
+            v1[c] = St<TNI>::ld(pnb + c * HW + q1);
+        }
+        if (FUSE_RR) {
+            ray_relu_f32(v0[0], v0[1], v0[2], __ldg(ray + q0), __ldg(ray + HW + q0),
+                         __ldg(ray + 2 * HW + q0));
+            ray_relu_f32(v1[0], v1[1], v1[2], __ldg(ray + q1), __ldg(ray + HW + q1),
+                         __ldg(ray + 2 * HW + q1));
+        }
+        const float i0 =
+            rsqrtf(fmaxf(fmaf(v0[0], v0[0], fmaf(v0[1], v0[1], v0[2] * v0[2])), 1e-24f));
+        const float i1 =
+            rsqrtf(fmaxf(fmaf(v1[0], v1[0], fmaf(v1[1], v1[1], v1[2] * v1[2])), 1e-24f));
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const float u0 = v0[c] * i0, u1 = v1[c] * i1;
+            T.e[c][i * SWH + k] = make_float2(u0, u1);     // E[i][k]
+            float* op = reinterpret_cast<float*>(T.o[c] + i * SWH);
+            op[2 * k] = u1;                                 // O[i][k].x
+            if (k > 0) op[2 * k - 1] = u0;                  // O[i][k-1].y
+        }
+    }
+    for (int k = threadIdx.x; k < SWH; k += kThreads) {
+        float t[3];
+#pragma unroll
+        for (int d = 0; d < 3; ++d)
+            t[d] = fmaf((float)clampi(x0 - R + 2 * k + d, 0, a.W - 1), a.ifu, a.tu_c);
+        T.tue[k] = make_float4(t[0], t[1], -t[0], -t[1]);
+        T.tuo[k] = make_float4(t[1], t[2], -t[1], -t[2]);
+    }
+    for (int i = threadIdx.x; i < SH; i += kThreads)
+        T.tv[i] = fmaf((float)clampi(y0 - R + i, 0, a.H - 1), a.ifv, a.tv_c);
 }
 
 // The staged operands of the pair starting at column j of halo row i.
@@ -521,7 +577,7 @@ angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* 
     auto ld = [&](const TS* base) -> float2 {
         return vec ? St<TS>::ld2s(base + p0) : f2(St<TS>::lds1(base + p0), St<TS>::lds1(base + p1));
     };
-    const float2 ifu2 = f2(a.ifu), ifv2 = f2(a.ifv), nifu2 = f2(-a.ifu), nifv2 = f2(-a.ifv);
+    const float2 ifu2 = f2(a.ifu), ifv2 = f2(a.ifv);
     PairAcc<Mask> A{f2(0.f), f2(0.f), f2(0.f), 0, 0};
 #pragma unroll 1
     for (int ky = 0; ky < PS; ++ky) {
@@ -532,7 +588,7 @@ angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* 
             const NPair q = npair(T, i, lx + kx * a.dil);
             angmf_pair<Mask>(n, ld(xyb + (long)n * HW), ld(xyb + (long)(P + n) * HW),
                              ld(anb + (long)n * HW), ld(prb + (long)n * HW), q.nx, q.ny, q.nz,
-                             q.tu, q.tun, q.tv, ifu2, ifv2, nifu2, nifv2, rx, ry, rz, A);
+                             q.tu, q.tun, q.tv, ifu2, ifv2, rx, ry, rz, A);
         }
     }
     finish_pair<PS, TS, TNI, TNO, FUSE_RR>(A, b, x, y, two, vec, pn, prob, xy, ang, ray, out, a);
@@ -544,10 +600,13 @@ angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* 
 // exactly the data its own lanes will consume -- the four channel strips
 // (prob, x offset, y offset, angle; 2 rows x 32 pixels each) -- global ->
 // shared with 16-byte cp.async into a warp-private ring of kN = kM * PS
-// slots, kN-1 slots ahead of the one being computed. Memory latency is covered
-// by the copies in flight instead of registers, and publishing a slot needs
-// only a warp barrier. With the window size, the dilation and the window
-// column compile-time constants, every shared-memory offset is an immediate.
+// slots (slot of neighbour n: n mod kN), kD = kN - kSP slots ahead of the one
+// being computed. Memory latency is covered by the copies in flight instead of
+// registers, and publishing slots needs only a warp barrier: one per kSP
+// neighbour slots (two for fp16 storage, so that two neighbours' dependency
+// chains interleave between barriers). With the window size, the dilation and
+// the window column compile-time constants, every shared-memory offset is an
+// immediate.
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
     const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem),
@@ -568,6 +627,8 @@ struct Stages {
     static constexpr int kElemsW = 4 * kRowsW * kTW;       // per warp per slot
     static constexpr int kM = (sizeof(TS) == 2 && PS < 7) ? 2 : 1;  // window rows per ring
     static constexpr int kN = kM * PS;                     // ring depth
+    static constexpr int kSP = sizeof(TS) == 2 ? 2 : 1;    // slots per warp barrier
+    static constexpr int kD = kN - kSP;                    // slots issued ahead
     static constexpr size_t kBytes = (size_t)(kThreads / 32) * kN * kElemsW * sizeof(TS);
 };
 
@@ -606,8 +667,8 @@ angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
     TS* ring = reinterpret_cast<TS*>(smem4) + warp * S::kN * S::kElemsW;  // this warp's slots
     NTile T;
     T.carve(reinterpret_cast<char*>(smem4) + S::kBytes, SW, SH);
-    int b, x0, y0;
-    tile_of(a, b, x0, y0);
+    // grid (tiles_x, tiles_y, frames)
+    const int b = blockIdx.z, x0 = blockIdx.x * kTW, y0 = blockIdx.y * kTH;
     const long HW = a.HW;
     const TS* xyb = xy + (long)b * 2 * P * HW;
     const TS* prb = prob + (long)b * P * HW;
@@ -638,13 +699,13 @@ angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
         }
     };
 
-    // prologue: the first kN-1 slots in flight while the normals are staged
+    // prologue: the first kD slots in flight while the normals are staged
 #pragma unroll
-    for (int sl = 0; sl < S::kN - 1; ++sl) {
+    for (int sl = 0; sl < S::kD; ++sl) {
         if (sl < P) issue(sl);
         cp_async_commit();
     }
-    stage_normals<TNI, FUSE_RR>(pn + (long)b * 3 * HW, ray, T, x0, y0, a);
+    stage_normals_ct<R, TNI, FUSE_RR>(pn + (long)b * 3 * HW, ray, T, x0, y0, a);
     __syncthreads();  // the normal halo is shared by all warps
 
     const int lx = 2 * (lane & 15);
@@ -656,7 +717,7 @@ angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
     const long p1 = two ? p0 + 1 : p0;
     float2 rx, ry, rz;
     pair_ray(ray, HW, p0, p1, rx, ry, rz);
-    const float2 ifu2 = f2(a.ifu), ifv2 = f2(a.ifv), nifu2 = f2(-a.ifu), nifv2 = f2(-a.ifv);
+    const float2 ifu2 = f2(a.ifu), ifv2 = f2(a.ifv);
     PairAcc<Mask> A{f2(0.f), f2(0.f), f2(0.f), 0, 0};
     constexpr int kStrip = S::kRowsW * kTW;
     const TS* ring_lane = ring + (lane >> 4) * kTW + lx;   // this pair inside a slot
@@ -672,10 +733,24 @@ angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
 #pragma unroll
         for (int kx = 0; kx < PS; ++kx) {
             const int n = ky * PS + kx;
-            cp_async_wait<S::kN - 2>();
-            __syncwarp();  // slot n visible to the warp; every lane is done with slot n-1
-            if (n + S::kN - 1 < P) issue(kx > 0 ? grp + kx - 1 : prev_grp + PS - 1);
-            cp_async_commit();
+            if (kx % S::kSP == 0) {
+                // a group of gs slots (the last of a window row may be short);
+                // one commit group per slot, so the wait depth is kD - gs
+                const int gs = PS - kx < S::kSP ? PS - kx : S::kSP;
+                static_assert(S::kSP <= 2, "wait depths below cover groups of 1 or 2");
+                if (gs == 2) cp_async_wait<S::kD - 2>();
+                else cp_async_wait<S::kD - 1>();
+                __syncwarp();  // the group's slots visible; every lane done with earlier slots
+                // refill the slots of the previous kSP neighbours with the ones kD ahead
+#pragma unroll
+                for (int e = 0; e < S::kSP; ++e) {
+                    if (e < gs) {
+                        const int j = kx + e - S::kSP;  // window column of neighbour n+e-kSP
+                        if (n + e + S::kD < P) issue(j >= 0 ? grp + j : prev_grp + PS + j);
+                        cp_async_commit();
+                    }
+                }
+            }
             if (active) {
                 const TS* st = st_row + kx * S::kElemsW;
                 // window column offset: a constant once the kx loop is unrolled
@@ -699,7 +774,7 @@ angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
                 }
                 angmf_pair<Mask>(n, lds2<TS>(st + 1 * kStrip), lds2<TS>(st + 2 * kStrip),
                                  lds2<TS>(st + 3 * kStrip), lds2<TS>(st), nx, ny, nz, tu, tun,
-                                 tv, ifu2, ifv2, nifu2, nifv2, rx, ry, rz, A);
+                                 tv, ifu2, ifv2, rx, ry, rz, A);
             }
         }
     }
@@ -733,18 +808,31 @@ cudaError_t launch_t(const AngmfLaunch& L, cudaStream_t s) {
     // staged copies need every 16-byte chunk of a row to start on a 16-byte
     // boundary (W a multiple of 16 bytes of storage); dilations 1 and 2 (the
     // benchmark windows) have compile-time staged variants
-    if ((L.W % Stages<TS, PS>::kEpc) == 0 && (L.dil == 1 || L.dil == 2)) {
+    if ((L.W % Stages<TS, PS>::kEpc) == 0 && (L.dil == 1 || L.dil == 2) &&
+        a.tiles_y <= 65535) {
         const size_t smem = Stages<TS, PS>::kBytes + nsmem;  // = StagedCfg<...>::kSmem
         auto kern = L.dil == 1 ? angmf_staged_kernel<PS, 1, TS, TNI, TNO, FUSE_RR>
                                : angmf_staged_kernel<PS, 2, TS, TNI, TNO, FUSE_RR>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
         if (e != cudaSuccess) return e;
-        kern<<<(unsigned)blocks, kThreads, smem, s>>>(
-            static_cast<const TNI*>(L.pn), static_cast<const TS*>(L.prob),
-            static_cast<const TS*>(L.xy), static_cast<const TS*>(L.angle), L.ray,
-            static_cast<TNO*>(L.out), a);
-        return cudaGetLastError();
+        // grid (tiles_x, tiles_y, frames), frames in launches of at most 65535
+        constexpr int P = PS * PS;
+        constexpr long kMaxZ = 65535;
+        for (long b0 = 0; b0 < L.B; b0 += kMaxZ) {
+            const long nb = L.B - b0 < kMaxZ ? L.B - b0 : kMaxZ;
+            a.B = (int)nb;
+            const dim3 grid((unsigned)a.tiles_x, (unsigned)a.tiles_y, (unsigned)nb);
+            kern<<<grid, kThreads, smem, s>>>(
+                static_cast<const TNI*>(L.pn) + b0 * 3 * a.HW,
+                static_cast<const TS*>(L.prob) + b0 * P * a.HW,
+                static_cast<const TS*>(L.xy) + b0 * 2 * P * a.HW,
+                static_cast<const TS*>(L.angle) + b0 * P * a.HW, L.ray,
+                static_cast<TNO*>(L.out) + b0 * 3 * a.HW, a);
+            e = cudaGetLastError();
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
     }
     auto kern = angmf_kernel<PS, TS, TNI, TNO, FUSE_RR>;
     if (nsmem > 48 * 1024) {
