@@ -35,6 +35,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import sys
@@ -211,15 +212,17 @@ def cpu_reference_sample(cfg, threads=0, seconds_min=10.0):
         return time.perf_counter() - t0
 
     frames = nthreads if kind == "reference" else 1
-    dt = run(frames)
-    # grow to a 10-30 s CPU-work sample
-    cpu_s = dt * (nthreads if kind == "reference" else 1)
+    dt = run(frames)  # also the warm-up
+    # grow to a sample of at least `seconds_min` of CPU work (wall x threads),
+    # whole rounds of one frame per thread, then time it warm
+    cores = nthreads if kind == "reference" else 1
+    cpu_s = dt * cores
     if cpu_s < seconds_min:
-        frames = max(frames, int(frames * seconds_min / max(cpu_s, 1e-3)))
+        frames = math.ceil(frames * seconds_min / max(cpu_s, 1e-3))
         if kind == "reference":
-            frames = max(nthreads, (frames // nthreads) * nthreads)
-        dt = run(frames)
-    return frames * per_frame_px / dt / 1e6, (nthreads if kind == "reference" else 1), frames, dt, kind
+            frames = math.ceil(frames / nthreads) * nthreads
+    dt = run(frames)
+    return frames * per_frame_px / dt / 1e6, cores, frames, dt, kind
 
 
 def reference_arm(args, cfg):
@@ -478,8 +481,9 @@ def main():
             line["cpu_baseline"] = {
                 "value": round(v, 3), "unit": "Mpixel/s", "cores": cores, "kind": kind,
                 "sample": f"{frames} frames of {cfg['W']}x{cfg['H']} (one generated frame "
-                          f"repeated), {secs:.1f} s wall; reference dsine_ops.cpp CPU twin "
-                          f"(fp32 storage, fp64 math) + restated upsample"}
+                          f"repeated), {secs:.1f} s wall x {cores} threads; reference "
+                          f"dsine_ops.cpp CPU twin (fp32 storage, fp64 math) + restated "
+                          f"upsample"}
         except Exception as e:  # the baseline is reported, never required
             line["cpu_baseline"] = {"value": None, "unit": "Mpixel/s", "cores": 0,
                                     "kind": "reference", "sample": f"failed: {e}"}
