@@ -213,7 +213,10 @@ struct PairAcc {
 // One neighbour slot n for a pixel pair: rotate the (unit) source normals,
 // RayReLU them against the pixels' (unit) rays, accumulate with weight w.
 // tun = -tu is supplied by the caller (from the staged table).
-template <typename Mask>
+// QRANGE: test |xy|^2 against [kQMin, kQMax]. fp16 inputs cannot leave that
+// range except for an all-zero pair (|xy|^2 lies in {0} u [3.6e-15, 8.6e9]),
+// and a zero pair makes dd = inf * 0 = NaN, which the |dd| test flags.
+template <typename Mask, bool QRANGE>
 __device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 th, float2 wt,
                                            float2 nx, float2 ny, float2 nz, float2 tu,
                                            float2 tun, float2 tv, float2 ifu2, float2 ifv2,
@@ -255,10 +258,15 @@ __device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 t
     const float2 mz = fma2(rz, dc, qz);
     const float2 l2 = fma2(mx, mx, fma2(my, my, mul2(mz, mz)));
     // bitwise | : every test is evaluated, no branches
-    const bool b0 = !(fabsf(dd.x) >= kTau) | !(gcond.x <= 1.0f / (kGCond * kGCond)) | !(l2.x >= kMMin) |
-                    !(q.x >= kQMin) | !(q.x <= kQMax) | !(fabsf(th.x) <= kThMax);
-    const bool b1 = !(fabsf(dd.y) >= kTau) | !(gcond.y <= 1.0f / (kGCond * kGCond)) | !(l2.y >= kMMin) |
-                    !(q.y >= kQMin) | !(q.y <= kQMax) | !(fabsf(th.y) <= kThMax);
+    constexpr float kGMax = 1.0f / (kGCond * kGCond);
+    bool b0 = !(fabsf(dd.x) >= kTau) | !(gcond.x <= kGMax) | !(l2.x >= kMMin) |
+              !(fabsf(th.x) <= kThMax);
+    bool b1 = !(fabsf(dd.y) >= kTau) | !(gcond.y <= kGMax) | !(l2.y >= kMMin) |
+              !(fabsf(th.y) <= kThMax);
+    if constexpr (QRANGE) {
+        b0 |= !(q.x >= kQMin) | !(q.x <= kQMax);
+        b1 |= !(q.y >= kQMin) | !(q.y <= kQMax);
+    }
     float2 wm = mul2(wt, rsqrt2_ftz(l2));
     float2 ux = mx, uy = my, uz = mz;
     if (b0 | b1) {  // rare: leave the neighbour to the exact fix-up
@@ -586,9 +594,10 @@ angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* 
         for (int kx = 0; kx < PS; ++kx) {
             const int n = ky * PS + kx;
             const NPair q = npair(T, i, lx + kx * a.dil);
-            angmf_pair<Mask>(n, ld(xyb + (long)n * HW), ld(xyb + (long)(P + n) * HW),
-                             ld(anb + (long)n * HW), ld(prb + (long)n * HW), q.nx, q.ny, q.nz,
-                             q.tu, q.tun, q.tv, ifu2, ifv2, rx, ry, rz, A);
+            angmf_pair<Mask, sizeof(TS) == 4>(
+                n, ld(xyb + (long)n * HW), ld(xyb + (long)(P + n) * HW), ld(anb + (long)n * HW),
+                ld(prb + (long)n * HW), q.nx, q.ny, q.nz, q.tu, q.tun, q.tv, ifu2, ifv2, rx, ry,
+                rz, A);
         }
     }
     finish_pair<PS, TS, TNI, TNO, FUSE_RR>(A, b, x, y, two, vec, pn, prob, xy, ang, ray, out, a);
@@ -772,9 +781,10 @@ angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
                     tu = f2(t4.x, t4.y);
                     tun = f2(t4.z, t4.w);
                 }
-                angmf_pair<Mask>(n, lds2<TS>(st + 1 * kStrip), lds2<TS>(st + 2 * kStrip),
-                                 lds2<TS>(st + 3 * kStrip), lds2<TS>(st), nx, ny, nz, tu, tun,
-                                 tv, ifu2, ifv2, rx, ry, rz, A);
+                angmf_pair<Mask, sizeof(TS) == 4>(
+                    n, lds2<TS>(st + 1 * kStrip), lds2<TS>(st + 2 * kStrip),
+                    lds2<TS>(st + 3 * kStrip), lds2<TS>(st), nx, ny, nz, tu, tun, tv, ifu2, ifv2,
+                    rx, ry, rz, A);
             }
         }
     }

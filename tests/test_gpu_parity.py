@@ -126,6 +126,32 @@ def test_angmf_f16_storage(ps, dil):
     report(f"angmf f16 ps{ps} d{dil}", got, want, TOL16)
 
 
+def test_angmf_f16_degenerate_offsets():
+    """fp16 storage (no |xy|^2 range test there): zero, signed-zero and
+    subnormal xy pairs, theta 0 and fp16(pi), through the staged kernel."""
+    b = lib()
+    u = O.to_f16_storage(O.gen_unit(512, 768, 1, iters=1, seed=91, upsample=False))
+    xy, ang = u.xy[0].copy(), u.angle[0].copy()
+    P = ang.shape[1]
+    g = np.random.default_rng(17)
+    pick = g.random(ang.shape)
+    xs, ys = xy[:, :P], xy[:, P:]
+    zero = pick < 0.08
+    xs[zero], ys[zero] = 0.0, -0.0
+    tiny = (pick >= 0.08) & (pick < 0.12)          # binary16 subnormals
+    xs[tiny] = np.where(g.random(tiny.sum()) < 0.5, 6e-8, -1.2e-7)
+    ys[tiny] = np.where(g.random(tiny.sum()) < 0.5, 0.0, 3e-7)
+    ang[(pick >= 0.12) & (pick < 0.15)] = 0.0
+    ang[(pick >= 0.15) & (pick < 0.18)] = np.pi
+    xy, ang = O.f16_round(xy), O.f16_round(ang)
+    n0 = O.f16_round(O.ray_relu(u.normal0, u.ray8))
+    want = O.angmf(n0, u.prob[0], xy, ang, u.ray8, u.fu, u.cu, u.fv, u.cv)
+    h16 = torch.float16
+    got = b.angmf_propagate(dev(n0, h16), dev(u.prob[0], h16), dev(xy, h16), dev(ang, h16),
+                            dev(u.ray8), u.fu, u.cu, u.fv, u.cv)
+    report("angmf f16 degenerate", host(got), want, TOL16)
+
+
 def test_angmf_golden_edge_cases():
     """Hand-placed degeneracies (zero xy, |xy| < 1e-12, theta 0 / 1e-7 / pi,
     zero and non-unit normals, (P+d).n ~ 0) against the reference's outputs."""
