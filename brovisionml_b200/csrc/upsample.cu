@@ -136,6 +136,7 @@ template <> struct OutRun<float> {
 };
 template <> struct OutRun<__half> {
     __half2 v[3][2][4];  // 8 sub-columns x 2 pixels per channel, as half pairs
+    float ev[3][2];      // the even sub-column's results, until the odd one packs them
 };
 
 template <typename TNI, typename TS, bool NORM, bool RR, bool STAGED>
@@ -305,16 +306,17 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
                 }
                 // collect; flush a 16-byte run per channel and pixel when complete
                 if constexpr (sizeof(TS) == 2) {
-                    // half pairs (kx even, kx odd) per pixel
+                    // half pairs (kx even, kx odd) per pixel, one packed
+                    // conversion each once the odd sub-column is done
                     const float o[3][2] = {{ox.x, ox.y}, {oy.x, oy.y}, {oz.x, oz.y}};
 #pragma unroll
                     for (int c = 0; c < 3; ++c)
 #pragma unroll
                         for (int e = 0; e < 2; ++e) {
                             if ((kx & 1) == 0)
-                                run.v[c][e][kx >> 1].x = __float2half_rn(o[c][e]);
+                                run.ev[c][e] = o[c][e];
                             else
-                                run.v[c][e][kx >> 1].y = __float2half_rn(o[c][e]);
+                                run.v[c][e][kx >> 1] = __floats2half2_rn(run.ev[c][e], o[c][e]);
                         }
                     if (kx == 7 && row_in && active) {
                         TS* orow = out + (long)b * 3 * a.out_h * a.out_w + (long)Yo * a.out_w;
