@@ -20,7 +20,7 @@ BVML_OK = 0
 EXPORTS = ("bvml_last_error", "bvml_abi_version", "bvml_ray_relu", "bvml_angmf_propagate",
            "bvml_convex_upsample", "bvml_l2_normalize_nchw", "bvml_slice2d",
            "bvml_refine_workspace_bytes", "bvml_refine", "bvml_probe_events",
-           "bvml_refine_noalloc")
+           "bvml_refine_noalloc", "bvml_angmf_propagate_logits", "bvml_refine_logits")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(
@@ -43,6 +43,8 @@ lib.bvml_ray_relu.argtypes = [_vp, _vp, _i, _i, _i, _i, _vp]
 lib.bvml_angmf_propagate.restype = _i
 lib.bvml_angmf_propagate.argtypes = [_vp, _vp, _vp, _vp, _vp, _d, _d, _d, _d, _i, _i, _i, _i, _i,
                                      _i, _vp, _vp]
+lib.bvml_angmf_propagate_logits.restype = _i
+lib.bvml_angmf_propagate_logits.argtypes = lib.bvml_angmf_propagate.argtypes
 lib.bvml_convex_upsample.restype = _i
 lib.bvml_convex_upsample.argtypes = [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp]
 lib.bvml_l2_normalize_nchw.restype = _i
@@ -55,6 +57,8 @@ lib.bvml_refine.restype = _i
 lib.bvml_refine.argtypes = ([_vp, _vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
                              ctypes.POINTER(_vp), _i, _vp] + [_i] * 5 + [_d] * 4 + [_i] * 6
                             + [_vp, _sz, _vp, _vp])
+lib.bvml_refine_logits.restype = _i
+lib.bvml_refine_logits.argtypes = lib.bvml_refine.argtypes
 lib.bvml_refine_noalloc.restype = _i
 lib.bvml_refine_noalloc.argtypes = ([_vp, _vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
                                      ctypes.POINTER(_vp), _i, _vp] + [_i] * 5 + [_d] * 4

@@ -1,898 +1,14 @@
-// Fused AngMF propagate for sm_100a.
-//
-// Replaces the reference's angmf_kernel (src/dsine_ops.cu:76-155, one thread
-// per pixel, fp64 math, 25 uncached gathers of the neighbour normals) with:
-//
-//  * a CTA tile of 16 x 32 output pixels whose replicate-padded halo of source
-//    normals ((16+2R) x (32+2R), R = (ps/2)*dil) is staged once in shared
-//    memory, already unit-length (and, for the first iteration of the fused
-//    refine, already RayReLU'd: the initial ray_relu of
-//    src/dsine_refine.cpp:241-242 costs no extra pass);
-//  * per-neighbour streams (prob, xy pair, angle) read exactly once, in
-//    coalesced pixel pairs, evict-first;
-//  * fp32 arithmetic carried two pixels at a time in packed f32x2 form, using
-//    a closed form of the reference's per-neighbour geometry (below) that
-//    needs no division and no fp64: three rsqrt and one sin / cos pair;
-//  * an exact fp64 fix-up, identical in arithmetic to the reference
-//    (src/dsine_ops.cpp:110-162), for the rare neighbours whose fp32
-//    evaluation would be ill-conditioned or out of range.
-//
-// Closed form. With source ray P = (tu0, tv0, 1), tu0 = (sx+0.5-cu)/fu,
-// tv0 = (sy+0.5-cv)/fv, unit xy offset (xs, ys), d = (xs/fu, ys/fv, 0), and
-// unit source normal n, the reference builds
-//     dd = (P + d).n,  dz = -(d.n)/dd,  a = d + dz (P + d),
-// so a.n = 0 and dd a = n x (d x P) (vector triple product). Writing
-// g = d x P and g_perp = g - n (n.g), the rotation about unit(a) by theta is
-//     R n = cos(theta) n + sign(dd) sin(theta) g_perp / |g_perp|
-// (Rodrigues with the axis orthogonal to n). g is scale-free here, so the raw
-// xy pair can be used for it: g ~ (ys/fv, -xs/fu, xs tv0/fu - ys tu0/fv);
-// only dd needs the normalised pair (one rsqrt). The quaternion route of
-// axis_angle_to_matrix (src/dsine_ops.cpp:31-51) computes the same rotation.
-// sin and cos come from the hardware approximations (sin.approx / cos.approx,
-// absolute error ~5e-7 on |theta| <= pi).
-//
-// Fix-up criteria (per pixel, per neighbour), each a place where the fp32
-// evaluation can leave the reference's fp64 result by more than ~1e-6:
-//  * |dd| < 1e-5: the sign of dd (which flips the rotation) may be wrong in
-//    fp32, and the reference clamps |dd| < 1e-8;
-//  * w |sin(theta)| |g| > 20 |g_perp|: g nearly parallel to n, so the rotation
-//    direction comes from a cancellation; its fp32 error (~2e-7 |g|/|g_perp|)
-//    is only tolerable while the neighbour's weighted sine is small;
-//  * |m|^2 < 0.04 after the RayReLU: the rotated normal points almost straight
-//    away from the camera and the clamped vector is a cancellation too;
-//  * |xy|^2 outside [1e-10, 1e30] (the reference's 1e-12 clamp on |xy|, or
-//    fp32 overflow), |theta| > pi (outside the approximations' range), or any
-//    NaN.
-// Such neighbours are dropped from the fast sum, recorded in a bit mask and
-// recomputed after the loop in fp64 exactly as the reference does. On
-// camera-facing inputs this is about 1 neighbour evaluation in 10^5.
-#include "bvml_common.cuh"
-#include "bvml_internal.h"
-
-#include <type_traits>
+// AngMF launch entry point: inputs already activated (prob in [0, 1], angle in
+// radians), as brovisionml's angmf_propagate takes them
+// (include/brovisionml/dsine_ops.h:28-54). Raw head outputs go to
+// angmf_logits.cu. The kernels live in angmf_kernels.cuh.
+#include "angmf_kernels.cuh"
 
 namespace bvml {
-namespace {
-
-constexpr int kTW = 32;         // tile width (16 pixel pairs)
-constexpr int kTH = 16;         // tile height
-constexpr int kThreads = 256;   // one pixel pair per thread
-
-struct AngmfArgs {
-    int B, H, W, dil, R, tiles_x, tiles_y;
-    long HW;
-    float ifu, ifv, tu_c, tv_c;   // 1/fu, 1/fv, (0.5-cu)/fu, (0.5-cv)/fv
-    double fu, cu, fv, cv;        // exact values for the fp64 fix-up
-};
-
-// RayReLU of one normal in fp32 (src/dsine_ops.cpp:55-76 semantics).
-__device__ __forceinline__ void ray_relu_f32(float& nx, float& ny, float& nz, float rx, float ry,
-                                             float rz) {
-    const float nn2 = fmaf(nx, nx, fmaf(ny, ny, nz * nz));
-    const float rr2 = fmaf(rx, rx, fmaf(ry, ry, rz * rz));
-    const float c = fmaf(nx, rx, fmaf(ny, ry, nz * rz)) * rsqrtf(fmaxf(nn2 * rr2, 1e-16f));
-    const float dc = fmaxf(kRayEps - c, 0.0f);
-    nx = fmaf(rx, dc, nx);
-    ny = fmaf(ry, dc, ny);
-    nz = fmaf(rz, dc, nz);
-    const float inv = rsqrtf(fmaxf(fmaf(nx, nx, fmaf(ny, ny, nz * nz)), 1e-24f));
-    nx *= inv;
-    ny *= inv;
-    nz *= inv;
-}
-
-__device__ __forceinline__ double dmax(double a, double b) { return (a < b) ? b : a; }
-
-// Products and sums in the fp64 code below go through __dmul_rn / __dadd_rn so
-// that no contracted fused multiply-add changes their rounding relative to the
-// CPU twin (which is compiled without contraction).
-__device__ __forceinline__ double dot3(double a0, double a1, double a2, double b0, double b1,
-                                       double b2) {
-    return __dadd_rn(__dadd_rn(__dmul_rn(a0, b0), __dmul_rn(a1, b1)), __dmul_rn(a2, b2));
-}
-
-// RayReLU in fp64 with the CPU twin's arithmetic (src/dsine_ops.cpp:59-75),
-// rounded to float like the reference's stored pred_norm.
-__device__ void ray_relu_exact(double& nx, double& ny, double& nz, double rx, double ry,
-                               double rz) {
-    const double nn = sqrt(dot3(nx, ny, nz, nx, ny, nz));
-    const double rr = sqrt(dot3(rx, ry, rz, rx, ry, rz));
-    const double denom = dmax(__dmul_rn(nn, rr), 1e-8);
-    const double cs = dot3(nx, ny, nz, rx, ry, rz) / denom;
-    const double eps = (double)kRayEps;
-    const double dcoef = (dmax(cs - eps, 0.0) + eps) - cs;
-    const double m0 = __dadd_rn(nx, __dmul_rn(rx, dcoef));
-    const double m1 = __dadd_rn(ny, __dmul_rn(ry, dcoef));
-    const double m2 = __dadd_rn(nz, __dmul_rn(rz, dcoef));
-    const double inv = 1.0 / dmax(sqrt(dot3(m0, m1, m2, m0, m1, m2)), 1e-12);
-    nx = (double)(float)__dmul_rn(m0, inv);
-    ny = (double)(float)__dmul_rn(m1, inv);
-    nz = (double)(float)__dmul_rn(m2, inv);
-}
-
-// One neighbour's weighted contribution in fp64, operation for operation as
-// src/dsine_ops.cpp:104-162 (the fix-up path; see the file header).
-__device__ __noinline__ double3 angmf_neighbor_exact(double nx, double ny, double nz, int sx,
-                                                     int sy, double xs, double ys, double theta,
-                                                     double w, double rx, double ry, double rz,
-                                                     double fu, double cu, double fv,
-                                                     double cv) {
-    const double pix_x = sx + 0.5, pix_y = sy + 0.5;
-    const double xyinv = 1.0 / dmax(sqrt(__dadd_rn(__dmul_rn(xs, xs), __dmul_rn(ys, ys))), 1e-12);
-    xs = __dmul_rn(xs, xyinv);
-    ys = __dmul_rn(ys, xyinv);
-    const double du = xs / fu;
-    const double dv = ys / fv;
-    const double tu = (pix_x + xs - cu) / fu;
-    const double tv = (pix_y + ys - cv) / fv;
-    const double num = -__dadd_rn(__dmul_rn(du, nx), __dmul_rn(dv, ny));
-    double dd = __dadd_rn(__dadd_rn(__dmul_rn(tu, nx), __dmul_rn(tv, ny)), nz);
-    if (fabs(dd) < 1e-8) {
-        const double sgn = (dd > 0.0) ? 1.0 : (dd < 0.0 ? -1.0 : 0.0);
-        dd = 1e-8 * sgn;
-    }
-    const double dz = num / dd;
-    double ax = __dadd_rn(du, __dmul_rn(dz, tu));
-    double ay = __dadd_rn(dv, __dmul_rn(dz, tv));
-    double az = dz;
-    const double an =
-        sqrt(__dadd_rn(__dadd_rn(__dmul_rn(ax, ax), __dmul_rn(ay, ay)), __dmul_rn(az, az)));
-    const double ainv = 1.0 / dmax(an, 1e-12);
-    ax = __dmul_rn(ax, ainv);
-    ay = __dmul_rn(ay, ainv);
-    az = __dmul_rn(az, ainv);
-    if (!isfinite(ax) || !isfinite(ay) || !isfinite(az)) ax = ay = az = 0.0;
-    // axis_angle_to_matrix on axis * theta (quaternion route).
-    const double vx = __dmul_rn(ax, theta), vy = __dmul_rn(ay, theta), vz = __dmul_rn(az, theta);
-    const double ang =
-        sqrt(__dadd_rn(__dadd_rn(__dmul_rn(vx, vx), __dmul_rn(vy, vy)), __dmul_rn(vz, vz)));
-    const double half = ang * 0.5;
-    double s;
-    if (ang < 1e-6)
-        s = 0.5 - __dmul_rn(ang, ang) / 48.0;
-    else
-        s = sin(half) / ang;
-    const double qr = cos(half);
-    const double qi = __dmul_rn(vx, s), qj = __dmul_rn(vy, s), qk = __dmul_rn(vz, s);
-    const double two_s =
-        2.0 / __dadd_rn(__dadd_rn(__dadd_rn(__dmul_rn(qr, qr), __dmul_rn(qi, qi)),
-                                  __dmul_rn(qj, qj)),
-                        __dmul_rn(qk, qk));
-    const double ii = __dmul_rn(qi, qi), jj = __dmul_rn(qj, qj), kk = __dmul_rn(qk, qk);
-    const double ij = __dmul_rn(qi, qj), ik = __dmul_rn(qi, qk), jk = __dmul_rn(qj, qk);
-    const double ir = __dmul_rn(qi, qr), jr = __dmul_rn(qj, qr), kr = __dmul_rn(qk, qr);
-    const double R0 = 1.0 - __dmul_rn(two_s, __dadd_rn(jj, kk));
-    const double R1 = __dmul_rn(two_s, ij - kr);
-    const double R2 = __dmul_rn(two_s, __dadd_rn(ik, jr));
-    const double R3 = __dmul_rn(two_s, __dadd_rn(ij, kr));
-    const double R4 = 1.0 - __dmul_rn(two_s, __dadd_rn(ii, kk));
-    const double R5 = __dmul_rn(two_s, jk - ir);
-    const double R6 = __dmul_rn(two_s, ik - jr);
-    const double R7 = __dmul_rn(two_s, __dadd_rn(jk, ir));
-    const double R8 = 1.0 - __dmul_rn(two_s, __dadd_rn(ii, jj));
-    double qx = __dadd_rn(__dadd_rn(__dmul_rn(R0, nx), __dmul_rn(R1, ny)), __dmul_rn(R2, nz));
-    double qy = __dadd_rn(__dadd_rn(__dmul_rn(R3, nx), __dmul_rn(R4, ny)), __dmul_rn(R5, nz));
-    double qz = __dadd_rn(__dadd_rn(__dmul_rn(R6, nx), __dmul_rn(R7, ny)), __dmul_rn(R8, nz));
-    const double rinv = 1.0 / dmax(sqrt(__dadd_rn(__dadd_rn(__dmul_rn(qx, qx), __dmul_rn(qy, qy)),
-                                                  __dmul_rn(qz, qz))),
-                                   1e-12);
-    qx = __dmul_rn(qx, rinv);
-    qy = __dmul_rn(qy, rinv);
-    qz = __dmul_rn(qz, rinv);
-    const double nn =
-        sqrt(__dadd_rn(__dadd_rn(__dmul_rn(qx, qx), __dmul_rn(qy, qy)), __dmul_rn(qz, qz)));
-    const double rr =
-        sqrt(__dadd_rn(__dadd_rn(__dmul_rn(rx, rx), __dmul_rn(ry, ry)), __dmul_rn(rz, rz)));
-    const double denom = dmax(__dmul_rn(nn, rr), 1e-8);
-    const double cs =
-        __dadd_rn(__dadd_rn(__dmul_rn(qx, rx), __dmul_rn(qy, ry)), __dmul_rn(qz, rz)) / denom;
-    const double eps = (double)kRayEps;
-    const double dcoef = (dmax(cs - eps, 0.0) + eps) - cs;
-    double m0 = __dadd_rn(qx, __dmul_rn(rx, dcoef));
-    double m1 = __dadd_rn(qy, __dmul_rn(ry, dcoef));
-    double m2 = __dadd_rn(qz, __dmul_rn(rz, dcoef));
-    const double minv = 1.0 / dmax(sqrt(__dadd_rn(__dadd_rn(__dmul_rn(m0, m0), __dmul_rn(m1, m1)),
-                                                  __dmul_rn(m2, m2))),
-                                   1e-12);
-    return make_double3(__dmul_rn(w, __dmul_rn(m0, minv)), __dmul_rn(w, __dmul_rn(m1, minv)),
-                        __dmul_rn(w, __dmul_rn(m2, minv)));
-}
-
-constexpr float kTau = 1e-5f;     // |dd| fix-up threshold
-constexpr float kGCond = 0.05f;   // 1 / (largest tolerated w |sin| |g| / |g_perp|)
-constexpr float kMMin = 0.04f;    // smallest tolerated |m|^2 after the RayReLU
-constexpr float kQMin = 1e-10f, kQMax = 1e30f;  // |xy|^2 range of the fast path
-constexpr float kThMax = 3.1416f; // |theta| range of the sin / cos approximations
-
-template <typename Mask>
-struct PairAcc {
-    float2 x, y, z;   // prob-weighted sums of the clamped, rotated neighbours
-    Mask bad0, bad1;  // neighbours left to the exact fix-up, per pixel of the pair
-};
-
-// One neighbour slot n for a pixel pair: rotate the (unit) source normals,
-// RayReLU them against the pixels' (unit) rays, accumulate with weight w.
-// tun = -tu is supplied by the caller (from the staged table).
-// QRANGE: test |xy|^2 against [kQMin, kQMax]. fp16 inputs cannot leave that
-// range except for an all-zero pair (|xy|^2 lies in {0} u [3.6e-15, 8.6e9]),
-// and a zero pair makes dd = inf * 0 = NaN, which the |dd| test flags.
-template <typename Mask, bool QRANGE>
-__device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 th, float2 wt,
-                                           float2 nx, float2 ny, float2 nz, float2 tu,
-                                           float2 tun, float2 tv, float2 ifu2, float2 ifv2,
-                                           float2 rx, float2 ry, float2 rz, PairAcc<Mask>& A) {
-    const float2 q = fma2(xs, xs, mul2(ys, ys));
-    const float2 iq = rsqrt2_ftz(q);
-    const float2 X = mul2(xs, ifu2), Y = mul2(ys, ifv2);     // d (unnormalised)
-    const float2 e = fma2(X, nx, mul2(Y, ny));               // d.n
-    const float2 as = fma2(tu, nx, fma2(tv, ny, nz));        // P.n
-    const float2 dd = fma2(iq, e, as);                       // (P + d).n, d normalised
-    // g = d x P = (Y, -X, gz); g_perp = g - n (g.n) = (gpx, -gpyn, gpz)
-    const float2 gz = fma2(X, tv, mul2(Y, tun));
-    const float2 ng = fma2(Y, nx, fnma2(X, ny, mul2(gz, nz)));
-    const float2 gpx = fnma2(nx, ng, Y);
-    const float2 gpyn = fma2(ny, ng, X);
-    const float2 gpz = fnma2(nz, ng, gz);
-    const float2 gp2 = fma2(gpx, gpx, fma2(gpyn, gpyn, mul2(gpz, gpz)));
-    const float2 gg2 = fma2(ng, ng, gp2);                    // |g|^2 = |g_perp|^2 + (n.g)^2
-    // |g_perp| = 0 gives an infinite or NaN kk below, which the fix-up tests catch
-    const float2 gi = rsqrt2_ftz(gp2);
-    // sin / cos of theta with the hardware approximations (abs. error ~5e-7
-    // on |theta| <= pi; larger angles are left to the fix-up)
-    const float2 sn = sin2_approx(th);
-    const float2 cs = cos2_approx(th);
-    float2 kk = mul2(sn, gi);
-    // w |sin| |g| > |g_perp| / kGCond  <=>  (w sin / |g_perp|)^2 |g|^2 > 1 / kGCond^2
-    const float2 wk = mul2(wt, kk);
-    const float2 gcond = mul2(mul2(wk, wk), gg2);
-    kk.x = __uint_as_float(__float_as_uint(kk.x) ^ (__float_as_uint(dd.x) & 0x80000000u));
-    kk.y = __uint_as_float(__float_as_uint(kk.y) ^ (__float_as_uint(dd.y) & 0x80000000u));
-    const float2 qx = fma2(kk, gpx, mul2(cs, nx));
-    const float2 qy = fnma2(kk, gpyn, mul2(cs, ny));
-    const float2 qz = fma2(kk, gpz, mul2(cs, nz));
-    // RayReLU against the pixels' rays, then the weighted sum
-    const float2 c = fma2(qx, rx, fma2(qy, ry, mul2(qz, rz)));
-    const float2 dc = max2(fma2(c, f2(-1.0f), f2(kRayEps)), f2(0.0f));
-    const float2 mx = fma2(rx, dc, qx);
-    const float2 my = fma2(ry, dc, qy);
-    const float2 mz = fma2(rz, dc, qz);
-    const float2 l2 = fma2(mx, mx, fma2(my, my, mul2(mz, mz)));
-    // bitwise | : every test is evaluated, no branches
-    constexpr float kGMax = 1.0f / (kGCond * kGCond);
-    bool b0 = !(fabsf(dd.x) >= kTau) | !(gcond.x <= kGMax) | !(l2.x >= kMMin) |
-              !(fabsf(th.x) <= kThMax);
-    bool b1 = !(fabsf(dd.y) >= kTau) | !(gcond.y <= kGMax) | !(l2.y >= kMMin) |
-              !(fabsf(th.y) <= kThMax);
-    if constexpr (QRANGE) {
-        b0 |= !(q.x >= kQMin) | !(q.x <= kQMax);
-        b1 |= !(q.y >= kQMin) | !(q.y <= kQMax);
-    }
-    float2 wm = mul2(wt, rsqrt2_ftz(l2));
-    float2 ux = mx, uy = my, uz = mz;
-    if (b0 | b1) {  // rare: leave the neighbour to the exact fix-up
-        // weight and vector both zeroed: the vector may be infinite or NaN here
-        if (b0) {
-            wm.x = ux.x = uy.x = uz.x = 0.0f;
-            A.bad0 |= Mask(1) << n;
-        }
-        if (b1) {
-            wm.y = ux.y = uy.y = uz.y = 0.0f;
-            A.bad1 |= Mask(1) << n;
-        }
-    }
-    A.x = fma2(wm, ux, A.x);
-    A.y = fma2(wm, uy, A.y);
-    A.z = fma2(wm, uz, A.z);
-}
-
-// The replicate-padded halo of unit source normals in shared memory. For each
-// component an "even" and an "odd" plane of float2 pairs,
-//   E[i][k] = (v[i][2k], v[i][2k+1]),  O[i][k] = (v[i][2k+1], v[i][2k+2]),
-// so the pair starting at column j is (j even ? E : O)[i][j >> 1]: a warp's
-// pairs for one neighbour slot are consecutive float2, conflict-free. tu0
-// (with its negation) and tv0 are tabulated the same way.
-struct NTile {
-    float2* e[3];
-    float2* o[3];
-    float4* tue;  // (tu0, tu1, -tu0, -tu1) of the pair starting at column 2k
-    float4* tuo;  // ... at column 2k + 1
-    float* tv;
-    int swh;      // pairs per plane row
-
-    static constexpr __host__ __device__ int pairs_per_row(int SW) { return SW / 2 + 1; }
-    static constexpr __host__ __device__ size_t bytes(int SW, int SH) {
-        const int h = pairs_per_row(SW);
-        return sizeof(float4) * 2 * h + sizeof(float2) * 6 * (size_t)SH * h + sizeof(float) * SH;
-    }
-    __device__ void carve(void* base, int SW, int SH) {
-        swh = pairs_per_row(SW);
-        tue = reinterpret_cast<float4*>(base);
-        tuo = tue + swh;
-        float2* p = reinterpret_cast<float2*>(tuo + swh);
-        for (int c = 0; c < 3; ++c) {
-            e[c] = p;
-            o[c] = p + SH * swh;
-            p += 2 * SH * swh;
-        }
-        tv = reinterpret_cast<float*>(p);
-    }
-};
-
-// Stage the tile's normal halo and tu0 / tv0 tables at (x0, y0).
-template <typename TNI, bool FUSE_RR>
-__device__ __forceinline__ void stage_normals(const TNI* __restrict__ pnb,
-                                              const float* __restrict__ ray, const NTile& T,
-                                              int x0, int y0, const AngmfArgs& a) {
-    const int R = a.R;
-    const int SW = kTW + 2 * R;
-    const int SH = kTH + 2 * R;
-    const long HW = a.HW;
-    for (int idx = threadIdx.x; idx < SH * SW; idx += kThreads) {
-        const int i = idx / SW, j = idx - i * SW;
-        const int sy = clampi(y0 - R + i, 0, a.H - 1);
-        const int sx = clampi(x0 - R + j, 0, a.W - 1);
-        const long sp = (long)sy * a.W + sx;
-        float v[3] = {St<TNI>::ld(pnb + sp), St<TNI>::ld(pnb + HW + sp),
-                      St<TNI>::ld(pnb + 2 * HW + sp)};
-        if (FUSE_RR) ray_relu_f32(v[0], v[1], v[2], __ldg(ray + sp), __ldg(ray + HW + sp),
-                                  __ldg(ray + 2 * HW + sp));
-        const float inv = rsqrtf(fmaxf(fmaf(v[0], v[0], fmaf(v[1], v[1], v[2] * v[2])), 1e-24f));
-        const int k = j >> 1;
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            const float u = v[c] * inv;
-            float* ep = reinterpret_cast<float*>(T.e[c] + i * T.swh + k);
-            float* op = reinterpret_cast<float*>(T.o[c] + i * T.swh);
-            if (j & 1) {
-                ep[1] = u;
-                op[2 * k] = u;          // O[i][k].x
-            } else {
-                ep[0] = u;
-                if (k > 0) op[2 * (k - 1) + 1] = u;  // O[i][k-1].y
-            }
-        }
-    }
-    for (int k = threadIdx.x; k < T.swh; k += kThreads) {
-        float t[3];
-#pragma unroll
-        for (int d = 0; d < 3; ++d)
-            t[d] = fmaf((float)clampi(x0 - R + 2 * k + d, 0, a.W - 1), a.ifu, a.tu_c);
-        T.tue[k] = make_float4(t[0], t[1], -t[0], -t[1]);
-        T.tuo[k] = make_float4(t[1], t[2], -t[1], -t[2]);
-    }
-    for (int i = threadIdx.x; i < SH; i += kThreads) {
-        const int s0 = clampi(y0 - R + i, 0, a.H - 1);
-        T.tv[i] = fmaf((float)s0, a.ifv, a.tv_c);
-    }
-}
-
-// Stage the same halo and tables with compile-time geometry (the staged
-// kernel): one item per two source columns, so each channel of an item is
-// one 8-byte store to the even plane and two 4-byte stores to the odd plane,
-// and the item index splits with a constant divisor.
-template <int R, typename TNI, bool FUSE_RR>
-__device__ __forceinline__ void stage_normals_ct(const TNI* __restrict__ pnb,
-                                                 const float* __restrict__ ray, const NTile& T,
-                                                 int x0, int y0, const AngmfArgs& a) {
-    constexpr int SW = kTW + 2 * R, SH = kTH + 2 * R;
-    constexpr int NP = SW / 2;  // column pairs per halo row (SW is even)
-    constexpr int SWH = NTile::pairs_per_row(SW);
-    static_assert(SW % 2 == 0, "halo width must be even");
-    const long HW = a.HW;
-    for (int it = threadIdx.x; it < SH * NP; it += kThreads) {
-        const int i = it / NP, k = it - (it / NP) * NP;
-        const long row = (long)clampi(y0 - R + i, 0, a.H - 1) * a.W;
-        const int sx = x0 - R + 2 * k;
-        const long q0 = row + clampi(sx, 0, a.W - 1);
-        const long q1 = row + clampi(sx + 1, 0, a.W - 1);
-        float v0[3], v1[3];
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            v0[c] = St<TNI>::ld(pnb + c * HW + q0);
-            v1[c] = St<TNI>::ld(pnb + c * HW + q1);
-        }
-        if (FUSE_RR) {
-            ray_relu_f32(v0[0], v0[1], v0[2], __ldg(ray + q0), __ldg(ray + HW + q0),
-                         __ldg(ray + 2 * HW + q0));
-            ray_relu_f32(v1[0], v1[1], v1[2], __ldg(ray + q1), __ldg(ray + HW + q1),
-                         __ldg(ray + 2 * HW + q1));
-        }
-        const float i0 =
-            rsqrtf(fmaxf(fmaf(v0[0], v0[0], fmaf(v0[1], v0[1], v0[2] * v0[2])), 1e-24f));
-        const float i1 =
-            rsqrtf(fmaxf(fmaf(v1[0], v1[0], fmaf(v1[1], v1[1], v1[2] * v1[2])), 1e-24f));
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            const float u0 = v0[c] * i0, u1 = v1[c] * i1;
-            T.e[c][i * SWH + k] = make_float2(u0, u1);     // E[i][k]
-            float* op = reinterpret_cast<float*>(T.o[c] + i * SWH);
-            op[2 * k] = u1;                                 // O[i][k].x
-            if (k > 0) op[2 * k - 1] = u0;                  // O[i][k-1].y
-        }
-    }
-    for (int k = threadIdx.x; k < SWH; k += kThreads) {
-        float t[3];
-#pragma unroll
-        for (int d = 0; d < 3; ++d)
-            t[d] = fmaf((float)clampi(x0 - R + 2 * k + d, 0, a.W - 1), a.ifu, a.tu_c);
-        T.tue[k] = make_float4(t[0], t[1], -t[0], -t[1]);
-        T.tuo[k] = make_float4(t[1], t[2], -t[1], -t[2]);
-    }
-    for (int i = threadIdx.x; i < SH; i += kThreads)
-        T.tv[i] = fmaf((float)clampi(y0 - R + i, 0, a.H - 1), a.ifv, a.tv_c);
-}
-
-// The staged operands of the pair starting at column j of halo row i.
-struct NPair {
-    float2 nx, ny, nz, tu, tun, tv;
-};
-__device__ __forceinline__ NPair npair(const NTile& T, int i, int j) {
-    const int k = i * T.swh + (j >> 1);
-    NPair r;
-    if (j & 1) {
-        r.nx = T.o[0][k];
-        r.ny = T.o[1][k];
-        r.nz = T.o[2][k];
-        const float4 t = T.tuo[j >> 1];
-        r.tu = f2(t.x, t.y);
-        r.tun = f2(t.z, t.w);
-    } else {
-        r.nx = T.e[0][k];
-        r.ny = T.e[1][k];
-        r.nz = T.e[2][k];
-        const float4 t = T.tue[j >> 1];
-        r.tu = f2(t.x, t.y);
-        r.tun = f2(t.z, t.w);
-    }
-    r.tv = f2(T.tv[i]);
-    return r;
-}
-
-// Exact fp64 fix-ups of the flagged neighbours of one pixel; returns the sum.
-template <int PS, typename TS, typename TNI, bool FUSE_RR, typename Mask>
-__device__ __noinline__ float3 fixups(Mask m, int b, int x, int y, const TNI* __restrict__ pn,
-                                      const TS* __restrict__ prob, const TS* __restrict__ xy,
-                                      const TS* __restrict__ ang, const float* __restrict__ ray,
-                                      const AngmfArgs a) {
-    constexpr int P = PS * PS;
-    const long HW = a.HW;
-    const long pp = (long)y * a.W + x;
-    const TNI* pnb = pn + (long)b * 3 * HW;
-    const TS* xyb = xy + (long)b * 2 * P * HW;
-    const TS* prb = prob + (long)b * P * HW;
-    const TS* anb = ang + (long)b * P * HW;
-    const double orx = __ldg(ray + pp), ory = __ldg(ray + HW + pp), orz = __ldg(ray + 2 * HW + pp);
-    double ax = 0.0, ay = 0.0, az = 0.0;
-    while (m != 0) {
-        int n;
-        if constexpr (sizeof(Mask) == 4) n = __ffs(m) - 1;
-        else n = __ffsll((long long)m) - 1;
-        m &= m - 1;
-        const int ky = n / PS, kx = n - (n / PS) * PS;
-        const int sy = clampi(y - a.R + ky * a.dil, 0, a.H - 1);
-        const int sx = clampi(x - a.R + kx * a.dil, 0, a.W - 1);
-        const long sp = (long)sy * a.W + sx;
-        double nx = St<TNI>::ld(pnb + sp), ny = St<TNI>::ld(pnb + HW + sp),
-               nz = St<TNI>::ld(pnb + 2 * HW + sp);
-        if (FUSE_RR)
-            ray_relu_exact(nx, ny, nz, __ldg(ray + sp), __ldg(ray + HW + sp),
-                           __ldg(ray + 2 * HW + sp));
-        const double3 c3 = angmf_neighbor_exact(
-            nx, ny, nz, sx, sy, St<TS>::ld(xyb + (long)n * HW + pp),
-            St<TS>::ld(xyb + (long)(P + n) * HW + pp), St<TS>::ld(anb + (long)n * HW + pp),
-            St<TS>::ld(prb + (long)n * HW + pp), orx, ory, orz, a.fu, a.cu, a.fv, a.cv);
-        ax += c3.x;
-        ay += c3.y;
-        az += c3.z;
-    }
-    return make_float3((float)ax, (float)ay, (float)az);
-}
-
-// Normalise the pair's sums (after fix-ups) and store.
-template <int PS, typename TS, typename TNI, typename TNO, bool FUSE_RR, typename Mask>
-__device__ __forceinline__ void finish_pair(PairAcc<Mask>& A, int b, int x, int y, bool two,
-                                            bool vec, const TNI* pn, const TS* prob,
-                                            const TS* xy, const TS* ang, const float* ray,
-                                            TNO* out, const AngmfArgs& a) {
-    if (A.bad0 != 0) {
-        const float3 f = fixups<PS, TS, TNI, FUSE_RR>(A.bad0, b, x, y, pn, prob, xy, ang, ray, a);
-        A.x.x += f.x;
-        A.y.x += f.y;
-        A.z.x += f.z;
-    }
-    if (two && A.bad1 != 0) {
-        const float3 f =
-            fixups<PS, TS, TNI, FUSE_RR>(A.bad1, b, x + 1, y, pn, prob, xy, ang, ray, a);
-        A.x.y += f.x;
-        A.y.y += f.y;
-        A.z.y += f.z;
-    }
-    const float2 l = fma2(A.x, A.x, fma2(A.y, A.y, mul2(A.z, A.z)));
-    const float2 inv = rsqrt2(max2(l, f2(1e-24f)));
-    const float2 ox = mul2(A.x, inv), oy = mul2(A.y, inv), oz = mul2(A.z, inv);
-    const long HW = a.HW;
-    const long p0 = (long)y * a.W + x;
-    TNO* ob = out + (long)b * 3 * HW;
-    if (vec) {
-        St<TNO>::st2(ob + p0, ox);
-        St<TNO>::st2(ob + HW + p0, oy);
-        St<TNO>::st2(ob + 2 * HW + p0, oz);
-    } else {
-        St<TNO>::st(ob + p0, ox.x);
-        St<TNO>::st(ob + HW + p0, oy.x);
-        St<TNO>::st(ob + 2 * HW + p0, oz.x);
-        if (two) {
-            St<TNO>::st(ob + p0 + 1, ox.y);
-            St<TNO>::st(ob + HW + p0 + 1, oy.y);
-            St<TNO>::st(ob + 2 * HW + p0 + 1, oz.y);
-        }
-    }
-}
-
-__device__ __forceinline__ void pair_ray(const float* __restrict__ ray, long HW, long p0, long p1,
-                                         float2& rx, float2& ry, float2& rz) {
-    rx = f2(__ldg(ray + p0), __ldg(ray + p1));
-    ry = f2(__ldg(ray + HW + p0), __ldg(ray + HW + p1));
-    rz = f2(__ldg(ray + 2 * HW + p0), __ldg(ray + 2 * HW + p1));
-    const float2 ri = rsqrt2(max2(fma2(rx, rx, fma2(ry, ry, mul2(rz, rz))), f2(1e-16f)));
-    rx = mul2(rx, ri);
-    ry = mul2(ry, ri);
-    rz = mul2(rz, ri);
-}
-
-__device__ __forceinline__ void tile_of(const AngmfArgs& a, int& b, int& x0, int& y0) {
-    int t = blockIdx.x;
-    const int tix = t % a.tiles_x;
-    t /= a.tiles_x;
-    const int tiy = t % a.tiles_y;
-    b = t / a.tiles_y;
-    x0 = tix * kTW;
-    y0 = tiy * kTH;
-}
-
-// ---------------------------------------------------------------------------
-// General kernel: per-neighbour channels read straight from global memory.
-// Any shape; used when the width does not allow 16-byte staged copies.
-template <int PS, typename TS, typename TNI, typename TNO, bool FUSE_RR>
-__global__ void __launch_bounds__(kThreads, 2)
-angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* __restrict__ xy,
-             const TS* __restrict__ ang, const float* __restrict__ ray, TNO* __restrict__ out,
-             const AngmfArgs a) {
-    constexpr int P = PS * PS;
-    using Mask = typename std::conditional<(P <= 32), uint32_t, unsigned long long>::type;
-    extern __shared__ float4 smem4[];
-    NTile T;
-    T.carve(smem4, kTW + 2 * a.R, kTH + 2 * a.R);
-    int b, x0, y0;
-    tile_of(a, b, x0, y0);
-    const long HW = a.HW;
-    stage_normals<TNI, FUSE_RR>(pn + (long)b * 3 * HW, ray, T, x0, y0, a);
-    __syncthreads();
-
-    const int lx = 2 * (threadIdx.x % (kTW / 2));
-    const int ly = threadIdx.x / (kTW / 2);
-    const int x = x0 + lx, y = y0 + ly;
-    if (y >= a.H || x >= a.W) return;
-    const bool two = x + 1 < a.W;
-    const bool vec = (a.W & 1) == 0;
-    const long p0 = (long)y * a.W + x;
-    const long p1 = two ? p0 + 1 : p0;
-    float2 rx, ry, rz;
-    pair_ray(ray, HW, p0, p1, rx, ry, rz);
-    const TS* xyb = xy + (long)b * 2 * P * HW;
-    const TS* prb = prob + (long)b * P * HW;
-    const TS* anb = ang + (long)b * P * HW;
-    auto ld = [&](const TS* base) -> float2 {
-        return vec ? St<TS>::ld2s(base + p0) : f2(St<TS>::lds1(base + p0), St<TS>::lds1(base + p1));
-    };
-    const float2 ifu2 = f2(a.ifu), ifv2 = f2(a.ifv);
-    PairAcc<Mask> A{f2(0.f), f2(0.f), f2(0.f), 0, 0};
-#pragma unroll 1
-    for (int ky = 0; ky < PS; ++ky) {
-        const int i = ly + ky * a.dil;
-#pragma unroll
-        for (int kx = 0; kx < PS; ++kx) {
-            const int n = ky * PS + kx;
-            const NPair q = npair(T, i, lx + kx * a.dil);
-            angmf_pair<Mask, sizeof(TS) == 4>(
-                n, ld(xyb + (long)n * HW), ld(xyb + (long)(P + n) * HW), ld(anb + (long)n * HW),
-                ld(prb + (long)n * HW), q.nx, q.ny, q.nz, q.tu, q.tun, q.tv, ifu2, ifv2, rx, ry,
-                rz, A);
-        }
-    }
-    finish_pair<PS, TS, TNI, TNO, FUSE_RR>(A, b, x, y, two, vec, pn, prob, xy, ang, ray, out, a);
-}
-
-// ---------------------------------------------------------------------------
-// Staged kernel (width a multiple of 16 bytes of storage, dilation 1 or 2).
-// Each warp owns two rows of the tile; for every neighbour slot n it copies
-// exactly the data its own lanes will consume -- the four channel strips
-// (prob, x offset, y offset, angle; 2 rows x 32 pixels each) -- global ->
-// shared with 16-byte cp.async into a warp-private ring of kN = kM * PS
-// slots (slot of neighbour n: n mod kN), kD = kN - kSP slots ahead of the one
-// being computed. Memory latency is covered by the copies in flight instead of
-// registers, and publishing slots needs only a warp barrier: one per kSP
-// neighbour slots (two for fp16 storage, so that two neighbours' dependency
-// chains interleave between barriers). With the window size, the dilation and
-// the window column compile-time constants, every shared-memory offset is an
-// immediate.
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
-    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem),
-                 "r"(valid ? 16 : 0)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
-
-template <typename TS, int PS>
-struct Stages {
-    static constexpr int kEpc = 16 / (int)sizeof(TS);     // elements per 16-byte chunk
-    static constexpr int kCpr = kTW / kEpc;                // chunks per strip row
-    static constexpr int kRowsW = 2;                       // tile rows per warp
-    static constexpr int kChunksW = 4 * kRowsW * kCpr;     // per warp per slot
-    static constexpr int kPerLane = kChunksW / 32;         // 1 (fp16) or 2 (fp32)
-    static constexpr int kElemsW = 4 * kRowsW * kTW;       // per warp per slot
-    static constexpr int kM = (sizeof(TS) == 2 && PS < 7) ? 2 : 1;  // window rows per ring
-    static constexpr int kN = kM * PS;                     // ring depth
-    static constexpr int kSP = sizeof(TS) == 2 ? 2 : 1;    // slots per warp barrier
-    static constexpr int kD = kN - kSP;                    // slots issued ahead
-    static constexpr size_t kBytes = (size_t)(kThreads / 32) * kN * kElemsW * sizeof(TS);
-};
-
-// Shared memory of a staged variant and the CTAs per SM it is compiled for:
-// three when three fit (more warps to hide the dependency chains; the
-// register cap is then 80 and a few loop invariants spill to L1), else two.
-template <int PS, int DIL, typename TS>
-struct StagedCfg {
-    static constexpr int R = (PS / 2) * DIL;
-    static constexpr size_t kSmem =
-        Stages<TS, PS>::kBytes + NTile::bytes(kTW + 2 * R, kTH + 2 * R);
-    static constexpr int kMinBlocks = 3 * (kSmem + 1024) <= 228 * 1024 ? 3 : 2;
-};
-
-template <typename TS> __device__ __forceinline__ float2 lds2(const TS* p);
-template <> __device__ __forceinline__ float2 lds2<float>(const float* p) {
-    return *reinterpret_cast<const float2*>(p);
-}
-template <> __device__ __forceinline__ float2 lds2<__half>(const __half* p) {
-    return __half22float2(*reinterpret_cast<const __half2*>(p));
-}
-
-template <int PS, int DIL, typename TS, typename TNI, typename TNO, bool FUSE_RR>
-__global__ void __launch_bounds__(kThreads, (StagedCfg<PS, DIL, TS>::kMinBlocks))
-angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
-                    const TS* __restrict__ xy, const TS* __restrict__ ang,
-                    const float* __restrict__ ray, TNO* __restrict__ out, const AngmfArgs a) {
-    constexpr int P = PS * PS;
-    constexpr int R = (PS / 2) * DIL;
-    constexpr int SW = kTW + 2 * R, SH = kTH + 2 * R;
-    constexpr int SWH = NTile::pairs_per_row(SW);
-    using Mask = typename std::conditional<(P <= 32), uint32_t, unsigned long long>::type;
-    using S = Stages<TS, PS>;
-    extern __shared__ float4 smem4[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    TS* ring = reinterpret_cast<TS*>(smem4) + warp * S::kN * S::kElemsW;  // this warp's slots
-    NTile T;
-    T.carve(reinterpret_cast<char*>(smem4) + S::kBytes, SW, SH);
-    // grid (tiles_x, tiles_y, frames)
-    const int b = blockIdx.z, x0 = blockIdx.x * kTW, y0 = blockIdx.y * kTH;
-    const long HW = a.HW;
-    const TS* xyb = xy + (long)b * 2 * P * HW;
-    const TS* prb = prob + (long)b * P * HW;
-    const TS* anb = ang + (long)b * P * HW;
-
-    // this lane's chunks: source of the next slot to issue, slot offset, validity
-    const TS* src[S::kPerLane];
-    int dst[S::kPerLane];
-    bool valid[S::kPerLane];
-#pragma unroll
-    for (int k = 0; k < S::kPerLane; ++k) {
-        const int q = lane + 32 * k;
-        const int c = q / (S::kRowsW * S::kCpr);
-        const int r = (q / S::kCpr) % S::kRowsW;
-        const int cc = q % S::kCpr;
-        const TS* base = c == 0 ? prb : c == 1 ? xyb : c == 2 ? xyb + (long)P * HW : anb;
-        const int gy = y0 + S::kRowsW * warp + r, gx = x0 + cc * S::kEpc;
-        valid[k] = gy < a.H && gx < a.W;
-        src[k] = valid[k] ? base + (long)gy * a.W + gx : base;
-        dst[k] = (c * S::kRowsW + r) * kTW + cc * S::kEpc;
-    }
-    auto issue = [&](int slot) {
-        TS* sl = ring + slot * S::kElemsW;
-#pragma unroll
-        for (int k = 0; k < S::kPerLane; ++k) {
-            cp_async16(sl + dst[k], src[k], valid[k]);
-            if (valid[k]) src[k] += HW;  // the same strip of the next neighbour slot
-        }
-    };
-
-    // prologue: the first kD slots in flight while the normals are staged
-#pragma unroll
-    for (int sl = 0; sl < S::kD; ++sl) {
-        if (sl < P) issue(sl);
-        cp_async_commit();
-    }
-    stage_normals_ct<R, TNI, FUSE_RR>(pn + (long)b * 3 * HW, ray, T, x0, y0, a);
-    __syncthreads();  // the normal halo is shared by all warps
-
-    const int lx = 2 * (lane & 15);
-    const int ly = S::kRowsW * warp + (lane >> 4);
-    const int x = x0 + lx, y = y0 + ly;
-    const bool active = y < a.H && x < a.W;
-    const bool two = x + 1 < a.W;
-    const long p0 = (long)min(y, a.H - 1) * a.W + min(x, a.W - 1);
-    const long p1 = two ? p0 + 1 : p0;
-    float2 rx, ry, rz;
-    pair_ray(ray, HW, p0, p1, rx, ry, rz);
-    const float2 ifu2 = f2(a.ifu), ifv2 = f2(a.ifv);
-    PairAcc<Mask> A{f2(0.f), f2(0.f), f2(0.f), 0, 0};
-    constexpr int kStrip = S::kRowsW * kTW;
-    const TS* ring_lane = ring + (lane >> 4) * kTW + lx;   // this pair inside a slot
-    const int pbase = ly * SWH + (lx >> 1);                // this pair's first window pair
-
-#pragma unroll 1
-    for (int ky = 0; ky < PS; ++ky) {
-        const int grp = (ky % S::kM) * PS;                  // slot group of this window row
-        const int prev_grp = ((ky + S::kM - 1) % S::kM) * PS;  // ... of the previous row
-        const TS* st_row = ring_lane + grp * S::kElemsW;
-        const int prow = pbase + ky * DIL * SWH;
-        const float2 tv = f2(T.tv[ly + ky * DIL]);
-#pragma unroll
-        for (int kx = 0; kx < PS; ++kx) {
-            const int n = ky * PS + kx;
-            if (kx % S::kSP == 0) {
-                // a group of gs slots (the last of a window row may be short);
-                // one commit group per slot, so the wait depth is kD - gs
-                const int gs = PS - kx < S::kSP ? PS - kx : S::kSP;
-                static_assert(S::kSP <= 2, "wait depths below cover groups of 1 or 2");
-                if (gs == 2) cp_async_wait<S::kD - 2>();
-                else cp_async_wait<S::kD - 1>();
-                __syncwarp();  // the group's slots visible; every lane done with earlier slots
-                // refill the slots of the previous kSP neighbours with the ones kD ahead
-#pragma unroll
-                for (int e = 0; e < S::kSP; ++e) {
-                    if (e < gs) {
-                        const int j = kx + e - S::kSP;  // window column of neighbour n+e-kSP
-                        if (n + e + S::kD < P) issue(j >= 0 ? grp + j : prev_grp + PS + j);
-                        cp_async_commit();
-                    }
-                }
-            }
-            if (active) {
-                const TS* st = st_row + kx * S::kElemsW;
-                // window column offset: a constant once the kx loop is unrolled
-                const int dj = kx * DIL;
-                const int pi = prow + (dj >> 1);
-                float2 nx, ny, nz, tu, tun;
-                if ((dj & 1) == 0) {
-                    nx = T.e[0][pi];
-                    ny = T.e[1][pi];
-                    nz = T.e[2][pi];
-                    const float4 t4 = T.tue[(lx >> 1) + (dj >> 1)];
-                    tu = f2(t4.x, t4.y);
-                    tun = f2(t4.z, t4.w);
-                } else {
-                    nx = T.o[0][pi];
-                    ny = T.o[1][pi];
-                    nz = T.o[2][pi];
-                    const float4 t4 = T.tuo[(lx >> 1) + (dj >> 1)];
-                    tu = f2(t4.x, t4.y);
-                    tun = f2(t4.z, t4.w);
-                }
-                angmf_pair<Mask, sizeof(TS) == 4>(
-                    n, lds2<TS>(st + 1 * kStrip), lds2<TS>(st + 2 * kStrip),
-                    lds2<TS>(st + 3 * kStrip), lds2<TS>(st), nx, ny, nz, tu, tun, tv, ifu2, ifv2,
-                    rx, ry, rz, A);
-            }
-        }
-    }
-    cp_async_wait<0>();
-    if (!active) return;
-    finish_pair<PS, TS, TNI, TNO, FUSE_RR>(A, b, x, y, two, true, pn, prob, xy, ang, ray, out, a);
-}
-
-template <int PS, typename TS, typename TNI, typename TNO, bool FUSE_RR>
-cudaError_t launch_t(const AngmfLaunch& L, cudaStream_t s) {
-    AngmfArgs a;
-    a.B = L.B;
-    a.H = L.H;
-    a.W = L.W;
-    a.dil = L.dil;
-    a.R = (PS / 2) * L.dil;
-    a.tiles_x = (L.W + kTW - 1) / kTW;
-    a.tiles_y = (L.H + kTH - 1) / kTH;
-    a.HW = (long)L.H * L.W;
-    a.ifu = (float)(1.0 / L.fu);
-    a.ifv = (float)(1.0 / L.fv);
-    a.tu_c = (float)((0.5 - L.cu) / L.fu);
-    a.tv_c = (float)((0.5 - L.cv) / L.fv);
-    a.fu = L.fu;
-    a.cu = L.cu;
-    a.fv = L.fv;
-    a.cv = L.cv;
-    const size_t nsmem = NTile::bytes(kTW + 2 * a.R, kTH + 2 * a.R);
-    const long blocks = (long)a.tiles_x * a.tiles_y * L.B;
-    if (blocks > 0x7fffffffL) return cudaErrorInvalidConfiguration;
-    // staged copies need every 16-byte chunk of a row to start on a 16-byte
-    // boundary (W a multiple of 16 bytes of storage); dilations 1 and 2 (the
-    // benchmark windows) have compile-time staged variants
-    if ((L.W % Stages<TS, PS>::kEpc) == 0 && (L.dil == 1 || L.dil == 2) &&
-        a.tiles_y <= 65535) {
-        const size_t smem = Stages<TS, PS>::kBytes + nsmem;  // = StagedCfg<...>::kSmem
-        auto kern = L.dil == 1 ? angmf_staged_kernel<PS, 1, TS, TNI, TNO, FUSE_RR>
-                               : angmf_staged_kernel<PS, 2, TS, TNI, TNO, FUSE_RR>;
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-        // grid (tiles_x, tiles_y, frames), frames in launches of at most 65535
-        constexpr int P = PS * PS;
-        constexpr long kMaxZ = 65535;
-        for (long b0 = 0; b0 < L.B; b0 += kMaxZ) {
-            const long nb = L.B - b0 < kMaxZ ? L.B - b0 : kMaxZ;
-            a.B = (int)nb;
-            const dim3 grid((unsigned)a.tiles_x, (unsigned)a.tiles_y, (unsigned)nb);
-            kern<<<grid, kThreads, smem, s>>>(
-                static_cast<const TNI*>(L.pn) + b0 * 3 * a.HW,
-                static_cast<const TS*>(L.prob) + b0 * P * a.HW,
-                static_cast<const TS*>(L.xy) + b0 * 2 * P * a.HW,
-                static_cast<const TS*>(L.angle) + b0 * P * a.HW, L.ray,
-                static_cast<TNO*>(L.out) + b0 * 3 * a.HW, a);
-            e = cudaGetLastError();
-            if (e != cudaSuccess) return e;
-        }
-        return cudaSuccess;
-    }
-    auto kern = angmf_kernel<PS, TS, TNI, TNO, FUSE_RR>;
-    if (nsmem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)nsmem);
-        if (e != cudaSuccess) return e;
-    }
-    kern<<<(unsigned)blocks, kThreads, nsmem, s>>>(
-        static_cast<const TNI*>(L.pn), static_cast<const TS*>(L.prob),
-        static_cast<const TS*>(L.xy), static_cast<const TS*>(L.angle), L.ray,
-        static_cast<TNO*>(L.out), a);
-    return cudaGetLastError();
-}
-
-template <int PS, typename TS>
-cudaError_t launch_ps(const AngmfLaunch& L, cudaStream_t s) {
-    const bool in_f32 = L.pn_t == SType::F32, out_f32 = L.out_t == SType::F32;
-    using TO = TS;
-    if (L.fuse_ray_relu) {
-        // fused refine, first iteration: storage-typed decoder normals in, fp32 out
-        if (!out_f32) return cudaErrorInvalidValue;
-        if (in_f32) return launch_t<PS, TS, float, float, true>(L, s);
-        return launch_t<PS, TS, TO, float, true>(L, s);
-    }
-    // fused refine, later iterations (fp32 intermediates) or the fp32 single op
-    if (in_f32 && out_f32) return launch_t<PS, TS, float, float, false>(L, s);
-    // single op on storage-typed normals
-    if (!in_f32 && !out_f32) return launch_t<PS, TS, TO, TO, false>(L, s);
-    return cudaErrorInvalidValue;
-}
-
-template <typename TS>
-cudaError_t launch_st(const AngmfLaunch& L, cudaStream_t s) {
-    switch (L.ps) {
-        case 3: return launch_ps<3, TS>(L, s);
-        case 5: return launch_ps<5, TS>(L, s);
-        case 7: return launch_ps<7, TS>(L, s);
-        default: return cudaErrorInvalidValue;
-    }
-}
-
-}  // namespace
 
 cudaError_t launch_angmf(const AngmfLaunch& L, cudaStream_t s) {
-    if (L.B == 0 || L.H == 0 || L.W == 0) return cudaSuccess;
-    if (L.st == SType::F32) {
-        if (L.pn_t != SType::F32 && !L.fuse_ray_relu) return cudaErrorInvalidValue;
-        return launch_st<float>(L, s);
-    }
-    return launch_st<__half>(L, s);
+    if (L.act) return launch_angmf_logits(L, s);
+    return launch_angmf_act<false>(L, s);
 }
 
 }  // namespace bvml

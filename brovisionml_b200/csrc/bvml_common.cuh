@@ -63,6 +63,14 @@ __device__ __forceinline__ float ex2_ftz(float x) {
     return y;
 }
 __device__ __forceinline__ float2 ex2_ftz2(float2 a) { return make_float2(ex2_ftz(a.x), ex2_ftz(a.y)); }
+// 1/x with the hardware approximation (PTX rcp.approx.ftz.f32, ~1 ulp);
+// 1/inf = 0.
+__device__ __forceinline__ float rcp_ftz(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float2 rcp2_ftz(float2 a) { return make_float2(rcp_ftz(a.x), rcp_ftz(a.y)); }
 
 // -------------------------------------------------------------- storage types
 template <typename T> struct St;

@@ -22,10 +22,12 @@ struct AngmfLaunch {
     void* out;           // (B,3,H,W); type out_t
     SType st, pn_t, out_t;
     bool fuse_ray_relu;  // apply RayReLU to the source normals while staging them
+    bool act;            // prob / angle are raw head outputs: activate them on load
     int B, H, W, ps, dil;
     double fu, cu, fv, cv;
 };
 cudaError_t launch_angmf(const AngmfLaunch& L, cudaStream_t s);
+cudaError_t launch_angmf_logits(const AngmfLaunch& L, cudaStream_t s);  // L.act variants
 
 struct UpsampleLaunch {
     const void* n;       // (B,3,h,w); type n_t

@@ -56,48 +56,22 @@ size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
 int bvml::report_error(int code, const std::string& msg) { return fail(code, msg); }
 
-extern "C" {
+namespace {
 
-const char* bvml_last_error(void) { return g_last_error.c_str(); }
-
-int bvml_abi_version(void) { return BVML_ABI_VERSION; }
-
-int bvml_probe_events(void* const* events, int n) {
-    if (n < 0 || (n > 0 && !events)) return einval("probe_events: bad event list");
-    g_probe.clear();
-    for (int i = 0; i < n; ++i) {
-        if (!events[i]) {
-            g_probe.clear();
-            return einval("probe_events: null event handle (create the events first)");
-        }
-        g_probe.push_back(static_cast<cudaEvent_t>(events[i]));
-    }
-    g_last_error.clear();
-    return BVML_OK;
-}
-
-int bvml_ray_relu(void* normal, const float* ray, int B, int H, int W, int dtype, void* stream) {
-    if (!dtype_ok(dtype)) return einval("ray_relu: unknown dtype");
-    if (!dims_ok(B, H, W)) return einval("ray_relu: bad shape");
-    if ((long)B * H * W == 0) return finish(cudaSuccess, "ray_relu");
-    if (!normal || !ray) return einval("ray_relu: null tensor");
-    return finish(bvml::launch_ray_relu(normal, st_of(dtype), ray, B, H, W,
-                                        static_cast<cudaStream_t>(stream)),
-                  "ray_relu launch");
-}
-
-int bvml_angmf_propagate(const void* pred_norm, const void* prob, const void* xy,
-                         const void* angle, const float* ray, double fu, double cu, double fv,
-                         double cv, int B, int H, int W, int ps, int dil, int dtype, void* out,
-                         void* stream) {
-    if (!dtype_ok(dtype)) return einval("angmf_propagate: unknown dtype");
-    if (!window_ok(ps, dil)) return einval("angmf_propagate: window must be 3/5/7, dilation 1..4");
-    if (!dims_ok(B, H, W)) return einval("angmf_propagate: bad shape");
-    if ((long)B * H * W == 0) return finish(cudaSuccess, "angmf_propagate");
+// bvml_angmf_propagate and bvml_angmf_propagate_logits (`act`: prob / angle
+// are raw head outputs, activated on load).
+int angmf_entry(const std::string& name, bool act, const void* pred_norm, const void* prob,
+                const void* xy, const void* angle, const float* ray, double fu, double cu,
+                double fv, double cv, int B, int H, int W, int ps, int dil, int dtype, void* out,
+                void* stream) {
+    if (!dtype_ok(dtype)) return einval(name + ": unknown dtype");
+    if (!window_ok(ps, dil)) return einval(name + ": window must be 3/5/7, dilation 1..4");
+    if (!dims_ok(B, H, W)) return einval(name + ": bad shape");
+    if ((long)B * H * W == 0) return finish(cudaSuccess, name.c_str());
     if (!pred_norm || !prob || !xy || !angle || !ray || !out)
-        return einval("angmf_propagate: null tensor");
-    if (out == pred_norm) return einval("angmf_propagate: out must not alias pred_norm");
-    if (!intr_ok(fu, fv)) return einval("angmf_propagate: focal lengths must be nonzero");
+        return einval(name + ": null tensor");
+    if (out == pred_norm) return einval(name + ": out must not alias pred_norm");
+    if (!intr_ok(fu, fv)) return einval(name + ": focal lengths must be nonzero");
     bvml::AngmfLaunch L{};
     L.pn = pred_norm;
     L.prob = prob;
@@ -107,6 +81,7 @@ int bvml_angmf_propagate(const void* pred_norm, const void* prob, const void* xy
     L.out = out;
     L.st = L.pn_t = L.out_t = st_of(dtype);
     L.fuse_ray_relu = false;
+    L.act = act;
     L.B = B;
     L.H = H;
     L.W = W;
@@ -117,72 +92,16 @@ int bvml_angmf_propagate(const void* pred_norm, const void* prob, const void* xy
     L.fv = fv;
     L.cv = cv;
     return finish(bvml::launch_angmf(L, static_cast<cudaStream_t>(stream)),
-                  "angmf_propagate launch");
+                  (name + " launch").c_str());
 }
 
-int bvml_convex_upsample(const void* x, const void* mask, int N, int C, int H, int W, int scale,
-                         int dtype, void* y, void* stream) {
-    if (!dtype_ok(dtype)) return einval("convex_upsample: unknown dtype");
-    if (C != 3 || scale != 8)
-        return fail(BVML_EUNSUPPORTED, "dsine ops: convex_upsample: only C = 3, scale = 8");
-    if (!dims_ok(N, H, W)) return einval("convex_upsample: bad shape");
-    if ((long)N * H * W == 0) return finish(cudaSuccess, "convex_upsample");
-    if (!x || !mask || !y) return einval("convex_upsample: null tensor");
-    bvml::UpsampleLaunch L{};
-    L.n = x;
-    L.mask = mask;
-    L.out = y;
-    L.st = L.n_t = st_of(dtype);
-    L.normalize = false;
-    L.ray_relu = false;
-    L.B = N;
-    L.h = H;
-    L.w = W;
-    L.crop_t = 0;
-    L.crop_l = 0;
-    L.out_h = 8 * H;
-    L.out_w = 8 * W;
-    L.fu = L.fv = 1.0;
-    return finish(bvml::launch_upsample(L, static_cast<cudaStream_t>(stream)),
-                  "convex_upsample launch");
-}
-
-int bvml_l2_normalize_nchw(const void* x, int N, int C, int H, int W, float eps, int dtype,
-                           void* y, void* stream) {
-    if (!dtype_ok(dtype)) return einval("l2_normalize: unknown dtype");
-    if (C < 0 || C > 16) return fail(BVML_EUNSUPPORTED, "dsine ops: l2_normalize: C must be <= 16");
-    if (N < 0 || H < 0 || W < 0) return einval("l2_normalize: bad shape");
-    if ((long)N * C * H * W == 0) return finish(cudaSuccess, "l2_normalize");
-    if (!x || !y) return einval("l2_normalize: null tensor");
-    return finish(bvml::launch_l2_normalize(x, y, st_of(dtype), N, C, H, W, eps,
-                                            static_cast<cudaStream_t>(stream)),
-                  "l2_normalize launch");
-}
-
-int bvml_slice2d(const void* x, int N, int C, int H, int W, int h0, int w0, int Ho, int Wo,
-                 int dtype, void* y, void* stream) {
-    if (!dtype_ok(dtype)) return einval("slice2d: unknown dtype");
-    if (N < 0 || C < 0 || H < 0 || W < 0 || Ho < 0 || Wo < 0 || h0 < 0 || w0 < 0 ||
-        h0 + Ho > H || w0 + Wo > W)
-        return einval("slice2d: window outside the input");
-    if ((long)N * C * Ho * Wo == 0) return finish(cudaSuccess, "slice2d");
-    if (!x || !y) return einval("slice2d: null tensor");
-    return finish(bvml::launch_slice2d(x, y, st_of(dtype), N, C, H, W, h0, w0, Ho, Wo,
-                                       static_cast<cudaStream_t>(stream)),
-                  "slice2d launch");
-}
-
-size_t bvml_refine_workspace_bytes(int B, int h, int w) {
-    if (B < 0 || h < 0 || w < 0) return 0;
-    const size_t plane = (size_t)h * (size_t)w;
-    return 2 * align256(sizeof(float) * 3 * plane * (size_t)B) + align256(sizeof(float) * 3 * plane);
-}
-
-int bvml_refine(const void* normal0, const float* ray8, const void* const* prob,
-                const void* const* xy, const void* const* angle, int iters, const void* mask,
-                int B, int h, int w, int ps, int dil, double fu, double cu, double fv, double cv,
-                int full_res_ray_relu, int crop_t, int crop_l, int out_h, int out_w, int dtype,
-                void* workspace, size_t workspace_bytes, void* out, void* stream) {
+// bvml_refine and bvml_refine_logits (`act`: the per-iteration prob / angle
+// are raw head outputs, activated on load).
+int refine_entry(bool act, const void* normal0, const float* ray8, const void* const* prob,
+                 const void* const* xy, const void* const* angle, int iters, const void* mask,
+                 int B, int h, int w, int ps, int dil, double fu, double cu, double fv,
+                 double cv, int full_res_ray_relu, int crop_t, int crop_l, int out_h, int out_w,
+                 int dtype, void* workspace, size_t workspace_bytes, void* out, void* stream) {
     if (!dtype_ok(dtype)) return einval("refine: unknown dtype");
     if (!window_ok(ps, dil)) return einval("refine: window must be 3/5/7, dilation 1..4");
     if (!dims_ok(B, h, w)) return einval("refine: bad shape");
@@ -248,6 +167,7 @@ int bvml_refine(const void* normal0, const float* ray8, const void* const* prob,
             L.pn_t = it == 0 ? st : bvml::SType::F32;
             L.out_t = bvml::SType::F32;
             L.fuse_ray_relu = it == 0;
+            L.act = act;
             L.B = B;
             L.H = h;
             L.W = w;
@@ -291,6 +211,133 @@ int bvml_refine(const void* normal0, const float* ray8, const void* const* prob,
     if ((e = probe(launch_no++, s)) != cudaSuccess)
         return cuda_fail(e, "refine: probe event record");
     return finish(cudaSuccess, "refine");
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* bvml_last_error(void) { return g_last_error.c_str(); }
+
+int bvml_abi_version(void) { return BVML_ABI_VERSION; }
+
+int bvml_probe_events(void* const* events, int n) {
+    if (n < 0 || (n > 0 && !events)) return einval("probe_events: bad event list");
+    g_probe.clear();
+    for (int i = 0; i < n; ++i) {
+        if (!events[i]) {
+            g_probe.clear();
+            return einval("probe_events: null event handle (create the events first)");
+        }
+        g_probe.push_back(static_cast<cudaEvent_t>(events[i]));
+    }
+    g_last_error.clear();
+    return BVML_OK;
+}
+
+int bvml_ray_relu(void* normal, const float* ray, int B, int H, int W, int dtype, void* stream) {
+    if (!dtype_ok(dtype)) return einval("ray_relu: unknown dtype");
+    if (!dims_ok(B, H, W)) return einval("ray_relu: bad shape");
+    if ((long)B * H * W == 0) return finish(cudaSuccess, "ray_relu");
+    if (!normal || !ray) return einval("ray_relu: null tensor");
+    return finish(bvml::launch_ray_relu(normal, st_of(dtype), ray, B, H, W,
+                                        static_cast<cudaStream_t>(stream)),
+                  "ray_relu launch");
+}
+
+int bvml_angmf_propagate(const void* pred_norm, const void* prob, const void* xy,
+                         const void* angle, const float* ray, double fu, double cu, double fv,
+                         double cv, int B, int H, int W, int ps, int dil, int dtype, void* out,
+                         void* stream) {
+    return angmf_entry("angmf_propagate", false, pred_norm, prob, xy, angle, ray, fu, cu, fv,
+                       cv, B, H, W, ps, dil, dtype, out, stream);
+}
+
+int bvml_angmf_propagate_logits(const void* pred_norm, const void* prob_logits, const void* xy,
+                                const void* angle_logits, const float* ray, double fu,
+                                double cu, double fv, double cv, int B, int H, int W, int ps,
+                                int dil, int dtype, void* out, void* stream) {
+    return angmf_entry("angmf_propagate_logits", true, pred_norm, prob_logits, xy, angle_logits,
+                       ray, fu, cu, fv, cv, B, H, W, ps, dil, dtype, out, stream);
+}
+
+int bvml_convex_upsample(const void* x, const void* mask, int N, int C, int H, int W, int scale,
+                         int dtype, void* y, void* stream) {
+    if (!dtype_ok(dtype)) return einval("convex_upsample: unknown dtype");
+    if (C != 3 || scale != 8)
+        return fail(BVML_EUNSUPPORTED, "dsine ops: convex_upsample: only C = 3, scale = 8");
+    if (!dims_ok(N, H, W)) return einval("convex_upsample: bad shape");
+    if ((long)N * H * W == 0) return finish(cudaSuccess, "convex_upsample");
+    if (!x || !mask || !y) return einval("convex_upsample: null tensor");
+    bvml::UpsampleLaunch L{};
+    L.n = x;
+    L.mask = mask;
+    L.out = y;
+    L.st = L.n_t = st_of(dtype);
+    L.normalize = false;
+    L.ray_relu = false;
+    L.B = N;
+    L.h = H;
+    L.w = W;
+    L.crop_t = 0;
+    L.crop_l = 0;
+    L.out_h = 8 * H;
+    L.out_w = 8 * W;
+    L.fu = L.fv = 1.0;
+    return finish(bvml::launch_upsample(L, static_cast<cudaStream_t>(stream)),
+                  "convex_upsample launch");
+}
+
+int bvml_l2_normalize_nchw(const void* x, int N, int C, int H, int W, float eps, int dtype,
+                           void* y, void* stream) {
+    if (!dtype_ok(dtype)) return einval("l2_normalize: unknown dtype");
+    if (C < 0 || C > 16) return fail(BVML_EUNSUPPORTED, "dsine ops: l2_normalize: C must be <= 16");
+    if (N < 0 || H < 0 || W < 0) return einval("l2_normalize: bad shape");
+    if ((long)N * C * H * W == 0) return finish(cudaSuccess, "l2_normalize");
+    if (!x || !y) return einval("l2_normalize: null tensor");
+    return finish(bvml::launch_l2_normalize(x, y, st_of(dtype), N, C, H, W, eps,
+                                            static_cast<cudaStream_t>(stream)),
+                  "l2_normalize launch");
+}
+
+int bvml_slice2d(const void* x, int N, int C, int H, int W, int h0, int w0, int Ho, int Wo,
+                 int dtype, void* y, void* stream) {
+    if (!dtype_ok(dtype)) return einval("slice2d: unknown dtype");
+    if (N < 0 || C < 0 || H < 0 || W < 0 || Ho < 0 || Wo < 0 || h0 < 0 || w0 < 0 ||
+        h0 + Ho > H || w0 + Wo > W)
+        return einval("slice2d: window outside the input");
+    if ((long)N * C * Ho * Wo == 0) return finish(cudaSuccess, "slice2d");
+    if (!x || !y) return einval("slice2d: null tensor");
+    return finish(bvml::launch_slice2d(x, y, st_of(dtype), N, C, H, W, h0, w0, Ho, Wo,
+                                       static_cast<cudaStream_t>(stream)),
+                  "slice2d launch");
+}
+
+size_t bvml_refine_workspace_bytes(int B, int h, int w) {
+    if (B < 0 || h < 0 || w < 0) return 0;
+    const size_t plane = (size_t)h * (size_t)w;
+    return 2 * align256(sizeof(float) * 3 * plane * (size_t)B) + align256(sizeof(float) * 3 * plane);
+}
+
+int bvml_refine(const void* normal0, const float* ray8, const void* const* prob,
+                const void* const* xy, const void* const* angle, int iters, const void* mask,
+                int B, int h, int w, int ps, int dil, double fu, double cu, double fv, double cv,
+                int full_res_ray_relu, int crop_t, int crop_l, int out_h, int out_w, int dtype,
+                void* workspace, size_t workspace_bytes, void* out, void* stream) {
+    return refine_entry(false, normal0, ray8, prob, xy, angle, iters, mask, B, h, w, ps, dil, fu,
+                        cu, fv, cv, full_res_ray_relu, crop_t, crop_l, out_h, out_w, dtype,
+                        workspace, workspace_bytes, out, stream);
+}
+
+int bvml_refine_logits(const void* normal0, const float* ray8, const void* const* prob_logits,
+                       const void* const* xy, const void* const* angle_logits, int iters,
+                       const void* mask, int B, int h, int w, int ps, int dil, double fu,
+                       double cu, double fv, double cv, int full_res_ray_relu, int crop_t,
+                       int crop_l, int out_h, int out_w, int dtype, void* workspace,
+                       size_t workspace_bytes, void* out, void* stream) {
+    return refine_entry(true, normal0, ray8, prob_logits, xy, angle_logits, iters, mask, B, h, w,
+                        ps, dil, fu, cu, fv, cv, full_res_ray_relu, crop_t, crop_l, out_h, out_w,
+                        dtype, workspace, workspace_bytes, out, stream);
 }
 
 }  // extern "C"

@@ -89,10 +89,12 @@ def ray_relu(normal: torch.Tensor, ray: torch.Tensor, H: int | None = None,
 def angmf_propagate(pred_norm: torch.Tensor, prob: torch.Tensor, xy: torch.Tensor,
                     angle: torch.Tensor, ray: torch.Tensor, fu: float, cu: float, fv: float,
                     cv: float, H: int | None = None, W: int | None = None,
-                    out: torch.Tensor | None = None, *, ps: int = 5,
-                    dil: int = 1) -> torch.Tensor:
+                    out: torch.Tensor | None = None, *, ps: int = 5, dil: int = 1,
+                    logits: bool = False) -> torch.Tensor:
     """Fused AngMF propagate; returns ``out`` (allocated like pred_norm when None,
-    as the reference (re)allocates it)."""
+    as the reference (re)allocates it). With ``logits=True`` prob and angle are
+    the prediction heads' raw outputs, activated on load (sigmoid, pi * sigmoid:
+    src/dsine_refine.cpp:262-267)."""
     dev = _cuda("angmf_propagate", pred_norm, prob, xy, angle, ray)
     B, H, W = _frames(pred_norm, 3, H, W)
     P = ps * ps
@@ -107,10 +109,11 @@ def angmf_propagate(pred_norm: torch.Tensor, prob: torch.Tensor, xy: torch.Tenso
     else:
         _cuda("angmf_propagate", pred_norm, out)
         _numel_check("angmf_propagate", out, pred_norm.numel(), "out")
+    fn = lib.bvml_angmf_propagate_logits if logits else lib.bvml_angmf_propagate
     with torch.cuda.device(dev):
-        check(lib.bvml_angmf_propagate(_p(pred_norm), _p(prob), _p(xy), _p(angle), _p(ray),
-                                       float(fu), float(cu), float(fv), float(cv), B, H, W, ps,
-                                       dil, _code(pred_norm), _p(out), _stream(dev)))
+        check(fn(_p(pred_norm), _p(prob), _p(xy), _p(angle), _p(ray), float(fu), float(cu),
+                 float(fv), float(cv), B, H, W, ps, dil, _code(pred_norm), _p(out),
+                 _stream(dev)))
     return out
 
 
@@ -157,13 +160,14 @@ def refine(normal0: torch.Tensor, prob: Sequence[torch.Tensor], xy: Sequence[tor
            angle: Sequence[torch.Tensor], mask: torch.Tensor, fu: float, cu: float, fv: float,
            cv: float, *, ray8: torch.Tensor | None = None, ps: int = 5, dil: int = 1,
            full_res_ray_relu: bool = False, crop: tuple[int, int, int, int] | None = None,
-           out: torch.Tensor | None = None,
-           workspace: torch.Tensor | None = None) -> torch.Tensor:
+           out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+           logits: bool = False) -> torch.Tensor:
     """The refine-ops unit of Refiner::forward for B frames (iters + 1 launches).
 
     normal0 (B,3,h,w); prob[i] (B,P,h,w); xy[i] (B,2P,h,w); angle[i] (B,P,h,w);
     mask (B,576,h,w); ray8 (3,h,w) fp32 or None (computed on the device);
-    crop = (top, left, out_h, out_w) in the 8x output (default: no crop).
+    crop = (top, left, out_h, out_w) in the 8x output (default: no crop);
+    logits=True: prob / angle are the heads' raw outputs (activated on load).
     Returns (B,3,out_h,out_w) in normal0's storage dtype.
     """
     iters = len(prob)
@@ -181,10 +185,10 @@ def refine(normal0: torch.Tensor, prob: Sequence[torch.Tensor], xy: Sequence[tor
     if workspace.numel() * workspace.element_size() < need:
         raise RuntimeError("dsine ops: refine: workspace too small")
     arr = lambda lst: (ctypes.c_void_p * max(1, len(lst)))(*[t.data_ptr() for t in lst])  # noqa
+    fn = lib.bvml_refine_logits if logits else lib.bvml_refine
     with torch.cuda.device(dev):
-        check(lib.bvml_refine(_p(normal0), _p(ray8) if ray8 is not None else None, arr(prob),
-                              arr(xy), arr(angle), iters, _p(mask), B, h, w, ps, dil, float(fu),
-                              float(cu), float(fv), float(cv), int(bool(full_res_ray_relu)),
-                              ct, cl, oh, ow, _code(normal0), _p(workspace), need, _p(out),
-                              _stream(dev)))
+        check(fn(_p(normal0), _p(ray8) if ray8 is not None else None, arr(prob), arr(xy),
+                 arr(angle), iters, _p(mask), B, h, w, ps, dil, float(fu), float(cu), float(fv),
+                 float(cv), int(bool(full_res_ray_relu)), ct, cl, oh, ow, _code(normal0),
+                 _p(workspace), need, _p(out), _stream(dev)))
     return out

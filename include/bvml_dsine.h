@@ -83,6 +83,20 @@ int bvml_angmf_propagate(const void* pred_norm, const void* prob, const void* xy
                          int dtype, void* out, void* stream);
 
 /*
+ * bvml_angmf_propagate on the prediction heads' raw outputs: prob_logits and
+ * angle_logits (shapes and dtype as prob / angle) are activated while they
+ * are loaded, prob = sigmoid(prob_logit), angle = pi * sigmoid(angle_logit)
+ * with pi the float 3.14159265f. Replaces the separate passes
+ * apply_sigmoid(prob); apply_sigmoid(angle); brotensor::scale_inplace(angle,
+ * kPi) of Refiner::forward (src/dsine_refine.cpp:262-267, kPi at :26) and the
+ * angmf_propagate call after them (:271-272). xy is raw in both entry points.
+ */
+int bvml_angmf_propagate_logits(const void* pred_norm, const void* prob_logits, const void* xy,
+                                const void* angle_logits, const float* ray, double fu,
+                                double cu, double fv, double cv, int B, int H, int W, int ps,
+                                int dil, int dtype, void* out, void* stream);
+
+/*
  * Convex upsample: mask (N, 9*s*s, H, W) viewed (9, s, s), softmax over the 9
  * taps, 3x3 replicate-padded unfold of x (N, C, H, W), output y (N, C, s*H, s*W)
  * with row s*y+ky, col s*x+kx. This build implements C = 3, s = 8 (the path's
@@ -136,6 +150,18 @@ int bvml_refine(const void* normal0, const float* ray8, const void* const* prob,
                 double cv, int full_res_ray_relu, int crop_t, int crop_l, int out_h,
                 int out_w, int dtype, void* workspace, size_t workspace_bytes, void* out,
                 void* stream);
+
+/*
+ * bvml_refine with every iteration's prob / angle given as the heads' raw
+ * outputs (activated on load, as bvml_angmf_propagate_logits): the unit of
+ * src/dsine_refine.cpp:241-292 including the activations at :262-267.
+ */
+int bvml_refine_logits(const void* normal0, const float* ray8, const void* const* prob_logits,
+                       const void* const* xy, const void* const* angle_logits, int iters,
+                       const void* mask, int B, int h, int w, int ps, int dil, double fu,
+                       double cu, double fv, double cv, int full_res_ray_relu, int crop_t,
+                       int crop_l, int out_h, int out_w, int dtype, void* workspace,
+                       size_t workspace_bytes, void* out, void* stream);
 
 /* Scratch bytes built into the library per device for bvml_refine_noalloc. */
 #define BVML_REFINE_NOALLOC_MAX_BYTES (32u * 1024u * 1024u)

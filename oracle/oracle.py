@@ -196,6 +196,24 @@ def build_ray_scaled(fu, cu, fv, cv, Hf, Wf) -> np.ndarray:
     return r
 
 
+# kPi of src/dsine_refine.cpp:26 (a float constant)
+KPI_F32 = np.float32(3.14159265358979323846)
+
+
+def head_activation(prob_logits, angle_logits):
+    """The head activations of Refiner::forward (src/dsine_refine.cpp:262-267):
+    prob = sigmoid(prob_logits); angle = sigmoid(angle_logits) * kPi, as the
+    fp32 tensors the reference produces. brotensor's sigmoid_forward is not in
+    the reference tree (parity unpinned): it is taken as the correctly rounded
+    fp32 logistic (fp64 evaluation, one rounding), and scale_inplace as an fp32
+    product."""
+    def sig(x):
+        with np.errstate(over="ignore"):
+            return (1.0 / (1.0 + np.exp(-np.asarray(x, np.float64)))).astype(np.float32)
+
+    return sig(prob_logits), (sig(angle_logits) * KPI_F32).astype(np.float32)
+
+
 # ---------------------------------------------------------------- fp16 storage
 
 def f16_round(a: np.ndarray) -> np.ndarray:

@@ -23,7 +23,7 @@ def test_header_symbols_exported():
     from brovisionml_b200 import _capi
 
     syms = declared_symbols()
-    assert len(syms) == 11, syms
+    assert len(syms) == 13, syms
     assert sorted(_capi.EXPORTS) == syms
     for s in syms:
         assert hasattr(b.lib, s), s
@@ -98,6 +98,17 @@ def test_argument_errors_without_gpu():
     rc = lib.bvml_refine(fake, None, arr, arr, arr, 1, fake, 2, 8, 8, 5, 1, 1.0, 0.0, 1.0, 0.0,
                          0, 0, 0, 64, 64, 0, ctypes.c_void_p(0x10010), need, fake, None)
     assert rc == 1 and "aligned" in lib.bvml_last_error().decode()
+    # the raw-head-output entry points check the same way, under their own names
+    rc = lib.bvml_angmf_propagate_logits(fake, fake, fake, fake, fake, 1.0, 0.0, 1.0, 0.0, 1, 4,
+                                         4, 4, 1, 0, ctypes.c_void_p(0x2000), None)
+    err = lib.bvml_last_error().decode()
+    assert rc == 1 and err.startswith("dsine ops: angmf_propagate_logits") and "window" in err
+    assert lib.bvml_angmf_propagate_logits(None, None, None, None, None, 1.0, 0.0, 1.0, 0.0, 1,
+                                           0, 5, 5, 1, 0, None, None) == 0
+    rc = lib.bvml_refine_logits(fake, None, arr, arr, arr, 1, fake, 2, 8, 8, 5, 1, 1.0, 0.0,
+                                1.0, 0.0, 0, 0, 0, 64, 64, 0, ctypes.c_void_p(0x10000), need - 1,
+                                fake, None)
+    assert rc == 1 and "workspace" in lib.bvml_last_error().decode()
 
 
 def test_python_mirror_rejects_cpu_tensors():

@@ -152,6 +152,24 @@ def test_angmf_f16_degenerate_offsets():
     report("angmf f16 degenerate", host(got), want, TOL16)
 
 
+def test_angmf_tiny_huge_zero_source_normals():
+    """Source normals far from unit length (the reference rotates them raw and
+    normalises after): 1e-14, 1e-30, subnormal, 1e25 and exactly zero, with
+    rotation angles over the whole (0, pi] range."""
+    b = lib()
+    u = O.gen_unit(320, 448, 1, iters=1, seed=29, upsample=False, angle_max=float(np.pi))
+    n0 = O.ray_relu(u.normal0, u.ray8).copy()
+    g = np.random.default_rng(29)
+    pick = g.random(n0.shape[2:])
+    for lo, scale in ((0.0, 1e-14), (0.05, 1e-30), (0.10, 1e-41), (0.15, 1e25), (0.20, 0.0)):
+        sel = (pick >= lo) & (pick < lo + 0.05)
+        n0[0][:, sel] *= np.float32(scale)
+    want = O.angmf(n0, u.prob[0], u.xy[0], u.angle[0], u.ray8, u.fu, u.cu, u.fv, u.cv)
+    got = b.angmf_propagate(dev(n0), dev(u.prob[0]), dev(u.xy[0]), dev(u.angle[0]),
+                            dev(u.ray8), u.fu, u.cu, u.fv, u.cv)
+    report("angmf tiny/huge/zero sources", host(got), want, TOL32)
+
+
 def test_angmf_golden_edge_cases():
     """Hand-placed degeneracies (zero xy, |xy| < 1e-12, theta 0 / 1e-7 / pi,
     zero and non-unit normals, (P+d).n ~ 0) against the reference's outputs."""

@@ -182,3 +182,20 @@ def test_generator_distributions():
     assert c.min() >= 0
     assert abs(np.linalg.norm(u.normal0, axis=1) - 1).max() < 1e-6
     assert u.mask.shape == (2, 576, 20, 30)
+
+
+def test_head_activation_oracle():
+    """sigmoid / pi * sigmoid of src/dsine_refine.cpp:262-267 in the oracle:
+    within 2 ulp of torch's fp32 sigmoid, saturating cleanly at the extremes,
+    angle never above the float kPi."""
+    g = np.random.default_rng(4)
+    x = np.concatenate([g.normal(0, 4, 4000), [-1e4, -100.0, -30.0, -0.0, 0.0, 30.0, 100.0,
+                                               1e4]]).astype(np.float32)
+    p, a = O.head_activation(x, x)
+    t = torch.sigmoid(torch.from_numpy(x)).numpy()
+    normal = t >= np.finfo(np.float32).tiny  # torch may flush subnormal results
+    assert np.all(np.abs(p - t)[normal] <= 2 * np.spacing(t[normal]))
+    assert np.all(np.abs(p - t)[~normal] <= 1e-37)
+    assert p[-1] == 1.0 and p[-8] == 0.0 and np.all(np.isfinite(a))
+    assert a.max() <= O.KPI_F32 and a.min() >= 0.0
+    assert a.dtype == np.float32 and np.array_equal(a, (p * O.KPI_F32).astype(np.float32))
