@@ -14,7 +14,9 @@
 //  * failures throw std::runtime_error("dsine cuda: <what>: <error>") or
 //    "dsine ops: ..." like the reference.
 // It additionally exposes refine_ops_cuda(), the fused unit of
-// Refiner::forward's op calls, for a Refiner that wants one call per forward.
+// Refiner::forward's op calls, for a Refiner that wants one call per forward,
+// and angmf_propagate_logits_cuda(), which takes the prediction heads' raw
+// prob / angle outputs and applies their activations on load.
 #include "brotensor/tensor.h"
 #include "bvml_dsine.h"
 
@@ -51,17 +53,37 @@ void angmf_propagate_cuda(const brotensor::Tensor& pred_norm, const brotensor::T
                                /*ps=*/5, /*dil=*/1, BVML_F32, out.data, nullptr));
 }
 
+// angmf_propagate_cuda on the heads' raw outputs: prob = sigmoid(prob_logits)
+// and angle = kPi * sigmoid(angle_logits) are applied while the kernel loads
+// them, so a Refiner can drop apply_sigmoid(prob), apply_sigmoid(angle) and
+// scale_inplace(angle, kPi) (src/dsine_refine.cpp:262-267).
+void angmf_propagate_logits_cuda(const brotensor::Tensor& pred_norm,
+                                 const brotensor::Tensor& prob_logits,
+                                 const brotensor::Tensor& xy,
+                                 const brotensor::Tensor& angle_logits,
+                                 const brotensor::Tensor& ray, double fu, double cu, double fv,
+                                 double cv, int H, int W, brotensor::Tensor& out) {
+    const int HW = H * W;
+    out = brotensor::Tensor::zeros_on(brotensor::Device::CUDA, 1, 3 * HW);
+    if (HW == 0) return;
+    check(bvml_angmf_propagate_logits(pred_norm.data, prob_logits.data, xy.data,
+                                      angle_logits.data, static_cast<const float*>(ray.data), fu,
+                                      cu, fv, cv, 1, H, W, /*ps=*/5, /*dil=*/1, BVML_F32,
+                                      out.data, nullptr));
+}
+
 // The op part of Refiner::forward (src/dsine_refine.cpp:241-292) in one call:
 // ray_relu(normal), iterations of angmf_propagate over the per-iteration head
 // outputs, one convex upsample + L2-normalise, crop to (out_h, out_w) at
-// (crop_t, crop_l). Returns the (1, 3*out_h*out_w) CUDA tensor.
+// (crop_t, crop_l). Returns the (1, 3*out_h*out_w) CUDA tensor. With
+// head_logits, prob / angle are the heads' raw outputs (activated on load).
 brotensor::Tensor refine_ops_cuda(const brotensor::Tensor& normal, const brotensor::Tensor& ray8,
                                   const std::vector<const brotensor::Tensor*>& prob,
                                   const std::vector<const brotensor::Tensor*>& xy,
                                   const std::vector<const brotensor::Tensor*>& angle,
                                   const brotensor::Tensor& up_mask, double fu, double cu,
                                   double fv, double cv, int H, int W, int crop_t, int crop_l,
-                                  int out_h, int out_w) {
+                                  int out_h, int out_w, bool head_logits) {
     if (prob.size() != xy.size() || prob.size() != angle.size())
         throw std::runtime_error("dsine ops: refine_ops: per-iteration lists differ in length");
     const int iters = static_cast<int>(prob.size());
@@ -76,10 +98,10 @@ brotensor::Tensor refine_ops_cuda(const brotensor::Tensor& normal, const brotens
         brotensor::Device::CUDA, 1, static_cast<int>((ws_bytes + sizeof(float) - 1) / sizeof(float)));
     brotensor::Tensor out =
         brotensor::Tensor::zeros_on(brotensor::Device::CUDA, 1, 3 * out_h * out_w);
-    check(bvml_refine(normal.data, static_cast<const float*>(ray8.data), pp.data(), xp.data(),
-                      ap.data(), iters, up_mask.data, 1, H, W, 5, 1, fu, cu, fv, cv,
-                      /*full_res_ray_relu=*/0, crop_t, crop_l, out_h, out_w, BVML_F32, ws.data,
-                      ws_bytes, out.data, nullptr));
+    auto fn = head_logits ? bvml_refine_logits : bvml_refine;
+    check(fn(normal.data, static_cast<const float*>(ray8.data), pp.data(), xp.data(), ap.data(),
+             iters, up_mask.data, 1, H, W, 5, 1, fu, cu, fv, cv, /*full_res_ray_relu=*/0, crop_t,
+             crop_l, out_h, out_w, BVML_F32, ws.data, ws_bytes, out.data, nullptr));
     return out;
 }
 

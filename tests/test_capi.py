@@ -44,6 +44,11 @@ def test_bridge_library_exports_reference_signatures():
             "brotensor::Tensor const&, brotensor::Tensor const&, brotensor::Tensor const&, "
             "brotensor::Tensor const&, double, double, double, double, int, int, "
             "brotensor::Tensor&)") in out
+    assert ("brovisionml::dsine::detail::angmf_propagate_logits_cuda(brotensor::Tensor const&, "
+            "brotensor::Tensor const&, brotensor::Tensor const&, brotensor::Tensor const&, "
+            "brotensor::Tensor const&, double, double, double, double, int, int, "
+            "brotensor::Tensor&)") in out
+    assert "brovisionml::dsine::detail::refine_ops_cuda(" in out
 
 
 def test_argument_errors_without_gpu():
