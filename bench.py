@@ -145,9 +145,11 @@ class ClockSampler:
 
 # ----------------------------------------------------------------- inputs
 
-def make_device_inputs(cfg, seed, device, torch):
+def make_device_inputs(cfg, seed, device, torch, logits=False):
     """Seeded synthetic inputs on the GPU, generator distributions of the
-    benchmark configurations (oracle.gen_unit draws the same laws on CPU)."""
+    benchmark configurations (oracle.gen_unit draws the same laws on CPU).
+    logits: prob / angle as raw head outputs instead (N(0, 2.5) and
+    N(-2.5, 1.5) logits, for the path that activates them on load)."""
     H, W, B, ps, iters = cfg["H"], cfg["W"], cfg["B"], cfg["ps"], cfg["iters"]
     h, w = H // 8, W // 8
     P = ps * ps
@@ -173,6 +175,11 @@ def make_device_inputs(cfg, seed, device, torch):
     prob, xy, angle = [], [], []
     for _ in range(iters):
         xy.append(torch.randn((B, 2 * P, h, w), generator=g, device=device).to(dt))
+        if logits:
+            angle.append((torch.randn((B, P, h, w), generator=g, device=device) * 1.5
+                          - 2.5).to(dt))
+            prob.append((torch.randn((B, P, h, w), generator=g, device=device) * 2.5).to(dt))
+            continue
         angle.append((torch.rand((B, P, h, w), generator=g, device=device) * 0.3).to(dt))
         lg = torch.randn((B, P, h, w), generator=g, device=device)
         prob.append(torch.softmax(lg, dim=1).to(dt))
@@ -282,6 +289,8 @@ def workload_config(args, cfg, extra=None):
          "parallelism": f"image-parallel x{args.gpus}",
          "l2": "inputs ~9 GB/GPU >> 126 MB L2 (no flush needed)" if args.config == "cfg4"
                else "inputs larger than L2" }
+    if getattr(args, "logits", False):
+        c["head_outputs"] = "raw logits, sigmoid / pi*sigmoid applied on load"
     if extra:
         c.update(extra)
     return c
@@ -299,7 +308,12 @@ def main():
     ap.add_argument("--frames", type=int, default=0, help="override frames per GPU")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--logits", action="store_true",
+                    help="raw head outputs for prob / angle, activated on load (device "
+                         "timing only)")
     args = ap.parse_args()
+    if args.logits:
+        args.no_e2e = args.no_cpu = True
     args.steps = max(1, args.steps)
     cfg = dict(CONFIGS[args.config])
     if args.frames:
@@ -340,7 +354,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    inp = make_device_inputs(cfg, 1000 + rank, device, torch)
+    inp = make_device_inputs(cfg, 1000 + rank, device, torch, logits=args.logits)
     h, w, B, P, I = inp["h"], inp["w"], cfg["B"], cfg["ps"] ** 2, cfg["iters"]
     s = 2 if cfg["f16"] else 4
     out = torch.empty((B, 3, 8 * h, 8 * w), device=device, dtype=inp["dt"])
@@ -350,7 +364,8 @@ def main():
     def step():
         bv.refine(inp["normal0"], inp["prob"], inp["xy"], inp["angle"], inp["mask"], inp["fu"],
                   inp["cu"], inp["fv"], inp["cv"], ray8=inp["ray8"], ps=cfg["ps"],
-                  dil=cfg["dil"], full_res_ray_relu=cfg["rr"], out=out, workspace=ws)
+                  dil=cfg["dil"], full_res_ray_relu=cfg["rr"], out=out, workspace=ws,
+                  logits=args.logits)
 
     n_launch = I + 1
     import ctypes
