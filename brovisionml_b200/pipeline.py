@@ -114,3 +114,99 @@ class HostRefiner:
 
 def pin(t: torch.Tensor) -> torch.Tensor:
     return t.pin_memory() if not t.is_pinned() else t
+
+
+# ------------------------------------------------------------ one large frame
+
+@dataclass(frozen=True)
+class BandJob:
+    """One exact-halo row band of a large frame: compute grid rows
+    [comp0, comp1), keep the owned ones, i.e. output rows
+    [8 * own0, 8 * own1) of the frame, which are rows
+    [crop_t, crop_t + out_h) of the band's 8x output."""
+    own0: int
+    own1: int
+    comp0: int
+    comp1: int
+    crop_t: int
+    out_h: int
+
+
+def plan_band_jobs(h: int, n_bands: int, iters: int, ps: int, dil: int) -> list[BandJob]:
+    """The band jobs of an h-row grid (brovisionml_b200.sharding.plan_bands
+    with the exact halo of the unit)."""
+    from .sharding import halo_rows, plan_bands
+
+    bands = plan_bands(h, max(1, min(n_bands, h)), halo_rows(iters, ps, dil))
+    return [BandJob(b.own0, b.own1, b.comp0, b.comp1, 8 * b.crop_top, 8 * (b.own1 - b.own0))
+            for b in bands if b.own1 > b.own0]
+
+
+@dataclass
+class HostFrame:
+    """Host inputs of ONE frame: normal0 (3,h,w), prob[i] (P,h,w),
+    xy[i] (2P,h,w), angle[i] (P,h,w), mask (576,h,w), ray8 (3,h,w) fp32 or
+    None (computed on the device for each band)."""
+    normal0: torch.Tensor
+    prob: Sequence[torch.Tensor]
+    xy: Sequence[torch.Tensor]
+    angle: Sequence[torch.Tensor]
+    mask: torch.Tensor
+    ray8: torch.Tensor | None = None
+
+
+def refine_frame_banded(frame: HostFrame, out_host: torch.Tensor, fu: float, cu: float,
+                        fv: float, cv: float, *, n_bands: int, devices: Sequence[int] = (0,),
+                        ps: int = 5, dil: int = 1, full_res_ray_relu: bool = False,
+                        logits: bool = False) -> None:
+    """Refine one frame too large for one call (or for one GPU's memory) as
+    exact-halo row bands: band k runs on devices[k % len(devices)] (one host
+    thread per device, bands of a device in order), and each band's owned
+    output rows are cropped by the fused unit itself and copied straight
+    into ``out_host`` (3, 8h, 8w) -- the 3-channel crop-stitch. The halo
+    (sharding.halo_rows) makes the result equal the whole-frame refine up to
+    the fp32 rounding of the band-shifted principal point; the reference
+    instead caps the resolution of a large frame (src/dsine.cpp:117-141)."""
+    import threading
+
+    from .sharding import Band, band_intrinsics
+
+    iters = len(frame.prob)
+    _, h, w = frame.normal0.shape
+    jobs = plan_band_jobs(h, n_bands, iters, ps, dil)
+    per_dev = {d: [j for k, j in enumerate(jobs) if devices[k % len(devices)] == d]
+               for d in dict.fromkeys(devices)}
+    errors = []
+
+    def rows(t: torch.Tensor, j: BandJob) -> torch.Tensor:
+        return t[:, j.comp0:j.comp1]
+
+    def work(d: int, my_jobs: list[BandJob]) -> None:
+        try:
+            dev = torch.device("cuda", d)
+            with torch.cuda.device(dev):
+                stream = torch.cuda.Stream(dev)
+                with torch.cuda.stream(stream):
+                    for j in my_jobs:
+                        up = lambda t: rows(t, j).contiguous().pin_memory().to(  # noqa: E731
+                            dev, non_blocking=True)
+                        res = refine(up(frame.normal0)[None], [up(t)[None] for t in frame.prob],
+                                     [up(t)[None] for t in frame.xy],
+                                     [up(t)[None] for t in frame.angle], up(frame.mask)[None],
+                                     fu, cu, fv,
+                                     band_intrinsics(cv, Band(j.own0, j.own1, j.comp0, j.comp1)),
+                                     ray8=up(frame.ray8) if frame.ray8 is not None else None,
+                                     ps=ps, dil=dil, full_res_ray_relu=full_res_ray_relu,
+                                     crop=(j.crop_t, 0, j.out_h, 8 * w), logits=logits)
+                        out_host[:, 8 * j.own0:8 * j.own1].copy_(res[0])
+                stream.synchronize()
+        except BaseException as e:  # surfaced on the calling thread
+            errors.append(e)
+
+    threads = [threading.Thread(target=work, args=(d, js)) for d, js in per_dev.items() if js]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    if errors:
+        raise errors[0]

@@ -98,3 +98,31 @@ def test_fullsize_cfg1_full_res_ray_relu_faces_camera():
     c = (out * r).sum(0)
     assert c.min().item() >= 0.01 - 1e-5
     check_unit(out[None], 1e-5)
+
+
+@pytest.mark.parametrize("name,n_bands,given_ray", [("cfg2", 5, False), ("cfg1", 3, True)])
+def test_large_frame_driver_matches_whole_frame(name, n_bands, given_ray):
+    """brovisionml_b200.pipeline.refine_frame_banded (host inputs of one
+    frame, exact-halo row bands, crop-stitch into a host buffer) equals the
+    whole-frame refine of the same frame."""
+    import brovisionml_b200 as bv
+    from brovisionml_b200.pipeline import HostFrame, refine_frame_banded
+
+    cfg = dict(bench.CONFIGS[name])
+    cfg["B"] = 1
+    dev = torch.device("cuda", 0)
+    inp = bench.make_device_inputs(cfg, 17, dev, torch)
+    ray = inp["ray8"] if given_ray else None
+    want = bv.refine(inp["normal0"], inp["prob"], inp["xy"], inp["angle"], inp["mask"],
+                     inp["fu"], inp["cu"], inp["fv"], inp["cv"], ray8=ray, ps=cfg["ps"],
+                     dil=cfg["dil"], full_res_ray_relu=cfg["rr"])[0].float().cpu()
+    host = lambda t: t[0].cpu()  # noqa: E731
+    frame = HostFrame(host(inp["normal0"]), [host(t) for t in inp["prob"]],
+                      [host(t) for t in inp["xy"]], [host(t) for t in inp["angle"]],
+                      host(inp["mask"]), ray.cpu() if given_ray else None)
+    out = torch.empty_like(want, dtype=inp["dt"])
+    refine_frame_banded(frame, out, inp["fu"], inp["cu"], inp["fv"], inp["cv"],
+                        n_bands=n_bands, ps=cfg["ps"], dil=cfg["dil"],
+                        full_res_ray_relu=cfg["rr"])
+    err = (out.float() - want).abs().max().item()
+    assert err <= (2e-3 if cfg["f16"] else 1e-5), err

@@ -158,3 +158,25 @@ def test_gather_with_two_gloo_ranks():
     e1, e2 = q.get(timeout=5)
     assert e1 == 0.0
     assert e2 < 1e-5
+
+
+@pytest.mark.parametrize("h,n,iters,ps,dil", [(90, 4, 5, 5, 1), (128, 8, 5, 5, 2), (512, 3, 5, 7, 1),
+                                              (7, 16, 2, 3, 1), (1, 1, 5, 5, 1)])
+def test_band_jobs_tile_the_frame(h, n, iters, ps, dil):
+    """The large-frame driver's jobs: owned rows tile the grid exactly, each
+    band computes its owned rows plus the exact halo (clipped at the frame),
+    and its crop selects exactly the owned 8x output rows."""
+    from brovisionml_b200.pipeline import plan_band_jobs
+    from brovisionml_b200.sharding import halo_rows
+
+    jobs = plan_band_jobs(h, n, iters, ps, dil)
+    halo = halo_rows(iters, ps, dil)
+    assert jobs[0].own0 == 0 and jobs[-1].own1 == h
+    for a, b in zip(jobs, jobs[1:]):
+        assert a.own1 == b.own0
+    for j in jobs:
+        assert j.own1 > j.own0
+        assert j.comp0 == max(0, j.own0 - halo) and j.comp1 == min(h, j.own1 + halo)
+        assert j.crop_t == 8 * (j.own0 - j.comp0) and j.out_h == 8 * (j.own1 - j.own0)
+        assert j.crop_t + j.out_h <= 8 * (j.comp1 - j.comp0)
+    assert len(jobs) == min(n, h)
