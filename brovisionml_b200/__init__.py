@@ -17,9 +17,10 @@ from __future__ import annotations
 
 from ._capi import (BVML_F16, BVML_F32, LIB_PATH, abi_version, check, lib,  # noqa: F401
                     loaded_library)
-from .ops import (angmf_propagate, convex_upsample, l2_normalize_nchw, ray_relu,  # noqa: F401
-                  refine, refine_workspace_bytes, slice2d)
+from .ops import (angmf_propagate, conv2d_nhwc, convex_upsample, l2_normalize_nchw,  # noqa: F401
+                  pack_conv_weight, ray_relu, refine, refine_workspace_bytes, slice2d)
 
 __all__ = ["ray_relu", "angmf_propagate", "convex_upsample", "l2_normalize_nchw", "slice2d",
+           "conv2d_nhwc", "pack_conv_weight",
            "refine", "refine_workspace_bytes", "lib", "abi_version", "loaded_library",
            "LIB_PATH", "BVML_F32", "BVML_F16"]

@@ -20,7 +20,8 @@ BVML_OK = 0
 EXPORTS = ("bvml_last_error", "bvml_abi_version", "bvml_ray_relu", "bvml_angmf_propagate",
            "bvml_convex_upsample", "bvml_l2_normalize_nchw", "bvml_slice2d",
            "bvml_refine_workspace_bytes", "bvml_refine", "bvml_probe_events",
-           "bvml_refine_noalloc", "bvml_angmf_propagate_logits", "bvml_refine_logits")
+           "bvml_refine_noalloc", "bvml_angmf_propagate_logits", "bvml_refine_logits",
+           "bvml_conv2d_nhwc_bf16")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(
@@ -64,6 +65,8 @@ lib.bvml_refine_noalloc.argtypes = ([_vp, _vp, ctypes.POINTER(_vp), ctypes.POINT
                                      ctypes.POINTER(_vp), _i, _vp] + [_i] * 5 + [_d] * 4
                                     + [_i] * 6 + [_vp, _vp])
 REFINE_NOALLOC_MAX_BYTES = 32 * 1024 * 1024
+lib.bvml_conv2d_nhwc_bf16.restype = _i
+lib.bvml_conv2d_nhwc_bf16.argtypes = [_vp, _vp, _vp] + [_i] * 8 + [_vp, _vp, _vp]
 lib.bvml_probe_events.restype = _i
 lib.bvml_probe_events.argtypes = [ctypes.POINTER(_vp), _i]
 

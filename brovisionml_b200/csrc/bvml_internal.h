@@ -42,6 +42,16 @@ struct UpsampleLaunch {
 };
 cudaError_t launch_upsample(const UpsampleLaunch& L, cudaStream_t s);
 
+struct ConvLaunch {
+    const void* x;       // (B,H,W,cin_pad) bf16
+    const void* w;       // (ks*ks, cout_pad, cin_pad) bf16
+    const float* bias;   // (cout) fp32
+    void* y;             // (B,H,W,cout_pad) bf16
+    int* err;            // device int: nonzero if a pipeline wait gave up
+    int B, H, W, cin_pad, cout, cout_pad, ks, act;
+};
+cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s);
+
 cudaError_t launch_ray_relu(void* normal, SType t, const float* ray, int B, int H, int W,
                             cudaStream_t s);
 cudaError_t launch_build_ray(float* ray, int H, int W, double fu, double cu, double fv,

@@ -313,6 +313,37 @@ int bvml_slice2d(const void* x, int N, int C, int H, int W, int h0, int w0, int 
                   "slice2d launch");
 }
 
+int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B, int H, int W,
+                          int cin_pad, int cout, int cout_pad, int ks, int act, void* y,
+                          int* err, void* stream) {
+    if (!(ks == 1 || ks == 3 || ks == 5)) return einval("conv2d: kernel size must be 1, 3 or 5");
+    if (act < 0 || act > 3) return einval("conv2d: unknown activation");
+    if (B < 0 || H < 0 || W < 0 || cin_pad <= 0 || cin_pad % 64 != 0 || cout_pad <= 0 ||
+        cout_pad % 64 != 0 || cout <= 0 || cout > cout_pad)
+        return einval("conv2d: channel counts must be positive, padded to multiples of 64");
+    if ((int64_t)B * H * W > INT32_MAX / 2) return einval("conv2d: too many pixels");
+    if ((long)B * H * W == 0) return finish(cudaSuccess, "conv2d");
+    if (!x || !w || !bias || !y || !err) return einval("conv2d: null tensor");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+         reinterpret_cast<uintptr_t>(y)) & 15)
+        return einval("conv2d: tensors must be 16-byte aligned");
+    bvml::ConvLaunch L{};
+    L.x = x;
+    L.w = w;
+    L.bias = bias;
+    L.y = y;
+    L.err = err;
+    L.B = B;
+    L.H = H;
+    L.W = W;
+    L.cin_pad = cin_pad;
+    L.cout = cout;
+    L.cout_pad = cout_pad;
+    L.ks = ks;
+    L.act = act;
+    return finish(bvml::launch_conv_tc(L, static_cast<cudaStream_t>(stream)), "conv2d launch");
+}
+
 size_t bvml_refine_workspace_bytes(int B, int h, int w) {
     if (B < 0 || h < 0 || w < 0) return 0;
     const size_t plane = (size_t)h * (size_t)w;

@@ -191,6 +191,25 @@ int bvml_refine_noalloc(const void* normal0, const float* ray8, const void* cons
                         int crop_l, int out_h, int out_w, int dtype, void* out, void* stream);
 
 /*
+ * 2-D convolution, stride 1, zero padding ks/2 ("same"), on bf16 NHWC tensors
+ * with fp32 accumulation on the tensor cores (tcgen05), plus bias and an
+ * activation (0 none, 1 ReLU, 2 sigmoid, 3 tanh): the conv2d_forward calls of
+ * the refine stage's ConvGRU (5x5, src/dsine_refine.cpp:140-158) and
+ * prediction heads (3x3, 1x1, :118-125), which the reference runs through
+ * brotensor on NCHW fp32 tensors.
+ *   x    (B,H,W,cin_pad) bf16, cin_pad a multiple of 64, pad channels zero
+ *   w    (ks*ks, cout_pad, cin_pad) bf16, w[ky*ks+kx][o][c] = weight[o][c][ky][kx]
+ *   bias (cout) fp32
+ *   y    (B,H,W,cout_pad) bf16, cout_pad a multiple of 64; channels >= cout
+ *        are written as zeros, so y can be the next convolution's x
+ *   ks in {1, 3, 5}; err: a device int the kernel sets nonzero if its
+ *   pipeline had to give up (read it after synchronising; 0 = fine).
+ */
+int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B, int H, int W,
+                          int cin_pad, int cout, int cout_pad, int ks, int act, void* y,
+                          int* err, void* stream);
+
+/*
  * Profiling aid (no reference counterpart): arm `n` caller-created CUDA events
  * (cudaEvent_t, cast to void*) for the calling thread. While armed,
  * bvml_refine records events[0] on its stream before its first kernel and

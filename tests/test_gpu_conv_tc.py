@@ -1,0 +1,61 @@
+"""Tensor-core (tcgen05) implicit-GEMM convolution against a plain PyTorch fp32
+conv2d of the same bf16-rounded inputs and weights: the refine stage's conv
+shapes (ConvGRU 5x5 over 130 -> 64 channels, head 3x3 66 -> 128 and 1x1
+layers, src/dsine_refine.cpp:95-158) and edge cases (one CTA, odd frames,
+output channels that are not a multiple of the tile).
+
+Tolerance: the kernel rounds its output to bf16 (relative 2^-9) and sums in
+another order than torch: |y - ref| <= 8e-3 |ref| + 2e-3.
+"""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def ref_conv(x_nhwc, weight, bias, ks, act, cin):
+    x = x_nhwc[..., :cin].permute(0, 3, 1, 2).float()
+    y = torch.nn.functional.conv2d(x, weight.to(torch.bfloat16).float(), bias, padding=ks // 2)
+    y = {"none": y, "relu": torch.relu(y), "sigmoid": torch.sigmoid(y),
+         "tanh": torch.tanh(y)}[act]
+    return y.permute(0, 2, 3, 1)
+
+
+def run_case(B, H, W, cin, cout, ks, act, seed=0):
+    import brovisionml_b200 as b
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    cin_pad, cout_pad = b.ops.pad64(cin), b.ops.pad64(cout)
+    x = torch.zeros((B, H, W, cin_pad), device="cuda", dtype=torch.bfloat16)
+    x[..., :cin] = torch.randn((B, H, W, cin), device="cuda", generator=g).to(torch.bfloat16)
+    wstd = (cin * ks * ks) ** -0.5
+    weight = torch.randn((cout, cin, ks, ks), device="cuda", generator=g) * wstd
+    bias = torch.randn(cout, device="cuda", generator=g) * 0.1
+    y = b.conv2d_nhwc(x, b.pack_conv_weight(weight, cin_pad, cout_pad), bias, cout, ks=ks,
+                      act=act)
+    torch.cuda.synchronize()
+    ref = ref_conv(x, weight, bias, ks, act, cin)
+    got = y[..., :cout].float()
+    err = ((got - ref).abs() - 8e-3 * ref.abs()).max().item()
+    print(f"conv B{B} {H}x{W} {cin}->{cout} k{ks} {act}: excess {err:.2e} "
+          f"max_abs {(got - ref).abs().max().item():.2e}")
+    assert torch.isfinite(got).all()
+    assert err <= 2e-3
+    if cout_pad > cout:  # pad channels are zeros
+        assert (y[..., cout:] == 0).all()
+
+
+def test_conv_single_cta_1x1():
+    run_case(1, 4, 32, 64, 64, 1, "none")
+
+
+@pytest.mark.parametrize("B,H,W,cin,cout,ks,act", [
+    (1, 8, 16, 64, 128, 3, "relu"),
+    (2, 23, 37, 130, 64, 5, "tanh"),     # ConvGRU q: odd frame, padded input channels
+    (1, 90, 160, 130, 128, 5, "sigmoid"),  # ConvGRU z, r (fused), config 4 grid
+    (1, 60, 80, 66, 512, 3, "relu"),     # the four heads' first layers fused
+    (2, 45, 67, 128, 576, 1, "none"),    # up_prob head's last layer
+    (1, 17, 9, 128, 25, 1, "none"),      # prob head's last layer: 25 of 64 channels
+])
+def test_conv_shapes(B, H, W, cin, cout, ks, act):
+    run_case(B, H, W, cin, cout, ks, act, seed=H + W)
