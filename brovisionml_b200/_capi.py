@@ -21,7 +21,7 @@ EXPORTS = ("bvml_last_error", "bvml_abi_version", "bvml_ray_relu", "bvml_angmf_p
            "bvml_convex_upsample", "bvml_l2_normalize_nchw", "bvml_slice2d",
            "bvml_refine_workspace_bytes", "bvml_refine", "bvml_probe_events",
            "bvml_refine_noalloc", "bvml_angmf_propagate_logits", "bvml_refine_logits",
-           "bvml_conv2d_nhwc_bf16")
+           "bvml_conv2d_nhwc_bf16", "bvml_conv2d_nhwc_bf16_ex")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(
@@ -67,6 +67,19 @@ lib.bvml_refine_noalloc.argtypes = ([_vp, _vp, ctypes.POINTER(_vp), ctypes.POINT
 REFINE_NOALLOC_MAX_BYTES = 32 * 1024 * 1024
 lib.bvml_conv2d_nhwc_bf16.restype = _i
 lib.bvml_conv2d_nhwc_bf16.argtypes = [_vp, _vp, _vp] + [_i] * 8 + [_vp, _vp, _vp]
+
+
+class ConvEpilogue(ctypes.Structure):
+    """bvml_conv_epilogue (include/bvml_dsine.h)."""
+    _fields_ = [("mode", _i), ("act", _i), ("out", _vp), ("out_c", _i), ("out_off", _i),
+                ("h32", _vp), ("z", _vp), ("rh", _vp), ("rh_c", _i), ("hx", _vp), ("hx_c", _i),
+                ("hin", _vp), ("hin_c", _i)]
+
+
+EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, EPI_GRU_ZR, EPI_GRU_Q = range(5)
+lib.bvml_conv2d_nhwc_bf16_ex.restype = _i
+lib.bvml_conv2d_nhwc_bf16_ex.argtypes = ([_vp, _i, _i, _i, _vp, _vp] + [_i] * 6
+                                          + [ctypes.POINTER(ConvEpilogue), _vp, _vp])
 lib.bvml_probe_events.restype = _i
 lib.bvml_probe_events.argtypes = [ctypes.POINTER(_vp), _i]
 

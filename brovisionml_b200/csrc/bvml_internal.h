@@ -42,13 +42,26 @@ struct UpsampleLaunch {
 };
 cudaError_t launch_upsample(const UpsampleLaunch& L, cudaStream_t s);
 
+enum class ConvEpi : int { NHWC = 0, PLANAR16 = 1, PLANAR32 = 2, GRU_ZR = 3, GRU_Q = 4 };
+
 struct ConvLaunch {
-    const void* x;       // (B,H,W,cin_pad) bf16
+    const void* x;       // (B,H,W,x_c) bf16; channels [cin_off, cin_off + cin_pad) are read
     const void* w;       // (ks*ks, cout_pad, cin_pad) bf16
     const float* bias;   // (cout) fp32
-    void* y;             // (B,H,W,cout_pad) bf16
     int* err;            // device int: nonzero if a pipeline wait gave up
-    int B, H, W, cin_pad, cout, cout_pad, ks, act;
+    int B, H, W, x_c, cin_off, cin_pad, cout, cout_pad, ks;
+    ConvEpi epi;
+    int act;             // NHWC: 0 none, 1 ReLU, 2 sigmoid, 3 tanh
+    void* y;             // NHWC: (B,H,W,out_c) bf16 written at out_off; PLANAR: (B,cout,H,W)
+    int out_c, out_off;
+    float* h32;          // GRU: fp32 hidden state (B,H,W,64)
+    void* z;             // GRU: gate z (B,H,W,64) bf16
+    void* rh;            // GRU_ZR: r * h at channels [0,64) of (B,H,W,rh_c)
+    int rh_c;
+    void* hx;            // GRU_Q: new h (bf16) at channels [0,64) of (B,H,W,hx_c)
+    int hx_c;
+    void* hin;           // GRU_Q: ... and of (B,H,W,hin_c) when not null
+    int hin_c;
 };
 cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s);
 

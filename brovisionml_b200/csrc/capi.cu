@@ -336,11 +336,83 @@ int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B
     L.B = B;
     L.H = H;
     L.W = W;
+    L.x_c = cin_pad;
+    L.cin_off = 0;
     L.cin_pad = cin_pad;
     L.cout = cout;
     L.cout_pad = cout_pad;
     L.ks = ks;
+    L.epi = bvml::ConvEpi::NHWC;
     L.act = act;
+    L.out_c = cout_pad;
+    L.out_off = 0;
+    return finish(bvml::launch_conv_tc(L, static_cast<cudaStream_t>(stream)), "conv2d launch");
+}
+
+int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, const void* w,
+                             const float* bias, int B, int H, int W, int cout, int cout_pad,
+                             int ks, const bvml_conv_epilogue* epi, int* err, void* stream) {
+    auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (!(ks == 1 || ks == 3 || ks == 5)) return einval("conv2d: kernel size must be 1, 3 or 5");
+    if (!epi || epi->mode < 0 || epi->mode > 4) return einval("conv2d: unknown epilogue");
+    if (B < 0 || H < 0 || W < 0 || x_c <= 0 || x_c % 8 != 0 || cin_off < 0 ||
+        cin_off % 64 != 0 || cin_pad <= 0 || cin_pad % 64 != 0 || cin_off + cin_pad > x_c + 63 ||
+        cout <= 0 || cout_pad % 64 != 0 || cout > cout_pad)
+        return einval("conv2d: bad channel layout");
+    if ((int64_t)B * H * W > INT32_MAX / 2) return einval("conv2d: too many pixels");
+    if ((long)B * H * W == 0) return finish(cudaSuccess, "conv2d");
+    if (!x || !w || !bias || !err || !a16(x) || !a16(w))
+        return einval("conv2d: null or unaligned tensor");
+    bvml::ConvLaunch L{};
+    L.x = x;
+    L.w = w;
+    L.bias = bias;
+    L.err = err;
+    L.B = B;
+    L.H = H;
+    L.W = W;
+    L.x_c = x_c;
+    L.cin_off = cin_off;
+    L.cin_pad = cin_pad;
+    L.cout = cout;
+    L.cout_pad = cout_pad;
+    L.ks = ks;
+    L.epi = static_cast<bvml::ConvEpi>(epi->mode);
+    L.act = epi->act;
+    L.y = epi->out;
+    L.out_c = epi->out_c;
+    L.out_off = epi->out_off;
+    L.h32 = epi->h32;
+    L.z = epi->z;
+    L.rh = epi->rh;
+    L.rh_c = epi->rh_c;
+    L.hx = epi->hx;
+    L.hx_c = epi->hx_c;
+    L.hin = epi->hin;
+    L.hin_c = epi->hin_c;
+    switch (epi->mode) {
+        case BVML_EPI_NHWC:
+            if (epi->act < 0 || epi->act > 3) return einval("conv2d: unknown activation");
+            if (!epi->out || !a16(epi->out) || epi->out_c % 8 || epi->out_off % 8 ||
+                epi->out_off + cout_pad > epi->out_c)
+                return einval("conv2d: bad NHWC output");
+            break;
+        case BVML_EPI_PLANAR_F16:
+        case BVML_EPI_PLANAR_F32:
+            if (!epi->out) return einval("conv2d: null planar output");
+            break;
+        case BVML_EPI_GRU_ZR:
+            if (cout != 128 || !epi->h32 || !epi->z || !epi->rh || !a16(epi->h32) ||
+                !a16(epi->z) || !a16(epi->rh) || epi->rh_c % 8 || epi->rh_c < 64)
+                return einval("conv2d: GRU z/r epilogue needs cout 128, h32, z and rh");
+            break;
+        case BVML_EPI_GRU_Q:
+            if (cout != 64 || !epi->h32 || !epi->z || !epi->hx || !a16(epi->h32) ||
+                !a16(epi->z) || !a16(epi->hx) || epi->hx_c % 8 || epi->hx_c < 64 ||
+                (epi->hin && (!a16(epi->hin) || epi->hin_c % 8 || epi->hin_c < 64)))
+                return einval("conv2d: GRU q epilogue needs cout 64, h32, z and hx");
+            break;
+    }
     return finish(bvml::launch_conv_tc(L, static_cast<cudaStream_t>(stream)), "conv2d launch");
 }
 

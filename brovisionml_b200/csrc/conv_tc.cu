@@ -45,21 +45,22 @@ constexpr uint32_t kWaitLimit = 1u << 22;
 
 struct ConvArgs {
     int B, H, W;
-    int cin_pad, cout, cout_pad;
+    int cin_off, cin_pad, cout, cout_pad;  // input channel slice, output channels
     int ks, pad;
     int tw, th, tiles_x, tiles_y;
     const float* bias;
-    __nv_bfloat16* out;
     int* err;
-};
-
-template <int N, int S>
-struct ConvCfg {
-    static constexpr int kABytes = kTM * kKC * 2;
-    static constexpr int kBBytes = N * kKC * 2;
-    static constexpr int kStage = kABytes + kBBytes;
-    static constexpr int kBarOff = S * kStage;                 // mbarriers after the ring
-    static constexpr int kSmem = kBarOff + 256 + 1024;         // + barriers, alignment slack
+    // epilogue targets (see ConvEpi)
+    void* out;
+    int out_c, out_off;
+    float* h32;
+    __nv_bfloat16* z;
+    __nv_bfloat16* rh;
+    int rh_c;
+    __nv_bfloat16* hx;
+    int hx_c;
+    __nv_bfloat16* hin;
+    int hin_c;
 };
 
 template <int ACT>
@@ -70,7 +71,111 @@ __device__ __forceinline__ float activate(float v) {
     else return v;
 }
 
-template <int N, int S, int ACT>
+// Epilogue of one thread's pixel for 32 consecutive output channels
+// cb .. cb+31 (accumulators + bias in v). Modes (ConvEpi in bvml_internal.h):
+//  NHWC      act(v) as bf16 at out[pix * out_c + out_off + c], zeros past cout;
+//  PLANAR16/32  v as fp16 / fp32 at out[(b * cout + c) * H * W + y * W + x]
+//            for c < cout (the NCHW planes the refine ops take);
+//  GRU_ZR    c < 64: z = sigmoid(v) -> z[pix * 64 + c];
+//            64 <= c < 128: r = sigmoid(v) -> rh[pix * rh_c + c - 64] = r * h32;
+//  GRU_Q     c < 64: q = tanh(v), h = (1 - z) h + z q -> h32 (fp32 state) and
+//            bf16 copies at hx[pix * hx_c + c] and, if set, hin[pix * hin_c + c]
+//  (src/dsine_refine.cpp:140-158).
+template <int EPI, int ACT>
+__device__ __forceinline__ void epilogue32(const ConvArgs& a, long pix, int b, int px, int py,
+                                           int cb, const uint32_t (&v)[32]) {
+    float f[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        f[i] = cb + i < a.cout ? __uint_as_float(v[i]) + a.bias[cb + i] : 0.0f;
+    if constexpr (EPI == (int)ConvEpi::NHWC) {
+        alignas(16) __nv_bfloat16 o[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            o[i] = __float2bfloat16_rn(cb + i < a.cout ? activate<ACT>(f[i]) : 0.0f);
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) +
+                                              pix * a.out_c + a.out_off + cb);
+        const uint4* src = reinterpret_cast<const uint4*>(o);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) dst[q] = src[q];
+    } else if constexpr (EPI == (int)ConvEpi::PLANAR16 || EPI == (int)ConvEpi::PLANAR32) {
+        const long hw = (long)a.H * a.W;
+        const long p = (long)py * a.W + px;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int c = cb + i;
+            if (c >= a.cout) break;
+            const long o = ((long)b * a.cout + c) * hw + p;
+            if constexpr (EPI == (int)ConvEpi::PLANAR16)
+                static_cast<__half*>(a.out)[o] = __float2half_rn(f[i]);
+            else
+                static_cast<float*>(a.out)[o] = f[i];
+        }
+    } else if constexpr (EPI == (int)ConvEpi::GRU_ZR) {
+        alignas(16) __nv_bfloat16 o[32];
+        if (cb < 64) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float2bfloat16_rn(activate<2>(f[i]));
+            uint4* dst = reinterpret_cast<uint4*>(a.z + pix * 64 + cb);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dst[q] = reinterpret_cast<const uint4*>(o)[q];
+        } else if (cb < 128) {
+            const float4* h4 = reinterpret_cast<const float4*>(a.h32 + pix * 64 + (cb - 64));
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 h = h4[q];
+                o[4 * q + 0] = __float2bfloat16_rn(activate<2>(f[4 * q + 0]) * h.x);
+                o[4 * q + 1] = __float2bfloat16_rn(activate<2>(f[4 * q + 1]) * h.y);
+                o[4 * q + 2] = __float2bfloat16_rn(activate<2>(f[4 * q + 2]) * h.z);
+                o[4 * q + 3] = __float2bfloat16_rn(activate<2>(f[4 * q + 3]) * h.w);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(a.rh + pix * a.rh_c + (cb - 64));
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dst[q] = reinterpret_cast<const uint4*>(o)[q];
+        }
+    } else if constexpr (EPI == (int)ConvEpi::GRU_Q) {
+        if (cb >= 64) return;
+        float4* h4 = reinterpret_cast<float4*>(a.h32 + pix * 64 + cb);
+        const uint4* z4 = reinterpret_cast<const uint4*>(a.z + pix * 64 + cb);
+        alignas(16) __nv_bfloat16 zb[32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) reinterpret_cast<uint4*>(zb)[q] = z4[q];
+        alignas(16) __nv_bfloat16 o[32];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            float4 h = h4[q];
+            float* hh = reinterpret_cast<float*>(&h);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int i = 4 * q + e;
+                const float z = __bfloat162float(zb[i]);
+                hh[e] = fmaf(z, tanhf(f[i]) - hh[e], hh[e]);  // (1 - z) h + z q
+                o[i] = __float2bfloat16_rn(hh[e]);
+            }
+            h4[q] = h;
+        }
+        uint4* d1 = reinterpret_cast<uint4*>(a.hx + pix * a.hx_c + cb);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) d1[q] = reinterpret_cast<const uint4*>(o)[q];
+        if (a.hin) {
+            uint4* d2 = reinterpret_cast<uint4*>(a.hin + pix * a.hin_c + cb);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) d2[q] = reinterpret_cast<const uint4*>(o)[q];
+        }
+    }
+}
+
+template <int N, int S>
+struct ConvCfg {
+    static constexpr int kABytes = kTM * kKC * 2;
+    static constexpr int kBBytes = N * kKC * 2;
+    static constexpr int kStage = kABytes + kBBytes;
+    static constexpr int kBarOff = S * kStage;                 // mbarriers after the ring
+    static constexpr int kSmem = kBarOff + 256 + 1024;         // + barriers, alignment slack
+};
+
+
+template <int N, int S, int EPI, int ACT>
 __global__ void __launch_bounds__(kConvThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                const ConvArgs a) {
@@ -134,7 +239,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             const int ky = tap / a.ks, kx = tap - ky * a.ks;
             const uint32_t sa = sbase + s * C::kStage, sb = sa + C::kABytes;
             tc::mbar_expect_tx(bar_full + 8 * s, C::kABytes + C::kBBytes);
-            tc::tma_load_4d(sa, &map_a, bar_full + 8 * s, ch * kKC, x0 + kx - a.pad,
+            tc::tma_load_4d(sa, &map_a, bar_full + 8 * s, a.cin_off + ch * kKC, x0 + kx - a.pad,
                             y0 + ky - a.pad, b);
             tc::tma_load_3d(sb, &map_b, bar_full + 8 * s, ch * kKC, n0, tap);
             issued = it + 1;
@@ -171,8 +276,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         tc::tc_fence_after();
         const int px = x0 + row % a.tw, py = y0 + row / a.tw;
         const bool in = ok && !aborted() && px < a.W && py < a.H;
-        __nv_bfloat16* orow =
-            a.out + (((long)b * a.H + (in ? py : 0)) * a.W + (in ? px : 0)) * a.cout_pad;
+        const long pix = ((long)b * a.H + py) * a.W + px;
 #pragma unroll 1
         for (int c0 = 0; c0 < N; c0 += 32) {
             uint32_t v[32];
@@ -180,18 +284,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             tc::tmem_ld_wait();
             const int cb = n0 + c0;
             if (!in || cb >= a.cout_pad) continue;
-            alignas(16) __nv_bfloat16 o[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const int c = cb + i;
-                const float val = c < a.cout ? activate<ACT>(__uint_as_float(v[i]) + a.bias[c])
-                                             : 0.0f;
-                o[i] = __float2bfloat16_rn(val);
-            }
-            uint4* dst = reinterpret_cast<uint4*>(orow + cb);
-            const uint4* src = reinterpret_cast<const uint4*>(o);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) dst[q] = src[q];
+            epilogue32<EPI, ACT>(a, pix, b, px, py, cb, v);
         }
     }
     tc::tc_fence_before();
@@ -228,10 +321,10 @@ bool encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int N, int S, int ACT>
+template <int N, int S, int EPI, int ACT>
 cudaError_t launch_n(const CUtensorMap& ma, const CUtensorMap& mb, const ConvArgs& a,
                      cudaStream_t s) {
-    auto kern = conv_tc_kernel<N, S, ACT>;
+    auto kern = conv_tc_kernel<N, S, EPI, ACT>;
     constexpr int smem = ConvCfg<N, S>::kSmem;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -240,13 +333,13 @@ cudaError_t launch_n(const CUtensorMap& ma, const CUtensorMap& mb, const ConvArg
     return cudaGetLastError();
 }
 
-template <int ACT>
+template <int EPI, int ACT>
 cudaError_t launch_act(int n, const CUtensorMap& ma, const CUtensorMap& mb, const ConvArgs& a,
                        cudaStream_t s) {
     switch (n) {
-        case 256: return launch_n<256, 4, ACT>(ma, mb, a, s);
-        case 128: return launch_n<128, 5, ACT>(ma, mb, a, s);
-        default: return launch_n<64, 6, ACT>(ma, mb, a, s);
+        case 256: return launch_n<256, 4, EPI, ACT>(ma, mb, a, s);
+        case 128: return launch_n<128, 5, EPI, ACT>(ma, mb, a, s);
+        default: return launch_n<64, 6, EPI, ACT>(ma, mb, a, s);
     }
 }
 
@@ -258,14 +351,25 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     a.B = L.B;
     a.H = L.H;
     a.W = L.W;
+    a.cin_off = L.cin_off;
     a.cin_pad = L.cin_pad;
     a.cout = L.cout;
     a.cout_pad = L.cout_pad;
     a.ks = L.ks;
     a.pad = L.ks / 2;
     a.bias = L.bias;
-    a.out = static_cast<__nv_bfloat16*>(L.y);
     a.err = L.err;
+    a.out = L.y;
+    a.out_c = L.out_c;
+    a.out_off = L.out_off;
+    a.h32 = L.h32;
+    a.z = static_cast<__nv_bfloat16*>(L.z);
+    a.rh = static_cast<__nv_bfloat16*>(L.rh);
+    a.rh_c = L.rh_c;
+    a.hx = static_cast<__nv_bfloat16*>(L.hx);
+    a.hx_c = L.hx_c;
+    a.hin = static_cast<__nv_bfloat16*>(L.hin);
+    a.hin_c = L.hin_c;
     // pixel tile tw x th (= 128): the shape with the fewest out-of-frame rows
     static const int tws[4] = {128, 64, 32, 16};
     long best = -1;
@@ -281,13 +385,16 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     a.tiles_x = (L.W + a.tw - 1) / a.tw;
     a.tiles_y = (L.H + a.th - 1) / a.th;
     if ((long)a.tiles_x * a.tiles_y * L.B > 0x7fffffffL) return cudaErrorInvalidConfiguration;
-    const int n = L.cout_pad >= 256 ? 256 : (L.cout_pad >= 128 ? 128 : 64);
+    // GRU gates need every channel of a pixel in one CTA (z with r, q with z)
+    int n = L.cout_pad >= 256 ? 256 : (L.cout_pad >= 128 ? 128 : 64);
+    if (L.epi == ConvEpi::GRU_ZR) n = 128;
+    if (L.epi == ConvEpi::GRU_Q) n = 64;
 
     CUtensorMap ma, mb;
-    const cuuint64_t dims_a[4] = {(cuuint64_t)L.cin_pad, (cuuint64_t)L.W, (cuuint64_t)L.H,
+    const cuuint64_t dims_a[4] = {(cuuint64_t)L.x_c, (cuuint64_t)L.W, (cuuint64_t)L.H,
                                   (cuuint64_t)L.B};
-    const cuuint64_t str_a[3] = {(cuuint64_t)L.cin_pad * 2, (cuuint64_t)L.W * L.cin_pad * 2,
-                                 (cuuint64_t)L.H * L.W * L.cin_pad * 2};
+    const cuuint64_t str_a[3] = {(cuuint64_t)L.x_c * 2, (cuuint64_t)L.W * L.x_c * 2,
+                                 (cuuint64_t)L.H * L.W * L.x_c * 2};
     const cuuint32_t box_a[4] = {(cuuint32_t)kKC, (cuuint32_t)a.tw, (cuuint32_t)a.th, 1};
     const cuuint64_t dims_b[3] = {(cuuint64_t)L.cin_pad, (cuuint64_t)L.cout_pad,
                                   (cuuint64_t)(L.ks * L.ks)};
@@ -296,13 +403,21 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     const cuuint32_t box_b[3] = {(cuuint32_t)kKC, (cuuint32_t)n, 1};
     if (!encode(&ma, L.x, 4, dims_a, str_a, box_a) || !encode(&mb, L.w, 3, dims_b, str_b, box_b))
         return cudaErrorInvalidValue;
-    switch (L.act) {
-        case 0: return launch_act<0>(n, ma, mb, a, s);
-        case 1: return launch_act<1>(n, ma, mb, a, s);
-        case 2: return launch_act<2>(n, ma, mb, a, s);
-        case 3: return launch_act<3>(n, ma, mb, a, s);
-        default: return cudaErrorInvalidValue;
+    switch (L.epi) {
+        case ConvEpi::NHWC:
+            switch (L.act) {
+                case 0: return launch_act<(int)ConvEpi::NHWC, 0>(n, ma, mb, a, s);
+                case 1: return launch_act<(int)ConvEpi::NHWC, 1>(n, ma, mb, a, s);
+                case 2: return launch_act<(int)ConvEpi::NHWC, 2>(n, ma, mb, a, s);
+                case 3: return launch_act<(int)ConvEpi::NHWC, 3>(n, ma, mb, a, s);
+                default: return cudaErrorInvalidValue;
+            }
+        case ConvEpi::PLANAR16: return launch_act<(int)ConvEpi::PLANAR16, 0>(n, ma, mb, a, s);
+        case ConvEpi::PLANAR32: return launch_act<(int)ConvEpi::PLANAR32, 0>(n, ma, mb, a, s);
+        case ConvEpi::GRU_ZR: return launch_act<(int)ConvEpi::GRU_ZR, 0>(n, ma, mb, a, s);
+        case ConvEpi::GRU_Q: return launch_act<(int)ConvEpi::GRU_Q, 0>(n, ma, mb, a, s);
     }
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace bvml

@@ -1,0 +1,190 @@
+"""The learned half of DSINE's refinement on the tensor cores: the ConvGRU and
+the four prediction heads of ``Refiner::forward`` (src/dsine_refine.cpp:
+95-158, 253-276), whose raw outputs feed the refine ops (``refine(...,
+logits=True)``).
+
+Per iteration (the GRU and heads never read the normals, so all iterations
+run first and the ops unit consumes their outputs afterwards):
+
+  hx  = [h | feat | uv]            (B,h,w,192) bf16 NHWC; feat, uv fixed
+  z, r = sigmoid(convz / convr(hx))      5x5, one fused GEMM (N = 128),
+         epilogue writes z and r*h into rhx = [r*h | feat | uv]
+  q   = tanh(convq(rhx))                 5x5, epilogue h = (1-z) h + z q
+                                          (fp32 state), bf16 h into hx and hin
+  hin = [h | uv]                   (B,h,w,128)
+  each head: conv3x3 -> ReLU -> conv1x1 -> ReLU -> conv1x1
+         the four 3x3 layers as one GEMM (N = 512); the 1x1 layers per head
+         on 128-channel slices; the last layer writes planar NCHW (fp16 or
+         fp32): prob (25), xy (50), angle (25), up_mask (576) logits.
+
+11 tensor-core launches per iteration, no separate elementwise or layout
+pass. Weights are the reference's (OIHW fp32, safetensors names
+``gru.convz`` ... ``up_prob_head.4``), rounded to bf16 once; activations are
+bf16 between layers, the GRU state fp32.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from ._capi import EPI_GRU_Q, EPI_GRU_ZR, EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, \
+    ConvEpilogue, check, lib
+from .ops import _cuda, _p, _stream, pack_conv_weight, pad64
+
+HEADS = (("prob_head", 25), ("xy_head", 50), ("angle_head", 25), ("up_prob_head", 576))
+HIDDEN = 64      # ConvGRU hidden channels
+FEATURE = 64     # decoder feature channels (input_dim 66 = feature + uv)
+HEAD_HIDDEN = 128
+
+
+def random_params(device, seed: int = 0) -> dict[str, torch.Tensor]:
+    """Random weights with the reference's shapes and names (no checkpoint is
+    available here): convs with std 1/sqrt(fan_in), small biases."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    p = {}
+
+    def conv(name, cout, cin, k):
+        p[name + ".weight"] = torch.randn((cout, cin, k, k), device=device,
+                                          generator=g) * (cin * k * k) ** -0.5
+        p[name + ".bias"] = torch.randn(cout, device=device, generator=g) * 0.05
+
+    cin = HIDDEN + FEATURE + 2
+    for n in ("gru.convz", "gru.convr", "gru.convq"):
+        conv(n, HIDDEN, cin, 5)
+    for head, out in HEADS:
+        conv(head + ".0", HEAD_HIDDEN, HIDDEN + 2, 3)
+        conv(head + ".2", HEAD_HIDDEN, HEAD_HIDDEN, 1)
+        conv(head + ".4", out, HEAD_HIDDEN, 1)
+    return p
+
+
+@dataclass
+class StageOutputs:
+    """Raw head outputs of one iteration, planar (B,C,h,w)."""
+    prob: torch.Tensor
+    xy: torch.Tensor
+    angle: torch.Tensor
+    up_mask: torch.Tensor
+
+
+class RefineStage:
+    """ConvGRU + prediction heads for B frames of an (h, w) grid on one GPU."""
+
+    def __init__(self, params: dict[str, torch.Tensor], B: int, h: int, w: int,
+                 device: torch.device | int = 0, out_dtype: torch.dtype = torch.float16):
+        self.dev = torch.device("cuda", device) if isinstance(device, int) else device
+        self.B, self.h, self.w = B, h, w
+        if out_dtype not in (torch.float16, torch.float32):
+            raise RuntimeError("dsine ops: refine stage: outputs are fp16 or fp32")
+        self.out_dtype = out_dtype
+        d = self.dev
+        f32 = lambda t: t.to(d, torch.float32).contiguous()  # noqa: E731
+        self.cin_gru = pad64(HIDDEN + FEATURE + 2)            # 192
+        self.cin_head = pad64(HIDDEN + 2)                     # 128
+        wz, wr = params["gru.convz.weight"], params["gru.convr.weight"]
+        self.w_zr = pack_conv_weight(torch.cat([wz, wr]).to(d), self.cin_gru, 128)
+        self.b_zr = f32(torch.cat([params["gru.convz.bias"], params["gru.convr.bias"]]))
+        self.w_q = pack_conv_weight(params["gru.convq.weight"].to(d), self.cin_gru, 64)
+        self.b_q = f32(params["gru.convq.bias"])
+        self.w_c0 = pack_conv_weight(torch.cat([params[f"{n}.0.weight"] for n, _ in HEADS]).to(d),
+                                     self.cin_head, 4 * HEAD_HIDDEN)
+        self.b_c0 = f32(torch.cat([params[f"{n}.0.bias"] for n, _ in HEADS]))
+        self.w_c2 = [pack_conv_weight(params[f"{n}.2.weight"].to(d), 128, 128) for n, _ in HEADS]
+        self.b_c2 = [f32(params[f"{n}.2.bias"]) for n, _ in HEADS]
+        self.w_c4 = [pack_conv_weight(params[f"{n}.4.weight"].to(d), 128, pad64(c))
+                     for n, c in HEADS]
+        self.b_c4 = [f32(params[f"{n}.4.bias"]) for n, _ in HEADS]
+        bf = torch.bfloat16
+        mk = lambda c, dt=bf: torch.zeros((B, h, w, c), device=d, dtype=dt)  # noqa: E731
+        self.hx, self.rhx, self.z = mk(self.cin_gru), mk(self.cin_gru), mk(HIDDEN)
+        self.hin, self.t1, self.t2 = mk(self.cin_head), mk(4 * HEAD_HIDDEN), mk(4 * HEAD_HIDDEN)
+        self.h32 = mk(HIDDEN, torch.float32)
+        self.err = torch.zeros(1, device=d, dtype=torch.int32)
+
+    # one launch through the C ABI
+    def _conv(self, x, cin_off, cin_pad, w, bias, cout, ks, **epi):
+        e = ConvEpilogue(**{k: (_p(v) if isinstance(v, torch.Tensor) else v)
+                            for k, v in epi.items()})
+        check(lib.bvml_conv2d_nhwc_bf16_ex(_p(x), x.shape[-1], cin_off, cin_pad, _p(w),
+                                           _p(bias), self.B, self.h, self.w, cout, w.shape[1],
+                                           ks, ctypes.byref(e), _p(self.err),
+                                           _stream(self.dev)))
+
+    def start(self, h0: torch.Tensor, feat: torch.Tensor, uv: torch.Tensor) -> None:
+        """Load the decoder's hidden state h0 (B,64,h,w), feature (B,64,h,w)
+        and uv (2,h,w) (src/dsine_refine.cpp:245-248)."""
+        _cuda("refine stage", h0, feat, uv)
+        B = self.B
+        nhwc = lambda t: t.permute(0, 2, 3, 1)  # noqa: E731
+        uvb = uv.permute(1, 2, 0)[None].expand(B, -1, -1, -1)
+        self.h32.copy_(nhwc(h0))
+        for buf in (self.hx, self.rhx):
+            buf[..., HIDDEN:HIDDEN + FEATURE] = nhwc(feat).to(torch.bfloat16)
+            buf[..., HIDDEN + FEATURE:HIDDEN + FEATURE + 2] = uvb.to(torch.bfloat16)
+        self.hx[..., :HIDDEN] = self.h32.to(torch.bfloat16)
+        self.hin[..., HIDDEN:HIDDEN + 2] = uvb.to(torch.bfloat16)
+
+    def step(self, out: StageOutputs | None = None) -> StageOutputs:
+        """One iteration: GRU update, then the four heads' raw outputs."""
+        B, h, w = self.B, self.h, self.w
+        if out is None:
+            mk = lambda c: torch.empty((B, c, h, w), device=self.dev,  # noqa: E731
+                                       dtype=self.out_dtype)
+            out = StageOutputs(*(mk(c) for _, c in HEADS))
+        with torch.cuda.device(self.dev):
+            self._conv(self.hx, 0, self.cin_gru, self.w_zr, self.b_zr, 128, 5, mode=EPI_GRU_ZR,
+                       h32=self.h32, z=self.z, rh=self.rhx, rh_c=self.cin_gru)
+            self._conv(self.rhx, 0, self.cin_gru, self.w_q, self.b_q, 64, 5, mode=EPI_GRU_Q,
+                       h32=self.h32, z=self.z, hx=self.hx, hx_c=self.cin_gru, hin=self.hin,
+                       hin_c=self.cin_head)
+            self._conv(self.hin, 0, self.cin_head, self.w_c0, self.b_c0, 4 * HEAD_HIDDEN, 3,
+                       mode=EPI_NHWC, act=1, out=self.t1, out_c=4 * HEAD_HIDDEN, out_off=0)
+            planar = EPI_PLANAR_F16 if self.out_dtype == torch.float16 else EPI_PLANAR_F32
+            dsts = (out.prob, out.xy, out.angle, out.up_mask)
+            for k, (_, c) in enumerate(HEADS):
+                self._conv(self.t1, k * HEAD_HIDDEN, HEAD_HIDDEN, self.w_c2[k], self.b_c2[k],
+                           HEAD_HIDDEN, 1, mode=EPI_NHWC, act=1, out=self.t2,
+                           out_c=4 * HEAD_HIDDEN, out_off=k * HEAD_HIDDEN)
+                self._conv(self.t2, k * HEAD_HIDDEN, HEAD_HIDDEN, self.w_c4[k], self.b_c4[k], c,
+                           1, mode=planar, out=dsts[k])
+        return out
+
+    def check_pipeline(self) -> None:
+        """Raise if any launch's pipeline gave up (one device sync)."""
+        if int(self.err.item()) != 0:
+            raise RuntimeError(f"dsine cuda: refine stage: pipeline gave up "
+                               f"(code {int(self.err.item())})")
+
+
+def reference_stage(params, h0, feat, uv, iters: int, *, emulate_bf16: bool = True):
+    """Plain PyTorch fp32 restatement of the same computation (the reference's
+    formulas, src/dsine_refine.cpp:118-158), for tests. With emulate_bf16 the
+    weights and the activations between layers are rounded to bf16 exactly
+    where RefineStage rounds them, so the two differ only in summation
+    order."""
+    F = torch.nn.functional
+    q16 = (lambda t: t.to(torch.bfloat16).float()) if emulate_bf16 else (lambda t: t)
+    W = {k: (q16(v) if k.endswith("weight") else v.float()) for k, v in params.items()}
+    B = h0.shape[0]
+    uvb = uv[None].expand(B, -1, -1, -1).float()
+    h = h0.float()
+    feat = feat.float()
+    outs = []
+    for _ in range(iters):
+        hx = q16(torch.cat([h, feat, uvb], 1))
+        z = torch.sigmoid(F.conv2d(hx, W["gru.convz.weight"], W["gru.convz.bias"], padding=2))
+        r = torch.sigmoid(F.conv2d(hx, W["gru.convr.weight"], W["gru.convr.bias"], padding=2))
+        z = q16(z)
+        rhx = torch.cat([q16(r * h), q16(feat), q16(uvb)], 1)
+        q = torch.tanh(F.conv2d(rhx, W["gru.convq.weight"], W["gru.convq.bias"], padding=2))
+        h = h + z * (q - h)
+        hin = q16(torch.cat([h, uvb], 1))
+        res = []
+        for name, _ in HEADS:
+            t = q16(F.relu(F.conv2d(hin, W[f"{name}.0.weight"], W[f"{name}.0.bias"], padding=1)))
+            t = q16(F.relu(F.conv2d(t, W[f"{name}.2.weight"], W[f"{name}.2.bias"])))
+            res.append(F.conv2d(t, W[f"{name}.4.weight"], W[f"{name}.4.bias"]))
+        outs.append(StageOutputs(*res))
+    return outs

@@ -209,6 +209,48 @@ int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B
                           int cin_pad, int cout, int cout_pad, int ks, int act, void* y,
                           int* err, void* stream);
 
+/* Epilogue modes of bvml_conv2d_nhwc_bf16_ex. */
+#define BVML_EPI_NHWC 0        /* act(conv) as bf16 at out[pixel * out_c + out_off + o] */
+#define BVML_EPI_PLANAR_F16 1  /* conv as fp16 at out[(b * cout + o) * H * W + y * W + x] */
+#define BVML_EPI_PLANAR_F32 2  /* the same in fp32 */
+#define BVML_EPI_GRU_ZR 3      /* ConvGRU gates z, r (cout = 128: z then r) */
+#define BVML_EPI_GRU_Q 4       /* ConvGRU candidate and update (cout = 64) */
+
+/*
+ * Where and how bvml_conv2d_nhwc_bf16_ex writes its result. Channel strides
+ * and offsets in elements, multiples of 8; tensors 16-byte aligned.
+ * GRU_ZR (src/dsine_refine.cpp:144-147): z = sigmoid(conv[0:64]) -> z
+ *   (B,H,W,64) bf16; r = sigmoid(conv[64:128]) -> rh[pixel * rh_c + o] = r * h,
+ *   h the fp32 hidden state h32 (B,H,W,64).
+ * GRU_Q (:148-156): q = tanh(conv) -> h32 = (1 - z) h32 + z q, with bf16
+ *   copies at hx[pixel * hx_c + o] and, when hin is not null, hin[...].
+ */
+typedef struct {
+    int mode;
+    int act;             /* BVML_EPI_NHWC: 0 none, 1 ReLU, 2 sigmoid, 3 tanh */
+    void* out;
+    int out_c, out_off;
+    float* h32;
+    void* z;
+    void* rh;
+    int rh_c;
+    void* hx;
+    int hx_c;
+    void* hin;
+    int hin_c;
+} bvml_conv_epilogue;
+
+/*
+ * bvml_conv2d_nhwc_bf16 reading input channels [cin_off, cin_off + cin_pad)
+ * of x (B,H,W,x_c) bf16 (cin_off and cin_pad multiples of 64; x_c a multiple
+ * of 8) and writing through `epi`: the fused ConvGRU gates and the
+ * prediction heads' planar outputs, so that the refine stage runs on NHWC
+ * buffers with no separate elementwise or layout passes.
+ */
+int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, const void* w,
+                             const float* bias, int B, int H, int W, int cout, int cout_pad,
+                             int ks, const bvml_conv_epilogue* epi, int* err, void* stream);
+
 /*
  * Profiling aid (no reference counterpart): arm `n` caller-created CUDA events
  * (cudaEvent_t, cast to void*) for the calling thread. While armed,

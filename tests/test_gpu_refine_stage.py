@@ -1,0 +1,77 @@
+"""ConvGRU + prediction heads on the tensor cores (brovisionml_b200.
+refine_stage, src/dsine_refine.cpp:95-158 and 253-276) against a plain
+PyTorch fp32 restatement of the same formulas, with weights and the
+activations between layers rounded to bf16 at the same points
+(refine_stage.reference_stage), so the two differ only in summation order
+and the rare bf16 rounding flip that order causes.
+
+Tolerances: per head output, max |d| <= 3e-2 and mean |d| <= 1e-3 after one
+iteration (outputs are O(1)); after three iterations of feedback through
+the GRU state, max |d| <= 6e-2 and mean |d| <= 3e-3. The unrounded fp32
+model's distance is printed for information.
+"""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def make_inputs(B, h, w, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    h0 = torch.tanh(torch.randn((B, 64, h, w), device="cuda", generator=g))
+    feat = torch.relu(torch.randn((B, 64, h, w), device="cuda", generator=g))
+    ys, xs = torch.meshgrid(torch.arange(h, device="cuda"), torch.arange(w, device="cuda"),
+                            indexing="ij")
+    uv = torch.stack([((xs + 0.5) - w / 2) / (0.8 * w), ((ys + 0.5) - h / 2) / (0.8 * w)]).float()
+    return h0, feat, uv
+
+
+@pytest.mark.parametrize("B,h,w,iters,out_dtype", [(2, 24, 40, 1, torch.float32),
+                                                   (1, 45, 80, 3, torch.float16)])
+def test_refine_stage_matches_torch(B, h, w, iters, out_dtype):
+    from brovisionml_b200.refine_stage import RefineStage, random_params, reference_stage
+
+    params = random_params("cuda", seed=B + h)
+    h0, feat, uv = make_inputs(B, h, w, seed=w)
+    st = RefineStage(params, B, h, w, out_dtype=out_dtype)
+    st.start(h0, feat, uv)
+    outs = [st.step() for _ in range(iters)]
+    torch.cuda.synchronize()
+    st.check_pipeline()
+    want = reference_stage(params, h0, feat, uv, iters)
+    exact = reference_stage(params, h0, feat, uv, iters, emulate_bf16=False)
+    lim_max, lim_mean = (3e-2, 1e-3) if iters == 1 else (6e-2, 3e-3)
+    for name in ("prob", "xy", "angle", "up_mask"):
+        got = getattr(outs[-1], name).float()
+        ref = getattr(want[-1], name)
+        d = (got - ref).abs()
+        de = (got - getattr(exact[-1], name)).abs()
+        print(f"stage {name} it{iters}: max {d.max().item():.2e} mean {d.mean().item():.2e} "
+              f"(vs unrounded fp32: max {de.max().item():.2e} mean {de.mean().item():.2e})")
+        assert torch.isfinite(got).all()
+        assert d.max().item() <= lim_max and d.mean().item() <= lim_mean
+
+
+def test_refine_stage_feeds_the_ops():
+    """Five iterations of the stage straight into the fused ops unit on the
+    raw head outputs (refine(..., logits=True)): unit, finite normals."""
+    import brovisionml_b200 as bv
+    from brovisionml_b200.refine_stage import RefineStage, random_params
+
+    B, h, w = 2, 60, 80
+    params = random_params("cuda", seed=3)
+    h0, feat, uv = make_inputs(B, h, w, seed=5)
+    st = RefineStage(params, B, h, w, out_dtype=torch.float16)
+    st.start(h0, feat, uv)
+    outs = [st.step() for _ in range(5)]
+    g = torch.Generator(device="cuda").manual_seed(1)
+    n0 = torch.nn.functional.normalize(torch.randn((B, 3, h, w), device="cuda", generator=g),
+                                       dim=1)
+    fu, cu, fv, cv = 0.8 * w, w / 2 + 0.06, 0.8 * w, h / 2 + 0.06
+    res = bv.refine(n0.half(), [o.prob for o in outs], [o.xy for o in outs],
+                    [o.angle for o in outs], outs[-1].up_mask, fu, cu, fv, cv, logits=True)
+    torch.cuda.synchronize()
+    st.check_pipeline()
+    r = res.float()
+    assert torch.isfinite(r).all()
+    assert (r.norm(dim=1) - 1).abs().max().item() <= 2e-3
