@@ -277,6 +277,118 @@ def reference_arm(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+def stage_flops_per_px(iters: int) -> float:
+    """Useful FLOPs per grid pixel of the ConvGRU + heads (unpadded channels):
+    convz, convr, convq 5x5 over 130 -> 64; per head 3x3 66 -> 128, 1x1
+    128 -> 128, 1x1 128 -> out (25, 50, 25, 576)."""
+    gru = 2 * (3 * 64) * 130 * 25
+    heads = 4 * (2 * 128 * 66 * 9 + 2 * 128 * 128) + 2 * 128 * (25 + 50 + 25 + 576)
+    return float(iters * (gru + heads))
+
+
+def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
+    """--stage: a step is the whole refinement of B frames -- `iters`
+    iterations of ConvGRU + heads (brovisionml_b200.refine_stage) and the
+    fused ops on their raw outputs (refine(..., logits=True))."""
+    import torch
+
+    import brovisionml_b200 as bv
+    from brovisionml_b200.refine_stage import RefineStage, StageOutputs, random_params
+
+    B, H, W, I = cfg["B"], cfg["H"], cfg["W"], cfg["iters"]
+    h, w = H // 8, W // 8
+    dt = torch.float16 if cfg["f16"] else torch.float32
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    h0 = torch.tanh(torch.randn((B, 64, h, w), device=device, generator=g))
+    feat = torch.relu(torch.randn((B, 64, h, w), device=device, generator=g))
+    fx = 0.8 * W
+    fu, cu, fv, cv = fx * w / W, (W / 2 + 0.5) * w / W, fx * h / H, (H / 2 + 0.5) * h / H
+    ys, xs = torch.meshgrid(torch.arange(h, device=device), torch.arange(w, device=device),
+                            indexing="ij")
+    uv = torch.stack([((xs + 0.5) - cu) / fu, ((ys + 0.5) - cv) / fv]).float()
+    n0 = torch.nn.functional.normalize(torch.randn((B, 3, h, w), device=device, generator=g),
+                                       dim=1).to(dt)
+    st = RefineStage(random_params(device, seed=7), B, h, w, device=device, out_dtype=dt)
+    mk = lambda c: torch.empty((B, c, h, w), device=device, dtype=dt)  # noqa: E731
+    outs = [StageOutputs(mk(25), mk(50), mk(25), mk(576)) for _ in range(I)]
+    res = torch.empty((B, 3, H, W), device=device, dtype=dt)
+    ws = torch.empty(bv.refine_workspace_bytes(B, h, w), device=device, dtype=torch.uint8)
+    stream = torch.cuda.Stream(device)
+
+    def stage():
+        st.start(h0, feat, uv)
+        for i in range(I):
+            st.step(outs[i])
+
+    def ops():
+        bv.refine(n0, [o.prob for o in outs], [o.xy for o in outs], [o.angle for o in outs],
+                  outs[-1].up_mask, fu, cu, fv, cv, out=res, workspace=ws, logits=True)
+
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            stage()
+            ops()
+        stream.synchronize()
+        st.check_pipeline()
+        barrier()
+        torch.cuda.synchronize()
+        uuid = None
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            pass
+        marks = [[ev(), ev(), ev()] for _ in range(args.steps)]
+        with ClockSampler(device.index, uuid) as clk:
+            for k in range(args.steps):
+                marks[k][0].record(stream)
+                stage()
+                marks[k][1].record(stream)
+                ops()
+                marks[k][2].record(stream)
+            stream.synchronize()
+        barrier()
+        st.check_pipeline()
+    step_ms = max_over_ranks(sum(m[0].elapsed_time(m[2]) for m in marks) / args.steps)
+    stage_ms = max_over_ranks(sum(m[0].elapsed_time(m[1]) for m in marks) / args.steps)
+    ops_ms = max_over_ranks(sum(m[1].elapsed_time(m[2]) for m in marks) / args.steps)
+    flops = stage_flops_per_px(I) * B * h * w
+    tflops = flops / (stage_ms * 1e-3) / 1e12
+    peak = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops_sustained"])
+        peak_src = "measured sustained (MEASURED_PEAKS.json bf16_tflops_sustained)"
+    except Exception:
+        peak, peak_src = 1400.0, "fallback sustained 1.4 PFLOP/s"
+    line = {
+        "metric": "Mpixel/s of the DSINE refinement (ConvGRU + heads + refine ops)",
+        "value": round(world * B * H * W / (step_ms * 1e-3) / 1e6, 1), "unit": "Mpixel/s",
+        "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": round(step_ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 (tensor cores, fp32 accumulate) + f32 ops",
+        "storage": "f16" if cfg["f16"] else "f32",
+        "data": "synthetic (random weights of the reference's shapes, seeded inputs)",
+        "config": workload_config(args, cfg, {"stage": "ConvGRU 5x5 130->64 x3, 4 heads "
+                                              "(3x3 66->128, 1x1 128->128, 1x1 128->out)"}),
+        "gpu_launches": args.steps * (11 * I + I + 1),
+        "stage": {"ms": round(stage_ms, 3), "tflops_useful": round(tflops, 1),
+                  "flops_per_step": flops},
+        "ops": {"ms": round(ops_ms, 3)},
+        "roofline": {"bound": "tensor", "kernel": "conv_tc (refine stage)",
+                     "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(tflops / peak, 4), "peak_source": peak_src,
+                     "traffic": None},
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def metric_name():
     return "Mpixel/s of DSINE refine ops (5 iters + upsample)"
 
@@ -308,11 +420,15 @@ def main():
     ap.add_argument("--frames", type=int, default=0, help="override frames per GPU")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--stage", action="store_true",
+                    help="time the whole learned refinement: ConvGRU + heads on the tensor "
+                         "cores (random weights of the reference's shapes), then the ops on "
+                         "their raw outputs (device timing only)")
     ap.add_argument("--logits", action="store_true",
                     help="raw head outputs for prob / angle, activated on load (device "
                          "timing only)")
     args = ap.parse_args()
-    if args.logits:
+    if args.logits or args.stage:
         args.no_e2e = args.no_cpu = True
     args.steps = max(1, args.steps)
     cfg = dict(CONFIGS[args.config])
@@ -354,6 +470,8 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    if args.stage:
+        return stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks)
     inp = make_device_inputs(cfg, 1000 + rank, device, torch, logits=args.logits)
     h, w, B, P, I = inp["h"], inp["w"], cfg["B"], cfg["ps"] ** 2, cfg["iters"]
     s = 2 if cfg["f16"] else 4
