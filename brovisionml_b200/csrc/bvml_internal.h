@@ -42,7 +42,7 @@ struct UpsampleLaunch {
 };
 cudaError_t launch_upsample(const UpsampleLaunch& L, cudaStream_t s);
 
-enum class ConvEpi : int { NHWC = 0, PLANAR16 = 1, PLANAR32 = 2, GRU_ZR = 3, GRU_Q = 4 };
+enum class ConvEpi : int { NHWC = 0, PLANAR16 = 1, PLANAR32 = 2, GRU_ZR = 3, GRU_Q = 4, NHWC32 = 5 };
 
 struct ConvLaunch {
     const void* x;       // (B,H,W,x_c) bf16; channels [cin_off, cin_off + cin_pad) are read
@@ -51,8 +51,8 @@ struct ConvLaunch {
     int* err;            // device int: nonzero if a pipeline wait gave up
     int B, H, W, x_c, cin_off, cin_pad, cout, cout_pad, ks;
     ConvEpi epi;
-    int act;             // NHWC: 0 none, 1 ReLU, 2 sigmoid, 3 tanh
-    void* y;             // NHWC: (B,H,W,out_c) bf16 written at out_off; PLANAR: (B,cout,H,W)
+    int act;             // NHWC, NHWC32: 0 none, 1 ReLU, 2 sigmoid, 3 tanh
+    void* y;             // NHWC (bf16) / NHWC32 (fp32): (B,H,W,out_c) at out_off; PLANAR: (B,cout,H,W)
     int out_c, out_off;
     float* h32;          // GRU: fp32 hidden state (B,H,W,64)
     void* z;             // GRU: gate z (B,H,W,64) bf16
@@ -62,6 +62,9 @@ struct ConvLaunch {
     int hx_c;
     void* hin;           // GRU_Q: ... and of (B,H,W,hin_c) when not null
     int hin_c;
+    const float* add;    // optional per-pixel addend (B or 1,H,W,add_c) fp32, channels [0,cout)
+    int add_c;
+    int add_shared;      // nonzero: one frame of addends shared by all B frames
 };
 cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s);
 

@@ -354,7 +354,7 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
                              int ks, const bvml_conv_epilogue* epi, int* err, void* stream) {
     auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     if (!(ks == 1 || ks == 3 || ks == 5)) return einval("conv2d: kernel size must be 1, 3 or 5");
-    if (!epi || epi->mode < 0 || epi->mode > 4) return einval("conv2d: unknown epilogue");
+    if (!epi || epi->mode < 0 || epi->mode > 5) return einval("conv2d: unknown epilogue");
     if (B < 0 || H < 0 || W < 0 || x_c <= 0 || x_c % 8 != 0 || cin_off < 0 ||
         cin_off % 64 != 0 || cin_pad <= 0 || cin_pad % 64 != 0 || cin_off + cin_pad > x_c + 63 ||
         cout <= 0 || cout_pad % 64 != 0 || cout > cout_pad)
@@ -390,12 +390,24 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
     L.hx_c = epi->hx_c;
     L.hin = epi->hin;
     L.hin_c = epi->hin_c;
+    L.add = epi->add;
+    L.add_c = epi->add_c;
+    L.add_shared = epi->add_shared;
+    if (epi->add && (!a16(epi->add) || epi->add_c % 4 || epi->add_c < cout))
+        return einval("conv2d: addend must be 16-byte aligned with add_c a multiple of 4, >= cout");
     switch (epi->mode) {
         case BVML_EPI_NHWC:
             if (epi->act < 0 || epi->act > 3) return einval("conv2d: unknown activation");
             if (!epi->out || !a16(epi->out) || epi->out_c % 8 || epi->out_off % 8 ||
                 epi->out_off + cout_pad > epi->out_c)
                 return einval("conv2d: bad NHWC output");
+            break;
+        case BVML_EPI_NHWC_F32:
+            if (epi->act < 0 || epi->act > 1)
+                return einval("conv2d: fp32 NHWC output takes no activation or ReLU");
+            if (!epi->out || !a16(epi->out) || epi->out_c % 4 || epi->out_off % 4 ||
+                epi->out_off + cout_pad > epi->out_c)
+                return einval("conv2d: bad NHWC fp32 output");
             break;
         case BVML_EPI_PLANAR_F16:
         case BVML_EPI_PLANAR_F32:

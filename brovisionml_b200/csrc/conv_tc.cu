@@ -62,6 +62,14 @@ struct ConvArgs {
     int hx_c;
     __nv_bfloat16* hin;
     int hin_c;
+    // optional per-pixel addend: add[f * add_fs + (y * W + x) * add_c + c]
+    const float* add;
+    long add_fs;  // frame stride in floats (0: one frame shared by all)
+    int add_c;
+    // shared-memory plan (see below)
+    int a_bytes, b_bytes;  // one A entry (halo tile), one B entry (one tap's weights)
+    int s_a, s_b;          // ring depths
+    int off_b, off_out, off_bar;
 };
 
 template <int ACT>
@@ -72,9 +80,42 @@ __device__ __forceinline__ float activate(float v) {
     else return v;
 }
 
+// The addend row of pixel (px, py) of frame b for channels cb.., or null.
+__device__ __forceinline__ const float* addend_at(const ConvArgs& a, int b, int px, int py,
+                                                  int cb) {
+    return a.add ? a.add + b * a.add_fs + ((long)py * a.W + px) * a.add_c + cb : nullptr;
+}
+
+// f[i] = accumulator + bias (+ addend) for channels cb + i < cout, else 0.
+__device__ __forceinline__ void pre_activation(const ConvArgs& a, const float* ad, int cb,
+                                               const uint32_t (&v)[32], float (&f)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        f[i] = cb + i < a.cout ? __uint_as_float(v[i]) + a.bias[cb + i] : 0.0f;
+    if (ad) {
+        if (cb + 32 <= a.add_c) {
+            const float4* a4 = reinterpret_cast<const float4*>(ad);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 t = a4[q];
+                f[4 * q + 0] += cb + 4 * q + 0 < a.cout ? t.x : 0.0f;
+                f[4 * q + 1] += cb + 4 * q + 1 < a.cout ? t.y : 0.0f;
+                f[4 * q + 2] += cb + 4 * q + 2 < a.cout ? t.z : 0.0f;
+                f[4 * q + 3] += cb + 4 * q + 3 < a.cout ? t.w : 0.0f;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (cb + i < a.cout) f[i] += ad[i];
+        }
+    }
+}
+
 // Epilogue of one thread's pixel for 32 consecutive output channels
-// cb .. cb+31 (accumulators + bias in v). Modes (ConvEpi in bvml_internal.h):
+// cb .. cb+31 (accumulators in v, plus bias and the optional addend at ad).
+// Modes (ConvEpi in bvml_internal.h):
 //  NHWC      act(v) as bf16 at out[pix * out_c + out_off + c], zeros past cout;
+//  NHWC32    the same in fp32;
 //  (PLANAR16/32: planar_chunk, through a shared-memory transpose)
 //  GRU_ZR    c < 64: z = sigmoid(v) -> z[pix * 64 + c];
 //            64 <= c < 128: r = sigmoid(v) -> rh[pix * rh_c + c - 64] = r * h32;
@@ -85,10 +126,20 @@ template <int EPI, int ACT>
 __device__ __forceinline__ void epilogue32(const ConvArgs& a, long pix, int b, int px, int py,
                                            int cb, const uint32_t (&v)[32]) {
     float f[32];
+    pre_activation(a, addend_at(a, b, px, py, cb), cb, v, f);
+    if constexpr (EPI == (int)ConvEpi::NHWC32) {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + pix * a.out_c +
+                                                a.out_off + cb);
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-        f[i] = cb + i < a.cout ? __uint_as_float(v[i]) + a.bias[cb + i] : 0.0f;
-    if constexpr (EPI == (int)ConvEpi::NHWC) {
+        for (int q = 0; q < 8; ++q) {
+            float4 o;
+            o.x = cb + 4 * q + 0 < a.cout ? activate<ACT>(f[4 * q + 0]) : 0.0f;
+            o.y = cb + 4 * q + 1 < a.cout ? activate<ACT>(f[4 * q + 1]) : 0.0f;
+            o.z = cb + 4 * q + 2 < a.cout ? activate<ACT>(f[4 * q + 2]) : 0.0f;
+            o.w = cb + 4 * q + 3 < a.cout ? activate<ACT>(f[4 * q + 3]) : 0.0f;
+            dst[q] = o;
+        }
+    } else if constexpr (EPI == (int)ConvEpi::NHWC) {
         alignas(16) __nv_bfloat16 o[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i)
@@ -152,26 +203,30 @@ __device__ __forceinline__ void epilogue32(const ConvArgs& a, long pix, int b, i
     }
 }
 
+// Shared-memory plan (byte offsets from the 1024-aligned base), decided on
+// the host per launch:
+//  * A ring, s_a entries of a_bytes: one halo tile each -- tw pixels x
+//    (MT * th + ks - 1) image rows x 64 channels, 128-byte swizzled. Rows are
+//    stored image row by image row, so the operand of sub-tile m and filter
+//    row ky starts (m * th + ky) image rows in: tw * 128 bytes per image row,
+//    a multiple of the 1024-byte swizzle atom (tw >= 8), and every filter
+//    row reuses the same copy;
+//  * B ring, s_b entries of N x 64 weights (one tap), or, for BRES, the
+//    layer's whole 1x1 weights resident (chunks entries, loaded once);
+//  * planar staging (PLANAR epilogues), then the barriers.
+constexpr int kMaxStages = 8;
+constexpr int kBarBytes = 512;
+constexpr int kSmemLimit = 227 * 1024;
+
 // BRES (1x1 convolutions with at most kBResChunks input chunks): the CTA's
 // weights stay resident in shared memory, loaded once, and the ring carries
 // only pixel tiles; each CTA then keeps one output-channel tile.
 constexpr int kBResChunks = 2;
 
-template <int N, int S, int EPI, bool BRES = false>
-struct ConvCfg {
-    static constexpr int kABytes = kTM * kKC * 2;
-    static constexpr int kBBytes = N * kKC * 2;
-    static constexpr int kBRes = BRES ? kBResChunks * kBBytes : 0;  // resident weights first
-    static constexpr int kStage = BRES ? kABytes : kABytes + kBBytes;
-    static constexpr bool kPlanar = EPI == (int)ConvEpi::PLANAR16 || EPI == (int)ConvEpi::PLANAR32;
-    static constexpr int kOutElem = EPI == (int)ConvEpi::PLANAR16 ? 2 : 4;
-    // planar outputs: per epilogue warp two 32-channel x 32-pixel staging buffers
-    static constexpr int kStageWarpBytes = 32 * 32 * kOutElem;
-    static constexpr int kStageOutOff = kBRes + S * kStage;
-    static constexpr int kStageOutBytes = kPlanar ? kEpiWarps * 2 * kStageWarpBytes : 0;
-    static constexpr int kBarOff = kStageOutOff + kStageOutBytes;  // mbarriers last
-    static constexpr int kSmem = kBarOff + 256 + 1024;         // + barriers, alignment slack
-};
+// planar outputs: per epilogue warp two 32-channel x 32-pixel staging buffers
+__host__ __device__ constexpr int stage_warp_bytes(int epi) {
+    return 32 * 32 * (epi == (int)ConvEpi::PLANAR16 ? 2 : 4);
+}
 
 // Planar output of one 32-channel chunk (channels cb .. cb+31) of one
 // epilogue warp's 32 pixels: every lane puts its pixel's values into the
@@ -184,14 +239,15 @@ template <typename TO>
 __device__ __forceinline__ void planar_chunk_tma(const ConvArgs& a, const CUtensorMap* map_o,
                                                  TO* stg, uint32_t stg_addr, int lane,
                                                  int px0, int py0, int b, int cb,
-                                                 const uint32_t (&v)[32]) {
+                                                 const float* ad, const uint32_t (&v)[32]) {
+    float f[32];
+    pre_activation(a, ad, cb, v, f);
     if (lane == 0) tc::bulk_wait_read<1>();  // this buffer's previous store has read it
     __syncwarp();
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-        const float f = cb + i < a.cout ? __uint_as_float(v[i]) + a.bias[cb + i] : 0.0f;
-        if constexpr (sizeof(TO) == 2) stg[i * 32 + lane] = __float2half_rn(f);
-        else stg[i * 32 + lane] = f;
+        if constexpr (sizeof(TO) == 2) stg[i * 32 + lane] = __float2half_rn(f[i]);
+        else stg[i * 32 + lane] = f[i];
     }
     tc::fence_proxy_async_smem();
     __syncwarp();
@@ -202,31 +258,37 @@ __device__ __forceinline__ void planar_chunk_tma(const ConvArgs& a, const CUtens
 }
 
 // Persistent: CTA c computes tiles c, c + G, c + 2G, ... (G CTAs, one per
-// SM). The TMA / MMA ring runs on across tiles; the accumulator is double
-// buffered in TMEM (2 x N columns), so the epilogue warps drain tile i while
-// the MMA lane accumulates tile i + 1.
-template <int N, int S, int EPI, int ACT, bool BRES>
+// SM). A tile is MT sub-tiles of 128 pixels (tw x th, stacked vertically)
+// by N output channels; each sub-tile has its own TMEM accumulator, so one
+// weight tile feeds MT MMAs. The TMA / MMA rings run on across tiles; the
+// accumulators are double buffered in TMEM (2 x MT x N columns), so the
+// epilogue warps drain tile i while the MMA lane accumulates tile i + 1.
+template <int N, int MT, int EPI, int ACT, bool BRES>
 __global__ void __launch_bounds__(kConvThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                const __grid_constant__ CUtensorMap map_o, const ConvArgs a) {
-    using C = ConvCfg<N, S, EPI, BRES>;
+    constexpr bool kPlanar = EPI == (int)ConvEpi::PLANAR16 || EPI == (int)ConvEpi::PLANAR32;
+    constexpr int kCols = 2 * MT * N;  // TMEM columns: two accumulator sets
+    static_assert(kCols <= 512 && (kCols & (kCols - 1)) == 0, "TMEM allocation");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const uint32_t sbase = tc::smem_u32(smem);
-    const uint32_t bar_full = sbase + C::kBarOff;        // S barriers: stage loaded
-    const uint32_t bar_empty = bar_full + 8 * S;         // S barriers: stage consumed
-    const uint32_t bar_acc_full = bar_empty + 8 * S;     // 2 barriers: accumulator ready
-    const uint32_t bar_acc_empty = bar_acc_full + 16;    // 2 barriers: accumulator drained
-    const uint32_t bar_end = bar_acc_empty + 16;         // 1 barrier: every MMA complete
-    const uint32_t bar_bres = bar_end + 8;               // 1 barrier: resident weights loaded
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOff + 16 * S + 48);
-    int* abort_flag = reinterpret_cast<int*>(smem + C::kBarOff + 16 * S + 56);
-    const uint32_t ring = sbase + C::kBRes;              // the A (and B) stages
+    const uint32_t bars = sbase + a.off_bar;
+    const uint32_t bar_full_a = bars;                 // kMaxStages: A entry loaded
+    const uint32_t bar_empty_a = bars + 64;           // kMaxStages: A entry consumed
+    const uint32_t bar_full_b = bars + 128;           // kMaxStages: B entry loaded
+    const uint32_t bar_empty_b = bars + 192;          // kMaxStages: B entry consumed
+    const uint32_t bar_acc_full = bars + 256;         // 2: accumulator set ready
+    const uint32_t bar_acc_empty = bars + 272;        // 2: accumulator set drained
+    const uint32_t bar_end = bars + 288;              // every MMA complete
+    const uint32_t bar_bres = bars + 296;             // resident weights loaded
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + a.off_bar + 304);
+    int* abort_flag = reinterpret_cast<int*>(smem + a.off_bar + 308);
+    const uint32_t ring_b = sbase + a.off_b;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int chunks = a.cin_pad / kKC;
-    const int k_iters = a.ks * a.ks * chunks;
     const int n_nt = (a.cout_pad + N - 1) / N;
     const int n_tiles = a.tiles_x * a.tiles_y * a.B * n_nt;
     // this CTA's tiles: t0, t0 + dt, ... (BRES: one output-channel tile per CTA)
@@ -245,13 +307,15 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const int ty = r % a.tiles_y;
         b = r / a.tiles_y;
         x0 = tx * a.tw;
-        y0 = ty * a.th;
+        y0 = ty * a.th * MT;
     };
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
-            tc::mbar_init(bar_full + 8 * s, 1);
-            tc::mbar_init(bar_empty + 8 * s, 1);
+        for (int s = 0; s < kMaxStages; ++s) {
+            tc::mbar_init(bar_full_a + 8 * s, 1);
+            tc::mbar_init(bar_empty_a + 8 * s, 1);
+            tc::mbar_init(bar_full_b + 8 * s, 1);
+            tc::mbar_init(bar_empty_b + 8 * s, 1);
         }
         for (int q = 0; q < 2; ++q) {
             tc::mbar_init(bar_acc_full + 8 * q, 1);
@@ -265,7 +329,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         tc::tma_prefetch_desc(&map_b);
     }
     if (warp == 1) {
-        tc::tmem_alloc(tc::smem_u32(tmem_slot), 2 * N);
+        tc::tmem_alloc(tc::smem_u32(tmem_slot), kCols);
         tc::tmem_relinquish();
     }
     tc::tc_fence_before();
@@ -281,63 +345,121 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 
     if (warp == 0 && lane == 0) {
         // ---------------------------------------------------------- producer
-        int g = 0;  // stages issued by this CTA
+        int ga = 0, gb = 0;  // A and B entries issued by this CTA
         if constexpr (BRES) {  // the CTA's weights, once
-            tc::mbar_expect_tx(bar_bres, chunks * C::kBBytes);
+            tc::mbar_expect_tx(bar_bres, chunks * a.b_bytes);
             for (int ch = 0; ch < chunks; ++ch)
-                tc::tma_load_3d(sbase + ch * C::kBBytes, &map_b, bar_bres, ch * kKC, my_nt * N, 0);
+                tc::tma_load_3d(ring_b + ch * a.b_bytes, &map_b, bar_bres, ch * kKC, my_nt * N, 0);
         }
-        for (int t = t0; t < t_end && !aborted(); t += dt) {
+        bool ok = true;
+        for (int t = t0; ok && t < t_end && !aborted(); t += dt) {
             int b, x0, y0, n0;
             tile_of(t, b, x0, y0, n0);
-            for (int it = 0; it < k_iters; ++it, ++g) {
-                const int s = g % S, j = g / S;
-                if (j > 0 && !tc::mbar_wait(bar_empty + 8 * s, (j - 1) & 1, kWaitLimit)) {
-                    fail(1);
-                    break;
+            for (int ch = 0; ok && ch < chunks; ++ch) {
+                for (int kx = 0; ok && kx < a.ks; ++kx) {
+                    const int s = ga % a.s_a, j = ga / a.s_a;
+                    if (j > 0 && !tc::mbar_wait(bar_empty_a + 8 * s, (j - 1) & 1, kWaitLimit)) {
+                        fail(1);
+                        ok = false;
+                        break;
+                    }
+                    if (aborted()) {
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_expect_tx(bar_full_a + 8 * s, a.a_bytes);
+                    tc::tma_load_4d(sbase + s * a.a_bytes, &map_a, bar_full_a + 8 * s,
+                                    a.cin_off + ch * kKC, x0 + kx - a.pad, y0 - a.pad, b);
+                    ++ga;
+                    if constexpr (!BRES) {
+                        for (int ky = 0; ky < a.ks; ++ky, ++gb) {
+                            const int q = gb % a.s_b, jb = gb / a.s_b;
+                            if (jb > 0 &&
+                                !tc::mbar_wait(bar_empty_b + 8 * q, (jb - 1) & 1, kWaitLimit)) {
+                                fail(1);
+                                ok = false;
+                                break;
+                            }
+                            tc::mbar_expect_tx(bar_full_b + 8 * q, a.b_bytes);
+                            tc::tma_load_3d(ring_b + q * a.b_bytes, &map_b, bar_full_b + 8 * q,
+                                            ch * kKC, n0, ky * a.ks + kx);
+                        }
+                    }
                 }
-                if (aborted()) break;
-                const int tap = it / chunks, ch = it - tap * chunks;
-                const int ky = tap / a.ks, kx = tap - ky * a.ks;
-                const uint32_t sa = ring + s * C::kStage, sb = sa + C::kABytes;
-                tc::mbar_expect_tx(bar_full + 8 * s, C::kStage);
-                tc::tma_load_4d(sa, &map_a, bar_full + 8 * s, a.cin_off + ch * kKC,
-                                x0 + kx - a.pad, y0 + ky - a.pad, b);
-                if constexpr (!BRES) tc::tma_load_3d(sb, &map_b, bar_full + 8 * s, ch * kKC, n0, tap);
             }
         }
         // no copy may still be landing when the CTA exits
-        for (int q = g - S > 0 ? g - S : 0; q < g; ++q)
-            if (!tc::mbar_wait(bar_full + 8 * (q % S), (q / S) & 1, kWaitLimit)) fail(2);
+        for (int q = ga - a.s_a > 0 ? ga - a.s_a : 0; q < ga; ++q)
+            if (!tc::mbar_wait(bar_full_a + 8 * (q % a.s_a), (q / a.s_a) & 1, kWaitLimit)) fail(2);
+        if constexpr (!BRES) {
+            for (int q = gb - a.s_b > 0 ? gb - a.s_b : 0; q < gb; ++q)
+                if (!tc::mbar_wait(bar_full_b + 8 * (q % a.s_b), (q / a.s_b) & 1, kWaitLimit))
+                    fail(2);
+        }
         if (BRES && !tc::mbar_wait(bar_bres, 0, kWaitLimit)) fail(2);
     } else if (warp == 1 && lane == 0) {
         // --------------------------------------------------------------- MMA
         constexpr uint32_t idesc = tc::idesc_bf16_f32(kTM, N);
-        int g = 0, tl = 0;
-        if (BRES && t0 < t_end && !tc::mbar_wait(bar_bres, 0, kWaitLimit)) fail(7);
-        for (int t = t0; t < t_end && !aborted(); t += dt, ++tl) {
+        const uint32_t row_bytes = (uint32_t)a.tw * 128;  // one image row of an A entry
+        int ga = 0, gb = 0, tl = 0;
+        bool ok = true;
+        if (BRES && t0 < t_end && !tc::mbar_wait(bar_bres, 0, kWaitLimit)) {
+            fail(7);
+            ok = false;
+        }
+        for (int t = t0; ok && t < t_end && !aborted(); t += dt, ++tl) {
             const int buf = tl & 1, u = tl >> 1;
             if (u > 0 && !tc::mbar_wait(bar_acc_empty + 8 * buf, (u - 1) & 1, kWaitLimit)) {
                 fail(3);
                 break;
             }
             tc::tc_fence_after();
-            const uint32_t acc = tmem + buf * N;
-            bool ok = true;
-            for (int it = 0; it < k_iters; ++it, ++g) {
-                const int s = g % S, j = g / S;
-                if (!tc::mbar_wait(bar_full + 8 * s, j & 1, kWaitLimit) || aborted()) {
-                    ok = false;
-                    break;
-                }
-                tc::tc_fence_after();
-                const uint32_t sa = ring + s * C::kStage;
-                const uint32_t sb = BRES ? sbase + it * C::kBBytes : sa + C::kABytes;
-                const uint64_t da = tc::umma_desc_k_sw128(sa), db = tc::umma_desc_k_sw128(sb);
+            const uint32_t acc = tmem + buf * (MT * N);
+            bool first = true;
+            for (int ch = 0; ok && ch < chunks; ++ch) {
+                for (int kx = 0; ok && kx < a.ks; ++kx) {
+                    const int s = ga % a.s_a, j = ga / a.s_a;
+                    if (!tc::mbar_wait(bar_full_a + 8 * s, j & 1, kWaitLimit) || aborted()) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint32_t sa = sbase + s * a.a_bytes;
+                    for (int ky = 0; ky < a.ks; ++ky) {
+                        int q = 0;
+                        uint32_t sb;
+                        if constexpr (BRES) {
+                            sb = ring_b + ch * a.b_bytes;  // ks == 1
+                        } else {
+                            q = gb % a.s_b;
+                            if (!tc::mbar_wait(bar_full_b + 8 * q, (gb / a.s_b) & 1, kWaitLimit) ||
+                                aborted()) {
+                                ok = false;
+                                break;
+                            }
+                            tc::tc_fence_after();
+                            sb = ring_b + q * a.b_bytes;
+                        }
+                        const uint64_t db = tc::umma_desc_k_sw128(sb);
 #pragma unroll
-                for (int k = 0; k < kKC / 16; ++k)  // K = 16 per MMA: 32 B = 2 descriptor units
-                    tc::umma_bf16(acc, da + 2 * k, db + 2 * k, idesc, it > 0 || k > 0);
-                tc::umma_commit(bar_empty + 8 * s);
+                        for (int m = 0; m < MT; ++m) {
+                            const uint64_t da =
+                                tc::umma_desc_k_sw128(sa + (uint32_t)(m * a.th + ky) * row_bytes);
+#pragma unroll
+                            for (int k = 0; k < kKC / 16; ++k)  // K = 16 per MMA: 2 descriptor units
+                                tc::umma_bf16(acc + m * N, da + 2 * k, db + 2 * k, idesc,
+                                              !first || k > 0);
+                        }
+                        first = false;
+                        if constexpr (!BRES) {
+                            tc::umma_commit(bar_empty_b + 8 * q);
+                            ++gb;
+                        }
+                    }
+                    if (!ok) break;
+                    tc::umma_commit(bar_empty_a + 8 * s);
+                    ++ga;
+                }
             }
             if (!ok) {
                 fail(4);
@@ -349,9 +471,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         if (!tc::mbar_wait(bar_end, 0, kWaitLimit)) fail(5);
     } else if (warp >= 2) {
         // ---------------------------------------------------------- epilogue
+        // MT = 1: two warps per TMEM lane quarter, each half of the columns;
+        // MT >= 2: warp group g (warps 2-5, 6-9) drains sub-tiles g, g + 2, ...
         const int wq = warp & 3;              // the TMEM lane quarter this warp may read
-        const int row = wq * 32 + lane;       // pixel index in the tile
-        const int half = (warp - 2) >> 2;     // which half of the N columns it drains
+        const int row = wq * 32 + lane;       // pixel index in the sub-tile
+        const int grp = (warp - 2) >> 2;
+        const int c_lo = MT == 1 ? grp * (N / 2) : 0;
+        const int c_hi = MT == 1 ? c_lo + N / 2 : N;
         int pcount = 0;                       // planar chunks stored by this warp
         int tl = 0;
         for (int t = t0; t < t_end; t += dt, ++tl) {
@@ -362,48 +488,53 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             tc::tc_fence_after();
             int b, x0, y0, n0;
             tile_of(t, b, x0, y0, n0);
-            const int px = x0 + row % a.tw, py = y0 + row / a.tw;
-            const bool in = px < a.W && py < a.H;
-            const long pix = ((long)b * a.H + py) * a.W + px;
-            const uint32_t acc = tmem + buf * N + ((uint32_t)(wq * 32) << 16);
 #pragma unroll 1
-            for (int c0 = half * (N / 2); c0 < (half + 1) * (N / 2); c0 += 32) {
-                uint32_t v[32];
-                tc::tmem_ld_32cols(acc + c0, v);
-                tc::tmem_ld_wait();
-                const int cb = n0 + c0;
-                if constexpr (C::kPlanar) {
-                    if (cb >= a.cout) continue;  // the same for the whole warp
-                    // this warp's 32 pixels: tile rows [wq * 32, wq * 32 + 32) as a
-                    // pw x ph box (pw = min(tw, 32))
-                    const int px0 = x0 + (wq * 32) % a.tw, py0 = y0 + (wq * 32) / a.tw;
-                    if (px0 >= a.W || py0 >= a.H) continue;  // the whole box is off the frame
-                    const int slot = (warp - 2) * 2 + (pcount & 1);
-                    uint8_t* stg = smem + C::kStageOutOff + slot * C::kStageWarpBytes;
-                    const uint32_t stg_addr = sbase + C::kStageOutOff + slot * C::kStageWarpBytes;
-                    if constexpr (EPI == (int)ConvEpi::PLANAR16)
-                        planar_chunk_tma<__half>(a, &map_o, reinterpret_cast<__half*>(stg),
-                                                 stg_addr, lane, px0, py0, b, cb, v);
-                    else
-                        planar_chunk_tma<float>(a, &map_o, reinterpret_cast<float*>(stg),
-                                                stg_addr, lane, px0, py0, b, cb, v);
-                    ++pcount;
-                } else {
-                    if (!in || cb >= a.cout_pad) continue;
-                    epilogue32<EPI, ACT>(a, pix, b, px, py, cb, v);
+            for (int m = MT == 1 ? 0 : grp; m < MT; m += 2) {
+                const int ys = y0 + m * a.th;  // the sub-tile's first image row
+                const int px = x0 + row % a.tw, py = ys + row / a.tw;
+                const bool in = px < a.W && py < a.H;
+                const long pix = ((long)b * a.H + py) * a.W + px;
+                const uint32_t acc = tmem + buf * (MT * N) + m * N + ((uint32_t)(wq * 32) << 16);
+#pragma unroll 1
+                for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
+                    uint32_t v[32];
+                    tc::tmem_ld_32cols(acc + c0, v);
+                    tc::tmem_ld_wait();
+                    const int cb = n0 + c0;
+                    if constexpr (kPlanar) {
+                        if (cb >= a.cout) continue;  // the same for the whole warp
+                        const float* ad = in ? addend_at(a, b, px, py, cb) : nullptr;
+                        // this warp's 32 pixels: sub-tile rows [wq * 32, wq * 32 + 32)
+                        // as a pw x ph box (pw = min(tw, 32))
+                        const int px0 = x0 + (wq * 32) % a.tw, py0 = ys + (wq * 32) / a.tw;
+                        if (px0 >= a.W || py0 >= a.H) continue;  // the whole box is off the frame
+                        const int slot = (warp - 2) * 2 + (pcount & 1);
+                        uint8_t* stg = smem + a.off_out + slot * stage_warp_bytes(EPI);
+                        const uint32_t stg_addr = sbase + a.off_out + slot * stage_warp_bytes(EPI);
+                        if constexpr (EPI == (int)ConvEpi::PLANAR16)
+                            planar_chunk_tma<__half>(a, &map_o, reinterpret_cast<__half*>(stg),
+                                                     stg_addr, lane, px0, py0, b, cb, ad, v);
+                        else
+                            planar_chunk_tma<float>(a, &map_o, reinterpret_cast<float*>(stg),
+                                                    stg_addr, lane, px0, py0, b, cb, ad, v);
+                        ++pcount;
+                    } else {
+                        if (!in || cb >= a.cout_pad) continue;
+                        epilogue32<EPI, ACT>(a, pix, b, px, py, cb, v);
+                    }
                 }
             }
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(bar_acc_empty + 8 * buf);
         }
-        if (C::kPlanar && lane == 0) tc::bulk_wait_all();  // stores complete before exit
+        if (kPlanar && lane == 0) tc::bulk_wait_all();  // stores complete before exit
     }
     tc::tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, 2 * N);
+        tc::tmem_dealloc(tmem, kCols);
     }
 }
 
@@ -434,12 +565,10 @@ bool encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int N, int S, int EPI, int ACT, bool BRES>
+template <int N, int MT, int EPI, int ACT, bool BRES>
 cudaError_t launch_n(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
-                     const ConvArgs& a, cudaStream_t s) {
-    auto kern = conv_tc_kernel<N, S, EPI, ACT, BRES>;
-    constexpr int smem = ConvCfg<N, S, EPI, BRES>::kSmem;
-    static_assert(smem <= 227 * 1024, "shared memory per CTA");
+                     const ConvArgs& a, int smem, cudaStream_t s) {
+    auto kern = conv_tc_kernel<N, MT, EPI, ACT, BRES>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     const long tiles = (long)a.tiles_x * a.tiles_y * a.B * ((a.cout_pad + N - 1) / N);
@@ -455,21 +584,76 @@ cudaError_t launch_n(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
 }
 
 template <int EPI, int ACT>
-cudaError_t launch_act(int n, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
-                       const ConvArgs& a, cudaStream_t s) {
-    const bool bres = a.ks == 1 && a.cin_pad <= kBResChunks * kKC;
+cudaError_t launch_act(int n, int mt, bool bres, const CUtensorMap& ma, const CUtensorMap& mb,
+                       const CUtensorMap& mo, const ConvArgs& a, int smem, cudaStream_t s) {
     if (bres) {
         switch (n) {
-            case 256: return launch_n<256, 6, EPI, ACT, true>(ma, mb, mo, a, s);
-            case 128: return launch_n<128, 8, EPI, ACT, true>(ma, mb, mo, a, s);
-            default: return launch_n<64, 8, EPI, ACT, true>(ma, mb, mo, a, s);
+            case 256: return launch_n<256, 1, EPI, ACT, true>(ma, mb, mo, a, smem, s);
+            case 128: return launch_n<128, 1, EPI, ACT, true>(ma, mb, mo, a, smem, s);
+            default: return launch_n<64, 1, EPI, ACT, true>(ma, mb, mo, a, smem, s);
         }
     }
-    switch (n) {
-        case 256: return launch_n<256, 3, EPI, ACT, false>(ma, mb, mo, a, s);
-        case 128: return launch_n<128, 5, EPI, ACT, false>(ma, mb, mo, a, s);
-        default: return launch_n<64, 6, EPI, ACT, false>(ma, mb, mo, a, s);
+    if (n == 256) return launch_n<256, 1, EPI, ACT, false>(ma, mb, mo, a, smem, s);
+    if (n == 128) {
+        if (mt == 2) return launch_n<128, 2, EPI, ACT, false>(ma, mb, mo, a, smem, s);
+        return launch_n<128, 1, EPI, ACT, false>(ma, mb, mo, a, smem, s);
     }
+    if (mt == 4) return launch_n<64, 4, EPI, ACT, false>(ma, mb, mo, a, smem, s);
+    if (mt == 2) return launch_n<64, 2, EPI, ACT, false>(ma, mb, mo, a, smem, s);
+    return launch_n<64, 1, EPI, ACT, false>(ma, mb, mo, a, smem, s);
+}
+
+// Tile geometry and shared-memory plan for one launch: sub-tile tw x th
+// (= 128 pixels), MT sub-tiles per CTA tile, ring depths. Returns the dynamic
+// shared-memory size, or 0 if nothing fits.
+int plan_conv(ConvArgs& a, int n, int& mt, bool bres, int out_bytes) {
+    const int budget = kSmemLimit - 1024 - kBarBytes - out_bytes;  // 1024: alignment slack
+    const int b_bytes = n * kKC * 2;
+    for (; mt >= 1; mt /= 2) {
+        // the tw with the fewest computed pixels; for ks > 1 ties go to the
+        // narrower tile (less halo per pixel), and tw = 128 is not used
+        static const int tws[4] = {128, 64, 32, 16};
+        long best = -1;
+        for (int tw : tws) {
+            if (a.ks > 1 && tw == 128) continue;
+            const int th = kTM / tw;
+            const long tiles = (long)((a.W + tw - 1) / tw) * ((a.H + th * mt - 1) / (th * mt));
+            if (best < 0 || tiles < best || (tiles == best && a.ks > 1)) {
+                best = tiles;
+                a.tw = tw;
+                a.th = th;
+            }
+        }
+        a.tiles_x = (a.W + a.tw - 1) / a.tw;
+        a.tiles_y = (a.H + a.th * mt - 1) / (a.th * mt);
+        a.a_bytes = a.tw * (mt * a.th + a.ks - 1) * kKC * 2;
+        a.b_bytes = b_bytes;
+        if (bres) {
+            const int rest = budget - (a.cin_pad / kKC) * b_bytes;
+            a.s_a = rest / a.a_bytes < kMaxStages ? rest / a.a_bytes : kMaxStages;
+            a.s_b = 0;
+            if (a.s_a < 2) continue;
+            a.off_b = a.s_a * a.a_bytes;
+            a.off_out = a.off_b + (a.cin_pad / kKC) * b_bytes;
+        } else if (a.ks == 1) {
+            const int st = budget / (a.a_bytes + b_bytes);
+            a.s_a = a.s_b = st < kMaxStages ? st : kMaxStages;
+            if (a.s_a < 2) continue;
+            a.off_b = a.s_a * a.a_bytes;
+            a.off_out = a.off_b + a.s_b * b_bytes;
+        } else {
+            // a few halo tiles, and as many weight taps as fit (up to 8)
+            a.s_a = 3 * a.a_bytes + kMaxStages * b_bytes <= budget ? 3 : 2;
+            const int sb = (budget - a.s_a * a.a_bytes) / b_bytes;
+            a.s_b = sb < kMaxStages ? sb : kMaxStages;
+            if (a.s_b < 2) continue;
+            a.off_b = a.s_a * a.a_bytes;
+            a.off_out = a.off_b + a.s_b * b_bytes;
+        }
+        a.off_bar = a.off_out + out_bytes;
+        return a.off_bar + kBarBytes + 1024;
+    }
+    return 0;
 }
 
 }  // namespace
@@ -499,32 +683,34 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     a.hx_c = L.hx_c;
     a.hin = static_cast<__nv_bfloat16*>(L.hin);
     a.hin_c = L.hin_c;
-    // pixel tile tw x th (= 128): the shape with the fewest out-of-frame rows
-    static const int tws[4] = {128, 64, 32, 16};
-    long best = -1;
-    for (int tw : tws) {
-        const int th = kTM / tw;
-        const long tiles = (long)((L.W + tw - 1) / tw) * ((L.H + th - 1) / th);
-        if (best < 0 || tiles < best) {
-            best = tiles;
-            a.tw = tw;
-            a.th = th;
-        }
-    }
-    a.tiles_x = (L.W + a.tw - 1) / a.tw;
-    a.tiles_y = (L.H + a.th - 1) / a.th;
-    if ((long)a.tiles_x * a.tiles_y * L.B > 0x7fffffffL) return cudaErrorInvalidConfiguration;
-    // GRU gates need every channel of a pixel in one CTA (z with r, q with z)
+    a.add = L.add;
+    a.add_c = L.add_c;
+    a.add_fs = L.add_shared ? 0 : (long)L.H * L.W * L.add_c;
+    // N: output channels per tile. GRU gates need every channel of a pixel in
+    // one CTA (z with r, q with z). Filters wider than 1x1 with N < 256 use 2
+    // or 4 sub-tiles per CTA tile, so one weight tile feeds 256 or 512 pixels
+    // and the halo tile is shared by more filter rows.
     int n = L.cout_pad >= 256 ? 256 : (L.cout_pad >= 128 ? 128 : 64);
     if (L.epi == ConvEpi::GRU_ZR) n = 128;
     if (L.epi == ConvEpi::GRU_Q) n = 64;
+    int mt = L.ks == 1 || n == 256 ? 1 : (n == 128 ? 2 : 4);
+    const bool bres = L.ks == 1 && L.cin_pad <= kBResChunks * kKC;
+    const bool planar = L.epi == ConvEpi::PLANAR16 || L.epi == ConvEpi::PLANAR32;
+    const int es = L.epi == ConvEpi::PLANAR16 ? 2 : 4;
+    const int out_bytes = planar ? kEpiWarps * 2 * stage_warp_bytes((int)L.epi) : 0;
+    const int smem = plan_conv(a, n, mt, bres, out_bytes);
+    if (smem == 0) return cudaErrorInvalidConfiguration;
+    if ((long)a.tiles_x * a.tiles_y * L.B * ((L.cout_pad + n - 1) / n) > 0x7fffffffL)
+        return cudaErrorInvalidConfiguration;
 
     CUtensorMap ma, mb;
     const cuuint64_t dims_a[4] = {(cuuint64_t)L.x_c, (cuuint64_t)L.W, (cuuint64_t)L.H,
                                   (cuuint64_t)L.B};
     const cuuint64_t str_a[3] = {(cuuint64_t)L.x_c * 2, (cuuint64_t)L.W * L.x_c * 2,
                                  (cuuint64_t)L.H * L.W * L.x_c * 2};
-    const cuuint32_t box_a[4] = {(cuuint32_t)kKC, (cuuint32_t)a.tw, (cuuint32_t)a.th, 1};
+    // the halo tile: tw pixels x (mt * th + ks - 1) rows x 64 channels
+    const cuuint32_t box_a[4] = {(cuuint32_t)kKC, (cuuint32_t)a.tw,
+                                 (cuuint32_t)(mt * a.th + L.ks - 1), 1};
     const cuuint64_t dims_b[3] = {(cuuint64_t)L.cin_pad, (cuuint64_t)L.cout_pad,
                                   (cuuint64_t)(L.ks * L.ks)};
     const cuuint64_t str_b[2] = {(cuuint64_t)L.cin_pad * 2,
@@ -535,8 +721,7 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     // planar outputs: a 4-D map (W, H, cout, B) over the output, written by each
     // epilogue warp as pw x ph pixels x 32 channels boxes
     CUtensorMap mo = ma;  // unused by the other epilogues
-    if (L.epi == ConvEpi::PLANAR16 || L.epi == ConvEpi::PLANAR32) {
-        const int es = L.epi == ConvEpi::PLANAR16 ? 2 : 4;
+    if (planar) {
         if ((L.W * es) % 16 != 0) return cudaErrorInvalidValue;
         const int pw = a.tw < 32 ? a.tw : 32;
         const cuuint64_t dims_o[4] = {(cuuint64_t)L.W, (cuuint64_t)L.H, (cuuint64_t)L.cout,
@@ -552,16 +737,22 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     switch (L.epi) {
         case ConvEpi::NHWC:
             switch (L.act) {
-                case 0: return launch_act<(int)ConvEpi::NHWC, 0>(n, ma, mb, mo, a, s);
-                case 1: return launch_act<(int)ConvEpi::NHWC, 1>(n, ma, mb, mo, a, s);
-                case 2: return launch_act<(int)ConvEpi::NHWC, 2>(n, ma, mb, mo, a, s);
-                case 3: return launch_act<(int)ConvEpi::NHWC, 3>(n, ma, mb, mo, a, s);
+                case 0: return launch_act<(int)ConvEpi::NHWC, 0>(n, mt, bres, ma, mb, mo, a, smem, s);
+                case 1: return launch_act<(int)ConvEpi::NHWC, 1>(n, mt, bres, ma, mb, mo, a, smem, s);
+                case 2: return launch_act<(int)ConvEpi::NHWC, 2>(n, mt, bres, ma, mb, mo, a, smem, s);
+                case 3: return launch_act<(int)ConvEpi::NHWC, 3>(n, mt, bres, ma, mb, mo, a, smem, s);
                 default: return cudaErrorInvalidValue;
             }
-        case ConvEpi::PLANAR16: return launch_act<(int)ConvEpi::PLANAR16, 0>(n, ma, mb, mo, a, s);
-        case ConvEpi::PLANAR32: return launch_act<(int)ConvEpi::PLANAR32, 0>(n, ma, mb, mo, a, s);
-        case ConvEpi::GRU_ZR: return launch_act<(int)ConvEpi::GRU_ZR, 0>(n, ma, mb, mo, a, s);
-        case ConvEpi::GRU_Q: return launch_act<(int)ConvEpi::GRU_Q, 0>(n, ma, mb, mo, a, s);
+        case ConvEpi::NHWC32:
+            switch (L.act) {
+                case 0: return launch_act<(int)ConvEpi::NHWC32, 0>(n, mt, bres, ma, mb, mo, a, smem, s);
+                case 1: return launch_act<(int)ConvEpi::NHWC32, 1>(n, mt, bres, ma, mb, mo, a, smem, s);
+                default: return cudaErrorInvalidValue;
+            }
+        case ConvEpi::PLANAR16: return launch_act<(int)ConvEpi::PLANAR16, 0>(n, mt, bres, ma, mb, mo, a, smem, s);
+        case ConvEpi::PLANAR32: return launch_act<(int)ConvEpi::PLANAR32, 0>(n, mt, bres, ma, mb, mo, a, smem, s);
+        case ConvEpi::GRU_ZR: return launch_act<(int)ConvEpi::GRU_ZR, 0>(n, mt, bres, ma, mb, mo, a, smem, s);
+        case ConvEpi::GRU_Q: return launch_act<(int)ConvEpi::GRU_Q, 0>(n, mt, bres, ma, mb, mo, a, smem, s);
     }
     return cudaErrorInvalidValue;
 }

@@ -3,24 +3,34 @@ the four prediction heads of ``Refiner::forward`` (src/dsine_refine.cpp:
 95-158, 253-276), whose raw outputs feed the refine ops (``refine(...,
 logits=True)``).
 
-Per iteration (the GRU and heads never read the normals, so all iterations
-run first and the ops unit consumes their outputs afterwards):
+The convolutions are linear in their input channels, and two of the three
+channel groups never change during a refinement: the decoder feature (64
+channels) and uv (2) are the same in every iteration, and uv is the same for
+every frame. So ``start`` convolves them once --
 
-  hx  = [h | feat | uv]            (B,h,w,192) bf16 NHWC; feat, uv fixed
-  z, r = sigmoid(convz / convr(hx))      5x5, one fused GEMM (N = 128),
-         epilogue writes z and r*h into rhx = [r*h | feat | uv]
-  q   = tanh(convq(rhx))                 5x5, epilogue h = (1-z) h + z q
-                                          (fp32 state), bf16 h into hx and hin
-  hin = [h | uv]                   (B,h,w,128)
-  each head: conv3x3 -> ReLU -> conv1x1 -> ReLU -> conv1x1
-         the four 3x3 layers as one GEMM (N = 512); the 1x1 layers per head
-         on 128-channel slices; the last layer writes planar NCHW (fp16 or
-         fp32): prob (25), xy (50), angle (25), up_mask (576) logits.
+  gx  = conv5x5([feat | uv], W_zr||q[:, 64:130])   (B,h,w,192) fp32
+  gu  = conv3x3(uv, W_heads3x3[:, 64:66])          (1,h,w,512) fp32, shared
 
-11 tensor-core launches per iteration, no separate elementwise or layout
-pass. Weights are the reference's (OIHW fp32, safetensors names
-``gru.convz`` ... ``up_prob_head.4``), rounded to bf16 once; activations are
-bf16 between layers, the GRU state fp32.
+-- and each iteration convolves only the hidden state, adding gx / gu in the
+epilogue (the same products, summed in another order):
+
+  z, r = sigmoid(conv5x5(h, W_zr[:, :64]) + gx[:128])   one GEMM (N = 128);
+         the epilogue writes z and r*h
+  q   = tanh(conv5x5(r*h, W_q[:, :64]) + gx[128:])      epilogue
+         h = (1-z) h + z q (fp32 state) and its bf16 copy
+  each head: conv3x3 -> ReLU -> conv1x1 -> ReLU -> conv1x1; the four 3x3
+         layers as one GEMM (N = 512) over h with gu added; the 1x1 layers
+         per head on 128-channel slices; the last layer writes planar NCHW
+         (fp16 or fp32): prob (25), xy (50), angle (25), up_mask (576) logits.
+
+(The GRU and heads never read the normals, so all iterations run first and
+the ops unit consumes their outputs afterwards.) 2 tensor-core launches per
+refinement plus 11 per iteration, no separate elementwise or layout pass;
+the 5x5 GEMMs contract 25 x 64 instead of 25 x 130 (padded: 192) channels,
+the heads' 3x3 9 x 64 instead of 9 x 66 (padded: 128). Weights are the
+reference's (OIHW fp32, safetensors names ``gru.convz`` ...
+``up_prob_head.4``), rounded to bf16 once; activations are bf16 between
+layers, the GRU state and the hoisted terms fp32.
 """
 from __future__ import annotations
 
@@ -29,8 +39,8 @@ from dataclasses import dataclass
 
 import torch
 
-from ._capi import EPI_GRU_Q, EPI_GRU_ZR, EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, \
-    ConvEpilogue, check, lib
+from ._capi import EPI_GRU_Q, EPI_GRU_ZR, EPI_NHWC, EPI_NHWC_F32, EPI_PLANAR_F16, \
+    EPI_PLANAR_F32, ConvEpilogue, check, lib
 from .ops import _cuda, _p, _stream, pack_conv_weight, pad64
 
 HEADS = (("prob_head", 25), ("xy_head", 50), ("angle_head", 25), ("up_prob_head", 576))
@@ -81,26 +91,33 @@ class RefineStage:
         self.out_dtype = out_dtype
         d = self.dev
         f32 = lambda t: t.to(d, torch.float32).contiguous()  # noqa: E731
-        self.cin_gru = pad64(HIDDEN + FEATURE + 2)            # 192
-        self.cin_head = pad64(HIDDEN + 2)                     # 128
-        wz, wr = params["gru.convz.weight"], params["gru.convr.weight"]
-        self.w_zr = pack_conv_weight(torch.cat([wz, wr]).to(d), self.cin_gru, 128)
+        H = HIDDEN
+        # hidden-state parts of the weights (input channels [0, 64))
+        wz, wr, wq = (params[f"gru.conv{g}.weight"].to(d) for g in "zrq")
+        self.w_zr = pack_conv_weight(torch.cat([wz, wr])[:, :H], H, 128)
         self.b_zr = f32(torch.cat([params["gru.convz.bias"], params["gru.convr.bias"]]))
-        self.w_q = pack_conv_weight(params["gru.convq.weight"].to(d), self.cin_gru, 64)
+        self.w_q = pack_conv_weight(wq[:, :H], H, 64)
         self.b_q = f32(params["gru.convq.bias"])
-        self.w_c0 = pack_conv_weight(torch.cat([params[f"{n}.0.weight"] for n, _ in HEADS]).to(d),
-                                     self.cin_head, 4 * HEAD_HIDDEN)
+        c0 = torch.cat([params[f"{n}.0.weight"] for n, _ in HEADS]).to(d)
+        self.w_c0 = pack_conv_weight(c0[:, :H], H, 4 * HEAD_HIDDEN)
         self.b_c0 = f32(torch.cat([params[f"{n}.0.bias"] for n, _ in HEADS]))
+        # the fixed inputs' parts: feat + uv -> z, r, q; uv -> the heads' 3x3
+        self.w_gx = pack_conv_weight(torch.cat([wz, wr, wq])[:, H:], 128, 192)
+        self.w_gu = pack_conv_weight(c0[:, H:], 64, 4 * HEAD_HIDDEN)
+        self.zeros = torch.zeros(4 * HEAD_HIDDEN, device=d)
         self.w_c2 = [pack_conv_weight(params[f"{n}.2.weight"].to(d), 128, 128) for n, _ in HEADS]
         self.b_c2 = [f32(params[f"{n}.2.bias"]) for n, _ in HEADS]
         self.w_c4 = [pack_conv_weight(params[f"{n}.4.weight"].to(d), 128, pad64(c))
                      for n, c in HEADS]
         self.b_c4 = [f32(params[f"{n}.4.bias"]) for n, _ in HEADS]
         bf = torch.bfloat16
-        mk = lambda c, dt=bf: torch.zeros((B, h, w, c), device=d, dtype=dt)  # noqa: E731
-        self.hx, self.rhx, self.z = mk(self.cin_gru), mk(self.cin_gru), mk(HIDDEN)
-        self.hin, self.t1, self.t2 = mk(self.cin_head), mk(4 * HEAD_HIDDEN), mk(4 * HEAD_HIDDEN)
-        self.h32 = mk(HIDDEN, torch.float32)
+        mk = lambda c, dt=bf, n=B: torch.zeros((n, h, w, c), device=d, dtype=dt)  # noqa: E731
+        self.hx, self.rhx, self.z = mk(H), mk(H), mk(H)      # h (bf16), r * h, z
+        self.h32 = mk(H, torch.float32)
+        self.fx, self.ux = mk(128), mk(64, n=1)              # [feat | uv], [uv]
+        self.gx = mk(192, torch.float32)                     # hoisted GRU terms
+        self.gu = mk(4 * HEAD_HIDDEN, torch.float32, n=1)    # hoisted head terms
+        self.t1, self.t2 = mk(4 * HEAD_HIDDEN), mk(4 * HEAD_HIDDEN)
         self.err = torch.zeros(1, device=d, dtype=torch.int32)
 
     # one launch through the C ABI
@@ -108,23 +125,27 @@ class RefineStage:
         e = ConvEpilogue(**{k: (_p(v) if isinstance(v, torch.Tensor) else v)
                             for k, v in epi.items()})
         check(lib.bvml_conv2d_nhwc_bf16_ex(_p(x), x.shape[-1], cin_off, cin_pad, _p(w),
-                                           _p(bias), self.B, self.h, self.w, cout, w.shape[1],
-                                           ks, ctypes.byref(e), _p(self.err),
+                                           _p(bias), x.shape[0], self.h, self.w, cout,
+                                           w.shape[1], ks, ctypes.byref(e), _p(self.err),
                                            _stream(self.dev)))
 
     def start(self, h0: torch.Tensor, feat: torch.Tensor, uv: torch.Tensor) -> None:
         """Load the decoder's hidden state h0 (B,64,h,w), feature (B,64,h,w)
-        and uv (2,h,w) (src/dsine_refine.cpp:245-248)."""
+        and uv (2,h,w) (src/dsine_refine.cpp:245-248), and convolve the fixed
+        inputs once (two launches)."""
         _cuda("refine stage", h0, feat, uv)
-        B = self.B
         nhwc = lambda t: t.permute(0, 2, 3, 1)  # noqa: E731
-        uvb = uv.permute(1, 2, 0)[None].expand(B, -1, -1, -1)
+        uvn = uv.permute(1, 2, 0)[None].to(torch.bfloat16)
         self.h32.copy_(nhwc(h0))
-        for buf in (self.hx, self.rhx):
-            buf[..., HIDDEN:HIDDEN + FEATURE] = nhwc(feat).to(torch.bfloat16)
-            buf[..., HIDDEN + FEATURE:HIDDEN + FEATURE + 2] = uvb.to(torch.bfloat16)
-        self.hx[..., :HIDDEN] = self.h32.to(torch.bfloat16)
-        self.hin[..., HIDDEN:HIDDEN + 2] = uvb.to(torch.bfloat16)
+        self.hx.copy_(self.h32)
+        self.fx[..., :FEATURE] = nhwc(feat)
+        self.fx[..., FEATURE:FEATURE + 2] = uvn
+        self.ux[..., :2] = uvn
+        with torch.cuda.device(self.dev):
+            self._conv(self.fx, 0, 128, self.w_gx, self.zeros, 192, 5, mode=EPI_NHWC_F32,
+                       out=self.gx, out_c=192, out_off=0)
+            self._conv(self.ux, 0, 64, self.w_gu, self.zeros, 4 * HEAD_HIDDEN, 3,
+                       mode=EPI_NHWC_F32, out=self.gu, out_c=4 * HEAD_HIDDEN, out_off=0)
 
     def step(self, out: StageOutputs | None = None) -> StageOutputs:
         """One iteration: GRU update, then the four heads' raw outputs."""
@@ -134,13 +155,14 @@ class RefineStage:
                                        dtype=self.out_dtype)
             out = StageOutputs(*(mk(c) for _, c in HEADS))
         with torch.cuda.device(self.dev):
-            self._conv(self.hx, 0, self.cin_gru, self.w_zr, self.b_zr, 128, 5, mode=EPI_GRU_ZR,
-                       h32=self.h32, z=self.z, rh=self.rhx, rh_c=self.cin_gru)
-            self._conv(self.rhx, 0, self.cin_gru, self.w_q, self.b_q, 64, 5, mode=EPI_GRU_Q,
-                       h32=self.h32, z=self.z, hx=self.hx, hx_c=self.cin_gru, hin=self.hin,
-                       hin_c=self.cin_head)
-            self._conv(self.hin, 0, self.cin_head, self.w_c0, self.b_c0, 4 * HEAD_HIDDEN, 3,
-                       mode=EPI_NHWC, act=1, out=self.t1, out_c=4 * HEAD_HIDDEN, out_off=0)
+            self._conv(self.hx, 0, HIDDEN, self.w_zr, self.b_zr, 128, 5, mode=EPI_GRU_ZR,
+                       h32=self.h32, z=self.z, rh=self.rhx, rh_c=HIDDEN, add=self.gx, add_c=192)
+            self._conv(self.rhx, 0, HIDDEN, self.w_q, self.b_q, 64, 5, mode=EPI_GRU_Q,
+                       h32=self.h32, z=self.z, hx=self.hx, hx_c=HIDDEN, add=self.gx[..., 128:],
+                       add_c=192)
+            self._conv(self.hx, 0, HIDDEN, self.w_c0, self.b_c0, 4 * HEAD_HIDDEN, 3,
+                       mode=EPI_NHWC, act=1, out=self.t1, out_c=4 * HEAD_HIDDEN, out_off=0,
+                       add=self.gu, add_c=4 * HEAD_HIDDEN, add_shared=1)
             planar = EPI_PLANAR_F16 if self.out_dtype == torch.float16 else EPI_PLANAR_F32
             dsts = (out.prob, out.xy, out.angle, out.up_mask)
             for k, (_, c) in enumerate(HEADS):
@@ -188,3 +210,53 @@ def reference_stage(params, h0, feat, uv, iters: int, *, emulate_bf16: bool = Tr
             res.append(F.conv2d(t, W[f"{name}.4.weight"], W[f"{name}.4.bias"]))
         outs.append(StageOutputs(*res))
     return outs
+
+
+def _main(argv=None) -> None:
+    """`python -m brovisionml_b200.refine_stage [--frames B] [--steps K]`:
+    run `steps` iterations of the stage on random weights over B frames of
+    the 160 x 90 grid (720p) and print each launch's time of the last
+    iteration (CUDA events). Also the target for profiling one layer: after
+    the two launches of start (the hoisted terms), the launches of iteration
+    k are numbers 2 + 11 k .. 12 + 11 k (zr, q, heads 3x3, then per head 1x1
+    and 1x1 planar)."""
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--frames", type=int, default=16)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--height", type=int, default=90)
+    ap.add_argument("--width", type=int, default=160)
+    args = ap.parse_args(argv)
+    B, h, w = args.frames, args.height, args.width
+    dev = torch.device("cuda", 0)
+    st = RefineStage(random_params(dev, seed=7), B, h, w, device=dev)
+    g = torch.Generator(device=dev).manual_seed(1)
+    h0 = torch.tanh(torch.randn((B, HIDDEN, h, w), device=dev, generator=g))
+    feat = torch.relu(torch.randn((B, FEATURE, h, w), device=dev, generator=g))
+    ys, xs = torch.meshgrid(torch.arange(h, device=dev), torch.arange(w, device=dev),
+                            indexing="ij")
+    uv = torch.stack([((xs + 0.5) - w / 2) / (0.8 * w), ((ys + 0.5) - h / 2) / (0.8 * w)])
+    st.start(h0, feat, uv.float())
+    marks = []
+    conv = st._conv
+
+    def timed(*a, **k):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        conv(*a, **k)
+        e1.record()
+        marks.append((e0, e1))
+
+    st._conv = timed
+    for _ in range(args.steps):
+        marks.clear()
+        st.step()
+    torch.cuda.synchronize()
+    st.check_pipeline()
+    names = ["zr", "q", "heads3x3"] + [f"{n}.{i}" for n, _ in HEADS for i in (2, 4)]
+    print(" ".join(f"{n} {a.elapsed_time(b):.3f}" for n, (a, b) in zip(names, marks)))
+
+
+if __name__ == "__main__":
+    _main()

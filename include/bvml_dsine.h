@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define BVML_ABI_VERSION 1
+#define BVML_ABI_VERSION 2
 
 enum bvml_dtype { BVML_F32 = 0, BVML_F16 = 1 };
 
@@ -216,6 +216,8 @@ int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B
 #define BVML_EPI_PLANAR_F32 2  /* the same in fp32 */
 #define BVML_EPI_GRU_ZR 3      /* ConvGRU gates z, r (cout = 128: z then r) */
 #define BVML_EPI_GRU_Q 4       /* ConvGRU candidate and update (cout = 64) */
+#define BVML_EPI_NHWC_F32 5    /* act(conv) as fp32 at out[pixel * out_c + out_off + o]
+                                  (act 0 or 1; out_c, out_off multiples of 4) */
 
 /*
  * Where and how bvml_conv2d_nhwc_bf16_ex writes its result. Channel strides
@@ -225,10 +227,17 @@ int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B
  *   h the fp32 hidden state h32 (B,H,W,64).
  * GRU_Q (:148-156): q = tanh(conv) -> h32 = (1 - z) h32 + z q, with bf16
  *   copies at hx[pixel * hx_c + o] and, when hin is not null, hin[...].
+ * add (optional, every mode): a per-pixel fp32 addend, add[(f * H * W + y * W
+ *   + x) * add_c + o] joins conv[o] + bias[o] before the epilogue, with
+ *   f = the frame (f = 0 for every frame when add_shared is nonzero); 16-byte
+ *   aligned, add_c a multiple of 4 and >= cout. It carries the part of a
+ *   convolution whose input does not change between calls: the ConvGRU's
+ *   feature and uv channels, the heads' uv channels, which the refine stage
+ *   convolves once per refinement instead of once per iteration.
  */
 typedef struct {
     int mode;
-    int act;             /* BVML_EPI_NHWC: 0 none, 1 ReLU, 2 sigmoid, 3 tanh */
+    int act;             /* NHWC: 0 none, 1 ReLU, 2 sigmoid, 3 tanh; NHWC_F32: 0, 1 */
     void* out;
     int out_c, out_off;
     float* h32;
@@ -239,6 +248,9 @@ typedef struct {
     int hx_c;
     void* hin;
     int hin_c;
+    const float* add;
+    int add_c;
+    int add_shared;
 } bvml_conv_epilogue;
 
 /*
