@@ -393,8 +393,8 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
     L.add = epi->add;
     L.add_c = epi->add_c;
     L.add_shared = epi->add_shared;
-    if (epi->add && (!a16(epi->add) || epi->add_c % 4 || epi->add_c < cout))
-        return einval("conv2d: addend must be 16-byte aligned with add_c a multiple of 4, >= cout");
+    if (epi->add && ((reinterpret_cast<uintptr_t>(epi->add) & 3) || epi->add_c < cout))
+        return einval("conv2d: addend must be 4-byte aligned with add_c >= cout planes");
     switch (epi->mode) {
         case BVML_EPI_NHWC:
             if (epi->act < 0 || epi->act > 3) return einval("conv2d: unknown activation");

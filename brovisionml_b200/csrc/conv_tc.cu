@@ -62,14 +62,13 @@ struct ConvArgs {
     int hx_c;
     __nv_bfloat16* hin;
     int hin_c;
-    // optional per-pixel addend: add[f * add_fs + (y * W + x) * add_c + c]
+    // optional per-pixel addend, planar: add[f * add_fs + c * H * W + y * W + x]
     const float* add;
     long add_fs;  // frame stride in floats (0: one frame shared by all)
-    int add_c;
     // shared-memory plan (see below)
     int a_bytes, b_bytes;  // one A entry (halo tile), one B entry (one tap's weights)
     int s_a, s_b;          // ring depths
-    int off_b, off_out, off_bar;
+    int off_b, off_out, off_bias, off_bar;
 };
 
 template <int ACT>
@@ -80,35 +79,50 @@ __device__ __forceinline__ float activate(float v) {
     else return v;
 }
 
-// The addend row of pixel (px, py) of frame b for channels cb.., or null.
+// The addend of pixel (px, py) of frame b at channel cb (planar: channel
+// cb + i at ad[i * H * W]), or null. Lanes hold consecutive pixels, so each
+// channel's read is one coalesced row segment per warp.
 __device__ __forceinline__ const float* addend_at(const ConvArgs& a, int b, int px, int py,
                                                   int cb) {
-    return a.add ? a.add + b * a.add_fs + ((long)py * a.W + px) * a.add_c + cb : nullptr;
+    return a.add ? a.add + b * a.add_fs + (long)cb * a.H * a.W + (long)py * a.W + px : nullptr;
 }
 
-// f[i] = accumulator + bias (+ addend) for channels cb + i < cout, else 0.
-__device__ __forceinline__ void pre_activation(const ConvArgs& a, const float* ad, int cb,
+// The addend of one thread's pixel for channels cb .. cb+31 into t (zeros
+// where there is none). Issued ahead of use: the epilogue loads chunk k + 1
+// while it finishes chunk k, and a tile's first chunk before waiting for its
+// accumulator, so the loads' latency overlaps other work. Channels past cout
+// re-read channel cout - 1 (always in bounds); pre_activation zeroes them.
+__device__ __forceinline__ void load_addend(const ConvArgs& a, bool in, int b, int px, int py,
+                                            int cb, float (&t)[32]) {
+    if (a.add && in && cb < a.cout) {
+        const float* ad = addend_at(a, b, px, py, cb);
+        const long hw = (long)a.H * a.W;
+        const int lim = a.cout - 1 - cb;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) t[i] = __ldg(ad + (i < lim ? i : lim) * hw);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) t[i] = 0.0f;
+    }
+}
+
+// f[i] = accumulator + bias + addend t for channels cb + i < cout, else 0.
+// sbias: the bias staged in shared memory, zero past cout (float4 broadcasts).
+__device__ __forceinline__ void pre_activation(const ConvArgs& a, const float* sbias,
+                                               const float (&t)[32], int cb,
                                                const uint32_t (&v)[32], float (&f)[32]) {
+    const float4* b4 = reinterpret_cast<const float4*>(sbias + cb);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const float4 bq = b4[q];
+        f[4 * q + 0] = __uint_as_float(v[4 * q + 0]) + bq.x + t[4 * q + 0];
+        f[4 * q + 1] = __uint_as_float(v[4 * q + 1]) + bq.y + t[4 * q + 1];
+        f[4 * q + 2] = __uint_as_float(v[4 * q + 2]) + bq.z + t[4 * q + 2];
+        f[4 * q + 3] = __uint_as_float(v[4 * q + 3]) + bq.w + t[4 * q + 3];
+    }
 #pragma unroll
     for (int i = 0; i < 32; ++i)
-        f[i] = cb + i < a.cout ? __uint_as_float(v[i]) + a.bias[cb + i] : 0.0f;
-    if (ad) {
-        if (cb + 32 <= a.add_c) {
-            const float4* a4 = reinterpret_cast<const float4*>(ad);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const float4 t = a4[q];
-                f[4 * q + 0] += cb + 4 * q + 0 < a.cout ? t.x : 0.0f;
-                f[4 * q + 1] += cb + 4 * q + 1 < a.cout ? t.y : 0.0f;
-                f[4 * q + 2] += cb + 4 * q + 2 < a.cout ? t.z : 0.0f;
-                f[4 * q + 3] += cb + 4 * q + 3 < a.cout ? t.w : 0.0f;
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (cb + i < a.cout) f[i] += ad[i];
-        }
-    }
+        if (cb + i >= a.cout) f[i] = 0.0f;
 }
 
 // Epilogue of one thread's pixel for 32 consecutive output channels
@@ -123,10 +137,11 @@ __device__ __forceinline__ void pre_activation(const ConvArgs& a, const float* a
 //            bf16 copies at hx[pix * hx_c + c] and, if set, hin[pix * hin_c + c]
 //  (src/dsine_refine.cpp:140-158).
 template <int EPI, int ACT>
-__device__ __forceinline__ void epilogue32(const ConvArgs& a, long pix, int b, int px, int py,
-                                           int cb, const uint32_t (&v)[32]) {
+__device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias, long pix,
+                                           int cb, const float (&t)[32],
+                                           const uint32_t (&v)[32]) {
     float f[32];
-    pre_activation(a, addend_at(a, b, px, py, cb), cb, v, f);
+    pre_activation(a, sbias, t, cb, v, f);
     if constexpr (EPI == (int)ConvEpi::NHWC32) {
         float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + pix * a.out_c +
                                                 a.out_off + cb);
@@ -225,7 +240,7 @@ constexpr int kBResChunks = 2;
 
 // planar outputs: per epilogue warp two 32-channel x 32-pixel staging buffers
 __host__ __device__ constexpr int stage_warp_bytes(int epi) {
-    return 32 * 32 * (epi == (int)ConvEpi::PLANAR16 ? 2 : 4);
+    return 32 * 32 * (epi == (int)ConvEpi::PLANAR32 ? 4 : 2);  // NHWC, PLANAR16: 2 bytes
 }
 
 // Planar output of one 32-channel chunk (channels cb .. cb+31) of one
@@ -239,9 +254,10 @@ template <typename TO>
 __device__ __forceinline__ void planar_chunk_tma(const ConvArgs& a, const CUtensorMap* map_o,
                                                  TO* stg, uint32_t stg_addr, int lane,
                                                  int px0, int py0, int b, int cb,
-                                                 const float* ad, const uint32_t (&v)[32]) {
+                                                 const float* sbias, const float (&t)[32],
+                                                 const uint32_t (&v)[32]) {
     float f[32];
-    pre_activation(a, ad, cb, v, f);
+    pre_activation(a, sbias, t, cb, v, f);
     if (lane == 0) tc::bulk_wait_read<1>();  // this buffer's previous store has read it
     __syncwarp();
 #pragma unroll
@@ -257,6 +273,40 @@ __device__ __forceinline__ void planar_chunk_tma(const ConvArgs& a, const CUtens
     }
 }
 
+// NHWC bf16 output of one 32-channel chunk of one epilogue warp's 32 pixels
+// through shared memory: lane r writes its pixel's 64 bytes as row r of the
+// warp's staging buffer ([pixel][channel], the TMA box layout) in the
+// 64-byte swizzle (16-byte unit u of row r at u ^ ((r >> 1) & 3), which
+// spreads a warp's rows over all banks), and lane 0 stores the box (32
+// channels at c0 x pw x ph pixels) with one TMA store, clipped at the frame
+// edges. The buffer is reused two chunks later, after the store has read it.
+template <int ACT>
+__device__ __forceinline__ void nhwc_chunk_tma(const ConvArgs& a, const CUtensorMap* map_o,
+                                               uint8_t* stg, uint32_t stg_addr, int lane, int c0,
+                                               int px0, int py0, int b, int cb,
+                                               const float* sbias, const float (&t)[32],
+                                               const uint32_t (&v)[32]) {
+    float f[32];
+    pre_activation(a, sbias, t, cb, v, f);
+    alignas(16) __nv_bfloat16 o[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        o[i] = __float2bfloat16_rn(cb + i < a.cout ? activate<ACT>(f[i]) : 0.0f);
+    if (lane == 0) tc::bulk_wait_read<1>();  // this buffer's previous store has read it
+    __syncwarp();
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4*>(stg + lane * 64 + ((q ^ sw) << 4)) =
+            reinterpret_cast<const uint4*>(o)[q];
+    tc::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        tc::tma_store_4d(map_o, stg_addr, c0, px0, py0, b);
+        tc::bulk_commit();
+    }
+}
+
 // Persistent: CTA c computes tiles c, c + G, c + 2G, ... (G CTAs, one per
 // SM). A tile is MT sub-tiles of 128 pixels (tw x th, stacked vertically)
 // by N output channels; each sub-tile has its own TMEM accumulator, so one
@@ -268,6 +318,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                const __grid_constant__ CUtensorMap map_o, const ConvArgs a) {
     constexpr bool kPlanar = EPI == (int)ConvEpi::PLANAR16 || EPI == (int)ConvEpi::PLANAR32;
+    constexpr bool kStaged = kPlanar || EPI == (int)ConvEpi::NHWC;  // TMA-store epilogues
     constexpr int kCols = 2 * MT * N;  // TMEM columns: two accumulator sets
     static_assert(kCols <= 512 && (kCols & (kCols - 1)) == 0, "TMEM allocation");
     extern __shared__ uint8_t smem_raw[];
@@ -332,6 +383,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         tc::tmem_alloc(tc::smem_u32(tmem_slot), kCols);
         tc::tmem_relinquish();
     }
+    float* sbias = reinterpret_cast<float*>(smem + a.off_bias);
+    for (int c = threadIdx.x; c < a.cout_pad; c += blockDim.x)
+        sbias[c] = c < a.cout ? a.bias[c] : 0.0f;
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
@@ -477,58 +531,84 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const int row = wq * 32 + lane;       // pixel index in the sub-tile
         const int grp = (warp - 2) >> 2;
         const int c_lo = MT == 1 ? grp * (N / 2) : 0;
-        const int c_hi = MT == 1 ? c_lo + N / 2 : N;
-        int pcount = 0;                       // planar chunks stored by this warp
+        int pcount = 0;                       // TMA-stored chunks of this warp
+        // this warp's chunks of a tile: sub-tiles m (MT >= 2: grp, grp + 2, ..)
+        // x 32-column groups from c_lo (MT = 1: this warp's half of the columns)
+        constexpr int kCPer = MT == 1 ? N / 64 : N / 32;  // column groups per sub-tile
+        constexpr int kChunks = (MT == 1 ? 1 : MT / 2) * kCPer;
+        int b = 0, x0 = 0, y0 = 0, n0 = 0;
+        auto geo = [&](int k, int& ys, int& px, int& py, bool& in, int& c0) {
+            const int m = MT == 1 ? 0 : grp + 2 * (k / kCPer);
+            c0 = c_lo + 32 * (k % kCPer);
+            ys = y0 + m * a.th;  // the sub-tile's first image row
+            px = x0 + row % a.tw;
+            py = ys + row / a.tw;
+            in = px < a.W && py < a.H;
+            return m;
+        };
+        auto prefetch = [&](int k, float (&tt)[32]) {
+            int ys, px, py, c0;
+            bool in;
+            geo(k, ys, px, py, in, c0);
+            load_addend(a, in, b, px, py, n0 + c0, tt);
+        };
+        auto process = [&](int k, int buf, const float (&tt)[32]) {
+            int ys, px, py, c0;
+            bool in;
+            const int m = geo(k, ys, px, py, in, c0);
+            const uint32_t acc = tmem + buf * (MT * N) + m * N + ((uint32_t)(wq * 32) << 16);
+            uint32_t v[32];
+            tc::tmem_ld_32cols(acc + c0, v);
+            tc::tmem_ld_wait();
+            const int cb = n0 + c0;
+            if constexpr (kStaged) {
+                if (cb >= (kPlanar ? a.cout : a.cout_pad)) return;  // the same for the whole warp
+                // this warp's 32 pixels: sub-tile rows [wq * 32, wq * 32 + 32) as a
+                // pw x ph box (pw = min(tw, 32))
+                const int px0 = x0 + (wq * 32) % a.tw, py0 = ys + (wq * 32) / a.tw;
+                if (px0 >= a.W || py0 >= a.H) return;  // the whole box is off the frame
+                const int slot = (warp - 2) * 2 + (pcount & 1);
+                uint8_t* stg = smem + a.off_out + slot * stage_warp_bytes(EPI);
+                const uint32_t stg_addr = sbase + a.off_out + slot * stage_warp_bytes(EPI);
+                if constexpr (EPI == (int)ConvEpi::PLANAR16)
+                    planar_chunk_tma<__half>(a, &map_o, reinterpret_cast<__half*>(stg), stg_addr,
+                                             lane, px0, py0, b, cb, sbias, tt, v);
+                else if constexpr (EPI == (int)ConvEpi::PLANAR32)
+                    planar_chunk_tma<float>(a, &map_o, reinterpret_cast<float*>(stg), stg_addr,
+                                            lane, px0, py0, b, cb, sbias, tt, v);
+                else
+                    nhwc_chunk_tma<ACT>(a, &map_o, stg, stg_addr, lane, a.out_off + cb, px0, py0,
+                                        b, cb, sbias, tt, v);
+                ++pcount;
+            } else {
+                if (!in || cb >= a.cout_pad) return;
+                epilogue32<EPI, ACT>(a, sbias, ((long)b * a.H + py) * a.W + px, cb, tt, v);
+            }
+        };
         int tl = 0;
         for (int t = t0; t < t_end; t += dt, ++tl) {
             const int buf = tl & 1, u = tl >> 1;
+            tile_of(t, b, x0, y0, n0);
+            float ta[32], tb[32];
+            prefetch(0, ta);  // overlaps the wait for this tile's MMAs
             const bool ok = tc::mbar_wait(bar_acc_full + 8 * buf, u & 1, kWaitLimit);
             if (!ok) fail(6);
             if (!ok || aborted()) break;
             tc::tc_fence_after();
-            int b, x0, y0, n0;
-            tile_of(t, b, x0, y0, n0);
 #pragma unroll 1
-            for (int m = MT == 1 ? 0 : grp; m < MT; m += 2) {
-                const int ys = y0 + m * a.th;  // the sub-tile's first image row
-                const int px = x0 + row % a.tw, py = ys + row / a.tw;
-                const bool in = px < a.W && py < a.H;
-                const long pix = ((long)b * a.H + py) * a.W + px;
-                const uint32_t acc = tmem + buf * (MT * N) + m * N + ((uint32_t)(wq * 32) << 16);
-#pragma unroll 1
-                for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
-                    uint32_t v[32];
-                    tc::tmem_ld_32cols(acc + c0, v);
-                    tc::tmem_ld_wait();
-                    const int cb = n0 + c0;
-                    if constexpr (kPlanar) {
-                        if (cb >= a.cout) continue;  // the same for the whole warp
-                        const float* ad = in ? addend_at(a, b, px, py, cb) : nullptr;
-                        // this warp's 32 pixels: sub-tile rows [wq * 32, wq * 32 + 32)
-                        // as a pw x ph box (pw = min(tw, 32))
-                        const int px0 = x0 + (wq * 32) % a.tw, py0 = ys + (wq * 32) / a.tw;
-                        if (px0 >= a.W || py0 >= a.H) continue;  // the whole box is off the frame
-                        const int slot = (warp - 2) * 2 + (pcount & 1);
-                        uint8_t* stg = smem + a.off_out + slot * stage_warp_bytes(EPI);
-                        const uint32_t stg_addr = sbase + a.off_out + slot * stage_warp_bytes(EPI);
-                        if constexpr (EPI == (int)ConvEpi::PLANAR16)
-                            planar_chunk_tma<__half>(a, &map_o, reinterpret_cast<__half*>(stg),
-                                                     stg_addr, lane, px0, py0, b, cb, ad, v);
-                        else
-                            planar_chunk_tma<float>(a, &map_o, reinterpret_cast<float*>(stg),
-                                                    stg_addr, lane, px0, py0, b, cb, ad, v);
-                        ++pcount;
-                    } else {
-                        if (!in || cb >= a.cout_pad) continue;
-                        epilogue32<EPI, ACT>(a, pix, b, px, py, cb, v);
-                    }
+            for (int k = 0; k < kChunks; k += 2) {
+                if (k + 1 < kChunks) prefetch(k + 1, tb);
+                process(k, buf, ta);
+                if (k + 1 < kChunks) {
+                    if (k + 2 < kChunks) prefetch(k + 2, ta);
+                    process(k + 1, buf, tb);
                 }
             }
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(bar_acc_empty + 8 * buf);
         }
-        if (kPlanar && lane == 0) tc::bulk_wait_all();  // stores complete before exit
+        if (kStaged && lane == 0) tc::bulk_wait_all();  // stores complete before exit
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -607,18 +687,23 @@ cudaError_t launch_act(int n, int mt, bool bres, const CUtensorMap& ma, const CU
 // (= 128 pixels), MT sub-tiles per CTA tile, ring depths. Returns the dynamic
 // shared-memory size, or 0 if nothing fits.
 int plan_conv(ConvArgs& a, int n, int& mt, bool bres, int out_bytes) {
-    const int budget = kSmemLimit - 1024 - kBarBytes - out_bytes;  // 1024: alignment slack
+    const int bias_bytes = (a.cout_pad * 4 + 127) / 128 * 128;
+    const int budget = kSmemLimit - 1024 - kBarBytes - out_bytes - bias_bytes;  // 1024: alignment
     const int b_bytes = n * kKC * 2;
     for (; mt >= 1; mt /= 2) {
-        // the tw with the fewest computed pixels; for ks > 1 ties go to the
-        // narrower tile (less halo per pixel), and tw = 128 is not used
-        static const int tws[4] = {128, 64, 32, 16};
+        // the tw with the fewest computed pixels; for ks > 1 tw = 128 is not
+        // used (its halo) and ties go to 32 (128-byte rows for the epilogue's
+        // planar reads and stores, a moderate halo)
+        static const int tws1[4] = {128, 64, 32, 16};
+        static const int tws3[3] = {32, 64, 16};
+        const int* tws = a.ks > 1 ? tws3 : tws1;
+        const int ntw = a.ks > 1 ? 3 : 4;
         long best = -1;
-        for (int tw : tws) {
-            if (a.ks > 1 && tw == 128) continue;
+        for (int i = 0; i < ntw; ++i) {
+            const int tw = tws[i];
             const int th = kTM / tw;
             const long tiles = (long)((a.W + tw - 1) / tw) * ((a.H + th * mt - 1) / (th * mt));
-            if (best < 0 || tiles < best || (tiles == best && a.ks > 1)) {
+            if (best < 0 || tiles < best) {
                 best = tiles;
                 a.tw = tw;
                 a.th = th;
@@ -650,7 +735,8 @@ int plan_conv(ConvArgs& a, int n, int& mt, bool bres, int out_bytes) {
             a.off_b = a.s_a * a.a_bytes;
             a.off_out = a.off_b + a.s_b * b_bytes;
         }
-        a.off_bar = a.off_out + out_bytes;
+        a.off_bias = a.off_out + out_bytes;
+        a.off_bar = a.off_bias + bias_bytes;
         return a.off_bar + kBarBytes + 1024;
     }
     return 0;
@@ -684,7 +770,6 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     a.hin = static_cast<__nv_bfloat16*>(L.hin);
     a.hin_c = L.hin_c;
     a.add = L.add;
-    a.add_c = L.add_c;
     a.add_fs = L.add_shared ? 0 : (long)L.H * L.W * L.add_c;
     // N: output channels per tile. GRU gates need every channel of a pixel in
     // one CTA (z with r, q with z). Filters wider than 1x1 with N < 256 use 2
@@ -697,7 +782,8 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     const bool bres = L.ks == 1 && L.cin_pad <= kBResChunks * kKC;
     const bool planar = L.epi == ConvEpi::PLANAR16 || L.epi == ConvEpi::PLANAR32;
     const int es = L.epi == ConvEpi::PLANAR16 ? 2 : 4;
-    const int out_bytes = planar ? kEpiWarps * 2 * stage_warp_bytes((int)L.epi) : 0;
+    const int out_bytes = planar || L.epi == ConvEpi::NHWC
+                              ? kEpiWarps * 2 * stage_warp_bytes((int)L.epi) : 0;
     const int smem = plan_conv(a, n, mt, bres, out_bytes);
     if (smem == 0) return cudaErrorInvalidConfiguration;
     if ((long)a.tiles_x * a.tiles_y * L.B * ((L.cout_pad + n - 1) / n) > 0x7fffffffL)
@@ -732,6 +818,18 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
         if (!encode(&mo, L.y, 4, dims_o, str_o, box_o,
                     es == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                     CU_TENSOR_MAP_SWIZZLE_NONE))
+            return cudaErrorInvalidValue;
+    } else if (L.epi == ConvEpi::NHWC) {
+        // NHWC bf16: a 4-D map (out_c, W, H, B); each epilogue warp stores
+        // 32 channels x pw x ph pixels, 64-byte swizzled in shared memory
+        const int pw = a.tw < 32 ? a.tw : 32;
+        const cuuint64_t dims_o[4] = {(cuuint64_t)L.out_c, (cuuint64_t)L.W, (cuuint64_t)L.H,
+                                      (cuuint64_t)L.B};
+        const cuuint64_t str_o[3] = {(cuuint64_t)L.out_c * 2, (cuuint64_t)L.W * L.out_c * 2,
+                                     (cuuint64_t)L.H * L.W * L.out_c * 2};
+        const cuuint32_t box_o[4] = {32, (cuuint32_t)pw, (cuuint32_t)(32 / pw), 1};
+        if (!encode(&mo, L.y, 4, dims_o, str_o, box_o, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                    CU_TENSOR_MAP_SWIZZLE_64B))
             return cudaErrorInvalidValue;
     }
     switch (L.epi) {

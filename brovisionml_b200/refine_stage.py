@@ -8,8 +8,8 @@ channel groups never change during a refinement: the decoder feature (64
 channels) and uv (2) are the same in every iteration, and uv is the same for
 every frame. So ``start`` convolves them once --
 
-  gx  = conv5x5([feat | uv], W_zr||q[:, 64:130])   (B,h,w,192) fp32
-  gu  = conv3x3(uv, W_heads3x3[:, 64:66])          (1,h,w,512) fp32, shared
+  gx  = conv5x5([feat | uv], W_zr||q[:, 64:130])   (B,192,h,w) fp32 planar
+  gu  = conv3x3(uv, W_heads3x3[:, 64:66])          (1,512,h,w) fp32, shared
 
 -- and each iteration convolves only the hidden state, adding gx / gu in the
 epilogue (the same products, summed in another order):
@@ -39,8 +39,8 @@ from dataclasses import dataclass
 
 import torch
 
-from ._capi import EPI_GRU_Q, EPI_GRU_ZR, EPI_NHWC, EPI_NHWC_F32, EPI_PLANAR_F16, \
-    EPI_PLANAR_F32, ConvEpilogue, check, lib
+from ._capi import EPI_GRU_Q, EPI_GRU_ZR, EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, \
+    ConvEpilogue, check, lib
 from .ops import _cuda, _p, _stream, pack_conv_weight, pad64
 
 HEADS = (("prob_head", 25), ("xy_head", 50), ("angle_head", 25), ("up_prob_head", 576))
@@ -115,8 +115,9 @@ class RefineStage:
         self.hx, self.rhx, self.z = mk(H), mk(H), mk(H)      # h (bf16), r * h, z
         self.h32 = mk(H, torch.float32)
         self.fx, self.ux = mk(128), mk(64, n=1)              # [feat | uv], [uv]
-        self.gx = mk(192, torch.float32)                     # hoisted GRU terms
-        self.gu = mk(4 * HEAD_HIDDEN, torch.float32, n=1)    # hoisted head terms
+        # hoisted terms, planar fp32: the epilogues read them coalesced
+        self.gx = torch.zeros((B, 192, h, w), device=d)
+        self.gu = torch.zeros((1, 4 * HEAD_HIDDEN, h, w), device=d)
         self.t1, self.t2 = mk(4 * HEAD_HIDDEN), mk(4 * HEAD_HIDDEN)
         self.err = torch.zeros(1, device=d, dtype=torch.int32)
 
@@ -142,10 +143,10 @@ class RefineStage:
         self.fx[..., FEATURE:FEATURE + 2] = uvn
         self.ux[..., :2] = uvn
         with torch.cuda.device(self.dev):
-            self._conv(self.fx, 0, 128, self.w_gx, self.zeros, 192, 5, mode=EPI_NHWC_F32,
-                       out=self.gx, out_c=192, out_off=0)
+            self._conv(self.fx, 0, 128, self.w_gx, self.zeros, 192, 5, mode=EPI_PLANAR_F32,
+                       out=self.gx)
             self._conv(self.ux, 0, 64, self.w_gu, self.zeros, 4 * HEAD_HIDDEN, 3,
-                       mode=EPI_NHWC_F32, out=self.gu, out_c=4 * HEAD_HIDDEN, out_off=0)
+                       mode=EPI_PLANAR_F32, out=self.gu)
 
     def step(self, out: StageOutputs | None = None) -> StageOutputs:
         """One iteration: GRU update, then the four heads' raw outputs."""
@@ -158,7 +159,7 @@ class RefineStage:
             self._conv(self.hx, 0, HIDDEN, self.w_zr, self.b_zr, 128, 5, mode=EPI_GRU_ZR,
                        h32=self.h32, z=self.z, rh=self.rhx, rh_c=HIDDEN, add=self.gx, add_c=192)
             self._conv(self.rhx, 0, HIDDEN, self.w_q, self.b_q, 64, 5, mode=EPI_GRU_Q,
-                       h32=self.h32, z=self.z, hx=self.hx, hx_c=HIDDEN, add=self.gx[..., 128:],
+                       h32=self.h32, z=self.z, hx=self.hx, hx_c=HIDDEN, add=self.gx[:, 128:],
                        add_c=192)
             self._conv(self.hx, 0, HIDDEN, self.w_c0, self.b_c0, 4 * HEAD_HIDDEN, 3,
                        mode=EPI_NHWC, act=1, out=self.t1, out_c=4 * HEAD_HIDDEN, out_off=0,

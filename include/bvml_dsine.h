@@ -227,10 +227,10 @@ int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B
  *   h the fp32 hidden state h32 (B,H,W,64).
  * GRU_Q (:148-156): q = tanh(conv) -> h32 = (1 - z) h32 + z q, with bf16
  *   copies at hx[pixel * hx_c + o] and, when hin is not null, hin[...].
- * add (optional, every mode): a per-pixel fp32 addend, add[(f * H * W + y * W
- *   + x) * add_c + o] joins conv[o] + bias[o] before the epilogue, with
- *   f = the frame (f = 0 for every frame when add_shared is nonzero); 16-byte
- *   aligned, add_c a multiple of 4 and >= cout. It carries the part of a
+ * add (optional, every mode): a per-pixel fp32 addend, planar,
+ *   add[(f * add_c + o) * H * W + y * W + x] joins conv[o] + bias[o] before
+ *   the epilogue, with f = the frame (f = 0 for every frame when add_shared
+ *   is nonzero) and add_c >= cout channel planes per frame. It carries the part of a
  *   convolution whose input does not change between calls: the ConvGRU's
  *   feature and uv channels, the heads' uv channels, which the refine stage
  *   convolves once per refinement instead of once per iteration.

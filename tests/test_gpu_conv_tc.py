@@ -63,8 +63,8 @@ def test_conv_shapes(B, H, W, cin, cout, ks, act):
 
 @pytest.mark.parametrize("shared", [False, True])
 def test_conv_addend_and_fp32_output(shared):
-    """The per-pixel addend (per frame, or one frame shared by all) joins
-    conv + bias before the activation; fp32 NHWC output
+    """The planar per-pixel addend (per frame, or one frame shared by all)
+    joins conv + bias before the activation; fp32 NHWC output
     (bvml_conv2d_nhwc_bf16_ex with BVML_EPI_NHWC_F32): the refine stage's
     hoisted feature / uv terms."""
     import ctypes
@@ -78,7 +78,7 @@ def test_conv_addend_and_fp32_output(shared):
     x = torch.randn((B, H, W, cin), device="cuda", generator=g).to(torch.bfloat16)
     weight = torch.randn((cout, cin, ks, ks), device="cuda", generator=g) * (cin * ks * ks) ** -0.5
     bias = torch.randn(cout, device="cuda", generator=g) * 0.1
-    add = torch.randn((1 if shared else B, H, W, cout + 8), device="cuda", generator=g)
+    add = torch.randn((1 if shared else B, cout + 8, H, W), device="cuda", generator=g)
     y = torch.full((B, H, W, cout), float("nan"), device="cuda")
     err = torch.zeros(1, device="cuda", dtype=torch.int32)
     e = ConvEpilogue(mode=EPI_NHWC_F32, act=1, out=_p(y), out_c=cout, out_off=0,
@@ -88,7 +88,7 @@ def test_conv_addend_and_fp32_output(shared):
                                        _p(err), _stream(torch.device("cuda"))))
     torch.cuda.synchronize()
     assert int(err.item()) == 0
-    ref = ref_conv(x, weight, bias, ks, "none", cin) + add[..., :cout]
+    ref = ref_conv(x, weight, bias, ks, "none", cin) + add[:, :cout].permute(0, 2, 3, 1)
     ref = torch.relu(ref)
     d = (y - ref).abs().max().item()
     print(f"conv addend shared={shared}: max_abs {d:.2e}")
