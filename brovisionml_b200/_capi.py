@@ -76,7 +76,7 @@ class ConvEpilogue(ctypes.Structure):
                 ("hin", _vp), ("hin_c", _i), ("add", _vp), ("add_c", _i), ("add_shared", _i)]
 
 
-EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, EPI_GRU_ZR, EPI_GRU_Q, EPI_NHWC_F32 = range(6)
+EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, EPI_GRU_ZR, EPI_GRU_Q, EPI_C4_F32 = range(6)
 lib.bvml_conv2d_nhwc_bf16_ex.restype = _i
 lib.bvml_conv2d_nhwc_bf16_ex.argtypes = ([_vp, _i, _i, _i, _vp, _vp] + [_i] * 6
                                           + [ctypes.POINTER(ConvEpilogue), _vp, _vp])

@@ -42,7 +42,7 @@ struct UpsampleLaunch {
 };
 cudaError_t launch_upsample(const UpsampleLaunch& L, cudaStream_t s);
 
-enum class ConvEpi : int { NHWC = 0, PLANAR16 = 1, PLANAR32 = 2, GRU_ZR = 3, GRU_Q = 4, NHWC32 = 5 };
+enum class ConvEpi : int { NHWC = 0, PLANAR16 = 1, PLANAR32 = 2, GRU_ZR = 3, GRU_Q = 4, C4_32 = 5 };
 
 struct ConvLaunch {
     const void* x;       // (B,H,W,x_c) bf16; channels [cin_off, cin_off + cin_pad) are read
@@ -51,18 +51,19 @@ struct ConvLaunch {
     int* err;            // device int: nonzero if a pipeline wait gave up
     int B, H, W, x_c, cin_off, cin_pad, cout, cout_pad, ks;
     ConvEpi epi;
-    int act;             // NHWC, NHWC32: 0 none, 1 ReLU, 2 sigmoid, 3 tanh
-    void* y;             // NHWC (bf16) / NHWC32 (fp32): (B,H,W,out_c) at out_off; PLANAR: (B,cout,H,W)
+    int act;             // NHWC: 0 none, 1 ReLU, 2 sigmoid, 3 tanh; C4_32: 0, 1
+    void* y;             // NHWC: (B,H,W,out_c) bf16 at out_off; C4_32: (B,out_c/4,H,W,4) fp32
+                         // at channel out_off; PLANAR: (B,cout,H,W)
     int out_c, out_off;
-    float* h32;          // GRU: fp32 hidden state (B,H,W,64)
-    void* z;             // GRU: gate z (B,H,W,64) bf16
+    float* h32;          // GRU: fp32 hidden state, C4 (B,16,H,W,4)
+    void* z;             // GRU: gate z, C8 bf16 (B,8,H,W,8)
     void* rh;            // GRU_ZR: r * h at channels [0,64) of (B,H,W,rh_c)
     int rh_c;
     void* hx;            // GRU_Q: new h (bf16) at channels [0,64) of (B,H,W,hx_c)
     int hx_c;
     void* hin;           // GRU_Q: ... and of (B,H,W,hin_c) when not null
     int hin_c;
-    const float* add;    // optional per-pixel addend (B or 1,H,W,add_c) fp32, channels [0,cout)
+    const float* add;    // optional per-pixel addend, C4 fp32 (B or 1,add_c/4,H,W,4)
     int add_c;
     int add_shared;      // nonzero: one frame of addends shared by all B frames
 };

@@ -393,8 +393,8 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
     L.add = epi->add;
     L.add_c = epi->add_c;
     L.add_shared = epi->add_shared;
-    if (epi->add && ((reinterpret_cast<uintptr_t>(epi->add) & 3) || epi->add_c < cout))
-        return einval("conv2d: addend must be 4-byte aligned with add_c >= cout planes");
+    if (epi->add && (!a16(epi->add) || epi->add_c % 4 || epi->add_c < cout))
+        return einval("conv2d: addend must be 16-byte aligned, add_c a multiple of 4 and >= cout");
     switch (epi->mode) {
         case BVML_EPI_NHWC:
             if (epi->act < 0 || epi->act > 3) return einval("conv2d: unknown activation");
@@ -402,12 +402,12 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
                 epi->out_off + cout_pad > epi->out_c)
                 return einval("conv2d: bad NHWC output");
             break;
-        case BVML_EPI_NHWC_F32:
+        case BVML_EPI_C4_F32:
             if (epi->act < 0 || epi->act > 1)
-                return einval("conv2d: fp32 NHWC output takes no activation or ReLU");
+                return einval("conv2d: fp32 C4 output takes no activation or ReLU");
             if (!epi->out || !a16(epi->out) || epi->out_c % 4 || epi->out_off % 4 ||
                 epi->out_off + cout_pad > epi->out_c)
-                return einval("conv2d: bad NHWC fp32 output");
+                return einval("conv2d: bad C4 fp32 output");
             break;
         case BVML_EPI_PLANAR_F16:
         case BVML_EPI_PLANAR_F32:

@@ -62,7 +62,7 @@ struct ConvArgs {
     int hx_c;
     __nv_bfloat16* hin;
     int hin_c;
-    // optional per-pixel addend, planar: add[f * add_fs + c * H * W + y * W + x]
+    // optional per-pixel addend in channel groups of 4 (C4, see load_addend)
     const float* add;
     long add_fs;  // frame stride in floats (0: one frame shared by all)
     // shared-memory plan (see below)
@@ -79,27 +79,34 @@ __device__ __forceinline__ float activate(float v) {
     else return v;
 }
 
-// The addend of pixel (px, py) of frame b at channel cb (planar: channel
-// cb + i at ad[i * H * W]), or null. Lanes hold consecutive pixels, so each
-// channel's read is one coalesced row segment per warp.
-__device__ __forceinline__ const float* addend_at(const ConvArgs& a, int b, int px, int py,
-                                                  int cb) {
-    return a.add ? a.add + b * a.add_fs + (long)cb * a.H * a.W + (long)py * a.W + px : nullptr;
+// Channel-group layouts of the fp32 / bf16 per-pixel tensors the epilogues
+// read and write (the addend, the GRU state h32 and gate z): C4 fp32 is
+// [frame][C / 4][H][W][4], C8 bf16 is [frame][C / 8][H][W][8]. A thread owns
+// one pixel and moves 16 bytes per access; the lanes of a warp hold
+// consecutive pixels, so every access is one coalesced 512-byte segment.
+__device__ __forceinline__ long c4_index(const ConvArgs& a, long frame_groups, int b, int g,
+                                         int p) {
+    return ((long)b * frame_groups + g) * ((long)a.H * a.W) + p;
 }
 
-// The addend of one thread's pixel for channels cb .. cb+31 into t (zeros
+// The addend of one thread's pixel p for channels cb .. cb+31 into t (zeros
 // where there is none). Issued ahead of use: the epilogue loads chunk k + 1
 // while it finishes chunk k, and a tile's first chunk before waiting for its
-// accumulator, so the loads' latency overlaps other work. Channels past cout
-// re-read channel cout - 1 (always in bounds); pre_activation zeroes them.
-__device__ __forceinline__ void load_addend(const ConvArgs& a, bool in, int b, int px, int py,
-                                            int cb, float (&t)[32]) {
+// accumulator, so the loads' latency overlaps other work.
+__device__ __forceinline__ void load_addend(const ConvArgs& a, bool in, int b, int p, int cb,
+                                            float (&t)[32]) {
     if (a.add && in && cb < a.cout) {
-        const float* ad = addend_at(a, b, px, py, cb);
         const long hw = (long)a.H * a.W;
-        const int lim = a.cout - 1 - cb;
+        const float4* ad = reinterpret_cast<const float4*>(a.add + b * a.add_fs) +
+                           (long)(cb / 4) * hw + p;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) t[i] = __ldg(ad + (i < lim ? i : lim) * hw);
+        for (int q = 0; q < 8; ++q) {
+            const float4 v = cb + 4 * q < a.cout ? __ldg(ad + q * hw) : make_float4(0, 0, 0, 0);
+            t[4 * q + 0] = v.x;
+            t[4 * q + 1] = v.y;
+            t[4 * q + 2] = v.z;
+            t[4 * q + 3] = v.w;
+        }
     } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) t[i] = 0.0f;
@@ -125,26 +132,31 @@ __device__ __forceinline__ void pre_activation(const ConvArgs& a, const float* s
         if (cb + i >= a.cout) f[i] = 0.0f;
 }
 
-// Epilogue of one thread's pixel for 32 consecutive output channels
-// cb .. cb+31 (accumulators in v, plus bias and the optional addend at ad).
+// Epilogue of one thread's pixel p of frame b for 32 consecutive output
+// channels cb .. cb+31 (accumulators in v, plus bias and the addend t).
 // Modes (ConvEpi in bvml_internal.h):
-//  NHWC      act(v) as bf16 at out[pix * out_c + out_off + c], zeros past cout;
-//  NHWC32    the same in fp32;
+//  NHWC      act(v) as bf16 at out[pix * out_c + out_off + c], zeros past cout
+//            (through shared memory and TMA stores: nhwc_chunk_tma);
+//  C4_32     act(v) as fp32 in C4 layout, out_c channels per frame, at
+//            channel out_off + c;
 //  (PLANAR16/32: planar_chunk, through a shared-memory transpose)
-//  GRU_ZR    c < 64: z = sigmoid(v) -> z[pix * 64 + c];
-//            64 <= c < 128: r = sigmoid(v) -> rh[pix * rh_c + c - 64] = r * h32;
-//  GRU_Q     c < 64: q = tanh(v), h = (1 - z) h + z q -> h32 (fp32 state) and
-//            bf16 copies at hx[pix * hx_c + c] and, if set, hin[pix * hin_c + c]
+//  GRU_ZR    c < 64: z = sigmoid(v) -> z (C8 bf16, 64 channels);
+//            64 <= c < 128: r = sigmoid(v) -> rh[pix * rh_c + c - 64] = r * h,
+//            h from h32 (C4 fp32, 64 channels);
+//  GRU_Q     c < 64: q = tanh(v), h = (1 - z) h + z q -> h32 and bf16 copies
+//            at hx[pix * hx_c + c] and, if set, hin[pix * hin_c + c]
 //  (src/dsine_refine.cpp:140-158).
 template <int EPI, int ACT>
-__device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias, long pix,
+__device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias, int b, int p,
                                            int cb, const float (&t)[32],
                                            const uint32_t (&v)[32]) {
     float f[32];
     pre_activation(a, sbias, t, cb, v, f);
-    if constexpr (EPI == (int)ConvEpi::NHWC32) {
-        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + pix * a.out_c +
-                                                a.out_off + cb);
+    const long hw = (long)a.H * a.W;
+    const long pix = b * hw + p;
+    if constexpr (EPI == (int)ConvEpi::C4_32) {
+        float4* dst = reinterpret_cast<float4*>(a.out) +
+                      c4_index(a, a.out_c / 4, b, (a.out_off + cb) / 4, p);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
             float4 o;
@@ -152,7 +164,7 @@ __device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias
             o.y = cb + 4 * q + 1 < a.cout ? activate<ACT>(f[4 * q + 1]) : 0.0f;
             o.z = cb + 4 * q + 2 < a.cout ? activate<ACT>(f[4 * q + 2]) : 0.0f;
             o.w = cb + 4 * q + 3 < a.cout ? activate<ACT>(f[4 * q + 3]) : 0.0f;
-            dst[q] = o;
+            dst[q * hw] = o;
         }
     } else if constexpr (EPI == (int)ConvEpi::NHWC) {
         alignas(16) __nv_bfloat16 o[32];
@@ -169,14 +181,15 @@ __device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias
         if (cb < 64) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float2bfloat16_rn(activate<2>(f[i]));
-            uint4* dst = reinterpret_cast<uint4*>(a.z + pix * 64 + cb);
+            uint4* dst = reinterpret_cast<uint4*>(a.z) + c4_index(a, 8, b, cb / 8, p);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) dst[q] = reinterpret_cast<const uint4*>(o)[q];
+            for (int q = 0; q < 4; ++q) dst[q * hw] = reinterpret_cast<const uint4*>(o)[q];
         } else if (cb < 128) {
-            const float4* h4 = reinterpret_cast<const float4*>(a.h32 + pix * 64 + (cb - 64));
+            const float4* h4 =
+                reinterpret_cast<const float4*>(a.h32) + c4_index(a, 16, b, (cb - 64) / 4, p);
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-                const float4 h = h4[q];
+                const float4 h = h4[q * hw];
                 o[4 * q + 0] = __float2bfloat16_rn(activate<2>(f[4 * q + 0]) * h.x);
                 o[4 * q + 1] = __float2bfloat16_rn(activate<2>(f[4 * q + 1]) * h.y);
                 o[4 * q + 2] = __float2bfloat16_rn(activate<2>(f[4 * q + 2]) * h.z);
@@ -188,15 +201,15 @@ __device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias
         }
     } else if constexpr (EPI == (int)ConvEpi::GRU_Q) {
         if (cb >= 64) return;
-        float4* h4 = reinterpret_cast<float4*>(a.h32 + pix * 64 + cb);
-        const uint4* z4 = reinterpret_cast<const uint4*>(a.z + pix * 64 + cb);
+        float4* h4 = reinterpret_cast<float4*>(a.h32) + c4_index(a, 16, b, cb / 4, p);
+        const uint4* z4 = reinterpret_cast<const uint4*>(a.z) + c4_index(a, 8, b, cb / 8, p);
         alignas(16) __nv_bfloat16 zb[32];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) reinterpret_cast<uint4*>(zb)[q] = z4[q];
+        for (int q = 0; q < 4; ++q) reinterpret_cast<uint4*>(zb)[q] = z4[q * hw];
         alignas(16) __nv_bfloat16 o[32];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-            float4 h = h4[q];
+            float4 h = h4[q * hw];
             float* hh = reinterpret_cast<float*>(&h);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -205,7 +218,7 @@ __device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias
                 hh[e] = fmaf(z, tanhf(f[i]) - hh[e], hh[e]);  // (1 - z) h + z q
                 o[i] = __float2bfloat16_rn(hh[e]);
             }
-            h4[q] = h;
+            h4[q * hw] = h;
         }
         uint4* d1 = reinterpret_cast<uint4*>(a.hx + pix * a.hx_c + cb);
 #pragma unroll
@@ -550,7 +563,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             int ys, px, py, c0;
             bool in;
             geo(k, ys, px, py, in, c0);
-            load_addend(a, in, b, px, py, n0 + c0, tt);
+            load_addend(a, in, b, py * a.W + px, n0 + c0, tt);
         };
         auto process = [&](int k, int buf, const float (&tt)[32]) {
             int ys, px, py, c0;
@@ -582,7 +595,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 ++pcount;
             } else {
                 if (!in || cb >= a.cout_pad) return;
-                epilogue32<EPI, ACT>(a, sbias, ((long)b * a.H + py) * a.W + px, cb, tt, v);
+                epilogue32<EPI, ACT>(a, sbias, b, py * a.W + px, cb, tt, v);
             }
         };
         int tl = 0;
@@ -841,10 +854,10 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
                 case 3: return launch_act<(int)ConvEpi::NHWC, 3>(n, mt, bres, ma, mb, mo, a, smem, s);
                 default: return cudaErrorInvalidValue;
             }
-        case ConvEpi::NHWC32:
+        case ConvEpi::C4_32:
             switch (L.act) {
-                case 0: return launch_act<(int)ConvEpi::NHWC32, 0>(n, mt, bres, ma, mb, mo, a, smem, s);
-                case 1: return launch_act<(int)ConvEpi::NHWC32, 1>(n, mt, bres, ma, mb, mo, a, smem, s);
+                case 0: return launch_act<(int)ConvEpi::C4_32, 0>(n, mt, bres, ma, mb, mo, a, smem, s);
+                case 1: return launch_act<(int)ConvEpi::C4_32, 1>(n, mt, bres, ma, mb, mo, a, smem, s);
                 default: return cudaErrorInvalidValue;
             }
         case ConvEpi::PLANAR16: return launch_act<(int)ConvEpi::PLANAR16, 0>(n, mt, bres, ma, mb, mo, a, smem, s);

@@ -8,8 +8,8 @@ channel groups never change during a refinement: the decoder feature (64
 channels) and uv (2) are the same in every iteration, and uv is the same for
 every frame. So ``start`` convolves them once --
 
-  gx  = conv5x5([feat | uv], W_zr||q[:, 64:130])   (B,192,h,w) fp32 planar
-  gu  = conv3x3(uv, W_heads3x3[:, 64:66])          (1,512,h,w) fp32, shared
+  gx  = conv5x5([feat | uv], W_zr||q[:, 64:130])   (B,192/4,h,w,4) fp32 (C4)
+  gu  = conv3x3(uv, W_heads3x3[:, 64:66])          (1,512/4,h,w,4) fp32, shared
 
 -- and each iteration convolves only the hidden state, adding gx / gu in the
 epilogue (the same products, summed in another order):
@@ -39,8 +39,8 @@ from dataclasses import dataclass
 
 import torch
 
-from ._capi import EPI_GRU_Q, EPI_GRU_ZR, EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, \
-    ConvEpilogue, check, lib
+from ._capi import EPI_C4_F32, EPI_GRU_Q, EPI_GRU_ZR, EPI_NHWC, EPI_PLANAR_F16, \
+    EPI_PLANAR_F32, ConvEpilogue, check, lib
 from .ops import _cuda, _p, _stream, pack_conv_weight, pad64
 
 HEADS = (("prob_head", 25), ("xy_head", 50), ("angle_head", 25), ("up_prob_head", 576))
@@ -112,12 +112,14 @@ class RefineStage:
         self.b_c4 = [f32(params[f"{n}.4.bias"]) for n, _ in HEADS]
         bf = torch.bfloat16
         mk = lambda c, dt=bf, n=B: torch.zeros((n, h, w, c), device=d, dtype=dt)  # noqa: E731
-        self.hx, self.rhx, self.z = mk(H), mk(H), mk(H)      # h (bf16), r * h, z
-        self.h32 = mk(H, torch.float32)
+        self.hx, self.rhx = mk(H), mk(H)                     # h (bf16), r * h
+        # per-pixel epilogue tensors in channel groups (C8 bf16, C4 fp32)
+        self.z = torch.zeros((B, H // 8, h, w, 8), device=d, dtype=bf)
+        self.h32 = torch.zeros((B, H // 4, h, w, 4), device=d)
         self.fx, self.ux = mk(128), mk(64, n=1)              # [feat | uv], [uv]
-        # hoisted terms, planar fp32: the epilogues read them coalesced
-        self.gx = torch.zeros((B, 192, h, w), device=d)
-        self.gu = torch.zeros((1, 4 * HEAD_HIDDEN, h, w), device=d)
+        # hoisted terms, C4 fp32: the epilogues read them coalesced
+        self.gx = torch.zeros((B, 192 // 4, h, w, 4), device=d)
+        self.gu = torch.zeros((1, HEAD_HIDDEN, h, w, 4), device=d)
         self.t1, self.t2 = mk(4 * HEAD_HIDDEN), mk(4 * HEAD_HIDDEN)
         self.err = torch.zeros(1, device=d, dtype=torch.int32)
 
@@ -137,16 +139,17 @@ class RefineStage:
         _cuda("refine stage", h0, feat, uv)
         nhwc = lambda t: t.permute(0, 2, 3, 1)  # noqa: E731
         uvn = uv.permute(1, 2, 0)[None].to(torch.bfloat16)
-        self.h32.copy_(nhwc(h0))
-        self.hx.copy_(self.h32)
+        h0 = h0.float()
+        self.h32.copy_(h0.reshape(self.B, HIDDEN // 4, 4, self.h, self.w).permute(0, 1, 3, 4, 2))
+        self.hx.copy_(nhwc(h0))
         self.fx[..., :FEATURE] = nhwc(feat)
         self.fx[..., FEATURE:FEATURE + 2] = uvn
         self.ux[..., :2] = uvn
         with torch.cuda.device(self.dev):
-            self._conv(self.fx, 0, 128, self.w_gx, self.zeros, 192, 5, mode=EPI_PLANAR_F32,
-                       out=self.gx)
+            self._conv(self.fx, 0, 128, self.w_gx, self.zeros, 192, 5, mode=EPI_C4_F32,
+                       out=self.gx, out_c=192, out_off=0)
             self._conv(self.ux, 0, 64, self.w_gu, self.zeros, 4 * HEAD_HIDDEN, 3,
-                       mode=EPI_PLANAR_F32, out=self.gu)
+                       mode=EPI_C4_F32, out=self.gu, out_c=4 * HEAD_HIDDEN, out_off=0)
 
     def step(self, out: StageOutputs | None = None) -> StageOutputs:
         """One iteration: GRU update, then the four heads' raw outputs."""
@@ -159,7 +162,7 @@ class RefineStage:
             self._conv(self.hx, 0, HIDDEN, self.w_zr, self.b_zr, 128, 5, mode=EPI_GRU_ZR,
                        h32=self.h32, z=self.z, rh=self.rhx, rh_c=HIDDEN, add=self.gx, add_c=192)
             self._conv(self.rhx, 0, HIDDEN, self.w_q, self.b_q, 64, 5, mode=EPI_GRU_Q,
-                       h32=self.h32, z=self.z, hx=self.hx, hx_c=HIDDEN, add=self.gx[:, 128:],
+                       h32=self.h32, z=self.z, hx=self.hx, hx_c=HIDDEN, add=self.gx[:, 32:],
                        add_c=192)
             self._conv(self.hx, 0, HIDDEN, self.w_c0, self.b_c0, 4 * HEAD_HIDDEN, 3,
                        mode=EPI_NHWC, act=1, out=self.t1, out_c=4 * HEAD_HIDDEN, out_off=0,

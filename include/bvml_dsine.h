@@ -216,28 +216,33 @@ int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B
 #define BVML_EPI_PLANAR_F32 2  /* the same in fp32 */
 #define BVML_EPI_GRU_ZR 3      /* ConvGRU gates z, r (cout = 128: z then r) */
 #define BVML_EPI_GRU_Q 4       /* ConvGRU candidate and update (cout = 64) */
-#define BVML_EPI_NHWC_F32 5    /* act(conv) as fp32 at out[pixel * out_c + out_off + o]
+#define BVML_EPI_C4_F32 5      /* act(conv) as fp32 in channel groups of 4 (C4, below),
+                                  out_c channels per frame, at channel out_off + o
                                   (act 0 or 1; out_c, out_off multiples of 4) */
 
 /*
  * Where and how bvml_conv2d_nhwc_bf16_ex writes its result. Channel strides
  * and offsets in elements, multiples of 8; tensors 16-byte aligned.
+ * Channel-group layouts: C4 fp32 = [frame][C / 4][H][W][4] (channel c of
+ * pixel (y, x) at ((f * C / 4 + c / 4) * H * W + y * W + x) * 4 + c % 4), C8
+ * bf16 the same with groups of 8 -- 16 bytes per pixel and group, so the
+ * epilogue's per-pixel reads and writes are coalesced.
  * GRU_ZR (src/dsine_refine.cpp:144-147): z = sigmoid(conv[0:64]) -> z
- *   (B,H,W,64) bf16; r = sigmoid(conv[64:128]) -> rh[pixel * rh_c + o] = r * h,
- *   h the fp32 hidden state h32 (B,H,W,64).
+ *   (C8 bf16, 64 channels); r = sigmoid(conv[64:128]) -> rh[pixel * rh_c +
+ *   o] = r * h, h the fp32 hidden state h32 (C4, 64 channels).
  * GRU_Q (:148-156): q = tanh(conv) -> h32 = (1 - z) h32 + z q, with bf16
  *   copies at hx[pixel * hx_c + o] and, when hin is not null, hin[...].
- * add (optional, every mode): a per-pixel fp32 addend, planar,
- *   add[(f * add_c + o) * H * W + y * W + x] joins conv[o] + bias[o] before
- *   the epilogue, with f = the frame (f = 0 for every frame when add_shared
- *   is nonzero) and add_c >= cout channel planes per frame. It carries the part of a
+ * add (optional, every mode): a per-pixel fp32 addend in C4 layout with
+ *   add_c channels per frame (a multiple of 4, >= cout); channel o of frame f
+ *   (f = 0 for every frame when add_shared is nonzero) joins conv[o] +
+ *   bias[o] before the epilogue. It carries the part of a
  *   convolution whose input does not change between calls: the ConvGRU's
  *   feature and uv channels, the heads' uv channels, which the refine stage
  *   convolves once per refinement instead of once per iteration.
  */
 typedef struct {
     int mode;
-    int act;             /* NHWC: 0 none, 1 ReLU, 2 sigmoid, 3 tanh; NHWC_F32: 0, 1 */
+    int act;             /* NHWC: 0 none, 1 ReLU, 2 sigmoid, 3 tanh; C4_F32: 0, 1 */
     void* out;
     int out_c, out_off;
     float* h32;

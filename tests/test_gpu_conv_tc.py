@@ -63,14 +63,14 @@ def test_conv_shapes(B, H, W, cin, cout, ks, act):
 
 @pytest.mark.parametrize("shared", [False, True])
 def test_conv_addend_and_fp32_output(shared):
-    """The planar per-pixel addend (per frame, or one frame shared by all)
-    joins conv + bias before the activation; fp32 NHWC output
-    (bvml_conv2d_nhwc_bf16_ex with BVML_EPI_NHWC_F32): the refine stage's
+    """The per-pixel addend (C4 fp32; per frame, or one frame shared by
+    all) joins conv + bias before the activation; fp32 C4 output
+    (bvml_conv2d_nhwc_bf16_ex with BVML_EPI_C4_F32): the refine stage's
     hoisted feature / uv terms."""
     import ctypes
 
     import brovisionml_b200 as b
-    from brovisionml_b200._capi import EPI_NHWC_F32, ConvEpilogue, check, lib
+    from brovisionml_b200._capi import EPI_C4_F32, ConvEpilogue, check, lib
     from brovisionml_b200.ops import _p, _stream
 
     B, H, W, cin, cout, ks = 2, 19, 40, 64, 192, 5
@@ -78,18 +78,18 @@ def test_conv_addend_and_fp32_output(shared):
     x = torch.randn((B, H, W, cin), device="cuda", generator=g).to(torch.bfloat16)
     weight = torch.randn((cout, cin, ks, ks), device="cuda", generator=g) * (cin * ks * ks) ** -0.5
     bias = torch.randn(cout, device="cuda", generator=g) * 0.1
-    add = torch.randn((1 if shared else B, cout + 8, H, W), device="cuda", generator=g)
-    y = torch.full((B, H, W, cout), float("nan"), device="cuda")
+    add = torch.randn((1 if shared else B, (cout + 8) // 4, H, W, 4), device="cuda", generator=g)
+    y = torch.full((B, cout // 4, H, W, 4), float("nan"), device="cuda")
     err = torch.zeros(1, device="cuda", dtype=torch.int32)
-    e = ConvEpilogue(mode=EPI_NHWC_F32, act=1, out=_p(y), out_c=cout, out_off=0,
+    e = ConvEpilogue(mode=EPI_C4_F32, act=1, out=_p(y), out_c=cout, out_off=0,
                      add=_p(add), add_c=cout + 8, add_shared=int(shared))
     check(lib.bvml_conv2d_nhwc_bf16_ex(_p(x), cin, 0, cin, _p(b.pack_conv_weight(weight)),
                                        _p(bias), B, H, W, cout, cout, ks, ctypes.byref(e),
                                        _p(err), _stream(torch.device("cuda"))))
     torch.cuda.synchronize()
     assert int(err.item()) == 0
-    ref = ref_conv(x, weight, bias, ks, "none", cin) + add[:, :cout].permute(0, 2, 3, 1)
-    ref = torch.relu(ref)
-    d = (y - ref).abs().max().item()
+    c4 = lambda t: t.permute(0, 2, 3, 1, 4).reshape(t.shape[0], H, W, -1)  # noqa: E731
+    ref = torch.relu(ref_conv(x, weight, bias, ks, "none", cin) + c4(add)[..., :cout])
+    d = (c4(y) - ref).abs().max().item()
     print(f"conv addend shared={shared}: max_abs {d:.2e}")
     assert d <= 1e-3  # fp32 output: summation order only
