@@ -289,11 +289,12 @@ def stage_flops_per_px(iters: int) -> float:
 
 def stage_executed_flops(iters: int, B: int, h: int, w: int) -> float:
     """FLOPs the tensor cores run for the same result (unpadded channels): the
-    fixed inputs' terms once (feat + uv 66 -> 192 over 5x5 per frame, uv
-    2 -> 512 over 3x3 once), then per iteration only the hidden state
+    fixed inputs' terms once (feat 64 -> 192 over 5x5 per frame; uv 2 -> 192
+    over 5x5 and 2 -> 512 over 3x3 once for all frames), then per iteration
+    only the hidden state
     (64 -> 192 over 5x5, 64 -> 512 over 3x3) and the 1x1 layers."""
     px = B * h * w
-    once = 2 * 192 * 66 * 25 * px + 2 * 512 * 2 * 9 * h * w
+    once = 2 * 192 * 64 * 25 * px + (2 * 192 * 2 * 25 + 2 * 512 * 2 * 9) * h * w
     it = 2 * 192 * 64 * 25 + 2 * 512 * 64 * 9 + 4 * 2 * 128 * 128 + 2 * 128 * 676
     return float(once + iters * it * px)
 
@@ -385,7 +386,7 @@ def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
         "data": "synthetic (random weights of the reference's shapes, seeded inputs)",
         "config": workload_config(args, cfg, {"stage": "ConvGRU 5x5 130->64 x3, 4 heads "
                                               "(3x3 66->128, 1x1 128->128, 1x1 128->out)"}),
-        "gpu_launches": args.steps * (2 + 11 * I + I + 1),
+        "gpu_launches": args.steps * (3 + 11 * I + I + 1),
         "stage": {"ms": round(stage_ms, 3), "tflops_model": round(tflops, 1),
                   "flops_model_per_step": flops, "tflops_executed": round(tflops_x, 1),
                   "flops_executed_per_step": flops_x},

@@ -332,8 +332,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                const __grid_constant__ CUtensorMap map_o, const ConvArgs a) {
     constexpr bool kPlanar = EPI == (int)ConvEpi::PLANAR16 || EPI == (int)ConvEpi::PLANAR32;
     constexpr bool kStaged = kPlanar || EPI == (int)ConvEpi::NHWC;  // TMA-store epilogues
-    constexpr int kCols = 2 * MT * N;  // TMEM columns: two accumulator sets
-    static_assert(kCols <= 512 && (kCols & (kCols - 1)) == 0, "TMEM allocation");
+    // TMEM columns: two accumulator sets, allocated as a power of two >= 32
+    constexpr int kCols = 2 * MT * N <= 128 ? 128 : (2 * MT * N <= 256 ? 256 : 512);
+    static_assert(2 * MT * N <= 512, "TMEM allocation");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -682,11 +683,13 @@ cudaError_t launch_act(int n, int mt, bool bres, const CUtensorMap& ma, const CU
     if (bres) {
         switch (n) {
             case 256: return launch_n<256, 1, EPI, ACT, true>(ma, mb, mo, a, smem, s);
+            case 192: return launch_n<192, 1, EPI, ACT, true>(ma, mb, mo, a, smem, s);
             case 128: return launch_n<128, 1, EPI, ACT, true>(ma, mb, mo, a, smem, s);
             default: return launch_n<64, 1, EPI, ACT, true>(ma, mb, mo, a, smem, s);
         }
     }
     if (n == 256) return launch_n<256, 1, EPI, ACT, false>(ma, mb, mo, a, smem, s);
+    if (n == 192) return launch_n<192, 1, EPI, ACT, false>(ma, mb, mo, a, smem, s);
     if (n == 128) {
         if (mt == 2) return launch_n<128, 2, EPI, ACT, false>(ma, mb, mo, a, smem, s);
         return launch_n<128, 1, EPI, ACT, false>(ma, mb, mo, a, smem, s);
@@ -788,10 +791,23 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     // one CTA (z with r, q with z). Filters wider than 1x1 with N < 256 use 2
     // or 4 sub-tiles per CTA tile, so one weight tile feeds 256 or 512 pixels
     // and the halo tile is shared by more filter rows.
-    int n = L.cout_pad >= 256 ? 256 : (L.cout_pad >= 128 ? 128 : 64);
+    // Among 256, 192, 128, 64 (in that order of preference) the N that pads
+    // cout_pad the least: 576 channels as 3 x 192, not 256 + 256 + 64.
+    int n = 64;
+    {
+        long waste = -1;
+        for (int cand : {256, 192, 128, 64}) {
+            if (cand > 64 && cand > L.cout_pad) continue;
+            const long w = (long)(L.cout_pad + cand - 1) / cand * cand - L.cout_pad;
+            if (waste < 0 || w < waste) {
+                waste = w;
+                n = cand;
+            }
+        }
+    }
     if (L.epi == ConvEpi::GRU_ZR) n = 128;
     if (L.epi == ConvEpi::GRU_Q) n = 64;
-    int mt = L.ks == 1 || n == 256 ? 1 : (n == 128 ? 2 : 4);
+    int mt = L.ks == 1 || n >= 192 ? 1 : (n == 128 ? 2 : 4);
     const bool bres = L.ks == 1 && L.cin_pad <= kBResChunks * kKC;
     const bool planar = L.epi == ConvEpi::PLANAR16 || L.epi == ConvEpi::PLANAR32;
     const int es = L.epi == ConvEpi::PLANAR16 ? 2 : 4;

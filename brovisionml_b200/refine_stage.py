@@ -8,7 +8,8 @@ channel groups never change during a refinement: the decoder feature (64
 channels) and uv (2) are the same in every iteration, and uv is the same for
 every frame. So ``start`` convolves them once --
 
-  gx  = conv5x5([feat | uv], W_zr||q[:, 64:130])   (B,192/4,h,w,4) fp32 (C4)
+  gxu = conv5x5(uv, W_zr||q[:, 128:130])          (1,192/4,h,w,4) fp32 (C4), shared
+  gx  = conv5x5(feat, W_zr||q[:, 64:128]) + gxu    (B,192/4,h,w,4) fp32 (C4)
   gu  = conv3x3(uv, W_heads3x3[:, 64:66])          (1,512/4,h,w,4) fp32, shared
 
 -- and each iteration convolves only the hidden state, adding gx / gu in the
@@ -24,7 +25,7 @@ epilogue (the same products, summed in another order):
          (fp16 or fp32): prob (25), xy (50), angle (25), up_mask (576) logits.
 
 (The GRU and heads never read the normals, so all iterations run first and
-the ops unit consumes their outputs afterwards.) 2 tensor-core launches per
+the ops unit consumes their outputs afterwards.) 3 tensor-core launches per
 refinement plus 11 per iteration, no separate elementwise or layout pass;
 the 5x5 GEMMs contract 25 x 64 instead of 25 x 130 (padded: 192) channels,
 the heads' 3x3 9 x 64 instead of 9 x 66 (padded: 128). Weights are the
@@ -102,7 +103,9 @@ class RefineStage:
         self.w_c0 = pack_conv_weight(c0[:, :H], H, 4 * HEAD_HIDDEN)
         self.b_c0 = f32(torch.cat([params[f"{n}.0.bias"] for n, _ in HEADS]))
         # the fixed inputs' parts: feat + uv -> z, r, q; uv -> the heads' 3x3
-        self.w_gx = pack_conv_weight(torch.cat([wz, wr, wq])[:, H:], 128, 192)
+        wg = torch.cat([wz, wr, wq])
+        self.w_gx = pack_conv_weight(wg[:, H:H + FEATURE], 64, 192)
+        self.w_gxu = pack_conv_weight(wg[:, H + FEATURE:], 64, 192)
         self.w_gu = pack_conv_weight(c0[:, H:], 64, 4 * HEAD_HIDDEN)
         self.zeros = torch.zeros(4 * HEAD_HIDDEN, device=d)
         self.w_c2 = [pack_conv_weight(params[f"{n}.2.weight"].to(d), 128, 128) for n, _ in HEADS]
@@ -116,9 +119,10 @@ class RefineStage:
         # per-pixel epilogue tensors in channel groups (C8 bf16, C4 fp32)
         self.z = torch.zeros((B, H // 8, h, w, 8), device=d, dtype=bf)
         self.h32 = torch.zeros((B, H // 4, h, w, 4), device=d)
-        self.fx, self.ux = mk(128), mk(64, n=1)              # [feat | uv], [uv]
+        self.fx, self.ux = mk(FEATURE), mk(64, n=1)          # feat, [uv | 0]
         # hoisted terms, C4 fp32: the epilogues read them coalesced
         self.gx = torch.zeros((B, 192 // 4, h, w, 4), device=d)
+        self.gxu = torch.zeros((1, 192 // 4, h, w, 4), device=d)
         self.gu = torch.zeros((1, HEAD_HIDDEN, h, w, 4), device=d)
         self.t1, self.t2 = mk(4 * HEAD_HIDDEN), mk(4 * HEAD_HIDDEN)
         self.err = torch.zeros(1, device=d, dtype=torch.int32)
@@ -135,19 +139,21 @@ class RefineStage:
     def start(self, h0: torch.Tensor, feat: torch.Tensor, uv: torch.Tensor) -> None:
         """Load the decoder's hidden state h0 (B,64,h,w), feature (B,64,h,w)
         and uv (2,h,w) (src/dsine_refine.cpp:245-248), and convolve the fixed
-        inputs once (two launches)."""
+        inputs once (three launches)."""
         _cuda("refine stage", h0, feat, uv)
         nhwc = lambda t: t.permute(0, 2, 3, 1)  # noqa: E731
         uvn = uv.permute(1, 2, 0)[None].to(torch.bfloat16)
         h0 = h0.float()
         self.h32.copy_(h0.reshape(self.B, HIDDEN // 4, 4, self.h, self.w).permute(0, 1, 3, 4, 2))
         self.hx.copy_(nhwc(h0))
-        self.fx[..., :FEATURE] = nhwc(feat)
-        self.fx[..., FEATURE:FEATURE + 2] = uvn
+        self.fx.copy_(nhwc(feat))
         self.ux[..., :2] = uvn
         with torch.cuda.device(self.dev):
-            self._conv(self.fx, 0, 128, self.w_gx, self.zeros, 192, 5, mode=EPI_C4_F32,
-                       out=self.gx, out_c=192, out_off=0)
+            self._conv(self.ux, 0, 64, self.w_gxu, self.zeros, 192, 5, mode=EPI_C4_F32,
+                       out=self.gxu, out_c=192, out_off=0)
+            self._conv(self.fx, 0, 64, self.w_gx, self.zeros, 192, 5, mode=EPI_C4_F32,
+                       out=self.gx, out_c=192, out_off=0, add=self.gxu, add_c=192,
+                       add_shared=1)
             self._conv(self.ux, 0, 64, self.w_gu, self.zeros, 4 * HEAD_HIDDEN, 3,
                        mode=EPI_C4_F32, out=self.gu, out_c=4 * HEAD_HIDDEN, out_off=0)
 
@@ -221,9 +227,9 @@ def _main(argv=None) -> None:
     run `steps` iterations of the stage on random weights over B frames of
     the 160 x 90 grid (720p) and print each launch's time of the last
     iteration (CUDA events). Also the target for profiling one layer: after
-    the two launches of start (the hoisted terms), the launches of iteration
-    k are numbers 2 + 11 k .. 12 + 11 k (zr, q, heads 3x3, then per head 1x1
-    and 1x1 planar)."""
+    the three launches of start (the hoisted terms), the launches of
+    iteration k are numbers 3 + 11 k .. 13 + 11 k (zr, q, heads 3x3, then per
+    head 1x1 and 1x1 planar)."""
     import argparse
 
     ap = argparse.ArgumentParser()
@@ -242,6 +248,10 @@ def _main(argv=None) -> None:
                             indexing="ij")
     uv = torch.stack([((xs + 0.5) - w / 2) / (0.8 * w), ((ys + 0.5) - h / 2) / (0.8 * w)])
     st.start(h0, feat, uv.float())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    st.start(h0, feat, uv.float())
+    e1.record()
     marks = []
     conv = st._conv
 
@@ -259,7 +269,8 @@ def _main(argv=None) -> None:
     torch.cuda.synchronize()
     st.check_pipeline()
     names = ["zr", "q", "heads3x3"] + [f"{n}.{i}" for n, _ in HEADS for i in (2, 4)]
-    print(" ".join(f"{n} {a.elapsed_time(b):.3f}" for n, (a, b) in zip(names, marks)))
+    print(f"start {e0.elapsed_time(e1):.3f} " +
+          " ".join(f"{n} {a.elapsed_time(b):.3f}" for n, (a, b) in zip(names, marks)))
 
 
 if __name__ == "__main__":
