@@ -62,6 +62,7 @@ struct ConvArgs {
     int hx_c;
     __nv_bfloat16* hin;
     int hin_c;
+    int obox;     // NHWC outputs: channels per TMA store (64: two chunks, 128-byte rows)
     // optional per-pixel addend in channel groups of 4 (C4, see load_addend)
     const float* add;
     long add_fs;  // frame stride in floats (0: one frame shared by all)
@@ -135,8 +136,8 @@ __device__ __forceinline__ void pre_activation(const ConvArgs& a, const float* s
 // Epilogue of one thread's pixel p of frame b for 32 consecutive output
 // channels cb .. cb+31 (accumulators in v, plus bias and the addend t).
 // Modes (ConvEpi in bvml_internal.h):
-//  NHWC      act(v) as bf16 at out[pix * out_c + out_off + c], zeros past cout
-//            (through shared memory and TMA stores: nhwc_chunk_tma);
+//  (NHWC: act(v) as bf16 at out[pix * out_c + out_off + c], zeros past cout,
+//  through shared memory and TMA stores: nhwc_chunk_tma, nhwc_pair_tma)
 //  C4_32     act(v) as fp32 in C4 layout, out_c channels per frame, at
 //            channel out_off + c;
 //  (PLANAR16/32: planar_chunk, through a shared-memory transpose)
@@ -166,16 +167,6 @@ __device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias
             o.w = cb + 4 * q + 3 < a.cout ? activate<ACT>(f[4 * q + 3]) : 0.0f;
             dst[q * hw] = o;
         }
-    } else if constexpr (EPI == (int)ConvEpi::NHWC) {
-        alignas(16) __nv_bfloat16 o[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-            o[i] = __float2bfloat16_rn(cb + i < a.cout ? activate<ACT>(f[i]) : 0.0f);
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) +
-                                              pix * a.out_c + a.out_off + cb);
-        const uint4* src = reinterpret_cast<const uint4*>(o);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) dst[q] = src[q];
     } else if constexpr (EPI == (int)ConvEpi::GRU_ZR) {
         alignas(16) __nv_bfloat16 o[32];
         if (cb < 64) {
@@ -317,6 +308,45 @@ __device__ __forceinline__ void nhwc_chunk_tma(const ConvArgs& a, const CUtensor
     if (lane == 0) {
         tc::tma_store_4d(map_o, stg_addr, c0, px0, py0, b);
         tc::bulk_commit();
+    }
+}
+
+// NHWC bf16 output of two consecutive 32-channel chunks (half 0: channels
+// cb .. cb+31, half 1: the next 32) of one epilogue warp's 32 pixels, stored
+// as one box of 64 channels: 128-byte rows, half as many as 32-channel boxes
+// (the TMA store engine's cost is per row). Lane r writes its half row into
+// row r of one of the warp's two 4 KB staging buffers (alternating per
+// pair) in the 128-byte swizzle (16-byte unit u at u ^ (r & 7)); lane 0
+// stores after half 1, and waits before half 0 until the store that used
+// this buffer two pairs ago has read it.
+template <int ACT>
+__device__ __forceinline__ void nhwc_pair_tma(const ConvArgs& a, const CUtensorMap* map_o,
+                                              uint8_t* stg, uint32_t stg_addr, int lane, int half,
+                                              int c0, int px0, int py0, int b, int cb,
+                                              const float* sbias, const float (&t)[32],
+                                              const uint32_t (&v)[32]) {
+    float f[32];
+    pre_activation(a, sbias, t, cb, v, f);
+    alignas(16) __nv_bfloat16 o[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        o[i] = __float2bfloat16_rn(cb + i < a.cout ? activate<ACT>(f[i]) : 0.0f);
+    if (half == 0) {
+        if (lane == 0) tc::bulk_wait_read<1>();  // this buffer's previous store has read it
+        __syncwarp();
+    }
+    const int sw = lane & 7;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4*>(stg + lane * 128 + (((half * 4 + q) ^ sw) << 4)) =
+            reinterpret_cast<const uint4*>(o)[q];
+    if (half == 1) {
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            tc::tma_store_4d(map_o, stg_addr, c0 - 32, px0, py0, b);
+            tc::bulk_commit();
+        }
     }
 }
 
@@ -581,6 +611,16 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 // pw x ph box (pw = min(tw, 32))
                 const int px0 = x0 + (wq * 32) % a.tw, py0 = ys + (wq * 32) / a.tw;
                 if (px0 >= a.W || py0 >= a.H) return;  // the whole box is off the frame
+                if constexpr (EPI == (int)ConvEpi::NHWC) {
+                    if (a.obox == 64) {  // chunk pairs share a 4 KB buffer and one store
+                        const int wbase = ((warp - 2) * 2 + ((pcount >> 1) & 1)) * 4096;
+                        nhwc_pair_tma<ACT>(a, &map_o, smem + a.off_out + wbase,
+                                           sbase + a.off_out + wbase, lane, (c0 >> 5) & 1,
+                                           a.out_off + cb, px0, py0, b, cb, sbias, tt, v);
+                        ++pcount;
+                        return;
+                    }
+                }
                 const int slot = (warp - 2) * 2 + (pcount & 1);
                 uint8_t* stg = smem + a.off_out + slot * stage_warp_bytes(EPI);
                 const uint32_t stg_addr = sbase + a.off_out + slot * stage_warp_bytes(EPI);
@@ -811,7 +851,9 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     const bool bres = L.ks == 1 && L.cin_pad <= kBResChunks * kKC;
     const bool planar = L.epi == ConvEpi::PLANAR16 || L.epi == ConvEpi::PLANAR32;
     const int es = L.epi == ConvEpi::PLANAR16 ? 2 : 4;
-    const int out_bytes = planar || L.epi == ConvEpi::NHWC
+    const bool obox64 = L.epi == ConvEpi::NHWC && bres && n != 64 && n != 192;
+    const int out_bytes = obox64 ? kEpiWarps * 2 * 4096
+                          : planar || L.epi == ConvEpi::NHWC
                               ? kEpiWarps * 2 * stage_warp_bytes((int)L.epi) : 0;
     const int smem = plan_conv(a, n, mt, bres, out_bytes);
     if (smem == 0) return cudaErrorInvalidConfiguration;
@@ -850,15 +892,19 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
             return cudaErrorInvalidValue;
     } else if (L.epi == ConvEpi::NHWC) {
         // NHWC bf16: a 4-D map (out_c, W, H, B); each epilogue warp stores
-        // 32 channels x pw x ph pixels, 64-byte swizzled in shared memory
+        // obox channels x pw x ph pixels, 64- or 128-byte swizzled in shared
+        // memory. 64-channel boxes (two 4 KB buffers per warp) for the 1x1
+        // layers, whose shared memory has room; they need every warp's
+        // column range to be whole chunk pairs (not so for N = 64 or 192).
+        a.obox = bres && n != 64 && n != 192 ? 64 : 32;
         const int pw = a.tw < 32 ? a.tw : 32;
         const cuuint64_t dims_o[4] = {(cuuint64_t)L.out_c, (cuuint64_t)L.W, (cuuint64_t)L.H,
                                       (cuuint64_t)L.B};
         const cuuint64_t str_o[3] = {(cuuint64_t)L.out_c * 2, (cuuint64_t)L.W * L.out_c * 2,
                                      (cuuint64_t)L.H * L.W * L.out_c * 2};
-        const cuuint32_t box_o[4] = {32, (cuuint32_t)pw, (cuuint32_t)(32 / pw), 1};
+        const cuuint32_t box_o[4] = {(cuuint32_t)a.obox, (cuuint32_t)pw, (cuuint32_t)(32 / pw), 1};
         if (!encode(&mo, L.y, 4, dims_o, str_o, box_o, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                    CU_TENSOR_MAP_SWIZZLE_64B))
+                    a.obox == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
             return cudaErrorInvalidValue;
     }
     switch (L.epi) {

@@ -226,10 +226,10 @@ def _main(argv=None) -> None:
     """`python -m brovisionml_b200.refine_stage [--frames B] [--steps K]`:
     run `steps` iterations of the stage on random weights over B frames of
     the 160 x 90 grid (720p) and print each launch's time of the last
-    iteration (CUDA events). Also the target for profiling one layer: after
-    the three launches of start (the hoisted terms), the launches of
-    iteration k are numbers 3 + 11 k .. 13 + 11 k (zr, q, heads 3x3, then per
-    head 1x1 and 1x1 planar)."""
+    iteration and of start (CUDA events). Also the target for profiling one
+    layer: start runs twice (3 launches each, the second one timed), then the
+    launches of iteration k are numbers 6 + 11 k .. 16 + 11 k (zr, q, heads
+    3x3, then per head 1x1 and 1x1 planar)."""
     import argparse
 
     ap = argparse.ArgumentParser()
