@@ -290,13 +290,15 @@ def stage_flops_per_px(iters: int) -> float:
 def stage_executed_flops(iters: int, B: int, h: int, w: int) -> float:
     """FLOPs the tensor cores run for the same result (unpadded channels): the
     fixed inputs' terms once (feat 64 -> 192 over 5x5 per frame; uv 2 -> 192
-    over 5x5 and 2 -> 512 over 3x3 once for all frames), then per iteration
-    only the hidden state
+    over 5x5 and 2 -> 512 over 3x3 once for all frames), the up-mask head
+    only in the last iteration (the only upsample that reaches the output),
+    and per iteration only the hidden state
     (64 -> 192 over 5x5, 64 -> 512 over 3x3) and the 1x1 layers."""
     px = B * h * w
     once = 2 * 192 * 64 * 25 * px + (2 * 192 * 2 * 25 + 2 * 512 * 2 * 9) * h * w
-    it = 2 * 192 * 64 * 25 + 2 * 512 * 64 * 9 + 4 * 2 * 128 * 128 + 2 * 128 * 676
-    return float(once + iters * it * px)
+    it = 2 * 192 * 64 * 25 + 2 * 512 * 64 * 9 + 3 * 2 * 128 * 128 + 2 * 128 * 100
+    mask = 2 * 128 * 128 + 2 * 128 * 576  # the up-mask head, last iteration only
+    return float(once + (iters * it + mask) * px)
 
 
 def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
@@ -323,15 +325,16 @@ def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
                                        dim=1).to(dt)
     st = RefineStage(random_params(device, seed=7), B, h, w, device=device, out_dtype=dt)
     mk = lambda c: torch.empty((B, c, h, w), device=device, dtype=dt)  # noqa: E731
-    outs = [StageOutputs(mk(25), mk(50), mk(25), mk(576)) for _ in range(I)]
+    outs = [StageOutputs(mk(25), mk(50), mk(25), mk(576) if i == I - 1 else None)
+            for i in range(I)]
     res = torch.empty((B, 3, H, W), device=device, dtype=dt)
     ws = torch.empty(bv.refine_workspace_bytes(B, h, w), device=device, dtype=torch.uint8)
     stream = torch.cuda.Stream(device)
 
     def stage():
         st.start(h0, feat, uv)
-        for i in range(I):
-            st.step(outs[i])
+        for i in range(I):  # only the last iteration's up-mask reaches the output
+            st.step(outs[i], up_mask=i == I - 1)
 
     def ops():
         bv.refine(n0, [o.prob for o in outs], [o.xy for o in outs], [o.angle for o in outs],
@@ -386,7 +389,7 @@ def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
         "data": "synthetic (random weights of the reference's shapes, seeded inputs)",
         "config": workload_config(args, cfg, {"stage": "ConvGRU 5x5 130->64 x3, 4 heads "
                                               "(3x3 66->128, 1x1 128->128, 1x1 128->out)"}),
-        "gpu_launches": args.steps * (3 + 11 * I + I + 1),
+        "gpu_launches": args.steps * (3 + 9 * I + 2 + I + 1),
         "stage": {"ms": round(stage_ms, 3), "tflops_model": round(tflops, 1),
                   "flops_model_per_step": flops, "tflops_executed": round(tflops_x, 1),
                   "flops_executed_per_step": flops_x},

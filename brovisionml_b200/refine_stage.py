@@ -73,11 +73,12 @@ def random_params(device, seed: int = 0) -> dict[str, torch.Tensor]:
 
 @dataclass
 class StageOutputs:
-    """Raw head outputs of one iteration, planar (B,C,h,w)."""
+    """Raw head outputs of one iteration, planar (B,C,h,w). up_mask is None
+    for an iteration run with ``up_mask=False``."""
     prob: torch.Tensor
     xy: torch.Tensor
     angle: torch.Tensor
-    up_mask: torch.Tensor
+    up_mask: torch.Tensor | None
 
 
 class RefineStage:
@@ -157,13 +158,19 @@ class RefineStage:
             self._conv(self.ux, 0, 64, self.w_gu, self.zeros, 4 * HEAD_HIDDEN, 3,
                        mode=EPI_C4_F32, out=self.gu, out_c=4 * HEAD_HIDDEN, out_off=0)
 
-    def step(self, out: StageOutputs | None = None) -> StageOutputs:
-        """One iteration: GRU update, then the four heads' raw outputs."""
+    def step(self, out: StageOutputs | None = None, up_mask: bool = True) -> StageOutputs:
+        """One iteration: GRU update, then the heads' raw outputs. The
+        up-mask head feeds only the convex upsample, and only the last
+        iteration's upsample reaches the refined normal
+        (src/dsine_refine.cpp:270-282): iterations before the last can pass
+        up_mask=False and skip its two launches (the 576-channel layer is the
+        stage's largest output)."""
         B, h, w = self.B, self.h, self.w
         if out is None:
             mk = lambda c: torch.empty((B, c, h, w), device=self.dev,  # noqa: E731
                                        dtype=self.out_dtype)
-            out = StageOutputs(*(mk(c) for _, c in HEADS))
+            out = StageOutputs(*(mk(c) if up_mask or name != "up_prob_head" else None
+                                 for name, c in HEADS))
         with torch.cuda.device(self.dev):
             self._conv(self.hx, 0, HIDDEN, self.w_zr, self.b_zr, 128, 5, mode=EPI_GRU_ZR,
                        h32=self.h32, z=self.z, rh=self.rhx, rh_c=HIDDEN, add=self.gx, add_c=192)
@@ -175,7 +182,9 @@ class RefineStage:
                        add=self.gu, add_c=4 * HEAD_HIDDEN, add_shared=1)
             planar = EPI_PLANAR_F16 if self.out_dtype == torch.float16 else EPI_PLANAR_F32
             dsts = (out.prob, out.xy, out.angle, out.up_mask)
-            for k, (_, c) in enumerate(HEADS):
+            for k, (name, c) in enumerate(HEADS):
+                if name == "up_prob_head" and not up_mask:
+                    continue
                 self._conv(self.t1, k * HEAD_HIDDEN, HEAD_HIDDEN, self.w_c2[k], self.b_c2[k],
                            HEAD_HIDDEN, 1, mode=EPI_NHWC, act=1, out=self.t2,
                            out_c=4 * HEAD_HIDDEN, out_off=k * HEAD_HIDDEN)

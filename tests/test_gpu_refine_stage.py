@@ -75,3 +75,27 @@ def test_refine_stage_feeds_the_ops():
     r = res.float()
     assert torch.isfinite(r).all()
     assert (r.norm(dim=1) - 1).abs().max().item() <= 2e-3
+
+
+def test_refine_stage_skip_up_mask():
+    """up_mask=False skips the up-mask head (only the last iteration's
+    upsample reaches the output, src/dsine_refine.cpp:270-282) and leaves
+    the other heads and the GRU state unchanged."""
+    from brovisionml_b200.refine_stage import RefineStage, random_params
+
+    B, h, w = 1, 24, 40
+    params = random_params("cuda", seed=9)
+    h0, feat, uv = make_inputs(B, h, w, seed=2)
+    outs = {}
+    for skip in (False, True):
+        st = RefineStage(params, B, h, w, out_dtype=torch.float32)
+        st.start(h0, feat, uv)
+        res = [st.step(up_mask=not skip or i == 2) for i in range(3)]
+        torch.cuda.synchronize()
+        st.check_pipeline()
+        outs[skip] = res
+    for i in range(3):
+        for name in ("prob", "xy", "angle"):
+            assert torch.equal(getattr(outs[False][i], name), getattr(outs[True][i], name))
+    assert outs[True][0].up_mask is None and outs[True][1].up_mask is None
+    assert torch.equal(outs[False][2].up_mask, outs[True][2].up_mask)
