@@ -71,6 +71,8 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s);
 
 cudaError_t launch_ray_relu(void* normal, SType t, const float* ray, int B, int H, int W,
                             cudaStream_t s);
+cudaError_t launch_stage_inputs(const float* h0, const float* feat, int B, int H, int W,
+                                float* h32, void* hx, void* fx, cudaStream_t s);
 cudaError_t launch_build_ray(float* ray, int H, int W, double fu, double cu, double fv,
                              double cv, cudaStream_t s);
 cudaError_t launch_l2_normalize(const void* x, void* y, SType t, int N, int C, int H, int W,

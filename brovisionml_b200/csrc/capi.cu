@@ -430,6 +430,18 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
     return finish(bvml::launch_conv_tc(L, static_cast<cudaStream_t>(stream)), "conv2d launch");
 }
 
+int bvml_stage_inputs(const float* h0, const float* feat, int B, int H, int W, float* h32,
+                      void* hx, void* fx, void* stream) {
+    auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (B < 0 || H < 0 || W < 0) return einval("stage inputs: negative size");
+    if ((long)B * H * W == 0) return finish(cudaSuccess, "stage inputs");
+    if (!h0 || !h32 || !hx || !a16(h32) || !a16(hx) || (!feat) != (!fx) || (fx && !a16(fx)))
+        return einval("stage inputs: null or unaligned tensor (feat and fx go together)");
+    return finish(bvml::launch_stage_inputs(h0, feat, B, H, W, h32, hx, fx,
+                                            static_cast<cudaStream_t>(stream)),
+                  "stage inputs");
+}
+
 size_t bvml_refine_workspace_bytes(int B, int h, int w) {
     if (B < 0 || h < 0 || w < 0) return 0;
     const size_t plane = (size_t)h * (size_t)w;

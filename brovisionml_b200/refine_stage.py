@@ -142,14 +142,13 @@ class RefineStage:
         and uv (2,h,w) (src/dsine_refine.cpp:245-248), and convolve the fixed
         inputs once (three launches)."""
         _cuda("refine stage", h0, feat, uv)
-        nhwc = lambda t: t.permute(0, 2, 3, 1)  # noqa: E731
         uvn = uv.permute(1, 2, 0)[None].to(torch.bfloat16)
-        h0 = h0.float()
-        self.h32.copy_(h0.reshape(self.B, HIDDEN // 4, 4, self.h, self.w).permute(0, 1, 3, 4, 2))
-        self.hx.copy_(nhwc(h0))
-        self.fx.copy_(nhwc(feat))
+        h0 = h0.float().contiguous()
+        feat = feat.float().contiguous()
         self.ux[..., :2] = uvn
         with torch.cuda.device(self.dev):
+            check(lib.bvml_stage_inputs(_p(h0), _p(feat), self.B, self.h, self.w, _p(self.h32),
+                                        _p(self.hx), _p(self.fx), _stream(self.dev)))
             self._conv(self.ux, 0, 64, self.w_gxu, self.zeros, 192, 5, mode=EPI_C4_F32,
                        out=self.gxu, out_c=192, out_off=0)
             self._conv(self.fx, 0, 64, self.w_gx, self.zeros, 192, 5, mode=EPI_C4_F32,

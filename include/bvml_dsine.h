@@ -270,6 +270,17 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
                              int ks, const bvml_conv_epilogue* epi, int* err, void* stream);
 
 /*
+ * The refine stage's inputs in its layouts, one pass: the decoder's hidden
+ * state h0 and feature (B,64,H,W) fp32 planar -> the GRU state h32 (C4 fp32,
+ * (B,16,H,W,4)) and its bf16 NHWC copy hx (B,H,W,64), and the feature as
+ * NHWC bf16 fx (B,H,W,64); feat and fx may both be null. Replaces the
+ * concat / layout work at the start of Refiner::forward
+ * (src/dsine_refine.cpp:245-248) for the tensor-core stage.
+ */
+int bvml_stage_inputs(const float* h0, const float* feat, int B, int H, int W, float* h32,
+                      void* hx, void* fx, void* stream);
+
+/*
  * Profiling aid (no reference counterpart): arm `n` caller-created CUDA events
  * (cudaEvent_t, cast to void*) for the calling thread. While armed,
  * bvml_refine records events[0] on its stream before its first kernel and

@@ -99,3 +99,24 @@ def test_refine_stage_skip_up_mask():
             assert torch.equal(getattr(outs[False][i], name), getattr(outs[True][i], name))
     assert outs[True][0].up_mask is None and outs[True][1].up_mask is None
     assert torch.equal(outs[False][2].up_mask, outs[True][2].up_mask)
+
+
+def test_stage_inputs_layouts():
+    """bvml_stage_inputs: planar fp32 h0 / feat -> h32 (C4 fp32), hx and fx
+    (NHWC bf16), against torch's own permutes; odd sizes."""
+    from brovisionml_b200._capi import check, lib
+    from brovisionml_b200.ops import _p, _stream
+
+    B, H, W = 3, 7, 13
+    g = torch.Generator(device="cuda").manual_seed(4)
+    h0 = torch.randn((B, 64, H, W), device="cuda", generator=g)
+    feat = torch.randn((B, 64, H, W), device="cuda", generator=g)
+    h32 = torch.full((B, 16, H, W, 4), float("nan"), device="cuda")
+    hx = torch.empty((B, H, W, 64), device="cuda", dtype=torch.bfloat16)
+    fx = torch.empty((B, H, W, 64), device="cuda", dtype=torch.bfloat16)
+    check(lib.bvml_stage_inputs(_p(h0), _p(feat), B, H, W, _p(h32), _p(hx), _p(fx),
+                                _stream(torch.device("cuda"))))
+    torch.cuda.synchronize()
+    assert torch.equal(h32, h0.reshape(B, 16, 4, H, W).permute(0, 1, 3, 4, 2))
+    assert torch.equal(hx, h0.permute(0, 2, 3, 1).to(torch.bfloat16))
+    assert torch.equal(fx, feat.permute(0, 2, 3, 1).to(torch.bfloat16))
