@@ -412,8 +412,6 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
         case BVML_EPI_PLANAR_F16:
         case BVML_EPI_PLANAR_F32:
             if (!epi->out || !a16(epi->out)) return einval("conv2d: null or unaligned planar output");
-            if ((W * (epi->mode == BVML_EPI_PLANAR_F16 ? 2 : 4)) % 16 != 0)
-                return einval("conv2d: planar output rows must be multiples of 16 bytes");
             break;
         case BVML_EPI_GRU_ZR:
             if (cout != 128 || !epi->h32 || !epi->z || !epi->rh || !a16(epi->h32) ||

@@ -63,6 +63,7 @@ struct ConvArgs {
     __nv_bfloat16* hin;
     int hin_c;
     int obox;     // NHWC outputs: channels per TMA store (64: two chunks, 128-byte rows)
+    int planar_direct;  // planar rows not a multiple of 16 bytes: plain stores, no TMA
     // optional per-pixel addend in channel groups of 4 (C4, see load_addend)
     const float* add;
     long add_fs;  // frame stride in floats (0: one frame shared by all)
@@ -262,6 +263,25 @@ __device__ __forceinline__ void planar_chunk_tma(const ConvArgs& a, const CUtens
                                                  const uint32_t (&v)[32]) {
     float f[32];
     pre_activation(a, sbias, t, cb, v, f);
+    if (a.planar_direct) {
+        // rows the TMA cannot address (W x element size not a multiple of 16
+        // bytes): each channel's 32 pixels as plain stores, coalesced across
+        // the warp's consecutive pixels
+        const int pw = a.tw < 32 ? a.tw : 32;
+        const int px = px0 + lane % pw, py = py0 + lane / pw;
+        if (px < a.W && py < a.H) {
+            const long hw = (long)a.H * a.W;
+            TO* o = static_cast<TO*>(a.out) + ((long)b * a.cout + cb) * hw + (long)py * a.W + px;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                if (cb + i < a.cout) {
+                    if constexpr (sizeof(TO) == 2) o[i * hw] = __float2half_rn(f[i]);
+                    else o[i * hw] = f[i];
+                }
+            }
+        }
+        return;
+    }
     if (lane == 0) tc::bulk_wait_read<1>();  // this buffer's previous store has read it
     __syncwarp();
 #pragma unroll
@@ -878,8 +898,8 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     // planar outputs: a 4-D map (W, H, cout, B) over the output, written by each
     // epilogue warp as pw x ph pixels x 32 channels boxes
     CUtensorMap mo = ma;  // unused by the other epilogues
-    if (planar) {
-        if ((L.W * es) % 16 != 0) return cudaErrorInvalidValue;
+    a.planar_direct = planar && (L.W * es) % 16 != 0;
+    if (planar && !a.planar_direct) {
         const int pw = a.tw < 32 ? a.tw : 32;
         const cuuint64_t dims_o[4] = {(cuuint64_t)L.W, (cuuint64_t)L.H, (cuuint64_t)L.cout,
                                       (cuuint64_t)L.B};

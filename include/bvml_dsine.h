@@ -211,8 +211,9 @@ int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B
 
 /* Epilogue modes of bvml_conv2d_nhwc_bf16_ex. */
 #define BVML_EPI_NHWC 0        /* act(conv) as bf16 at out[pixel * out_c + out_off + o] */
-#define BVML_EPI_PLANAR_F16 1  /* conv as fp16 at out[(b * cout + o) * H * W + y * W + x];
-                                  planar rows W * element size a multiple of 16 bytes */
+#define BVML_EPI_PLANAR_F16 1  /* conv as fp16 at out[(b * cout + o) * H * W + y * W + x]
+                                  (TMA stores when W * 2 is a multiple of 16 bytes,
+                                  plain stores otherwise) */
 #define BVML_EPI_PLANAR_F32 2  /* the same in fp32 */
 #define BVML_EPI_GRU_ZR 3      /* ConvGRU gates z, r (cout = 128: z then r) */
 #define BVML_EPI_GRU_Q 4       /* ConvGRU candidate and update (cout = 64) */

@@ -93,3 +93,42 @@ def test_conv_addend_and_fp32_output(shared):
     d = (c4(y) - ref).abs().max().item()
     print(f"conv addend shared={shared}: max_abs {d:.2e}")
     assert d <= 1e-3  # fp32 output: summation order only
+
+
+@pytest.mark.parametrize("B,H,W,cin,cout,ks,f16", [
+    (2, 9, 45, 128, 25, 1, True),     # odd width: plain stores
+    (1, 16, 44, 64, 50, 3, True),     # 88-byte rows: plain stores
+    (1, 12, 40, 128, 576, 1, True),   # 80-byte rows: TMA stores, N = 192 tiles
+    (1, 7, 37, 64, 30, 5, False),     # fp32, odd width
+])
+def test_conv_planar_outputs(B, H, W, cin, cout, ks, f16):
+    """Planar (B, cout, H, W) outputs of bvml_conv2d_nhwc_bf16_ex (the heads'
+    raw outputs), through TMA stores where the rows allow it and plain stores
+    otherwise."""
+    import ctypes
+
+    import brovisionml_b200 as b
+    from brovisionml_b200._capi import EPI_PLANAR_F16, EPI_PLANAR_F32, ConvEpilogue, check, lib
+    from brovisionml_b200.ops import _p, _stream
+
+    g = torch.Generator(device="cuda").manual_seed(W + cout)
+    cin_pad = b.ops.pad64(cin)
+    x = torch.zeros((B, H, W, cin_pad), device="cuda", dtype=torch.bfloat16)
+    x[..., :cin] = torch.randn((B, H, W, cin), device="cuda", generator=g).to(torch.bfloat16)
+    weight = torch.randn((cout, cin, ks, ks), device="cuda", generator=g) * (cin * ks * ks) ** -0.5
+    bias = torch.randn(cout, device="cuda", generator=g) * 0.1
+    dt = torch.float16 if f16 else torch.float32
+    y = torch.full((B, cout, H, W), float("nan"), device="cuda", dtype=dt)
+    err = torch.zeros(1, device="cuda", dtype=torch.int32)
+    e = ConvEpilogue(mode=EPI_PLANAR_F16 if f16 else EPI_PLANAR_F32, out=_p(y))
+    wp = b.pack_conv_weight(weight, cin_pad)
+    check(lib.bvml_conv2d_nhwc_bf16_ex(_p(x), cin_pad, 0, cin_pad, _p(wp), _p(bias), B, H, W,
+                                       cout, wp.shape[1], ks, ctypes.byref(e), _p(err),
+                                       _stream(torch.device("cuda"))))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = ref_conv(x, weight, bias, ks, "none", cin).permute(0, 3, 1, 2)
+    d = ((y.float() - ref).abs() - (1e-3 if f16 else 0.0) * ref.abs()).max().item()
+    print(f"planar conv {B}x{H}x{W} {cin}->{cout} k{ks} f16={f16}: excess {d:.2e}")
+    assert torch.isfinite(y.float()).all()
+    assert d <= 2e-3  # fp16 output rounding (2^-11 relative) or fp32 summation order

@@ -27,7 +27,12 @@ def make_inputs(B, h, w, seed):
 
 
 @pytest.mark.parametrize("B,h,w,iters,out_dtype", [(2, 24, 40, 1, torch.float32),
-                                                   (1, 45, 80, 3, torch.float16)])
+                                                   (1, 45, 80, 3, torch.float16),
+                                                   # the reference's 500 x 348 golden case
+                                                   # padded to 512 x 352: fp16 planar rows
+                                                   # of 88 bytes (plain stores, no TMA)
+                                                   (1, 44, 64, 1, torch.float16),
+                                                   (1, 64, 44, 1, torch.float16)])
 def test_refine_stage_matches_torch(B, h, w, iters, out_dtype):
     from brovisionml_b200.refine_stage import RefineStage, random_params, reference_stage
 
