@@ -36,6 +36,7 @@ layers, the GRU state and the hoisted terms fp32.
 from __future__ import annotations
 
 import ctypes
+import json
 from dataclasses import dataclass
 
 import torch
@@ -55,20 +56,67 @@ def random_params(device, seed: int = 0) -> dict[str, torch.Tensor]:
     available here): convs with std 1/sqrt(fan_in), small biases."""
     g = torch.Generator(device=device).manual_seed(seed)
     p = {}
-
-    def conv(name, cout, cin, k):
-        p[name + ".weight"] = torch.randn((cout, cin, k, k), device=device,
-                                          generator=g) * (cin * k * k) ** -0.5
-        p[name + ".bias"] = torch.randn(cout, device=device, generator=g) * 0.05
-
-    cin = HIDDEN + FEATURE + 2
-    for n in ("gru.convz", "gru.convr", "gru.convq"):
-        conv(n, HIDDEN, cin, 5)
-    for head, out in HEADS:
-        conv(head + ".0", HEAD_HIDDEN, HIDDEN + 2, 3)
-        conv(head + ".2", HEAD_HIDDEN, HEAD_HIDDEN, 1)
-        conv(head + ".4", out, HEAD_HIDDEN, 1)
+    for name, shape in param_shapes().items():
+        if name.endswith(".weight"):
+            fan_in = shape[1] * shape[2] * shape[3]
+            p[name] = torch.randn(shape, device=device, generator=g) * fan_in ** -0.5
+        else:
+            p[name] = torch.randn(shape, device=device, generator=g) * 0.05
     return p
+
+
+def param_shapes() -> dict[str, tuple[int, ...]]:
+    """The refine stage's tensors as the reference names and shapes them
+    (src/dsine_refine.cpp:51-92, 185-194): gru.conv{z,r,q} 5x5 over 130
+    channels, per head .0 3x3 66 -> 128, .2 1x1 128 -> 128, .4 1x1 128 -> out."""
+    cin = HIDDEN + FEATURE + 2
+    shapes = {}
+    for g in "zrq":
+        shapes[f"gru.conv{g}.weight"] = (HIDDEN, cin, 5, 5)
+        shapes[f"gru.conv{g}.bias"] = (HIDDEN,)
+    for head, out in HEADS:
+        for i, (co, ci, k) in zip((0, 2, 4), ((HEAD_HIDDEN, HIDDEN + 2, 3),
+                                             (HEAD_HIDDEN, HEAD_HIDDEN, 1),
+                                             (out, HEAD_HIDDEN, 1))):
+            shapes[f"{head}.{i}.weight"] = (co, ci, k, k)
+            shapes[f"{head}.{i}.bias"] = (co,)
+    return shapes
+
+
+_ST_DTYPES = {"F32": torch.float32, "F16": torch.float16, "BF16": torch.bfloat16}
+
+
+def load_params(path: str) -> dict[str, torch.Tensor]:
+    """The refine stage's weights from a safetensors file (the reference's
+    Refiner::load_file, src/dsine_refine.cpp:185-194, and load_f32,
+    src/weights_util.h): F32, F16 or BF16 tensors widened to fp32 on the
+    host; other tensors in the file (encoder, decoder) are not read. Errors
+    name the file and the tensor, as the reference's do."""
+    with open(path, "rb") as f:
+        n = int.from_bytes(f.read(8), "little")
+        if n <= 0 or n > (1 << 30):
+            raise RuntimeError(f"dsine refine: {path}: not a safetensors file")
+        header = json.loads(f.read(n))
+        base = 8 + n
+        out = {}
+        for name, shape in param_shapes().items():
+            meta = header.get(name)
+            if meta is None:
+                raise RuntimeError(f"dsine refine: {path}: missing tensor '{name}'")
+            dt = _ST_DTYPES.get(meta["dtype"])
+            if dt is None:
+                raise RuntimeError(f"dsine refine: {path}: tensor '{name}' has dtype "
+                                   f"{meta['dtype']} (F32, F16 or BF16 expected)")
+            if tuple(meta["shape"]) != shape:
+                raise RuntimeError(f"dsine refine: {path}: tensor '{name}' has shape "
+                                   f"{tuple(meta['shape'])}, expected {shape}")
+            b0, b1 = meta["data_offsets"]
+            f.seek(base + b0)
+            raw = bytearray(f.read(b1 - b0))
+            if len(raw) != b1 - b0:
+                raise RuntimeError(f"dsine refine: {path}: tensor '{name}' is truncated")
+            out[name] = torch.frombuffer(raw, dtype=dt).reshape(shape).float()
+    return out
 
 
 @dataclass
@@ -127,6 +175,13 @@ class RefineStage:
         self.gu = torch.zeros((1, HEAD_HIDDEN, h, w, 4), device=d)
         self.t1, self.t2 = mk(4 * HEAD_HIDDEN), mk(4 * HEAD_HIDDEN)
         self.err = torch.zeros(1, device=d, dtype=torch.int32)
+
+    @classmethod
+    def from_safetensors(cls, path: str, B: int, h: int, w: int,
+                         device: torch.device | int = 0,
+                         out_dtype: torch.dtype = torch.float16) -> "RefineStage":
+        """A stage with the weights of a DSINE checkpoint (model.safetensors)."""
+        return cls(load_params(path), B, h, w, device=device, out_dtype=out_dtype)
 
     # one launch through the C ABI
     def _conv(self, x, cin_off, cin_pad, w, bias, cout, ks, **epi):
