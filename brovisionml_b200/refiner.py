@@ -1,0 +1,122 @@
+"""The whole DSINE refinement on one GPU: the B200 counterpart of
+``brovisionml::dsine::Refiner`` (include/brovisionml/dsine_refine.h,
+src/dsine_refine.cpp:181-294) -- load / to / forward over B frames of one
+camera.
+
+forward = the stage inputs and the hoisted feature / uv terms (RefineStage.
+start), 5 iterations of ConvGRU + heads on the tensor cores (the up-mask head
+in the last one only: only the last upsample reaches the result), then the
+refine ops on the heads' raw outputs (AngMF with the activations fused,
+convex 8x upsample, L2-normalise, crop: ``refine(..., logits=True)``). The
+uv map and the ray are computed on the device from the intrinsics, with the
+reference's +0.5 principal-point convention (src/dsine_decoder.cpp:242-290).
+"""
+from __future__ import annotations
+
+import os
+import struct
+from typing import Sequence
+
+import torch
+
+from .ops import refine
+from .refine_stage import RefineStage, load_params
+
+ITERS = 5  # kIter, src/dsine_refine.cpp:251
+
+
+def _f32(v: float) -> float:
+    return struct.unpack("f", struct.pack("f", float(v)))[0]
+
+
+def grid_intrinsics(intrins: Sequence[float], h8: int, w8: int, origH: int,
+                    origW: int) -> tuple[float, float, float, float]:
+    """(fu, cu, fv, cv) on the /8 grid from the raw preprocess intrinsics
+    (fx, fy, cx, cy) and the padded image size (src/dsine_refine.cpp:230-237);
+    the intrinsics are the reference's float fields (Intrinsics,
+    include/brovisionml/dsine_preprocess.h), widened to double."""
+    fx, fy, cx, cy = (_f32(v) for v in intrins)
+    sw, sh = w8 / origW, h8 / origH
+    return fx * sw, (cx + 0.5) * sw, fy * sh, (cy + 0.5) * sh
+
+
+def build_uv(intrins: Sequence[float], h8: int, w8: int, origH: int, origW: int,
+             device) -> torch.Tensor:
+    """The (2, h8, w8) uv conditioning map, computed as the reference does
+    (double arithmetic, rounded to float; src/dsine_decoder.cpp:242-275)."""
+    fu, cu, fv, cv = grid_intrinsics(intrins, h8, w8, origH, origW)
+    xs = torch.arange(w8, device=device, dtype=torch.float64) + 0.5
+    ys = torch.arange(h8, device=device, dtype=torch.float64) + 0.5
+    u = ((xs - cu) / fu).float()
+    v = ((ys - cv) / fv).float()
+    return torch.stack([u[None, :].expand(h8, w8), v[:, None].expand(h8, w8)]).contiguous()
+
+
+class Refiner:
+    """load(dir) / load_file(path) / to(device) / forward(...), as the
+    reference's Refiner, for B frames at once."""
+
+    def __init__(self) -> None:
+        self.params: dict[str, torch.Tensor] | None = None
+        self.device = torch.device("cpu")
+        self._stages: dict[tuple, RefineStage] = {}
+
+    def load(self, directory: str) -> None:
+        self.load_file(os.path.join(directory, "model.safetensors"))
+
+    def load_file(self, path: str) -> None:
+        self.params = load_params(path)
+        self._stages.clear()
+
+    def load_params(self, params: dict[str, torch.Tensor]) -> None:
+        """Weights already in memory (the reference's names and shapes)."""
+        self.params = {k: v.detach().float().cpu() for k, v in params.items()}
+        self._stages.clear()
+
+    def to(self, device) -> "Refiner":
+        device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        if device.type != "cuda":
+            raise RuntimeError("dsine refine: the B200 refiner runs on CUDA devices only")
+        if device != self.device:
+            self.device = device
+            self._stages.clear()
+        return self
+
+    def _stage(self, B: int, h: int, w: int, out_dtype: torch.dtype) -> RefineStage:
+        if self.params is None:
+            raise RuntimeError("dsine refine: forward() called before load()")
+        if self.device.type != "cuda":
+            raise RuntimeError("dsine refine: forward() called before to(cuda device)")
+        key = (B, h, w, out_dtype)
+        if key not in self._stages:
+            self._stages[key] = RefineStage(self.params, B, h, w, device=self.device,
+                                            out_dtype=out_dtype)
+        return self._stages[key]
+
+    def forward(self, normal: torch.Tensor, feature: torch.Tensor, hidden: torch.Tensor,
+                intrins: Sequence[float], origH: int, origW: int,
+                crop: tuple[int, int, int, int] | None = None,
+                out_dtype: torch.dtype = torch.float16, check: bool = True) -> torch.Tensor:
+        """normal (B,3,h8,w8), feature and hidden (B,64,h8,w8): the decoder's
+        outputs on this device. intrins = raw (fx, fy, cx, cy); origH, origW
+        the padded image size; crop = (pad_t, pad_l, orig_h, orig_w) of the
+        DsineTransform (default: none). Returns (B,3,orig_h,orig_w) unit
+        normals in out_dtype (the storage of the heads' outputs and of the
+        result; fp16 or fp32). check=True synchronises once to raise if a
+        tensor-core pipeline gave up; with check=False the call stays
+        asynchronous on the current stream, like the reference's brotensor
+        ops."""
+        B, _, h, w = normal.shape
+        if tuple(feature.shape) != (B, 64, h, w) or tuple(hidden.shape) != (B, 64, h, w):
+            raise RuntimeError("dsine refine: feature and hidden must be (B,64,h8,w8) like "
+                               "the normal's grid")
+        st = self._stage(B, h, w, out_dtype)
+        fu, cu, fv, cv = grid_intrinsics(intrins, h, w, origH, origW)
+        st.start(hidden, feature, build_uv(intrins, h, w, origH, origW, self.device))
+        outs = [st.step(up_mask=i == ITERS - 1) for i in range(ITERS)]
+        res = refine(normal.to(out_dtype).contiguous(), [o.prob for o in outs],
+                     [o.xy for o in outs], [o.angle for o in outs], outs[-1].up_mask,
+                     fu, cu, fv, cv, crop=crop, logits=True)
+        if check:
+            st.check_pipeline()
+        return res
