@@ -60,17 +60,22 @@ class Refiner:
         self.params: dict[str, torch.Tensor] | None = None
         self.device = torch.device("cpu")
         self._stages: dict[tuple, RefineStage] = {}
+        self._graphs: dict[tuple, tuple] = {}
 
     def load(self, directory: str) -> None:
         self.load_file(os.path.join(directory, "model.safetensors"))
 
     def load_file(self, path: str) -> None:
         self.params = load_params(path)
-        self._stages.clear()
+        self._reset()
 
     def load_params(self, params: dict[str, torch.Tensor]) -> None:
         """Weights already in memory (the reference's names and shapes)."""
         self.params = {k: v.detach().float().cpu() for k, v in params.items()}
+        self._reset()
+
+    def _reset(self) -> None:
+        self._graphs.clear()  # graphs hold the stages' buffers: release them first
         self._stages.clear()
 
     def to(self, device) -> "Refiner":
@@ -79,7 +84,7 @@ class Refiner:
             raise RuntimeError("dsine refine: the B200 refiner runs on CUDA devices only")
         if device != self.device:
             self.device = device
-            self._stages.clear()
+            self._reset()
         return self
 
     def _stage(self, B: int, h: int, w: int, out_dtype: torch.dtype) -> RefineStage:
@@ -96,7 +101,8 @@ class Refiner:
     def forward(self, normal: torch.Tensor, feature: torch.Tensor, hidden: torch.Tensor,
                 intrins: Sequence[float], origH: int, origW: int,
                 crop: tuple[int, int, int, int] | None = None,
-                out_dtype: torch.dtype = torch.float16, check: bool = True) -> torch.Tensor:
+                out_dtype: torch.dtype = torch.float16, check: bool = True,
+                graph: bool = False) -> torch.Tensor:
         """normal (B,3,h8,w8), feature and hidden (B,64,h8,w8): the decoder's
         outputs on this device. intrins = raw (fx, fy, cx, cy); origH, origW
         the padded image size; crop = (pad_t, pad_l, orig_h, orig_w) of the
@@ -105,7 +111,14 @@ class Refiner:
         result; fp16 or fp32). check=True synchronises once to raise if a
         tensor-core pipeline gave up; with check=False the call stays
         asynchronous on the current stream, like the reference's brotensor
-        ops."""
+        ops. graph=True replays a CUDA graph of the whole refinement (about
+        60 launches), captured on the first call for this shape, intrinsics
+        and crop: the inputs are copied into the graph's buffers and the
+        result is returned as a new tensor; for small batches the host's
+        launch work otherwise dominates."""
+        if graph:
+            return self._forward_graph(normal, feature, hidden, intrins, origH, origW, crop,
+                                       out_dtype, check)
         B, _, h, w = normal.shape
         if tuple(feature.shape) != (B, 64, h, w) or tuple(hidden.shape) != (B, 64, h, w):
             raise RuntimeError("dsine refine: feature and hidden must be (B,64,h8,w8) like "
@@ -119,4 +132,30 @@ class Refiner:
                      fu, cu, fv, cv, crop=crop, logits=True)
         if check:
             st.check_pipeline()
+        return res
+
+    def _forward_graph(self, normal, feature, hidden, intrins, origH, origW, crop, out_dtype,
+                       check):
+        B, _, h, w = normal.shape
+        key = (B, h, w, out_dtype, tuple(float(v) for v in intrins), origH, origW,
+               tuple(crop) if crop is not None else None)
+        if key not in self._graphs:
+            ins = [t.detach().clone() for t in (normal, feature, hidden)]
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):  # warm-up: kernel attributes, workspace
+                self.forward(*ins, intrins, origH, origW, crop, out_dtype, check=False)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                out = self.forward(*ins, intrins, origH, origW, crop, out_dtype, check=False)
+            self._graphs[key] = (g, ins, out)
+        g, ins, out = self._graphs[key]
+        for dst, src in zip(ins, (normal, feature, hidden)):
+            dst.copy_(src)
+        g.replay()
+        res = out.clone()
+        if check:
+            self._stage(B, h, w, out_dtype).check_pipeline()
         return res

@@ -40,3 +40,29 @@ def test_refiner_forward_composes_stage_and_ops():
                      [o.angle for o in outs], outs[-1].up_mask, fu, cu, fv, cv, logits=True)
     torch.cuda.synchronize()
     assert torch.equal(got, want)
+
+
+def test_refiner_graph_replay_matches_eager():
+    """forward(graph=True): a CUDA graph of the whole refinement, captured
+    once per shape / intrinsics / crop, replayed with new inputs, equals the
+    eager call."""
+    from brovisionml_b200.refine_stage import random_params
+    from brovisionml_b200.refiner import Refiner
+
+    B, h, w = 1, 24, 40
+    H, W = 8 * h, 8 * w
+    intr = (0.8 * W, 0.8 * W, W / 2, H / 2)
+    r = Refiner()
+    r.load_params(random_params("cpu", seed=6))
+    r.to(0)
+    for seed in (1, 2):
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        normal = torch.nn.functional.normalize(torch.randn((B, 3, h, w), device="cuda",
+                                                           generator=g), dim=1)
+        feat = torch.relu(torch.randn((B, 64, h, w), device="cuda", generator=g))
+        hid = torch.tanh(torch.randn((B, 64, h, w), device="cuda", generator=g))
+        eager = r.forward(normal, feat, hid, intr, H, W, crop=(4, 8, 180, 300))
+        replay = r.forward(normal, feat, hid, intr, H, W, crop=(4, 8, 180, 300), graph=True)
+        torch.cuda.synchronize()
+        assert torch.equal(eager, replay), seed
+    assert len(r._graphs) == 1
