@@ -1,28 +1,29 @@
 // Implicit-GEMM 2-D convolution on the 5th-generation tensor cores (sm_100a):
 // the dense convolutions of the refine stage's ConvGRU and prediction heads
 // (src/dsine_refine.cpp:95-158: 5x5 pad 2, 3x3 pad 1, 1x1), which the
-// reference runs as brotensor conv2d_forward calls.
+// reference runs as brotensor conv2d_forward calls followed by separate
+// activation, concat and elementwise passes.
 //
-// Layout: activations NHWC bf16 with the channel count padded to a multiple
-// of 64 (pad channels zero), weights [tap][C_out_pad][C_in_pad] bf16 (K-major
+// Layout: inputs NHWC bf16 with the channel count padded to a multiple of 64
+// (pad channels zero), weights [tap][C_out_pad][C_in_pad] bf16 (K-major
 // rows), fp32 bias, fp32 accumulation in tensor memory.
 //
-// GEMM view: M = pixels, N = output channels, K = taps x input channels. A CTA
-// owns a tile of 128 pixels (tw x th, chosen per width to waste the fewest
-// rows) and N output channels (64, 128 or 256). For each filter tap and
-// 64-channel chunk:
-//  * warp 0 (one lane) loads the A tile -- the 128 pixels shifted by the tap,
-//    64 channels -- with one 4-D TMA box from the NHWC tensor (coordinates
-//    outside the frame read zeros: the convolution's zero padding), and the
-//    B tile (N x 64 weights) with one 3-D box, both 128-byte swizzled, into a
-//    ring of S stages;
-//  * warp 1 (one lane) issues four tcgen05.mma (K = 16 each) per stage into
-//    the TMEM accumulator (128 lanes x N fp32 columns) and releases the stage
-//    with tcgen05.commit;
-//  * warps 2-9 wait for the last commit, read the accumulator with
-//    tcgen05.ld (one pixel per thread; two warps per TMEM lane quarter, each
-//    half of the columns), add the bias, apply the epilogue and store (pad
-//    channels as zeros, so the output can feed the next convolution).
+// GEMM view: M = pixels, N = output channels, K = taps x input channels. A
+// persistent CTA (one per SM) walks tiles of MT sub-tiles of 128 pixels (tw x
+// th each, stacked vertically) by N output channels (64, 128, 192 or 256):
+//  * warp 0 (one lane) streams operands with TMA into two rings: halo tiles
+//    (one 4-D box per 64-channel chunk and filter column; coordinates outside
+//    the frame read zeros, the convolution's zero padding; every filter row
+//    reuses the same copy at a whole-image-row offset) and per-tap weight
+//    tiles, both 128-byte swizzled; 1x1 layers keep their weights resident;
+//  * warp 1 allocates TMEM and one lane issues tcgen05.mma (M = 128, K = 16)
+//    into two accumulator sets, committing each ring entry back to the
+//    producer and each finished tile to the epilogue;
+//  * warps 2-9 drain the other accumulator set with tcgen05.ld while the next
+//    tile accumulates: bias, an optional per-pixel addend (the hoisted terms
+//    of the refine stage), activation or the GRU gate arithmetic, and stores
+//    (NHWC and planar outputs through per-warp shared-memory staging and TMA
+//    stores; the GRU tensors in coalesced channel-group layouts).
 // All waits are bounded (tc_common.cuh); a wait that gives up sets *err and
 // the CTA tears down after its copies and MMAs in flight have completed.
 #include <cuda_bf16.h>
@@ -41,7 +42,7 @@ namespace {
 constexpr int kTM = 128;             // pixels per tile (MMA M)
 constexpr int kKC = 64;              // channels per K chunk (one 128-byte swizzle row)
 constexpr int kConvThreads = 320;    // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 epilogue
-constexpr int kEpiWarps = 8;         // two per TMEM lane quarter, each half the columns
+constexpr int kEpiWarps = 8;         // two per TMEM lane quarter (see the epilogue)
 constexpr uint32_t kWaitLimit = 1u << 22;
 
 struct ConvArgs {
@@ -141,7 +142,7 @@ __device__ __forceinline__ void pre_activation(const ConvArgs& a, const float* s
 //  through shared memory and TMA stores: nhwc_chunk_tma, nhwc_pair_tma)
 //  C4_32     act(v) as fp32 in C4 layout, out_c channels per frame, at
 //            channel out_off + c;
-//  (PLANAR16/32: planar_chunk, through a shared-memory transpose)
+//  (PLANAR16/32: planar_chunk_tma, through a shared-memory transpose)
 //  GRU_ZR    c < 64: z = sigmoid(v) -> z (C8 bf16, 64 channels);
 //            64 <= c < 128: r = sigmoid(v) -> rh[pix * rh_c + c - 64] = r * h,
 //            h from h32 (C4 fp32, 64 channels);
