@@ -77,7 +77,7 @@ struct ConvArgs {
 template <int ACT>
 __device__ __forceinline__ float activate(float v) {
     if constexpr (ACT == 1) return fmaxf(v, 0.0f);
-    else if constexpr (ACT == 2) return 1.0f / (1.0f + __expf(-v));
+    else if constexpr (ACT == 2) return __fdividef(1.0f, 1.0f + __expf(-v));  // 0 as e^-v -> inf
     else if constexpr (ACT == 3) return tanhf(v);
     else return v;
 }
