@@ -151,6 +151,11 @@ class RefineStage:
         c0 = torch.cat([params[f"{n}.0.weight"] for n, _ in HEADS]).to(d)
         self.w_c0 = pack_conv_weight(c0[:, :H], H, 4 * HEAD_HIDDEN)
         self.b_c0 = f32(torch.cat([params[f"{n}.0.bias"] for n, _ in HEADS]))
+        # the same layer without the up-mask head's slice (the last 128
+        # channels), for iterations that skip that head
+        assert HEADS[-1][0] == "up_prob_head"
+        self.w_c0_3 = pack_conv_weight(c0[:3 * HEAD_HIDDEN, :H], H, 3 * HEAD_HIDDEN)
+        self.b_c0_3 = self.b_c0[:3 * HEAD_HIDDEN].contiguous()
         # the fixed inputs' parts: feat + uv -> z, r, q; uv -> the heads' 3x3
         wg = torch.cat([wz, wr, wq])
         self.w_gx = pack_conv_weight(wg[:, H:H + FEATURE], 64, 192)
@@ -217,8 +222,9 @@ class RefineStage:
         up-mask head feeds only the convex upsample, and only the last
         iteration's upsample reaches the refined normal
         (src/dsine_refine.cpp:270-282): iterations before the last can pass
-        up_mask=False and skip its two launches (the 576-channel layer is the
-        stage's largest output)."""
+        up_mask=False and skip its two 1x1 launches (the 576-channel layer is
+        the stage's largest output) and its quarter of the heads' shared 3x3
+        layer."""
         B, h, w = self.B, self.h, self.w
         if out is None:
             mk = lambda c: torch.empty((B, c, h, w), device=self.dev,  # noqa: E731
@@ -231,9 +237,10 @@ class RefineStage:
             self._conv(self.rhx, 0, HIDDEN, self.w_q, self.b_q, 64, 5, mode=EPI_GRU_Q,
                        h32=self.h32, z=self.z, hx=self.hx, hx_c=HIDDEN, add=self.gx[:, 32:],
                        add_c=192)
-            self._conv(self.hx, 0, HIDDEN, self.w_c0, self.b_c0, 4 * HEAD_HIDDEN, 3,
-                       mode=EPI_NHWC, act=1, out=self.t1, out_c=4 * HEAD_HIDDEN, out_off=0,
-                       add=self.gu, add_c=4 * HEAD_HIDDEN, add_shared=1)
+            w_c0, b_c0 = (self.w_c0, self.b_c0) if up_mask else (self.w_c0_3, self.b_c0_3)
+            self._conv(self.hx, 0, HIDDEN, w_c0, b_c0, b_c0.numel(), 3, mode=EPI_NHWC, act=1,
+                       out=self.t1, out_c=4 * HEAD_HIDDEN, out_off=0, add=self.gu,
+                       add_c=4 * HEAD_HIDDEN, add_shared=1)
             planar = EPI_PLANAR_F16 if self.out_dtype == torch.float16 else EPI_PLANAR_F32
             dsts = (out.prob, out.xy, out.angle, out.up_mask)
             for k, (name, c) in enumerate(HEADS):
