@@ -296,7 +296,9 @@ def stage_executed_flops(iters: int, B: int, h: int, w: int) -> float:
     (64 -> 192 over 5x5, 64 -> 512 over 3x3) and the 1x1 layers."""
     px = B * h * w
     once = 2 * 192 * 64 * 25 * px + (2 * 192 * 2 * 25 + 2 * 512 * 2 * 9) * h * w
-    it = 2 * 192 * 64 * 25 + 2 * 384 * 64 * 9 + 3 * 2 * 128 * 128 + 2 * 128 * 100
+    # (+ the extra K that adds the hoisted GRU terms as bf16 hi + lo)
+    it = (2 * 192 * 64 * 25 + 2 * 128 * 256 + 2 * 64 * 128 + 2 * 384 * 64 * 9
+          + 3 * 2 * 128 * 128 + 2 * 128 * 100)
     # the up-mask head (its 3x3 slice and two 1x1 layers), last iteration only
     mask = 2 * 128 * 64 * 9 + 2 * 128 * 128 + 2 * 128 * 576
     return float(once + (iters * it + mask) * px)

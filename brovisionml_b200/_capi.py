@@ -73,10 +73,12 @@ class ConvEpilogue(ctypes.Structure):
     """bvml_conv_epilogue (include/bvml_dsine.h)."""
     _fields_ = [("mode", _i), ("act", _i), ("out", _vp), ("out_c", _i), ("out_off", _i),
                 ("h32", _vp), ("z", _vp), ("rh", _vp), ("rh_c", _i), ("hx", _vp), ("hx_c", _i),
-                ("hin", _vp), ("hin_c", _i), ("add", _vp), ("add_c", _i), ("add_shared", _i)]
+                ("hin", _vp), ("hin_c", _i), ("add", _vp), ("add_c", _i), ("add_shared", _i),
+                ("xin", _vp), ("xin_c", _i), ("wx", _vp), ("xin_stride", _i)]
 
 
-EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, EPI_GRU_ZR, EPI_GRU_Q, EPI_C4_F32 = range(6)
+EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, EPI_GRU_ZR, EPI_GRU_Q, EPI_C4_F32, EPI_SPLIT_BF16 = \
+    range(7)
 lib.bvml_conv2d_nhwc_bf16_ex.restype = _i
 lib.bvml_conv2d_nhwc_bf16_ex.argtypes = ([_vp, _i, _i, _i, _vp, _vp] + [_i] * 6
                                           + [ctypes.POINTER(ConvEpilogue), _vp, _vp])

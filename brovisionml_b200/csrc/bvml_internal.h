@@ -42,7 +42,9 @@ struct UpsampleLaunch {
 };
 cudaError_t launch_upsample(const UpsampleLaunch& L, cudaStream_t s);
 
-enum class ConvEpi : int { NHWC = 0, PLANAR16 = 1, PLANAR32 = 2, GRU_ZR = 3, GRU_Q = 4, C4_32 = 5 };
+enum class ConvEpi : int {
+    NHWC = 0, PLANAR16 = 1, PLANAR32 = 2, GRU_ZR = 3, GRU_Q = 4, C4_32 = 5, SPLIT16 = 6
+};
 
 struct ConvLaunch {
     const void* x;       // (B,H,W,x_c) bf16; channels [cin_off, cin_off + cin_pad) are read
@@ -66,6 +68,10 @@ struct ConvLaunch {
     const float* add;    // optional per-pixel addend, C4 fp32 (B or 1,add_c/4,H,W,4)
     int add_c;
     int add_shared;      // nonzero: one frame of addends shared by all B frames
+    const void* xin;     // optional extra K: conv += xin[.., 0:xin_c] . wx^T per pixel, bf16
+    int xin_c;           // a multiple of 64
+    int xin_stride;      // channels per pixel of xin (0: xin_c)
+    const void* wx;      // (cout_pad, xin_c) bf16
 };
 cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s);
 

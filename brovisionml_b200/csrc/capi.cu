@@ -354,7 +354,7 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
                              int ks, const bvml_conv_epilogue* epi, int* err, void* stream) {
     auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     if (!(ks == 1 || ks == 3 || ks == 5)) return einval("conv2d: kernel size must be 1, 3 or 5");
-    if (!epi || epi->mode < 0 || epi->mode > 5) return einval("conv2d: unknown epilogue");
+    if (!epi || epi->mode < 0 || epi->mode > 6) return einval("conv2d: unknown epilogue");
     if (B < 0 || H < 0 || W < 0 || x_c <= 0 || x_c % 8 != 0 || cin_off < 0 ||
         cin_off % 64 != 0 || cin_pad <= 0 || cin_pad % 64 != 0 || cin_off + cin_pad > x_c + 63 ||
         cout <= 0 || cout_pad % 64 != 0 || cout > cout_pad)
@@ -395,12 +395,27 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
     L.add_shared = epi->add_shared;
     if (epi->add && (!a16(epi->add) || epi->add_c % 4 || epi->add_c < cout))
         return einval("conv2d: addend must be 16-byte aligned, add_c a multiple of 4 and >= cout");
+    L.xin = epi->xin;
+    L.xin_c = epi->xin_c;
+    L.wx = epi->wx;
+    L.xin_stride = epi->xin_stride;
+    if (epi->xin && (!epi->wx || !a16(epi->xin) || !a16(epi->wx) || epi->xin_c <= 0 ||
+                     epi->xin_c % 64 || epi->xin_stride < 0 || epi->xin_stride % 8 ||
+                     (epi->xin_stride && epi->xin_stride < epi->xin_c)))
+        return einval("conv2d: extra K needs xin and wx, 16-byte aligned, xin_c a positive "
+                      "multiple of 64, xin_stride 0 or a multiple of 8 >= xin_c");
     switch (epi->mode) {
         case BVML_EPI_NHWC:
             if (epi->act < 0 || epi->act > 3) return einval("conv2d: unknown activation");
             if (!epi->out || !a16(epi->out) || epi->out_c % 8 || epi->out_off % 8 ||
                 epi->out_off + cout_pad > epi->out_c)
                 return einval("conv2d: bad NHWC output");
+            break;
+        case BVML_EPI_SPLIT_BF16:
+            if (cout % 32 || !epi->out || !a16(epi->out) || epi->out_c % 8 ||
+                epi->out_off % 8 || epi->out_off + 2 * cout_pad > epi->out_c)
+                return einval("conv2d: split bf16 output needs cout a multiple of 32 and "
+                              "out_c >= out_off + 2 cout_pad");
             break;
         case BVML_EPI_C4_F32:
             if (epi->act < 0 || epi->act > 1)

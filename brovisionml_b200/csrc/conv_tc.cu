@@ -64,6 +64,8 @@ struct ConvArgs {
     __nv_bfloat16* hin;
     int hin_c;
     int obox;     // NHWC outputs: channels per TMA store (64: two chunks, 128-byte rows)
+    int xchunks;  // extra K: 64-channel chunks of a 1x1 term xin . wx^T (0: none)
+    int x_bytes;  // bytes of one extra-K A box (the tile's pixels, no halo)
     int planar_direct;  // planar rows not a multiple of 16 bytes: plain stores, no TMA
     // optional per-pixel addend in channel groups of 4 (C4, see load_addend)
     const float* add;
@@ -142,6 +144,10 @@ __device__ __forceinline__ void pre_activation(const ConvArgs& a, const float* s
 //  through shared memory and TMA stores: nhwc_chunk_tma, nhwc_pair_tma)
 //  C4_32     act(v) as fp32 in C4 layout, out_c channels per frame, at
 //            channel out_off + c;
+//  (SPLIT16: v as two bf16 halves (hi, lo = v - hi), per 64-channel block
+//  hi then lo, at NHWC channels out_off + 128 (c / 64) + c % 64 and 64
+//  further, through shared memory and TMA stores; an operand for the extra K
+//  of another convolution that keeps about 16 mantissa bits)
 //  (PLANAR16/32: planar_chunk_tma, through a shared-memory transpose)
 //  GRU_ZR    c < 64: z = sigmoid(v) -> z (C8 bf16, 64 channels);
 //            64 <= c < 128: r = sigmoid(v) -> rh[pix * rh_c + c - 64] = r * h,
@@ -305,18 +311,9 @@ __device__ __forceinline__ void planar_chunk_tma(const ConvArgs& a, const CUtens
 // spreads a warp's rows over all banks), and lane 0 stores the box (32
 // channels at c0 x pw x ph pixels) with one TMA store, clipped at the frame
 // edges. The buffer is reused two chunks later, after the store has read it.
-template <int ACT>
-__device__ __forceinline__ void nhwc_chunk_tma(const ConvArgs& a, const CUtensorMap* map_o,
-                                               uint8_t* stg, uint32_t stg_addr, int lane, int c0,
-                                               int px0, int py0, int b, int cb,
-                                               const float* sbias, const float (&t)[32],
-                                               const uint32_t (&v)[32]) {
-    float f[32];
-    pre_activation(a, sbias, t, cb, v, f);
-    alignas(16) __nv_bfloat16 o[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i)
-        o[i] = __float2bfloat16_rn(cb + i < a.cout ? activate<ACT>(f[i]) : 0.0f);
+__device__ __forceinline__ void stage_bf16_box(const CUtensorMap* map_o, uint8_t* stg,
+                                               uint32_t stg_addr, int lane, int c0, int px0,
+                                               int py0, int b, const __nv_bfloat16 (&o)[32]) {
     if (lane == 0) tc::bulk_wait_read<1>();  // this buffer's previous store has read it
     __syncwarp();
     const int sw = (lane >> 1) & 3;
@@ -330,6 +327,21 @@ __device__ __forceinline__ void nhwc_chunk_tma(const ConvArgs& a, const CUtensor
         tc::tma_store_4d(map_o, stg_addr, c0, px0, py0, b);
         tc::bulk_commit();
     }
+}
+
+template <int ACT>
+__device__ __forceinline__ void nhwc_chunk_tma(const ConvArgs& a, const CUtensorMap* map_o,
+                                               uint8_t* stg, uint32_t stg_addr, int lane, int c0,
+                                               int px0, int py0, int b, int cb,
+                                               const float* sbias, const float (&t)[32],
+                                               const uint32_t (&v)[32]) {
+    float f[32];
+    pre_activation(a, sbias, t, cb, v, f);
+    alignas(16) __nv_bfloat16 o[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        o[i] = __float2bfloat16_rn(cb + i < a.cout ? activate<ACT>(f[i]) : 0.0f);
+    stage_bf16_box(map_o, stg, stg_addr, lane, c0, px0, py0, b, o);
 }
 
 // NHWC bf16 output of two consecutive 32-channel chunks (half 0: channels
@@ -380,9 +392,11 @@ __device__ __forceinline__ void nhwc_pair_tma(const ConvArgs& a, const CUtensorM
 template <int N, int MT, int EPI, int ACT, bool BRES>
 __global__ void __launch_bounds__(kConvThreads, 1)
 conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-               const __grid_constant__ CUtensorMap map_o, const ConvArgs a) {
+               const __grid_constant__ CUtensorMap map_o, const __grid_constant__ CUtensorMap map_x,
+               const __grid_constant__ CUtensorMap map_bx, const ConvArgs a) {
     constexpr bool kPlanar = EPI == (int)ConvEpi::PLANAR16 || EPI == (int)ConvEpi::PLANAR32;
-    constexpr bool kStaged = kPlanar || EPI == (int)ConvEpi::NHWC;  // TMA-store epilogues
+    constexpr bool kStaged =  // TMA-store epilogues
+        kPlanar || EPI == (int)ConvEpi::NHWC || EPI == (int)ConvEpi::SPLIT16;
     // TMEM columns: two accumulator sets, allocated as a power of two >= 32
     constexpr int kCols = 2 * MT * N <= 128 ? 128 : (2 * MT * N <= 256 ? 256 : 512);
     static_assert(2 * MT * N <= 512, "TMEM allocation");
@@ -506,6 +520,36 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     }
                 }
             }
+            if constexpr (!BRES) {
+                // extra K: the tile's pixels of xin (no halo) and the weights wx,
+                // through the same rings
+                for (int xc = 0; ok && xc < a.xchunks; ++xc) {
+                    const int s = ga % a.s_a, j = ga / a.s_a;
+                    if (j > 0 && !tc::mbar_wait(bar_empty_a + 8 * s, (j - 1) & 1, kWaitLimit)) {
+                        fail(1);
+                        ok = false;
+                        break;
+                    }
+                    if (aborted()) {
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_expect_tx(bar_full_a + 8 * s, a.x_bytes);
+                    tc::tma_load_4d(sbase + s * a.a_bytes, &map_x, bar_full_a + 8 * s, xc * kKC, x0,
+                                    y0, b);
+                    ++ga;
+                    const int q = gb % a.s_b, jb = gb / a.s_b;
+                    if (jb > 0 && !tc::mbar_wait(bar_empty_b + 8 * q, (jb - 1) & 1, kWaitLimit)) {
+                        fail(1);
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_expect_tx(bar_full_b + 8 * q, a.b_bytes);
+                    tc::tma_load_3d(ring_b + q * a.b_bytes, &map_bx, bar_full_b + 8 * q, xc * kKC,
+                                    n0, 0);
+                    ++gb;
+                }
+            }
         }
         // no copy may still be landing when the CTA exits
         for (int q = ga - a.s_a > 0 ? ga - a.s_a : 0; q < ga; ++q)
@@ -580,6 +624,39 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     ++ga;
                 }
             }
+            if constexpr (!BRES) {
+                for (int xc = 0; ok && xc < a.xchunks; ++xc) {  // extra K (no halo: ky = 0)
+                    const int s = ga % a.s_a, j = ga / a.s_a;
+                    if (!tc::mbar_wait(bar_full_a + 8 * s, j & 1, kWaitLimit) || aborted()) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint32_t sa = sbase + s * a.a_bytes;
+                    const int q = gb % a.s_b;
+                    if (!tc::mbar_wait(bar_full_b + 8 * q, (gb / a.s_b) & 1, kWaitLimit) ||
+                        aborted()) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint64_t db = tc::umma_desc_k_sw128(ring_b + q * a.b_bytes);
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) {
+                        const uint64_t da =
+                            tc::umma_desc_k_sw128(sa + (uint32_t)(m * a.th) * row_bytes);
+#pragma unroll
+                        for (int k = 0; k < kKC / 16; ++k)
+                            tc::umma_bf16(acc + m * N, da + 2 * k, db + 2 * k, idesc,
+                                          !first || k > 0);
+                    }
+                    first = false;
+                    tc::umma_commit(bar_empty_b + 8 * q);
+                    ++gb;
+                    tc::umma_commit(bar_empty_a + 8 * s);
+                    ++ga;
+                }
+            }
             if (!ok) {
                 fail(4);
                 break;
@@ -632,6 +709,27 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 // pw x ph box (pw = min(tw, 32))
                 const int px0 = x0 + (wq * 32) % a.tw, py0 = ys + (wq * 32) / a.tw;
                 if (px0 >= a.W || py0 >= a.H) return;  // the whole box is off the frame
+                if constexpr (EPI == (int)ConvEpi::SPLIT16) {
+                    if (cb >= a.cout) return;  // cout is a multiple of 32
+                    float f[32];
+                    pre_activation(a, sbias, tt, cb, v, f);
+                    alignas(16) __nv_bfloat16 hi[32], lo[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        hi[i] = __float2bfloat16_rn(f[i]);
+                        lo[i] = __float2bfloat16_rn(f[i] - __bfloat162float(hi[i]));
+                    }
+                    const int cx = a.out_off + (cb / 64) * 128 + cb % 64;
+#pragma unroll
+                    for (int part = 0; part < 2; ++part) {
+                        const int slot = (warp - 2) * 2 + (pcount & 1);
+                        stage_bf16_box(&map_o, smem + a.off_out + slot * stage_warp_bytes(EPI),
+                                       sbase + a.off_out + slot * stage_warp_bytes(EPI), lane,
+                                       cx + 64 * part, px0, py0, b, part ? lo : hi);
+                        ++pcount;
+                    }
+                    return;
+                }
                 if constexpr (EPI == (int)ConvEpi::NHWC) {
                     if (a.obox == 64) {  // chunk pairs share a 4 KB buffer and one store
                         const int wbase = ((warp - 2) * 2 + ((pcount >> 1) & 1)) * 4096;
@@ -722,7 +820,8 @@ bool encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
 
 template <int N, int MT, int EPI, int ACT, bool BRES>
 cudaError_t launch_n(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
-                     const ConvArgs& a, int smem, cudaStream_t s) {
+                     const CUtensorMap& mx, const CUtensorMap& mbx, const ConvArgs& a, int smem,
+                     cudaStream_t s) {
     auto kern = conv_tc_kernel<N, MT, EPI, ACT, BRES>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -734,30 +833,31 @@ cudaError_t launch_n(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
     const long n_nt = (a.cout_pad + N - 1) / N;
     unsigned grid = (unsigned)(tiles < sms ? tiles : sms);  // one CTA per SM
     if (BRES) grid = (unsigned)(n_nt * (sms / n_nt > 0 ? sms / n_nt : 1));  // whole groups
-    kern<<<grid, kConvThreads, smem, s>>>(ma, mb, mo, a);
+    kern<<<grid, kConvThreads, smem, s>>>(ma, mb, mo, mx, mbx, a);
     return cudaGetLastError();
 }
 
 template <int EPI, int ACT>
 cudaError_t launch_act(int n, int mt, bool bres, const CUtensorMap& ma, const CUtensorMap& mb,
-                       const CUtensorMap& mo, const ConvArgs& a, int smem, cudaStream_t s) {
+                       const CUtensorMap& mo, const CUtensorMap& mx, const CUtensorMap& mbx,
+                       const ConvArgs& a, int smem, cudaStream_t s) {
     if (bres) {
         switch (n) {
-            case 256: return launch_n<256, 1, EPI, ACT, true>(ma, mb, mo, a, smem, s);
-            case 192: return launch_n<192, 1, EPI, ACT, true>(ma, mb, mo, a, smem, s);
-            case 128: return launch_n<128, 1, EPI, ACT, true>(ma, mb, mo, a, smem, s);
-            default: return launch_n<64, 1, EPI, ACT, true>(ma, mb, mo, a, smem, s);
+            case 256: return launch_n<256, 1, EPI, ACT, true>(ma, mb, mo, mx, mbx, a, smem, s);
+            case 192: return launch_n<192, 1, EPI, ACT, true>(ma, mb, mo, mx, mbx, a, smem, s);
+            case 128: return launch_n<128, 1, EPI, ACT, true>(ma, mb, mo, mx, mbx, a, smem, s);
+            default: return launch_n<64, 1, EPI, ACT, true>(ma, mb, mo, mx, mbx, a, smem, s);
         }
     }
-    if (n == 256) return launch_n<256, 1, EPI, ACT, false>(ma, mb, mo, a, smem, s);
-    if (n == 192) return launch_n<192, 1, EPI, ACT, false>(ma, mb, mo, a, smem, s);
+    if (n == 256) return launch_n<256, 1, EPI, ACT, false>(ma, mb, mo, mx, mbx, a, smem, s);
+    if (n == 192) return launch_n<192, 1, EPI, ACT, false>(ma, mb, mo, mx, mbx, a, smem, s);
     if (n == 128) {
-        if (mt == 2) return launch_n<128, 2, EPI, ACT, false>(ma, mb, mo, a, smem, s);
-        return launch_n<128, 1, EPI, ACT, false>(ma, mb, mo, a, smem, s);
+        if (mt == 2) return launch_n<128, 2, EPI, ACT, false>(ma, mb, mo, mx, mbx, a, smem, s);
+        return launch_n<128, 1, EPI, ACT, false>(ma, mb, mo, mx, mbx, a, smem, s);
     }
-    if (mt == 4) return launch_n<64, 4, EPI, ACT, false>(ma, mb, mo, a, smem, s);
-    if (mt == 2) return launch_n<64, 2, EPI, ACT, false>(ma, mb, mo, a, smem, s);
-    return launch_n<64, 1, EPI, ACT, false>(ma, mb, mo, a, smem, s);
+    if (mt == 4) return launch_n<64, 4, EPI, ACT, false>(ma, mb, mo, mx, mbx, a, smem, s);
+    if (mt == 2) return launch_n<64, 2, EPI, ACT, false>(ma, mb, mo, mx, mbx, a, smem, s);
+    return launch_n<64, 1, EPI, ACT, false>(ma, mb, mo, mx, mbx, a, smem, s);
 }
 
 // Tile geometry and shared-memory plan for one launch: sub-tile tw x th
@@ -869,12 +969,13 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     if (L.epi == ConvEpi::GRU_ZR) n = 128;
     if (L.epi == ConvEpi::GRU_Q) n = 64;
     int mt = L.ks == 1 || n >= 192 ? 1 : (n == 128 ? 2 : 4);
-    const bool bres = L.ks == 1 && L.cin_pad <= kBResChunks * kKC;
+    // resident weights (1x1, few input chunks) unless an extra K block is given
+    const bool bres = L.ks == 1 && L.cin_pad <= kBResChunks * kKC && !L.xin;
     const bool planar = L.epi == ConvEpi::PLANAR16 || L.epi == ConvEpi::PLANAR32;
     const int es = L.epi == ConvEpi::PLANAR16 ? 2 : 4;
     const bool obox64 = L.epi == ConvEpi::NHWC && bres && n != 64 && n != 192;
     const int out_bytes = obox64 ? kEpiWarps * 2 * 4096
-                          : planar || L.epi == ConvEpi::NHWC
+                          : planar || L.epi == ConvEpi::NHWC || L.epi == ConvEpi::SPLIT16
                               ? kEpiWarps * 2 * stage_warp_bytes((int)L.epi) : 0;
     const int smem = plan_conv(a, n, mt, bres, out_bytes);
     if (smem == 0) return cudaErrorInvalidConfiguration;
@@ -911,13 +1012,13 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
                     es == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                     CU_TENSOR_MAP_SWIZZLE_NONE))
             return cudaErrorInvalidValue;
-    } else if (L.epi == ConvEpi::NHWC) {
+    } else if (L.epi == ConvEpi::NHWC || L.epi == ConvEpi::SPLIT16) {
         // NHWC bf16: a 4-D map (out_c, W, H, B); each epilogue warp stores
         // obox channels x pw x ph pixels, 64- or 128-byte swizzled in shared
         // memory. 64-channel boxes (two 4 KB buffers per warp) for the 1x1
         // layers, whose shared memory has room; they need every warp's
         // column range to be whole chunk pairs (not so for N = 64 or 192).
-        a.obox = bres && n != 64 && n != 192 ? 64 : 32;
+        a.obox = L.epi == ConvEpi::NHWC && bres && n != 64 && n != 192 ? 64 : 32;
         const int pw = a.tw < 32 ? a.tw : 32;
         const cuuint64_t dims_o[4] = {(cuuint64_t)L.out_c, (cuuint64_t)L.W, (cuuint64_t)L.H,
                                       (cuuint64_t)L.B};
@@ -928,25 +1029,46 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
                     a.obox == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
             return cudaErrorInvalidValue;
     }
+    // extra K: xin (B,H,W,xin_c) bf16 NHWC as boxes of the tile's pixels (no
+    // halo), wx (xin_c-long rows for each of cout_pad outputs) as N x 64 boxes
+    CUtensorMap mx = ma, mbx = mb;  // unused without an extra K block
+    if (L.xin) {
+        const cuuint64_t dims_x[4] = {(cuuint64_t)L.xin_c, (cuuint64_t)L.W, (cuuint64_t)L.H,
+                                      (cuuint64_t)L.B};
+        const long xs = L.xin_stride ? L.xin_stride : L.xin_c;  // channels per pixel
+        const cuuint64_t str_x[3] = {(cuuint64_t)xs * 2, (cuuint64_t)L.W * xs * 2,
+                                     (cuuint64_t)L.H * L.W * xs * 2};
+        const cuuint32_t box_x[4] = {(cuuint32_t)kKC, (cuuint32_t)a.tw, (cuuint32_t)(mt * a.th), 1};
+        const cuuint64_t dims_bx[3] = {(cuuint64_t)L.xin_c, (cuuint64_t)L.cout_pad, 1};
+        const cuuint64_t str_bx[2] = {(cuuint64_t)L.xin_c * 2,
+                                      (cuuint64_t)L.cout_pad * L.xin_c * 2};
+        const cuuint32_t box_bx[3] = {(cuuint32_t)kKC, (cuuint32_t)n, 1};
+        if (!encode(&mx, L.xin, 4, dims_x, str_x, box_x) ||
+            !encode(&mbx, L.wx, 3, dims_bx, str_bx, box_bx))
+            return cudaErrorInvalidValue;
+        a.xchunks = L.xin_c / kKC;
+        a.x_bytes = kKC * 2 * a.tw * mt * a.th;
+    }
     switch (L.epi) {
+        case ConvEpi::SPLIT16: return launch_act<(int)ConvEpi::SPLIT16, 0>(n, mt, bres, ma, mb, mo, mx, mbx, a, smem, s);
         case ConvEpi::NHWC:
             switch (L.act) {
-                case 0: return launch_act<(int)ConvEpi::NHWC, 0>(n, mt, bres, ma, mb, mo, a, smem, s);
-                case 1: return launch_act<(int)ConvEpi::NHWC, 1>(n, mt, bres, ma, mb, mo, a, smem, s);
-                case 2: return launch_act<(int)ConvEpi::NHWC, 2>(n, mt, bres, ma, mb, mo, a, smem, s);
-                case 3: return launch_act<(int)ConvEpi::NHWC, 3>(n, mt, bres, ma, mb, mo, a, smem, s);
+                case 0: return launch_act<(int)ConvEpi::NHWC, 0>(n, mt, bres, ma, mb, mo, mx, mbx, a, smem, s);
+                case 1: return launch_act<(int)ConvEpi::NHWC, 1>(n, mt, bres, ma, mb, mo, mx, mbx, a, smem, s);
+                case 2: return launch_act<(int)ConvEpi::NHWC, 2>(n, mt, bres, ma, mb, mo, mx, mbx, a, smem, s);
+                case 3: return launch_act<(int)ConvEpi::NHWC, 3>(n, mt, bres, ma, mb, mo, mx, mbx, a, smem, s);
                 default: return cudaErrorInvalidValue;
             }
         case ConvEpi::C4_32:
             switch (L.act) {
-                case 0: return launch_act<(int)ConvEpi::C4_32, 0>(n, mt, bres, ma, mb, mo, a, smem, s);
-                case 1: return launch_act<(int)ConvEpi::C4_32, 1>(n, mt, bres, ma, mb, mo, a, smem, s);
+                case 0: return launch_act<(int)ConvEpi::C4_32, 0>(n, mt, bres, ma, mb, mo, mx, mbx, a, smem, s);
+                case 1: return launch_act<(int)ConvEpi::C4_32, 1>(n, mt, bres, ma, mb, mo, mx, mbx, a, smem, s);
                 default: return cudaErrorInvalidValue;
             }
-        case ConvEpi::PLANAR16: return launch_act<(int)ConvEpi::PLANAR16, 0>(n, mt, bres, ma, mb, mo, a, smem, s);
-        case ConvEpi::PLANAR32: return launch_act<(int)ConvEpi::PLANAR32, 0>(n, mt, bres, ma, mb, mo, a, smem, s);
-        case ConvEpi::GRU_ZR: return launch_act<(int)ConvEpi::GRU_ZR, 0>(n, mt, bres, ma, mb, mo, a, smem, s);
-        case ConvEpi::GRU_Q: return launch_act<(int)ConvEpi::GRU_Q, 0>(n, mt, bres, ma, mb, mo, a, smem, s);
+        case ConvEpi::PLANAR16: return launch_act<(int)ConvEpi::PLANAR16, 0>(n, mt, bres, ma, mb, mo, mx, mbx, a, smem, s);
+        case ConvEpi::PLANAR32: return launch_act<(int)ConvEpi::PLANAR32, 0>(n, mt, bres, ma, mb, mo, mx, mbx, a, smem, s);
+        case ConvEpi::GRU_ZR: return launch_act<(int)ConvEpi::GRU_ZR, 0>(n, mt, bres, ma, mb, mo, mx, mbx, a, smem, s);
+        case ConvEpi::GRU_Q: return launch_act<(int)ConvEpi::GRU_Q, 0>(n, mt, bres, ma, mb, mo, mx, mbx, a, smem, s);
     }
     return cudaErrorInvalidValue;
 }

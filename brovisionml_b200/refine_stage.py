@@ -9,11 +9,16 @@ channels) and uv (2) are the same in every iteration, and uv is the same for
 every frame. So ``start`` convolves them once --
 
   gxu = conv5x5(uv, W_zr||q[:, 128:130])          (1,192/4,h,w,4) fp32 (C4), shared
-  gx  = conv5x5(feat, W_zr||q[:, 64:128]) + gxu    (B,192/4,h,w,4) fp32 (C4)
+  gx  = conv5x5(feat, W_zr||q[:, 64:128]) + gxu    per frame, stored as bf16
+        halves hi = bf16(gx), lo = bf16(gx - hi), each 64-channel block (z, r,
+        q) as hi then lo: (B,h,w,384), about 16 mantissa bits
   gu  = conv3x3(uv, W_heads3x3[:, 64:66])          (1,512/4,h,w,4) fp32, shared
 
--- and each iteration convolves only the hidden state, adding gx / gu in the
-epilogue (the same products, summed in another order):
+-- and each iteration convolves only the hidden state and adds the hoisted
+terms (the same products, summed in another order): gx by the tensor cores,
+as an extra K block (its hi and lo times identity blocks) after the 5x5 taps,
+so the epilogue reads
+no per-pixel table; gu in the epilogue (one frame, L2-resident):
 
   z, r = sigmoid(conv5x5(h, W_zr[:, :64]) + gx[:128])   one GEMM (N = 128);
          the epilogue writes z and r*h
@@ -41,7 +46,7 @@ from dataclasses import dataclass
 
 import torch
 
-from ._capi import EPI_C4_F32, EPI_GRU_Q, EPI_GRU_ZR, EPI_NHWC, EPI_PLANAR_F16, \
+from ._capi import EPI_C4_F32, EPI_GRU_Q, EPI_GRU_ZR, EPI_NHWC, EPI_PLANAR_F16, EPI_SPLIT_BF16, \
     EPI_PLANAR_F32, ConvEpilogue, check, lib
 from .ops import _cuda, _p, _stream, pack_conv_weight, pad64
 
@@ -159,6 +164,15 @@ class RefineStage:
         # the fixed inputs' parts: feat + uv -> z, r, q; uv -> the heads' 3x3
         wg = torch.cat([wz, wr, wq])
         self.w_gx = pack_conv_weight(wg[:, H:H + FEATURE], 64, 192)
+        # identity blocks: the extra K that adds hi + lo of the hoisted GRU
+        # terms (z, r: blocks 0 and 1 of gx; q: block 2)
+        iz = torch.zeros((1, 128, 256), device=d, dtype=torch.bfloat16)
+        for n in range(128):
+            iz[0, n, (n // 64) * 128 + n % 64] = 1
+            iz[0, n, (n // 64) * 128 + 64 + n % 64] = 1
+        e64 = torch.eye(64, device=d, dtype=torch.bfloat16)
+        self.iz = iz
+        self.iq = torch.cat([e64, e64], 1)[None].contiguous()   # (1, 64, 128)
         self.w_gxu = pack_conv_weight(wg[:, H + FEATURE:], 64, 192)
         self.w_gu = pack_conv_weight(c0[:, H:], 64, 4 * HEAD_HIDDEN)
         self.zeros = torch.zeros(4 * HEAD_HIDDEN, device=d)
@@ -175,7 +189,7 @@ class RefineStage:
         self.h32 = torch.zeros((B, H // 4, h, w, 4), device=d)
         self.fx, self.ux = mk(FEATURE), mk(64, n=1)          # feat, [uv | 0]
         # hoisted terms, C4 fp32: the epilogues read them coalesced
-        self.gx = torch.zeros((B, 192 // 4, h, w, 4), device=d)
+        self.gx = mk(384)                                     # gx as hi | lo blocks
         self.gxu = torch.zeros((1, 192 // 4, h, w, 4), device=d)
         self.gu = torch.zeros((1, HEAD_HIDDEN, h, w, 4), device=d)
         self.t1, self.t2 = mk(4 * HEAD_HIDDEN), mk(4 * HEAD_HIDDEN)
@@ -200,7 +214,7 @@ class RefineStage:
     def start(self, h0: torch.Tensor, feat: torch.Tensor, uv: torch.Tensor) -> None:
         """Load the decoder's hidden state h0 (B,64,h,w), feature (B,64,h,w)
         and uv (2,h,w) (src/dsine_refine.cpp:245-248), and convolve the fixed
-        inputs once (three launches)."""
+        inputs once (three convolutions)."""
         _cuda("refine stage", h0, feat, uv)
         uvn = uv.permute(1, 2, 0)[None].to(torch.bfloat16)
         h0 = h0.float().contiguous()
@@ -211,8 +225,8 @@ class RefineStage:
                                         _p(self.hx), _p(self.fx), _stream(self.dev)))
             self._conv(self.ux, 0, 64, self.w_gxu, self.zeros, 192, 5, mode=EPI_C4_F32,
                        out=self.gxu, out_c=192, out_off=0)
-            self._conv(self.fx, 0, 64, self.w_gx, self.zeros, 192, 5, mode=EPI_C4_F32,
-                       out=self.gx, out_c=192, out_off=0, add=self.gxu, add_c=192,
+            self._conv(self.fx, 0, 64, self.w_gx, self.zeros, 192, 5, mode=EPI_SPLIT_BF16,
+                       out=self.gx, out_c=384, out_off=0, add=self.gxu, add_c=192,
                        add_shared=1)
             self._conv(self.ux, 0, 64, self.w_gu, self.zeros, 4 * HEAD_HIDDEN, 3,
                        mode=EPI_C4_F32, out=self.gu, out_c=4 * HEAD_HIDDEN, out_off=0)
@@ -233,10 +247,11 @@ class RefineStage:
                                  for name, c in HEADS))
         with torch.cuda.device(self.dev):
             self._conv(self.hx, 0, HIDDEN, self.w_zr, self.b_zr, 128, 5, mode=EPI_GRU_ZR,
-                       h32=self.h32, z=self.z, rh=self.rhx, rh_c=HIDDEN, add=self.gx, add_c=192)
+                       h32=self.h32, z=self.z, rh=self.rhx, rh_c=HIDDEN, xin=self.gx,
+                       xin_c=256, xin_stride=384, wx=self.iz)
             self._conv(self.rhx, 0, HIDDEN, self.w_q, self.b_q, 64, 5, mode=EPI_GRU_Q,
-                       h32=self.h32, z=self.z, hx=self.hx, hx_c=HIDDEN, add=self.gx[:, 32:],
-                       add_c=192)
+                       h32=self.h32, z=self.z, hx=self.hx, hx_c=HIDDEN,
+                       xin=self.gx[..., 256:], xin_c=128, xin_stride=384, wx=self.iq)
             w_c0, b_c0 = (self.w_c0, self.b_c0) if up_mask else (self.w_c0_3, self.b_c0_3)
             self._conv(self.hx, 0, HIDDEN, w_c0, b_c0, b_c0.numel(), 3, mode=EPI_NHWC, act=1,
                        out=self.t1, out_c=4 * HEAD_HIDDEN, out_off=0, add=self.gu,
@@ -297,9 +312,9 @@ def _main(argv=None) -> None:
     run `steps` iterations of the stage on random weights over B frames of
     the 160 x 90 grid (720p) and print each launch's time of the last
     iteration and of start (CUDA events). Also the target for profiling one
-    layer: start runs twice (3 launches each, the second one timed), then the
-    launches of iteration k are numbers 6 + 11 k .. 16 + 11 k (zr, q, heads
-    3x3, then per head 1x1 and 1x1 planar)."""
+    layer: start runs twice (3 convolutions each, the second one timed), then
+    the convolutions of iteration k are numbers 6 + 11 k .. 16 + 11 k (zr, q,
+    heads 3x3, then per head 1x1 and 1x1 planar)."""
     import argparse
 
     ap = argparse.ArgumentParser()

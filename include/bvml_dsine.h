@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define BVML_ABI_VERSION 2
+#define BVML_ABI_VERSION 3
 
 enum bvml_dtype { BVML_F32 = 0, BVML_F16 = 1 };
 
@@ -220,6 +220,11 @@ int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B
 #define BVML_EPI_C4_F32 5      /* act(conv) as fp32 in channel groups of 4 (C4, below),
                                   out_c channels per frame, at channel out_off + o
                                   (act 0 or 1; out_c, out_off multiples of 4) */
+#define BVML_EPI_SPLIT_BF16 6  /* conv as two bf16 halves per 64-channel block:
+                                  hi = bf16(v) at NHWC channel out_off + 128 (o / 64) +
+                                  o % 64, lo = bf16(v - hi) 64 channels further (cout a
+                                  multiple of 32, out_c >= out_off + 2 cout_pad): an
+                                  extra-K operand (xin below) keeping ~16 bits of v */
 
 /*
  * Where and how bvml_conv2d_nhwc_bf16_ex writes its result. Channel strides
@@ -240,6 +245,12 @@ int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B
  *   convolution whose input does not change between calls: the ConvGRU's
  *   feature and uv channels, the heads' uv channels, which the refine stage
  *   convolves once per refinement instead of once per iteration.
+ * xin (optional, every mode): an extra K block, conv[o] += sum_k xin[pixel *
+ *   xin_stride + k] * wx[o * xin_c + k] for k < xin_c, xin bf16 with
+ *   xin_stride channels per pixel (0: xin_c; a multiple of 8), wx (cout_pad,
+ *   xin_c) bf16, xin_c a multiple of 64 -- a 1x1 term the tensor cores add
+ *   before the epilogue (the refine stage adds its hoisted terms this way, as
+ *   BVML_EPI_SPLIT_BF16 halves times identity blocks).
  */
 typedef struct {
     int mode;
@@ -257,6 +268,10 @@ typedef struct {
     const float* add;
     int add_c;
     int add_shared;
+    const void* xin;     /* optional extra K, below */
+    int xin_c;
+    const void* wx;
+    int xin_stride;
 } bvml_conv_epilogue;
 
 /*

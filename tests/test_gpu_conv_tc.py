@@ -132,3 +132,60 @@ def test_conv_planar_outputs(B, H, W, cin, cout, ks, f16):
     print(f"planar conv {B}x{H}x{W} {cin}->{cout} k{ks} f16={f16}: excess {d:.2e}")
     assert torch.isfinite(y.float()).all()
     assert d <= 2e-3  # fp16 output rounding (2^-11 relative) or fp32 summation order
+
+
+def _conv_ex(x, cin, w_packed, bias, cout, ks, **epi):
+    import ctypes
+
+    from brovisionml_b200._capi import ConvEpilogue, check, lib
+    from brovisionml_b200.ops import _p, _stream
+
+    B, H, W, xc = x.shape
+    err = torch.zeros(1, device="cuda", dtype=torch.int32)
+    e = ConvEpilogue(**{k: (_p(v) if isinstance(v, torch.Tensor) else v) for k, v in epi.items()})
+    check(lib.bvml_conv2d_nhwc_bf16_ex(_p(x), xc, 0, cin, _p(w_packed), _p(bias), B, H, W, cout,
+                                       w_packed.shape[1], ks, ctypes.byref(e), _p(err),
+                                       _stream(torch.device("cuda"))))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+
+
+@pytest.mark.parametrize("cout,ks", [(128, 5), (64, 5), (192, 3)])
+def test_conv_extra_k_and_split(cout, ks):
+    """The extra K block (conv += xin . wx^T per pixel, through the MMA
+    pipeline) and the split-bf16 output (hi + lo of the fp32 result): the
+    refine stage's hoisted GRU terms, added by the tensor cores."""
+    import brovisionml_b200 as b
+    from brovisionml_b200._capi import EPI_C4_F32, EPI_SPLIT_BF16
+
+    B, H, W, cin, xc = 2, 21, 40, 64, 128
+    g = torch.Generator(device="cuda").manual_seed(cout + ks)
+    x = torch.randn((B, H, W, cin), device="cuda", generator=g).to(torch.bfloat16)
+    weight = torch.randn((cout, cin, ks, ks), device="cuda", generator=g) * (cin * ks * ks) ** -0.5
+    bias = torch.randn(cout, device="cuda", generator=g) * 0.1
+    wp = b.pack_conv_weight(weight)
+    ref = ref_conv(x, weight, bias, ks, "none", cin)  # (B,H,W,cout) fp32
+
+    # split output, per 64-channel block hi then lo: hi + lo reproduces the
+    # fp32 result to ~2^-16
+    sp = torch.full((B, H, W, 2 * cout), float("nan"), device="cuda", dtype=torch.bfloat16)
+    _conv_ex(x, cin, wp, bias, cout, ks, mode=EPI_SPLIT_BF16, out=sp, out_c=2 * cout, out_off=0)
+    blk = sp.reshape(B, H, W, cout // 64, 2, 64).float()
+    got = (blk[..., 0, :] + blk[..., 1, :]).reshape(B, H, W, cout)
+    d = ((got - ref).abs() - 1e-4 * ref.abs()).max().item()
+    print(f"split bf16 cout={cout} k{ks}: excess {d:.2e}")
+    assert d <= 1e-3
+
+    # extra K: a 1x1 term of another input (the middle 128 of 256 channels per
+    # pixel: a strided view), accumulated by the same MMAs
+    xfull = torch.randn((B, H, W, 2 * xc), device="cuda", generator=g).to(torch.bfloat16)
+    xin = xfull[..., 64:64 + xc]
+    wx = (torch.randn((cout, xc), device="cuda", generator=g) * xc ** -0.5).to(torch.bfloat16)
+    y = torch.full((B, cout // 4, H, W, 4), float("nan"), device="cuda")
+    _conv_ex(x, cin, wp, bias, cout, ks, mode=EPI_C4_F32, out=y, out_c=cout, out_off=0,
+             xin=xin, xin_c=xc, xin_stride=2 * xc, wx=wx[None].contiguous())
+    c4 = y.permute(0, 2, 3, 1, 4).reshape(B, H, W, cout)
+    want = ref + xin.float() @ wx.float().t()
+    d = (c4 - want).abs().max().item()
+    print(f"extra K cout={cout} k{ks}: max_abs {d:.2e}")
+    assert d <= 1e-3  # fp32 output: summation order only
