@@ -395,6 +395,8 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
     L.add_shared = epi->add_shared;
     if (epi->add && (!a16(epi->add) || epi->add_c % 4 || epi->add_c < cout))
         return einval("conv2d: addend must be 16-byte aligned, add_c a multiple of 4 and >= cout");
+    if (epi->add && (epi->mode == BVML_EPI_GRU_ZR || epi->mode == BVML_EPI_GRU_Q))
+        return einval("conv2d: the GRU epilogues take no addend (use the extra K block)");
     L.xin = epi->xin;
     L.xin_c = epi->xin_c;
     L.wx = epi->wx;

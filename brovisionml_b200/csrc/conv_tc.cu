@@ -118,6 +118,31 @@ __device__ __forceinline__ void load_addend(const ConvArgs& a, bool in, int b, i
     }
 }
 
+// The GRU state h (C4 fp32) a GRU epilogue chunk needs, into t: for GRU_ZR
+// the r channels' h (cb in [64, 128): h channels cb - 64 ..), for GRU_Q the
+// updated channels' h (cb < 64). Prefetched like the addend of the other
+// modes, through the same buffers.
+template <int EPI>
+__device__ __forceinline__ void load_gru_state(const ConvArgs& a, bool in, int b, int p, int cb,
+                                               float (&t)[32]) {
+    const int hc = EPI == (int)ConvEpi::GRU_ZR ? cb - 64 : cb;
+    if (in && hc >= 0 && hc < 64) {
+        const long hw = (long)a.H * a.W;
+        const float4* h4 = reinterpret_cast<const float4*>(a.h32) + c4_index(a, 16, b, hc / 4, p);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float4 v = h4[q * hw];
+            t[4 * q + 0] = v.x;
+            t[4 * q + 1] = v.y;
+            t[4 * q + 2] = v.z;
+            t[4 * q + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) t[i] = 0.0f;
+    }
+}
+
 // f[i] = accumulator + bias + addend t for channels cb + i < cout, else 0.
 // sbias: the bias staged in shared memory, zero past cout (float4 broadcasts).
 __device__ __forceinline__ void pre_activation(const ConvArgs& a, const float* sbias,
@@ -159,8 +184,18 @@ template <int EPI, int ACT>
 __device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias, int b, int p,
                                            int cb, const float (&t)[32],
                                            const uint32_t (&v)[32]) {
+    // GRU modes: t holds the GRU state h of these channels (prefetched), not
+    // an addend; the other modes: t is the addend
+    constexpr bool kGru = EPI == (int)ConvEpi::GRU_ZR || EPI == (int)ConvEpi::GRU_Q;
     float f[32];
-    pre_activation(a, sbias, t, cb, v, f);
+    if constexpr (kGru) {
+        float zero[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) zero[i] = 0.0f;
+        pre_activation(a, sbias, zero, cb, v, f);
+    } else {
+        pre_activation(a, sbias, t, cb, v, f);
+    }
     const long hw = (long)a.H * a.W;
     const long pix = b * hw + p;
     if constexpr (EPI == (int)ConvEpi::C4_32) {
@@ -184,11 +219,9 @@ __device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias
 #pragma unroll
             for (int q = 0; q < 4; ++q) dst[q * hw] = reinterpret_cast<const uint4*>(o)[q];
         } else if (cb < 128) {
-            const float4* h4 =
-                reinterpret_cast<const float4*>(a.h32) + c4_index(a, 16, b, (cb - 64) / 4, p);
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-                const float4 h = h4[q * hw];
+                const float4 h = make_float4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
                 o[4 * q + 0] = __float2bfloat16_rn(activate<2>(f[4 * q + 0]) * h.x);
                 o[4 * q + 1] = __float2bfloat16_rn(activate<2>(f[4 * q + 1]) * h.y);
                 o[4 * q + 2] = __float2bfloat16_rn(activate<2>(f[4 * q + 2]) * h.z);
@@ -208,7 +241,7 @@ __device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias
         alignas(16) __nv_bfloat16 o[32];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-            float4 h = h4[q * hw];
+            float4 h = make_float4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
             float* hh = reinterpret_cast<float*>(&h);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -692,7 +725,10 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             int ys, px, py, c0;
             bool in;
             geo(k, ys, px, py, in, c0);
-            load_addend(a, in, b, py * a.W + px, n0 + c0, tt);
+            if constexpr (EPI == (int)ConvEpi::GRU_ZR || EPI == (int)ConvEpi::GRU_Q)
+                load_gru_state<EPI>(a, in, b, py * a.W + px, n0 + c0, tt);
+            else
+                load_addend(a, in, b, py * a.W + px, n0 + c0, tt);
         };
         auto process = [&](int k, int buf, const float (&tt)[32]) {
             int ys, px, py, c0;

@@ -238,7 +238,7 @@ int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B
  *   o] = r * h, h the fp32 hidden state h32 (C4, 64 channels).
  * GRU_Q (:148-156): q = tanh(conv) -> h32 = (1 - z) h32 + z q, with bf16
  *   copies at hx[pixel * hx_c + o] and, when hin is not null, hin[...].
- * add (optional, every mode): a per-pixel fp32 addend in C4 layout with
+ * add (optional, every mode but the GRU ones): a per-pixel fp32 addend in C4 layout with
  *   add_c channels per frame (a multiple of 4, >= cout); channel o of frame f
  *   (f = 0 for every frame when add_shared is nonzero) joins conv[o] +
  *   bias[o] before the epilogue. It carries the part of a
