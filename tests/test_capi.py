@@ -116,6 +116,35 @@ def test_argument_errors_without_gpu():
     assert rc == 1 and "workspace" in lib.bvml_last_error().decode()
 
 
+def test_conv_argument_errors_without_gpu():
+    """bvml_conv2d_nhwc_bf16_ex validates before touching the GPU: kernel
+    size, the GRU epilogues' refusal of an addend, the extra K block's
+    layout and the split output's room."""
+    import ctypes
+
+    from brovisionml_b200._capi import (EPI_GRU_ZR, EPI_NHWC, EPI_SPLIT_BF16, ConvEpilogue,
+                                        lib)
+
+    fake = 0x10000  # aligned, never dereferenced: every call fails validation first
+
+    def call(ks=5, cout=128, cout_pad=128, **epi):
+        e = ConvEpilogue(**epi)
+        return lib.bvml_conv2d_nhwc_bf16_ex(fake, 64, 0, 64, fake, fake, 1, 8, 16, cout,
+                                            cout_pad, ks, ctypes.byref(e), fake, None)
+
+    assert call(ks=4, mode=EPI_NHWC, out=fake, out_c=128) == 1
+    assert "kernel size" in lib.bvml_last_error().decode()
+    assert call(mode=EPI_GRU_ZR, h32=fake, z=fake, rh=fake, rh_c=64, add=fake, add_c=128) == 1
+    assert "no addend" in lib.bvml_last_error().decode()
+    assert call(mode=EPI_NHWC, out=fake, out_c=128, xin=fake, xin_c=96, wx=fake) == 1
+    assert "extra K" in lib.bvml_last_error().decode()
+    assert call(mode=EPI_NHWC, out=fake, out_c=128, xin=fake, xin_c=128, xin_stride=64,
+                wx=fake) == 1
+    assert "xin_stride" in lib.bvml_last_error().decode()
+    assert call(mode=EPI_SPLIT_BF16, out=fake, out_c=128) == 1
+    assert "split" in lib.bvml_last_error().decode()
+
+
 def test_python_mirror_rejects_cpu_tensors():
     import torch
 
