@@ -392,9 +392,10 @@ def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
         "data": "synthetic (random weights of the reference's shapes, seeded inputs)",
         "config": workload_config(args, cfg, {"stage": "ConvGRU 5x5 130->64 x3, 4 heads "
                                               "(3x3 66->128, 1x1 128->128, 1x1 128->out)"}),
-        # per step: stage inputs 1, hoisted terms 3, 9 per iteration, the
-        # up-mask head 2 (last iteration), AngMF I, upsample 1
-        "gpu_launches": args.steps * (1 + 3 + 9 * I + 2 + I + 1),
+        # per step: stage inputs 1, hoisted terms 3, 6 per iteration (zr, q,
+        # heads 3x3, three head tails), the up-mask head 2 (last iteration),
+        # AngMF I, upsample 1
+        "gpu_launches": args.steps * (1 + 3 + 6 * I + 2 + I + 1),
         "stage": {"ms": round(stage_ms, 3), "tflops_model": round(tflops, 1),
                   "flops_model_per_step": flops, "tflops_executed": round(tflops_x, 1),
                   "flops_executed_per_step": flops_x},

@@ -21,7 +21,8 @@ EXPORTS = ("bvml_last_error", "bvml_abi_version", "bvml_ray_relu", "bvml_angmf_p
            "bvml_convex_upsample", "bvml_l2_normalize_nchw", "bvml_slice2d",
            "bvml_refine_workspace_bytes", "bvml_refine", "bvml_probe_events",
            "bvml_refine_noalloc", "bvml_angmf_propagate_logits", "bvml_refine_logits",
-           "bvml_conv2d_nhwc_bf16", "bvml_conv2d_nhwc_bf16_ex", "bvml_stage_inputs")
+           "bvml_conv2d_nhwc_bf16", "bvml_conv2d_nhwc_bf16_ex", "bvml_stage_inputs",
+           "bvml_head_tail_1x1")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(
@@ -82,6 +83,8 @@ EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, EPI_GRU_ZR, EPI_GRU_Q, EPI_C4_F32, EPI
 lib.bvml_conv2d_nhwc_bf16_ex.restype = _i
 lib.bvml_conv2d_nhwc_bf16_ex.argtypes = ([_vp, _i, _i, _i, _vp, _vp] + [_i] * 6
                                           + [ctypes.POINTER(ConvEpilogue), _vp, _vp])
+lib.bvml_head_tail_1x1.restype = _i
+lib.bvml_head_tail_1x1.argtypes = [_vp, _i, _i, _vp, _vp, _vp, _vp] + [_i] * 5 + [_vp, _vp, _vp]
 lib.bvml_stage_inputs.restype = _i
 lib.bvml_stage_inputs.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp]
 lib.bvml_probe_events.restype = _i

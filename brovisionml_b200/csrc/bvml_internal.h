@@ -75,6 +75,23 @@ struct ConvLaunch {
 };
 cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s);
 
+// The last two 1x1 layers of a prediction head in one kernel: x channels
+// [cin_off, cin_off + 128) (B,H,W,x_c) bf16 -> ReLU(. W2^T + b2) -> . W4^T + b4
+// -> planar (B,cout,H,W) fp16 / fp32, cout <= 64. w2 (128,128), w4 (64,128) bf16.
+struct HeadTailLaunch {
+    const void* x;
+    int x_c, cin_off;
+    const void* w2;
+    const float* b2;
+    const void* w4;
+    const float* b4;
+    int B, H, W, cout;
+    int f16;
+    void* y;
+    int* err;
+};
+cudaError_t launch_head_tail(const HeadTailLaunch& L, cudaStream_t s);
+
 cudaError_t launch_ray_relu(void* normal, SType t, const float* ray, int B, int H, int W,
                             cudaStream_t s);
 cudaError_t launch_stage_inputs(const float* h0, const float* feat, int B, int H, int W,

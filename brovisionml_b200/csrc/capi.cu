@@ -445,6 +445,38 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
     return finish(bvml::launch_conv_tc(L, static_cast<cudaStream_t>(stream)), "conv2d launch");
 }
 
+int bvml_head_tail_1x1(const void* x, int x_c, int cin_off, const void* w2, const float* b2,
+                       const void* w4, const float* b4, int B, int H, int W, int cout,
+                       int dtype, void* out, int* err, void* stream) {
+    auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (B < 0 || H < 0 || W < 0 || cout <= 0 || cout > 64 || x_c % 8 || cin_off < 0 ||
+        cin_off % 64 || cin_off + 128 > x_c)
+        return einval("head tail: bad shape (cout 1..64, 128 input channels at a multiple of "
+                      "64 within x_c)");
+    if (dtype != BVML_F32 && dtype != BVML_F16) return einval("head tail: dtype must be F32 or F16");
+    if ((long)B * H * W == 0) return finish(cudaSuccess, "head tail");
+    if ((int64_t)B * H * W > INT32_MAX / 2) return einval("head tail: too many pixels");
+    if (!x || !w2 || !b2 || !w4 || !b4 || !out || !err || !a16(x) || !a16(w2) || !a16(w4) ||
+        !a16(out))
+        return einval("head tail: null or unaligned tensor");
+    bvml::HeadTailLaunch L{};
+    L.x = x;
+    L.x_c = x_c;
+    L.cin_off = cin_off;
+    L.w2 = w2;
+    L.b2 = b2;
+    L.w4 = w4;
+    L.b4 = b4;
+    L.B = B;
+    L.H = H;
+    L.W = W;
+    L.cout = cout;
+    L.f16 = dtype == BVML_F16;
+    L.y = out;
+    L.err = err;
+    return finish(bvml::launch_head_tail(L, static_cast<cudaStream_t>(stream)), "head tail launch");
+}
+
 int bvml_stage_inputs(const float* h0, const float* feat, int B, int H, int W, float* h32,
                       void* hx, void* fx, void* stream) {
     auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };

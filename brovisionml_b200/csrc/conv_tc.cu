@@ -51,6 +51,7 @@ struct ConvArgs {
     int ks, pad;
     int tw, th, tiles_x, tiles_y;
     const float* bias;
+    const float* bias1;  // head tail: the first layer's bias (128)
     int* err;
     // epilogue targets (see ConvEpi)
     void* out;
@@ -827,6 +828,262 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     }
 }
 
+// ------------------------------------------------------------ head tail
+// The last two layers of a prediction head in one kernel (src/dsine_refine.cpp:
+// 118-125: conv1x1 128 -> 128, ReLU, conv1x1 128 -> C with C <= 64): GEMM1 of
+// a 128-pixel tile into TMEM, bias + ReLU + bf16 written by the epilogue warps
+// straight into shared memory in the 128-byte-swizzled K-major layout the MMA
+// reads (row r = pixel, 16-byte unit u at u ^ (r & 7)), GEMM2 from there, and
+// the planar epilogue -- the 128-channel intermediate never reaches global
+// memory. Both weight matrices stay resident. GEMM1 of tile i + 1 is issued
+// before GEMM2 of tile i, so the tensor core works while the epilogue
+// converts; the two GEMM1 accumulators alternate, the GEMM2 one and the
+// intermediate are single (the epilogue warps finish tile i's GEMM2 output
+// before they write tile i + 1's intermediate).
+constexpr int kHTRing = 8;         // A ring entries (16 KB: 128 pixels x 64 channels)
+constexpr int kHTW2 = 0;           // W2 resident: 2 chunks x 128 rows x 128 B
+constexpr int kHTW4 = 32768;       // W4 resident: 2 chunks x 64 rows x 128 B
+constexpr int kHTA2 = 49152;       // intermediate: 2 chunks x 128 rows x 128 B
+constexpr int kHTRingOff = 81920;  // the A ring
+
+template <int EPI>
+__global__ void __launch_bounds__(kConvThreads, 1)
+head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w2,
+                 const __grid_constant__ CUtensorMap map_w4, const __grid_constant__ CUtensorMap map_o,
+                 const ConvArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const uint32_t sbase = tc::smem_u32(smem);
+    const uint32_t bars = sbase + a.off_bar;
+    const uint32_t bar_full_a = bars;            // kHTRing: A entry loaded
+    const uint32_t bar_empty_a = bars + 64;      // kHTRing: A entry consumed
+    const uint32_t bar_acc1_full = bars + 128;   // 2: GEMM1 accumulator ready
+    const uint32_t bar_acc1_empty = bars + 144;  // 2: GEMM1 accumulator drained
+    const uint32_t bar_a2_full = bars + 160;     // intermediate written
+    const uint32_t bar_acc2_full = bars + 168;   // GEMM2 accumulator ready
+    const uint32_t bar_acc2_empty = bars + 176;  // GEMM2 accumulator drained
+    const uint32_t bar_wres = bars + 184;        // resident weights loaded
+    const uint32_t bar_end = bars + 192;         // every MMA complete
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + a.off_bar + 200);
+    int* abort_flag = reinterpret_cast<int*>(smem + a.off_bar + 204);
+    const int s_a = a.s_a;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles = a.tiles_x * a.tiles_y * a.B;
+    auto tile_of = [&](int t, int& b, int& x0, int& y0) {
+        const int tx = t % a.tiles_x;
+        const int r = t / a.tiles_x;
+        x0 = tx * a.tw;
+        y0 = (r % a.tiles_y) * a.th;
+        b = r / a.tiles_y;
+    };
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kHTRing; ++s) {
+            tc::mbar_init(bar_full_a + 8 * s, 1);
+            tc::mbar_init(bar_empty_a + 8 * s, 1);
+        }
+        for (int q = 0; q < 2; ++q) {
+            tc::mbar_init(bar_acc1_full + 8 * q, 1);
+            tc::mbar_init(bar_acc1_empty + 8 * q, kEpiWarps);
+        }
+        tc::mbar_init(bar_a2_full, kEpiWarps);
+        tc::mbar_init(bar_acc2_full, 1);
+        tc::mbar_init(bar_acc2_empty, kEpiWarps);
+        tc::mbar_init(bar_wres, 1);
+        tc::mbar_init(bar_end, 1);
+        *abort_flag = 0;
+        tc::mbar_fence_init();
+        tc::tma_prefetch_desc(&map_a);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tc::smem_u32(tmem_slot), 512);  // acc1 x 2 (256) + acc2 (64)
+        tc::tmem_relinquish();
+    }
+    float* sbias1 = reinterpret_cast<float*>(smem + a.off_bias);
+    float* sbias2 = sbias1 + 128;
+    for (int c = threadIdx.x; c < 128 + 64; c += blockDim.x) {
+        if (c < 128) sbias1[c] = a.bias1[c];
+        else sbias2[c - 128] = c - 128 < a.cout ? a.bias[c - 128] : 0.0f;
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto fail = [&](int code) {
+        atomicExch(a.err, code);
+        *reinterpret_cast<volatile int*>(abort_flag) = 1;
+    };
+    auto aborted = [&]() { return *reinterpret_cast<volatile int*>(abort_flag) != 0; };
+
+    if (warp == 0 && lane == 0) {
+        // ---------------------------------------------------------- producer
+        tc::mbar_expect_tx(bar_wres, 32768 + 16384);
+        for (int ch = 0; ch < 2; ++ch) {
+            tc::tma_load_3d(sbase + kHTW2 + ch * 16384, &map_w2, bar_wres, ch * kKC, 0, 0);
+            tc::tma_load_3d(sbase + kHTW4 + ch * 8192, &map_w4, bar_wres, ch * kKC, 0, 0);
+        }
+        int ga = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < n_tiles && !aborted(); t += gridDim.x) {
+            int b, x0, y0;
+            tile_of(t, b, x0, y0);
+            for (int ch = 0; ch < 2; ++ch, ++ga) {
+                const int s = ga % s_a, j = ga / s_a;
+                if (j > 0 && !tc::mbar_wait(bar_empty_a + 8 * s, (j - 1) & 1, kWaitLimit)) {
+                    fail(1);
+                    ok = false;
+                    break;
+                }
+                tc::mbar_expect_tx(bar_full_a + 8 * s, 16384);
+                tc::tma_load_4d(sbase + kHTRingOff + s * 16384, &map_a, bar_full_a + 8 * s,
+                                a.cin_off + ch * kKC, x0, y0, b);
+            }
+        }
+        for (int q = ga - s_a > 0 ? ga - s_a : 0; q < ga; ++q)  // nothing still landing
+            if (!tc::mbar_wait(bar_full_a + 8 * (q % s_a), (q / s_a) & 1, kWaitLimit)) fail(2);
+        if (!tc::mbar_wait(bar_wres, 0, kWaitLimit)) fail(2);
+    } else if (warp == 1 && lane == 0) {
+        // --------------------------------------------------------------- MMA
+        constexpr uint32_t idesc1 = tc::idesc_bf16_f32(kTM, 128);
+        constexpr uint32_t idesc2 = tc::idesc_bf16_f32(kTM, 64);
+        const uint32_t acc2 = tmem + 256;
+        bool ok = tc::mbar_wait(bar_wres, 0, kWaitLimit);
+        if (!ok) fail(7);
+        // GEMM2 of tile j: intermediate (2 chunks) x W4^T into acc2
+        auto gemm2 = [&](int j) {
+            if (!tc::mbar_wait(bar_a2_full, j & 1, kWaitLimit) ||
+                (j > 0 && !tc::mbar_wait(bar_acc2_empty, (j - 1) & 1, kWaitLimit)) || aborted())
+                return false;
+            tc::tc_fence_after();
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch) {
+                const uint64_t da = tc::umma_desc_k_sw128(sbase + kHTA2 + ch * 16384);
+                const uint64_t db = tc::umma_desc_k_sw128(sbase + kHTW4 + ch * 8192);
+#pragma unroll
+                for (int k = 0; k < kKC / 16; ++k)
+                    tc::umma_bf16(acc2, da + 2 * k, db + 2 * k, idesc2, ch > 0 || k > 0);
+            }
+            tc::umma_commit(bar_acc2_full);
+            return true;
+        };
+        int ga = 0, tl = 0;
+        for (int t = blockIdx.x; ok && t < n_tiles && !aborted(); t += gridDim.x, ++tl) {
+            const int buf = tl & 1, u = tl >> 1;
+            if (u > 0 && !tc::mbar_wait(bar_acc1_empty + 8 * buf, (u - 1) & 1, kWaitLimit)) {
+                fail(3);
+                ok = false;
+                break;
+            }
+            tc::tc_fence_after();
+            const uint32_t acc1 = tmem + buf * 128;
+            for (int ch = 0; ch < 2; ++ch, ++ga) {
+                const int s = ga % s_a;
+                if (!tc::mbar_wait(bar_full_a + 8 * s, (ga / s_a) & 1, kWaitLimit) || aborted()) {
+                    ok = false;
+                    break;
+                }
+                tc::tc_fence_after();
+                const uint64_t da = tc::umma_desc_k_sw128(sbase + kHTRingOff + s * 16384);
+                const uint64_t db = tc::umma_desc_k_sw128(sbase + kHTW2 + ch * 16384);
+#pragma unroll
+                for (int k = 0; k < kKC / 16; ++k)
+                    tc::umma_bf16(acc1, da + 2 * k, db + 2 * k, idesc1, ch > 0 || k > 0);
+                tc::umma_commit(bar_empty_a + 8 * s);
+            }
+            if (!ok) {
+                fail(4);
+                break;
+            }
+            tc::umma_commit(bar_acc1_full + 8 * buf);
+            if (tl > 0 && !gemm2(tl - 1)) {
+                fail(4);
+                ok = false;
+                break;
+            }
+        }
+        if (ok && tl > 0 && !gemm2(tl - 1)) fail(4);
+        tc::umma_commit(bar_end);  // also after an abort: every issued MMA has completed
+        if (!tc::mbar_wait(bar_end, 0, kWaitLimit)) fail(5);
+    } else if (warp >= 2) {
+        // ---------------------------------------------------------- epilogue
+        const int wq = warp & 3, grp = (warp - 2) >> 2;
+        const int row = wq * 32 + lane;  // pixel of the tile = row of the intermediate
+        const float zero[32] = {};
+        int tl = 0, pcount = 0;
+        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tl) {
+            const int buf = tl & 1, u = tl >> 1;
+            if (!tc::mbar_wait(bar_acc1_full + 8 * buf, u & 1, kWaitLimit)) {
+                fail(6);
+                break;
+            }
+            if (aborted()) break;
+            tc::tc_fence_after();
+            int b, x0, y0;
+            tile_of(t, b, x0, y0);
+            // GEMM1 columns [64 grp, 64 grp + 64): bias, ReLU, bf16 -> intermediate
+            // chunk grp, row `row`
+            uint8_t* a2row = smem + kHTA2 + grp * 16384 + row * 128;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                uint32_t v[32];
+                tc::tmem_ld_32cols(tmem + buf * 128 + grp * 64 + c * 32 + ((uint32_t)(wq * 32) << 16),
+                                   v);
+                tc::tmem_ld_wait();
+                alignas(16) __nv_bfloat16 o[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    o[i] = __float2bfloat16_rn(
+                        fmaxf(__uint_as_float(v[i]) + sbias1[grp * 64 + c * 32 + i], 0.0f));
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<uint4*>(a2row + (((c * 4 + q) ^ (row & 7)) << 4)) =
+                        reinterpret_cast<const uint4*>(o)[q];
+            }
+            tc::fence_proxy_async_smem();  // the MMA reads the intermediate through the async proxy
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                tc::mbar_arrive(bar_a2_full);
+                tc::mbar_arrive(bar_acc1_empty + 8 * buf);
+            }
+            // GEMM2 columns [32 grp, 32 grp + 32): bias, planar store
+            if (!tc::mbar_wait(bar_acc2_full, tl & 1, kWaitLimit)) {
+                fail(6);
+                break;
+            }
+            tc::tc_fence_after();
+            uint32_t v[32];
+            tc::tmem_ld_32cols(tmem + 256 + grp * 32 + ((uint32_t)(wq * 32) << 16), v);
+            tc::tmem_ld_wait();
+            const int cb = grp * 32;
+            const int px0 = x0 + (wq * 32) % a.tw, py0 = y0 + (wq * 32) / a.tw;
+            if (cb < a.cout && px0 < a.W && py0 < a.H) {
+                const int slot = (warp - 2) * 2 + (pcount & 1);
+                uint8_t* stg = smem + a.off_out + slot * stage_warp_bytes(EPI);
+                const uint32_t stg_addr = sbase + a.off_out + slot * stage_warp_bytes(EPI);
+                if constexpr (EPI == (int)ConvEpi::PLANAR16)
+                    planar_chunk_tma<__half>(a, &map_o, reinterpret_cast<__half*>(stg), stg_addr,
+                                             lane, px0, py0, b, cb, sbias2, zero, v);
+                else
+                    planar_chunk_tma<float>(a, &map_o, reinterpret_cast<float*>(stg), stg_addr,
+                                            lane, px0, py0, b, cb, sbias2, zero, v);
+                ++pcount;
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(bar_acc2_empty);
+        }
+        if (lane == 0) tc::bulk_wait_all();  // stores complete before exit
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 512);
+    }
+}
+
 // ------------------------------------------------------------------- host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -1107,6 +1364,98 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
         case ConvEpi::GRU_Q: return launch_act<(int)ConvEpi::GRU_Q, 0>(n, mt, bres, ma, mb, mo, mx, mbx, a, smem, s);
     }
     return cudaErrorInvalidValue;
+}
+
+
+cudaError_t launch_head_tail(const HeadTailLaunch& L, cudaStream_t s) {
+    if (L.B == 0 || L.H == 0 || L.W == 0) return cudaSuccess;
+    ConvArgs a{};
+    a.B = L.B;
+    a.H = L.H;
+    a.W = L.W;
+    a.cin_off = L.cin_off;
+    a.cout = L.cout;
+    a.cout_pad = 64;
+    a.bias = L.b4;
+    a.bias1 = L.b2;
+    a.err = L.err;
+    a.out = L.y;
+    // pixel tile: the tw with the fewest tiles (ties to the wider one)
+    long best = -1;
+    for (int tw : {128, 64, 32, 16}) {
+        const int th = kTM / tw;
+        const long tiles = (long)((L.W + tw - 1) / tw) * ((L.H + th - 1) / th);
+        if (best < 0 || tiles < best) {
+            best = tiles;
+            a.tw = tw;
+            a.th = th;
+        }
+    }
+    a.tiles_x = (L.W + a.tw - 1) / a.tw;
+    a.tiles_y = (L.H + a.th - 1) / a.th;
+    if ((long)a.tiles_x * a.tiles_y * L.B > 0x7fffffffL) return cudaErrorInvalidConfiguration;
+    const int es = L.f16 ? 2 : 4;
+    a.planar_direct = (L.W * es) % 16 != 0;
+    // shared memory: weights, intermediate, ring, planar staging, biases, barriers
+    const int stage = kEpiWarps * 2 * 32 * 32 * es;
+    const int fixed = kHTRingOff + stage + 1024 + kBarBytes + 1024;  // bias 768 B, rounded
+    const int ring = (kSmemLimit - fixed) / 16384;
+    a.s_a = ring < kHTRing ? ring : kHTRing;
+    if (a.s_a < 2) return cudaErrorInvalidConfiguration;
+    a.off_out = kHTRingOff + a.s_a * 16384;
+    a.off_bias = a.off_out + stage;
+    a.off_bar = a.off_bias + 1024;
+    const int smem = a.off_bar + kBarBytes + 1024;
+
+    CUtensorMap ma, mw2, mw4, mo;
+    const cuuint64_t dims_a[4] = {(cuuint64_t)L.x_c, (cuuint64_t)L.W, (cuuint64_t)L.H,
+                                  (cuuint64_t)L.B};
+    const cuuint64_t str_a[3] = {(cuuint64_t)L.x_c * 2, (cuuint64_t)L.W * L.x_c * 2,
+                                 (cuuint64_t)L.H * L.W * L.x_c * 2};
+    const cuuint32_t box_a[4] = {(cuuint32_t)kKC, (cuuint32_t)a.tw, (cuuint32_t)a.th, 1};
+    const cuuint64_t dims_w2[3] = {128, 128, 1};
+    const cuuint64_t str_w2[2] = {256, 128 * 256};
+    const cuuint32_t box_w2[3] = {(cuuint32_t)kKC, 128, 1};
+    const cuuint64_t dims_w4[3] = {128, 64, 1};
+    const cuuint64_t str_w4[2] = {256, 64 * 256};
+    const cuuint32_t box_w4[3] = {(cuuint32_t)kKC, 64, 1};
+    if (!encode(&ma, L.x, 4, dims_a, str_a, box_a) || !encode(&mw2, L.w2, 3, dims_w2, str_w2, box_w2) ||
+        !encode(&mw4, L.w4, 3, dims_w4, str_w4, box_w4))
+        return cudaErrorInvalidValue;
+    mo = ma;  // unused when the rows take plain stores
+    if (!a.planar_direct) {
+        const int pw = a.tw < 32 ? a.tw : 32;
+        const cuuint64_t dims_o[4] = {(cuuint64_t)L.W, (cuuint64_t)L.H, (cuuint64_t)L.cout,
+                                      (cuuint64_t)L.B};
+        const cuuint64_t str_o[3] = {(cuuint64_t)L.W * es, (cuuint64_t)L.H * L.W * es,
+                                     (cuuint64_t)L.cout * L.H * L.W * es};
+        const cuuint32_t box_o[4] = {(cuuint32_t)pw, (cuuint32_t)(32 / pw), 32, 1};
+        if (!encode(&mo, L.y, 4, dims_o, str_o, box_o,
+                    es == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+            return cudaErrorInvalidValue;
+    }
+    int dev = 0, sms = 0;
+    cudaError_t e;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return e;
+    const long tiles = (long)a.tiles_x * a.tiles_y * L.B;
+    const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
+    if (L.f16) {
+        auto kern = head_tail_kernel<(int)ConvEpi::PLANAR16>;
+        if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) !=
+            cudaSuccess)
+            return e;
+        kern<<<grid, kConvThreads, smem, s>>>(ma, mw2, mw4, mo, a);
+    } else {
+        auto kern = head_tail_kernel<(int)ConvEpi::PLANAR32>;
+        if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) !=
+            cudaSuccess)
+            return e;
+        kern<<<grid, kConvThreads, smem, s>>>(ma, mw2, mw4, mo, a);
+    }
+    return cudaGetLastError();
 }
 
 }  // namespace bvml

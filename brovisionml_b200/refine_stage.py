@@ -25,13 +25,16 @@ no per-pixel table; gu in the epilogue (one frame, L2-resident):
   q   = tanh(conv5x5(r*h, W_q[:, :64]) + gx[128:])      epilogue
          h = (1-z) h + z q (fp32 state) and its bf16 copy
   each head: conv3x3 -> ReLU -> conv1x1 -> ReLU -> conv1x1; the four 3x3
-         layers as one GEMM (N = 512) over h with gu added; the 1x1 layers
-         per head on 128-channel slices; the last layer writes planar NCHW
-         (fp16 or fp32): prob (25), xy (50), angle (25), up_mask (576) logits.
+         layers as one GEMM (N = 512) over h with gu added; the two 1x1
+         layers of prob (25), xy (50) and angle (25) as one kernel each with
+         the intermediate on chip (bvml_head_tail_1x1), the up_mask (576)
+         head's as two; the last layer writes planar NCHW (fp16 or fp32)
+         logits.
 
 (The GRU and heads never read the normals, so all iterations run first and
 the ops unit consumes their outputs afterwards.) 3 tensor-core launches per
-refinement plus 11 per iteration, no separate elementwise or layout pass;
+refinement plus 8 per iteration (6 without the up-mask head), no separate
+elementwise or layout pass;
 the 5x5 GEMMs contract 25 x 64 instead of 25 x 130 (padded: 192) channels,
 the heads' 3x3 9 x 64 instead of 9 x 66 (padded: 128). Weights are the
 reference's (OIHW fp32, safetensors names ``gru.convz`` ...
@@ -202,6 +205,13 @@ class RefineStage:
         """A stage with the weights of a DSINE checkpoint (model.safetensors)."""
         return cls(load_params(path), B, h, w, device=device, out_dtype=out_dtype)
 
+    def _tail(self, k: int, c: int, code: int, dst: torch.Tensor) -> None:
+        """Head k's two 1x1 layers in one launch (bvml_head_tail_1x1)."""
+        check(lib.bvml_head_tail_1x1(
+            _p(self.t1), 4 * HEAD_HIDDEN, k * HEAD_HIDDEN, _p(self.w_c2[k]), _p(self.b_c2[k]),
+            _p(self.w_c4[k]), _p(self.b_c4[k]), self.B, self.h, self.w, c, code, _p(dst),
+            _p(self.err), _stream(self.dev)))
+
     # one launch through the C ABI
     def _conv(self, x, cin_off, cin_pad, w, bias, cout, ks, **epi):
         e = ConvEpilogue(**{k: (_p(v) if isinstance(v, torch.Tensor) else v)
@@ -258,8 +268,12 @@ class RefineStage:
                        add_c=4 * HEAD_HIDDEN, add_shared=1)
             planar = EPI_PLANAR_F16 if self.out_dtype == torch.float16 else EPI_PLANAR_F32
             dsts = (out.prob, out.xy, out.angle, out.up_mask)
+            code = 1 if self.out_dtype == torch.float16 else 0
             for k, (name, c) in enumerate(HEADS):
                 if name == "up_prob_head" and not up_mask:
+                    continue
+                if c <= 64:  # 1x1 -> ReLU -> 1x1 in one kernel, intermediate on chip
+                    self._tail(k, c, code, dsts[k])
                     continue
                 self._conv(self.t1, k * HEAD_HIDDEN, HEAD_HIDDEN, self.w_c2[k], self.b_c2[k],
                            HEAD_HIDDEN, 1, mode=EPI_NHWC, act=1, out=self.t2,
@@ -312,9 +326,10 @@ def _main(argv=None) -> None:
     run `steps` iterations of the stage on random weights over B frames of
     the 160 x 90 grid (720p) and print each launch's time of the last
     iteration and of start (CUDA events). Also the target for profiling one
-    layer: start runs twice (3 convolutions each, the second one timed), then
-    the convolutions of iteration k are numbers 6 + 11 k .. 16 + 11 k (zr, q,
-    heads 3x3, then per head 1x1 and 1x1 planar)."""
+    layer: start runs twice (3 conv_tc kernels each, the second one timed),
+    then each iteration launches 5 conv_tc kernels (zr, q, heads 3x3, the
+    up-mask head's two 1x1) -- numbers 6 + 5 k .. 10 + 5 k -- and 3
+    head_tail kernels (prob, xy, angle heads' last two layers)."""
     import argparse
 
     ap = argparse.ArgumentParser()
@@ -338,22 +353,24 @@ def _main(argv=None) -> None:
     st.start(h0, feat, uv.float())
     e1.record()
     marks = []
-    conv = st._conv
 
-    def timed(*a, **k):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        conv(*a, **k)
-        e1.record()
-        marks.append((e0, e1))
+    def timed(fn):
+        def run(*a, **k):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn(*a, **k)
+            e1.record()
+            marks.append((e0, e1))
+        return run
 
-    st._conv = timed
+    st._conv, st._tail = timed(st._conv), timed(st._tail)
     for _ in range(args.steps):
         marks.clear()
         st.step()
     torch.cuda.synchronize()
     st.check_pipeline()
-    names = ["zr", "q", "heads3x3"] + [f"{n}.{i}" for n, _ in HEADS for i in (2, 4)]
+    names = (["zr", "q", "heads3x3"] + [f"{n}.2+4" for n, c in HEADS if c <= 64] +
+             [f"{n}.{i}" for n, c in HEADS if c > 64 for i in (2, 4)])
     print(f"start {e0.elapsed_time(e1):.3f} " +
           " ".join(f"{n} {a.elapsed_time(b):.3f}" for n, (a, b) in zip(names, marks)))
 

@@ -286,6 +286,24 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
                              int ks, const bvml_conv_epilogue* epi, int* err, void* stream);
 
 /*
+ * The last two layers of a prediction head in one kernel: conv1x1 (128 ->
+ * 128) + ReLU + conv1x1 (128 -> cout), src/dsine_refine.cpp:118-125, which
+ * the reference runs as two brotensor conv2d_forward calls and a relu_forward
+ * with the 128-channel intermediate in memory; here it stays on the chip.
+ *   x     (B,H,W,x_c) bf16 NHWC; input channels [cin_off, cin_off + 128)
+ *         (cin_off a multiple of 64)
+ *   w2    (1,128,128) bf16, b2 (128) fp32: the first 1x1 layer
+ *   w4    (1,64,128) bf16 (rows >= cout zero), b4 (cout) fp32: the second
+ *   out   (B,cout,H,W) planar, dtype BVML_F16 or BVML_F32; cout <= 64
+ *   err   as bvml_conv2d_nhwc_bf16
+ * The results equal the two separate convolutions'
+ * (bvml_conv2d_nhwc_bf16_ex with NHWC + ReLU, then planar), bit for bit.
+ */
+int bvml_head_tail_1x1(const void* x, int x_c, int cin_off, const void* w2, const float* b2,
+                       const void* w4, const float* b4, int B, int H, int W, int cout,
+                       int dtype, void* out, int* err, void* stream);
+
+/*
  * The refine stage's inputs in its layouts, one pass: the decoder's hidden
  * state h0 and feature (B,64,H,W) fp32 planar -> the GRU state h32 (C4 fp32,
  * (B,16,H,W,4)) and its bf16 NHWC copy hx (B,H,W,64), and the feature as

@@ -23,7 +23,7 @@ def test_header_symbols_exported():
     from brovisionml_b200 import _capi
 
     syms = declared_symbols()
-    assert len(syms) == 16, syms
+    assert len(syms) == 17, syms
     assert sorted(_capi.EXPORTS) == syms
     for s in syms:
         assert hasattr(b.lib, s), s

@@ -189,3 +189,40 @@ def test_conv_extra_k_and_split(cout, ks):
     d = (c4 - want).abs().max().item()
     print(f"extra K cout={cout} k{ks}: max_abs {d:.2e}")
     assert d <= 1e-3  # fp32 output: summation order only
+
+
+@pytest.mark.parametrize("W,cout,f16", [(40, 25, True), (44, 50, True), (37, 25, False),
+                                        (160, 64, True)])
+def test_head_tail_matches_two_convolutions(W, cout, f16):
+    """bvml_head_tail_1x1 (1x1 -> ReLU -> 1x1 with the intermediate on chip)
+    equals the two separate convolutions bit for bit: the same products,
+    the same bf16 rounding of the intermediate, the same summation order."""
+    import brovisionml_b200 as b
+    from brovisionml_b200._capi import EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, check, lib
+    from brovisionml_b200.ops import _p, _stream
+
+    B, H, k = 2, 19, 1
+    g = torch.Generator(device="cuda").manual_seed(W + cout)
+    t1 = torch.randn((B, H, W, 512), device="cuda", generator=g).to(torch.bfloat16)
+    w2 = torch.randn((128, 128, 1, 1), device="cuda", generator=g) * 128 ** -0.5
+    b2 = torch.randn(128, device="cuda", generator=g) * 0.1
+    w4 = torch.randn((cout, 128, 1, 1), device="cuda", generator=g) * 128 ** -0.5
+    b4 = torch.randn(cout, device="cuda", generator=g) * 0.1
+    w2p, w4p = b.pack_conv_weight(w2), b.pack_conv_weight(w4, 128, 64)
+    dt = torch.float16 if f16 else torch.float32
+    t2 = torch.zeros((B, H, W, 512), device="cuda", dtype=torch.bfloat16)
+    _conv_ex(t1[..., k * 128:(k + 1) * 128].contiguous(), 128, w2p, b2, 128, 1, mode=EPI_NHWC,
+             act=1, out=t2, out_c=512, out_off=k * 128)
+    want = torch.full((B, cout, H, W), float("nan"), device="cuda", dtype=dt)
+    _conv_ex(t2[..., k * 128:(k + 1) * 128].contiguous(), 128, w4p, b4, cout, 1,
+             mode=EPI_PLANAR_F16 if f16 else EPI_PLANAR_F32, out=want)
+    got = torch.full((B, cout, H, W), float("nan"), device="cuda", dtype=dt)
+    err = torch.zeros(1, device="cuda", dtype=torch.int32)
+    check(lib.bvml_head_tail_1x1(_p(t1), 512, k * 128, _p(w2p), _p(b2), _p(w4p), _p(b4), B, H,
+                                 W, cout, 1 if f16 else 0, _p(got), _p(err),
+                                 _stream(torch.device("cuda"))))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    d = (got.float() - want.float()).abs().max().item()
+    print(f"head tail W={W} cout={cout} f16={f16}: max |d| {d:.2e}")
+    assert torch.equal(got, want)
