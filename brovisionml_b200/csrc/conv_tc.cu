@@ -835,16 +835,16 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 // straight into shared memory in the 128-byte-swizzled K-major layout the MMA
 // reads (row r = pixel, 16-byte unit u at u ^ (r & 7)), GEMM2 from there, and
 // the planar epilogue -- the 128-channel intermediate never reaches global
-// memory. Both weight matrices stay resident. GEMM1 of tile i + 1 is issued
-// before GEMM2 of tile i, so the tensor core works while the epilogue
-// converts; the two GEMM1 accumulators alternate, the GEMM2 one and the
-// intermediate are single (the epilogue warps finish tile i's GEMM2 output
-// before they write tile i + 1's intermediate).
-constexpr int kHTRing = 8;         // A ring entries (16 KB: 128 pixels x 64 channels)
-constexpr int kHTW2 = 0;           // W2 resident: 2 chunks x 128 rows x 128 B
-constexpr int kHTW4 = 32768;       // W4 resident: 2 chunks x 64 rows x 128 B
-constexpr int kHTA2 = 49152;       // intermediate: 2 chunks x 128 rows x 128 B
-constexpr int kHTRingOff = 81920;  // the A ring
+// memory. Both weight matrices stay resident. Everything after the operand
+// loads is double buffered -- GEMM1 and GEMM2 accumulators, intermediate --
+// and issued one tile apart: the MMA lane issues GEMM1 of tile i + 1 before
+// GEMM2 of tile i, the epilogue warps convert tile i + 1's GEMM1 output
+// before they store tile i's GEMM2 output, so neither waits on the other.
+constexpr int kHTRing = 8;          // A ring entries (16 KB: 128 pixels x 64 channels)
+constexpr int kHTW2 = 0;            // W2 resident: 2 chunks x 128 rows x 128 B
+constexpr int kHTW4 = 32768;        // W4 resident: 2 chunks x 64 rows x 128 B
+constexpr int kHTA2 = 49152;        // intermediates: 2 x (2 chunks x 128 rows x 128 B)
+constexpr int kHTRingOff = 114688;  // the A ring
 
 template <int EPI>
 __global__ void __launch_bounds__(kConvThreads, 1)
@@ -860,13 +860,13 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     const uint32_t bar_empty_a = bars + 64;      // kHTRing: A entry consumed
     const uint32_t bar_acc1_full = bars + 128;   // 2: GEMM1 accumulator ready
     const uint32_t bar_acc1_empty = bars + 144;  // 2: GEMM1 accumulator drained
-    const uint32_t bar_a2_full = bars + 160;     // intermediate written
-    const uint32_t bar_acc2_full = bars + 168;   // GEMM2 accumulator ready
-    const uint32_t bar_acc2_empty = bars + 176;  // GEMM2 accumulator drained
-    const uint32_t bar_wres = bars + 184;        // resident weights loaded
-    const uint32_t bar_end = bars + 192;         // every MMA complete
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + a.off_bar + 200);
-    int* abort_flag = reinterpret_cast<int*>(smem + a.off_bar + 204);
+    const uint32_t bar_a2_full = bars + 160;     // 2: intermediate written
+    const uint32_t bar_acc2_full = bars + 176;   // 2: GEMM2 accumulator ready
+    const uint32_t bar_acc2_empty = bars + 192;  // 2: GEMM2 accumulator drained
+    const uint32_t bar_wres = bars + 208;        // resident weights loaded
+    const uint32_t bar_end = bars + 216;         // every MMA complete
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + a.off_bar + 224);
+    int* abort_flag = reinterpret_cast<int*>(smem + a.off_bar + 228);
     const int s_a = a.s_a;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -886,10 +886,10 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         for (int q = 0; q < 2; ++q) {
             tc::mbar_init(bar_acc1_full + 8 * q, 1);
             tc::mbar_init(bar_acc1_empty + 8 * q, kEpiWarps);
+            tc::mbar_init(bar_a2_full + 8 * q, kEpiWarps);
+            tc::mbar_init(bar_acc2_full + 8 * q, 1);
+            tc::mbar_init(bar_acc2_empty + 8 * q, kEpiWarps);
         }
-        tc::mbar_init(bar_a2_full, kEpiWarps);
-        tc::mbar_init(bar_acc2_full, 1);
-        tc::mbar_init(bar_acc2_empty, kEpiWarps);
         tc::mbar_init(bar_wres, 1);
         tc::mbar_init(bar_end, 1);
         *abort_flag = 0;
@@ -897,7 +897,7 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         tc::tma_prefetch_desc(&map_a);
     }
     if (warp == 1) {
-        tc::tmem_alloc(tc::smem_u32(tmem_slot), 512);  // acc1 x 2 (256) + acc2 (64)
+        tc::tmem_alloc(tc::smem_u32(tmem_slot), 512);  // acc1 x 2 (256) + acc2 x 2 (128)
         tc::tmem_relinquish();
     }
     float* sbias1 = reinterpret_cast<float*>(smem + a.off_bias);
@@ -947,24 +947,27 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         // --------------------------------------------------------------- MMA
         constexpr uint32_t idesc1 = tc::idesc_bf16_f32(kTM, 128);
         constexpr uint32_t idesc2 = tc::idesc_bf16_f32(kTM, 64);
-        const uint32_t acc2 = tmem + 256;
         bool ok = tc::mbar_wait(bar_wres, 0, kWaitLimit);
         if (!ok) fail(7);
-        // GEMM2 of tile j: intermediate (2 chunks) x W4^T into acc2
+        // GEMM2 of tile j: intermediate j & 1 (2 chunks) x W4^T into acc2 j & 1
         auto gemm2 = [&](int j) {
-            if (!tc::mbar_wait(bar_a2_full, j & 1, kWaitLimit) ||
-                (j > 0 && !tc::mbar_wait(bar_acc2_empty, (j - 1) & 1, kWaitLimit)) || aborted())
+            const int q = j & 1, v = j >> 1;
+            if (!tc::mbar_wait(bar_a2_full + 8 * q, v & 1, kWaitLimit) ||
+                (v > 0 && !tc::mbar_wait(bar_acc2_empty + 8 * q, (v - 1) & 1, kWaitLimit)) ||
+                aborted())
                 return false;
             tc::tc_fence_after();
+            const uint32_t acc2 = tmem + 256 + q * 64;
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch) {
-                const uint64_t da = tc::umma_desc_k_sw128(sbase + kHTA2 + ch * 16384);
+                const uint64_t da =
+                    tc::umma_desc_k_sw128(sbase + kHTA2 + q * 32768 + ch * 16384);
                 const uint64_t db = tc::umma_desc_k_sw128(sbase + kHTW4 + ch * 8192);
 #pragma unroll
                 for (int k = 0; k < kKC / 16; ++k)
                     tc::umma_bf16(acc2, da + 2 * k, db + 2 * k, idesc2, ch > 0 || k > 0);
             }
-            tc::umma_commit(bar_acc2_full);
+            tc::umma_commit(bar_acc2_full + 8 * q);
             return true;
         };
         int ga = 0, tl = 0;
@@ -1010,20 +1013,58 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         const int wq = warp & 3, grp = (warp - 2) >> 2;
         const int row = wq * 32 + lane;  // pixel of the tile = row of the intermediate
         const float zero[32] = {};
-        int tl = 0, pcount = 0;
+        int pcount = 0;
+        // E2 of tile j at (b, x0, y0): GEMM2 columns [32 grp, 32 grp + 32) +
+        // bias, planar store
+        auto e2 = [&](int j, int b, int x0, int y0) {
+            const int q = j & 1;
+            if (!tc::mbar_wait(bar_acc2_full + 8 * q, (j >> 1) & 1, kWaitLimit)) {
+                fail(6);
+                return false;
+            }
+            tc::tc_fence_after();
+            uint32_t v[32];
+            tc::tmem_ld_32cols(tmem + 256 + q * 64 + grp * 32 + ((uint32_t)(wq * 32) << 16), v);
+            tc::tmem_ld_wait();
+            const int cb = grp * 32;
+            const int px0 = x0 + (wq * 32) % a.tw, py0 = y0 + (wq * 32) / a.tw;
+            if (cb < a.cout && px0 < a.W && py0 < a.H) {
+                const int slot = (warp - 2) * 2 + (pcount & 1);
+                uint8_t* stg = smem + a.off_out + slot * stage_warp_bytes(EPI);
+                const uint32_t stg_addr = sbase + a.off_out + slot * stage_warp_bytes(EPI);
+                if constexpr (EPI == (int)ConvEpi::PLANAR16)
+                    planar_chunk_tma<__half>(a, &map_o, reinterpret_cast<__half*>(stg), stg_addr,
+                                             lane, px0, py0, b, cb, sbias2, zero, v);
+                else
+                    planar_chunk_tma<float>(a, &map_o, reinterpret_cast<float*>(stg), stg_addr,
+                                            lane, px0, py0, b, cb, sbias2, zero, v);
+                ++pcount;
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(bar_acc2_empty + 8 * q);
+            return true;
+        };
+        int tl = 0, pb = 0, px = 0, py = 0;  // the previous tile's frame and origin
+        bool ok = true;
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tl) {
             const int buf = tl & 1, u = tl >> 1;
             if (!tc::mbar_wait(bar_acc1_full + 8 * buf, u & 1, kWaitLimit)) {
                 fail(6);
+                ok = false;
                 break;
             }
-            if (aborted()) break;
+            if (aborted()) {
+                ok = false;
+                break;
+            }
             tc::tc_fence_after();
             int b, x0, y0;
             tile_of(t, b, x0, y0);
-            // GEMM1 columns [64 grp, 64 grp + 64): bias, ReLU, bf16 -> intermediate
-            // chunk grp, row `row`
-            uint8_t* a2row = smem + kHTA2 + grp * 16384 + row * 128;
+            // E1: GEMM1 columns [64 grp, 64 grp + 64) + bias, ReLU, bf16 ->
+            // intermediate buf, chunk grp, row `row` (its previous reader, GEMM2
+            // of tile tl - 2, completed before this warp's E2 of that tile)
+            uint8_t* a2row = smem + kHTA2 + buf * 32768 + grp * 16384 + row * 128;
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 uint32_t v[32];
@@ -1044,36 +1085,18 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                tc::mbar_arrive(bar_a2_full);
+                tc::mbar_arrive(bar_a2_full + 8 * buf);
                 tc::mbar_arrive(bar_acc1_empty + 8 * buf);
             }
-            // GEMM2 columns [32 grp, 32 grp + 32): bias, planar store
-            if (!tc::mbar_wait(bar_acc2_full, tl & 1, kWaitLimit)) {
-                fail(6);
+            if (tl > 0 && !e2(tl - 1, pb, px, py)) {
+                ok = false;
                 break;
             }
-            tc::tc_fence_after();
-            uint32_t v[32];
-            tc::tmem_ld_32cols(tmem + 256 + grp * 32 + ((uint32_t)(wq * 32) << 16), v);
-            tc::tmem_ld_wait();
-            const int cb = grp * 32;
-            const int px0 = x0 + (wq * 32) % a.tw, py0 = y0 + (wq * 32) / a.tw;
-            if (cb < a.cout && px0 < a.W && py0 < a.H) {
-                const int slot = (warp - 2) * 2 + (pcount & 1);
-                uint8_t* stg = smem + a.off_out + slot * stage_warp_bytes(EPI);
-                const uint32_t stg_addr = sbase + a.off_out + slot * stage_warp_bytes(EPI);
-                if constexpr (EPI == (int)ConvEpi::PLANAR16)
-                    planar_chunk_tma<__half>(a, &map_o, reinterpret_cast<__half*>(stg), stg_addr,
-                                             lane, px0, py0, b, cb, sbias2, zero, v);
-                else
-                    planar_chunk_tma<float>(a, &map_o, reinterpret_cast<float*>(stg), stg_addr,
-                                            lane, px0, py0, b, cb, sbias2, zero, v);
-                ++pcount;
-            }
-            tc::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(bar_acc2_empty);
+            pb = b;
+            px = x0;
+            py = y0;
         }
+        if (ok && tl > 0) e2(tl - 1, pb, px, py);
         if (lane == 0) tc::bulk_wait_all();  // stores complete before exit
     }
     tc::tc_fence_before();
