@@ -123,7 +123,7 @@ stage_inputs_kernel(const float* __restrict__ h0, const float* __restrict__ feat
     for (long i = (long)blockIdx.x * kThreads + threadIdx.x; i < total;
          i += (long)gridDim.x * kThreads) {
         const long b = i / HW, p = i - b * HW;
-#pragma unroll 2
+#pragma unroll
         for (int g = 0; g < 8; ++g) {
             float v[8];
 #pragma unroll
