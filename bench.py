@@ -2,19 +2,21 @@
 """Benchmark of the DSINE refine-ops unit on B200 (one process per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg4]
-                    [--impl ours|reference]
+                    [--impl ours|reference] [--frames F] [--no-weak]
+                    [--no-bands] [--no-e2e] [--no-cpu]
 
 A step is one pass of the unit over one batch: the initial RayReLU, I AngMF
 iterations and the convex 8x upsample (+ L2, crop), i.e. one bvml_refine
-call. The default workload is BASELINE.json config 4 -- B = 256 frames of
-720x1280 per GPU (grid 90x160), fp16 storage, 5x5 window at dilation 1, 5
-iterations -- the configuration its Mpixel/s metric is swept on over 1/2/4/8
-GPUs. Under torchrun every rank processes its own 256 frames (image-parallel,
-no collective on the data path: weak scaling); time is the max over ranks.
+call. The default workload is BASELINE.json config 4 -- 256 frames of
+720x1280 IN TOTAL (grid 90x160), fp16 storage, 5x5 window at dilation 1, 5
+iterations -- split image-parallel over the N ranks with
+sharding.plan_frames (32 frames per GPU at N = 8): strong scaling, no
+collective on the data path, time = max over ranks.
 
 Inputs are seeded synthetic tensors with the benchmark generators'
-distributions (no dataset exists for this path). They total ~9.4 GB per GPU,
-far above the 126 MB L2, so no L2 flush is needed between steps.
+distributions (no dataset exists for this path). At 256 frames they total
+~9.4 GB on one GPU and 1.2 GB per GPU at N = 8, far above the 126 MB L2 in
+both cases, so no L2 flush is needed between steps.
 
 The JSON line carries, beyond the driver contract:
   roofline      the dominant kernel's algorithmic bytes per launch over its
@@ -24,20 +26,29 @@ The JSON line carries, beyond the driver contract:
                 carry no extra stream operations) against
                 MEASURED_PEAKS.json's HBM copy bandwidth;
   unit_roofline the same for the whole step (the fused refinement);
+  weak          (N > 1) the same unit with 256 frames on EVERY rank;
+  bands         config 3: one 4096^2 frame (grid 512^2, 7x7, fp32) as exact
+                halo row bands over the N ranks, timed three ways: the band
+                compute alone; compute + NCCL gather of the owned rows to
+                rank 0 + device-to-host copy of the frame there; compute +
+                each rank copying its owned rows into one shared pinned host
+                frame (the gather to host over every GPU's own PCIe link);
   e2e           the same metric through the host-buffer API
                 (brovisionml_b200.pipeline), pinned host inputs copied in and
                 the result copied out every step;
   cpu_baseline  the reference's own CPU ops (oracle/_ref) on this host's
-                cores, on a bounded sample of the same workload (rank 0, N=1).
+                cores -- all cores and one thread -- on a bounded sample of
+                the same workload (rank 0, N=1), with the angular error of
+                the GPU result on that sample.
 
 ``--impl reference`` times the reference CPU implementation alone (rank 0;
-other ranks exit) and prints the same metric with "impl": "reference".
+other ranks exit) with the same sampling routine and prints the same metric
+with "impl": "reference".
 """
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import sys
@@ -49,7 +60,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 CONFIGS = {
-    # name: full-res H, W, frames per GPU, window, dilation, iterations, storage, full-res RayReLU
+    # name: full-res H, W, frames in total (split over the ranks), window,
+    # dilation, iterations, storage, full-res RayReLU
     "cfg4": dict(H=720, W=1280, B=256, ps=5, dil=1, iters=5, f16=True, rr=False),
     "cfg2": dict(H=1024, W=1024, B=16, ps=5, dil=2, iters=5, f16=False, rr=False),
     "cfg2h": dict(H=1024, W=1024, B=16, ps=5, dil=2, iters=5, f16=True, rr=False),
@@ -145,21 +157,29 @@ class ClockSampler:
 
 # ----------------------------------------------------------------- inputs
 
-def make_device_inputs(cfg, seed, device, torch, logits=False):
-    """Seeded synthetic inputs on the GPU, generator distributions of the
-    benchmark configurations (oracle.gen_unit draws the same laws on CPU).
-    logits: prob / angle as raw head outputs instead (N(0, 2.5) and
-    N(-2.5, 1.5) logits, for the path that activates them on load)."""
-    H, W, B, ps, iters = cfg["H"], cfg["W"], cfg["B"], cfg["ps"], cfg["iters"]
+def grid_intrinsics(H: int, W: int):
+    """Grid (1/8) intrinsics of a frame with fx = fy = 0.8 W, cx = W/2,
+    cy = H/2 (the reference's pre-"+0.5" intrinsics scaled to the grid as
+    src/dsine_refine.cpp:232-237 does)."""
+    h, w = H // 8, W // 8
+    fx = fy = 0.8 * W
+    cx, cy = W / 2.0, H / 2.0
+    return fx * w / W, (cx + 0.5) * w / W, fy * h / H, (cy + 0.5) * h / H
+
+
+def make_device_inputs(cfg, B, seed, device, torch, logits=False):
+    """Seeded synthetic inputs of B frames on the GPU, generator
+    distributions of the benchmark configurations (oracle.gen_unit draws the
+    same laws on CPU). logits: prob / angle as raw head outputs instead
+    (N(0, 2.5) and N(-2.5, 1.5) logits, for the path that activates them on
+    load)."""
+    H, W, ps, iters = cfg["H"], cfg["W"], cfg["ps"], cfg["iters"]
     h, w = H // 8, W // 8
     P = ps * ps
     dt = torch.float16 if cfg["f16"] else torch.float32
     g = torch.Generator(device=device)
     g.manual_seed(seed)
-    fx = fy = 0.8 * W
-    cx, cy = W / 2.0, H / 2.0
-    fu, cu = fx * w / W, (cx + 0.5) * w / W
-    fv, cv = fy * h / H, (cy + 0.5) * h / H
+    fu, cu, fv, cv = grid_intrinsics(H, W)
     ys, xs = torch.meshgrid(torch.arange(h, device=device, dtype=torch.float64),
                             torch.arange(w, device=device, dtype=torch.float64), indexing="ij")
     rx = ((xs + 0.5) - cu) / fu
@@ -192,90 +212,111 @@ def make_device_inputs(cfg, seed, device, torch, logits=False):
                 cu=cu, fv=fv, cv=cv, h=h, w=w, dt=dt)
 
 
+def frames_slice(inp, b0, b1):
+    """The inputs of frames [b0, b1) (views: frames are the leading dim)."""
+    out = dict(inp)
+    for k in ("normal0", "mask"):
+        out[k] = inp[k][b0:b1]
+    for k in ("prob", "xy", "angle"):
+        out[k] = [t[b0:b1] for t in inp[k]]
+    return out
+
+
 # ----------------------------------------------------------------- CPU reference
 
-def cpu_reference_sample(cfg, threads=0, seconds_min=10.0):
-    """Time the reference CPU ops (oracle/_ref, threaded over frames) on a
-    bounded sample: one distinct generated frame repeated over `frames`
-    output frames. Returns (Mpx/s, threads, frames, seconds, kind)."""
-    from oracle import oracle as O
+class RefSampler:
+    """The reference's CPU ops on a bounded sample of the workload, over a
+    persistent pool of host threads: one step is one frame per thread, each
+    frame the reference twin's unit (oracle/_ref: ray_relu + I x
+    angmf_propagate of src/dsine_ops.cpp, then the restated upsample / L2 /
+    crop) on one generated frame of the configuration. Windows the reference
+    does not have (dilation 2, 7x7) run the C restatement instead ("port").
+    Both the bench's cpu_baseline leg and ``--impl reference`` time steps of
+    this one routine."""
 
-    if cfg["ps"] != 5 or cfg["dil"] != 1 or not O.ref_available():
-        kind = "port"
-    else:
-        kind = "reference"
-    u = O.gen_unit(cfg["H"], cfg["W"], 1, ps=cfg["ps"], dil=cfg["dil"], iters=cfg["iters"],
-                   seed=123)
-    if cfg["f16"]:
-        u = O.to_f16_storage(u)
-    nthreads = threads or os.cpu_count() or 1
-    per_frame_px = cfg["H"] * cfg["W"]
+    def __init__(self, cfg, threads: int):
+        from concurrent.futures import ThreadPoolExecutor
 
-    def run(frames):
+        from oracle import oracle as O
+
+        self.O = O
+        self.cfg = cfg
+        self.threads = max(1, threads)
+        self.kind = ("reference" if (O.ref_available() and cfg["ps"] == 5 and cfg["dil"] == 1)
+                     else "port")
+        u = O.gen_unit(cfg["H"], cfg["W"], 1, ps=cfg["ps"], dil=cfg["dil"], iters=cfg["iters"],
+                       seed=123)
+        self.u = O.to_f16_storage(u) if cfg["f16"] else u
+        self.outs = [np.empty((1, 3, cfg["H"], cfg["W"]), np.float32)
+                     for _ in range(self.threads)]
+        self.pool = ThreadPoolExecutor(self.threads)
+
+    def _frame(self, k: int):
+        # the oracle libraries are ctypes calls, which release the GIL
+        if self.kind == "reference":
+            self.O.ref_unit_mt(self.u, threads=1, full_res_ray_relu=self.cfg["rr"], frames=1,
+                               out=self.outs[k])
+        else:
+            self.outs[k][:] = self.O.refine_unit(self.u, full_res_ray_relu=self.cfg["rr"])
+
+    def step(self) -> float:
+        """One frame per thread; returns the wall seconds."""
         t0 = time.perf_counter()
-        if kind == "reference":
-            O.ref_unit_mt(u, threads=nthreads, full_res_ray_relu=cfg["rr"], frames=frames)
-        else:  # the restatement (non-reference windows), one frame per call
-            for _ in range(frames):
-                O.refine_unit(u, full_res_ray_relu=cfg["rr"])
+        list(self.pool.map(self._frame, range(self.threads)))
         return time.perf_counter() - t0
 
-    frames = nthreads if kind == "reference" else 1
-    dt = run(frames)  # also the warm-up
-    # grow to a sample of at least `seconds_min` of CPU work (wall x threads),
-    # whole rounds of one frame per thread, then time it warm
-    cores = nthreads if kind == "reference" else 1
-    cpu_s = dt * cores
-    if cpu_s < seconds_min:
-        frames = math.ceil(frames * seconds_min / max(cpu_s, 1e-3))
-        if kind == "reference":
-            frames = math.ceil(frames / nthreads) * nthreads
-    dt = run(frames)
-    return frames * per_frame_px / dt / 1e6, cores, frames, dt, kind
+    def frames_per_step(self) -> int:
+        return self.threads
+
+    def rate(self, steps: int, warmup: int = 1):
+        """Mpixel/s over `steps` timed steps after `warmup` untimed ones."""
+        for _ in range(warmup):
+            self.step()
+        secs = sum(self.step() for _ in range(steps))
+        px = steps * self.threads * self.cfg["H"] * self.cfg["W"]
+        return px / secs / 1e6, secs
+
+    def close(self):
+        self.pool.shutdown()
+
+    def sample_text(self, steps: int, secs: float) -> str:
+        c = self.cfg
+        what = ("reference dsine_ops.cpp CPU twin (fp32 storage, fp64 math) + restated upsample"
+                if self.kind == "reference" else
+                "fp64 C restatement of dsine_ops.cpp (window not in the reference) + restated "
+                "upsample")
+        return (f"{steps} steps x {self.threads} frames of {c['W']}x{c['H']} (one generated "
+                f"frame, {'fp16-rounded ' if c['f16'] else ''}inputs), {secs:.1f} s wall on "
+                f"{self.threads} persistent host thread(s); {what}")
 
 
 def reference_arm(args, cfg):
-    """--impl reference: the reference's own CPU path, all host threads."""
-    from oracle import oracle as O
-
+    """--impl reference: the reference's own CPU path, all host threads, the
+    same per-step sample as the bench's cpu_baseline leg."""
     nthreads = os.cpu_count() or 1
-    kind = "reference" if (O.ref_available() and cfg["ps"] == 5 and cfg["dil"] == 1) else "port"
-    u = O.gen_unit(cfg["H"], cfg["W"], 1, ps=cfg["ps"], dil=cfg["dil"], iters=cfg["iters"],
-                   seed=123)
-    if cfg["f16"]:
-        u = O.to_f16_storage(u)
-    frames = nthreads if kind == "reference" else 1
-    out = np.empty((frames, 3, cfg["H"], cfg["W"]), np.float32)
-
-    def step():
-        if kind == "reference":
-            O.ref_unit_mt(u, threads=nthreads, full_res_ray_relu=cfg["rr"], frames=frames, out=out)
-        else:
-            O.refine_unit(u, full_res_ray_relu=cfg["rr"])
-
+    rs = RefSampler(cfg, nthreads)
     for _ in range(args.warmup):
-        step()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
-    dt = (time.perf_counter() - t0) / args.steps
+        rs.step()
+    secs = sum(rs.step() for _ in range(args.steps))
+    rs.close()
+    dt = secs / args.steps
+    frames = rs.frames_per_step()
     value = frames * cfg["H"] * cfg["W"] / dt / 1e6
     line = {
         "impl": "reference", "metric": metric_name(), "value": round(value, 3),
         "unit": "Mpixel/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded generators)",
-        "config": workload_config(args, cfg, extra={"sample_frames": frames}),
+        "config": workload_config(args, cfg, 1, extra={"sample_frames_per_step": frames}),
         "cpu_baseline": {"value": round(value, 3), "unit": "Mpixel/s", "cores": nthreads,
-                         "kind": kind,
-                         "sample": f"{frames} frames of {cfg['W']}x{cfg['H']} per step "
-                                   f"(one generated frame repeated), reference dsine_ops.cpp "
-                                   f"CPU twin (fp32 storage, fp64 math) + restated upsample"},
+                         "kind": rs.kind, "sample": rs.sample_text(args.steps, secs)},
         "e2e": {"value": round(value, 3), "unit": "Mpixel/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
+
+# ----------------------------------------------------------------- stage bench
 
 def stage_flops_per_px(iters: int) -> float:
     """Model FLOPs per grid pixel of the ConvGRU + heads as the reference
@@ -305,7 +346,7 @@ def stage_executed_flops(iters: int, B: int, h: int, w: int) -> float:
 
 
 def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
-    """--stage: a step is the whole refinement of B frames -- `iters`
+    """--stage: a step is the whole refinement of B frames per GPU -- `iters`
     iterations of ConvGRU + heads (brovisionml_b200.refine_stage) and the
     fused ops on their raw outputs (refine(..., logits=True))."""
     import torch
@@ -319,8 +360,7 @@ def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
     g = torch.Generator(device=device).manual_seed(1000 + rank)
     h0 = torch.tanh(torch.randn((B, 64, h, w), device=device, generator=g))
     feat = torch.relu(torch.randn((B, 64, h, w), device=device, generator=g))
-    fx = 0.8 * W
-    fu, cu, fv, cv = fx * w / W, (W / 2 + 0.5) * w / W, fx * h / H, (H / 2 + 0.5) * h / H
+    fu, cu, fv, cv = grid_intrinsics(H, W)
     ys, xs = torch.meshgrid(torch.arange(h, device=device), torch.arange(w, device=device),
                             indexing="ij")
     uv = torch.stack([((xs + 0.5) - cu) / fu, ((ys + 0.5) - cv) / fv]).float()
@@ -352,13 +392,8 @@ def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
         st.check_pipeline()
         barrier()
         torch.cuda.synchronize()
-        uuid = None
-        try:
-            uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
-        except Exception:
-            pass
         marks = [[ev(), ev(), ev()] for _ in range(args.steps)]
-        with ClockSampler(device.index, uuid) as clk:
+        with ClockSampler(device.index, gpu_uuid(torch, device)) as clk:
             for k in range(args.steps):
                 marks[k][0].record(stream)
                 stage()
@@ -375,7 +410,6 @@ def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
     tflops = flops / (stage_ms * 1e-3) / 1e12
     flops_x = stage_executed_flops(I, B, h, w)
     tflops_x = flops_x / (stage_ms * 1e-3) / 1e12
-    peak = None
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             peak = float(json.load(f)["bf16_tflops_sustained"])
@@ -390,8 +424,9 @@ def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
         "vs_baseline": None, "dtype": "bf16 (tensor cores, fp32 accumulate) + f32 ops",
         "storage": "f16" if cfg["f16"] else "f32",
         "data": "synthetic (random weights of the reference's shapes, seeded inputs)",
-        "config": workload_config(args, cfg, {"stage": "ConvGRU 5x5 130->64 x3, 4 heads "
-                                              "(3x3 66->128, 1x1 128->128, 1x1 128->out)"}),
+        "config": workload_config(args, cfg, world, {"frames_per_gpu": B, "stage":
+                                  "ConvGRU 5x5 130->64 x3, 4 heads (3x3 66->128, 1x1 128->128, "
+                                  "1x1 128->out)"}),
         # per step: stage inputs 1, hoisted terms 3, 6 per iteration (zr, q,
         # heads 3x3, three head tails), the up-mask head 2 (last iteration),
         # AngMF I, upsample 1
@@ -409,29 +444,219 @@ def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
 
-        dist.destroy_process_group()
+
+def stage_layers(args, cfg, device):
+    """--stage-layers: run `steps` iterations of the refine stage on random
+    weights over B frames of the configuration's grid and print each
+    launch's time in the last iteration and of start (CUDA events, one GPU).
+    Also the target for profiling one layer: start runs twice (3 conv_tc
+    kernels each, the second one timed), then each iteration launches 5
+    conv_tc kernels (zr, q, heads 3x3, the up-mask head's two 1x1) --
+    numbers 6 + 5 k .. 10 + 5 k -- and 3 head_tail kernels (the prob, xy and
+    angle heads' last two layers)."""
+    import torch
+
+    from brovisionml_b200.refine_stage import (FEATURE, HEADS, HIDDEN, RefineStage,
+                                               random_params)
+
+    B, h, w = cfg["B"], cfg["H"] // 8, cfg["W"] // 8
+    st = RefineStage(random_params(device, seed=7), B, h, w, device=device)
+    g = torch.Generator(device=device).manual_seed(1)
+    h0 = torch.tanh(torch.randn((B, HIDDEN, h, w), device=device, generator=g))
+    feat = torch.relu(torch.randn((B, FEATURE, h, w), device=device, generator=g))
+    ys, xs = torch.meshgrid(torch.arange(h, device=device), torch.arange(w, device=device),
+                            indexing="ij")
+    uv = torch.stack([((xs + 0.5) - w / 2) / (0.8 * w), ((ys + 0.5) - h / 2) / (0.8 * w)])
+    st.start(h0, feat, uv.float())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    st.start(h0, feat, uv.float())
+    e1.record()
+    marks = []
+
+    def timed(fn):
+        def run(*a, **k):
+            m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            m0.record()
+            fn(*a, **k)
+            m1.record()
+            marks.append((m0, m1))
+        return run
+
+    st._conv, st._tail = timed(st._conv), timed(st._tail)
+    for _ in range(max(1, args.steps)):
+        marks.clear()
+        st.step()
+    torch.cuda.synchronize()
+    st.check_pipeline()
+    names = (["zr", "q", "heads3x3"] + [f"{n}.2+4" for n, c in HEADS if c <= 64] +
+             [f"{n}.{i}" for n, c in HEADS if c > 64 for i in (2, 4)])
+    print(f"frames {B} grid {w}x{h}: start {e0.elapsed_time(e1):.3f} ms; " +
+          " ".join(f"{n} {a.elapsed_time(b):.3f}" for n, (a, b) in zip(names, marks)))
 
 
 def metric_name():
     return "Mpixel/s of DSINE refine ops (5 iters + upsample)"
 
 
-def workload_config(args, cfg, extra=None):
-    c = {"workload": args.config, "frames_per_gpu": cfg["B"],
+def workload_config(args, cfg, world, extra=None):
+    from brovisionml_b200.sharding import plan_frames
+
+    split = [n for _, n in plan_frames(cfg["B"], world)]
+    c = {"workload": args.config, "frames_total": cfg["B"], "frames_per_gpu": split,
          "image": f"{cfg['W']}x{cfg['H']}", "grid": f"{cfg['W'] // 8}x{cfg['H'] // 8}",
          "window": f"{cfg['ps']}x{cfg['ps']}", "dilation": cfg["dil"], "iters": cfg["iters"],
          "storage": "f16" if cfg["f16"] else "f32", "full_res_ray_relu": cfg["rr"],
-         "parallelism": f"image-parallel x{args.gpus}",
-         "l2": "inputs ~9 GB/GPU >> 126 MB L2 (no flush needed)" if args.config == "cfg4"
-               else "inputs larger than L2" }
+         "parallelism": f"image-parallel x{world} (sharding.plan_frames; no collective on the "
+                        f"data path)",
+         "l2": "inputs >= 1.2 GB per GPU >> 126 MB L2 (no flush needed)" if args.config == "cfg4"
+               else "inputs larger than L2"}
     if getattr(args, "logits", False):
         c["head_outputs"] = "raw logits, sigmoid / pi*sigmoid applied on load"
     if extra:
         c.update(extra)
     return c
+
+
+def gpu_uuid(torch, device):
+    try:
+        return "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+    except Exception:
+        return None
+
+
+# ----------------------------------------------------------------- config 3 bands
+
+def bands_bench(args, device, rank, world, barrier, max_over_ranks, stream):
+    """Config 3 as the path shards it over N GPUs: one 4096^2 frame (grid
+    512^2, 7x7, dilation 1, 5 iterations, fp32), rank r refining the exact
+    halo row band sharding.plan_bands(512, N, halo_rows(5, 7, 1))[r] and
+    cropping its owned rows. Every rank generates the same frame (same seed)
+    and keeps its band's rows, resident before timing."""
+    import torch
+    import torch.distributed as dist
+
+    import brovisionml_b200 as bv
+    from brovisionml_b200.sharding import band_intrinsics, gather_bands, halo_rows, plan_bands
+
+    cfg = CONFIGS["cfg3"]
+    H, W, I, ps = cfg["H"], cfg["W"], cfg["iters"], cfg["ps"]
+    h, w = H // 8, W // 8
+    bands = plan_bands(h, world, halo_rows(I, ps, cfg["dil"]))
+    bd = bands[rank]
+    full = make_device_inputs(cfg, 1, 777, device, torch)
+    rows = lambda t: t[..., bd.comp0:bd.comp1, :].contiguous()  # noqa: E731
+    inp = {k: ([rows(t) for t in v] if isinstance(v, list) else
+               rows(v) if k in ("normal0", "mask", "ray8") else v) for k, v in full.items()}
+    del full
+    torch.cuda.empty_cache()
+    own_h = 8 * (bd.own1 - bd.own0)
+    out = torch.empty((1, 3, own_h, W), device=device, dtype=torch.float32)
+    ws = torch.empty(bv.refine_workspace_bytes(1, bd.rows, w), device=device, dtype=torch.uint8)
+    cvb = band_intrinsics(inp["cv"], bd)
+
+    def compute():
+        bv.refine(inp["normal0"], inp["prob"], inp["xy"], inp["angle"], inp["mask"], inp["fu"],
+                  inp["cu"], inp["fv"], cvb, ray8=inp["ray8"], ps=ps, dil=cfg["dil"],
+                  crop=(8 * bd.crop_top, 0, own_h, W), out=out, workspace=ws)
+
+    host = torch.empty((3, H, W), dtype=torch.float32).pin_memory() if rank == 0 else None
+
+    def gather_d2h():
+        compute()
+        frame = gather_bands(out[0], bands)  # NCCL gather of owned rows to rank 0
+        if rank == 0:
+            host.copy_(frame, non_blocking=True)
+
+    # the shared pinned host frame: one /dev/shm file mapped by every rank
+    shm = None
+    shm_path = f"/dev/shm/bvml_bench_cfg3_{os.environ.get('MASTER_PORT', 'solo')}"
+    shm_err = None
+    try:
+        if rank == 0:
+            with open(shm_path, "wb") as f:
+                f.truncate(3 * H * W * 4)
+        barrier()
+        shm = torch.from_file(shm_path, shared=True, size=3 * H * W,
+                              dtype=torch.float32).view(3, H, W)
+        rc = torch.cuda.cudart().cudaHostRegister(shm.data_ptr(), 3 * H * W * 4, 0)
+        if int(rc) != 0:
+            raise RuntimeError(f"cudaHostRegister: {rc}")
+    except Exception as e:  # reported, never required
+        shm_err = str(e)
+        shm = None
+    flag = torch.tensor([1 if shm is None else 0], device=device)
+    if world > 1:
+        dist.all_reduce(flag)
+    use_shm = int(flag.item()) == 0
+
+    def host_gather():
+        compute()
+        for c in range(3):  # one contiguous device-to-host copy per channel
+            shm[c, 8 * bd.own0:8 * bd.own1].copy_(out[0, c], non_blocking=True)
+
+    def timed(fn):
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                fn()
+            stream.synchronize()
+            barrier()
+            torch.cuda.synchronize()
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            for _ in range(args.steps):
+                fn()
+            t1.record(stream)
+            t1.synchronize()
+            torch.cuda.synchronize()
+            barrier()
+        return max_over_ranks(t0.elapsed_time(t1) / args.steps)
+
+    px = H * W
+    res = {"workload": "cfg3", "image": f"{W}x{H}", "window": "7x7", "iters": I,
+           "storage": "f32", "halo_rows": halo_rows(I, ps, cfg["dil"]),
+           "bands": [[b.own0, b.own1, b.comp0, b.comp1] for b in bands],
+           "scaling": "strong (one frame over N GPUs)"}
+    ms = timed(compute)
+    res["compute"] = {"value": round(px / (ms * 1e-3) / 1e6, 1), "unit": "Mpixel/s",
+                      "ms_per_step": round(ms, 4)}
+    ms = timed(gather_d2h)
+    res["gather_nccl_d2h"] = {
+        "value": round(px / (ms * 1e-3) / 1e6, 1), "unit": "Mpixel/s", "ms_per_step": round(ms, 4),
+        "what": "compute + NCCL gather of the owned rows to rank 0 + device-to-host copy of "
+                "the frame on rank 0", "d2h_bytes_per_step": 3 * H * W * 4}
+    if use_shm:
+        ms = timed(host_gather)
+        res["host_gather"] = {
+            "value": round(px / (ms * 1e-3) / 1e6, 1), "unit": "Mpixel/s",
+            "ms_per_step": round(ms, 4),
+            "what": "compute + every rank copying its owned rows into one shared pinned host "
+                    "frame (/dev/shm mapped by all ranks)",
+            "d2h_bytes_per_step": 3 * H * W * 4}
+        if rank == 0:
+            ref = torch.empty((3, H, W), dtype=torch.float32)
+            gather_d2h()
+            torch.cuda.synchronize()
+            ref.copy_(host)
+            host_gather()
+            torch.cuda.synchronize()
+            barrier()
+            res["host_gather"]["equal_to_nccl_gather"] = bool(torch.equal(ref, shm))
+        else:
+            gather_d2h()
+            torch.cuda.synchronize()
+            host_gather()
+            torch.cuda.synchronize()
+            barrier()
+    else:
+        res["host_gather"] = {"unavailable": shm_err or "shared host frame unavailable"}
+    if shm is not None:
+        torch.cuda.cudart().cudaHostUnregister(shm.data_ptr())
+    barrier()
+    if rank == 0 and os.path.exists(shm_path):
+        os.unlink(shm_path)
+    return res
 
 
 # ----------------------------------------------------------------- our arm
@@ -443,23 +668,34 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="cfg4", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--frames", type=int, default=0, help="override frames per GPU")
+    ap.add_argument("--frames", type=int, default=0,
+                    help="override the frames in total (split over the ranks)")
+    ap.add_argument("--no-weak", action="store_true",
+                    help="skip the weak-scaling key (all frames on every rank)")
+    ap.add_argument("--no-bands", action="store_true", help="skip the config-3 band key")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--stage", action="store_true",
                     help="time the whole learned refinement: ConvGRU + heads on the tensor "
                          "cores (random weights of the reference's shapes), then the ops on "
-                         "their raw outputs (device timing only)")
+                         "their raw outputs (device timing only; frames per GPU)")
+    ap.add_argument("--stage-layers", action="store_true",
+                    help="time each launch of one refine-stage iteration and of start "
+                         "(CUDA events; --frames frames of 720p, default 16)")
     ap.add_argument("--logits", action="store_true",
                     help="raw head outputs for prob / angle, activated on load (device "
                          "timing only)")
     args = ap.parse_args()
-    if args.logits or args.stage:
-        args.no_e2e = args.no_cpu = True
+    if args.logits or args.stage or args.stage_layers:
+        args.no_e2e = args.no_cpu = args.no_bands = args.no_weak = True
     args.steps = max(1, args.steps)
     cfg = dict(CONFIGS[args.config])
     if args.frames:
         cfg["B"] = args.frames
+    if args.stage and not args.frames:
+        cfg["B"] = 64
+    if args.stage_layers and not args.frames:
+        cfg["B"] = 16
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -475,6 +711,7 @@ def main():
 
     import brovisionml_b200 as bv
     from brovisionml_b200.pipeline import HostBatch, HostRefiner
+    from brovisionml_b200.sharding import plan_frames
 
     if not torch.cuda.is_available():
         raise SystemExit("bench.py needs a CUDA GPU")
@@ -483,7 +720,7 @@ def main():
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
 
     def barrier():
         if world > 1:
@@ -496,90 +733,123 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    if args.stage:
-        return stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks)
-    inp = make_device_inputs(cfg, 1000 + rank, device, torch, logits=args.logits)
-    h, w, B, P, I = inp["h"], inp["w"], cfg["B"], cfg["ps"] ** 2, cfg["iters"]
+    try:
+        if args.stage_layers:
+            return stage_layers(args, cfg, device)
+        if args.stage:
+            return stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks)
+        return unit_bench(args, cfg, device, rank, world, barrier, max_over_ranks, torch, bv,
+                          HostBatch, HostRefiner, plan_frames)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+def unit_bench(args, cfg, device, rank, world, barrier, max_over_ranks, torch, bv, HostBatch,
+               HostRefiner, plan_frames):
+    split = plan_frames(cfg["B"], world)
+    b_off, B = split[rank]
+    weak = world > 1 and not args.no_weak
+    B_alloc = max(B, cfg["B"] if weak else 0, 1)
+    inp_all = make_device_inputs(cfg, B_alloc, 1000 + rank, device, torch, logits=args.logits)
+    h, w, P, I = inp_all["h"], inp_all["w"], cfg["ps"] ** 2, cfg["iters"]
     s = 2 if cfg["f16"] else 4
-    out = torch.empty((B, 3, 8 * h, 8 * w), device=device, dtype=inp["dt"])
-    ws = torch.empty(bv.refine_workspace_bytes(B, h, w), device=device, dtype=torch.uint8)
     stream = torch.cuda.Stream(device)
-
-    def step():
-        bv.refine(inp["normal0"], inp["prob"], inp["xy"], inp["angle"], inp["mask"], inp["fu"],
-                  inp["cu"], inp["fv"], inp["cv"], ray8=inp["ray8"], ps=cfg["ps"],
-                  dil=cfg["dil"], full_res_ray_relu=cfg["rr"], out=out, workspace=ws,
-                  logits=args.logits)
-
     n_launch = I + 1
+
+    def unit(nf):
+        """A step over nf frames: the fused unit, its output and workspace."""
+        inp = frames_slice(inp_all, 0, nf)
+        out = torch.empty((nf, 3, 8 * h, 8 * w), device=device, dtype=inp["dt"])
+        ws = torch.empty(bv.refine_workspace_bytes(max(nf, 1), h, w), device=device,
+                         dtype=torch.uint8)
+
+        def step():
+            if nf == 0:
+                return
+            bv.refine(inp["normal0"], inp["prob"], inp["xy"], inp["angle"], inp["mask"],
+                      inp["fu"], inp["cu"], inp["fv"], inp["cv"], ray8=inp["ray8"],
+                      ps=cfg["ps"], dil=cfg["dil"], full_res_ray_relu=cfg["rr"], out=out,
+                      workspace=ws, logits=args.logits)
+        return step, out
+
+    def time_steps(step, clocks=False):
+        """Device ms per step on this rank (W warm-up steps, then K timed
+        steps bracketed by a barrier and a synchronize on both sides)."""
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                step()
+            stream.synchronize()
+            start = torch.cuda.Event(enable_timing=True)
+            stop = torch.cuda.Event(enable_timing=True)
+            barrier()
+            torch.cuda.synchronize()
+            clk = ClockSampler(local_index(device), gpu_uuid(torch, device)) if clocks else None
+            if clk:
+                clk.__enter__()
+            start.record(stream)
+            for _ in range(args.steps):
+                step()
+            stop.record(stream)
+            stream.synchronize()
+            if clk:
+                clk.__exit__(None, None, None)
+            torch.cuda.synchronize()
+            barrier()
+        return start.elapsed_time(stop) / args.steps, clk
+
+    step, out = unit(B)
+    ms_local, clk = time_steps(step, clocks=True)
+    ms = max_over_ranks(ms_local)
+    clocks = clk.summary()
+    out_px = cfg["B"] * cfg["H"] * cfg["W"]
+    value = out_px / (ms / 1e3) / 1e6
+
+    # per-kernel launch times: the same steps again with probe events
     import ctypes
 
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_launch + 1)]
+           for _ in range(args.steps)]
     with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup)):
-            step()
-        stream.synchronize()
-        # per-launch probe events for every timed step
-        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_launch + 1)]
-               for _ in range(args.steps)]
         for e in evs:  # torch creates the CUDA event at its first record
             for ev in e:
                 ev.record(stream)
         stream.synchronize()
         arrs = [(ctypes.c_void_p * len(e))(*[ev.cuda_event for ev in e]) for e in evs]
-        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        torch.cuda.synchronize()
-        uuid = None
-        try:
-            uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
-        except Exception:
-            pass
-        # the timed steps run without probes (no extra stream operations)
-        with ClockSampler(local, uuid) as clk:
-            start.record(stream)
+        if B:
             for k in range(args.steps):
+                bv.check(bv.lib.bvml_probe_events(arrs[k], len(evs[k])))
                 step()
-            stop.record(stream)
-            stream.synchronize()
-        barrier()
-        torch.cuda.synchronize()
-        # the same steps again with probes, for the per-kernel breakdown
-        for k in range(args.steps):
-            bv.check(bv.lib.bvml_probe_events(arrs[k], len(evs[k])))
-            step()
-        bv.lib.bvml_probe_events(None, 0)
+            bv.lib.bvml_probe_events(None, 0)
         stream.synchronize()
-        barrier()
-    clocks = clk.summary()
-    ms_local = start.elapsed_time(stop) / args.steps
-    ms = max_over_ranks(ms_local)
-    out_px = world * B * cfg["H"] * cfg["W"]
-    value = out_px / (ms / 1e3) / 1e6
-
-    # per-kernel launch times from the probes
-    per = np.array([[evs[k][j].elapsed_time(evs[k][j + 1]) for j in range(n_launch)]
-                    for k in range(args.steps)])  # ms
-    angmf_ms = per[:, :I].mean() if I else 0.0
-    up_ms = per[:, I].mean()
-    hw = h * w
-    angmf_bytes = [B * hw * (4 * P * s + (3 * s if i == 0 else 12) + 12) + 12 * hw
-                   for i in range(I)]
-    up_bytes = B * hw * (576 * s + 12) + B * 3 * 64 * hw * s
+    barrier()
     peak, peak_kind = hbm_peak()
-    kernels = {
-        "angmf": {"launches_per_step": I, "avg_ms": round(float(angmf_ms), 5),
-                  "bytes_per_launch": int(np.mean(angmf_bytes)) if I else 0,
-                  "share": round(float(per[:, :I].sum() / per.sum()), 4)},
-        "upsample": {"launches_per_step": 1, "avg_ms": round(float(up_ms), 5),
-                     "bytes_per_launch": int(up_bytes),
-                     "share": round(float(per[:, I].sum() / per.sum()), 4)},
-    }
-    for k in kernels.values():
-        k["gbs"] = round(k["bytes_per_launch"] / (k["avg_ms"] * 1e-3) / 1e9, 1) if k["avg_ms"] else 0
-    dom = max(kernels, key=lambda k: kernels[k]["share"])
+    hw = h * w
+    kernels = {}
+    dom = "angmf"
+    if B:
+        per = np.array([[evs[k][j].elapsed_time(evs[k][j + 1]) for j in range(n_launch)]
+                        for k in range(args.steps)])  # ms
+        angmf_ms = per[:, :I].mean() if I else 0.0
+        up_ms = per[:, I].mean()
+        angmf_bytes = [B * hw * (4 * P * s + (3 * s if i == 0 else 12) + 12) + 12 * hw
+                       for i in range(I)]
+        up_bytes = B * hw * (576 * s + 12) + B * 3 * 64 * hw * s
+        kernels = {
+            "angmf": {"launches_per_step": I, "avg_ms": round(float(angmf_ms), 5),
+                      "bytes_per_launch": int(np.mean(angmf_bytes)) if I else 0,
+                      "share": round(float(per[:, :I].sum() / per.sum()), 4)},
+            "upsample": {"launches_per_step": 1, "avg_ms": round(float(up_ms), 5),
+                         "bytes_per_launch": int(up_bytes),
+                         "share": round(float(per[:, I].sum() / per.sum()), 4)},
+        }
+        for k in kernels.values():
+            k["gbs"] = (round(k["bytes_per_launch"] / (k["avg_ms"] * 1e-3) / 1e9, 1)
+                        if k["avg_ms"] else 0)
+        dom = max(kernels, key=lambda k: kernels[k]["share"])
     traffic = None
     tp = os.path.join(ROOT, "profiles", "dram_traffic.json")
-    if os.path.exists(tp):
+    if os.path.exists(tp) and B:
         try:
             with open(tp) as f:
                 t = json.load(f)
@@ -588,49 +858,71 @@ def main():
                 traffic = int(t[key]["dram_bytes_per_grid_px"] * B * hw)
         except Exception:
             traffic = None
-    achieved = kernels[dom]["gbs"]
+    achieved = kernels[dom]["gbs"] if kernels else 0.0
     unit_bytes = s * (6 + I * 4 * P + 576 + 192) * B * hw
-    unit_gbs = world * unit_bytes / (ms * 1e-3) / 1e9
+    unit_gbs_rank = unit_bytes / (ms * 1e-3) / 1e9
 
     line = {
         "metric": metric_name(), "value": round(value, 1), "unit": "Mpixel/s",
         "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
-        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "storage": "f16" if cfg["f16"] else "f32",
         "data": "synthetic (seeded generators, BASELINE config distributions)",
-        "config": workload_config(args, cfg),
+        "config": workload_config(args, cfg, world),
         "gpu_launches": args.steps * n_launch,
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                      if peak_kind == "measured" else "fallback 6.65 TB/s",
-                     "traffic": traffic},
-        "unit_roofline": {"bytes_per_step_per_gpu": int(unit_bytes),
-                          "achieved": round(unit_gbs / world, 1), "frac": round(unit_gbs / world / peak, 4)},
+                     "traffic": traffic, "rank": rank, "frames": B},
+        "unit_roofline": {"bytes_per_step_per_gpu": int(unit_bytes), "rank": rank,
+                          "achieved": round(unit_gbs_rank, 1),
+                          "frac": round(unit_gbs_rank / peak, 4)},
         "kernels": kernels,
         "clocks": clocks,
     }
 
+    # ------------------------------------------------------------- weak scaling
+    if weak:
+        wstep, _ = unit(cfg["B"])
+        wms = max_over_ranks(time_steps(wstep)[0])
+        line["weak"] = {"frames_per_gpu": cfg["B"], "frames_total": world * cfg["B"],
+                        "value": round(world * out_px / (wms * 1e-3) / 1e6, 1),
+                        "unit": "Mpixel/s", "ms_per_step": round(wms, 4)}
+        del wstep
+    del step, out
+    torch.cuda.empty_cache()
+
+    # ------------------------------------------------------------- config 3 bands
+    if not args.no_bands and args.config == "cfg4":
+        line["bands"] = bands_bench(args, device, rank, world, barrier, max_over_ranks, stream)
+        torch.cuda.empty_cache()
+
     # ------------------------------------------------------------- e2e
     if not args.no_e2e:
-        hb = HostBatch(normal0=inp["normal0"].cpu().pin_memory(),
-                       prob=[t.cpu().pin_memory() for t in inp["prob"]],
-                       xy=[t.cpu().pin_memory() for t in inp["xy"]],
-                       angle=[t.cpu().pin_memory() for t in inp["angle"]],
-                       mask=inp["mask"].cpu().pin_memory(), ray8=inp["ray8"].cpu().pin_memory())
-        out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-        del inp
+        src = frames_slice(inp_all, 0, B)
+        pin = lambda t: t.cpu().pin_memory()  # noqa: E731
+        hb = HostBatch(normal0=pin(src["normal0"]), prob=[pin(t) for t in src["prob"]],
+                       xy=[pin(t) for t in src["xy"]], angle=[pin(t) for t in src["angle"]],
+                       mask=pin(src["mask"]), ray8=pin(src["ray8"]))
+        out_host = torch.empty((B, 3, 8 * h, 8 * w), dtype=src["dt"]).pin_memory()
+        del src, inp_all
         torch.cuda.empty_cache()
-        hr = HostRefiner(device, B, h, w, I, out.dtype, ps=cfg["ps"], chunk=32)
+        hr = HostRefiner(device, max(B, 1), h, w, I, out_host.dtype, ps=cfg["ps"], chunk=32)
         e2e_steps = max(1, min(args.steps, 5))
-        fu, cu, fv, cv = make_intrinsics(cfg)
+        fu, cu, fv, cv = grid_intrinsics(cfg["H"], cfg["W"])
+
+        def run():
+            if B:
+                hr.run(hb, out_host, fu, cu, fv, cv, dil=cfg["dil"],
+                       full_res_ray_relu=cfg["rr"])
         for _ in range(2):
-            hr.run(hb, out_host, fu, cu, fv, cv, dil=cfg["dil"], full_res_ray_relu=cfg["rr"])
+            run()
         barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         for _ in range(e2e_steps):
-            hr.run(hb, out_host, fu, cu, fv, cv, dil=cfg["dil"], full_res_ray_relu=cfg["rr"])
+            run()
         torch.cuda.synchronize()
         e2e_local = (time.perf_counter() - t0) / e2e_steps
         barrier()
@@ -639,34 +931,58 @@ def main():
                        "h2d_bytes_per_step": int(hr.h2d_bytes(hb)),
                        "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size()),
                        "ms_per_step": round(e2e_s * 1e3, 2), "steps": e2e_steps,
+                       "bytes": f"per rank (rank {rank}, {B} frames)",
                        "api": "brovisionml_b200.pipeline.HostRefiner (pinned host buffers)"}
 
     # ------------------------------------------------------------- CPU baseline
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
-            v, cores, frames, secs, kind = cpu_reference_sample(cfg)
-            line["cpu_baseline"] = {
-                "value": round(v, 3), "unit": "Mpixel/s", "cores": cores, "kind": kind,
-                "sample": f"{frames} frames of {cfg['W']}x{cfg['H']} (one generated frame "
-                          f"repeated), {secs:.1f} s wall x {cores} threads; reference "
-                          f"dsine_ops.cpp CPU twin (fp32 storage, fp64 math) + restated "
-                          f"upsample"}
+            line["cpu_baseline"], line["accuracy"] = cpu_baseline_leg(cfg, device, torch, bv)
         except Exception as e:  # the baseline is reported, never required
             line["cpu_baseline"] = {"value": None, "unit": "Mpixel/s", "cores": 0,
                                     "kind": "reference", "sample": f"failed: {e}"}
 
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
 
 
-def make_intrinsics(cfg):
-    H, W = cfg["H"], cfg["W"]
-    h, w = H // 8, W // 8
-    fx = fy = 0.8 * W
-    cx, cy = W / 2.0, H / 2.0
-    return fx * w / W, (cx + 0.5) * w / W, fy * h / H, (cy + 0.5) * h / H
+def local_index(device):
+    return device.index if device.index is not None else 0
+
+
+def cpu_baseline_leg(cfg, device, torch, bv):
+    """The reference CPU ops on all host cores and on one thread (the same
+    sampling routine as --impl reference), and the angular error of the GPU
+    path against the reference twin on the sampled frame."""
+    from oracle import oracle as O
+
+    nthreads = os.cpu_count() or 1
+    rs = RefSampler(cfg, nthreads)
+    v_all, secs_all = rs.rate(steps=3, warmup=1)
+    rs.close()
+    rs1 = RefSampler(cfg, 1)
+    v_one, secs_one = rs1.rate(steps=2, warmup=1)
+    want = rs1.outs[0]
+    u = rs1.u
+    rs1.close()
+    base = {"value": round(v_all, 3), "unit": "Mpixel/s", "cores": nthreads, "kind": rs.kind,
+            "sample": rs.sample_text(3, secs_all),
+            "single_thread": {"value": round(v_one, 3), "unit": "Mpixel/s", "cores": 1,
+                              "sample": rs1.sample_text(2, secs_one)}}
+    dt = torch.float16 if cfg["f16"] else torch.float32
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device, dt)  # noqa: E731
+    got = bv.refine(t(u.normal0), [t(a) for a in u.prob], [t(a) for a in u.xy],
+                    [t(a) for a in u.angle], t(u.mask), u.fu, u.cu, u.fv, u.cv,
+                    ray8=torch.from_numpy(u.ray8).to(device), ps=cfg["ps"], dil=cfg["dil"],
+                    full_res_ray_relu=cfg["rr"])
+    torch.cuda.synchronize()
+    m = O.compare(got.float().cpu().numpy(), want)
+    acc = {"against": f"{rs1.kind} CPU path on the sampled frame (same inputs)",
+           "max_abs": m["max_abs"], "mean_abs": m["mean_abs"],
+           "ang_mean_deg": m["ang_mean_deg"], "ang_p99_deg": m["ang_p99_deg"],
+           "ang_max_deg": m["ang_max_deg"],
+           "tolerance_max_abs": O.TOL_F16 if cfg["f16"] else O.TOL_F32}
+    return base, acc
 
 
 if __name__ == "__main__":

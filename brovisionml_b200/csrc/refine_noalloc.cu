@@ -12,11 +12,15 @@
 // library's device code on a GPU, and that stays there until the process
 // exits.
 //
-// Set-up: the array's device address is looked up (cudaGetSymbolAddress) the
-// first time the entry point runs on each device, with that device current.
-// That first call should therefore come before any stream capture. The
-// host-side name of the array is NOT a device address and is never passed to
-// a kernel; only the looked-up pointer is.
+// Set-up: every call looks the array's device address up
+// (cudaGetSymbolAddress) with the caller's device current, and passes that
+// pointer, never the array's host-side name, to the kernels. Nothing is
+// cached between calls, so a device reset or another context made current
+// through the driver API cannot leave a stale address behind. Under CUDA's
+// default lazy module loading, the first call on a device is also the one
+// that loads this library's device code there and so reserves the array;
+// callers with a fixed memory budget should make one call at start-up, and
+// before any stream capture.
 //
 // Limits and sharing: the array holds BVML_REFINE_NOALLOC_MAX_BYTES bytes;
 // requests needing more scratch (bvml_refine_workspace_bytes(B, h, w)) are
@@ -31,18 +35,12 @@
 
 #include <cuda_runtime.h>
 
-#include <cstdint>
-#include <mutex>
 #include <string>
 
 namespace {
 
 // The scratch itself: BVML_REFINE_NOALLOC_MAX_BYTES bytes per device.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[BVML_REFINE_NOALLOC_MAX_BYTES];
-
-constexpr int kMaxDevices = 64;
-std::mutex g_setup_mutex;
-void* g_scratch_ptr[kMaxDevices] = {};
 
 }  // namespace
 
@@ -52,9 +50,9 @@ extern "C" int bvml_refine_noalloc(const void* normal0, const float* ray8,
                                    int h, int w, int ps, int dil, double fu, double cu, double fv,
                                    double cv, int full_res_ray_relu, int crop_t, int crop_l,
                                    int out_h, int out_w, int dtype, void* out, void* stream) {
-    const size_t need = bvml_refine_workspace_bytes(B, h, w);
     if (B < 0 || h < 0 || w < 0)
         return bvml::report_error(BVML_EINVAL, "dsine ops: refine_noalloc: bad shape");
+    const size_t need = bvml_refine_workspace_bytes(B, h, w);
     if (need > (size_t)BVML_REFINE_NOALLOC_MAX_BYTES)
         return bvml::report_error(
             BVML_EINVAL, "dsine ops: refine_noalloc: " + std::to_string(B) + " frames of " +
@@ -62,30 +60,15 @@ extern "C" int bvml_refine_noalloc(const void* normal0, const float* ray8,
                              std::to_string(need) + " bytes of scratch, more than the " +
                              std::to_string((size_t)BVML_REFINE_NOALLOC_MAX_BYTES) +
                              "-byte built-in buffer (use bvml_refine with a workspace)");
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess)
-        return bvml::report_error(BVML_ECUDA, std::string("dsine cuda: refine_noalloc: "
-                                                          "cudaGetDevice: ") +
-                                                  cudaGetErrorString(e));
-    if (dev < 0 || dev >= kMaxDevices)
-        return bvml::report_error(BVML_EUNSUPPORTED,
-                                  "dsine ops: refine_noalloc: device ordinal above 63");
+    // the device address of the array in the current device's context; the
+    // runtime resolves this without allocating once the module is loaded
     void* scratch = nullptr;
-    {
-        std::lock_guard<std::mutex> lock(g_setup_mutex);
-        if (!g_scratch_ptr[dev]) {
-            void* p = nullptr;
-            e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-            if (e != cudaSuccess || !p)
-                return bvml::report_error(
-                    BVML_ECUDA, std::string("dsine cuda: refine_noalloc: scratch set-up "
-                                            "(cudaGetSymbolAddress): ") +
-                                    cudaGetErrorString(e != cudaSuccess ? e : cudaErrorUnknown));
-            g_scratch_ptr[dev] = p;
-        }
-        scratch = g_scratch_ptr[dev];
-    }
+    cudaError_t e = cudaGetSymbolAddress(&scratch, g_noalloc_scratch);
+    if (e != cudaSuccess || !scratch)
+        return bvml::report_error(
+            BVML_ECUDA, std::string("dsine cuda: refine_noalloc: scratch set-up "
+                                    "(cudaGetSymbolAddress): ") +
+                            cudaGetErrorString(e != cudaSuccess ? e : cudaErrorUnknown));
     return bvml_refine(normal0, ray8, prob, xy, angle, iters, mask, B, h, w, ps, dil, fu, cu, fv,
                        cv, full_res_ray_relu, crop_t, crop_l, out_h, out_w, dtype, scratch,
                        (size_t)BVML_REFINE_NOALLOC_MAX_BYTES, out, stream);

@@ -226,6 +226,7 @@ class RefineStage:
         and uv (2,h,w) (src/dsine_refine.cpp:245-248), and convolve the fixed
         inputs once (three convolutions)."""
         _cuda("refine stage", h0, feat, uv)
+        self.err.zero_()  # each refinement reports its own pipeline status
         uvn = uv.permute(1, 2, 0)[None].to(torch.bfloat16)
         h0 = h0.float().contiguous()
         feat = feat.float().contiguous()
@@ -283,10 +284,13 @@ class RefineStage:
         return out
 
     def check_pipeline(self) -> None:
-        """Raise if any launch's pipeline gave up (one device sync)."""
-        if int(self.err.item()) != 0:
-            raise RuntimeError(f"dsine cuda: refine stage: pipeline gave up "
-                               f"(code {int(self.err.item())})")
+        """Raise if any launch since the last start() or check gave up (one
+        device sync). The error word is cleared after it is read, so each
+        check reports only the launches since the previous one."""
+        code = int(self.err.item())
+        if code != 0:
+            self.err.zero_()
+            raise RuntimeError(f"dsine cuda: refine stage: pipeline gave up (code {code})")
 
 
 def reference_stage(params, h0, feat, uv, iters: int, *, emulate_bf16: bool = True):
@@ -319,61 +323,3 @@ def reference_stage(params, h0, feat, uv, iters: int, *, emulate_bf16: bool = Tr
             res.append(F.conv2d(t, W[f"{name}.4.weight"], W[f"{name}.4.bias"]))
         outs.append(StageOutputs(*res))
     return outs
-
-
-def _main(argv=None) -> None:
-    """`python -m brovisionml_b200.refine_stage [--frames B] [--steps K]`:
-    run `steps` iterations of the stage on random weights over B frames of
-    the 160 x 90 grid (720p) and print each launch's time of the last
-    iteration and of start (CUDA events). Also the target for profiling one
-    layer: start runs twice (3 conv_tc kernels each, the second one timed),
-    then each iteration launches 5 conv_tc kernels (zr, q, heads 3x3, the
-    up-mask head's two 1x1) -- numbers 6 + 5 k .. 10 + 5 k -- and 3
-    head_tail kernels (prob, xy, angle heads' last two layers)."""
-    import argparse
-
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--frames", type=int, default=16)
-    ap.add_argument("--steps", type=int, default=3)
-    ap.add_argument("--height", type=int, default=90)
-    ap.add_argument("--width", type=int, default=160)
-    args = ap.parse_args(argv)
-    B, h, w = args.frames, args.height, args.width
-    dev = torch.device("cuda", 0)
-    st = RefineStage(random_params(dev, seed=7), B, h, w, device=dev)
-    g = torch.Generator(device=dev).manual_seed(1)
-    h0 = torch.tanh(torch.randn((B, HIDDEN, h, w), device=dev, generator=g))
-    feat = torch.relu(torch.randn((B, FEATURE, h, w), device=dev, generator=g))
-    ys, xs = torch.meshgrid(torch.arange(h, device=dev), torch.arange(w, device=dev),
-                            indexing="ij")
-    uv = torch.stack([((xs + 0.5) - w / 2) / (0.8 * w), ((ys + 0.5) - h / 2) / (0.8 * w)])
-    st.start(h0, feat, uv.float())
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    st.start(h0, feat, uv.float())
-    e1.record()
-    marks = []
-
-    def timed(fn):
-        def run(*a, **k):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            fn(*a, **k)
-            e1.record()
-            marks.append((e0, e1))
-        return run
-
-    st._conv, st._tail = timed(st._conv), timed(st._tail)
-    for _ in range(args.steps):
-        marks.clear()
-        st.step()
-    torch.cuda.synchronize()
-    st.check_pipeline()
-    names = (["zr", "q", "heads3x3"] + [f"{n}.2+4" for n, c in HEADS if c <= 64] +
-             [f"{n}.{i}" for n, c in HEADS if c > 64 for i in (2, 4)])
-    print(f"start {e0.elapsed_time(e1):.3f} " +
-          " ".join(f"{n} {a.elapsed_time(b):.3f}" for n, (a, b) in zip(names, marks)))
-
-
-if __name__ == "__main__":
-    _main()

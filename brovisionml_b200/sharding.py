@@ -130,10 +130,15 @@ def gather_frames(local, counts: Sequence[int], group=None):
     """Gather each rank's (count_r, ...) output to rank 0 (torch.distributed).
 
     Returns the concatenated tensor on rank 0 and None elsewhere. Every rank
-    must call it (a collective)."""
+    must call it (a collective). Without an initialised process group (one
+    process) the local part is the whole result."""
     import torch
     import torch.distributed as dist
 
+    if not (dist.is_available() and dist.is_initialized()):
+        if len(counts) != 1:
+            raise RuntimeError("gather_frames: several ranks' counts but no process group")
+        return local[: counts[0]]
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     mx = max(counts)

@@ -174,8 +174,13 @@ int bvml_refine_logits(const void* normal0, const float* ray8, const void* const
  * exits. For hosts that own the GPU memory budget and forbid allocations after
  * start-up (a plugin in another application's inference or render loop), or
  * loops that cannot take cudaMalloc's implicit device synchronisation.
- *  - The first call on each device looks the array's address up with that
- *    device current; make that first call before any stream capture.
+ *  - Every call looks the array's device address up (cudaGetSymbolAddress)
+ *    in the current device's context; no address is cached, so a device
+ *    reset between calls is harmless. Under CUDA's default lazy module
+ *    loading the first call on a device loads this library's device code
+ *    there, which is when the 32 MiB are reserved: a caller with a fixed
+ *    memory budget should make one call at start-up, before any stream
+ *    capture.
  *  - Work needing more than BVML_REFINE_NOALLOC_MAX_BYTES of scratch
  *    (bvml_refine_workspace_bytes(B, h, w); about 1.39 M grid pixels, e.g. 96
  *    frames of 90x160) is rejected with BVML_EINVAL.

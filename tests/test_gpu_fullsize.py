@@ -7,13 +7,22 @@ oracle would take too long: size-independent properties instead.
 * row bands (config 3's multi-GPU split) stitched together equal the whole
   frame (exact halo, see brovisionml_b200.sharding);
 * full-res RayReLU leaves every output facing the camera.
+
+Config 3 (one 4096^2 frame, 7x7, 5 iterations, fp32) is also compared with
+the CPU oracle at its full size: the oracle runs as exact halo row bands
+(proven equal to its whole-frame result in tests/test_sharding.py) over the
+host's cores, so the whole frame is checked within the fp32 tolerance.
 """
+import os
+from concurrent.futures import ThreadPoolExecutor
+
 import numpy as np
 import pytest
 import torch
 
 import bench
-from brovisionml_b200.sharding import band_intrinsics, halo_rows, plan_bands
+from brovisionml_b200.sharding import Band, band_intrinsics, halo_rows, plan_bands
+from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 
@@ -37,7 +46,7 @@ def check_unit(out, tol):
 def test_fullsize_unit_norm_and_batch_split(name):
     cfg = dict(bench.CONFIGS[name])
     dev = torch.device("cuda", 0)
-    inp = bench.make_device_inputs(cfg, 5, dev, torch)
+    inp = bench.make_device_inputs(cfg, cfg["B"], 5, dev, torch)
     out = run(inp, cfg)
     torch.cuda.synchronize()
     check_unit(out, 2e-3 if cfg["f16"] else 1e-5)
@@ -61,7 +70,7 @@ def test_fullsize_cfg3_bands_match_whole_frame():
     and as 8 exact halo bands (what 8 GPUs would each compute)."""
     cfg = dict(bench.CONFIGS["cfg3"])
     dev = torch.device("cuda", 0)
-    inp = bench.make_device_inputs(cfg, 9, dev, torch)
+    inp = bench.make_device_inputs(cfg, 1, 9, dev, torch)
     whole = run(inp, cfg)
     check_unit(whole, 1e-5)
     h = inp["h"]
@@ -87,7 +96,7 @@ def test_fullsize_cfg3_bands_match_whole_frame():
 def test_fullsize_cfg1_full_res_ray_relu_faces_camera():
     cfg = dict(bench.CONFIGS["cfg1"])
     dev = torch.device("cuda", 0)
-    inp = bench.make_device_inputs(cfg, 3, dev, torch)
+    inp = bench.make_device_inputs(cfg, 1, 3, dev, torch)
     out = run(inp, cfg)[0].double()
     H, W = cfg["H"], cfg["W"]
     fu, cu, fv, cv = 8 * inp["fu"], 8 * inp["cu"], 8 * inp["fv"], 8 * inp["cv"]
@@ -111,7 +120,7 @@ def test_large_frame_driver_matches_whole_frame(name, n_bands, given_ray):
     cfg = dict(bench.CONFIGS[name])
     cfg["B"] = 1
     dev = torch.device("cuda", 0)
-    inp = bench.make_device_inputs(cfg, 17, dev, torch)
+    inp = bench.make_device_inputs(cfg, 1, 17, dev, torch)
     ray = inp["ray8"] if given_ray else None
     want = bv.refine(inp["normal0"], inp["prob"], inp["xy"], inp["angle"], inp["mask"],
                      inp["fu"], inp["cu"], inp["fv"], inp["cv"], ray8=ray, ps=cfg["ps"],
@@ -126,3 +135,46 @@ def test_large_frame_driver_matches_whole_frame(name, n_bands, given_ray):
                         full_res_ray_relu=cfg["rr"])
     err = (out.float() - want).abs().max().item()
     assert err <= (2e-3 if cfg["f16"] else 1e-5), err
+
+
+def _oracle_band(u: O.UnitInputs, b: Band) -> np.ndarray:
+    """The oracle's unit on one exact-halo band of frame u, owned rows only."""
+    sl = slice(b.comp0, b.comp1)
+    ub = O.UnitInputs(**{**u.__dict__, "h": b.rows, "H": 8 * b.rows,
+                         "cv": band_intrinsics(u.cv, b),
+                         "normal0": np.ascontiguousarray(u.normal0[:, :, sl]),
+                         "ray8": np.ascontiguousarray(u.ray8[:, sl]),
+                         "prob": [np.ascontiguousarray(a[:, :, sl]) for a in u.prob],
+                         "xy": [np.ascontiguousarray(a[:, :, sl]) for a in u.xy],
+                         "angle": [np.ascontiguousarray(a[:, :, sl]) for a in u.angle],
+                         "mask": np.ascontiguousarray(u.mask[:, :, sl])})
+    return O.refine_unit(ub, crop=(8 * b.crop_top, 0, 8 * (b.own1 - b.own0), 8 * u.w))
+
+
+def test_fullsize_cfg3_matches_oracle():
+    """Config 3 at full size against the oracle: the whole 4096^2 frame
+    refined on the GPU in one call, the fp64 C restatement run as exact halo
+    bands on every host core (its ctypes calls release the GIL)."""
+    import brovisionml_b200 as bv
+
+    cfg = bench.CONFIGS["cfg3"]
+    u = O.gen_unit(cfg["H"], cfg["W"], 1, ps=cfg["ps"], dil=cfg["dil"], iters=cfg["iters"],
+                   seed=303)
+    dev = torch.device("cuda", 0)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+    got = bv.refine(t(u.normal0), [t(a) for a in u.prob], [t(a) for a in u.xy],
+                    [t(a) for a in u.angle], t(u.mask), u.fu, u.cu, u.fv, u.cv,
+                    ray8=t(u.ray8), ps=cfg["ps"], dil=cfg["dil"])
+    got = got.cpu().numpy()
+    n = max(1, min(64, os.cpu_count() or 1))
+    bands = plan_bands(u.h, n, halo_rows(cfg["iters"], cfg["ps"], cfg["dil"]))
+    with ThreadPoolExecutor(n) as ex:
+        parts = list(ex.map(lambda b: _oracle_band(u, b), bands))
+    want = np.concatenate(parts, axis=2)
+    assert want.shape == got.shape == (1, 3, cfg["H"], cfg["W"])
+    m = O.compare(got, want)
+    print(f"cfg3 full frame vs oracle ({n} bands): max-abs {m['max_abs']:.2e} mean-abs "
+          f"{m['mean_abs']:.2e}; angular error mean {m['ang_mean_deg']:.2e} p99 "
+          f"{m['ang_p99_deg']:.2e} max {m['ang_max_deg']:.2e} deg")
+    assert m["nonfinite"] == 0
+    assert m["max_abs"] <= O.TOL_F32, m

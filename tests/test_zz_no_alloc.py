@@ -7,7 +7,10 @@ refine with its scratch in a fixed array built into the library. This test
 calls it through the C ABI and checks it against bvml_refine with a caller
 workspace, on two calls in a row with different inputs (the shared scratch
 keeps the previous call's contents, which must not leak into the next
-result), and checks that work above the built-in scratch size is refused.
+result). Both entry points run the same kernels on the same inputs, so the
+results must be bit-identical, not merely within the parity tolerance. It
+also runs the largest batch the built-in scratch accepts and checks that one
+frame more is refused.
 
 The file name makes pytest collect it last; it also passes alone in a fresh
 process.
@@ -61,7 +64,49 @@ def test_refine_noalloc_matches_refine_twice(f16):
         assert rc == 0, lib.bvml_last_error().decode()
         err = (got.float() - want.float()).abs().max().item()
         assert err <= tol, (call, err)
+        # same kernels, same inputs: a partial scratch leak would show here
+        assert torch.equal(got, want), (call, err)
         assert torch.isfinite(got.float()).all()
+
+
+def test_refine_noalloc_largest_accepted_batch():
+    """96 frames of a 90x160 grid: the scratch regions reach the end of the
+    built-in array. Device-generated inputs (the CPU oracle is not needed:
+    the check is bit-equality with bvml_refine over a caller workspace)."""
+    from brovisionml_b200 import _capi
+
+    lib = _capi.lib
+    B, h, w, iters, P = 96, 90, 160, 2, 25
+    need = lib.bvml_refine_workspace_bytes(B, h, w)
+    assert need <= _capi.REFINE_NOALLOC_MAX_BYTES
+    assert lib.bvml_refine_workspace_bytes(B + 1, h, w) > _capi.REFINE_NOALLOC_MAX_BYTES
+    dev, dt = "cuda:0", torch.float16
+    g = torch.Generator(device=dev).manual_seed(5)
+    n0 = torch.nn.functional.normalize(torch.randn((B, 3, h, w), device=dev, generator=g),
+                                       dim=1)
+    n0[:, 2] = n0[:, 2].abs()  # roughly camera-facing
+    n0 = n0.to(dt)
+    prob = [torch.softmax(torch.randn((B, P, h, w), device=dev, generator=g), 1).to(dt)
+            for _ in range(iters)]
+    xy = [torch.randn((B, 2 * P, h, w), device=dev, generator=g).to(dt) for _ in range(iters)]
+    ang = [(0.3 * torch.rand((B, P, h, w), device=dev, generator=g)).to(dt)
+           for _ in range(iters)]
+    mask = torch.randn((B, 576, h, w), device=dev, generator=g).to(dt)
+    fu, cu, fv, cv = 0.8 * w, w / 2 + 0.0625, 0.8 * w, h / 2 + 0.0625
+    outs = []
+    for fn, extra in ((lib.bvml_refine, "ws"), (lib.bvml_refine_noalloc, None)):
+        out = torch.full((B, 3, 8 * h, 8 * w), float("nan"), device=dev, dtype=dt)
+        args = [n0.data_ptr(), None, _ptrs(prob), _ptrs(xy), _ptrs(ang), iters,
+                mask.data_ptr(), B, h, w, 5, 1, fu, cu, fv, cv, 0, 0, 0, 8 * h, 8 * w, 1]
+        if extra:
+            ws = torch.empty(need, device=dev, dtype=torch.uint8)
+            args += [ws.data_ptr(), need]
+        rc = fn(*(args + [out.data_ptr(), None]))
+        torch.cuda.synchronize()
+        assert rc == 0, lib.bvml_last_error().decode()
+        outs.append(out)
+    assert torch.isfinite(outs[1].float()).all()
+    assert torch.equal(outs[0], outs[1])
 
 
 def test_refine_noalloc_rejects_oversize():
