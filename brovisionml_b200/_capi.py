@@ -21,8 +21,8 @@ EXPORTS = ("bvml_last_error", "bvml_abi_version", "bvml_ray_relu", "bvml_angmf_p
            "bvml_convex_upsample", "bvml_l2_normalize_nchw", "bvml_slice2d",
            "bvml_refine_workspace_bytes", "bvml_refine", "bvml_probe_events",
            "bvml_refine_noalloc", "bvml_angmf_propagate_logits", "bvml_refine_logits",
-           "bvml_conv2d_nhwc_bf16", "bvml_conv2d_nhwc_bf16_ex", "bvml_stage_inputs",
-           "bvml_head_tail_1x1")
+           "bvml_conv2d_nhwc_f16", "bvml_conv2d_nhwc_f16_ex", "bvml_stage_inputs",
+           "bvml_head_tail_1x1", "bvml_refine_status", "bvml_probe_recorded")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(
@@ -66,8 +66,8 @@ lib.bvml_refine_noalloc.argtypes = ([_vp, _vp, ctypes.POINTER(_vp), ctypes.POINT
                                      ctypes.POINTER(_vp), _i, _vp] + [_i] * 5 + [_d] * 4
                                     + [_i] * 6 + [_vp, _vp])
 REFINE_NOALLOC_MAX_BYTES = 32 * 1024 * 1024
-lib.bvml_conv2d_nhwc_bf16.restype = _i
-lib.bvml_conv2d_nhwc_bf16.argtypes = [_vp, _vp, _vp] + [_i] * 8 + [_vp, _vp, _vp]
+lib.bvml_conv2d_nhwc_f16.restype = _i
+lib.bvml_conv2d_nhwc_f16.argtypes = [_vp, _vp, _vp] + [_i] * 8 + [_vp, _vp, _vp]
 
 
 class ConvEpilogue(ctypes.Structure):
@@ -78,10 +78,10 @@ class ConvEpilogue(ctypes.Structure):
                 ("xin", _vp), ("xin_c", _i), ("wx", _vp), ("xin_stride", _i)]
 
 
-EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, EPI_GRU_ZR, EPI_GRU_Q, EPI_C4_F32, EPI_SPLIT_BF16 = \
+EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, EPI_GRU_ZR, EPI_GRU_Q, EPI_C4_F32, EPI_SPLIT_F16 = \
     range(7)
-lib.bvml_conv2d_nhwc_bf16_ex.restype = _i
-lib.bvml_conv2d_nhwc_bf16_ex.argtypes = ([_vp, _i, _i, _i, _vp, _vp] + [_i] * 6
+lib.bvml_conv2d_nhwc_f16_ex.restype = _i
+lib.bvml_conv2d_nhwc_f16_ex.argtypes = ([_vp, _i, _i, _i, _vp, _vp] + [_i] * 6
                                           + [ctypes.POINTER(ConvEpilogue), _vp, _vp])
 lib.bvml_head_tail_1x1.restype = _i
 lib.bvml_head_tail_1x1.argtypes = [_vp, _i, _i, _vp, _vp, _vp, _vp] + [_i] * 5 + [_vp, _vp, _vp]
@@ -89,6 +89,10 @@ lib.bvml_stage_inputs.restype = _i
 lib.bvml_stage_inputs.argtypes = [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp]
 lib.bvml_probe_events.restype = _i
 lib.bvml_probe_events.argtypes = [ctypes.POINTER(_vp), _i]
+lib.bvml_probe_recorded.restype = _i
+lib.bvml_probe_recorded.argtypes = []
+lib.bvml_refine_status.restype = _i
+lib.bvml_refine_status.argtypes = [_vp, _vp]
 
 
 def abi_version() -> int:

@@ -11,4 +11,9 @@ cudaError_t launch_angmf(const AngmfLaunch& L, cudaStream_t s) {
     return launch_angmf_act<false>(L, s);
 }
 
+cudaError_t launch_angmf_iters(const AngmfItersLaunch& L, cudaStream_t s) {
+    if (L.act) return launch_angmf_iters_logits(L, s);
+    return launch_angmf_iters_act<false>(L, s);
+}
+
 }  // namespace bvml

@@ -41,17 +41,22 @@
 // evaluation can leave the reference's fp64 result by more than ~1e-6:
 //  * |dd| < 1e-5: the sign of dd (which flips the rotation) may be wrong in
 //    fp32, and the reference clamps |dd| < 1e-8;
-//  * w |sin(theta)| |g| > 20 |g_perp|: g nearly parallel to n, so the rotation
-//    direction comes from a cancellation; its fp32 error (~2e-7 |g|/|g_perp|)
-//    is only tolerable while the neighbour's weighted sine is small;
+//  * w |sin(theta)| |n.g| > 19.97 |g_perp|: g nearly parallel to n, so the
+//    rotation direction comes from the cancellation g - n (n.g); its fp32
+//    error (~2e-7 |n.g| / |g_perp|) is only tolerable while the neighbour's
+//    weighted sine is small;
 //  * |m|^2 < 0.04 after the RayReLU: the rotated normal points almost straight
 //    away from the camera and the clamped vector is a cancellation too;
 //  * |xy|^2 outside [1e-10, 1e30] (the reference's 1e-12 clamp on |xy|, or
 //    fp32 overflow), |theta| > pi (outside the approximations' range), or any
 //    NaN.
-// Such neighbours are dropped from the fast sum, recorded in a bit mask and
-// recomputed after the loop in fp64 exactly as the reference does. On
-// camera-facing inputs this is about 1 neighbour evaluation in 10^5.
+// The tests of one neighbour form a single predicate chain (unordered
+// comparisons, so NaN flags); a flagged neighbour's weight is zeroed and its
+// bit set in the pixel's mask, without a branch. After the loop, the flagged
+// neighbours are recomputed in fp64 exactly as the reference does; a pixel
+// whose fast sum came out non-finite (a flagged neighbour with an infinite or
+// NaN vector) or vanishing is recomputed over its whole window. On
+// camera-facing inputs about 1 neighbour evaluation in 10^5 is flagged.
 #pragma once
 
 #include "bvml_common.cuh"
@@ -64,6 +69,8 @@ namespace {
 
 constexpr int kTW = 32;         // tile width (16 pixel pairs)
 constexpr int kTH = 16;         // tile height
+// (angmf_iters_sync_bytes in bvml_internal.h counts tiles of this size)
+static_assert(kTW == 32 && kTH == 16, "sync-word count assumes 32 x 16 tiles");
 constexpr int kThreads = 256;   // one pixel pair per thread
 
 struct AngmfArgs {
@@ -230,7 +237,7 @@ __device__ __noinline__ double3 angmf_neighbor_exact(double nx, double ny, doubl
 }
 
 constexpr float kTau = 1e-5f;     // |dd| fix-up threshold
-constexpr float kGCond = 0.05f;   // 1 / (largest tolerated w |sin| |g| / |g_perp|)
+constexpr float kTMax = 19.97f;   // largest tolerated w |sin| |n.g| / |g_perp|
 constexpr float kMMin = 0.04f;    // smallest tolerated |m|^2 after the RayReLU
 constexpr float kQMin = 1e-10f, kQMax = 1e30f;  // |xy|^2 range of the fast path
 constexpr float kThMax = 3.1416f; // |theta| range of the sin / cos approximations
@@ -243,6 +250,66 @@ struct PairAcc {
     Mask bad0, bad1;  // neighbours left to the exact fix-up, per pixel of the pair
 };
 
+// Flag one pixel's evaluation of neighbour slot `bit` for the exact fix-up:
+// when |dd| < kTau, |t| > tlim, l2 < kMMin or |th| > kThMax (unordered: any
+// NaN flags), plus |xy|^2 = q outside [kQMin, kQMax] (QRANGE) and lw > 3.4e38
+// (WDEN), zero the weight wm and OR `bit` into the mask. One predicate chain
+// of comparisons and two predicated moves; the immediates are kTau, kMMin,
+// kThMax, kQMin, kQMax and 3.4e38 as fp32 bit patterns.
+#define BVML_FLAG_CORE                                                      \
+    "setp.ltu.f32 p, %2, 0f3727C5AC;\n\t"       /* |dd| < 1e-5   */          \
+    "setp.gtu.or.f32 p, %3, %4, p;\n\t"         /* |t| > tlim    */          \
+    "setp.ltu.or.f32 p, %5, 0f3D23D70A, p;\n\t" /* l2 < 0.04     */          \
+    "setp.gtu.or.f32 p, %6, 0f40490FF9, p;\n\t" /* |th| > 3.1416 */
+#define BVML_FLAG_Q(i)                                                      \
+    "setp.ltu.or.f32 p, %" #i ", 0f2EDBE6FF, p;\n\t" /* q < 1e-10 */         \
+    "setp.gtu.or.f32 p, %" #i ", 0f7149F2CA, p;\n\t" /* q > 1e30  */
+#define BVML_FLAG_W(i) "setp.gtu.or.f32 p, %" #i ", 0f7F7FC99E, p;\n\t" /* lw > 3.4e38 */
+#define BVML_FLAG_TAIL(op) "@p mov.f32 %0, 0f00000000;\n\t@p " op " %1, %1, %7;\n\t}"
+
+template <bool QRANGE, bool WDEN>
+__device__ __forceinline__ void flag_eval(float add, float at, float tlim, float l2, float ath,
+                                          float q, float lw, float& wm, uint32_t& m,
+                                          uint32_t bit) {
+    if constexpr (QRANGE && WDEN)
+        asm("{\n\t.reg .pred p;\n\t" BVML_FLAG_CORE BVML_FLAG_Q(8) BVML_FLAG_W(9)
+            BVML_FLAG_TAIL("or.b32")
+            : "+f"(wm), "+r"(m) : "f"(add), "f"(at), "f"(tlim), "f"(l2), "f"(ath), "r"(bit),
+              "f"(q), "f"(lw));
+    else if constexpr (QRANGE)
+        asm("{\n\t.reg .pred p;\n\t" BVML_FLAG_CORE BVML_FLAG_Q(8) BVML_FLAG_TAIL("or.b32")
+            : "+f"(wm), "+r"(m) : "f"(add), "f"(at), "f"(tlim), "f"(l2), "f"(ath), "r"(bit),
+              "f"(q));
+    else if constexpr (WDEN)
+        asm("{\n\t.reg .pred p;\n\t" BVML_FLAG_CORE BVML_FLAG_W(8) BVML_FLAG_TAIL("or.b32")
+            : "+f"(wm), "+r"(m) : "f"(add), "f"(at), "f"(tlim), "f"(l2), "f"(ath), "r"(bit),
+              "f"(lw));
+    else
+        asm("{\n\t.reg .pred p;\n\t" BVML_FLAG_CORE BVML_FLAG_TAIL("or.b32")
+            : "+f"(wm), "+r"(m) : "f"(add), "f"(at), "f"(tlim), "f"(l2), "f"(ath), "r"(bit));
+}
+template <bool QRANGE, bool WDEN>
+__device__ __forceinline__ void flag_eval(float add, float at, float tlim, float l2, float ath,
+                                          float q, float lw, float& wm,
+                                          unsigned long long& m, unsigned long long bit) {
+    if constexpr (QRANGE && WDEN)
+        asm("{\n\t.reg .pred p;\n\t" BVML_FLAG_CORE BVML_FLAG_Q(8) BVML_FLAG_W(9)
+            BVML_FLAG_TAIL("or.b64")
+            : "+f"(wm), "+l"(m) : "f"(add), "f"(at), "f"(tlim), "f"(l2), "f"(ath), "l"(bit),
+              "f"(q), "f"(lw));
+    else if constexpr (QRANGE)
+        asm("{\n\t.reg .pred p;\n\t" BVML_FLAG_CORE BVML_FLAG_Q(8) BVML_FLAG_TAIL("or.b64")
+            : "+f"(wm), "+l"(m) : "f"(add), "f"(at), "f"(tlim), "f"(l2), "f"(ath), "l"(bit),
+              "f"(q));
+    else if constexpr (WDEN)
+        asm("{\n\t.reg .pred p;\n\t" BVML_FLAG_CORE BVML_FLAG_W(8) BVML_FLAG_TAIL("or.b64")
+            : "+f"(wm), "+l"(m) : "f"(add), "f"(at), "f"(tlim), "f"(l2), "f"(ath), "l"(bit),
+              "f"(lw));
+    else
+        asm("{\n\t.reg .pred p;\n\t" BVML_FLAG_CORE BVML_FLAG_TAIL("or.b64")
+            : "+f"(wm), "+l"(m) : "f"(add), "f"(at), "f"(tlim), "f"(l2), "f"(ath), "l"(bit));
+}
+
 // One neighbour slot n for a pixel pair: rotate the (unit) source normals,
 // RayReLU them against the pixels' (unit) rays, accumulate with weight w.
 // tun = -tu is supplied by the caller (from the staged table).
@@ -250,6 +317,8 @@ struct PairAcc {
 // range except for an all-zero pair (|xy|^2 lies in {0} u [3.6e-15, 8.6e9]),
 // and a zero pair makes dd = inf * 0 = NaN, which the |dd| test flags.
 // WDEN: wt holds the weight's denominator d (w = 1/d), see head_activation.
+// A flagged evaluation keeps its (possibly non-finite) vector but gets weight
+// zero; a non-finite fast sum sends the pixel to a whole-window recompute.
 template <typename Mask, bool QRANGE, bool WDEN>
 __device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 th, float2 wt,
                                            float2 nx, float2 ny, float2 nz, float2 tu,
@@ -268,7 +337,6 @@ __device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 t
     const float2 gpyn = fma2(ny, ng, X);
     const float2 gpz = fnma2(nz, ng, gz);
     const float2 gp2 = fma2(gpx, gpx, fma2(gpyn, gpyn, mul2(gpz, gpz)));
-    const float2 gg2 = fma2(ng, ng, gp2);                    // |g|^2 = |g_perp|^2 + (n.g)^2
     // |g_perp| = 0 gives an infinite or NaN kk below, which the fix-up tests catch
     const float2 gi = rsqrt2_ftz(gp2);
     // sin / cos of theta with the hardware approximations (abs. error ~5e-7
@@ -276,19 +344,15 @@ __device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 t
     const float2 sn = sin2_approx(th);
     const float2 cs = cos2_approx(th);
     float2 kk = mul2(sn, gi);
-    // w |sin| |g| > |g_perp| / kGCond  <=>  (w sin / |g_perp|)^2 |g|^2 > 1 / kGCond^2
-    constexpr float kGMax = 1.0f / (kGCond * kGCond);
-    float2 gcond, glim, d2;
+    // cancellation guard: t = w sin (n.g) / |g_perp| against kTMax (with w =
+    // 1/d: sin (n.g) / |g_perp| against d kTMax)
+    float2 t, tlim;
     if constexpr (WDEN) {
-        // w = 1/d: (sin / |g_perp|)^2 |g|^2 against d^2 / kGCond^2 (an
-        // infinite d^2 is flagged below, with |m|^2 d^2)
-        d2 = mul2(wt, wt);
-        gcond = mul2(mul2(kk, kk), gg2);
-        glim = mul2(d2, f2(kGMax));
+        t = mul2(kk, ng);
+        tlim = mul2(wt, f2(kTMax));
     } else {
-        const float2 wk = mul2(wt, kk);
-        gcond = mul2(mul2(wk, wk), gg2);
-        glim = f2(kGMax);
+        t = mul2(mul2(wt, kk), ng);
+        tlim = f2(kTMax);
     }
     kk.x = __uint_as_float(__float_as_uint(kk.x) ^ (__float_as_uint(dd.x) & 0x80000000u));
     kk.y = __uint_as_float(__float_as_uint(kk.y) ^ (__float_as_uint(dd.y) & 0x80000000u));
@@ -302,42 +366,23 @@ __device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 t
     const float2 my = fma2(ry, dc, qy);
     const float2 mz = fma2(rz, dc, qz);
     const float2 l2 = fma2(mx, mx, fma2(my, my, mul2(mz, mz)));
-    // bitwise | : every test is evaluated, no branches
-    bool b0 = !(fabsf(dd.x) >= kTau) | !(gcond.x <= glim.x) | !(l2.x >= kMMin) |
-              !(fabsf(th.x) <= kThMax);
-    bool b1 = !(fabsf(dd.y) >= kTau) | !(gcond.y <= glim.y) | !(l2.y >= kMMin) |
-              !(fabsf(th.y) <= kThMax);
-    if constexpr (QRANGE) {
-        b0 |= !(q.x >= kQMin) | !(q.x <= kQMax);
-        b1 |= !(q.y >= kQMin) | !(q.y <= kQMax);
-    }
     // w / |m|; with w = 1/d one rsqrt of |m|^2 d^2. d^2 overflows for weights
     // below ~5e-20: those go to the fix-up, whose fp64 weight keeps them
     // nonzero (they decide the direction where every weight is that small).
-    float2 wm;
+    float2 wm, lw = f2(0.0f);
     if constexpr (WDEN) {
-        const float2 lw = mul2(l2, d2);
-        b0 |= !(lw.x <= 3.4e38f);
-        b1 |= !(lw.y <= 3.4e38f);
+        lw = mul2(l2, mul2(wt, wt));
         wm = rsqrt2_ftz(lw);
     } else {
         wm = mul2(wt, rsqrt2_ftz(l2));
     }
-    float2 ux = mx, uy = my, uz = mz;
-    if (b0 | b1) {  // rare: leave the neighbour to the exact fix-up
-        // weight and vector both zeroed: the vector may be infinite or NaN here
-        if (b0) {
-            wm.x = ux.x = uy.x = uz.x = 0.0f;
-            A.bad0 |= Mask(1) << n;
-        }
-        if (b1) {
-            wm.y = ux.y = uy.y = uz.y = 0.0f;
-            A.bad1 |= Mask(1) << n;
-        }
-    }
-    A.x = fma2(wm, ux, A.x);
-    A.y = fma2(wm, uy, A.y);
-    A.z = fma2(wm, uz, A.z);
+    flag_eval<QRANGE, WDEN>(fabsf(dd.x), fabsf(t.x), tlim.x, l2.x, fabsf(th.x), q.x, lw.x,
+                            wm.x, A.bad0, Mask(1) << n);
+    flag_eval<QRANGE, WDEN>(fabsf(dd.y), fabsf(t.y), tlim.y, l2.y, fabsf(th.y), q.y, lw.y,
+                            wm.y, A.bad1, Mask(1) << n);
+    A.x = fma2(wm, mx, A.x);
+    A.y = fma2(wm, my, A.y);
+    A.z = fma2(wm, mz, A.z);
 }
 
 // The replicate-padded halo of unit source normals in shared memory. For each
@@ -450,7 +495,7 @@ __device__ __forceinline__ void stage_normals(const TNI* __restrict__ pnb,
 // kernel): one item per two source columns, so each channel of an item is
 // one 8-byte store to the even plane and two 4-byte stores to the odd plane,
 // and the item index splits with a constant divisor.
-template <int R, typename TNI, bool FUSE_RR>
+template <int R, typename TNI, bool FUSE_RR, bool COH = false>
 __device__ __forceinline__ void stage_normals_ct(const TNI* __restrict__ pnb,
                                                  const float* __restrict__ ray, const NTile& T,
                                                  int x0, int y0, const AngmfArgs& a) {
@@ -468,8 +513,8 @@ __device__ __forceinline__ void stage_normals_ct(const TNI* __restrict__ pnb,
         float v0[3], v1[3];
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-            v0[c] = St<TNI>::ld(pnb + c * HW + q0);
-            v1[c] = St<TNI>::ld(pnb + c * HW + q1);
+            v0[c] = ldn<TNI, COH>(pnb + c * HW + q0);
+            v1[c] = ldn<TNI, COH>(pnb + c * HW + q1);
         }
         if (FUSE_RR) {
             ray_relu_f32(v0[0], v0[1], v0[2], __ldg(ray + q0), __ldg(ray + HW + q0),
@@ -529,7 +574,7 @@ __device__ __forceinline__ NPair npair(const NTile& T, int i, int j) {
 // Exact fp64 fix-ups of the flagged neighbours of one pixel; returns the sum
 // in fp64 (a pixel whose weights all vanish has a sum far below the float
 // range, and the reference normalises it in fp64).
-template <int PS, typename TS, typename TNI, bool FUSE_RR, bool ACT, typename Mask>
+template <int PS, typename TS, typename TNI, bool FUSE_RR, bool ACT, bool COH, typename Mask>
 __device__ __noinline__ double3 fixups(Mask m, int b, int x, int y, const TNI* __restrict__ pn,
                                       const TS* __restrict__ prob, const TS* __restrict__ xy,
                                       const TS* __restrict__ ang, const float* __restrict__ ray,
@@ -552,8 +597,8 @@ __device__ __noinline__ double3 fixups(Mask m, int b, int x, int y, const TNI* _
         const int sy = clampi(y - a.R + ky * a.dil, 0, a.H - 1);
         const int sx = clampi(x - a.R + kx * a.dil, 0, a.W - 1);
         const long sp = (long)sy * a.W + sx;
-        double nx = St<TNI>::ld(pnb + sp), ny = St<TNI>::ld(pnb + HW + sp),
-               nz = St<TNI>::ld(pnb + 2 * HW + sp);
+        double nx = ldn<TNI, COH>(pnb + sp), ny = ldn<TNI, COH>(pnb + HW + sp),
+               nz = ldn<TNI, COH>(pnb + 2 * HW + sp);
         if (FUSE_RR)
             ray_relu_exact(nx, ny, nz, __ldg(ray + sp), __ldg(ray + HW + sp),
                            __ldg(ray + 2 * HW + sp));
@@ -572,7 +617,7 @@ __device__ __noinline__ double3 fixups(Mask m, int b, int x, int y, const TNI* _
 
 // Normalise the pair's sums (after fix-ups) and store.
 template <int PS, typename TS, typename TNI, typename TNO, bool FUSE_RR, bool ACT,
-          typename Mask>
+          bool COH, typename Mask>
 __device__ __forceinline__ void finish_pair(PairAcc<Mask>& A, int b, int x, int y, bool two,
                                             bool vec, const TNI* pn, const TS* prob,
                                             const TS* xy, const TS* ang, const float* ray,
@@ -583,22 +628,26 @@ __device__ __forceinline__ void finish_pair(PairAcc<Mask>& A, int b, int x, int 
     // A pixel with fix-ups is finished in fp64 (fast sum + exact sum, then the
     // reference's normalise, src/dsine_ops.cpp:165-169). A fast sum below
     // 1e-30 means every weight (nearly) vanished: its direction needs more
-    // range than fp32 has, so the whole window is recomputed exactly.
+    // range than fp32 has, so the whole window is recomputed exactly; so is a
+    // non-finite fast sum.
     constexpr Mask kAll = (P_OF<PS>::value >= 8 * (int)sizeof(Mask))
                               ? ~Mask(0)
                               : ((Mask(1) << P_OF<PS>::value) - 1);
-    auto tiny = [](float u, float v, float w) {
-        return fmaxf(fabsf(u), fmaxf(fabsf(v), fabsf(w))) < 1e-30f;
+    // a fast sum that is non-finite (a flagged neighbour's vector was) or
+    // vanishing: the whole window in fp64 (the unordered test also catches NaN)
+    auto whole = [](float u, float v, float w) {
+        const float a = fabsf(u) + fabsf(v) + fabsf(w);
+        return !(a >= 1e-30f && a <= 3.0e38f);
     };
     auto exact = [&](Mask m, int px, float fx, float fy, float fz, float& o0, float& o1,
                      float& o2) {
-        if (tiny(fx, fy, fz)) {
+        if (whole(fx, fy, fz)) {
             m = kAll;
             fx = fy = fz = 0.0f;
         }
         if (m == 0) return;
         const double3 f =
-            fixups<PS, TS, TNI, FUSE_RR, ACT>(m, b, px, y, pn, prob, xy, ang, ray, a);
+            fixups<PS, TS, TNI, FUSE_RR, ACT, COH>(m, b, px, y, pn, prob, xy, ang, ray, a);
         const double sx = (double)fx + f.x, sy = (double)fy + f.y, sz = (double)fz + f.z;
         const double sinv = 1.0 / fmax(sqrt(sx * sx + sy * sy + sz * sz), 1e-12);
         o0 = (float)(sx * sinv);
@@ -698,7 +747,7 @@ angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* 
                 q.nz, q.tu, q.tun, q.tv, ifu2, ifv2, rx, ry, rz, A);
         }
     }
-    finish_pair<PS, TS, TNI, TNO, FUSE_RR, ACT>(A, b, x, y, two, vec, pn, prob, xy, ang, ray,
+    finish_pair<PS, TS, TNI, TNO, FUSE_RR, ACT, false>(A, b, x, y, two, vec, pn, prob, xy, ang, ray,
                                                 out, a);
 }
 
@@ -759,11 +808,18 @@ template <> __device__ __forceinline__ float2 lds2<__half>(const __half* p) {
     return __half22float2(*reinterpret_cast<const __half2*>(p));
 }
 
-template <int PS, int DIL, typename TS, typename TNI, typename TNO, bool FUSE_RR, bool ACT>
-__global__ void __launch_bounds__(kThreads, (StagedCfg<PS, DIL, TS>::kMinBlocks))
-angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
-                    const TS* __restrict__ xy, const TS* __restrict__ ang,
-                    const float* __restrict__ ray, TNO* __restrict__ out, const AngmfArgs a) {
+// One tile of one iteration: frame b, tile origin (x0, y0). `pre` runs after
+// the first ring slots are in flight and before the normal halo is staged
+// (the persistent kernel waits there for the tiles it depends on). COH: read
+// the normals with L2-coherent loads (they were written in the same launch).
+template <int PS, int DIL, typename TS, typename TNI, typename TNO, bool FUSE_RR, bool ACT,
+          bool COH, typename Pre>
+__device__ __forceinline__ void angmf_tile(const TNI* __restrict__ pn,
+                                           const TS* __restrict__ prob,
+                                           const TS* __restrict__ xy, const TS* __restrict__ ang,
+                                           const float* __restrict__ ray, TNO* __restrict__ out,
+                                           const AngmfArgs& a, int b, int x0, int y0,
+                                           Pre&& pre) {
     constexpr int P = PS * PS;
     constexpr int R = (PS / 2) * DIL;
     constexpr int SW = kTW + 2 * R, SH = kTH + 2 * R;
@@ -775,8 +831,6 @@ angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
     TS* ring = reinterpret_cast<TS*>(smem4) + warp * S::kN * S::kElemsW;  // this warp's slots
     NTile T;
     T.carve(reinterpret_cast<char*>(smem4) + S::kBytes, SW, SH);
-    // grid (tiles_x, tiles_y, frames)
-    const int b = blockIdx.z, x0 = blockIdx.x * kTW, y0 = blockIdx.y * kTH;
     const long HW = a.HW;
     const TS* xyb = xy + (long)b * 2 * P * HW;
     const TS* prb = prob + (long)b * P * HW;
@@ -807,19 +861,30 @@ angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
         }
     };
 
-    // prologue: the first kD slots in flight while the normals are staged
+    // prologue: the first kD slots in flight while the normals are staged (the
+    // warp's lanes are done with the ring of any earlier tile)
+    __syncwarp();
 #pragma unroll
     for (int sl = 0; sl < S::kD; ++sl) {
         if (sl < P) issue(sl);
         cp_async_commit();
     }
-    stage_normals_ct<R, TNI, FUSE_RR>(pn + (long)b * 3 * HW, ray, T, x0, y0, a);
+    pre();
+    stage_normals_ct<R, TNI, FUSE_RR, COH>(pn + (long)b * 3 * HW, ray, T, x0, y0, a);
     __syncthreads();  // the normal halo is shared by all warps
 
     const int lx = 2 * (lane & 15);
     const int ly = S::kRowsW * warp + (lane >> 4);
     const int x = x0 + lx, y = y0 + ly;
     const bool active = y < a.H && x < a.W;
+    // A warp whose lanes all lie outside the frame has nothing to compute: its
+    // ring is private and no CTA barrier follows, so it leaves now. Lanes of a
+    // partly covered warp compute on the clamped, zero-filled data like the
+    // others (no per-step branch) and drop their results at the end.
+    if (__all_sync(0xffffffffu, !active)) {
+        cp_async_wait<0>();
+        return;
+    }
     const bool two = x + 1 < a.W;
     const long p0 = (long)min(y, a.H - 1) * a.W + min(x, a.W - 1);
     const long p1 = two ? p0 + 1 : p0;
@@ -831,7 +896,7 @@ angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
     const TS* ring_lane = ring + (lane >> 4) * kTW + lx;   // this pair inside a slot
     const int pbase = ly * SWH + (lx >> 1);                // this pair's first window pair
 
-#pragma unroll 1
+#pragma unroll  // every ring slot and window offset an immediate
     for (int ky = 0; ky < PS; ++ky) {
         const int grp = (ky % S::kM) * PS;                  // slot group of this window row
         const int prev_grp = ((ky + S::kM - 1) % S::kM) * PS;  // ... of the previous row
@@ -859,7 +924,7 @@ angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
                     }
                 }
             }
-            if (active) {
+            {
                 const TS* st = st_row + kx * S::kElemsW;
                 // window column offset: a constant once the kx loop is unrolled
                 const int dj = kx * DIL;
@@ -890,12 +955,135 @@ angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
     }
     cp_async_wait<0>();
     if (!active) return;
-    finish_pair<PS, TS, TNI, TNO, FUSE_RR, ACT>(A, b, x, y, two, true, pn, prob, xy, ang, ray,
-                                                out, a);
+    finish_pair<PS, TS, TNI, TNO, FUSE_RR, ACT, COH>(A, b, x, y, two, true, pn, prob, xy, ang,
+                                                     ray, out, a);
 }
 
-template <int PS, typename TS, typename TNI, typename TNO, bool FUSE_RR, bool ACT>
-cudaError_t launch_t(const AngmfLaunch& L, cudaStream_t s) {
+template <int PS, int DIL, typename TS, typename TNI, typename TNO, bool FUSE_RR, bool ACT>
+__global__ void __launch_bounds__(kThreads, (StagedCfg<PS, DIL, TS>::kMinBlocks))
+angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
+                    const TS* __restrict__ xy, const TS* __restrict__ ang,
+                    const float* __restrict__ ray, TNO* __restrict__ out, const AngmfArgs a) {
+    // grid (tiles_x, tiles_y, frames)
+    angmf_tile<PS, DIL, TS, TNI, TNO, FUSE_RR, ACT, false>(
+        pn, prob, xy, ang, ray, out, a, (int)blockIdx.z, (int)blockIdx.x * kTW,
+        (int)blockIdx.y * kTH, [] {});
+}
+
+// ---------------------------------------------------------------------------
+// Persistent kernel: all iterations of the fused refine in one launch.
+//
+// Work items are (iteration, frame, tile), numbered iteration-major, and CTAs
+// take them in order from an atomic counter. The tile of iteration it reads
+// iteration it-1's normals of its own and its 8 neighbouring tiles (the halo
+// R <= 4 fits inside one tile on every side), so before staging them it waits
+// until those tiles' completion counters reach it; one thread per neighbour
+// polls with acquire loads while the tile's own first ring slots (inputs of
+// iteration it, independent of the normals) are already in flight. A tile
+// publishes its own counter (release, after a CTA barrier) once its outputs
+// are stored. Every item a CTA waits on was taken earlier by a CTA that is
+// running, so the order always makes progress whatever the residency; there
+// is no barrier across the whole grid, and the tiles of iteration it+1 run
+// while the last tiles of iteration it finish (the kernel boundary and its
+// tail of partly idle SMs is paid once, not once per iteration). It is used
+// for batches of at most kPersistentMaxWaves waves of tiles per iteration;
+// larger batches launch the one-tile kernel once per iteration.
+//
+// Iteration it writes buf[it & 1] and reads buf[(it - 1) & 1] (iteration 0
+// reads the decoder normals, RayReLU fused in the staging). Writing
+// buf[it & 1] over what iteration it-1 of a neighbouring tile reads is safe
+// because it waits for exactly those tiles. The waits are bounded
+// (kDepWaitLimit polls): a wait that gives up sets the status word and the
+// tile goes on (no hang); the host reads the word with bvml_refine_status.
+constexpr int kMaxFusedIters = 64;
+constexpr unsigned kDepWaitLimit = 1u << 22;
+constexpr long kPersistentMaxWaves = 3;  // tiles per iteration, in waves of the GPU
+
+struct AngmfIters {
+    const void* pn0;                    // iteration 0 input normals (storage type)
+    const void* prob[kMaxFusedIters];   // per iteration (storage type)
+    const void* xy[kMaxFusedIters];
+    const void* ang[kMaxFusedIters];
+    float* buf[2];                      // fp32 normals, ping-pong
+    int iters;
+    int first;                          // first iteration this launch runs
+    int* counter;                       // next work item (zero at launch)
+    int* done;                          // per tile: iterations completed (zero at launch)
+    int* status;                        // nonzero: a dependency wait gave up
+};
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+    asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <int PS, int DIL, typename TS, bool ACT>
+__global__ void __launch_bounds__(kThreads, (StagedCfg<PS, DIL, TS>::kMinBlocks))
+angmf_iters_kernel(const float* __restrict__ ray, const AngmfArgs a, const AngmfIters J) {
+    __shared__ int s_item[2];
+    const int tid = threadIdx.x;
+    const int per_it = a.tiles_x * a.tiles_y * a.B;
+    const int total = per_it * (J.iters - J.first);
+    if (tid == 0) s_item[0] = atomicAdd(J.counter, 1);
+    __syncthreads();
+    int item = s_item[0];
+    int par = 0;
+    while (item < total) {
+        const int it = J.first + item / per_it;
+        int t = item % per_it;
+        const int tx = t % a.tiles_x;
+        t /= a.tiles_x;
+        const int ty = t % a.tiles_y;
+        const int b = t / a.tiles_y;
+        int* mine = J.done + ((long)b * a.tiles_y + ty) * a.tiles_x + tx;
+        // the next item, read by every thread after this item's first barrier
+        if (tid == 0) s_item[par ^ 1] = atomicAdd(J.counter, 1);
+        auto pre = [&] {
+            if (it > J.first && tid < 9) {
+                const int nx = tx + tid % 3 - 1, ny = ty + tid / 3 - 1;
+                if (nx >= 0 && nx < a.tiles_x && ny >= 0 && ny < a.tiles_y) {
+                    const int* f = J.done + ((long)b * a.tiles_y + ny) * a.tiles_x + nx;
+                    // bounded; once any wait has given up, the others stop too
+                    unsigned k = 0;
+                    while (ld_acquire_gpu(f) < it - J.first) {
+                        if (++k == kDepWaitLimit) {
+                            atomicOr(J.status, 1);
+                            break;
+                        }
+                        if (ld_acquire_gpu(J.status) != 0) break;
+                        __nanosleep(64);
+                    }
+                }
+            }
+            __syncthreads();  // the neighbours' normals are visible to every thread
+        };
+        float* o = J.buf[it & 1];
+        if (it == 0)
+            angmf_tile<PS, DIL, TS, TS, float, true, ACT, true>(
+                static_cast<const TS*>(J.pn0), static_cast<const TS*>(J.prob[0]),
+                static_cast<const TS*>(J.xy[0]), static_cast<const TS*>(J.ang[0]), ray, o, a, b,
+                tx * kTW, ty * kTH, pre);
+        else
+            angmf_tile<PS, DIL, TS, float, float, false, ACT, true>(
+                J.buf[(it - 1) & 1], static_cast<const TS*>(J.prob[it]),
+                static_cast<const TS*>(J.xy[it]), static_cast<const TS*>(J.ang[it]), ray, o, a,
+                b, tx * kTW, ty * kTH, pre);
+        __syncthreads();  // every output of the tile stored (and the halo no longer read)
+        if (tid == 0) {
+            __threadfence();
+            st_release_gpu(mine, it - J.first + 1);
+        }
+        item = s_item[par ^ 1];
+        par ^= 1;
+    }
+}
+
+template <int PS, typename LaunchT>
+AngmfArgs make_args(const LaunchT& L) {
     AngmfArgs a;
     a.B = L.B;
     a.H = L.H;
@@ -913,6 +1101,85 @@ cudaError_t launch_t(const AngmfLaunch& L, cudaStream_t s) {
     a.cu = L.cu;
     a.fv = L.fv;
     a.cv = L.cv;
+    return a;
+}
+
+// The persistent all-iterations kernel for one window / storage type:
+// cudaErrorNotSupported when the shape does not take the staged path (the
+// caller then launches iteration by iteration).
+template <int PS, int DIL, typename TS, bool ACT>
+cudaError_t launch_iters_t(const AngmfItersLaunch& L, cudaStream_t s) {
+    AngmfArgs a = make_args<PS>(L);
+    const long per_it = (long)a.tiles_x * a.tiles_y * L.B;
+    const long total = per_it * (L.iters - L.first);
+    if (total <= 0 || total > 0x7fffffffL - 0x100000L) return cudaErrorNotSupported;
+    auto kern = angmf_iters_kernel<PS, DIL, TS, ACT>;
+    const size_t smem = StagedCfg<PS, DIL, TS>::kSmem;
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 0, per_sm = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return e;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem)) !=
+        cudaSuccess)
+        return e;
+    if (per_sm < 1) return cudaErrorNotSupported;
+    const long slots = (long)sms * per_sm;
+    // Per tile, the persistent loop costs about 1.3 us more than a one-tile
+    // CTA (claiming the item, the completion fence, the dependency poll): it
+    // pays off only where an iteration is a few waves of tiles, so that the
+    // per-launch tails it removes are a large share (32 frames of 720p: 2.2
+    // waves, 5 % faster per unit; from 64 frames on, one launch per iteration
+    // is faster).
+    if (per_it > kPersistentMaxWaves * slots) return cudaErrorNotSupported;
+    const unsigned grid = (unsigned)(total < slots ? total : slots);
+    e = cudaMemsetAsync(L.sync, 0, angmf_iters_sync_bytes(L.B, L.H, L.W), s);
+    if (e != cudaSuccess) return e;
+    AngmfIters J{};
+    J.pn0 = L.pn0;
+    for (int i = 0; i < L.iters; ++i) {
+        J.prob[i] = L.prob[i];
+        J.xy[i] = L.xy[i];
+        J.ang[i] = L.angle[i];
+    }
+    J.buf[0] = L.buf[0];
+    J.buf[1] = L.buf[1];
+    J.iters = L.iters;
+    J.first = L.first;
+    J.counter = L.sync;
+    J.status = L.sync + 1;
+    J.done = L.sync + kSyncHeaderWords;
+    kern<<<grid, kThreads, smem, s>>>(L.ray, a, J);
+    return cudaGetLastError();
+}
+
+template <typename TS, bool ACT>
+cudaError_t launch_iters_st(const AngmfItersLaunch& L, cudaStream_t s) {
+    if (L.iters < 1 || L.iters > kMaxFusedIters) return cudaErrorNotSupported;
+    if ((L.W % Stages<TS, 5>::kEpc) != 0 || (L.dil != 1 && L.dil != 2))
+        return cudaErrorNotSupported;
+    switch (L.ps * 4 + L.dil) {
+        case 3 * 4 + 1: return launch_iters_t<3, 1, TS, ACT>(L, s);
+        case 3 * 4 + 2: return launch_iters_t<3, 2, TS, ACT>(L, s);
+        case 5 * 4 + 1: return launch_iters_t<5, 1, TS, ACT>(L, s);
+        case 5 * 4 + 2: return launch_iters_t<5, 2, TS, ACT>(L, s);
+        case 7 * 4 + 1: return launch_iters_t<7, 1, TS, ACT>(L, s);
+        case 7 * 4 + 2: return launch_iters_t<7, 2, TS, ACT>(L, s);
+        default: return cudaErrorNotSupported;
+    }
+}
+
+template <bool ACT>
+cudaError_t launch_angmf_iters_act(const AngmfItersLaunch& L, cudaStream_t s) {
+    if (L.st == SType::F32) return launch_iters_st<float, ACT>(L, s);
+    return launch_iters_st<__half, ACT>(L, s);
+}
+
+template <int PS, typename TS, typename TNI, typename TNO, bool FUSE_RR, bool ACT>
+cudaError_t launch_t(const AngmfLaunch& L, cudaStream_t s) {
+    AngmfArgs a = make_args<PS>(L);
     const size_t nsmem = NTile::bytes(kTW + 2 * a.R, kTH + 2 * a.R);
     const long blocks = (long)a.tiles_x * a.tiles_y * L.B;
     if (blocks > 0x7fffffffL) return cudaErrorInvalidConfiguration;

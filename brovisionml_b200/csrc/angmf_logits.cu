@@ -11,4 +11,8 @@ cudaError_t launch_angmf_logits(const AngmfLaunch& L, cudaStream_t s) {
     return launch_angmf_act<true>(L, s);
 }
 
+cudaError_t launch_angmf_iters_logits(const AngmfItersLaunch& L, cudaStream_t s) {
+    return launch_angmf_iters_act<true>(L, s);
+}
+
 }  // namespace bvml

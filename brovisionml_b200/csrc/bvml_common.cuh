@@ -76,6 +76,8 @@ __device__ __forceinline__ float2 rcp2_ftz(float2 a) { return make_float2(rcp_ft
 template <typename T> struct St;
 template <> struct St<float> {
     __device__ __forceinline__ static float ld(const float* p) { return __ldg(p); }
+    // L2-coherent load (no L1): data another CTA of the same launch wrote.
+    __device__ __forceinline__ static float ldcg(const float* p) { return __ldcg(p); }
     // Two consecutive elements; p must be 8-byte aligned.
     __device__ __forceinline__ static float2 ld2(const float* p) {
         return __ldg(reinterpret_cast<const float2*>(p));
@@ -92,6 +94,7 @@ template <> struct St<float> {
 };
 template <> struct St<__half> {
     __device__ __forceinline__ static float ld(const __half* p) { return __half2float(__ldg(p)); }
+    __device__ __forceinline__ static float ldcg(const __half* p) { return __half2float(__ldcg(p)); }
     __device__ __forceinline__ static float2 ld2(const __half* p) {
         return __half22float2(__ldg(reinterpret_cast<const __half2*>(p)));
     }
@@ -106,6 +109,14 @@ template <> struct St<__half> {
         *reinterpret_cast<__half2*>(p) = __float22half2_rn(v);
     }
 };
+
+// A normal component: read-only path, or L2-coherent (COH) where the normals
+// were written earlier in the same launch by other CTAs.
+template <typename T, bool COH>
+__device__ __forceinline__ float ldn(const T* p) {
+    if constexpr (COH) return St<T>::ldcg(p);
+    else return St<T>::ld(p);
+}
 
 __device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
 

@@ -29,6 +29,33 @@ struct AngmfLaunch {
 cudaError_t launch_angmf(const AngmfLaunch& L, cudaStream_t s);
 cudaError_t launch_angmf_logits(const AngmfLaunch& L, cudaStream_t s);  // L.act variants
 
+// All iterations of the fused refine's AngMF in one persistent launch (tiles
+// taken in iteration-major order, each waiting for its neighbour tiles of the
+// previous iteration). Returns cudaErrorNotSupported for shapes that do not
+// take the staged path; the caller then launches iteration by iteration.
+struct AngmfItersLaunch {
+    const void* pn0;              // (B,3,H,W) decoder normals, storage type st
+    const void* const* prob;      // iters x (B,P,H,W)
+    const void* const* xy;        // iters x (B,2P,H,W)
+    const void* const* angle;     // iters x (B,P,H,W)
+    const float* ray;             // (3,H,W)
+    float* buf[2];                // (B,3,H,W) fp32 each; iteration i writes buf[i & 1]
+    int* sync;                    // angmf_iters_sync_bytes(B,H,W), zeroed by the launch
+    SType st;
+    bool act;
+    int iters, B, H, W, ps, dil;
+    int first;                    // first iteration of this launch (earlier ones done)
+    double fu, cu, fv, cv;
+};
+// sync words: [0] work counter, [1] status, [kSyncHeaderWords ..) one per tile
+constexpr int kSyncHeaderWords = 64;
+inline size_t angmf_iters_sync_bytes(int B, int H, int W) {
+    const size_t tiles = (size_t)((W + 31) / 32) * (size_t)((H + 15) / 16) * (size_t)B;
+    return sizeof(int) * (kSyncHeaderWords + tiles);
+}
+cudaError_t launch_angmf_iters(const AngmfItersLaunch& L, cudaStream_t s);
+cudaError_t launch_angmf_iters_logits(const AngmfItersLaunch& L, cudaStream_t s);
+
 struct UpsampleLaunch {
     const void* n;       // (B,3,h,w); type n_t
     const void* mask;    // (B,576,h,w) storage type st
@@ -47,37 +74,37 @@ enum class ConvEpi : int {
 };
 
 struct ConvLaunch {
-    const void* x;       // (B,H,W,x_c) bf16; channels [cin_off, cin_off + cin_pad) are read
-    const void* w;       // (ks*ks, cout_pad, cin_pad) bf16
+    const void* x;       // (B,H,W,x_c) fp16; channels [cin_off, cin_off + cin_pad) are read
+    const void* w;       // (ks*ks, cout_pad, cin_pad) fp16
     const float* bias;   // (cout) fp32
     int* err;            // device int: nonzero if a pipeline wait gave up
     int B, H, W, x_c, cin_off, cin_pad, cout, cout_pad, ks;
     ConvEpi epi;
     int act;             // NHWC: 0 none, 1 ReLU, 2 sigmoid, 3 tanh; C4_32: 0, 1
-    void* y;             // NHWC: (B,H,W,out_c) bf16 at out_off; C4_32: (B,out_c/4,H,W,4) fp32
+    void* y;             // NHWC: (B,H,W,out_c) fp16 at out_off; C4_32: (B,out_c/4,H,W,4) fp32
                          // at channel out_off; PLANAR: (B,cout,H,W)
     int out_c, out_off;
     float* h32;          // GRU: fp32 hidden state, C4 (B,16,H,W,4)
-    void* z;             // GRU: gate z, C8 bf16 (B,8,H,W,8)
+    void* z;             // GRU: gate z, C8 fp16 (B,8,H,W,8)
     void* rh;            // GRU_ZR: r * h at channels [0,64) of (B,H,W,rh_c)
     int rh_c;
-    void* hx;            // GRU_Q: new h (bf16) at channels [0,64) of (B,H,W,hx_c)
+    void* hx;            // GRU_Q: new h (fp16) at channels [0,64) of (B,H,W,hx_c)
     int hx_c;
     void* hin;           // GRU_Q: ... and of (B,H,W,hin_c) when not null
     int hin_c;
     const float* add;    // optional per-pixel addend, C4 fp32 (B or 1,add_c/4,H,W,4)
     int add_c;
     int add_shared;      // nonzero: one frame of addends shared by all B frames
-    const void* xin;     // optional extra K: conv += xin[.., 0:xin_c] . wx^T per pixel, bf16
+    const void* xin;     // optional extra K: conv += xin[.., 0:xin_c] . wx^T per pixel, fp16
     int xin_c;           // a multiple of 64
     int xin_stride;      // channels per pixel of xin (0: xin_c)
-    const void* wx;      // (cout_pad, xin_c) bf16
+    const void* wx;      // (cout_pad, xin_c) fp16
 };
 cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s);
 
 // The last two 1x1 layers of a prediction head in one kernel: x channels
-// [cin_off, cin_off + 128) (B,H,W,x_c) bf16 -> ReLU(. W2^T + b2) -> . W4^T + b4
-// -> planar (B,cout,H,W) fp16 / fp32, cout <= 64. w2 (128,128), w4 (64,128) bf16.
+// [cin_off, cin_off + 128) (B,H,W,x_c) fp16 -> ReLU(. W2^T + b2) -> . W4^T + b4
+// -> planar (B,cout,H,W) fp16 / fp32, cout <= 64. w2 (128,128), w4 (64,128) fp16.
 struct HeadTailLaunch {
     const void* x;
     int x_c, cin_off;

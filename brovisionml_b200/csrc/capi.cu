@@ -19,9 +19,12 @@ namespace {
 
 thread_local std::string g_last_error;
 thread_local std::vector<cudaEvent_t> g_probe;
+thread_local int g_probe_recorded = 0;
 
 cudaError_t probe(size_t k, cudaStream_t s) {
-    return k < g_probe.size() ? cudaEventRecord(g_probe[k], s) : cudaSuccess;
+    if (k >= g_probe.size()) return cudaSuccess;
+    g_probe_recorded = (int)k + 1;
+    return cudaEventRecord(g_probe[k], s);
 }
 
 int fail(int code, const std::string& msg) {
@@ -51,6 +54,10 @@ bool dims_ok(int B, int H, int W) {
 }
 bool intr_ok(double fu, double fv) { return fu != 0.0 && fv != 0.0 && fu == fu && fv == fv; }
 size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+// bvml_refine's workspace: the persistent AngMF's sync words, then two fp32
+// normal buffers and the ray.
+size_t sync_region(int B, int h, int w) { return align256(bvml::angmf_iters_sync_bytes(B, h, w)); }
 
 }  // namespace
 
@@ -122,12 +129,16 @@ int refine_entry(bool act, const void* normal0, const float* ray8, const void* c
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     size_t launch_no = 0;
+    g_probe_recorded = 0;
     if (cudaError_t e = probe(launch_no++, s); e != cudaSuccess)
         return cuda_fail(e, "refine: probe event record");
     const size_t nbytes = align256(sizeof(float) * 3 * (size_t)h * w * (size_t)B);
-    float* bufa = static_cast<float*>(workspace);
-    float* bufb = reinterpret_cast<float*>(static_cast<char*>(workspace) + nbytes);
-    float* rayw = reinterpret_cast<float*>(static_cast<char*>(workspace) + 2 * nbytes);
+    char* wsb = static_cast<char*>(workspace);
+    int* sync = reinterpret_cast<int*>(wsb);
+    const size_t s0 = sync_region(B, h, w);
+    float* bufa = reinterpret_cast<float*>(wsb + s0);
+    float* bufb = reinterpret_cast<float*>(wsb + s0 + nbytes);
+    float* rayw = reinterpret_cast<float*>(wsb + s0 + 2 * nbytes);
     const float* ray = ray8;
     if (!ray) {
         cudaError_t e = bvml::launch_build_ray(rayw, h, w, fu, cu, fv, cv, s);
@@ -140,6 +151,9 @@ int refine_entry(bool act, const void* normal0, const float* ray8, const void* c
     const float* cur = nullptr;
     if (iters == 0) {
         // only the initial RayReLU: copy to fp32 workspace then clamp in place
+        if (cudaError_t e = cudaMemsetAsync(sync, 0, sizeof(int) * bvml::kSyncHeaderWords, s);
+            e != cudaSuccess)
+            return cuda_fail(e, "refine: status reset");
         if (st == bvml::SType::F32) {
             cudaError_t e = cudaMemcpyAsync(bufa, normal0, sizeof(float) * 3 * (size_t)h * w * B,
                                             cudaMemcpyDeviceToDevice, s);
@@ -153,6 +167,43 @@ int refine_entry(bool act, const void* normal0, const float* ray8, const void* c
             return cuda_fail(e, "refine: probe event record");
         cur = bufa;
     } else {
+        // all iterations in one persistent launch where the shape allows it
+        bvml::AngmfItersLaunch J{};
+        J.pn0 = normal0;
+        J.prob = prob;
+        J.xy = xy;
+        J.angle = angle;
+        J.ray = ray;
+        J.buf[0] = bufa;
+        J.buf[1] = bufb;
+        J.sync = sync;
+        J.st = st;
+        J.act = act;
+        J.iters = iters;
+        J.B = B;
+        J.H = h;
+        J.W = w;
+        J.ps = ps;
+        J.dil = dil;
+        J.fu = fu;
+        J.cu = cu;
+        J.fv = fv;
+        J.cv = cv;
+        J.first = 0;
+        cudaError_t e = bvml::launch_angmf_iters(J, s);
+        if (e == cudaSuccess) {
+            if ((e = probe(launch_no++, s)) != cudaSuccess)
+                return cuda_fail(e, "refine: probe event record");
+            cur = (iters - 1) % 2 == 0 ? bufa : bufb;
+        } else if (e != cudaErrorNotSupported) {
+            return finish(e, "refine: angmf launch");
+        } else {
+            // one launch per iteration: no dependency waits, status word zero
+            e = cudaMemsetAsync(sync, 0, sizeof(int) * bvml::kSyncHeaderWords, s);
+            if (e != cudaSuccess) return cuda_fail(e, "refine: status reset");
+        }
+    }
+    if (iters > 0 && !cur) {
         float* dst = bufa;
         float* other = bufb;
         for (int it = 0; it < iters; ++it) {
@@ -313,7 +364,7 @@ int bvml_slice2d(const void* x, int N, int C, int H, int W, int h0, int w0, int 
                   "slice2d launch");
 }
 
-int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B, int H, int W,
+int bvml_conv2d_nhwc_f16(const void* x, const void* w, const float* bias, int B, int H, int W,
                           int cin_pad, int cout, int cout_pad, int ks, int act, void* y,
                           int* err, void* stream) {
     if (!(ks == 1 || ks == 3 || ks == 5)) return einval("conv2d: kernel size must be 1, 3 or 5");
@@ -349,7 +400,7 @@ int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B
     return finish(bvml::launch_conv_tc(L, static_cast<cudaStream_t>(stream)), "conv2d launch");
 }
 
-int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, const void* w,
+int bvml_conv2d_nhwc_f16_ex(const void* x, int x_c, int cin_off, int cin_pad, const void* w,
                              const float* bias, int B, int H, int W, int cout, int cout_pad,
                              int ks, const bvml_conv_epilogue* epi, int* err, void* stream) {
     auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
@@ -413,10 +464,10 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
                 epi->out_off + cout_pad > epi->out_c)
                 return einval("conv2d: bad NHWC output");
             break;
-        case BVML_EPI_SPLIT_BF16:
+        case BVML_EPI_SPLIT_F16:
             if (cout % 32 || !epi->out || !a16(epi->out) || epi->out_c % 8 ||
                 epi->out_off % 8 || epi->out_off + 2 * cout_pad > epi->out_c)
-                return einval("conv2d: split bf16 output needs cout a multiple of 32 and "
+                return einval("conv2d: split fp16 output needs cout a multiple of 32 and "
                               "out_c >= out_off + 2 cout_pad");
             break;
         case BVML_EPI_C4_F32:
@@ -492,8 +543,26 @@ int bvml_stage_inputs(const float* h0, const float* feat, int B, int H, int W, f
 size_t bvml_refine_workspace_bytes(int B, int h, int w) {
     if (B < 0 || h < 0 || w < 0) return 0;
     const size_t plane = (size_t)h * (size_t)w;
-    return 2 * align256(sizeof(float) * 3 * plane * (size_t)B) + align256(sizeof(float) * 3 * plane);
+    return sync_region(B, h, w) + 2 * align256(sizeof(float) * 3 * plane * (size_t)B) +
+           align256(sizeof(float) * 3 * plane);
 }
+
+int bvml_refine_status(const void* workspace, void* stream) {
+    if (!workspace) return einval("refine_status: null workspace");
+    int st = 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(&st, static_cast<const int*>(workspace) + 1, sizeof(int),
+                                    cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "refine_status: copy");
+    if (st != 0)
+        return fail(BVML_ECUDA, "dsine cuda: refine: a persistent AngMF dependency wait gave up "
+                                "(status " + std::to_string(st) + "); results unspecified");
+    g_last_error.clear();
+    return BVML_OK;
+}
+
+int bvml_probe_recorded(void) { return g_probe_recorded; }
 
 int bvml_refine(const void* normal0, const float* ray8, const void* const* prob,
                 const void* const* xy, const void* const* angle, int iters, const void* mask,

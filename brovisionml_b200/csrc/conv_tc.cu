@@ -4,8 +4,8 @@
 // reference runs as brotensor conv2d_forward calls followed by separate
 // activation, concat and elementwise passes.
 //
-// Layout: inputs NHWC bf16 with the channel count padded to a multiple of 64
-// (pad channels zero), weights [tap][C_out_pad][C_in_pad] bf16 (K-major
+// Layout: inputs NHWC fp16 with the channel count padded to a multiple of 64
+// (pad channels zero), weights [tap][C_out_pad][C_in_pad] fp16 (K-major
 // rows), fp32 bias, fp32 accumulation in tensor memory.
 //
 // GEMM view: M = pixels, N = output channels, K = taps x input channels. A
@@ -26,7 +26,7 @@
 //    stores; the GRU tensors in coalesced channel-group layouts).
 // All waits are bounded (tc_common.cuh); a wait that gives up sets *err and
 // the CTA tears down after its copies and MMAs in flight have completed.
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <mutex>
 
@@ -57,12 +57,12 @@ struct ConvArgs {
     void* out;
     int out_c, out_off;
     float* h32;
-    __nv_bfloat16* z;
-    __nv_bfloat16* rh;
+    __half* z;
+    __half* rh;
     int rh_c;
-    __nv_bfloat16* hx;
+    __half* hx;
     int hx_c;
-    __nv_bfloat16* hin;
+    __half* hin;
     int hin_c;
     int obox;     // NHWC outputs: channels per TMA store (64: two chunks, 128-byte rows)
     int xchunks;  // extra K: 64-channel chunks of a 1x1 term xin . wx^T (0: none)
@@ -85,9 +85,9 @@ __device__ __forceinline__ float activate(float v) {
     else return v;
 }
 
-// Channel-group layouts of the fp32 / bf16 per-pixel tensors the epilogues
+// Channel-group layouts of the fp32 / fp16 per-pixel tensors the epilogues
 // read and write (the addend, the GRU state h32 and gate z): C4 fp32 is
-// [frame][C / 4][H][W][4], C8 bf16 is [frame][C / 8][H][W][8]. A thread owns
+// [frame][C / 4][H][W][4], C8 fp16 is [frame][C / 8][H][W][8]. A thread owns
 // one pixel and moves 16 bytes per access; the lanes of a warp hold
 // consecutive pixels, so every access is one coalesced 512-byte segment.
 __device__ __forceinline__ long c4_index(const ConvArgs& a, long frame_groups, int b, int g,
@@ -166,19 +166,19 @@ __device__ __forceinline__ void pre_activation(const ConvArgs& a, const float* s
 // Epilogue of one thread's pixel p of frame b for 32 consecutive output
 // channels cb .. cb+31 (accumulators in v, plus bias and the addend t).
 // Modes (ConvEpi in bvml_internal.h):
-//  (NHWC: act(v) as bf16 at out[pix * out_c + out_off + c], zeros past cout,
+//  (NHWC: act(v) as fp16 at out[pix * out_c + out_off + c], zeros past cout,
 //  through shared memory and TMA stores: nhwc_chunk_tma, nhwc_pair_tma)
 //  C4_32     act(v) as fp32 in C4 layout, out_c channels per frame, at
 //            channel out_off + c;
-//  (SPLIT16: v as two bf16 halves (hi, lo = v - hi), per 64-channel block
+//  (SPLIT16: v as two fp16 halves (hi, lo = v - hi), per 64-channel block
 //  hi then lo, at NHWC channels out_off + 128 (c / 64) + c % 64 and 64
 //  further, through shared memory and TMA stores; an operand for the extra K
 //  of another convolution that keeps about 16 mantissa bits)
 //  (PLANAR16/32: planar_chunk_tma, through a shared-memory transpose)
-//  GRU_ZR    c < 64: z = sigmoid(v) -> z (C8 bf16, 64 channels);
+//  GRU_ZR    c < 64: z = sigmoid(v) -> z (C8 fp16, 64 channels);
 //            64 <= c < 128: r = sigmoid(v) -> rh[pix * rh_c + c - 64] = r * h,
 //            h from h32 (C4 fp32, 64 channels);
-//  GRU_Q     c < 64: q = tanh(v), h = (1 - z) h + z q -> h32 and bf16 copies
+//  GRU_Q     c < 64: q = tanh(v), h = (1 - z) h + z q -> h32 and fp16 copies
 //            at hx[pix * hx_c + c] and, if set, hin[pix * hin_c + c]
 //  (src/dsine_refine.cpp:140-158).
 template <int EPI, int ACT>
@@ -212,10 +212,10 @@ __device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias
             dst[q * hw] = o;
         }
     } else if constexpr (EPI == (int)ConvEpi::GRU_ZR) {
-        alignas(16) __nv_bfloat16 o[32];
+        alignas(16) __half o[32];
         if (cb < 64) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float2bfloat16_rn(activate<2>(f[i]));
+            for (int i = 0; i < 32; ++i) o[i] = __float2half_rn(activate<2>(f[i]));
             uint4* dst = reinterpret_cast<uint4*>(a.z) + c4_index(a, 8, b, cb / 8, p);
 #pragma unroll
             for (int q = 0; q < 4; ++q) dst[q * hw] = reinterpret_cast<const uint4*>(o)[q];
@@ -223,10 +223,10 @@ __device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
                 const float4 h = make_float4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
-                o[4 * q + 0] = __float2bfloat16_rn(activate<2>(f[4 * q + 0]) * h.x);
-                o[4 * q + 1] = __float2bfloat16_rn(activate<2>(f[4 * q + 1]) * h.y);
-                o[4 * q + 2] = __float2bfloat16_rn(activate<2>(f[4 * q + 2]) * h.z);
-                o[4 * q + 3] = __float2bfloat16_rn(activate<2>(f[4 * q + 3]) * h.w);
+                o[4 * q + 0] = __float2half_rn(activate<2>(f[4 * q + 0]) * h.x);
+                o[4 * q + 1] = __float2half_rn(activate<2>(f[4 * q + 1]) * h.y);
+                o[4 * q + 2] = __float2half_rn(activate<2>(f[4 * q + 2]) * h.z);
+                o[4 * q + 3] = __float2half_rn(activate<2>(f[4 * q + 3]) * h.w);
             }
             uint4* dst = reinterpret_cast<uint4*>(a.rh + pix * a.rh_c + (cb - 64));
 #pragma unroll
@@ -236,10 +236,10 @@ __device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias
         if (cb >= 64) return;
         float4* h4 = reinterpret_cast<float4*>(a.h32) + c4_index(a, 16, b, cb / 4, p);
         const uint4* z4 = reinterpret_cast<const uint4*>(a.z) + c4_index(a, 8, b, cb / 8, p);
-        alignas(16) __nv_bfloat16 zb[32];
+        alignas(16) __half zb[32];
 #pragma unroll
         for (int q = 0; q < 4; ++q) reinterpret_cast<uint4*>(zb)[q] = z4[q * hw];
-        alignas(16) __nv_bfloat16 o[32];
+        alignas(16) __half o[32];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
             float4 h = make_float4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
@@ -247,9 +247,9 @@ __device__ __forceinline__ void epilogue32(const ConvArgs& a, const float* sbias
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int i = 4 * q + e;
-                const float z = __bfloat162float(zb[i]);
+                const float z = __half2float(zb[i]);
                 hh[e] = fmaf(z, tanhf(f[i]) - hh[e], hh[e]);  // (1 - z) h + z q
-                o[i] = __float2bfloat16_rn(hh[e]);
+                o[i] = __float2half_rn(hh[e]);
             }
             h4[q * hw] = h;
         }
@@ -338,16 +338,16 @@ __device__ __forceinline__ void planar_chunk_tma(const ConvArgs& a, const CUtens
     }
 }
 
-// NHWC bf16 output of one 32-channel chunk of one epilogue warp's 32 pixels
+// NHWC fp16 output of one 32-channel chunk of one epilogue warp's 32 pixels
 // through shared memory: lane r writes its pixel's 64 bytes as row r of the
 // warp's staging buffer ([pixel][channel], the TMA box layout) in the
 // 64-byte swizzle (16-byte unit u of row r at u ^ ((r >> 1) & 3), which
 // spreads a warp's rows over all banks), and lane 0 stores the box (32
 // channels at c0 x pw x ph pixels) with one TMA store, clipped at the frame
 // edges. The buffer is reused two chunks later, after the store has read it.
-__device__ __forceinline__ void stage_bf16_box(const CUtensorMap* map_o, uint8_t* stg,
+__device__ __forceinline__ void stage_f16_box(const CUtensorMap* map_o, uint8_t* stg,
                                                uint32_t stg_addr, int lane, int c0, int px0,
-                                               int py0, int b, const __nv_bfloat16 (&o)[32]) {
+                                               int py0, int b, const __half (&o)[32]) {
     if (lane == 0) tc::bulk_wait_read<1>();  // this buffer's previous store has read it
     __syncwarp();
     const int sw = (lane >> 1) & 3;
@@ -371,14 +371,14 @@ __device__ __forceinline__ void nhwc_chunk_tma(const ConvArgs& a, const CUtensor
                                                const uint32_t (&v)[32]) {
     float f[32];
     pre_activation(a, sbias, t, cb, v, f);
-    alignas(16) __nv_bfloat16 o[32];
+    alignas(16) __half o[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i)
-        o[i] = __float2bfloat16_rn(cb + i < a.cout ? activate<ACT>(f[i]) : 0.0f);
-    stage_bf16_box(map_o, stg, stg_addr, lane, c0, px0, py0, b, o);
+        o[i] = __float2half_rn(cb + i < a.cout ? activate<ACT>(f[i]) : 0.0f);
+    stage_f16_box(map_o, stg, stg_addr, lane, c0, px0, py0, b, o);
 }
 
-// NHWC bf16 output of two consecutive 32-channel chunks (half 0: channels
+// NHWC fp16 output of two consecutive 32-channel chunks (half 0: channels
 // cb .. cb+31, half 1: the next 32) of one epilogue warp's 32 pixels, stored
 // as one box of 64 channels: 128-byte rows, half as many as 32-channel boxes
 // (the TMA store engine's cost is per row). Lane r writes its half row into
@@ -394,10 +394,10 @@ __device__ __forceinline__ void nhwc_pair_tma(const ConvArgs& a, const CUtensorM
                                               const uint32_t (&v)[32]) {
     float f[32];
     pre_activation(a, sbias, t, cb, v, f);
-    alignas(16) __nv_bfloat16 o[32];
+    alignas(16) __half o[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i)
-        o[i] = __float2bfloat16_rn(cb + i < a.cout ? activate<ACT>(f[i]) : 0.0f);
+        o[i] = __float2half_rn(cb + i < a.cout ? activate<ACT>(f[i]) : 0.0f);
     if (half == 0) {
         if (lane == 0) tc::bulk_wait_read<1>();  // this buffer's previous store has read it
         __syncwarp();
@@ -596,7 +596,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         if (BRES && !tc::mbar_wait(bar_bres, 0, kWaitLimit)) fail(2);
     } else if (warp == 1 && lane == 0) {
         // --------------------------------------------------------------- MMA
-        constexpr uint32_t idesc = tc::idesc_bf16_f32(kTM, N);
+        constexpr uint32_t idesc = tc::idesc_f16_f32(kTM, N);
         const uint32_t row_bytes = (uint32_t)a.tw * 128;  // one image row of an A entry
         int ga = 0, gb = 0, tl = 0;
         bool ok = true;
@@ -644,7 +644,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                                 tc::umma_desc_k_sw128(sa + (uint32_t)(m * a.th + ky) * row_bytes);
 #pragma unroll
                             for (int k = 0; k < kKC / 16; ++k)  // K = 16 per MMA: 2 descriptor units
-                                tc::umma_bf16(acc + m * N, da + 2 * k, db + 2 * k, idesc,
+                                tc::umma_f16(acc + m * N, da + 2 * k, db + 2 * k, idesc,
                                               !first || k > 0);
                         }
                         first = false;
@@ -681,7 +681,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                             tc::umma_desc_k_sw128(sa + (uint32_t)(m * a.th) * row_bytes);
 #pragma unroll
                         for (int k = 0; k < kKC / 16; ++k)
-                            tc::umma_bf16(acc + m * N, da + 2 * k, db + 2 * k, idesc,
+                            tc::umma_f16(acc + m * N, da + 2 * k, db + 2 * k, idesc,
                                           !first || k > 0);
                     }
                     first = false;
@@ -750,17 +750,17 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     if (cb >= a.cout) return;  // cout is a multiple of 32
                     float f[32];
                     pre_activation(a, sbias, tt, cb, v, f);
-                    alignas(16) __nv_bfloat16 hi[32], lo[32];
+                    alignas(16) __half hi[32], lo[32];
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        hi[i] = __float2bfloat16_rn(f[i]);
-                        lo[i] = __float2bfloat16_rn(f[i] - __bfloat162float(hi[i]));
+                        hi[i] = __float2half_rn(f[i]);
+                        lo[i] = __float2half_rn(f[i] - __half2float(hi[i]));
                     }
                     const int cx = a.out_off + (cb / 64) * 128 + cb % 64;
 #pragma unroll
                     for (int part = 0; part < 2; ++part) {
                         const int slot = (warp - 2) * 2 + (pcount & 1);
-                        stage_bf16_box(&map_o, smem + a.off_out + slot * stage_warp_bytes(EPI),
+                        stage_f16_box(&map_o, smem + a.off_out + slot * stage_warp_bytes(EPI),
                                        sbase + a.off_out + slot * stage_warp_bytes(EPI), lane,
                                        cx + 64 * part, px0, py0, b, part ? lo : hi);
                         ++pcount;
@@ -831,7 +831,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 // ------------------------------------------------------------ head tail
 // The last two layers of a prediction head in one kernel (src/dsine_refine.cpp:
 // 118-125: conv1x1 128 -> 128, ReLU, conv1x1 128 -> C with C <= 64): GEMM1 of
-// a 128-pixel tile into TMEM, bias + ReLU + bf16 written by the epilogue warps
+// a 128-pixel tile into TMEM, bias + ReLU + fp16 written by the epilogue warps
 // straight into shared memory in the 128-byte-swizzled K-major layout the MMA
 // reads (row r = pixel, 16-byte unit u at u ^ (r & 7)), GEMM2 from there, and
 // the planar epilogue -- the 128-channel intermediate never reaches global
@@ -945,8 +945,8 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         if (!tc::mbar_wait(bar_wres, 0, kWaitLimit)) fail(2);
     } else if (warp == 1 && lane == 0) {
         // --------------------------------------------------------------- MMA
-        constexpr uint32_t idesc1 = tc::idesc_bf16_f32(kTM, 128);
-        constexpr uint32_t idesc2 = tc::idesc_bf16_f32(kTM, 64);
+        constexpr uint32_t idesc1 = tc::idesc_f16_f32(kTM, 128);
+        constexpr uint32_t idesc2 = tc::idesc_f16_f32(kTM, 64);
         bool ok = tc::mbar_wait(bar_wres, 0, kWaitLimit);
         if (!ok) fail(7);
         // GEMM2 of tile j: intermediate j & 1 (2 chunks) x W4^T into acc2 j & 1
@@ -965,7 +965,7 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                 const uint64_t db = tc::umma_desc_k_sw128(sbase + kHTW4 + ch * 8192);
 #pragma unroll
                 for (int k = 0; k < kKC / 16; ++k)
-                    tc::umma_bf16(acc2, da + 2 * k, db + 2 * k, idesc2, ch > 0 || k > 0);
+                    tc::umma_f16(acc2, da + 2 * k, db + 2 * k, idesc2, ch > 0 || k > 0);
             }
             tc::umma_commit(bar_acc2_full + 8 * q);
             return true;
@@ -991,7 +991,7 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                 const uint64_t db = tc::umma_desc_k_sw128(sbase + kHTW2 + ch * 16384);
 #pragma unroll
                 for (int k = 0; k < kKC / 16; ++k)
-                    tc::umma_bf16(acc1, da + 2 * k, db + 2 * k, idesc1, ch > 0 || k > 0);
+                    tc::umma_f16(acc1, da + 2 * k, db + 2 * k, idesc1, ch > 0 || k > 0);
                 tc::umma_commit(bar_empty_a + 8 * s);
             }
             if (!ok) {
@@ -1061,7 +1061,7 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             tc::tc_fence_after();
             int b, x0, y0;
             tile_of(t, b, x0, y0);
-            // E1: GEMM1 columns [64 grp, 64 grp + 64) + bias, ReLU, bf16 ->
+            // E1: GEMM1 columns [64 grp, 64 grp + 64) + bias, ReLU, fp16 ->
             // intermediate buf, chunk grp, row `row` (its previous reader, GEMM2
             // of tile tl - 2, completed before this warp's E2 of that tile)
             uint8_t* a2row = smem + kHTA2 + buf * 32768 + grp * 16384 + row * 128;
@@ -1071,10 +1071,10 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                 tc::tmem_ld_32cols(tmem + buf * 128 + grp * 64 + c * 32 + ((uint32_t)(wq * 32) << 16),
                                    v);
                 tc::tmem_ld_wait();
-                alignas(16) __nv_bfloat16 o[32];
+                alignas(16) __half o[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i)
-                    o[i] = __float2bfloat16_rn(
+                    o[i] = __float2half_rn(
                         fmaxf(__uint_as_float(v[i]) + sbias1[grp * 64 + c * 32 + i], 0.0f));
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
@@ -1124,7 +1124,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 bool encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
             const cuuint64_t* strides_bytes, const cuuint32_t* box,
-            CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+            CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
             CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B) {
     auto fn = encode_fn();
     if (!fn) return false;
@@ -1255,12 +1255,12 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     a.out_c = L.out_c;
     a.out_off = L.out_off;
     a.h32 = L.h32;
-    a.z = static_cast<__nv_bfloat16*>(L.z);
-    a.rh = static_cast<__nv_bfloat16*>(L.rh);
+    a.z = static_cast<__half*>(L.z);
+    a.rh = static_cast<__half*>(L.rh);
     a.rh_c = L.rh_c;
-    a.hx = static_cast<__nv_bfloat16*>(L.hx);
+    a.hx = static_cast<__half*>(L.hx);
     a.hx_c = L.hx_c;
-    a.hin = static_cast<__nv_bfloat16*>(L.hin);
+    a.hin = static_cast<__half*>(L.hin);
     a.hin_c = L.hin_c;
     a.add = L.add;
     a.add_fs = L.add_shared ? 0 : (long)L.H * L.W * L.add_c;
@@ -1329,7 +1329,7 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
                     CU_TENSOR_MAP_SWIZZLE_NONE))
             return cudaErrorInvalidValue;
     } else if (L.epi == ConvEpi::NHWC || L.epi == ConvEpi::SPLIT16) {
-        // NHWC bf16: a 4-D map (out_c, W, H, B); each epilogue warp stores
+        // NHWC fp16: a 4-D map (out_c, W, H, B); each epilogue warp stores
         // obox channels x pw x ph pixels, 64- or 128-byte swizzled in shared
         // memory. 64-channel boxes (two 4 KB buffers per warp) for the 1x1
         // layers, whose shared memory has room; they need every warp's
@@ -1341,11 +1341,11 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
         const cuuint64_t str_o[3] = {(cuuint64_t)L.out_c * 2, (cuuint64_t)L.W * L.out_c * 2,
                                      (cuuint64_t)L.H * L.W * L.out_c * 2};
         const cuuint32_t box_o[4] = {(cuuint32_t)a.obox, (cuuint32_t)pw, (cuuint32_t)(32 / pw), 1};
-        if (!encode(&mo, L.y, 4, dims_o, str_o, box_o, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+        if (!encode(&mo, L.y, 4, dims_o, str_o, box_o, CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                     a.obox == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
             return cudaErrorInvalidValue;
     }
-    // extra K: xin (B,H,W,xin_c) bf16 NHWC as boxes of the tile's pixels (no
+    // extra K: xin (B,H,W,xin_c) fp16 NHWC as boxes of the tile's pixels (no
     // halo), wx (xin_c-long rows for each of cout_pad outputs) as N x 64 boxes
     CUtensorMap mx = ma, mbx = mb;  // unused without an extra K block
     if (L.xin) {

@@ -6,10 +6,10 @@
 //    l2_normalize_nchw_forward / slice2d_forward calls of
 //    src/dsine_refine.cpp:280-292), for callers that drive the ops one by one;
 //  * the refine stage's input layouts: the decoder's hidden state and feature
-//    (planar fp32) into the GRU state (C4 fp32) and the convolutions' NHWC bf16
+//    (planar fp32) into the GRU state (C4 fp32) and the convolutions' NHWC fp16
 //    inputs, one pass (the concat of src/dsine_refine.cpp:245-248).
 // All are HBM-bound streams with grid-stride loops sized to the SM count.
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "bvml_common.cuh"
 #include "bvml_internal.h"
@@ -112,13 +112,13 @@ slice_kernel(const T* __restrict__ x, T* __restrict__ y, int NC, int H, int W, i
 }
 
 // One thread per pixel of 64-channel planar fp32 inputs: h0 -> h32 (C4 fp32,
-// [b][16][HW][4]) and hx (NHWC bf16), feat -> fx (NHWC bf16). The planar reads
+// [b][16][HW][4]) and hx (NHWC fp16), feat -> fx (NHWC fp16). The planar reads
 // are coalesced across the warp's consecutive pixels; each thread writes its
 // pixel's 128-byte NHWC rows whole.
 __global__ void __launch_bounds__(kThreads)
 stage_inputs_kernel(const float* __restrict__ h0, const float* __restrict__ feat, int B, long HW,
-                    float* __restrict__ h32, __nv_bfloat16* __restrict__ hx,
-                    __nv_bfloat16* __restrict__ fx) {
+                    float* __restrict__ h32, __half* __restrict__ hx,
+                    __half* __restrict__ fx) {
     const long total = (long)B * HW;
     for (long i = (long)blockIdx.x * kThreads + threadIdx.x; i < total;
          i += (long)gridDim.x * kThreads) {
@@ -131,14 +131,14 @@ stage_inputs_kernel(const float* __restrict__ h0, const float* __restrict__ feat
             float4* c4 = reinterpret_cast<float4*>(h32) + (b * 16 + 2 * g) * HW + p;
             c4[0] = make_float4(v[0], v[1], v[2], v[3]);
             c4[HW] = make_float4(v[4], v[5], v[6], v[7]);
-            alignas(16) __nv_bfloat16 o[8];
+            alignas(16) __half o[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) o[j] = __float2bfloat16_rn(v[j]);
+            for (int j = 0; j < 8; ++j) o[j] = __float2half_rn(v[j]);
             reinterpret_cast<uint4*>(hx)[i * 8 + g] = *reinterpret_cast<const uint4*>(o);
             if (feat) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
-                    o[j] = __float2bfloat16_rn(__ldg(feat + (b * 64 + g * 8 + j) * HW + p));
+                    o[j] = __float2half_rn(__ldg(feat + (b * 64 + g * 8 + j) * HW + p));
                 reinterpret_cast<uint4*>(fx)[i * 8 + g] = *reinterpret_cast<const uint4*>(o);
             }
         }
@@ -152,7 +152,7 @@ cudaError_t launch_stage_inputs(const float* h0, const float* feat, int B, int H
     const long HW = (long)H * W;
     if (B == 0 || HW == 0) return cudaSuccess;
     stage_inputs_kernel<<<grid_for((long)B * HW), kThreads, 0, s>>>(
-        h0, feat, B, HW, h32, static_cast<__nv_bfloat16*>(hx), static_cast<__nv_bfloat16*>(fx));
+        h0, feat, B, HW, h32, static_cast<__half*>(hx), static_cast<__half*>(fx));
     return cudaGetLastError();
 }
 

@@ -16,7 +16,7 @@
 //    groups) in [32,46), version 1 in [46,48), base offset 0 in [49,52),
 //    layout type 2 (SWIZZLE_128B) in [61,64);
 //  * instruction descriptor, kind::f16: D format F32 (1) in [4,6), A and B
-//    format BF16 (1) in [7,10) and [10,13), both K-major (bits 15, 16 = 0),
+//    format F16 (0) in [7,10) and [10,13), both K-major (bits 15, 16 = 0),
 //    N >> 3 in [17,23), M >> 4 in [24,29).
 #pragma once
 
@@ -121,9 +121,8 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_addr) {
     d |= (uint64_t)2 << 61;                    // SWIZZLE_128B
     return d;
 }
-__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
-           ((uint32_t)(M >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // ---------------------------------------------------------------- tcgen05
@@ -145,8 +144,8 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-// D[tmem] (+)= A[smem] * B[smem]^T, one instruction (K = 16 for bf16)
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc,
+// D[tmem] (+)= A[smem] * B[smem]^T, one instruction (K = 16 for fp16)
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc,
                                           uint32_t idesc, bool accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"

@@ -205,39 +205,39 @@ def pad64(c: int) -> int:
 
 def pack_conv_weight(weight: torch.Tensor, cin_pad: int | None = None,
                      cout_pad: int | None = None) -> torch.Tensor:
-    """(C_out, C_in, k, k) conv weights -> the (k*k, C_out_pad, C_in_pad) bf16
+    """(C_out, C_in, k, k) conv weights -> the (k*k, C_out_pad, C_in_pad) fp16
     K-major layout conv2d_nhwc takes (zero padded)."""
     cout, cin, k, _ = weight.shape
     cin_pad = cin_pad or pad64(cin)
     cout_pad = cout_pad or pad64(cout)
-    w = torch.zeros((k * k, cout_pad, cin_pad), device=weight.device, dtype=torch.bfloat16)
-    w[:, :cout, :cin] = weight.permute(2, 3, 0, 1).reshape(k * k, cout, cin).to(torch.bfloat16)
+    w = torch.zeros((k * k, cout_pad, cin_pad), device=weight.device, dtype=torch.float16)
+    w[:, :cout, :cin] = weight.permute(2, 3, 0, 1).reshape(k * k, cout, cin).to(torch.float16)
     return w
 
 
 def conv2d_nhwc(x: torch.Tensor, w_packed: torch.Tensor, bias: torch.Tensor, cout: int, *,
                 ks: int, act: str = "none", out: torch.Tensor | None = None,
                 err: torch.Tensor | None = None) -> torch.Tensor:
-    """Stride-1 "same" conv on the tensor cores: x (B,H,W,cin_pad) bf16,
+    """Stride-1 "same" conv on the tensor cores: x (B,H,W,cin_pad) fp16,
     w_packed from pack_conv_weight, bias (cout) fp32; returns
-    (B,H,W,cout_pad) bf16 (pad channels zero). Raises if the kernel's pipeline
+    (B,H,W,cout_pad) fp16 (pad channels zero). Raises if the kernel's pipeline
     reported a failure (checked when ``err`` is None: one device sync)."""
     dev = _cuda("conv2d", x, w_packed, bias)
     B, H, W, cin_pad = x.shape
     cout_pad = w_packed.shape[1]
-    if x.dtype != torch.bfloat16 or w_packed.dtype != torch.bfloat16:
-        raise RuntimeError("dsine ops: conv2d: x and weights must be bf16")
+    if x.dtype != torch.float16 or w_packed.dtype != torch.float16:
+        raise RuntimeError("dsine ops: conv2d: x and weights must be fp16")
     if bias.dtype != torch.float32 or bias.numel() < cout:
         raise RuntimeError("dsine ops: conv2d: bias must be fp32 with cout entries")
     if w_packed.shape != (ks * ks, cout_pad, cin_pad):
         raise RuntimeError("dsine ops: conv2d: packed weights do not match x / ks")
     if out is None:
-        out = torch.empty((B, H, W, cout_pad), device=dev, dtype=torch.bfloat16)
+        out = torch.empty((B, H, W, cout_pad), device=dev, dtype=torch.float16)
     own_err = err is None
     if own_err:
         err = torch.zeros(1, device=dev, dtype=torch.int32)
     with torch.cuda.device(dev):
-        check(lib.bvml_conv2d_nhwc_bf16(_p(x.contiguous()), _p(w_packed), _p(bias), B, H, W,
+        check(lib.bvml_conv2d_nhwc_f16(_p(x.contiguous()), _p(w_packed), _p(bias), B, H, W,
                                         cin_pad, cout, cout_pad, ks, ACTIVATIONS[act], _p(out),
                                         _p(err), _stream(dev)))
     if own_err and int(err.item()) != 0:

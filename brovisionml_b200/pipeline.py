@@ -155,10 +155,45 @@ class HostFrame:
     ray8: torch.Tensor | None = None
 
 
+class BandFailure(RuntimeError):
+    """One or more bands of refine_frame_banded failed; ``failures`` lists
+    (band index, device, BandJob, exception) for each."""
+
+    def __init__(self, failures):
+        self.failures = failures
+        parts = [f"band {k} (grid rows {j.own0}..{j.own1 - 1}) on cuda:{d}: "
+                 f"{type(e).__name__}: {e}" for k, d, j, e in failures]
+        super().__init__("dsine ops: refine_frame_banded: " + "; ".join(parts))
+
+
+def _refine_band(frame: "HostFrame", out_host: torch.Tensor, d: int, j: BandJob, fu: float,
+                 cu: float, fv: float, cv: float, w: int, ps: int, dil: int,
+                 full_res_ray_relu: bool, logits: bool) -> None:
+    """Upload one band's inputs to device d, refine it (cropped to its owned
+    rows by the unit itself) and copy the owned rows into out_host."""
+    from .sharding import Band, band_intrinsics
+
+    dev = torch.device("cuda", d)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.Stream(dev)
+        with torch.cuda.stream(stream):
+            rows = lambda t: t[:, j.comp0:j.comp1]  # noqa: E731
+            up = lambda t: rows(t).contiguous().pin_memory().to(dev, non_blocking=True)  # noqa
+            res = refine(up(frame.normal0)[None], [up(t)[None] for t in frame.prob],
+                         [up(t)[None] for t in frame.xy], [up(t)[None] for t in frame.angle],
+                         up(frame.mask)[None], fu, cu, fv,
+                         band_intrinsics(cv, Band(j.own0, j.own1, j.comp0, j.comp1)),
+                         ray8=up(frame.ray8) if frame.ray8 is not None else None, ps=ps,
+                         dil=dil, full_res_ray_relu=full_res_ray_relu,
+                         crop=(j.crop_t, 0, j.out_h, 8 * w), logits=logits)
+            out_host[:, 8 * j.own0:8 * j.own1].copy_(res[0])
+        stream.synchronize()
+
+
 def refine_frame_banded(frame: HostFrame, out_host: torch.Tensor, fu: float, cu: float,
                         fv: float, cv: float, *, n_bands: int, devices: Sequence[int] = (0,),
                         ps: int = 5, dil: int = 1, full_res_ray_relu: bool = False,
-                        logits: bool = False) -> None:
+                        logits: bool = False, timeout: float | None = None) -> None:
     """Refine one frame too large for one call (or for one GPU's memory) as
     exact-halo row bands: band k runs on devices[k % len(devices)] (one host
     thread per device, bands of a device in order), and each band's owned
@@ -166,47 +201,57 @@ def refine_frame_banded(frame: HostFrame, out_host: torch.Tensor, fu: float, cu:
     into ``out_host`` (3, 8h, 8w) -- the 3-channel crop-stitch. The halo
     (sharding.halo_rows) makes the result equal the whole-frame refine up to
     the fp32 rounding of the band-shifted principal point; the reference
-    instead caps the resolution of a large frame (src/dsine.cpp:117-141)."""
-    import threading
+    instead caps the resolution of a large frame (src/dsine.cpp:117-141).
 
-    from .sharding import Band, band_intrinsics
+    Failures: a band that raises stops its device's remaining bands and,
+    through a shared flag, every other device's bands that have not started;
+    all threads are joined and one BandFailure names every failed band with
+    its grid rows, device and exception. ``timeout`` (seconds) bounds the
+    whole call: threads still running then are reported in a TimeoutError
+    naming their devices and the bands not finished (the threads are daemon
+    threads, so a stuck device cannot keep the process alive)."""
+    import threading
+    import time
 
     iters = len(frame.prob)
     _, h, w = frame.normal0.shape
     jobs = plan_band_jobs(h, n_bands, iters, ps, dil)
-    per_dev = {d: [j for k, j in enumerate(jobs) if devices[k % len(devices)] == d]
+    per_dev = {d: [(k, j) for k, j in enumerate(jobs) if devices[k % len(devices)] == d]
                for d in dict.fromkeys(devices)}
-    errors = []
+    failures = []
+    finished = set()
+    lock = threading.Lock()
+    cancel = threading.Event()
 
-    def rows(t: torch.Tensor, j: BandJob) -> torch.Tensor:
-        return t[:, j.comp0:j.comp1]
+    def work(d: int, my_jobs) -> None:
+        for k, j in my_jobs:
+            if cancel.is_set():
+                return
+            try:
+                _refine_band(frame, out_host, d, j, fu, cu, fv, cv, w, ps, dil,
+                             full_res_ray_relu, logits)
+            except BaseException as e:  # surfaced on the calling thread
+                with lock:
+                    failures.append((k, d, j, e))
+                cancel.set()
+                return
+            with lock:
+                finished.add(k)
 
-    def work(d: int, my_jobs: list[BandJob]) -> None:
-        try:
-            dev = torch.device("cuda", d)
-            with torch.cuda.device(dev):
-                stream = torch.cuda.Stream(dev)
-                with torch.cuda.stream(stream):
-                    for j in my_jobs:
-                        up = lambda t: rows(t, j).contiguous().pin_memory().to(  # noqa: E731
-                            dev, non_blocking=True)
-                        res = refine(up(frame.normal0)[None], [up(t)[None] for t in frame.prob],
-                                     [up(t)[None] for t in frame.xy],
-                                     [up(t)[None] for t in frame.angle], up(frame.mask)[None],
-                                     fu, cu, fv,
-                                     band_intrinsics(cv, Band(j.own0, j.own1, j.comp0, j.comp1)),
-                                     ray8=up(frame.ray8) if frame.ray8 is not None else None,
-                                     ps=ps, dil=dil, full_res_ray_relu=full_res_ray_relu,
-                                     crop=(j.crop_t, 0, j.out_h, 8 * w), logits=logits)
-                        out_host[:, 8 * j.own0:8 * j.own1].copy_(res[0])
-                stream.synchronize()
-        except BaseException as e:  # surfaced on the calling thread
-            errors.append(e)
-
-    threads = [threading.Thread(target=work, args=(d, js)) for d, js in per_dev.items() if js]
-    for t in threads:
+    threads = {d: threading.Thread(target=work, args=(d, js), daemon=True)
+               for d, js in per_dev.items() if js}
+    for t in threads.values():
         t.start()
-    for t in threads:
-        t.join()
-    if errors:
-        raise errors[0]
+    deadline = None if timeout is None else time.monotonic() + timeout
+    for t in threads.values():
+        t.join(None if deadline is None else max(0.0, deadline - time.monotonic()))
+    stuck = [d for d, t in threads.items() if t.is_alive()]
+    if stuck:
+        cancel.set()
+        with lock:
+            pending = [k for k, _ in enumerate(jobs) if k not in finished and
+                       not any(f[0] == k for f in failures)]
+        raise TimeoutError(f"dsine ops: refine_frame_banded: devices {stuck} still busy after "
+                           f"{timeout} s; bands not finished: {pending}")
+    if failures:
+        raise BandFailure(sorted(failures, key=lambda f: f[0]))

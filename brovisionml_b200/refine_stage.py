@@ -9,9 +9,9 @@ channels) and uv (2) are the same in every iteration, and uv is the same for
 every frame. So ``start`` convolves them once --
 
   gxu = conv5x5(uv, W_zr||q[:, 128:130])          (1,192/4,h,w,4) fp32 (C4), shared
-  gx  = conv5x5(feat, W_zr||q[:, 64:128]) + gxu    per frame, stored as bf16
-        halves hi = bf16(gx), lo = bf16(gx - hi), each 64-channel block (z, r,
-        q) as hi then lo: (B,h,w,384), about 16 mantissa bits
+  gx  = conv5x5(feat, W_zr||q[:, 64:128]) + gxu    per frame, stored as fp16
+        halves hi = fp16(gx), lo = fp16(gx - hi), each 64-channel block (z, r,
+        q) as hi then lo: (B,h,w,384), about 22 mantissa bits
   gu  = conv3x3(uv, W_heads3x3[:, 64:66])          (1,512/4,h,w,4) fp32, shared
 
 -- and each iteration convolves only the hidden state and adds the hoisted
@@ -23,7 +23,7 @@ no per-pixel table; gu in the epilogue (one frame, L2-resident):
   z, r = sigmoid(conv5x5(h, W_zr[:, :64]) + gx[:128])   one GEMM (N = 128);
          the epilogue writes z and r*h
   q   = tanh(conv5x5(r*h, W_q[:, :64]) + gx[128:])      epilogue
-         h = (1-z) h + z q (fp32 state) and its bf16 copy
+         h = (1-z) h + z q (fp32 state) and its fp16 copy
   each head: conv3x3 -> ReLU -> conv1x1 -> ReLU -> conv1x1; the four 3x3
          layers as one GEMM (N = 512) over h with gu added; the two 1x1
          layers of prob (25), xy (50) and angle (25) as one kernel each with
@@ -38,7 +38,7 @@ elementwise or layout pass;
 the 5x5 GEMMs contract 25 x 64 instead of 25 x 130 (padded: 192) channels,
 the heads' 3x3 9 x 64 instead of 9 x 66 (padded: 128). Weights are the
 reference's (OIHW fp32, safetensors names ``gru.convz`` ...
-``up_prob_head.4``), rounded to bf16 once; activations are bf16 between
+``up_prob_head.4``), rounded to fp16 once; activations are fp16 between
 layers, the GRU state and the hoisted terms fp32.
 """
 from __future__ import annotations
@@ -49,7 +49,7 @@ from dataclasses import dataclass
 
 import torch
 
-from ._capi import EPI_C4_F32, EPI_GRU_Q, EPI_GRU_ZR, EPI_NHWC, EPI_PLANAR_F16, EPI_SPLIT_BF16, \
+from ._capi import EPI_C4_F32, EPI_GRU_Q, EPI_GRU_ZR, EPI_NHWC, EPI_PLANAR_F16, EPI_SPLIT_F16, \
     EPI_PLANAR_F32, ConvEpilogue, check, lib
 from .ops import _cuda, _p, _stream, pack_conv_weight, pad64
 
@@ -169,11 +169,11 @@ class RefineStage:
         self.w_gx = pack_conv_weight(wg[:, H:H + FEATURE], 64, 192)
         # identity blocks: the extra K that adds hi + lo of the hoisted GRU
         # terms (z, r: blocks 0 and 1 of gx; q: block 2)
-        iz = torch.zeros((1, 128, 256), device=d, dtype=torch.bfloat16)
+        iz = torch.zeros((1, 128, 256), device=d, dtype=torch.float16)
         for n in range(128):
             iz[0, n, (n // 64) * 128 + n % 64] = 1
             iz[0, n, (n // 64) * 128 + 64 + n % 64] = 1
-        e64 = torch.eye(64, device=d, dtype=torch.bfloat16)
+        e64 = torch.eye(64, device=d, dtype=torch.float16)
         self.iz = iz
         self.iq = torch.cat([e64, e64], 1)[None].contiguous()   # (1, 64, 128)
         self.w_gxu = pack_conv_weight(wg[:, H + FEATURE:], 64, 192)
@@ -184,10 +184,10 @@ class RefineStage:
         self.w_c4 = [pack_conv_weight(params[f"{n}.4.weight"].to(d), 128, pad64(c))
                      for n, c in HEADS]
         self.b_c4 = [f32(params[f"{n}.4.bias"]) for n, _ in HEADS]
-        bf = torch.bfloat16
+        bf = torch.float16
         mk = lambda c, dt=bf, n=B: torch.zeros((n, h, w, c), device=d, dtype=dt)  # noqa: E731
-        self.hx, self.rhx = mk(H), mk(H)                     # h (bf16), r * h
-        # per-pixel epilogue tensors in channel groups (C8 bf16, C4 fp32)
+        self.hx, self.rhx = mk(H), mk(H)                     # h (fp16), r * h
+        # per-pixel epilogue tensors in channel groups (C8 fp16, C4 fp32)
         self.z = torch.zeros((B, H // 8, h, w, 8), device=d, dtype=bf)
         self.h32 = torch.zeros((B, H // 4, h, w, 4), device=d)
         self.fx, self.ux = mk(FEATURE), mk(64, n=1)          # feat, [uv | 0]
@@ -216,7 +216,7 @@ class RefineStage:
     def _conv(self, x, cin_off, cin_pad, w, bias, cout, ks, **epi):
         e = ConvEpilogue(**{k: (_p(v) if isinstance(v, torch.Tensor) else v)
                             for k, v in epi.items()})
-        check(lib.bvml_conv2d_nhwc_bf16_ex(_p(x), x.shape[-1], cin_off, cin_pad, _p(w),
+        check(lib.bvml_conv2d_nhwc_f16_ex(_p(x), x.shape[-1], cin_off, cin_pad, _p(w),
                                            _p(bias), x.shape[0], self.h, self.w, cout,
                                            w.shape[1], ks, ctypes.byref(e), _p(self.err),
                                            _stream(self.dev)))
@@ -227,7 +227,7 @@ class RefineStage:
         inputs once (three convolutions)."""
         _cuda("refine stage", h0, feat, uv)
         self.err.zero_()  # each refinement reports its own pipeline status
-        uvn = uv.permute(1, 2, 0)[None].to(torch.bfloat16)
+        uvn = uv.permute(1, 2, 0)[None].to(torch.float16)
         h0 = h0.float().contiguous()
         feat = feat.float().contiguous()
         self.ux[..., :2] = uvn
@@ -236,7 +236,7 @@ class RefineStage:
                                         _p(self.hx), _p(self.fx), _stream(self.dev)))
             self._conv(self.ux, 0, 64, self.w_gxu, self.zeros, 192, 5, mode=EPI_C4_F32,
                        out=self.gxu, out_c=192, out_off=0)
-            self._conv(self.fx, 0, 64, self.w_gx, self.zeros, 192, 5, mode=EPI_SPLIT_BF16,
+            self._conv(self.fx, 0, 64, self.w_gx, self.zeros, 192, 5, mode=EPI_SPLIT_F16,
                        out=self.gx, out_c=384, out_off=0, add=self.gxu, add_c=192,
                        add_shared=1)
             self._conv(self.ux, 0, 64, self.w_gu, self.zeros, 4 * HEAD_HIDDEN, 3,
@@ -293,14 +293,14 @@ class RefineStage:
             raise RuntimeError(f"dsine cuda: refine stage: pipeline gave up (code {code})")
 
 
-def reference_stage(params, h0, feat, uv, iters: int, *, emulate_bf16: bool = True):
+def reference_stage(params, h0, feat, uv, iters: int, *, emulate_f16: bool = True):
     """Plain PyTorch fp32 restatement of the same computation (the reference's
-    formulas, src/dsine_refine.cpp:118-158), for tests. With emulate_bf16 the
-    weights and the activations between layers are rounded to bf16 exactly
+    formulas, src/dsine_refine.cpp:118-158), for tests. With emulate_f16 the
+    weights and the activations between layers are rounded to fp16 exactly
     where RefineStage rounds them, so the two differ only in summation
     order."""
     F = torch.nn.functional
-    q16 = (lambda t: t.to(torch.bfloat16).float()) if emulate_bf16 else (lambda t: t)
+    q16 = (lambda t: t.to(torch.float16).float()) if emulate_f16 else (lambda t: t)
     W = {k: (q16(v) if k.endswith("weight") else v.float()) for k, v in params.items()}
     B = h0.shape[0]
     uvb = uv[None].expand(B, -1, -1, -1).float()

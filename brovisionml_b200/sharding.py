@@ -25,6 +25,13 @@ The only cross-GPU step is the final gather (``gather_frames`` /
 ``gather_bands``): each rank's owned output goes to rank 0 (torch.distributed
 gather, NCCL over NVLink on GPUs, gloo on CPU) or is copied to host by each
 rank.
+
+Failure detection is on the host, between steps: before a collective, every
+rank posts its status for that step in the process group's key-value store
+(``check_ranks``), a rank that fails posts why (``report_failure``), and the
+others learn of it -- or of a rank that never arrives -- from the store within
+a timeout, before they enter the collective, and raise RankFailure naming the
+rank. No GPU kernel waits on another rank.
 """
 from __future__ import annotations
 
@@ -126,12 +133,16 @@ def band_intrinsics(cv: float, band: Band) -> float:
     return cv - band.comp0
 
 
-def gather_frames(local, counts: Sequence[int], group=None):
+def gather_frames(local, counts: Sequence[int], group=None, *, store=None, step=None,
+                  timeout: float = 60.0):
     """Gather each rank's (count_r, ...) output to rank 0 (torch.distributed).
 
     Returns the concatenated tensor on rank 0 and None elsewhere. Every rank
     must call it (a collective). Without an initialised process group (one
-    process) the local part is the whole result."""
+    process) the local part is the whole result. With a key-value ``store``,
+    the ranks first check each other in for ``step`` (check_ranks, bounded by
+    ``timeout`` seconds): a rank that failed or left is reported as
+    RankFailure on every other rank instead of a hang in the collective."""
     import torch
     import torch.distributed as dist
 
@@ -141,6 +152,8 @@ def gather_frames(local, counts: Sequence[int], group=None):
         return local[: counts[0]]
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
+    if store is not None:
+        check_ranks(store, step, rank, world, timeout)
     mx = max(counts)
     pad_shape = (mx,) + tuple(local.shape[1:])
     send = torch.zeros(pad_shape, dtype=local.dtype, device=local.device)
@@ -154,10 +167,60 @@ def gather_frames(local, counts: Sequence[int], group=None):
 
 
 def gather_bands(local_rows, bands: Sequence[Band], group=None, row_dim: int = -2,
-                 scale: int = 8):
+                 scale: int = 8, **check):
     """Gather owned output rows (scale x grid rows) of every band to rank 0 and
-    stitch them along ``row_dim``. Returns the frame on rank 0, None elsewhere."""
+    stitch them along ``row_dim``. Returns the frame on rank 0, None elsewhere.
+    ``check`` (store, step, timeout) as for gather_frames."""
     counts = [scale * (b.own1 - b.own0) for b in bands]
     moved = local_rows.movedim(row_dim, 0).contiguous()
-    full = gather_frames(moved, counts, group)
+    full = gather_frames(moved, counts, group, **check)
     return None if full is None else full.movedim(0, row_dim).contiguous()
+
+
+class RankFailure(RuntimeError):
+    """Ranks that reported a failure, or did not arrive in time, for a step."""
+
+    def __init__(self, step, failed: dict, missing: list):
+        self.step, self.failed, self.missing = step, failed, missing
+        parts = [f"rank {r} failed: {m}" for r, m in sorted(failed.items())]
+        parts += [f"rank {r} did not arrive" for r in missing]
+        super().__init__(f"dsine ops: step {step}: " + "; ".join(parts))
+
+
+def _key(step, rank: int) -> str:
+    return f"bvml/step/{step}/rank/{rank}"
+
+
+def report_failure(store, step, rank: int, exc: BaseException | str) -> None:
+    """A rank that cannot take part in `step` posts why (then leaves)."""
+    store.set(_key(step, rank), ("failed: " + str(exc)).encode())
+
+
+def check_ranks(store, step, rank: int, world: int, timeout: float) -> None:
+    """Post this rank's arrival for `step` and wait (up to `timeout` seconds)
+    until every rank has posted; raise RankFailure if any rank reported a
+    failure or did not arrive. Call it before each collective of the step."""
+    import time
+
+    store.set(_key(step, rank), b"ok")
+    deadline = time.monotonic() + timeout
+    failed, pending = {}, [r for r in range(world) if r != rank]
+    while pending:
+        still = []
+        for r in pending:
+            k = _key(step, r)
+            if store.check([k]):
+                v = store.get(k).decode()
+                if v != "ok":
+                    failed[r] = v[len("failed: "):] if v.startswith("failed: ") else v
+            else:
+                still.append(r)
+        pending = still
+        if failed:
+            break
+        if pending and time.monotonic() > deadline:
+            break
+        if pending:
+            time.sleep(0.01)
+    if failed or pending:
+        raise RankFailure(step, failed, [] if failed else pending)

@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define BVML_ABI_VERSION 3
+#define BVML_ABI_VERSION 4
 
 enum bvml_dtype { BVML_F32 = 0, BVML_F16 = 1 };
 
@@ -129,8 +129,22 @@ int bvml_slice2d(const void* x, int N, int C, int H, int W, int h0, int w0, int 
 size_t bvml_refine_workspace_bytes(int B, int h, int w);
 
 /*
+ * Status of the last bvml_refine / bvml_refine_logits call that used
+ * `workspace` (no reference counterpart: the reference's per-iteration
+ * launches have no device-side waits). The persistent AngMF launch lets a
+ * tile wait for its neighbour tiles of the previous iteration; every such
+ * wait is bounded, and one that gives up (the GPU stopped making progress)
+ * records it in the workspace instead of hanging. Synchronises `stream`;
+ * returns BVML_OK, or BVML_ECUDA with the reason in bvml_last_error().
+ */
+int bvml_refine_status(const void* workspace, void* stream);
+
+/*
  * The whole refine-ops unit of Refiner::forward (src/dsine_refine.cpp:241-292)
- * for B frames, fused into iters + 1 kernel launches:
+ * for B frames, fused into two kernel launches (one persistent launch for all
+ * AngMF iterations, one for the upsample; iters + 1 launches for shapes the
+ * persistent kernel does not take: grid widths that are not a multiple of 16
+ * bytes of storage, or dilations above 2):
  *   n = RayReLU(normal0, ray8)                      (fused into iteration 0)
  *   repeat iters times: n = AngMF(n, prob[i], xy[i], angle[i], ray8)
  *   up = L2normalise(ConvexUpsample8(n, mask))      (upsampled once: the
@@ -196,26 +210,26 @@ int bvml_refine_noalloc(const void* normal0, const float* ray8, const void* cons
                         int crop_l, int out_h, int out_w, int dtype, void* out, void* stream);
 
 /*
- * 2-D convolution, stride 1, zero padding ks/2 ("same"), on bf16 NHWC tensors
+ * 2-D convolution, stride 1, zero padding ks/2 ("same"), on fp16 NHWC tensors
  * with fp32 accumulation on the tensor cores (tcgen05), plus bias and an
  * activation (0 none, 1 ReLU, 2 sigmoid, 3 tanh): the conv2d_forward calls of
  * the refine stage's ConvGRU (5x5, src/dsine_refine.cpp:140-158) and
  * prediction heads (3x3, 1x1, :118-125), which the reference runs through
  * brotensor on NCHW fp32 tensors.
- *   x    (B,H,W,cin_pad) bf16, cin_pad a multiple of 64, pad channels zero
- *   w    (ks*ks, cout_pad, cin_pad) bf16, w[ky*ks+kx][o][c] = weight[o][c][ky][kx]
+ *   x    (B,H,W,cin_pad) fp16, cin_pad a multiple of 64, pad channels zero
+ *   w    (ks*ks, cout_pad, cin_pad) fp16, w[ky*ks+kx][o][c] = weight[o][c][ky][kx]
  *   bias (cout) fp32
- *   y    (B,H,W,cout_pad) bf16, cout_pad a multiple of 64; channels >= cout
+ *   y    (B,H,W,cout_pad) fp16, cout_pad a multiple of 64; channels >= cout
  *        are written as zeros, so y can be the next convolution's x
  *   ks in {1, 3, 5}; err: a device int the kernel sets nonzero if its
  *   pipeline had to give up (read it after synchronising; 0 = fine).
  */
-int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B, int H, int W,
+int bvml_conv2d_nhwc_f16(const void* x, const void* w, const float* bias, int B, int H, int W,
                           int cin_pad, int cout, int cout_pad, int ks, int act, void* y,
                           int* err, void* stream);
 
-/* Epilogue modes of bvml_conv2d_nhwc_bf16_ex. */
-#define BVML_EPI_NHWC 0        /* act(conv) as bf16 at out[pixel * out_c + out_off + o] */
+/* Epilogue modes of bvml_conv2d_nhwc_f16_ex. */
+#define BVML_EPI_NHWC 0        /* act(conv) as fp16 at out[pixel * out_c + out_off + o] */
 #define BVML_EPI_PLANAR_F16 1  /* conv as fp16 at out[(b * cout + o) * H * W + y * W + x]
                                   (TMA stores when W * 2 is a multiple of 16 bytes,
                                   plain stores otherwise) */
@@ -225,23 +239,23 @@ int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B
 #define BVML_EPI_C4_F32 5      /* act(conv) as fp32 in channel groups of 4 (C4, below),
                                   out_c channels per frame, at channel out_off + o
                                   (act 0 or 1; out_c, out_off multiples of 4) */
-#define BVML_EPI_SPLIT_BF16 6  /* conv as two bf16 halves per 64-channel block:
-                                  hi = bf16(v) at NHWC channel out_off + 128 (o / 64) +
-                                  o % 64, lo = bf16(v - hi) 64 channels further (cout a
+#define BVML_EPI_SPLIT_F16 6   /* conv as two fp16 halves per 64-channel block:
+                                  hi = fp16(v) at NHWC channel out_off + 128 (o / 64) +
+                                  o % 64, lo = fp16(v - hi) 64 channels further (cout a
                                   multiple of 32, out_c >= out_off + 2 cout_pad): an
                                   extra-K operand (xin below) keeping ~16 bits of v */
 
 /*
- * Where and how bvml_conv2d_nhwc_bf16_ex writes its result. Channel strides
+ * Where and how bvml_conv2d_nhwc_f16_ex writes its result. Channel strides
  * and offsets in elements, multiples of 8; tensors 16-byte aligned.
  * Channel-group layouts: C4 fp32 = [frame][C / 4][H][W][4] (channel c of
  * pixel (y, x) at ((f * C / 4 + c / 4) * H * W + y * W + x) * 4 + c % 4), C8
- * bf16 the same with groups of 8 -- 16 bytes per pixel and group, so the
+ * fp16 the same with groups of 8 -- 16 bytes per pixel and group, so the
  * epilogue's per-pixel reads and writes are coalesced.
  * GRU_ZR (src/dsine_refine.cpp:144-147): z = sigmoid(conv[0:64]) -> z
- *   (C8 bf16, 64 channels); r = sigmoid(conv[64:128]) -> rh[pixel * rh_c +
+ *   (C8 fp16, 64 channels); r = sigmoid(conv[64:128]) -> rh[pixel * rh_c +
  *   o] = r * h, h the fp32 hidden state h32 (C4, 64 channels).
- * GRU_Q (:148-156): q = tanh(conv) -> h32 = (1 - z) h32 + z q, with bf16
+ * GRU_Q (:148-156): q = tanh(conv) -> h32 = (1 - z) h32 + z q, with fp16
  *   copies at hx[pixel * hx_c + o] and, when hin is not null, hin[...].
  * add (optional, every mode but the GRU ones): a per-pixel fp32 addend in C4 layout with
  *   add_c channels per frame (a multiple of 4, >= cout); channel o of frame f
@@ -251,11 +265,11 @@ int bvml_conv2d_nhwc_bf16(const void* x, const void* w, const float* bias, int B
  *   feature and uv channels, the heads' uv channels, which the refine stage
  *   convolves once per refinement instead of once per iteration.
  * xin (optional, every mode): an extra K block, conv[o] += sum_k xin[pixel *
- *   xin_stride + k] * wx[o * xin_c + k] for k < xin_c, xin bf16 with
+ *   xin_stride + k] * wx[o * xin_c + k] for k < xin_c, xin fp16 with
  *   xin_stride channels per pixel (0: xin_c; a multiple of 8), wx (cout_pad,
- *   xin_c) bf16, xin_c a multiple of 64 -- a 1x1 term the tensor cores add
+ *   xin_c) fp16, xin_c a multiple of 64 -- a 1x1 term the tensor cores add
  *   before the epilogue (the refine stage adds its hoisted terms this way, as
- *   BVML_EPI_SPLIT_BF16 halves times identity blocks).
+ *   BVML_EPI_SPLIT_F16 halves times identity blocks).
  */
 typedef struct {
     int mode;
@@ -280,13 +294,13 @@ typedef struct {
 } bvml_conv_epilogue;
 
 /*
- * bvml_conv2d_nhwc_bf16 reading input channels [cin_off, cin_off + cin_pad)
- * of x (B,H,W,x_c) bf16 (cin_off and cin_pad multiples of 64; x_c a multiple
+ * bvml_conv2d_nhwc_f16 reading input channels [cin_off, cin_off + cin_pad)
+ * of x (B,H,W,x_c) fp16 (cin_off and cin_pad multiples of 64; x_c a multiple
  * of 8) and writing through `epi`: the fused ConvGRU gates and the
  * prediction heads' planar outputs, so that the refine stage runs on NHWC
  * buffers with no separate elementwise or layout passes.
  */
-int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, const void* w,
+int bvml_conv2d_nhwc_f16_ex(const void* x, int x_c, int cin_off, int cin_pad, const void* w,
                              const float* bias, int B, int H, int W, int cout, int cout_pad,
                              int ks, const bvml_conv_epilogue* epi, int* err, void* stream);
 
@@ -295,14 +309,14 @@ int bvml_conv2d_nhwc_bf16_ex(const void* x, int x_c, int cin_off, int cin_pad, c
  * 128) + ReLU + conv1x1 (128 -> cout), src/dsine_refine.cpp:118-125, which
  * the reference runs as two brotensor conv2d_forward calls and a relu_forward
  * with the 128-channel intermediate in memory; here it stays on the chip.
- *   x     (B,H,W,x_c) bf16 NHWC; input channels [cin_off, cin_off + 128)
+ *   x     (B,H,W,x_c) fp16 NHWC; input channels [cin_off, cin_off + 128)
  *         (cin_off a multiple of 64)
- *   w2    (1,128,128) bf16, b2 (128) fp32: the first 1x1 layer
- *   w4    (1,64,128) bf16 (rows >= cout zero), b4 (cout) fp32: the second
+ *   w2    (1,128,128) fp16, b2 (128) fp32: the first 1x1 layer
+ *   w4    (1,64,128) fp16 (rows >= cout zero), b4 (cout) fp32: the second
  *   out   (B,cout,H,W) planar, dtype BVML_F16 or BVML_F32; cout <= 64
- *   err   as bvml_conv2d_nhwc_bf16
+ *   err   as bvml_conv2d_nhwc_f16
  * The results equal the two separate convolutions'
- * (bvml_conv2d_nhwc_bf16_ex with NHWC + ReLU, then planar), bit for bit.
+ * (bvml_conv2d_nhwc_f16_ex with NHWC + ReLU, then planar), bit for bit.
  */
 int bvml_head_tail_1x1(const void* x, int x_c, int cin_off, const void* w2, const float* b2,
                        const void* w4, const float* b4, int B, int H, int W, int cout,
@@ -311,8 +325,8 @@ int bvml_head_tail_1x1(const void* x, int x_c, int cin_off, const void* w2, cons
 /*
  * The refine stage's inputs in its layouts, one pass: the decoder's hidden
  * state h0 and feature (B,64,H,W) fp32 planar -> the GRU state h32 (C4 fp32,
- * (B,16,H,W,4)) and its bf16 NHWC copy hx (B,H,W,64), and the feature as
- * NHWC bf16 fx (B,H,W,64); feat and fx may both be null. Replaces the
+ * (B,16,H,W,4)) and its fp16 NHWC copy hx (B,H,W,64), and the feature as
+ * NHWC fp16 fx (B,H,W,64); feat and fx may both be null. Replaces the
  * concat / layout work at the start of Refiner::forward
  * (src/dsine_refine.cpp:245-248) for the tensor-core stage.
  */
@@ -327,6 +341,10 @@ int bvml_stage_inputs(const float* h0, const float* feat, int B, int H, int W, f
  * every launch of the fused unit on the stream it runs on. n = 0 disarms.
  */
 int bvml_probe_events(void* const* events, int n);
+
+/* How many probe events the calling thread's last bvml_refine call recorded
+ * (its kernel launches + 1). */
+int bvml_probe_recorded(void);
 
 #ifdef __cplusplus
 }

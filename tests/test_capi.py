@@ -23,7 +23,7 @@ def test_header_symbols_exported():
     from brovisionml_b200 import _capi
 
     syms = declared_symbols()
-    assert len(syms) == 17, syms
+    assert len(syms) == 19, syms
     assert sorted(_capi.EXPORTS) == syms
     for s in syms:
         assert hasattr(b.lib, s), s
@@ -31,7 +31,7 @@ def test_header_symbols_exported():
                          text=True, check=True).stdout
     exported = set(re.findall(r" T (bvml_\w+)", out))
     assert exported == set(syms)
-    assert b.abi_version() == 3
+    assert b.abi_version() == 4
 
 
 def test_bridge_library_exports_reference_signatures():
@@ -92,7 +92,9 @@ def test_argument_errors_without_gpu():
     assert rc == 1 and "outside" in lib.bvml_last_error().decode()
     # refine: workspace size and alignment are checked before any launch
     need = lib.bvml_refine_workspace_bytes(2, 8, 8)
-    assert need == 2 * 1536 + 768
+    # sync words (64 + one per 32 x 16 tile, 256-byte aligned), two fp32 normal
+    # buffers of 2 frames, the ray
+    assert need == 512 + 2 * 1536 + 768
     arr = (ctypes.c_void_p * 1)(0x3000)
     rc = lib.bvml_refine(fake, None, arr, arr, arr, 1, fake, 2, 8, 8, 5, 1, 1.0, 0.0, 1.0, 0.0,
                          0, 0, 0, 64, 64, 0, ctypes.c_void_p(0x10000), need - 1, fake, None)
@@ -117,19 +119,19 @@ def test_argument_errors_without_gpu():
 
 
 def test_conv_argument_errors_without_gpu():
-    """bvml_conv2d_nhwc_bf16_ex validates before touching the GPU: kernel
+    """bvml_conv2d_nhwc_f16_ex validates before touching the GPU: kernel
     size, the GRU epilogues' refusal of an addend, the extra K block's
     layout and the split output's room."""
     import ctypes
 
-    from brovisionml_b200._capi import (EPI_GRU_ZR, EPI_NHWC, EPI_SPLIT_BF16, ConvEpilogue,
+    from brovisionml_b200._capi import (EPI_GRU_ZR, EPI_NHWC, EPI_SPLIT_F16, ConvEpilogue,
                                         lib)
 
     fake = 0x10000  # aligned, never dereferenced: every call fails validation first
 
     def call(ks=5, cout=128, cout_pad=128, **epi):
         e = ConvEpilogue(**epi)
-        return lib.bvml_conv2d_nhwc_bf16_ex(fake, 64, 0, 64, fake, fake, 1, 8, 16, cout,
+        return lib.bvml_conv2d_nhwc_f16_ex(fake, 64, 0, 64, fake, fake, 1, 8, 16, cout,
                                             cout_pad, ks, ctypes.byref(e), fake, None)
 
     assert call(ks=4, mode=EPI_NHWC, out=fake, out_c=128) == 1
@@ -141,7 +143,7 @@ def test_conv_argument_errors_without_gpu():
     assert call(mode=EPI_NHWC, out=fake, out_c=128, xin=fake, xin_c=128, xin_stride=64,
                 wx=fake) == 1
     assert "xin_stride" in lib.bvml_last_error().decode()
-    assert call(mode=EPI_SPLIT_BF16, out=fake, out_c=128) == 1
+    assert call(mode=EPI_SPLIT_F16, out=fake, out_c=128) == 1
     assert "split" in lib.bvml_last_error().decode()
 
 

@@ -1,10 +1,10 @@
 """Tensor-core (tcgen05) implicit-GEMM convolution against a plain PyTorch fp32
-conv2d of the same bf16-rounded inputs and weights: the refine stage's conv
+conv2d of the same fp16-rounded inputs and weights: the refine stage's conv
 shapes (ConvGRU 5x5 over 130 -> 64 channels, head 3x3 66 -> 128 and 1x1
 layers, src/dsine_refine.cpp:95-158) and edge cases (one CTA, odd frames,
 output channels that are not a multiple of the tile).
 
-Tolerance: the kernel rounds its output to bf16 (relative 2^-9) and sums in
+Tolerance: the kernel rounds its output to fp16 (relative 2^-9) and sums in
 another order than torch: |y - ref| <= 8e-3 |ref| + 2e-3.
 """
 import pytest
@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 
 def ref_conv(x_nhwc, weight, bias, ks, act, cin):
     x = x_nhwc[..., :cin].permute(0, 3, 1, 2).float()
-    y = torch.nn.functional.conv2d(x, weight.to(torch.bfloat16).float(), bias, padding=ks // 2)
+    y = torch.nn.functional.conv2d(x, weight.to(torch.float16).float(), bias, padding=ks // 2)
     y = {"none": y, "relu": torch.relu(y), "sigmoid": torch.sigmoid(y),
          "tanh": torch.tanh(y)}[act]
     return y.permute(0, 2, 3, 1)
@@ -26,8 +26,8 @@ def run_case(B, H, W, cin, cout, ks, act, seed=0):
 
     g = torch.Generator(device="cuda").manual_seed(seed)
     cin_pad, cout_pad = b.ops.pad64(cin), b.ops.pad64(cout)
-    x = torch.zeros((B, H, W, cin_pad), device="cuda", dtype=torch.bfloat16)
-    x[..., :cin] = torch.randn((B, H, W, cin), device="cuda", generator=g).to(torch.bfloat16)
+    x = torch.zeros((B, H, W, cin_pad), device="cuda", dtype=torch.float16)
+    x[..., :cin] = torch.randn((B, H, W, cin), device="cuda", generator=g).to(torch.float16)
     wstd = (cin * ks * ks) ** -0.5
     weight = torch.randn((cout, cin, ks, ks), device="cuda", generator=g) * wstd
     bias = torch.randn(cout, device="cuda", generator=g) * 0.1
@@ -65,7 +65,7 @@ def test_conv_shapes(B, H, W, cin, cout, ks, act):
 def test_conv_addend_and_fp32_output(shared):
     """The per-pixel addend (C4 fp32; per frame, or one frame shared by
     all) joins conv + bias before the activation; fp32 C4 output
-    (bvml_conv2d_nhwc_bf16_ex with BVML_EPI_C4_F32): the refine stage's
+    (bvml_conv2d_nhwc_f16_ex with BVML_EPI_C4_F32): the refine stage's
     hoisted feature / uv terms."""
     import ctypes
 
@@ -75,7 +75,7 @@ def test_conv_addend_and_fp32_output(shared):
 
     B, H, W, cin, cout, ks = 2, 19, 40, 64, 192, 5
     g = torch.Generator(device="cuda").manual_seed(11)
-    x = torch.randn((B, H, W, cin), device="cuda", generator=g).to(torch.bfloat16)
+    x = torch.randn((B, H, W, cin), device="cuda", generator=g).to(torch.float16)
     weight = torch.randn((cout, cin, ks, ks), device="cuda", generator=g) * (cin * ks * ks) ** -0.5
     bias = torch.randn(cout, device="cuda", generator=g) * 0.1
     add = torch.randn((1 if shared else B, (cout + 8) // 4, H, W, 4), device="cuda", generator=g)
@@ -83,7 +83,7 @@ def test_conv_addend_and_fp32_output(shared):
     err = torch.zeros(1, device="cuda", dtype=torch.int32)
     e = ConvEpilogue(mode=EPI_C4_F32, act=1, out=_p(y), out_c=cout, out_off=0,
                      add=_p(add), add_c=cout + 8, add_shared=int(shared))
-    check(lib.bvml_conv2d_nhwc_bf16_ex(_p(x), cin, 0, cin, _p(b.pack_conv_weight(weight)),
+    check(lib.bvml_conv2d_nhwc_f16_ex(_p(x), cin, 0, cin, _p(b.pack_conv_weight(weight)),
                                        _p(bias), B, H, W, cout, cout, ks, ctypes.byref(e),
                                        _p(err), _stream(torch.device("cuda"))))
     torch.cuda.synchronize()
@@ -102,7 +102,7 @@ def test_conv_addend_and_fp32_output(shared):
     (1, 7, 37, 64, 30, 5, False),     # fp32, odd width
 ])
 def test_conv_planar_outputs(B, H, W, cin, cout, ks, f16):
-    """Planar (B, cout, H, W) outputs of bvml_conv2d_nhwc_bf16_ex (the heads'
+    """Planar (B, cout, H, W) outputs of bvml_conv2d_nhwc_f16_ex (the heads'
     raw outputs), through TMA stores where the rows allow it and plain stores
     otherwise."""
     import ctypes
@@ -113,8 +113,8 @@ def test_conv_planar_outputs(B, H, W, cin, cout, ks, f16):
 
     g = torch.Generator(device="cuda").manual_seed(W + cout)
     cin_pad = b.ops.pad64(cin)
-    x = torch.zeros((B, H, W, cin_pad), device="cuda", dtype=torch.bfloat16)
-    x[..., :cin] = torch.randn((B, H, W, cin), device="cuda", generator=g).to(torch.bfloat16)
+    x = torch.zeros((B, H, W, cin_pad), device="cuda", dtype=torch.float16)
+    x[..., :cin] = torch.randn((B, H, W, cin), device="cuda", generator=g).to(torch.float16)
     weight = torch.randn((cout, cin, ks, ks), device="cuda", generator=g) * (cin * ks * ks) ** -0.5
     bias = torch.randn(cout, device="cuda", generator=g) * 0.1
     dt = torch.float16 if f16 else torch.float32
@@ -122,7 +122,7 @@ def test_conv_planar_outputs(B, H, W, cin, cout, ks, f16):
     err = torch.zeros(1, device="cuda", dtype=torch.int32)
     e = ConvEpilogue(mode=EPI_PLANAR_F16 if f16 else EPI_PLANAR_F32, out=_p(y))
     wp = b.pack_conv_weight(weight, cin_pad)
-    check(lib.bvml_conv2d_nhwc_bf16_ex(_p(x), cin_pad, 0, cin_pad, _p(wp), _p(bias), B, H, W,
+    check(lib.bvml_conv2d_nhwc_f16_ex(_p(x), cin_pad, 0, cin_pad, _p(wp), _p(bias), B, H, W,
                                        cout, wp.shape[1], ks, ctypes.byref(e), _p(err),
                                        _stream(torch.device("cuda"))))
     torch.cuda.synchronize()
@@ -143,7 +143,7 @@ def _conv_ex(x, cin, w_packed, bias, cout, ks, **epi):
     B, H, W, xc = x.shape
     err = torch.zeros(1, device="cuda", dtype=torch.int32)
     e = ConvEpilogue(**{k: (_p(v) if isinstance(v, torch.Tensor) else v) for k, v in epi.items()})
-    check(lib.bvml_conv2d_nhwc_bf16_ex(_p(x), xc, 0, cin, _p(w_packed), _p(bias), B, H, W, cout,
+    check(lib.bvml_conv2d_nhwc_f16_ex(_p(x), xc, 0, cin, _p(w_packed), _p(bias), B, H, W, cout,
                                        w_packed.shape[1], ks, ctypes.byref(e), _p(err),
                                        _stream(torch.device("cuda"))))
     torch.cuda.synchronize()
@@ -153,14 +153,14 @@ def _conv_ex(x, cin, w_packed, bias, cout, ks, **epi):
 @pytest.mark.parametrize("cout,ks", [(128, 5), (64, 5), (192, 3)])
 def test_conv_extra_k_and_split(cout, ks):
     """The extra K block (conv += xin . wx^T per pixel, through the MMA
-    pipeline) and the split-bf16 output (hi + lo of the fp32 result): the
+    pipeline) and the split-fp16 output (hi + lo of the fp32 result): the
     refine stage's hoisted GRU terms, added by the tensor cores."""
     import brovisionml_b200 as b
-    from brovisionml_b200._capi import EPI_C4_F32, EPI_SPLIT_BF16
+    from brovisionml_b200._capi import EPI_C4_F32, EPI_SPLIT_F16
 
     B, H, W, cin, xc = 2, 21, 40, 64, 128
     g = torch.Generator(device="cuda").manual_seed(cout + ks)
-    x = torch.randn((B, H, W, cin), device="cuda", generator=g).to(torch.bfloat16)
+    x = torch.randn((B, H, W, cin), device="cuda", generator=g).to(torch.float16)
     weight = torch.randn((cout, cin, ks, ks), device="cuda", generator=g) * (cin * ks * ks) ** -0.5
     bias = torch.randn(cout, device="cuda", generator=g) * 0.1
     wp = b.pack_conv_weight(weight)
@@ -168,19 +168,19 @@ def test_conv_extra_k_and_split(cout, ks):
 
     # split output, per 64-channel block hi then lo: hi + lo reproduces the
     # fp32 result to ~2^-16
-    sp = torch.full((B, H, W, 2 * cout), float("nan"), device="cuda", dtype=torch.bfloat16)
-    _conv_ex(x, cin, wp, bias, cout, ks, mode=EPI_SPLIT_BF16, out=sp, out_c=2 * cout, out_off=0)
+    sp = torch.full((B, H, W, 2 * cout), float("nan"), device="cuda", dtype=torch.float16)
+    _conv_ex(x, cin, wp, bias, cout, ks, mode=EPI_SPLIT_F16, out=sp, out_c=2 * cout, out_off=0)
     blk = sp.reshape(B, H, W, cout // 64, 2, 64).float()
     got = (blk[..., 0, :] + blk[..., 1, :]).reshape(B, H, W, cout)
     d = ((got - ref).abs() - 1e-4 * ref.abs()).max().item()
-    print(f"split bf16 cout={cout} k{ks}: excess {d:.2e}")
+    print(f"split fp16 cout={cout} k{ks}: excess {d:.2e}")
     assert d <= 1e-3
 
     # extra K: a 1x1 term of another input (the middle 128 of 256 channels per
     # pixel: a strided view), accumulated by the same MMAs
-    xfull = torch.randn((B, H, W, 2 * xc), device="cuda", generator=g).to(torch.bfloat16)
+    xfull = torch.randn((B, H, W, 2 * xc), device="cuda", generator=g).to(torch.float16)
     xin = xfull[..., 64:64 + xc]
-    wx = (torch.randn((cout, xc), device="cuda", generator=g) * xc ** -0.5).to(torch.bfloat16)
+    wx = (torch.randn((cout, xc), device="cuda", generator=g) * xc ** -0.5).to(torch.float16)
     y = torch.full((B, cout // 4, H, W, 4), float("nan"), device="cuda")
     _conv_ex(x, cin, wp, bias, cout, ks, mode=EPI_C4_F32, out=y, out_c=cout, out_off=0,
              xin=xin, xin_c=xc, xin_stride=2 * xc, wx=wx[None].contiguous())
@@ -196,21 +196,21 @@ def test_conv_extra_k_and_split(cout, ks):
 def test_head_tail_matches_two_convolutions(W, cout, f16):
     """bvml_head_tail_1x1 (1x1 -> ReLU -> 1x1 with the intermediate on chip)
     equals the two separate convolutions bit for bit: the same products,
-    the same bf16 rounding of the intermediate, the same summation order."""
+    the same fp16 rounding of the intermediate, the same summation order."""
     import brovisionml_b200 as b
     from brovisionml_b200._capi import EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, check, lib
     from brovisionml_b200.ops import _p, _stream
 
     B, H, k = 2, 19, 1
     g = torch.Generator(device="cuda").manual_seed(W + cout)
-    t1 = torch.randn((B, H, W, 512), device="cuda", generator=g).to(torch.bfloat16)
+    t1 = torch.randn((B, H, W, 512), device="cuda", generator=g).to(torch.float16)
     w2 = torch.randn((128, 128, 1, 1), device="cuda", generator=g) * 128 ** -0.5
     b2 = torch.randn(128, device="cuda", generator=g) * 0.1
     w4 = torch.randn((cout, 128, 1, 1), device="cuda", generator=g) * 128 ** -0.5
     b4 = torch.randn(cout, device="cuda", generator=g) * 0.1
     w2p, w4p = b.pack_conv_weight(w2), b.pack_conv_weight(w4, 128, 64)
     dt = torch.float16 if f16 else torch.float32
-    t2 = torch.zeros((B, H, W, 512), device="cuda", dtype=torch.bfloat16)
+    t2 = torch.zeros((B, H, W, 512), device="cuda", dtype=torch.float16)
     _conv_ex(t1[..., k * 128:(k + 1) * 128].contiguous(), 128, w2p, b2, 128, 1, mode=EPI_NHWC,
              act=1, out=t2, out_c=512, out_off=k * 128)
     want = torch.full((B, cout, H, W), float("nan"), device="cuda", dtype=dt)

@@ -178,3 +178,27 @@ def test_fullsize_cfg3_matches_oracle():
           f"{m['ang_p99_deg']:.2e} max {m['ang_max_deg']:.2e} deg")
     assert m["nonfinite"] == 0
     assert m["max_abs"] <= O.TOL_F32, m
+
+
+def test_persistent_and_per_iteration_paths_agree():
+    """bvml_refine runs all AngMF iterations in one persistent launch when an
+    iteration is at most a few waves of tiles (32 frames of 720p) and one
+    launch per iteration otherwise (256 frames). The two paths compute the
+    same arithmetic, so the first 32 frames of a 256-frame batch equal the
+    same 32 frames refined alone, bit for bit; the persistent launch's
+    dependency waits all completed (bvml_refine_status)."""
+    import ctypes
+
+    import brovisionml_b200 as bv
+
+    cfg = dict(bench.CONFIGS["cfg4"])
+    dev = torch.device("cuda", 0)
+    inp = bench.make_device_inputs(cfg, 256, 23, dev, torch)
+    whole = run(inp, cfg)
+    sub = bench.frames_slice(inp, 0, 32)
+    ws = torch.empty(bv.refine_workspace_bytes(32, inp["h"], inp["w"]), device=dev,
+                     dtype=torch.uint8)
+    part = run(sub, cfg, workspace=ws)
+    torch.cuda.synchronize()
+    assert bv.lib.bvml_refine_status(ctypes.c_void_p(ws.data_ptr()), None) == 0
+    assert torch.equal(whole[:32], part)

@@ -2,18 +2,18 @@
 
 The reference runs the ConvGRU and the prediction heads in fp32
 (src/dsine_refine.cpp:95-158). The B200 stage runs the same convolutions on
-the tensor cores with bf16 operands and fp32 accumulation. These tests bound
+the tensor cores with fp16 operands and fp32 accumulation. These tests bound
 what that costs, against the UNROUNDED fp32 model:
 
 * per stage output (tests/test_gpu_refine_stage.py bounds the stage only
-  against a copy that rounds to bf16 at the same points): every conv input
-  and weight is rounded to bf16 (relative error <= 2^-9 each, so <= 2^-8 per
-  product); a head output sits behind L = 5 such layers per iteration (3x3,
-  1x1, 1x1 of the head after the GRU's two convs), and the GRU state carries
-  the error of earlier iterations forward. The bounds are L * iters * 2^-8
-  relative to the output's own RMS for the mean absolute difference and four
-  times that for the maximum;
-* through the whole refinement: Refiner.forward (bf16 stage + the fused ops
+  against a copy that rounds to fp16 at the same points): every conv input
+  and weight is rounded to fp16 (relative error <= 2^-12 each, so <= 2^-11
+  per product); a head output sits behind L = 5 such layers per iteration
+  (3x3, 1x1, 1x1 of the head after the GRU's two convs), and the GRU state
+  carries the error of earlier iterations forward. The bounds are
+  L * iters * 2^-11 relative to the output's own RMS for the mean absolute
+  difference and four times that for the maximum;
+* through the whole refinement: Refiner.forward (fp16 stage + the fused ops
   on its raw head outputs) against the fp32 stage whose raw outputs go
   through the oracle's head activations and refine unit (fp64 C
   restatement). Bound: the reference's own staged-refine golden bound,
@@ -56,8 +56,8 @@ def test_stage_outputs_against_unrounded_fp32(iters):
     outs = [st.step() for _ in range(iters)]
     torch.cuda.synchronize()
     st.check_pipeline()
-    exact = reference_stage(params, hid, feat, uv, iters, emulate_bf16=False)
-    rel = 5 * iters * 2.0 ** -8
+    exact = reference_stage(params, hid, feat, uv, iters, emulate_f16=False)
+    rel = 5 * iters * 2.0 ** -11
     for name in ("prob", "xy", "angle", "up_mask"):
         got = getattr(outs[-1], name).float()
         ref = getattr(exact[-1], name).float()
@@ -71,14 +71,19 @@ def test_stage_outputs_against_unrounded_fp32(iters):
         assert d.max().item() <= 4 * rel * rms, name
 
 
-@pytest.mark.xfail(strict=True, reason="bf16 tensor-core operands: the final normals differ "
-                   "from the fp32 stage by max-abs ~5e-2 / mean-abs ~3e-3 on this case, outside "
-                   "the reference's 1e-2 / 1e-3 golden bound")
-def test_refiner_against_fp32_stage_and_oracle():
+_REFINER_CMP = {}
+
+
+def _refiner_vs_fp32():
+    """Refiner.forward (fp16 stage + fused ops) against the unrounded fp32
+    stage + the oracle's activations and ops, on config 1's 480 x 640 frame
+    (computed once for the tests below)."""
+    if _REFINER_CMP:
+        return _REFINER_CMP["m"]
     from brovisionml_b200.refine_stage import random_params, reference_stage
     from brovisionml_b200.refiner import Refiner, build_uv, grid_intrinsics
 
-    B, h, w = 1, 60, 80              # config 1's 480 x 640 frame
+    B, h, w = 1, 60, 80
     H, W = 8 * h, 8 * w
     intr = (0.8 * W, 0.8 * W, W / 2, H / 2)
     normal, feat, hid = _inputs(B, h, w, seed=21)
@@ -91,7 +96,7 @@ def test_refiner_against_fp32_stage_and_oracle():
 
     pc = {k: v.cuda() for k, v in params.items()}
     outs = reference_stage(pc, hid, feat, build_uv(intr, h, w, H, W, "cuda"), 5,
-                           emulate_bf16=False)
+                           emulate_f16=False)
     fu, cu, fv, cv = grid_intrinsics(intr, h, w, H, W)
     npy = lambda t: t.float().cpu().numpy()  # noqa: E731
     prob, angle = zip(*[O.head_activation(npy(o.prob), npy(o.angle)) for o in outs])
@@ -103,8 +108,23 @@ def test_refiner_against_fp32_stage_and_oracle():
                      mask=npy(outs[-1].up_mask))
     want = O.refine_unit(u)
     m = O.compare(got.cpu().numpy(), want)
-    print(f"Refiner (bf16 stage) vs fp32 stage + oracle ops: max-abs {m['max_abs']:.2e} "
+    print(f"Refiner (fp16 stage) vs fp32 stage + oracle ops: max-abs {m['max_abs']:.2e} "
           f"mean-abs {m['mean_abs']:.2e}; angular error mean {m['ang_mean_deg']:.2e} p99 "
           f"{m['ang_p99_deg']:.2e} max {m['ang_max_deg']:.2e} deg")
+    _REFINER_CMP["m"] = m
+    return m
+
+
+def test_refiner_mean_error_within_reference_bound():
+    m = _refiner_vs_fp32()
     assert m["nonfinite"] == 0
-    assert m["max_abs"] < 1e-2 and m["mean_abs"] < 1e-3, m
+    assert m["mean_abs"] < 1e-3, m
+
+
+@pytest.mark.xfail(strict=True, reason="fp16 tensor-core operands: max-abs 1.06e-2 on this "
+                   "random-weight frame, 6 % over the reference's 1e-2 bound; the largest "
+                   "errors sit where a pixel's xy offset is near zero, whose direction "
+                   "amplifies small logit errors")
+def test_refiner_max_error_within_reference_bound():
+    m = _refiner_vs_fp32()
+    assert m["max_abs"] < 1e-2, m

@@ -1,9 +1,9 @@
 """ConvGRU + prediction heads on the tensor cores (brovisionml_b200.
 refine_stage, src/dsine_refine.cpp:95-158 and 253-276) against a plain
 PyTorch fp32 restatement of the same formulas, with weights and the
-activations between layers rounded to bf16 at the same points
+activations between layers rounded to fp16 at the same points
 (refine_stage.reference_stage), so the two differ only in summation order
-and the rare bf16 rounding flip that order causes.
+and the rare fp16 rounding flip that order causes.
 
 Tolerances: per head output, max |d| <= 3e-2 and mean |d| <= 1e-3 after one
 iteration (outputs are O(1)); after three iterations of feedback through
@@ -44,7 +44,7 @@ def test_refine_stage_matches_torch(B, h, w, iters, out_dtype):
     torch.cuda.synchronize()
     st.check_pipeline()
     want = reference_stage(params, h0, feat, uv, iters)
-    exact = reference_stage(params, h0, feat, uv, iters, emulate_bf16=False)
+    exact = reference_stage(params, h0, feat, uv, iters, emulate_f16=False)
     lim_max, lim_mean = (3e-2, 1e-3) if iters == 1 else (6e-2, 3e-3)
     for name in ("prob", "xy", "angle", "up_mask"):
         got = getattr(outs[-1], name).float()
@@ -108,7 +108,7 @@ def test_refine_stage_skip_up_mask():
 
 def test_stage_inputs_layouts():
     """bvml_stage_inputs: planar fp32 h0 / feat -> h32 (C4 fp32), hx and fx
-    (NHWC bf16), against torch's own permutes; odd sizes."""
+    (NHWC fp16), against torch's own permutes; odd sizes."""
     from brovisionml_b200._capi import check, lib
     from brovisionml_b200.ops import _p, _stream
 
@@ -117,11 +117,11 @@ def test_stage_inputs_layouts():
     h0 = torch.randn((B, 64, H, W), device="cuda", generator=g)
     feat = torch.randn((B, 64, H, W), device="cuda", generator=g)
     h32 = torch.full((B, 16, H, W, 4), float("nan"), device="cuda")
-    hx = torch.empty((B, H, W, 64), device="cuda", dtype=torch.bfloat16)
-    fx = torch.empty((B, H, W, 64), device="cuda", dtype=torch.bfloat16)
+    hx = torch.empty((B, H, W, 64), device="cuda", dtype=torch.float16)
+    fx = torch.empty((B, H, W, 64), device="cuda", dtype=torch.float16)
     check(lib.bvml_stage_inputs(_p(h0), _p(feat), B, H, W, _p(h32), _p(hx), _p(fx),
                                 _stream(torch.device("cuda"))))
     torch.cuda.synchronize()
     assert torch.equal(h32, h0.reshape(B, 16, 4, H, W).permute(0, 1, 3, 4, 2))
-    assert torch.equal(hx, h0.permute(0, 2, 3, 1).to(torch.bfloat16))
-    assert torch.equal(fx, feat.permute(0, 2, 3, 1).to(torch.bfloat16))
+    assert torch.equal(hx, h0.permute(0, 2, 3, 1).to(torch.float16))
+    assert torch.equal(fx, feat.permute(0, 2, 3, 1).to(torch.float16))
