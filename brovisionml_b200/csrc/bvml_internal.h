@@ -1,6 +1,7 @@
 // Internal launcher interface between the C ABI (capi.cu) and the kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 
@@ -66,6 +67,7 @@ struct UpsampleLaunch {
     int B, h, w;
     int crop_t, crop_l, out_h, out_w;
     double fu, cu, fv, cv;  // GRID intrinsics; the full-res ray uses 8x these
+    int* status;         // optional: bit 2 set if a staging wait gave up
 };
 cudaError_t launch_upsample(const UpsampleLaunch& L, cudaStream_t s);
 
@@ -118,6 +120,11 @@ struct HeadTailLaunch {
     int* err;
 };
 cudaError_t launch_head_tail(const HeadTailLaunch& L, cudaStream_t s);
+
+// Encode a tiled TMA tensor map (defined in conv_tc.cu).
+bool tma_encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
+                const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapDataType dt,
+                CUtensorMapSwizzle sw);
 
 cudaError_t launch_ray_relu(void* normal, SType t, const float* ray, int B, int H, int W,
                             cudaStream_t s);

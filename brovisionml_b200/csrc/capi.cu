@@ -257,6 +257,7 @@ int refine_entry(bool act, const void* normal0, const float* ray8, const void* c
     U.cu = cu;
     U.fv = fv;
     U.cv = cv;
+    U.status = sync + 1;
     cudaError_t e = bvml::launch_upsample(U, s);
     if (e != cudaSuccess) return finish(e, "refine: upsample launch");
     if ((e = probe(launch_no++, s)) != cudaSuccess)

@@ -1108,30 +1108,11 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
 }
 
 // ------------------------------------------------------------------- host side
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
 bool encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
             const cuuint64_t* strides_bytes, const cuuint32_t* box,
             CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
             CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B) {
-    auto fn = encode_fn();
-    if (!fn) return false;
-    cuuint32_t estr[4] = {1, 1, 1, 1};
-    return fn(m, dt, rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return tma_encode(m, base, rank, dims, strides_bytes, box, dt, sw);
 }
 
 template <int N, int MT, int EPI, int ACT, bool BRES>
@@ -1236,6 +1217,28 @@ int plan_conv(ConvArgs& a, int n, int& mt, bool bres, int out_bytes) {
 }
 
 }  // namespace
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda); false when the driver lacks it or refuses the map.
+bool tma_encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
+                const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapDataType dt,
+                CUtensorMapSwizzle sw) {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    if (!fn) return false;
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    return fn(m, dt, rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     if (L.B == 0 || L.H == 0 || L.W == 0 || L.cout_pad == 0) return cudaSuccess;

@@ -16,22 +16,29 @@
 // writes them with 16-byte stores. The pair's 3x3 source normals (27 float2)
 // stay in registers for all 64 sub-pixels.
 //
-// Logit staging: when the grid width is a multiple of 16 bytes of storage,
-// each warp copies, for every (ky, kx), the 9 logit strips of its own row
-// (9 planes x 64 columns) global -> shared with 16-byte cp.async into a
-// warp-private ring kN stages deep. Stages go in groups of kSP: one warp
-// barrier publishes a group, and the kSP sub-pixels of a group are computed
-// together so that their independent dependency chains interleave (the kernel
-// is otherwise bound by fixed-latency waits at 4 warps per scheduler). The
-// bytes in flight do not cost registers. Other widths read the logits
-// straight from global memory.
+// Logit staging (grid width a multiple of 16 bytes of storage): the 9 logit
+// strips of a warp's row for one (ky, kx) -- planes t*64 + ky*8 + kx, t < 9,
+// 64 columns -- are one box of a 4-D tensor map (columns, rows, sub-pixel
+// plane, frame * 9 + tap), copied by one TMA load into a warp-private ring
+// slot and counted on that slot's mbarrier. kN stages per ring (kN divides
+// 8, so every slot index is a compile-time constant); one lane keeps kN - kSP
+// stages in flight and refills a group's slots once the warp has read them.
+// Stages are consumed in groups of kSP so that the sub-pixels of a group,
+// independent dependency chains, interleave. The mbarrier waits are bounded;
+// one that gives up records it in the status word (when one is given) and the
+// kernel carries on without hanging. Other widths read the logits straight
+// from global memory.
 //
 // The softmax denominator is folded into the normalise: with e_t = exp(l_t -
 // max l), normalise(sum_t (e_t/S) n_t) = a / max(|a|, 1e-12 S) for
 // a = sum_t e_t n_t, which is the reference's x / max(|x|, eps) exactly in
-// real arithmetic.
+// real arithmetic. Since 1 <= S <= 9, the clamp can only act when
+// |a|^2 < 8.1e-23; a sub-pixel that close is flagged, and a run with a
+// flagged sub-pixel is recomputed with S summed before it is stored (one
+// warp vote per 16-byte run instead of a branch per sub-pixel).
 #include "bvml_common.cuh"
 #include "bvml_internal.h"
+#include "tc_common.cuh"
 
 namespace bvml {
 namespace {
@@ -39,29 +46,20 @@ namespace {
 constexpr int kUTW = 64;        // grid columns per tile (32 pairs = one warp)
 constexpr int kUTH = 8;         // grid rows per tile (one per warp)
 constexpr int kUThreads = 256;
+constexpr uint32_t kUpWaitLimit = 1u << 22;
 
+// The TMA ring of one warp: kN stages of 9 x 64 logits.
 template <typename TS>
-struct UpStages {
-    static constexpr int kEpc = 16 / (int)sizeof(TS);             // elements per chunk
-    static constexpr int kCpr = kUTW / kEpc;                      // chunks per strip
-    static constexpr int kChunksW = 9 * kCpr;                     // per warp per stage
-    static constexpr int kElemsW = 9 * kUTW;                      // per warp per stage
-    static constexpr int kSP = sizeof(TS) == 2 ? 2 : 1;           // stages per group
-    static constexpr int kN = sizeof(TS) == 2 ? 6 : 4;            // ring depth
-    static constexpr int kG = kN / kSP;                           // groups in the ring
-    static_assert(kN % kSP == 0 && 8 % kSP == 0, "stage groups must tile the ring and a row");
-    static constexpr size_t kBytes = (size_t)(kUThreads / 32) * kN * kElemsW * sizeof(TS);
+struct UpRing {
+    static constexpr int kN = sizeof(TS) == 2 ? 8 : 4;          // stages (divides 8)
+    static constexpr int kSP = sizeof(TS) == 2 ? 2 : 1;         // stages per group
+    static constexpr int kElems = 9 * kUTW;                     // elements per stage
+    static constexpr uint32_t kBytes = kElems * sizeof(TS);     // a multiple of 128
+    static constexpr size_t kWarpBytes = (size_t)kN * kBytes;
+    static constexpr size_t kSmem = (kUThreads / 32) * (kWarpBytes + 8 * kN);
+    static_assert(8 % kN == 0 && kN % kSP == 0, "slots must tile a sub-row");
+    static_assert(kBytes % 128 == 0, "stage size keeps every slot 128-byte aligned");
 };
-
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
-    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem),
-                 "r"(valid ? 16 : 0)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
 // Logits of a pixel pair in storage form: half2 for fp16 storage (their max is
 // taken packed, exactly, before any conversion), float2 for fp32.
@@ -85,46 +83,13 @@ template <> struct Logit<__half> {
     __device__ __forceinline__ static float2 f(T v) { return __half22float2(v); }
 };
 
-// A lane's share of one stage: chunks q = lane + 32 m (m < kPerLane) of the
-// 9 x kCpr chunk grid. Because 32 is a multiple of kCpr, a lane keeps one
-// column cc for all its chunks and its plane advances by 32 / kCpr per m, so
-// only a base offset, a column validity flag and a plane stride are kept.
-template <typename TS>
-struct LaneChunks {
-    using U = UpStages<TS>;
-    static constexpr int kPerLane = (U::kChunksW + 31) / 32;
-    static constexpr int kTStep = 32 / U::kCpr;   // planes between a lane's chunks
-    int off0;       // element offset of chunk m = 0 from the stage's plane-0 row
-    int doff0;      // its offset inside a warp slot
-    int tstep_hw;   // 64 * kTStep * hw: source distance between consecutive m
-    int nlast;      // chunks this lane has (kPerLane or kPerLane - 1)
-    bool col_ok;    // the lane's column lies inside the frame
-    __device__ void init(int lane, int ncols, long hw) {
-        const int t0 = lane / U::kCpr, cc = lane % U::kCpr;
-        off0 = t0 * 64 * (int)hw + cc * U::kEpc;
-        doff0 = t0 * kUTW + cc * U::kEpc;
-        tstep_hw = 64 * kTStep * (int)hw;
-        nlast = (lane + 32 * (kPerLane - 1) < U::kChunksW) ? kPerLane : kPerLane - 1;
-        col_ok = cc * U::kEpc < ncols;
-    }
-    // copy the lane's chunks of the stage whose plane-0 row starts at `src`
-    __device__ __forceinline__ void issue(TS* slot, const TS* src) const {
-        const TS* p = src + off0;
-#pragma unroll
-        for (int m = 0; m < kPerLane; ++m) {
-            if (m < nlast)
-                cp_async16(slot + doff0 + m * kTStep * kUTW, col_ok ? p : src, col_ok);
-            p += tstep_hw;
-        }
-    }
-};
-
 struct UpArgs {
     int B, h, w, tiles_x, tiles_y;
     long hw;
     int crop_t, crop_l, out_h, out_w;
     bool vec_out;                   // 16-byte aligned output runs
     float ifu8, ifv8, tu8_c, tv8_c; // full-res ray: ((X+0.5)-8cu)/(8fu) = X*ifu8 + tu8_c
+    int* status;                    // nonzero after a staging wait gave up (may be null)
 };
 
 // Packs two fp32 results into one 32-bit storage word for TS = half; for
@@ -139,42 +104,192 @@ template <> struct OutRun<__half> {
     float ev[3][2];      // the even sub-column's results, until the odd one packs them
 };
 
-template <typename TNI, typename TS, bool NORM, bool RR, bool STAGED>
+constexpr float kL2E = 1.4426950408889634f;
+
+// One sub-pixel of a pixel pair from its 9 logits: softmax-weighted combine of
+// the 3x3 normals N, then (NORM) the L2 normalise, (RR) the full-res RayReLU.
+// EXACT sums S and applies the 1e-12 S clamp; otherwise the result is a / |a|
+// and `tiny` is raised where the clamp could act.
+template <typename TS, bool NORM, bool RR, bool EXACT>
+__device__ __forceinline__ void subpixel(const typename Logit<TS>::T (&l)[9],
+                                         const float2 (&N)[9][3], const UpArgs& a, int x,
+                                         int y, int ky, int kx, float2& ox, float2& oy,
+                                         float2& oz, bool& tiny) {
+    using L = Logit<TS>;
+    const float2 m = L::f(L::mx(L::mx(L::mx(l[0], l[1]), L::mx(l[2], l[3])),
+                                L::mx(L::mx(l[4], l[5]), L::mx(L::mx(l[6], l[7]), l[8]))));
+    const float2 mo = mul2(m, f2(-kL2E));
+    float2 ax = f2(0.f), ay = f2(0.f), az = f2(0.f);
+    // softmax weights up to the factor 1/S (e_t = exp(l_t - max l))
+    auto ew = [&](int tp) { return ex2_ftz2(fma2(L::f(l[tp]), f2(kL2E), mo)); };
+#pragma unroll
+    for (int tp = 0; tp < 9; ++tp) {
+        const float2 e = ew(tp);
+        ax = fma2(e, N[tp][0], ax);
+        ay = fma2(e, N[tp][1], ay);
+        az = fma2(e, N[tp][2], az);
+    }
+    if (NORM) {
+        // x / max(|x|, 1e-12) for x = a / S; with 1 <= S <= 9 the clamp can
+        // only act when |a| < 9e-12
+        float2 l2 = fma2(ax, ax, fma2(ay, ay, mul2(az, az)));
+        if constexpr (EXACT) {
+            float2 S = ew(0);
+#pragma unroll
+            for (int tp = 1; tp < 9; ++tp) S = add2(S, ew(tp));
+            const float2 se = mul2(S, f2(1e-12f));
+            l2 = max2(l2, mul2(se, se));
+        } else {
+            tiny |= (l2.x < 8.1e-23f) | (l2.y < 8.1e-23f);
+        }
+        const float2 inv = rsqrt2(l2);
+        ox = mul2(ax, inv);
+        oy = mul2(ay, inv);
+        oz = mul2(az, inv);
+    } else {
+        float2 S = ew(0);
+#pragma unroll
+        for (int tp = 1; tp < 9; ++tp) S = add2(S, ew(tp));
+        const float2 inv = f2(__frcp_rn(S.x), __frcp_rn(S.y));
+        ox = mul2(ax, inv);
+        oy = mul2(ay, inv);
+        oz = mul2(az, inv);
+    }
+    if (RR) {
+        // full-res ray at (8y+ky, 8x+kx) and (8y+ky, 8x+8+kx)
+        const float X0 = (float)(8 * x + kx);
+        float2 rx = f2(fmaf(X0, a.ifu8, a.tu8_c), fmaf(X0 + 8.0f, a.ifu8, a.tu8_c));
+        float2 ry = f2(fmaf((float)(8 * y + ky), a.ifv8, a.tv8_c));
+        const float2 ri = rsqrt2(fma2(rx, rx, fma2(ry, ry, f2(1.0f))));
+        rx = mul2(rx, ri);
+        ry = mul2(ry, ri);
+        const float2 rz = ri;
+        const float2 nn2 = fma2(ox, ox, fma2(oy, oy, mul2(oz, oz)));
+        const float2 c = mul2(fma2(ox, rx, fma2(oy, ry, mul2(oz, rz))),
+                              rsqrt2(max2(nn2, f2(1e-16f))));
+        const float2 dc = max2(fma2(c, f2(-1.0f), f2(kRayEps)), f2(0.0f));
+        ox = fma2(rx, dc, ox);
+        oy = fma2(ry, dc, oy);
+        oz = fma2(rz, dc, oz);
+        const float2 inv = rsqrt2(max2(fma2(ox, ox, fma2(oy, oy, mul2(oz, oz))), f2(1e-24f)));
+        ox = mul2(ox, inv);
+        oy = mul2(oy, inv);
+        oz = mul2(oz, inv);
+    }
+}
+
+// Collect sub-column kx of a sub-row into the pixels' 16-byte runs.
+template <typename TS>
+__device__ __forceinline__ void collect(OutRun<TS>& run, int kx, float2 ox, float2 oy, float2 oz) {
+    const float o[3][2] = {{ox.x, ox.y}, {oy.x, oy.y}, {oz.x, oz.y}};
+    if constexpr (sizeof(TS) == 2) {
+        // half pairs (kx even, kx odd) per pixel, one packed conversion each
+        // once the odd sub-column is done
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                if ((kx & 1) == 0)
+                    run.ev[c][e] = o[c][e];
+                else
+                    run.v[c][e][kx >> 1] = __floats2half2_rn(run.ev[c][e], o[c][e]);
+            }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) run.v[c][e][kx & 3] = o[c][e];
+    }
+}
+
+// Store the pair's completed runs of output row Yo (kx: the run's last
+// sub-column), cropped.
+template <typename TS>
+__device__ __forceinline__ void store_run(const OutRun<TS>& run, int kx, TS* __restrict__ out,
+                                          const UpArgs& a, int b, int x, int Yo) {
+    TS* orow = out + (long)b * 3 * a.out_h * a.out_w + (long)Yo * a.out_w;
+    if constexpr (sizeof(TS) == 2) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int X = 8 * (x + e) - a.crop_l;  // first column of the run
+                TS* dst = orow + (long)c * a.out_h * a.out_w + X;
+                if (e == 1 && x + 1 >= a.w) continue;
+                if (a.vec_out && X >= 0 && X + 8 <= a.out_w) {
+                    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(&run.v[c][e][0]);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const __half hv = (k & 1) ? run.v[c][e][k >> 1].y : run.v[c][e][k >> 1].x;
+                        if (X + k >= 0 && X + k < a.out_w) dst[k] = hv;
+                    }
+                }
+            }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int X = 8 * (x + e) + (kx & 4) - a.crop_l;
+                TS* dst = orow + (long)c * a.out_h * a.out_w + X;
+                if (e == 1 && x + 1 >= a.w) continue;
+                if (a.vec_out && X >= 0 && X + 4 <= a.out_w) {
+                    *reinterpret_cast<float4*>(dst) = make_float4(run.v[c][e][0], run.v[c][e][1],
+                                                                  run.v[c][e][2], run.v[c][e][3]);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (X + k >= 0 && X + k < a.out_w) dst[k] = run.v[c][e][k];
+                }
+            }
+    }
+}
+
+template <typename TNI, typename TS, bool NORM, bool RR, bool TMA>
 __global__ void __launch_bounds__(kUThreads, 2)
 upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __restrict__ out,
-                const UpArgs a) {
-    using U = UpStages<TS>;
-    extern __shared__ float4 up_smem[];
-    TS* ring = reinterpret_cast<TS*>(up_smem) + (threadIdx.x >> 5) * U::kN * U::kElemsW;
+                const UpArgs a, const __grid_constant__ CUtensorMap mmap) {
+    using U = UpRing<TS>;
+    using L = Logit<TS>;
+    constexpr int kRun = sizeof(TS) == 2 ? 8 : 4;  // sub-columns per 16-byte run
+    extern __shared__ __align__(128) unsigned char up_smem[];
     int t = blockIdx.x;
     const int tix = t % a.tiles_x;
     t /= a.tiles_x;
     const int tiy = t % a.tiles_y;
     const int b = t / a.tiles_y;
-    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int x0 = tix * kUTW, y0 = tiy * kUTH;
-    const int y = y0 + (threadIdx.x >> 5);
+    const int y = y0 + warp;
     const int x = x0 + 2 * lane;
-    const bool active = y < a.h && x < a.w;
-    // only warp barriers below: a warp past the last row, or (unstaged) a
-    // lane past the last column, can leave now
-    if (y >= a.h || (!STAGED && !active)) return;
+    const bool active = x < a.w;
+    // only warp barriers and warp votes below: a warp past the last row can
+    // leave now; every lane of a row computes (lanes past the last column on
+    // clamped, zero-filled data) and stores only its own columns
+    if (y >= a.h) return;
     const long hw = a.hw;
-    const TS* mframe = mask + (long)b * 576 * hw;
-    const TS* mrow = mframe + (long)y * a.w + x0;  // plane 0 of this warp's row
-    LaneChunks<TS> lc;
-    const TS* mnext = mrow;                         // plane-0 row of the next stage to copy
-    if (STAGED) {
-        lc.init(lane, a.w - x0, hw);
+
+    TS* ring = reinterpret_cast<TS*>(up_smem + warp * U::kWarpBytes);
+    const uint32_t bar0 =
+        tc::smem_u32(up_smem + (kUThreads / 32) * U::kWarpBytes) + 8 * U::kN * warp;
+    bool failed = false;
+    auto issue = [&](int k) {  // lane 0: stage k (= ky * 8 + kx) into slot k % kN
+        const int s = k % U::kN;
+        tc::mbar_expect_tx(bar0 + 8 * s, U::kBytes);
+        tc::tma_load_4d(tc::smem_u32(ring + s * U::kElems), &mmap, bar0 + 8 * s, x0, y, k, b * 9);
+    };
+    if constexpr (TMA) {
+        if (lane == 0) {
 #pragma unroll
-        for (int s = 0; s < U::kN - U::kSP; ++s) {  // the first kG-1 groups
-            lc.issue(ring + s * U::kElemsW, mnext);
-            mnext += hw;
-            if (s % U::kSP == U::kSP - 1) cp_async_commit();
+            for (int s = 0; s < U::kN; ++s) tc::mbar_init(bar0 + 8 * s, 1);
+            tc::mbar_fence_init();
+#pragma unroll
+            for (int k = 0; k < U::kN - U::kSP; ++k) issue(k);
         }
+        __syncwarp();
     }
     const bool vec = (a.w & 1) == 0;   // pairs start at even offsets: 8/4-byte aligned
-    const int yc = min(y, a.h - 1);
     const int xc = vec ? min(x, a.w - 2) : min(x, a.w - 1);
     const int x1 = min(xc + 1, a.w - 1);
 
@@ -183,7 +298,7 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
     float2 N[9][3];
 #pragma unroll
     for (int ty = 0; ty < 3; ++ty) {
-        const long row = (long)clampi(yc + ty - 1, 0, a.h - 1) * a.w;
+        const long row = (long)clampi(y + ty - 1, 0, a.h - 1) * a.w;
 #pragma unroll
         for (int tx = 0; tx < 3; ++tx) {
             const long c0 = row + clampi(xc + tx - 1, 0, a.w - 1);
@@ -194,43 +309,45 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
         }
     }
 
-    const TS* mb = mframe + (long)yc * a.w + xc;
+    const TS* mb = mask + (long)b * 576 * hw + (long)y * a.w + xc;
     const long d1 = x1 - xc;
-    constexpr float kL2E = 1.4426950408889634f;
-    using L = Logit<TS>;
     const int so = 2 * lane;  // pair offset in a staged strip
-    int rslot = 0;            // ring slot of the first stage of the group being computed
 
 #pragma unroll 1
     for (int ky = 0; ky < 8; ++ky) {
         const int Yo = 8 * y + ky - a.crop_t;
         const bool row_in = Yo >= 0 && Yo < a.out_h;
         OutRun<TS> run;
+        bool tiny = false;
 #pragma unroll
         for (int kg = 0; kg < 8 / U::kSP; ++kg) {
             typename L::T lg[U::kSP][9];
-            if (STAGED) {
+            if constexpr (TMA) {
                 const int k = ky * 8 + kg * U::kSP;  // first stage of the group
-                cp_async_wait<U::kG - 2>();
-                __syncwarp();  // group visible to the warp; every lane done with the previous one
-                // the group kG-1 ahead goes to the slots of the previous group
-                // (slot counters wrap instead of taking k % kN)
-                const int islot = rslot == 0 ? U::kN - U::kSP : rslot - U::kSP;
-                if (k + U::kN - U::kSP < 64) {
 #pragma unroll
-                    for (int e = 0; e < U::kSP; ++e) {
-                        lc.issue(ring + (islot + e) * U::kElemsW, mnext);
-                        mnext += hw;
+                for (int e = 0; e < U::kSP; ++e) {
+                    const int s = (kg * U::kSP + e) % U::kN;
+                    const uint32_t parity = ((k + e) / U::kN) & 1;
+                    if (!failed && !tc::mbar_wait(bar0 + 8 * s, parity, kUpWaitLimit)) {
+                        failed = true;
+                        if (lane == 0 && a.status) atomicOr(a.status, 2);
                     }
                 }
-                cp_async_commit();
-                const TS* st = ring + rslot * U::kElemsW + so;
-                rslot = rslot == U::kN - U::kSP ? 0 : rslot + U::kSP;
+                __syncwarp();  // every lane done with the previous group's slots
+                if (lane == 0) {
+                    // the previous group's slots get the stages kN - kSP ahead
+                    // (every lane's loads from them were consumed by the
+                    // previous group's arithmetic, so they have completed)
 #pragma unroll
-                for (int e = 0; e < U::kSP; ++e)
+                    for (int e = 0; e < U::kSP; ++e)
+                        if (k + e + U::kN - U::kSP < 64) issue(k + e + U::kN - U::kSP);
+                }
 #pragma unroll
-                    for (int tp = 0; tp < 9; ++tp)
-                        lg[e][tp] = L::lds(st + e * U::kElemsW + tp * kUTW);
+                for (int e = 0; e < U::kSP; ++e) {
+                    const TS* st = ring + ((kg * U::kSP + e) % U::kN) * U::kElems + so;
+#pragma unroll
+                    for (int tp = 0; tp < 9; ++tp) lg[e][tp] = L::lds(st + tp * kUTW);
+                }
             } else {
 #pragma unroll
                 for (int e = 0; e < U::kSP; ++e)
@@ -239,158 +356,66 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
                         lg[e][tp] = L::ldg(mb + (long)(tp * 64 + ky * 8 + kg * U::kSP + e) * hw,
                                            d1, vec);
             }
-            if (!active) continue;  // staged mode: idle lanes only keep the warp barriers
 #pragma unroll
             for (int sg = 0; sg < U::kSP; ++sg) {
                 const int kx = kg * U::kSP + sg;
-                const typename L::T* l = lg[sg];
-                const float2 m =
-                    L::f(L::mx(L::mx(L::mx(l[0], l[1]), L::mx(l[2], l[3])),
-                               L::mx(L::mx(l[4], l[5]), L::mx(L::mx(l[6], l[7]), l[8]))));
-                const float2 mo = mul2(m, f2(-kL2E));
-                float2 ax = f2(0.f), ay = f2(0.f), az = f2(0.f);
-                // softmax weights up to the factor 1/S (e_t = exp(l_t - max l))
-                auto ew = [&](int tp) { return ex2_ftz2(fma2(L::f(l[tp]), f2(kL2E), mo)); };
-#pragma unroll
-                for (int tp = 0; tp < 9; ++tp) {
-                    const float2 e = ew(tp);
-                    ax = fma2(e, N[tp][0], ax);
-                    ay = fma2(e, N[tp][1], ay);
-                    az = fma2(e, N[tp][2], az);
-                }
                 float2 ox, oy, oz;
-                if (NORM) {
-                    // x / max(|x|, 1e-12) for x = a / S; with 1 <= S <= 9 the clamp can
-                    // only act when |a| < 9e-12, so S is summed only then.
-                    float2 l2 = fma2(ax, ax, fma2(ay, ay, mul2(az, az)));
-                    if ((l2.x < 8.1e-23f) | (l2.y < 8.1e-23f)) {
-                        float2 S = ew(0);
-                        for (int tp = 1; tp < 9; ++tp) S = add2(S, ew(tp));
-                        const float2 se = mul2(S, f2(1e-12f));
-                        l2 = max2(l2, mul2(se, se));
-                    }
-                    const float2 inv = rsqrt2(l2);
-                    ox = mul2(ax, inv);
-                    oy = mul2(ay, inv);
-                    oz = mul2(az, inv);
-                } else {
-                    float2 S = ew(0);
+                subpixel<TS, NORM, RR, false>(lg[sg], N, a, x, y, ky, kx, ox, oy, oz, tiny);
+                collect<TS>(run, kx, ox, oy, oz);
+                if (kx % kRun == kRun - 1) {
+                    if (NORM && __any_sync(0xffffffffu, tiny)) {
+                        // rare: a sub-pixel of this run came within the clamp's
+                        // reach; recompute the run with S summed
 #pragma unroll
-                    for (int tp = 1; tp < 9; ++tp) S = add2(S, ew(tp));
-                    const float2 inv = f2(__frcp_rn(S.x), __frcp_rn(S.y));
-                    ox = mul2(ax, inv);
-                    oy = mul2(ay, inv);
-                    oz = mul2(az, inv);
-                }
-                if (RR) {
-                    // full-res ray at (8y+ky, 8x+kx) and (8y+ky, 8x+8+kx)
-                    const float X0 = (float)(8 * x + kx);
-                    float2 rx = f2(fmaf(X0, a.ifu8, a.tu8_c), fmaf(X0 + 8.0f, a.ifu8, a.tu8_c));
-                    float2 ry = f2(fmaf((float)(8 * y + ky), a.ifv8, a.tv8_c));
-                    const float2 ri = rsqrt2(fma2(rx, rx, fma2(ry, ry, f2(1.0f))));
-                    rx = mul2(rx, ri);
-                    ry = mul2(ry, ri);
-                    const float2 rz = ri;
-                    const float2 nn2 = fma2(ox, ox, fma2(oy, oy, mul2(oz, oz)));
-                    const float2 c = mul2(fma2(ox, rx, fma2(oy, ry, mul2(oz, rz))),
-                                          rsqrt2(max2(nn2, f2(1e-16f))));
-                    const float2 dc = max2(fma2(c, f2(-1.0f), f2(kRayEps)), f2(0.0f));
-                    ox = fma2(rx, dc, ox);
-                    oy = fma2(ry, dc, oy);
-                    oz = fma2(rz, dc, oz);
-                    const float2 inv =
-                        rsqrt2(max2(fma2(ox, ox, fma2(oy, oy, mul2(oz, oz))), f2(1e-24f)));
-                    ox = mul2(ox, inv);
-                    oy = mul2(oy, inv);
-                    oz = mul2(oz, inv);
-                }
-                // collect; flush a 16-byte run per channel and pixel when complete
-                if constexpr (sizeof(TS) == 2) {
-                    // half pairs (kx even, kx odd) per pixel, one packed
-                    // conversion each once the odd sub-column is done
-                    const float o[3][2] = {{ox.x, ox.y}, {oy.x, oy.y}, {oz.x, oz.y}};
+                        for (int k2 = kx + 1 - kRun; k2 <= kx; ++k2) {
+                            typename L::T l2[9];
 #pragma unroll
-                    for (int c = 0; c < 3; ++c)
-#pragma unroll
-                        for (int e = 0; e < 2; ++e) {
-                            if ((kx & 1) == 0)
-                                run.ev[c][e] = o[c][e];
-                            else
-                                run.v[c][e][kx >> 1] = __floats2half2_rn(run.ev[c][e], o[c][e]);
+                            for (int tp = 0; tp < 9; ++tp)
+                                l2[tp] = L::ldg(mb + (long)(tp * 64 + ky * 8 + k2) * hw, d1, vec);
+                            bool unused = false;
+                            subpixel<TS, NORM, RR, true>(l2, N, a, x, y, ky, k2, ox, oy, oz,
+                                                         unused);
+                            collect<TS>(run, k2, ox, oy, oz);
                         }
-                    if (kx == 7 && row_in && active) {
-                        TS* orow = out + (long)b * 3 * a.out_h * a.out_w + (long)Yo * a.out_w;
-#pragma unroll
-                        for (int c = 0; c < 3; ++c)
-#pragma unroll
-                            for (int e = 0; e < 2; ++e) {
-                                const int X = 8 * (x + e) - a.crop_l;  // first column of the run
-                                TS* dst = orow + (long)c * a.out_h * a.out_w + X;
-                                if (e == 1 && x + 1 >= a.w) continue;
-                                if (a.vec_out && X >= 0 && X + 8 <= a.out_w) {
-                                    *reinterpret_cast<uint4*>(dst) =
-                                        *reinterpret_cast<const uint4*>(&run.v[c][e][0]);
-                                } else {
-#pragma unroll
-                                    for (int k = 0; k < 8; ++k) {
-                                        const __half hv = (k & 1) ? run.v[c][e][k >> 1].y
-                                                                  : run.v[c][e][k >> 1].x;
-                                        if (X + k >= 0 && X + k < a.out_w) dst[k] = hv;
-                                    }
-                                }
-                            }
+                        tiny = false;
                     }
-                } else {
-                    const float o[3][2] = {{ox.x, ox.y}, {oy.x, oy.y}, {oz.x, oz.y}};
-#pragma unroll
-                    for (int c = 0; c < 3; ++c)
-#pragma unroll
-                        for (int e = 0; e < 2; ++e) run.v[c][e][kx & 3] = o[c][e];
-                    if ((kx & 3) == 3 && row_in && active) {
-                        TS* orow = out + (long)b * 3 * a.out_h * a.out_w + (long)Yo * a.out_w;
-#pragma unroll
-                        for (int c = 0; c < 3; ++c)
-#pragma unroll
-                            for (int e = 0; e < 2; ++e) {
-                                const int X = 8 * (x + e) + (kx & 4) - a.crop_l;
-                                TS* dst = orow + (long)c * a.out_h * a.out_w + X;
-                                if (e == 1 && x + 1 >= a.w) continue;
-                                if (a.vec_out && X >= 0 && X + 4 <= a.out_w) {
-                                    *reinterpret_cast<float4*>(dst) =
-                                        make_float4(run.v[c][e][0], run.v[c][e][1], run.v[c][e][2],
-                                                    run.v[c][e][3]);
-                                } else {
-#pragma unroll
-                                    for (int k = 0; k < 4; ++k)
-                                        if (X + k >= 0 && X + k < a.out_w) dst[k] = run.v[c][e][k];
-                                }
-                            }
-                    }
+                    if (row_in && active) store_run<TS>(run, kx, out, a, b, x, Yo);
                 }
             }
         }
     }
-    if (STAGED) cp_async_wait<0>();
 }
 
 template <typename TNI, typename TS, bool NORM, bool RR>
 cudaError_t launch_t(const UpsampleLaunch& L, const UpArgs& a, cudaStream_t s) {
     const long blocks = (long)a.tiles_x * a.tiles_y * a.B;
     if (blocks > 0x7fffffffL) return cudaErrorInvalidConfiguration;
-    if (a.w % UpStages<TS>::kEpc == 0) {
-        auto kern = upsample_kernel<TNI, TS, NORM, RR, true>;
-        const size_t smem = UpStages<TS>::kBytes;
-        cudaError_t e =
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        kern<<<(unsigned)blocks, kUThreads, smem, s>>>(static_cast<const TNI*>(L.n),
-                                                      static_cast<const TS*>(L.mask),
-                                                      static_cast<TS*>(L.out), a);
-    } else {
-        upsample_kernel<TNI, TS, NORM, RR, false><<<(unsigned)blocks, kUThreads, 0, s>>>(
-            static_cast<const TNI*>(L.n), static_cast<const TS*>(L.mask),
-            static_cast<TS*>(L.out), a);
+    CUtensorMap m{};
+    // staged: the mask as a 4-D tensor (w, h, 64 sub-pixel planes, B * 9
+    // taps; the frame stride is 9 tap strides); rows a multiple of 16 bytes
+    if ((a.w * (int)sizeof(TS)) % 16 == 0 && (long)L.B * 9 < 0x7fffffffL) {
+        const cuuint64_t dims[4] = {(cuuint64_t)a.w, (cuuint64_t)a.h, 64, (cuuint64_t)L.B * 9};
+        const cuuint64_t str[3] = {(cuuint64_t)a.w * sizeof(TS), (cuuint64_t)a.hw * sizeof(TS),
+                                   (cuuint64_t)a.hw * 64 * sizeof(TS)};
+        const cuuint32_t box[4] = {kUTW, 1, 1, 9};
+        if (tma_encode(&m, L.mask, 4, dims, str, box,
+                       sizeof(TS) == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                       CU_TENSOR_MAP_SWIZZLE_NONE)) {
+            auto kern = upsample_kernel<TNI, TS, NORM, RR, true>;
+            const size_t smem = UpRing<TS>::kSmem;
+            cudaError_t e =
+                cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            kern<<<(unsigned)blocks, kUThreads, smem, s>>>(static_cast<const TNI*>(L.n),
+                                                          static_cast<const TS*>(L.mask),
+                                                          static_cast<TS*>(L.out), a, m);
+            return cudaGetLastError();
+        }
     }
+    upsample_kernel<TNI, TS, NORM, RR, false><<<(unsigned)blocks, kUThreads, 0, s>>>(
+        static_cast<const TNI*>(L.n), static_cast<const TS*>(L.mask), static_cast<TS*>(L.out), a,
+        m);
     return cudaGetLastError();
 }
 
@@ -425,6 +450,7 @@ cudaError_t launch_upsample(const UpsampleLaunch& L, cudaStream_t s) {
     a.ifv8 = (float)(1.0 / (8.0 * L.fv));
     a.tu8_c = (float)((0.5 - 8.0 * L.cu) / (8.0 * L.fu));
     a.tv8_c = (float)((0.5 - 8.0 * L.cv) / (8.0 * L.fv));
+    a.status = L.status;
     if (L.st == SType::F32) {
         if (L.n_t != SType::F32) return cudaErrorInvalidValue;
         return launch_flags<float, float>(L, a, s);
