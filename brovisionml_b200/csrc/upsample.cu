@@ -52,7 +52,7 @@ constexpr uint32_t kUpWaitLimit = 1u << 22;
 template <typename TS>
 struct UpRing {
     static constexpr int kN = sizeof(TS) == 2 ? 8 : 4;          // stages (divides 8)
-    static constexpr int kSP = sizeof(TS) == 2 ? 2 : 1;         // stages per group
+    static constexpr int kSP = sizeof(TS) == 2 ? 4 : 1;         // stages per group
     static constexpr int kElems = 9 * kUTW;                     // elements per stage
     static constexpr uint32_t kBytes = kElems * sizeof(TS);     // a multiple of 128
     static constexpr size_t kWarpBytes = (size_t)kN * kBytes;
