@@ -1024,11 +1024,17 @@ __device__ __forceinline__ void st_release_gpu(int* p, int v) {
 template <int PS, int DIL, typename TS, bool ACT>
 __global__ void __launch_bounds__(kThreads, (StagedCfg<PS, DIL, TS>::kMinBlocks))
 angmf_iters_kernel(const float* __restrict__ ray, const AngmfArgs a, const AngmfIters J) {
+    // Three round trips per item are spread over three warps so that their
+    // latencies overlap instead of adding up ahead of a CTA barrier: warp 2
+    // claims the next item (its atomic issued at the start, its result stored
+    // only at the end), warp 1 polls the dependencies, warp 7 publishes the
+    // completion.
+    constexpr int kClaim = 64, kPoll = 32, kSignal = kThreads - 32;
     __shared__ int s_item[2];
     const int tid = threadIdx.x;
     const int per_it = a.tiles_x * a.tiles_y * a.B;
     const int total = per_it * (J.iters - J.first);
-    if (tid == 0) s_item[0] = atomicAdd(J.counter, 1);
+    if (tid == kClaim) s_item[0] = atomicAdd(J.counter, 1);
     __syncthreads();
     int item = s_item[0];
     int par = 0;
@@ -1040,11 +1046,12 @@ angmf_iters_kernel(const float* __restrict__ ray, const AngmfArgs a, const Angmf
         const int ty = t % a.tiles_y;
         const int b = t / a.tiles_y;
         int* mine = J.done + ((long)b * a.tiles_y + ty) * a.tiles_x + tx;
-        // the next item, read by every thread after this item's first barrier
-        if (tid == 0) s_item[par ^ 1] = atomicAdd(J.counter, 1);
+        int next = 0;
+        if (tid == kClaim) next = atomicAdd(J.counter, 1);
         auto pre = [&] {
-            if (it > J.first && tid < 9) {
-                const int nx = tx + tid % 3 - 1, ny = ty + tid / 3 - 1;
+            const int q = tid - kPoll;
+            if (it > J.first && q >= 0 && q < 9) {
+                const int nx = tx + q % 3 - 1, ny = ty + q / 3 - 1;
                 if (nx >= 0 && nx < a.tiles_x && ny >= 0 && ny < a.tiles_y) {
                     const int* f = J.done + ((long)b * a.tiles_y + ny) * a.tiles_x + nx;
                     // bounded; once any wait has given up, the others stop too
@@ -1072,11 +1079,11 @@ angmf_iters_kernel(const float* __restrict__ ray, const AngmfArgs a, const Angmf
                 J.buf[(it - 1) & 1], static_cast<const TS*>(J.prob[it]),
                 static_cast<const TS*>(J.xy[it]), static_cast<const TS*>(J.ang[it]), ray, o, a,
                 b, tx * kTW, ty * kTH, pre);
-        __syncthreads();  // every output of the tile stored (and the halo no longer read)
-        if (tid == 0) {
-            __threadfence();
-            st_release_gpu(mine, it - J.first + 1);
-        }
+        if (tid == kClaim) s_item[par ^ 1] = next;
+        // every output of the tile stored (and the halo no longer read); the
+        // release store is cumulative over the stores ordered before the barrier
+        __syncthreads();
+        if (tid == kSignal) st_release_gpu(mine, it - J.first + 1);
         item = s_item[par ^ 1];
         par ^= 1;
     }
