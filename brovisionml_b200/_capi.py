@@ -22,7 +22,9 @@ EXPORTS = ("bvml_last_error", "bvml_abi_version", "bvml_ray_relu", "bvml_angmf_p
            "bvml_refine_workspace_bytes", "bvml_refine", "bvml_probe_events",
            "bvml_refine_noalloc", "bvml_angmf_propagate_logits", "bvml_refine_logits",
            "bvml_conv2d_nhwc_f16", "bvml_conv2d_nhwc_f16_ex", "bvml_stage_inputs",
-           "bvml_head_tail_1x1", "bvml_refine_status", "bvml_probe_recorded")
+           "bvml_head_tail_1x1", "bvml_refine_status", "bvml_probe_recorded",
+           "bvml_refiner_weight_name", "bvml_refiner_weight_shape", "bvml_refiner_create",
+           "bvml_refiner_forward", "bvml_refiner_status", "bvml_refiner_destroy")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(
@@ -93,6 +95,20 @@ lib.bvml_probe_recorded.restype = _i
 lib.bvml_probe_recorded.argtypes = []
 lib.bvml_refine_status.restype = _i
 lib.bvml_refine_status.argtypes = [_vp, _vp]
+REFINER_WEIGHTS = 30
+lib.bvml_refiner_weight_name.restype = ctypes.c_char_p
+lib.bvml_refiner_weight_name.argtypes = [_i]
+lib.bvml_refiner_weight_shape.restype = _i
+lib.bvml_refiner_weight_shape.argtypes = [_i, ctypes.POINTER(_i)]
+lib.bvml_refiner_create.restype = _i
+lib.bvml_refiner_create.argtypes = [ctypes.POINTER(_vp), _i, ctypes.POINTER(_vp)]
+lib.bvml_refiner_forward.restype = _i
+lib.bvml_refiner_forward.argtypes = ([_vp, _vp, _vp, _vp] + [_i] * 3 + [ctypes.POINTER(ctypes.c_float)]
+                                     + [_i] * 8 + [_vp, _vp])
+lib.bvml_refiner_status.restype = _i
+lib.bvml_refiner_status.argtypes = [_vp, _vp]
+lib.bvml_refiner_destroy.restype = None
+lib.bvml_refiner_destroy.argtypes = [_vp]
 
 
 def abi_version() -> int:

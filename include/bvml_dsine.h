@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define BVML_ABI_VERSION 4
+#define BVML_ABI_VERSION 5
 
 enum bvml_dtype { BVML_F32 = 0, BVML_F16 = 1 };
 
@@ -332,6 +332,41 @@ int bvml_head_tail_1x1(const void* x, int x_c, int cin_off, const void* w2, cons
  */
 int bvml_stage_inputs(const float* h0, const float* feat, int B, int H, int W, float* h32,
                       void* hx, void* fx, void* stream);
+
+/*
+ * The whole learned refinement of Refiner::forward (src/dsine_refine.cpp:
+ * 212-294) for C / C++ hosts that run no Python: an opaque handle holding the
+ * refine stage's weights packed once for the tensor cores, and a forward that
+ * runs `iters` iterations of the ConvGRU + the four prediction heads
+ * (src/dsine_refine.cpp:95-158, 245-276) on the tensor cores and then the
+ * fused refine ops on the heads' raw outputs (as bvml_refine_logits), on the
+ * caller's stream. The same sequence and packing as the Python
+ * brovisionml_b200.refiner.Refiner, with bit-identical results.
+ *   weights: host fp32 arrays in the reference's OIHW layout, in the order of
+ *     bvml_refiner_weight_name(0 .. BVML_REFINER_WEIGHTS - 1) (the reference's
+ *     safetensors names, gru.convz.weight ... up_prob_head.4.bias) with the
+ *     shapes bvml_refiner_weight_shape gives (biases: shape[1..3] = 0).
+ *   normal (B,3,h,w), feature and hidden (B,64,h,w): the decoder's outputs,
+ *     fp32 on the handle's device; intrins = raw (fx, fy, cx, cy) of the
+ *     padded origH x origW image (src/dsine_refine.cpp:230-237);
+ *     crop (crop_t, crop_l, out_h, out_w) in the 8x output (the
+ *     DsineTransform's pad_t, pad_l, orig_h, orig_w); out (B,3,out_h,out_w)
+ *     in dtype (the storage of the head outputs and of the result).
+ * Buffers for a shape are allocated (cudaMalloc) on its first forward and
+ * reused; bvml_refiner_status synchronises the stream and reports whether a
+ * tensor-core pipeline or a persistent AngMF wait gave up.
+ */
+#define BVML_REFINER_WEIGHTS 30
+typedef struct bvml_refiner bvml_refiner;
+const char* bvml_refiner_weight_name(int i);
+int bvml_refiner_weight_shape(int i, int* shape4);
+int bvml_refiner_create(const float* const* weights, int device, bvml_refiner** out);
+int bvml_refiner_forward(bvml_refiner* r, const float* normal, const float* feature,
+                         const float* hidden, int B, int h, int w, const float* intrins,
+                         int origH, int origW, int iters, int crop_t, int crop_l, int out_h,
+                         int out_w, int dtype, void* out, void* stream);
+int bvml_refiner_status(bvml_refiner* r, void* stream);
+void bvml_refiner_destroy(bvml_refiner* r);
 
 /*
  * Profiling aid (no reference counterpart): arm `n` caller-created CUDA events
