@@ -255,3 +255,70 @@ def refine_frame_banded(frame: HostFrame, out_host: torch.Tensor, fu: float, cu:
                            f"{timeout} s; bands not finished: {pending}")
     if failures:
         raise BandFailure(sorted(failures, key=lambda f: f[0]))
+
+
+# ------------------------------------------------ the whole refinement, banded
+
+def plan_refine_bands(h: int, n_bands: int, iters: int, ps: int = 5, dil: int = 1):
+    """Exact-halo row bands of an h-row grid for the whole learned refinement
+    (sharding.refine_halo_rows)."""
+    from .sharding import plan_bands, refine_halo_rows
+
+    bands = plan_bands(h, max(1, min(n_bands, h)), refine_halo_rows(iters, ps, dil))
+    return [b for b in bands if b.own1 > b.own0]
+
+
+def band_inputs(intrins, origH: int, band):
+    """The band's raw intrinsics and padded image height: the band is an
+    image of 8 * rows padded rows whose principal point is 8 * comp0 pixels
+    higher (the grid intrinsics then follow src/dsine_refine.cpp:230-237 as
+    for a whole frame)."""
+    fx, fy, cx, cy = (float(v) for v in intrins)
+    return (fx, fy, cx, cy - 8.0 * band.comp0), 8 * band.rows
+
+
+def refine_frame_banded_full(normal: torch.Tensor, feature: torch.Tensor, hidden: torch.Tensor,
+                             intrins, origH: int, origW: int, out: torch.Tensor, *,
+                             n_bands: int, run_band, iters: int = 5, ps: int = 5,
+                             dil: int = 1) -> None:
+    """The whole learned refinement of ONE frame as exact-halo row bands.
+
+    normal (3,h,w), feature and hidden (64,h,w): the decoder's outputs for
+    the frame (host or device); out (3, 8h, 8w): the refined normals. Band k
+    computes grid rows [comp0, comp1) -- its owned rows plus
+    sharding.refine_halo_rows on each side, clipped to the frame -- and keeps
+    its owned output rows, so the stitched frame equals the whole-frame
+    refinement (the convolutions' zero padding and AngMF's replicate padding
+    apply only at the true frame edges; inside, the halo rows carry real data
+    and the rows the band edge contaminates are exactly the halo). This
+    replaces the reference's resolution cap for large frames
+    (src/dsine.cpp:117-141: downscale, run, upsample, renormalise).
+
+    run_band(normal, feature, hidden, intrins, origH, origW, crop) refines one
+    band, given as (1,C,rows,w) slices with the band's intrinsics, and
+    returns its (1, 3, out_h, 8w) output for crop = (top, 0, out_h, 8w);
+    banded_refiner() gives the runner for brovisionml_b200.refiner.Refiner on
+    one or more GPUs."""
+    _, h, w = normal.shape
+    for b in plan_refine_bands(h, n_bands, iters, ps, dil):
+        rows = lambda t: t[None, :, b.comp0:b.comp1]  # noqa: E731
+        intr_b, origH_b = band_inputs(intrins, origH, b)
+        res = run_band(rows(normal), rows(feature), rows(hidden), intr_b, origH_b, origW,
+                       (8 * b.crop_top, 0, 8 * (b.own1 - b.own0), 8 * w))
+        out[:, 8 * b.own0:8 * b.own1].copy_(res[0])
+
+
+def banded_refiner(refiners, out_dtype: torch.dtype = torch.float32):
+    """A run_band for refine_frame_banded_full over Refiner instances (one
+    per device, each loaded and moved with .to(device)); bands go to the
+    devices in turn."""
+    state = {"k": 0}
+
+    def run_band(normal, feature, hidden, intr, origH, origW, crop):
+        r = refiners[state["k"] % len(refiners)]
+        state["k"] += 1
+        dev = r.device
+        t = lambda x: x.to(dev, torch.float32).contiguous()  # noqa: E731
+        return r.forward(t(normal), t(feature), t(hidden), intr, origH, origW, crop=crop,
+                         out_dtype=out_dtype)
+    return run_band

@@ -293,19 +293,22 @@ class RefineStage:
             raise RuntimeError(f"dsine cuda: refine stage: pipeline gave up (code {code})")
 
 
-def reference_stage(params, h0, feat, uv, iters: int, *, emulate_f16: bool = True):
-    """Plain PyTorch fp32 restatement of the same computation (the reference's
-    formulas, src/dsine_refine.cpp:118-158), for tests. With emulate_f16 the
-    weights and the activations between layers are rounded to fp16 exactly
-    where RefineStage rounds them, so the two differ only in summation
-    order."""
+def reference_stage(params, h0, feat, uv, iters: int, *, emulate_f16: bool = True,
+                    dtype: torch.dtype = torch.float32):
+    """Plain PyTorch restatement of the same computation (the reference's
+    formulas, src/dsine_refine.cpp:118-158), for tests, in fp32 (or `dtype`,
+    e.g. float64 where a test needs results independent of summation order).
+    With emulate_f16 the weights and the activations between layers are
+    rounded to fp16 exactly where RefineStage rounds them, so the two differ
+    only in summation order."""
     F = torch.nn.functional
-    q16 = (lambda t: t.to(torch.float16).float()) if emulate_f16 else (lambda t: t)
-    W = {k: (q16(v) if k.endswith("weight") else v.float()) for k, v in params.items()}
+    q16 = (lambda t: t.to(torch.float16).to(dtype)) if emulate_f16 else (lambda t: t)
+    W = {k: (q16(v.to(dtype)) if k.endswith("weight") else v.to(dtype))
+         for k, v in params.items()}
     B = h0.shape[0]
-    uvb = uv[None].expand(B, -1, -1, -1).float()
-    h = h0.float()
-    feat = feat.float()
+    uvb = uv[None].expand(B, -1, -1, -1).to(dtype)
+    h = h0.to(dtype)
+    feat = feat.to(dtype)
     outs = []
     for _ in range(iters):
         hx = q16(torch.cat([h, feat, uvb], 1))

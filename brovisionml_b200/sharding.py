@@ -53,8 +53,32 @@ def plan_frames(B: int, world: int) -> list[tuple[int, int]]:
 
 
 def halo_rows(iters: int, ps: int, dil: int, upsample: bool = True) -> int:
-    """Grid rows of halo a band needs per side for an exact result."""
+    """Grid rows of halo a band needs per side for an exact result of the
+    refine OPS (given head outputs)."""
     return iters * (ps // 2) * dil + (1 if upsample else 0)
+
+
+def refine_halo_rows(iters: int, ps: int = 5, dil: int = 1, upsample: bool = True) -> int:
+    """Grid rows of halo a band needs per side for an exact result of the
+    WHOLE learned refinement (ConvGRU + heads + ops), from the decoder's
+    normal, feature and hidden state.
+
+    With R = (ps // 2) * dil and n = 1 (the upsample's 3x3) or 0: iteration
+    i's normals are needed n + (I - i) R rows out; AngMF reads the iteration's
+    head outputs at its own pixel only, and the heads' 3x3 reads the hidden
+    state h_i one row further; h_i at a row reads h_(i-1) four rows out (z and
+    r: 5x5 over h; q: 5x5 over r * h), so
+        need(h_I) = n + 1,  need(h_i) = max(n + (I - i) R + 1, need(h_(i+1)) + 4);
+    the decoder's hidden state and feature (through the hoisted 5x5 terms of
+    z, r and q) are read need(h_1) + 4 rows out, its normal n + I R rows out."""
+    n = 1 if upsample else 0
+    R = (ps // 2) * dil
+    if iters <= 0:
+        return n
+    need = n + 1
+    for i in range(iters - 1, 0, -1):
+        need = max(n + (iters - i) * R + 1, need + 4)
+    return max(need + 4, n + iters * R)
 
 
 @dataclass(frozen=True)
