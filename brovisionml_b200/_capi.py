@@ -77,7 +77,8 @@ class ConvEpilogue(ctypes.Structure):
     _fields_ = [("mode", _i), ("act", _i), ("out", _vp), ("out_c", _i), ("out_off", _i),
                 ("h32", _vp), ("z", _vp), ("rh", _vp), ("rh_c", _i), ("hx", _vp), ("hx_c", _i),
                 ("hin", _vp), ("hin_c", _i), ("add", _vp), ("add_c", _i), ("add_shared", _i),
-                ("xin", _vp), ("xin_c", _i), ("wx", _vp), ("xin_stride", _i)]
+                ("xin", _vp), ("xin_c", _i), ("wx", _vp), ("xin_stride", _i),
+                ("wait_limit", ctypes.c_uint)]
 
 
 EPI_NHWC, EPI_PLANAR_F16, EPI_PLANAR_F32, EPI_GRU_ZR, EPI_GRU_Q, EPI_C4_F32, EPI_SPLIT_F16 = \

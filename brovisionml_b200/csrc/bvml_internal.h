@@ -80,6 +80,7 @@ struct ConvLaunch {
     const void* w;       // (ks*ks, cout_pad, cin_pad) fp16
     const float* bias;   // (cout) fp32
     int* err;            // device int: nonzero if a pipeline wait gave up
+    uint32_t wait_limit; // attempts of a pipeline wait before it gives up (0: 1 << 22)
     int B, H, W, x_c, cin_off, cin_pad, cout, cout_pad, ks;
     ConvEpi epi;
     int act;             // NHWC: 0 none, 1 ReLU, 2 sigmoid, 3 tanh; C4_32: 0, 1
@@ -118,6 +119,7 @@ struct HeadTailLaunch {
     int f16;
     void* y;
     int* err;
+    uint32_t wait_limit;  // as ConvLaunch::wait_limit
 };
 cudaError_t launch_head_tail(const HeadTailLaunch& L, cudaStream_t s);
 

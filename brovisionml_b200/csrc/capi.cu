@@ -453,6 +453,7 @@ int bvml_conv2d_nhwc_f16_ex(const void* x, int x_c, int cin_off, int cin_pad, co
     L.xin_c = epi->xin_c;
     L.wx = epi->wx;
     L.xin_stride = epi->xin_stride;
+    L.wait_limit = epi->wait_limit;
     if (epi->xin && (!epi->wx || !a16(epi->xin) || !a16(epi->wx) || epi->xin_c <= 0 ||
                      epi->xin_c % 64 || epi->xin_stride < 0 || epi->xin_stride % 8 ||
                      (epi->xin_stride && epi->xin_stride < epi->xin_c)))

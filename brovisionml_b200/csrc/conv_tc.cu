@@ -25,7 +25,9 @@
 //    (NHWC and planar outputs through per-warp shared-memory staging and TMA
 //    stores; the GRU tensors in coalesced channel-group layouts).
 // All waits are bounded (tc_common.cuh); a wait that gives up sets *err and
-// the CTA tears down after its copies and MMAs in flight have completed.
+// the CTA tears down after its copies and MMAs in flight have completed. The
+// pipeline waits' bound is a launch argument (ConvLaunch::wait_limit, default
+// kWaitLimit); the teardown waits for work already in flight keep kWaitLimit.
 #include <cuda_fp16.h>
 
 #include <mutex>
@@ -53,6 +55,7 @@ struct ConvArgs {
     const float* bias;
     const float* bias1;  // head tail: the first layer's bias (128)
     int* err;
+    uint32_t wait_limit;  // attempts of a pipeline wait before it gives up (mbar_wait_pipe)
     // epilogue targets (see ConvEpi)
     void* out;
     int out_c, out_off;
@@ -525,7 +528,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             for (int ch = 0; ok && ch < chunks; ++ch) {
                 for (int kx = 0; ok && kx < a.ks; ++kx) {
                     const int s = ga % a.s_a, j = ga / a.s_a;
-                    if (j > 0 && !tc::mbar_wait(bar_empty_a + 8 * s, (j - 1) & 1, kWaitLimit)) {
+                    if (j > 0 && !tc::mbar_wait_pipe(bar_empty_a + 8 * s, (j - 1) & 1, a.wait_limit)) {
                         fail(1);
                         ok = false;
                         break;
@@ -542,7 +545,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         for (int ky = 0; ky < a.ks; ++ky, ++gb) {
                             const int q = gb % a.s_b, jb = gb / a.s_b;
                             if (jb > 0 &&
-                                !tc::mbar_wait(bar_empty_b + 8 * q, (jb - 1) & 1, kWaitLimit)) {
+                                !tc::mbar_wait_pipe(bar_empty_b + 8 * q, (jb - 1) & 1, a.wait_limit)) {
                                 fail(1);
                                 ok = false;
                                 break;
@@ -559,7 +562,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 // through the same rings
                 for (int xc = 0; ok && xc < a.xchunks; ++xc) {
                     const int s = ga % a.s_a, j = ga / a.s_a;
-                    if (j > 0 && !tc::mbar_wait(bar_empty_a + 8 * s, (j - 1) & 1, kWaitLimit)) {
+                    if (j > 0 && !tc::mbar_wait_pipe(bar_empty_a + 8 * s, (j - 1) & 1, a.wait_limit)) {
                         fail(1);
                         ok = false;
                         break;
@@ -573,7 +576,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                                     y0, b);
                     ++ga;
                     const int q = gb % a.s_b, jb = gb / a.s_b;
-                    if (jb > 0 && !tc::mbar_wait(bar_empty_b + 8 * q, (jb - 1) & 1, kWaitLimit)) {
+                    if (jb > 0 && !tc::mbar_wait_pipe(bar_empty_b + 8 * q, (jb - 1) & 1, a.wait_limit)) {
                         fail(1);
                         ok = false;
                         break;
@@ -600,13 +603,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const uint32_t row_bytes = (uint32_t)a.tw * 128;  // one image row of an A entry
         int ga = 0, gb = 0, tl = 0;
         bool ok = true;
-        if (BRES && t0 < t_end && !tc::mbar_wait(bar_bres, 0, kWaitLimit)) {
+        if (BRES && t0 < t_end && !tc::mbar_wait_pipe(bar_bres, 0, a.wait_limit)) {
             fail(7);
             ok = false;
         }
         for (int t = t0; ok && t < t_end && !aborted(); t += dt, ++tl) {
             const int buf = tl & 1, u = tl >> 1;
-            if (u > 0 && !tc::mbar_wait(bar_acc_empty + 8 * buf, (u - 1) & 1, kWaitLimit)) {
+            if (u > 0 && !tc::mbar_wait_pipe(bar_acc_empty + 8 * buf, (u - 1) & 1, a.wait_limit)) {
                 fail(3);
                 break;
             }
@@ -616,7 +619,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             for (int ch = 0; ok && ch < chunks; ++ch) {
                 for (int kx = 0; ok && kx < a.ks; ++kx) {
                     const int s = ga % a.s_a, j = ga / a.s_a;
-                    if (!tc::mbar_wait(bar_full_a + 8 * s, j & 1, kWaitLimit) || aborted()) {
+                    if (!tc::mbar_wait_pipe(bar_full_a + 8 * s, j & 1, a.wait_limit) || aborted()) {
                         ok = false;
                         break;
                     }
@@ -629,7 +632,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                             sb = ring_b + ch * a.b_bytes;  // ks == 1
                         } else {
                             q = gb % a.s_b;
-                            if (!tc::mbar_wait(bar_full_b + 8 * q, (gb / a.s_b) & 1, kWaitLimit) ||
+                            if (!tc::mbar_wait_pipe(bar_full_b + 8 * q, (gb / a.s_b) & 1, a.wait_limit) ||
                                 aborted()) {
                                 ok = false;
                                 break;
@@ -661,14 +664,14 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             if constexpr (!BRES) {
                 for (int xc = 0; ok && xc < a.xchunks; ++xc) {  // extra K (no halo: ky = 0)
                     const int s = ga % a.s_a, j = ga / a.s_a;
-                    if (!tc::mbar_wait(bar_full_a + 8 * s, j & 1, kWaitLimit) || aborted()) {
+                    if (!tc::mbar_wait_pipe(bar_full_a + 8 * s, j & 1, a.wait_limit) || aborted()) {
                         ok = false;
                         break;
                     }
                     tc::tc_fence_after();
                     const uint32_t sa = sbase + s * a.a_bytes;
                     const int q = gb % a.s_b;
-                    if (!tc::mbar_wait(bar_full_b + 8 * q, (gb / a.s_b) & 1, kWaitLimit) ||
+                    if (!tc::mbar_wait_pipe(bar_full_b + 8 * q, (gb / a.s_b) & 1, a.wait_limit) ||
                         aborted()) {
                         ok = false;
                         break;
@@ -801,7 +804,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             tile_of(t, b, x0, y0, n0);
             float ta[32], tb[32];
             prefetch(0, ta);  // overlaps the wait for this tile's MMAs
-            const bool ok = tc::mbar_wait(bar_acc_full + 8 * buf, u & 1, kWaitLimit);
+            const bool ok = tc::mbar_wait_pipe(bar_acc_full + 8 * buf, u & 1, a.wait_limit);
             if (!ok) fail(6);
             if (!ok || aborted()) break;
             tc::tc_fence_after();
@@ -930,7 +933,7 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             tile_of(t, b, x0, y0);
             for (int ch = 0; ch < 2; ++ch, ++ga) {
                 const int s = ga % s_a, j = ga / s_a;
-                if (j > 0 && !tc::mbar_wait(bar_empty_a + 8 * s, (j - 1) & 1, kWaitLimit)) {
+                if (j > 0 && !tc::mbar_wait_pipe(bar_empty_a + 8 * s, (j - 1) & 1, a.wait_limit)) {
                     fail(1);
                     ok = false;
                     break;
@@ -947,13 +950,13 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         // --------------------------------------------------------------- MMA
         constexpr uint32_t idesc1 = tc::idesc_f16_f32(kTM, 128);
         constexpr uint32_t idesc2 = tc::idesc_f16_f32(kTM, 64);
-        bool ok = tc::mbar_wait(bar_wres, 0, kWaitLimit);
+        bool ok = tc::mbar_wait_pipe(bar_wres, 0, a.wait_limit);
         if (!ok) fail(7);
         // GEMM2 of tile j: intermediate j & 1 (2 chunks) x W4^T into acc2 j & 1
         auto gemm2 = [&](int j) {
             const int q = j & 1, v = j >> 1;
-            if (!tc::mbar_wait(bar_a2_full + 8 * q, v & 1, kWaitLimit) ||
-                (v > 0 && !tc::mbar_wait(bar_acc2_empty + 8 * q, (v - 1) & 1, kWaitLimit)) ||
+            if (!tc::mbar_wait_pipe(bar_a2_full + 8 * q, v & 1, a.wait_limit) ||
+                (v > 0 && !tc::mbar_wait_pipe(bar_acc2_empty + 8 * q, (v - 1) & 1, a.wait_limit)) ||
                 aborted())
                 return false;
             tc::tc_fence_after();
@@ -973,7 +976,7 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         int ga = 0, tl = 0;
         for (int t = blockIdx.x; ok && t < n_tiles && !aborted(); t += gridDim.x, ++tl) {
             const int buf = tl & 1, u = tl >> 1;
-            if (u > 0 && !tc::mbar_wait(bar_acc1_empty + 8 * buf, (u - 1) & 1, kWaitLimit)) {
+            if (u > 0 && !tc::mbar_wait_pipe(bar_acc1_empty + 8 * buf, (u - 1) & 1, a.wait_limit)) {
                 fail(3);
                 ok = false;
                 break;
@@ -982,7 +985,7 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             const uint32_t acc1 = tmem + buf * 128;
             for (int ch = 0; ch < 2; ++ch, ++ga) {
                 const int s = ga % s_a;
-                if (!tc::mbar_wait(bar_full_a + 8 * s, (ga / s_a) & 1, kWaitLimit) || aborted()) {
+                if (!tc::mbar_wait_pipe(bar_full_a + 8 * s, (ga / s_a) & 1, a.wait_limit) || aborted()) {
                     ok = false;
                     break;
                 }
@@ -1018,7 +1021,7 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         // bias, planar store
         auto e2 = [&](int j, int b, int x0, int y0) {
             const int q = j & 1;
-            if (!tc::mbar_wait(bar_acc2_full + 8 * q, (j >> 1) & 1, kWaitLimit)) {
+            if (!tc::mbar_wait_pipe(bar_acc2_full + 8 * q, (j >> 1) & 1, a.wait_limit)) {
                 fail(6);
                 return false;
             }
@@ -1049,7 +1052,7 @@ head_tail_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         bool ok = true;
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tl) {
             const int buf = tl & 1, u = tl >> 1;
-            if (!tc::mbar_wait(bar_acc1_full + 8 * buf, u & 1, kWaitLimit)) {
+            if (!tc::mbar_wait_pipe(bar_acc1_full + 8 * buf, u & 1, a.wait_limit)) {
                 fail(6);
                 ok = false;
                 break;
@@ -1254,6 +1257,7 @@ cudaError_t launch_conv_tc(const ConvLaunch& L, cudaStream_t s) {
     a.pad = L.ks / 2;
     a.bias = L.bias;
     a.err = L.err;
+    a.wait_limit = L.wait_limit ? L.wait_limit : kWaitLimit;
     a.out = L.y;
     a.out_c = L.out_c;
     a.out_off = L.out_off;
@@ -1405,6 +1409,7 @@ cudaError_t launch_head_tail(const HeadTailLaunch& L, cudaStream_t s) {
     a.bias = L.b4;
     a.bias1 = L.b2;
     a.err = L.err;
+    a.wait_limit = L.wait_limit ? L.wait_limit : kWaitLimit;
     a.out = L.y;
     // pixel tile: the tw with the fewest tiles (ties to the wider one)
     long best = -1;

@@ -62,6 +62,23 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
     return false;
 }
 
+// A pipeline wait with a caller-chosen bound: `limit` attempts, the first a
+// non-blocking test (so that limit = 1 gives up at once on a phase that has
+// not completed, whatever the hardware's try_wait suspend time), the rest
+// try_wait. Waits for copies and MMAs already in flight use mbar_wait with
+// a fixed large limit instead: a CTA must not exit before they land.
+__device__ __forceinline__ bool mbar_wait_pipe(uint32_t bar, uint32_t parity, uint32_t limit) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done || (limit > 1 && mbar_wait(bar, parity, limit - 1));
+}
+
 // ----------------------------------------------------------------------- TMA
 // Tiled tensor loads into this CTA's shared memory, completion counted on
 // `bar` in bytes. No cluster multicast.

@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define BVML_ABI_VERSION 5
+#define BVML_ABI_VERSION 6
 
 enum bvml_dtype { BVML_F32 = 0, BVML_F16 = 1 };
 
@@ -291,6 +291,13 @@ typedef struct {
     int xin_c;
     const void* wx;
     int xin_stride;
+    unsigned wait_limit; /* attempts of each pipeline wait (between the TMA,
+                            MMA and epilogue warps) before the kernel gives
+                            up, sets *err and ends; 0: the default, 1 << 22.
+                            The first attempt does not block, so 1 gives up
+                            at the first wait that is not already satisfied.
+                            The kernel still waits (with the default bound)
+                            for its copies and MMAs in flight before it ends. */
 } bvml_conv_epilogue;
 
 /*

@@ -31,7 +31,7 @@ def test_header_symbols_exported():
                          text=True, check=True).stdout
     exported = set(re.findall(r" T (bvml_\w+)", out))
     assert exported == set(syms)
-    assert b.abi_version() == 5
+    assert b.abi_version() == 6
 
 
 def test_bridge_library_exports_reference_signatures():

@@ -226,3 +226,49 @@ def test_head_tail_matches_two_convolutions(W, cout, f16):
     d = (got.float() - want.float()).abs().max().item()
     print(f"head tail W={W} cout={cout} f16={f16}: max |d| {d:.2e}")
     assert torch.equal(got, want)
+
+
+def test_conv_wait_limit_gives_up_then_next_launch_is_normal():
+    """bvml_conv_epilogue.wait_limit bounds every pipeline wait between the
+    TMA, MMA and epilogue warps. With 1 (a single non-blocking test) the MMA
+    lane's first wait for a tile's operands and the epilogue's first wait for
+    an accumulator come before any copy can have landed, so every CTA gives
+    up: the kernel sets err and ends, after waiting (with the default bound)
+    for the copies and MMAs it had in flight and freeing its TMEM. The next
+    launches on the same stream, with the default bound, are normal: err 0
+    and the same output, bit for bit, as the launch before the failure."""
+    import ctypes
+
+    import brovisionml_b200 as b
+    from brovisionml_b200._capi import EPI_NHWC, ConvEpilogue, check, lib
+    from brovisionml_b200.ops import _p, _stream
+
+    g = torch.Generator(device="cuda").manual_seed(81)
+    B, H, W, cin, cout, ks = 2, 64, 96, 128, 128, 5
+    x = torch.randn((B, H, W, cin), device="cuda", generator=g).to(torch.float16)
+    weight = torch.randn((cout, cin, ks, ks), device="cuda", generator=g) * (cin * ks * ks) ** -0.5
+    bias = torch.randn(cout, device="cuda", generator=g) * 0.1
+    wp = b.pack_conv_weight(weight, cin, cout)
+
+    def launch(limit):
+        y = torch.full((B, H, W, cout), float("nan"), device="cuda", dtype=torch.float16)
+        err = torch.zeros(1, device="cuda", dtype=torch.int32)
+        e = ConvEpilogue(mode=EPI_NHWC, act=1, out=_p(y), out_c=cout, out_off=0,
+                         wait_limit=limit)
+        check(lib.bvml_conv2d_nhwc_f16_ex(_p(x), cin, 0, cin, _p(wp), _p(bias), B, H, W, cout,
+                                           cout, ks, ctypes.byref(e), _p(err),
+                                           _stream(torch.device("cuda"))))
+        torch.cuda.synchronize()
+        return y, int(err.item())
+
+    y0, e0 = launch(0)
+    assert e0 == 0
+    ref = ref_conv(x, weight, bias, ks, "relu", cin)
+    assert ((y0.float() - ref).abs() - 8e-3 * ref.abs()).max().item() <= 2e-3
+    for _ in range(2):
+        _, e1 = launch(1)
+        print(f"wait_limit 1: err {e1}")
+        assert e1 != 0
+        y2, e2 = launch(0)
+        assert e2 == 0
+        assert torch.equal(y2, y0)
