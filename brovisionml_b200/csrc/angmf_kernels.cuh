@@ -246,9 +246,21 @@ template <int PS> struct P_OF { static constexpr int value = PS * PS; };
 
 template <typename Mask>
 struct PairAcc {
-    float2 x, y, z;   // prob-weighted sums of the clamped, rotated neighbours
+    float2 x, y, z;   // prob-weighted sums of the rotated neighbours (before the RayReLU)
+    float2 d;         // prob-weighted sum of the RayReLU coefficients dc
     Mask bad0, bad1;  // neighbours left to the exact fix-up, per pixel of the pair
 };
+
+// The RayReLU of neighbour k adds dc_k r to its rotated normal q_k, and r is
+// the output pixel's own ray, the same for every neighbour, so
+// sum_k w_k (q_k + dc_k r) = sum_k w_k q_k + (sum_k w_k dc_k) r: the loop
+// accumulates the two sums and this adds the second once per pixel.
+template <typename Mask>
+__device__ __forceinline__ void fold_ray(PairAcc<Mask>& A, float2 rx, float2 ry, float2 rz) {
+    A.x = fma2(A.d, rx, A.x);
+    A.y = fma2(A.d, ry, A.y);
+    A.z = fma2(A.d, rz, A.z);
+}
 
 // Flag one pixel's evaluation of neighbour slot `bit` for the exact fix-up:
 // when |dd| < kTau, |t| > tlim, l2 < kMMin or |th| > kThMax (unordered: any
@@ -321,14 +333,13 @@ __device__ __forceinline__ void flag_eval(float add, float at, float tlim, float
 // zero; a non-finite fast sum sends the pixel to a whole-window recompute.
 template <typename Mask, bool QRANGE, bool WDEN>
 __device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 th, float2 wt,
-                                           float2 nx, float2 ny, float2 nz, float2 tu,
+                                           float2 nx, float2 ny, float2 nz, float2 as,
                                            float2 tun, float2 tv, float2 ifu2, float2 ifv2,
                                            float2 rx, float2 ry, float2 rz, PairAcc<Mask>& A) {
     const float2 q = fma2(xs, xs, mul2(ys, ys));
     const float2 iq = rsqrt2_ftz(q);
     const float2 X = mul2(xs, ifu2), Y = mul2(ys, ifv2);     // d (unnormalised)
     const float2 e = fma2(X, nx, mul2(Y, ny));               // d.n
-    const float2 as = fma2(tu, nx, fma2(tv, ny, nz));        // P.n
     const float2 dd = fma2(iq, e, as);                       // (P + d).n, d normalised
     // g = d x P = (Y, -X, gz); g_perp = g - n (g.n) = (gpx, -gpyn, gpz)
     const float2 gz = fma2(X, tv, mul2(Y, tun));
@@ -359,13 +370,12 @@ __device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 t
     const float2 qx = fma2(kk, gpx, mul2(cs, nx));
     const float2 qy = fnma2(kk, gpyn, mul2(cs, ny));
     const float2 qz = fma2(kk, gpz, mul2(cs, nz));
-    // RayReLU against the pixels' rays, then the weighted sum
+    // RayReLU against the pixels' rays: m = q + dc r. q and r are unit
+    // vectors, so |m|^2 = 1 + 2 dc c + dc^2 = 1 + dc (2c + dc) (exactly 1 when
+    // dc = 0); m itself is never formed (fold_ray).
     const float2 c = fma2(qx, rx, fma2(qy, ry, mul2(qz, rz)));
     const float2 dc = max2(fma2(c, f2(-1.0f), f2(kRayEps)), f2(0.0f));
-    const float2 mx = fma2(rx, dc, qx);
-    const float2 my = fma2(ry, dc, qy);
-    const float2 mz = fma2(rz, dc, qz);
-    const float2 l2 = fma2(mx, mx, fma2(my, my, mul2(mz, mz)));
+    const float2 l2 = fma2(dc, fma2(c, f2(2.0f), dc), f2(1.0f));
     // w / |m|; with w = 1/d one rsqrt of |m|^2 d^2. d^2 overflows for weights
     // below ~5e-20: those go to the fix-up, whose fp64 weight keeps them
     // nonzero (they decide the direction where every weight is that small).
@@ -380,20 +390,24 @@ __device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 t
                             wm.x, A.bad0, Mask(1) << n);
     flag_eval<QRANGE, WDEN>(fabsf(dd.y), fabsf(t.y), tlim.y, l2.y, fabsf(th.y), q.y, lw.y,
                             wm.y, A.bad1, Mask(1) << n);
-    A.x = fma2(wm, mx, A.x);
-    A.y = fma2(wm, my, A.y);
-    A.z = fma2(wm, mz, A.z);
+    A.x = fma2(wm, qx, A.x);
+    A.y = fma2(wm, qy, A.y);
+    A.z = fma2(wm, qz, A.z);
+    A.d = fma2(wm, dc, A.d);
 }
 
 // The replicate-padded halo of unit source normals in shared memory. For each
 // component an "even" and an "odd" plane of float2 pairs,
 //   E[i][k] = (v[i][2k], v[i][2k+1]),  O[i][k] = (v[i][2k+1], v[i][2k+2]),
 // so the pair starting at column j is (j even ? E : O)[i][j >> 1]: a warp's
-// pairs for one neighbour slot are consecutive float2, conflict-free. tu0
-// (with its negation) and tv0 are tabulated the same way.
+// pairs for one neighbour slot are consecutive float2, conflict-free. A fourth
+// pair of planes holds P.n = tu0 nx + tv0 ny + nz of each source pixel (it
+// does not depend on the output pixel, so it is formed once per tile instead
+// of once per evaluation). tu0 (with its negation) and tv0 are tabulated the
+// same way.
 struct NTile {
-    float2* e[3];
-    float2* o[3];
+    float2* e[4];
+    float2* o[4];
     float4* tue;  // (tu0, tu1, -tu0, -tu1) of the pair starting at column 2k
     float4* tuo;  // ... at column 2k + 1
     float* tv;
@@ -402,14 +416,14 @@ struct NTile {
     static constexpr __host__ __device__ int pairs_per_row(int SW) { return SW / 2 + 1; }
     static constexpr __host__ __device__ size_t bytes(int SW, int SH) {
         const int h = pairs_per_row(SW);
-        return sizeof(float4) * 2 * h + sizeof(float2) * 6 * (size_t)SH * h + sizeof(float) * SH;
+        return sizeof(float4) * 2 * h + sizeof(float2) * 8 * (size_t)SH * h + sizeof(float) * SH;
     }
     __device__ void carve(void* base, int SW, int SH) {
         swh = pairs_per_row(SW);
         tue = reinterpret_cast<float4*>(base);
         tuo = tue + swh;
         float2* p = reinterpret_cast<float2*>(tuo + swh);
-        for (int c = 0; c < 3; ++c) {
+        for (int c = 0; c < 4; ++c) {
             e[c] = p;
             o[c] = p + SH * swh;
             p += 2 * SH * swh;
@@ -462,10 +476,12 @@ __device__ __forceinline__ void stage_normals(const TNI* __restrict__ pnb,
         if (FUSE_RR) ray_relu_f32(v[0], v[1], v[2], __ldg(ray + sp), __ldg(ray + HW + sp),
                                   __ldg(ray + 2 * HW + sp));
         stage_unit(v);
+        const float tu = fmaf((float)sx, a.ifu, a.tu_c), tv = fmaf((float)sy, a.ifv, a.tv_c);
+        const float u4[4] = {v[0], v[1], v[2], fmaf(tu, v[0], fmaf(tv, v[1], v[2]))};  // P.n
         const int k = j >> 1;
 #pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            const float u = v[c];
+        for (int c = 0; c < 4; ++c) {
+            const float u = u4[c];
             float* ep = reinterpret_cast<float*>(T.e[c] + i * T.swh + k);
             float* op = reinterpret_cast<float*>(T.o[c] + i * T.swh);
             if (j & 1) {
@@ -524,9 +540,15 @@ __device__ __forceinline__ void stage_normals_ct(const TNI* __restrict__ pnb,
         }
         stage_unit(v0);
         stage_unit(v1);
+        // P.n of both source pixels (the same tu0 / tv0 as the tables below)
+        const float tv = fmaf((float)clampi(y0 - R + i, 0, a.H - 1), a.ifv, a.tv_c);
+        const float tu0 = fmaf((float)clampi(sx, 0, a.W - 1), a.ifu, a.tu_c);
+        const float tu1 = fmaf((float)clampi(sx + 1, 0, a.W - 1), a.ifu, a.tu_c);
+        const float w0[4] = {v0[0], v0[1], v0[2], fmaf(tu0, v0[0], fmaf(tv, v0[1], v0[2]))};
+        const float w1[4] = {v1[0], v1[1], v1[2], fmaf(tu1, v1[0], fmaf(tv, v1[1], v1[2]))};
 #pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            const float u0 = v0[c], u1 = v1[c];
+        for (int c = 0; c < 4; ++c) {
+            const float u0 = w0[c], u1 = w1[c];
             T.e[c][i * SWH + k] = make_float2(u0, u1);     // E[i][k]
             float* op = reinterpret_cast<float*>(T.o[c] + i * SWH);
             op[2 * k] = u1;                                 // O[i][k].x
@@ -547,7 +569,7 @@ __device__ __forceinline__ void stage_normals_ct(const TNI* __restrict__ pnb,
 
 // The staged operands of the pair starting at column j of halo row i.
 struct NPair {
-    float2 nx, ny, nz, tu, tun, tv;
+    float2 nx, ny, nz, as, tun, tv;  // as = P.n
 };
 __device__ __forceinline__ NPair npair(const NTile& T, int i, int j) {
     const int k = i * T.swh + (j >> 1);
@@ -556,15 +578,15 @@ __device__ __forceinline__ NPair npair(const NTile& T, int i, int j) {
         r.nx = T.o[0][k];
         r.ny = T.o[1][k];
         r.nz = T.o[2][k];
+        r.as = T.o[3][k];
         const float4 t = T.tuo[j >> 1];
-        r.tu = f2(t.x, t.y);
         r.tun = f2(t.z, t.w);
     } else {
         r.nx = T.e[0][k];
         r.ny = T.e[1][k];
         r.nz = T.e[2][k];
+        r.as = T.e[3][k];
         const float4 t = T.tue[j >> 1];
-        r.tu = f2(t.x, t.y);
         r.tun = f2(t.z, t.w);
     }
     r.tv = f2(T.tv[i]);
@@ -732,7 +754,7 @@ angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* 
         return vec ? St<TS>::ld2s(base + p0) : f2(St<TS>::lds1(base + p0), St<TS>::lds1(base + p1));
     };
     const float2 ifu2 = f2(a.ifu), ifv2 = f2(a.ifv);
-    PairAcc<Mask> A{f2(0.f), f2(0.f), f2(0.f), 0, 0};
+    PairAcc<Mask> A{f2(0.f), f2(0.f), f2(0.f), f2(0.f), 0, 0};
 #pragma unroll 1
     for (int ky = 0; ky < PS; ++ky) {
         const int i = ly + ky * a.dil;
@@ -744,9 +766,10 @@ angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* 
             if (ACT) head_activation(wt, th);
             angmf_pair<Mask, sizeof(TS) == 4, ACT>(
                 n, ld(xyb + (long)n * HW), ld(xyb + (long)(P + n) * HW), th, wt, q.nx, q.ny,
-                q.nz, q.tu, q.tun, q.tv, ifu2, ifv2, rx, ry, rz, A);
+                q.nz, q.as, q.tun, q.tv, ifu2, ifv2, rx, ry, rz, A);
         }
     }
+    fold_ray(A, rx, ry, rz);
     finish_pair<PS, TS, TNI, TNO, FUSE_RR, ACT, false>(A, b, x, y, two, vec, pn, prob, xy, ang, ray,
                                                 out, a);
 }
@@ -891,7 +914,7 @@ __device__ __forceinline__ void angmf_tile(const TNI* __restrict__ pn,
     float2 rx, ry, rz;
     pair_ray(ray, HW, p0, p1, rx, ry, rz);
     const float2 ifu2 = f2(a.ifu), ifv2 = f2(a.ifv);
-    PairAcc<Mask> A{f2(0.f), f2(0.f), f2(0.f), 0, 0};
+    PairAcc<Mask> A{f2(0.f), f2(0.f), f2(0.f), f2(0.f), 0, 0};
     constexpr int kStrip = S::kRowsW * kTW;
     const TS* ring_lane = ring + (lane >> 4) * kTW + lx;   // this pair inside a slot
     const int pbase = ly * SWH + (lx >> 1);                // this pair's first window pair
@@ -929,32 +952,33 @@ __device__ __forceinline__ void angmf_tile(const TNI* __restrict__ pn,
                 // window column offset: a constant once the kx loop is unrolled
                 const int dj = kx * DIL;
                 const int pi = prow + (dj >> 1);
-                float2 nx, ny, nz, tu, tun;
+                float2 nx, ny, nz, as, tun;
                 if ((dj & 1) == 0) {
                     nx = T.e[0][pi];
                     ny = T.e[1][pi];
                     nz = T.e[2][pi];
+                    as = T.e[3][pi];
                     const float4 t4 = T.tue[(lx >> 1) + (dj >> 1)];
-                    tu = f2(t4.x, t4.y);
                     tun = f2(t4.z, t4.w);
                 } else {
                     nx = T.o[0][pi];
                     ny = T.o[1][pi];
                     nz = T.o[2][pi];
+                    as = T.o[3][pi];
                     const float4 t4 = T.tuo[(lx >> 1) + (dj >> 1)];
-                    tu = f2(t4.x, t4.y);
                     tun = f2(t4.z, t4.w);
                 }
                 float2 th = lds2<TS>(st + 3 * kStrip), wt = lds2<TS>(st);
                 if (ACT) head_activation(wt, th);
                 angmf_pair<Mask, sizeof(TS) == 4, ACT>(
                     n, lds2<TS>(st + 1 * kStrip), lds2<TS>(st + 2 * kStrip), th, wt, nx, ny, nz,
-                    tu, tun, tv, ifu2, ifv2, rx, ry, rz, A);
+                    as, tun, tv, ifu2, ifv2, rx, ry, rz, A);
             }
         }
     }
     cp_async_wait<0>();
     if (!active) return;
+    fold_ray(A, rx, ry, rz);
     finish_pair<PS, TS, TNI, TNO, FUSE_RR, ACT, COH>(A, b, x, y, two, true, pn, prob, xy, ang,
                                                      ray, out, a);
 }
