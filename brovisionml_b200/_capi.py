@@ -1,6 +1,6 @@
 """ctypes binding of libbvml_dsine.so (the C ABI in include/bvml_dsine.h).
 
-The library must have been built in-tree (``python -m brovisionml_b200.build``
+The library must have been built in-tree (``python brovisionml_b200/build.py``
 or ``__graft_entry__.build()``); a missing library is an ImportError, never a
 silent fallback.
 """
@@ -29,7 +29,7 @@ EXPORTS = ("bvml_last_error", "bvml_abi_version", "bvml_ray_relu", "bvml_angmf_p
 if not os.path.exists(LIB_PATH):
     raise ImportError(
         f"brovisionml_b200: CUDA library not built ({LIB_PATH} missing); run "
-        "`python -m brovisionml_b200.build` (nvcc for sm_100a)")
+        "`python brovisionml_b200/build.py` (nvcc for sm_100a)")
 
 lib = ctypes.CDLL(LIB_PATH)
 
