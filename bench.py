@@ -43,7 +43,9 @@ The JSON line carries, beyond the driver contract:
 
 ``--impl reference`` times the reference CPU implementation alone (rank 0;
 other ranks exit) with the same sampling routine and prints the same metric
-with "impl": "reference".
+with "impl": "reference"; on a GPU box its line also carries
+``reference_cuda``: the reference's own CUDA kernels (src/dsine_ops.cu,
+compiled unchanged) timed on the GPU for the same frame size.
 """
 from __future__ import annotations
 
@@ -313,7 +315,72 @@ def reference_arm(args, cfg):
         "e2e": {"value": round(value, 3), "unit": "Mpixel/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    line["reference_cuda"] = reference_cuda_leg(cfg)
     print(json.dumps(line), flush=True)
+
+
+REFGPU_LIB = os.path.join(ROOT, "oracle", "_ref", "libbvml_refgpu.so")
+
+
+def reference_cuda_leg(cfg, frames: int = 16, reps: int = 3):
+    """The reference's own CUDA kernels (src/dsine_ops.cu compiled unchanged
+    for sm_100a by oracle/Makefile) on this GPU, driven as Refiner::forward
+    drives them (src/dsine_refine.cpp:241-272): per frame ray_relu_cuda, then
+    `iters` x angmf_propagate_cuda, fp32 storage (the reference's only one),
+    legacy default stream, CUDA events. `frames` frames of the workload's
+    size; Mpixel/s in full-resolution output pixels like `value`, although
+    this GPU path has no upsample (brotensor's, absent). None of this
+    repository's kernels run here."""
+    if cfg["ps"] != 5 or cfg["dil"] != 1:
+        return {"unavailable": "the reference's CUDA kernel is 5x5, dilation 1 only"}
+    try:
+        import ctypes
+
+        import torch
+    except ImportError as e:  # pragma: no cover
+        return {"unavailable": f"torch: {e}"}
+    if not torch.cuda.is_available():
+        return {"unavailable": "no GPU"}
+    if not os.path.exists(REFGPU_LIB):
+        return {"unavailable": "oracle/_ref/libbvml_refgpu.so not built (needs the reference "
+                               "tree at build time)"}
+    lib = ctypes.CDLL(REFGPU_LIB)
+    lib.bvml_refgpu_unit.restype = ctypes.c_int
+    lib.bvml_refgpu_unit.argtypes = ([ctypes.c_void_p] * 5 + [ctypes.c_int] * 4 +
+                                     [ctypes.c_double] * 4 + [ctypes.c_void_p])
+    dev = torch.device("cuda", 0)
+    c = dict(cfg, f16=False)
+    inp = make_device_inputs(c, frames, 4242, dev, torch)
+    h, w, iters = inp["h"], inp["w"], cfg["iters"]
+    arr = lambda ts: (ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts])  # noqa: E731
+    prob, xy, ang = arr(inp["prob"]), arr(inp["xy"]), arr(inp["angle"])
+    out = torch.empty((frames, 3, h, w), device=dev)
+
+    def run():
+        rc = lib.bvml_refgpu_unit(inp["normal0"].data_ptr(), inp["ray8"].data_ptr(), prob, xy,
+                                  ang, iters, frames, h, w, inp["fu"], inp["cu"], inp["fv"],
+                                  inp["cv"], out.data_ptr())
+        if rc != 0:
+            raise RuntimeError("reference CUDA kernels failed")
+
+    stream = torch.cuda.default_stream(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            run()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            run()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / reps
+    return {"value": round(frames * cfg["H"] * cfg["W"] / (ms * 1e-3) / 1e6, 1),
+            "unit": "Mpixel/s", "ms_per_step": round(ms, 4), "frames": frames,
+            "storage": "f32", "device": torch.cuda.get_device_name(dev),
+            "what": "the reference's ray_relu_cuda + iters x angmf_propagate_cuda per frame "
+                    "(src/dsine_ops.cu, fp64 math, one thread per pixel); no upsample on "
+                    "this GPU path"}
 
 
 # ----------------------------------------------------------------- stage bench
