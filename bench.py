@@ -36,6 +36,10 @@ The JSON line carries, beyond the driver contract:
   e2e           the same metric through the host-buffer API
                 (brovisionml_b200.pipeline), pinned host inputs copied in and
                 the result copied out every step;
+  stage         (one GPU, 5x5 configs) the whole learned refinement of 64
+                frames: ConvGRU + heads on the tensor cores with random weights
+                of the reference's shapes, then the fused ops on their raw
+                outputs; executed TFLOP/s against the measured tensor peak;
   cpu_baseline  the reference's own CPU ops (oracle/_ref) on this host's
                 cores -- all cores and one thread -- on a bounded sample of
                 the same workload (rank 0, N=1), with the angular error of
@@ -412,19 +416,21 @@ def stage_executed_flops(iters: int, B: int, h: int, w: int) -> float:
     return float(once + (iters * it + mask) * px)
 
 
-def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
-    """--stage: a step is the whole refinement of B frames per GPU -- `iters`
-    iterations of ConvGRU + heads (brovisionml_b200.refine_stage) and the
-    fused ops on their raw outputs (refine(..., logits=True))."""
+def stage_measure(cfg, B, steps, warmup, device, seed, barrier, max_over_ranks):
+    """Time the whole learned refinement of B frames: RefineStage.start +
+    `iters` iterations of ConvGRU + heads (brovisionml_b200.refine_stage, random
+    weights of the reference's shapes) and the fused ops on their raw outputs
+    (refine(..., logits=True)); CUDA events per step. Returns the times (ms,
+    max over ranks) and the clock summary."""
     import torch
 
     import brovisionml_b200 as bv
     from brovisionml_b200.refine_stage import RefineStage, StageOutputs, random_params
 
-    B, H, W, I = cfg["B"], cfg["H"], cfg["W"], cfg["iters"]
+    H, W, I = cfg["H"], cfg["W"], cfg["iters"]
     h, w = H // 8, W // 8
     dt = torch.float16 if cfg["f16"] else torch.float32
-    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    g = torch.Generator(device=device).manual_seed(seed)
     h0 = torch.tanh(torch.randn((B, 64, h, w), device=device, generator=g))
     feat = torch.relu(torch.randn((B, 64, h, w), device=device, generator=g))
     fu, cu, fv, cv = grid_intrinsics(H, W)
@@ -452,16 +458,16 @@ def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
 
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
     with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup)):
+        for _ in range(max(3, warmup)):
             stage()
             ops()
         stream.synchronize()
         st.check_pipeline()
         barrier()
         torch.cuda.synchronize()
-        marks = [[ev(), ev(), ev()] for _ in range(args.steps)]
+        marks = [[ev(), ev(), ev()] for _ in range(steps)]
         with ClockSampler(device.index, gpu_uuid(torch, device)) as clk:
-            for k in range(args.steps):
+            for k in range(steps):
                 marks[k][0].record(stream)
                 stage()
                 marks[k][1].record(stream)
@@ -470,20 +476,59 @@ def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
             stream.synchronize()
         barrier()
         st.check_pipeline()
-    step_ms = max_over_ranks(sum(m[0].elapsed_time(m[2]) for m in marks) / args.steps)
-    stage_ms = max_over_ranks(sum(m[0].elapsed_time(m[1]) for m in marks) / args.steps)
-    ops_ms = max_over_ranks(sum(m[1].elapsed_time(m[2]) for m in marks) / args.steps)
+    return {
+        "step_ms": max_over_ranks(sum(m[0].elapsed_time(m[2]) for m in marks) / steps),
+        "stage_ms": max_over_ranks(sum(m[0].elapsed_time(m[1]) for m in marks) / steps),
+        "ops_ms": max_over_ranks(sum(m[1].elapsed_time(m[2]) for m in marks) / steps),
+        "clocks": clk.summary(),
+    }
+
+
+def tensor_peak():
+    """The measured sustained dense bf16 peak (fp16 runs at the same rate)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return (float(json.load(f)["bf16_tflops_sustained"]),
+                    "measured sustained (MEASURED_PEAKS.json bf16_tflops_sustained; dense fp16 "
+                    "runs at the bf16 rate)")
+    except Exception:
+        return 1400.0, "fallback sustained 1.4 PFLOP/s"
+
+
+def stage_key(cfg, B, steps, warmup, device):
+    """The whole learned refinement measured inside the default run (one GPU):
+    the tensor-core stage's executed TFLOP/s against the measured peak, the
+    ops on its raw outputs, Mpixel/s of the whole refinement."""
+    I = cfg["iters"]
+    h, w = cfg["H"] // 8, cfg["W"] // 8
+    t = stage_measure(cfg, B, steps, warmup, device, 1000, lambda: None, lambda v: v)
+    peak, _ = tensor_peak()
+    tf = stage_executed_flops(I, B, h, w) / (t["stage_ms"] * 1e-3) / 1e12
+    return {"what": "whole learned refinement: ConvGRU + 4 heads on the tensor cores (random "
+                    "weights of the reference's shapes) + the fused ops on their raw outputs",
+            "frames": B, "value": round(B * cfg["H"] * cfg["W"] / (t["step_ms"] * 1e-3) / 1e6, 1),
+            "unit": "Mpixel/s", "ms_per_step": round(t["step_ms"], 3),
+            "stage_ms": round(t["stage_ms"], 3), "ops_ms": round(t["ops_ms"], 3),
+            "tflops_executed": round(tf, 1), "tensor_frac": round(tf / peak, 4),
+            "tflops_model": round(stage_flops_per_px(I) * B * h * w /
+                                  (t["stage_ms"] * 1e-3) / 1e12, 1),
+            "steps": steps, "clocks": t["clocks"]}
+
+
+def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
+    """--stage: a step is the whole refinement of B frames per GPU -- `iters`
+    iterations of ConvGRU + heads (brovisionml_b200.refine_stage) and the
+    fused ops on their raw outputs (refine(..., logits=True))."""
+    B, H, W, I = cfg["B"], cfg["H"], cfg["W"], cfg["iters"]
+    h, w = H // 8, W // 8
+    t = stage_measure(cfg, B, args.steps, args.warmup, device, 1000 + rank, barrier,
+                      max_over_ranks)
+    step_ms, stage_ms, ops_ms = t["step_ms"], t["stage_ms"], t["ops_ms"]
     flops = stage_flops_per_px(I) * B * h * w
     tflops = flops / (stage_ms * 1e-3) / 1e12
     flops_x = stage_executed_flops(I, B, h, w)
     tflops_x = flops_x / (stage_ms * 1e-3) / 1e12
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peak = float(json.load(f)["bf16_tflops_sustained"])
-        peak_src = ("measured sustained (MEASURED_PEAKS.json bf16_tflops_sustained; dense fp16 "
-                    "runs at the bf16 rate)")
-    except Exception:
-        peak, peak_src = 1400.0, "fallback sustained 1.4 PFLOP/s"
+    peak, peak_src = tensor_peak()
     line = {
         "metric": "Mpixel/s of the DSINE refinement (ConvGRU + heads + refine ops)",
         "value": round(world * B * H * W / (step_ms * 1e-3) / 1e6, 1), "unit": "Mpixel/s",
@@ -508,7 +553,7 @@ def stage_bench(args, cfg, device, rank, world, barrier, max_over_ranks):
                      "frac": round(tflops_x / peak, 4), "peak_source": peak_src,
                      "flops": "executed (hoisted feature/uv terms counted once)",
                      "traffic": None},
-        "clocks": clk.summary(),
+        "clocks": t["clocks"],
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -743,6 +788,8 @@ def main():
     ap.add_argument("--no-bands", action="store_true", help="skip the config-3 band key")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-stage-key", action="store_true",
+                    help="skip the whole-learned-refinement key of the one-GPU run")
     ap.add_argument("--stage", action="store_true",
                     help="time the whole learned refinement: ConvGRU + heads on the tensor "
                          "cores (random weights of the reference's shapes), then the ops on "
@@ -756,6 +803,7 @@ def main():
     args = ap.parse_args()
     if args.logits or args.stage or args.stage_layers:
         args.no_e2e = args.no_cpu = args.no_bands = args.no_weak = True
+        args.no_stage_key = True
     args.steps = max(1, args.steps)
     cfg = dict(CONFIGS[args.config])
     if args.frames:
@@ -1019,6 +1067,15 @@ def unit_bench(args, cfg, device, rank, world, barrier, max_over_ranks, torch, b
                        "ms_per_step": round(e2e_s * 1e3, 2), "steps": e2e_steps,
                        "bytes": f"per rank (rank {rank}, {B} frames)",
                        "api": "brovisionml_b200.pipeline.HostRefiner (pinned host buffers)"}
+
+    # ------------------------------------- the whole learned refinement (f3)
+    if rank == 0 and world == 1 and not args.no_stage_key and cfg["ps"] == 5 and \
+            cfg["dil"] == 1:
+        try:
+            line["stage"] = stage_key(cfg, min(64, cfg["B"]), min(args.steps, 10), args.warmup,
+                                      device)
+        except Exception as e:  # reported, never required for the ops' number
+            line["stage"] = {"failed": str(e)[:300]}
 
     # ------------------------------------------------------------- CPU baseline
     if rank == 0 and world == 1 and not args.no_cpu:
