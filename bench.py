@@ -313,7 +313,10 @@ def reference_arm(args, cfg):
         "unit": "Mpixel/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded generators)",
-        "config": workload_config(args, cfg, 1, extra={"sample_frames_per_step": frames}),
+        "config": workload_config(args, cfg, int(os.environ.get("WORLD_SIZE", "1")),
+                                  extra={"sample_frames_per_step": frames,
+                                         "reference_ranks": "rank 0 alone on all host cores "
+                                                            "(the reference's CPU path)"}),
         "cpu_baseline": {"value": round(value, 3), "unit": "Mpixel/s", "cores": nthreads,
                          "kind": rs.kind, "sample": rs.sample_text(args.steps, secs)},
         "e2e": {"value": round(value, 3), "unit": "Mpixel/s", "h2d_bytes_per_step": 0,
