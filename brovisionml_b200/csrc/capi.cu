@@ -32,7 +32,12 @@ int fail(int code, const std::string& msg) {
     return code;
 }
 int einval(const std::string& msg) { return fail(BVML_EINVAL, "dsine ops: " + msg); }
+// A failed runtime call (an allocation that did not fit, a bad launch
+// configuration) also sets the thread's last-error state; it is read and
+// reset here so that the next call's launch checks do not report it again.
+// Sticky errors (a lost context) stay, as they must.
 int cuda_fail(cudaError_t e, const char* what) {
+    (void)cudaGetLastError();
     return fail(BVML_ECUDA, std::string("dsine cuda: ") + what + ": " + cudaGetErrorString(e));
 }
 int finish(cudaError_t e, const char* what) {

@@ -34,7 +34,10 @@ constexpr int kHeadOut[4] = {25, 50, 25, 576};  // prob, xy, angle, up-mask head
 constexpr const char* kHeadName[4] = {"prob_head", "xy_head", "angle_head", "up_prob_head"};
 
 int fail(int code, const std::string& msg) { return bvml::report_error(code, msg); }
+// Resets the thread's last-error state like capi.cu's cuda_fail, so that a
+// failed allocation does not resurface in the next forward's launch checks.
 int cuda_fail(cudaError_t e, const char* what) {
+    (void)cudaGetLastError();
     return fail(BVML_ECUDA, std::string("dsine cuda: refiner: ") + what + ": " +
                                 cudaGetErrorString(e));
 }

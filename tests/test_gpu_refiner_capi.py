@@ -121,3 +121,47 @@ def test_refiner_from_a_cpp_program(tmp_path):
     r.to(0)
     want = r.forward(normal, feat, hid, intr, H, W, out_dtype=torch.float16).float().cpu().numpy()
     assert np.array_equal(got, want)
+
+
+@pytest.mark.gpu
+def test_refiner_allocation_failure_is_reported_and_the_handle_recovers():
+    """Failure injection through the allocator, with no GPU fault: a forward
+    for 200 000 frames of 90 x 160 asks for a 369 GB first buffer, which
+    cudaMalloc refuses. The call must fail with BVML_ECUDA naming the allocation, and the
+    next forward on the same handle (a normal shape) must run and equal the
+    Python Refiner -- the refused allocation must not resurface in its launch
+    checks."""
+    from brovisionml_b200._capi import check, lib
+    from brovisionml_b200.refine_stage import random_params
+    from brovisionml_b200.refiner import Refiner
+
+    B, h, w = 1, 24, 40
+    H, W = 8 * h, 8 * w
+    intr = (0.8 * W, 0.8 * W, W / 2, H / 2)
+    normal, feat, hid = _inputs(B, h, w, seed=51)
+    params = random_params("cpu", seed=52)
+    keep, wptrs = _weights(params)
+    handle = ctypes.c_void_p()
+    check(lib.bvml_refiner_create(wptrs, 0, ctypes.byref(handle)))
+    try:
+        fi = (ctypes.c_float * 4)(*intr)
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        out = torch.empty((B, 3, H, W), device="cuda", dtype=torch.float16)
+        big = 200_000
+        rc = lib.bvml_refiner_forward(handle, normal.data_ptr(), feat.data_ptr(), hid.data_ptr(),
+                                      big, 90, 160, fi, 720, 1280, 5, 0, 0, 720, 1280, 1,
+                                      out.data_ptr(), stream)
+        assert rc != 0
+        assert b"buffer allocation" in lib.bvml_last_error()
+        check(lib.bvml_refiner_forward(handle, normal.data_ptr(), feat.data_ptr(), hid.data_ptr(),
+                                       B, h, w, fi, H, W, 5, 0, 0, H, W, 1, out.data_ptr(),
+                                       stream))
+        check(lib.bvml_refiner_status(handle, stream))
+        torch.cuda.synchronize()
+        r = Refiner()
+        r.load_params(params)
+        r.to(0)
+        assert torch.equal(out, r.forward(normal, feat, hid, intr, H, W,
+                                          out_dtype=torch.float16))
+    finally:
+        lib.bvml_refiner_destroy(handle)
