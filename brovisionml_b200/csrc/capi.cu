@@ -7,11 +7,14 @@
 // no exception may cross a C ABI.
 #include "bvml_dsine.h"
 #include "bvml_internal.h"
+#include "trace.h"
 
 #include <cuda_runtime.h>
 
+#include <chrono>
 #include <cstdio>
 #include <cstdint>
+#include <cstdlib>
 #include <string>
 #include <vector>
 
@@ -67,6 +70,26 @@ size_t sync_region(int B, int h, int w) { return align256(bvml::angmf_iters_sync
 }  // namespace
 
 int bvml::report_error(int code, const std::string& msg) { return fail(code, msg); }
+
+bool bvml::profile_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("BROVISIONML_PROFILE");
+        return v != nullptr && v[0] != '\0' && v[0] != '0';
+    }();
+    return on;
+}
+
+void bvml::profile_mark(cudaStream_t s, const char* name) {
+    if (!profile_enabled()) return;
+    cudaStreamSynchronize(s);
+    using clock = std::chrono::steady_clock;
+    static thread_local clock::time_point last = clock::now();
+    const clock::time_point now = clock::now();
+    if (name)
+        std::fprintf(stderr, "[brovisionml-prof] %-28s %9.2f ms\n", name,
+                     std::chrono::duration<double, std::milli>(now - last).count());
+    last = now;
+}
 
 namespace {
 
@@ -293,6 +316,7 @@ int bvml_probe_events(void* const* events, int n) {
 }
 
 int bvml_ray_relu(void* normal, const float* ray, int B, int H, int W, int dtype, void* stream) {
+    bvml::NvtxRange nvtx("bvml_ray_relu");
     if (!dtype_ok(dtype)) return einval("ray_relu: unknown dtype");
     if (!dims_ok(B, H, W)) return einval("ray_relu: bad shape");
     if ((long)B * H * W == 0) return finish(cudaSuccess, "ray_relu");
@@ -306,6 +330,7 @@ int bvml_angmf_propagate(const void* pred_norm, const void* prob, const void* xy
                          const void* angle, const float* ray, double fu, double cu, double fv,
                          double cv, int B, int H, int W, int ps, int dil, int dtype, void* out,
                          void* stream) {
+    bvml::NvtxRange nvtx("bvml_angmf_propagate");
     return angmf_entry("angmf_propagate", false, pred_norm, prob, xy, angle, ray, fu, cu, fv,
                        cv, B, H, W, ps, dil, dtype, out, stream);
 }
@@ -314,12 +339,14 @@ int bvml_angmf_propagate_logits(const void* pred_norm, const void* prob_logits, 
                                 const void* angle_logits, const float* ray, double fu,
                                 double cu, double fv, double cv, int B, int H, int W, int ps,
                                 int dil, int dtype, void* out, void* stream) {
+    bvml::NvtxRange nvtx("bvml_angmf_propagate_logits");
     return angmf_entry("angmf_propagate_logits", true, pred_norm, prob_logits, xy, angle_logits,
                        ray, fu, cu, fv, cv, B, H, W, ps, dil, dtype, out, stream);
 }
 
 int bvml_convex_upsample(const void* x, const void* mask, int N, int C, int H, int W, int scale,
                          int dtype, void* y, void* stream) {
+    bvml::NvtxRange nvtx("bvml_convex_upsample");
     if (!dtype_ok(dtype)) return einval("convex_upsample: unknown dtype");
     if (C != 3 || scale != 8)
         return fail(BVML_EUNSUPPORTED, "dsine ops: convex_upsample: only C = 3, scale = 8");
@@ -347,6 +374,7 @@ int bvml_convex_upsample(const void* x, const void* mask, int N, int C, int H, i
 
 int bvml_l2_normalize_nchw(const void* x, int N, int C, int H, int W, float eps, int dtype,
                            void* y, void* stream) {
+    bvml::NvtxRange nvtx("bvml_l2_normalize_nchw");
     if (!dtype_ok(dtype)) return einval("l2_normalize: unknown dtype");
     if (C < 0 || C > 16) return fail(BVML_EUNSUPPORTED, "dsine ops: l2_normalize: C must be <= 16");
     if (N < 0 || H < 0 || W < 0) return einval("l2_normalize: bad shape");
@@ -359,6 +387,7 @@ int bvml_l2_normalize_nchw(const void* x, int N, int C, int H, int W, float eps,
 
 int bvml_slice2d(const void* x, int N, int C, int H, int W, int h0, int w0, int Ho, int Wo,
                  int dtype, void* y, void* stream) {
+    bvml::NvtxRange nvtx("bvml_slice2d");
     if (!dtype_ok(dtype)) return einval("slice2d: unknown dtype");
     if (N < 0 || C < 0 || H < 0 || W < 0 || Ho < 0 || Wo < 0 || h0 < 0 || w0 < 0 ||
         h0 + Ho > H || w0 + Wo > W)
@@ -373,6 +402,7 @@ int bvml_slice2d(const void* x, int N, int C, int H, int W, int h0, int w0, int 
 int bvml_conv2d_nhwc_f16(const void* x, const void* w, const float* bias, int B, int H, int W,
                           int cin_pad, int cout, int cout_pad, int ks, int act, void* y,
                           int* err, void* stream) {
+    bvml::NvtxRange nvtx("bvml_conv2d_nhwc_f16");
     if (!(ks == 1 || ks == 3 || ks == 5)) return einval("conv2d: kernel size must be 1, 3 or 5");
     if (act < 0 || act > 3) return einval("conv2d: unknown activation");
     if (B < 0 || H < 0 || W < 0 || cin_pad <= 0 || cin_pad % 64 != 0 || cout_pad <= 0 ||
@@ -409,6 +439,7 @@ int bvml_conv2d_nhwc_f16(const void* x, const void* w, const float* bias, int B,
 int bvml_conv2d_nhwc_f16_ex(const void* x, int x_c, int cin_off, int cin_pad, const void* w,
                              const float* bias, int B, int H, int W, int cout, int cout_pad,
                              int ks, const bvml_conv_epilogue* epi, int* err, void* stream) {
+    bvml::NvtxRange nvtx("bvml_conv2d_nhwc_f16_ex");
     auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     if (!(ks == 1 || ks == 3 || ks == 5)) return einval("conv2d: kernel size must be 1, 3 or 5");
     if (!epi || epi->mode < 0 || epi->mode > 6) return einval("conv2d: unknown epilogue");
@@ -506,6 +537,7 @@ int bvml_conv2d_nhwc_f16_ex(const void* x, int x_c, int cin_off, int cin_pad, co
 int bvml_head_tail_1x1(const void* x, int x_c, int cin_off, const void* w2, const float* b2,
                        const void* w4, const float* b4, int B, int H, int W, int cout,
                        int dtype, void* out, int* err, void* stream) {
+    bvml::NvtxRange nvtx("bvml_head_tail_1x1");
     auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     if (B < 0 || H < 0 || W < 0 || cout <= 0 || cout > 64 || x_c % 8 || cin_off < 0 ||
         cin_off % 64 || cin_off + 128 > x_c)
@@ -537,6 +569,7 @@ int bvml_head_tail_1x1(const void* x, int x_c, int cin_off, const void* w2, cons
 
 int bvml_stage_inputs(const float* h0, const float* feat, int B, int H, int W, float* h32,
                       void* hx, void* fx, void* stream) {
+    bvml::NvtxRange nvtx("bvml_stage_inputs");
     auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     if (B < 0 || H < 0 || W < 0) return einval("stage inputs: negative size");
     if ((long)B * H * W == 0) return finish(cudaSuccess, "stage inputs");
@@ -576,6 +609,7 @@ int bvml_refine(const void* normal0, const float* ray8, const void* const* prob,
                 int B, int h, int w, int ps, int dil, double fu, double cu, double fv, double cv,
                 int full_res_ray_relu, int crop_t, int crop_l, int out_h, int out_w, int dtype,
                 void* workspace, size_t workspace_bytes, void* out, void* stream) {
+    bvml::NvtxRange nvtx("bvml_refine");
     return refine_entry(false, normal0, ray8, prob, xy, angle, iters, mask, B, h, w, ps, dil, fu,
                         cu, fv, cv, full_res_ray_relu, crop_t, crop_l, out_h, out_w, dtype,
                         workspace, workspace_bytes, out, stream);
@@ -587,6 +621,7 @@ int bvml_refine_logits(const void* normal0, const float* ray8, const void* const
                        double cu, double fv, double cv, int full_res_ray_relu, int crop_t,
                        int crop_l, int out_h, int out_w, int dtype, void* workspace,
                        size_t workspace_bytes, void* out, void* stream) {
+    bvml::NvtxRange nvtx("bvml_refine_logits");
     return refine_entry(true, normal0, ray8, prob_logits, xy, angle_logits, iters, mask, B, h, w,
                         ps, dil, fu, cu, fv, cv, full_res_ray_relu, crop_t, crop_l, out_h, out_w,
                         dtype, workspace, workspace_bytes, out, stream);

@@ -19,6 +19,7 @@
 // shape and reused.
 #include "bvml_dsine.h"
 #include "bvml_internal.h"
+#include "trace.h"
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -166,6 +167,148 @@ int conv(bvml_refiner* r, const void* x, int x_c, int cin_off, const DevBuf& w, 
 
 }  // namespace
 
+namespace {
+
+// ConvGRU + heads: `iters` iterations from the decoder's hidden state and
+// feature, raw head outputs into the handle's buffers.
+int stage(bvml_refiner* r, const float* normal, const float* feature, const float* hidden, int B,
+          int h, int w, int iters, int dtype, size_t px, size_t es, cudaStream_t s) {
+    (void)normal;
+    int rc;
+    if ((rc = bvml_stage_inputs(hidden, feature, B, h, w, r->h32.as<float>(), r->hx.p, r->fx.p,
+                                s)) != BVML_OK)
+        return rc;
+    // the fixed inputs, once: uv -> z|r|q (one frame, shared), feature (+ that)
+    // -> z|r|q as fp16 hi / lo halves, uv -> the heads' 3x3 (shared)
+    const int saved_B = r->B;
+    {
+        bvml_conv_epilogue ep{};
+        ep.mode = BVML_EPI_C4_F32;
+        ep.out = r->gxu.p;
+        ep.out_c = 192;
+        r->B = 1;
+        rc = conv(r, r->ux.p, 64, 0, r->w_gxu, r->zeros.as<float>(), 192, 192, 5, ep, s);
+        if (rc == BVML_OK) {
+            ep = bvml_conv_epilogue{};
+            ep.mode = BVML_EPI_C4_F32;
+            ep.out = r->gu.p;
+            ep.out_c = 512;
+            rc = conv(r, r->ux.p, 64, 0, r->w_gu, r->zeros.as<float>(), 512, 512, 3, ep, s);
+        }
+        r->B = saved_B;
+        if (rc != BVML_OK) return rc;
+        ep = bvml_conv_epilogue{};
+        ep.mode = BVML_EPI_SPLIT_F16;
+        ep.out = r->gx.p;
+        ep.out_c = 384;
+        ep.add = r->gxu.as<float>();
+        ep.add_c = 192;
+        ep.add_shared = 1;
+        if ((rc = conv(r, r->fx.p, 64, 0, r->w_gx, r->zeros.as<float>(), 192, 192, 5, ep, s)) !=
+            BVML_OK)
+            return rc;
+    }
+    char* prob = r->prob.as<char>();
+    char* xy = r->xy.as<char>();
+    char* angle = r->angle.as<char>();
+    const int planar = dtype == BVML_F16 ? BVML_EPI_PLANAR_F16 : BVML_EPI_PLANAR_F32;
+    for (int it = 0; it < iters; ++it) {
+        const bool up = it == iters - 1;  // only the last upsample reaches the output
+        bvml_conv_epilogue ep{};
+        ep.mode = BVML_EPI_GRU_ZR;
+        ep.h32 = r->h32.as<float>();
+        ep.z = r->z.p;
+        ep.rh = r->rhx.p;
+        ep.rh_c = 64;
+        ep.xin = r->gx.p;
+        ep.xin_c = 256;
+        ep.xin_stride = 384;
+        ep.wx = r->iz.p;
+        if ((rc = conv(r, r->hx.p, 64, 0, r->w_zr, r->b_zr.as<float>(), 128, 128, 5, ep, s)) !=
+            BVML_OK)
+            return rc;
+        ep = bvml_conv_epilogue{};
+        ep.mode = BVML_EPI_GRU_Q;
+        ep.h32 = r->h32.as<float>();
+        ep.z = r->z.p;
+        ep.hx = r->hx.p;
+        ep.hx_c = 64;
+        ep.xin = r->gx.as<__half>() + 256;
+        ep.xin_c = 128;
+        ep.xin_stride = 384;
+        ep.wx = r->iq.p;
+        if ((rc = conv(r, r->rhx.p, 64, 0, r->w_q, r->b_q.as<float>(), 64, 64, 5, ep, s)) !=
+            BVML_OK)
+            return rc;
+        ep = bvml_conv_epilogue{};
+        ep.mode = BVML_EPI_NHWC;
+        ep.act = 1;
+        ep.out = r->t1.p;
+        ep.out_c = 512;
+        ep.add = r->gu.as<float>();
+        ep.add_c = 512;
+        ep.add_shared = 1;
+        const int n3 = up ? 512 : 384;
+        if ((rc = conv(r, r->hx.p, 64, 0, up ? r->w_c0 : r->w_c0_3, r->b_c0.as<float>(), n3, n3,
+                       3, ep, s)) != BVML_OK)
+            return rc;
+        void* dst[3] = {prob + es * px * 25 * it, xy + es * px * 50 * it,
+                        angle + es * px * 25 * it};
+        for (int k = 0; k < 3; ++k)
+            if ((rc = bvml_head_tail_1x1(r->t1.p, 512, k * kHeadHidden, r->w_c2[k].p,
+                                         r->b_c2[k].as<float>(), r->w_c4[k].p,
+                                         r->b_c4[k].as<float>(), B, h, w, kHeadOut[k], dtype,
+                                         dst[k], r->err.as<int>(), s)) != BVML_OK)
+                return rc;
+        if (up) {
+            ep = bvml_conv_epilogue{};
+            ep.mode = BVML_EPI_NHWC;
+            ep.act = 1;
+            ep.out = r->t2.p;
+            ep.out_c = 512;
+            ep.out_off = 3 * kHeadHidden;
+            if ((rc = conv(r, r->t1.p, 512, 3 * kHeadHidden, r->w_c2[3], r->b_c2[3].as<float>(),
+                           128, 128, 1, ep, s, kHeadHidden)) != BVML_OK)
+                return rc;
+            ep = bvml_conv_epilogue{};
+            ep.mode = planar;
+            ep.out = r->mask.p;
+            if ((rc = conv(r, r->t2.p, 512, 3 * kHeadHidden, r->w_c4[3], r->b_c4[3].as<float>(),
+                           576, 576, 1, ep, s, kHeadHidden)) != BVML_OK)
+                return rc;
+        }
+    }
+    return BVML_OK;
+}
+
+// The refine ops on the raw head outputs (activations applied on load).
+int ops(bvml_refiner* r, const float* normal, int B, int h, int w, int iters, double fu,
+        double cu, double fv, double cv, int crop_t, int crop_l, int out_h, int out_w, int dtype,
+        size_t px, size_t es, void* out, cudaStream_t s) {
+    cudaError_t e;
+    char* prob = r->prob.as<char>();
+    char* xy = r->xy.as<char>();
+    char* angle = r->angle.as<char>();
+    const void* n0 = normal;
+    if (dtype == BVML_F16) {
+        to_half_kernel<<<(unsigned)((px * 3 + 255) / 256 < 4096 ? (px * 3 + 255) / 256 : 4096),
+                         256, 0, s>>>(normal, r->n16.as<__half>(), (long)px * 3);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "normal conversion");
+        n0 = r->n16.p;
+    }
+    std::vector<const void*> pp(iters), xp(iters), ap(iters);
+    for (int it = 0; it < iters; ++it) {
+        pp[it] = prob + es * px * 25 * it;
+        xp[it] = xy + es * px * 50 * it;
+        ap[it] = angle + es * px * 25 * it;
+    }
+    return bvml_refine_logits(n0, nullptr, pp.data(), xp.data(), ap.data(), iters, r->mask.p, B, h,
+                              w, 5, 1, fu, cu, fv, cv, 0, crop_t, crop_l, out_h, out_w, dtype,
+                              r->ws.p, r->ws.n, out, s);
+}
+
+}  // namespace
+
 extern "C" {
 
 const char* bvml_refiner_weight_name(int i) {
@@ -292,6 +435,8 @@ int bvml_refiner_forward(bvml_refiner* r, const float* normal, const float* feat
     if (dtype != BVML_F32 && dtype != BVML_F16)
         return fail(BVML_EINVAL, "dsine ops: refiner: dtype must be F32 or F16");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    bvml::NvtxRange nvtx("bvml_refiner_forward");
+    bvml::profile_mark(s, nullptr);
     cudaError_t e = cudaSetDevice(r->device);
     if (e != cudaSuccess) return cuda_fail(e, "set device");
     const size_t px = (size_t)B * h * w, hw = (size_t)h * w;
@@ -328,126 +473,17 @@ int bvml_refiner_forward(bvml_refiner* r, const float* normal, const float* feat
                 s>>>(r->ux.as<__half>(), h, w, fu, cu, fv, cv);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "uv launch");
     int rc;
-    if ((rc = bvml_stage_inputs(hidden, feature, B, h, w, r->h32.as<float>(), r->hx.p, r->fx.p,
-                                s)) != BVML_OK)
-        return rc;
-    // the fixed inputs, once: uv -> z|r|q (one frame, shared), feature (+ that)
-    // -> z|r|q as fp16 hi / lo halves, uv -> the heads' 3x3 (shared)
-    const int saved_B = r->B;
-    {
-        bvml_conv_epilogue ep{};
-        ep.mode = BVML_EPI_C4_F32;
-        ep.out = r->gxu.p;
-        ep.out_c = 192;
-        r->B = 1;
-        rc = conv(r, r->ux.p, 64, 0, r->w_gxu, r->zeros.as<float>(), 192, 192, 5, ep, s);
-        if (rc == BVML_OK) {
-            ep = bvml_conv_epilogue{};
-            ep.mode = BVML_EPI_C4_F32;
-            ep.out = r->gu.p;
-            ep.out_c = 512;
-            rc = conv(r, r->ux.p, 64, 0, r->w_gu, r->zeros.as<float>(), 512, 512, 3, ep, s);
-        }
-        r->B = saved_B;
-        if (rc != BVML_OK) return rc;
-        ep = bvml_conv_epilogue{};
-        ep.mode = BVML_EPI_SPLIT_F16;
-        ep.out = r->gx.p;
-        ep.out_c = 384;
-        ep.add = r->gxu.as<float>();
-        ep.add_c = 192;
-        ep.add_shared = 1;
-        if ((rc = conv(r, r->fx.p, 64, 0, r->w_gx, r->zeros.as<float>(), 192, 192, 5, ep, s)) !=
-            BVML_OK)
-            return rc;
-    }
-    char* prob = r->prob.as<char>();
-    char* xy = r->xy.as<char>();
-    char* angle = r->angle.as<char>();
-    const int planar = dtype == BVML_F16 ? BVML_EPI_PLANAR_F16 : BVML_EPI_PLANAR_F32;
-    for (int it = 0; it < iters; ++it) {
-        const bool up = it == iters - 1;  // only the last upsample reaches the output
-        bvml_conv_epilogue ep{};
-        ep.mode = BVML_EPI_GRU_ZR;
-        ep.h32 = r->h32.as<float>();
-        ep.z = r->z.p;
-        ep.rh = r->rhx.p;
-        ep.rh_c = 64;
-        ep.xin = r->gx.p;
-        ep.xin_c = 256;
-        ep.xin_stride = 384;
-        ep.wx = r->iz.p;
-        if ((rc = conv(r, r->hx.p, 64, 0, r->w_zr, r->b_zr.as<float>(), 128, 128, 5, ep, s)) !=
-            BVML_OK)
-            return rc;
-        ep = bvml_conv_epilogue{};
-        ep.mode = BVML_EPI_GRU_Q;
-        ep.h32 = r->h32.as<float>();
-        ep.z = r->z.p;
-        ep.hx = r->hx.p;
-        ep.hx_c = 64;
-        ep.xin = r->gx.as<__half>() + 256;
-        ep.xin_c = 128;
-        ep.xin_stride = 384;
-        ep.wx = r->iq.p;
-        if ((rc = conv(r, r->rhx.p, 64, 0, r->w_q, r->b_q.as<float>(), 64, 64, 5, ep, s)) !=
-            BVML_OK)
-            return rc;
-        ep = bvml_conv_epilogue{};
-        ep.mode = BVML_EPI_NHWC;
-        ep.act = 1;
-        ep.out = r->t1.p;
-        ep.out_c = 512;
-        ep.add = r->gu.as<float>();
-        ep.add_c = 512;
-        ep.add_shared = 1;
-        const int n3 = up ? 512 : 384;
-        if ((rc = conv(r, r->hx.p, 64, 0, up ? r->w_c0 : r->w_c0_3, r->b_c0.as<float>(), n3, n3,
-                       3, ep, s)) != BVML_OK)
-            return rc;
-        void* dst[3] = {prob + es * px * 25 * it, xy + es * px * 50 * it,
-                        angle + es * px * 25 * it};
-        for (int k = 0; k < 3; ++k)
-            if ((rc = bvml_head_tail_1x1(r->t1.p, 512, k * kHeadHidden, r->w_c2[k].p,
-                                         r->b_c2[k].as<float>(), r->w_c4[k].p,
-                                         r->b_c4[k].as<float>(), B, h, w, kHeadOut[k], dtype,
-                                         dst[k], r->err.as<int>(), s)) != BVML_OK)
-                return rc;
-        if (up) {
-            ep = bvml_conv_epilogue{};
-            ep.mode = BVML_EPI_NHWC;
-            ep.act = 1;
-            ep.out = r->t2.p;
-            ep.out_c = 512;
-            ep.out_off = 3 * kHeadHidden;
-            if ((rc = conv(r, r->t1.p, 512, 3 * kHeadHidden, r->w_c2[3], r->b_c2[3].as<float>(),
-                           128, 128, 1, ep, s, kHeadHidden)) != BVML_OK)
-                return rc;
-            ep = bvml_conv_epilogue{};
-            ep.mode = planar;
-            ep.out = r->mask.p;
-            if ((rc = conv(r, r->t2.p, 512, 3 * kHeadHidden, r->w_c4[3], r->b_c4[3].as<float>(),
-                           576, 576, 1, ep, s, kHeadHidden)) != BVML_OK)
-                return rc;
-        }
-    }
-    // the refine ops on the raw head outputs (activations applied on load)
-    const void* n0 = normal;
-    if (dtype == BVML_F16) {
-        to_half_kernel<<<(unsigned)((px * 3 + 255) / 256 < 4096 ? (px * 3 + 255) / 256 : 4096),
-                         256, 0, s>>>(normal, r->n16.as<__half>(), (long)px * 3);
-        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "normal conversion");
-        n0 = r->n16.p;
-    }
-    std::vector<const void*> pp(iters), xp(iters), ap(iters);
-    for (int it = 0; it < iters; ++it) {
-        pp[it] = prob + es * px * 25 * it;
-        xp[it] = xy + es * px * 50 * it;
-        ap[it] = angle + es * px * 25 * it;
-    }
-    return bvml_refine_logits(n0, nullptr, pp.data(), xp.data(), ap.data(), iters, r->mask.p, B, h,
-                              w, 5, 1, fu, cu, fv, cv, 0, crop_t, crop_l, out_h, out_w, dtype,
-                              r->ws.p, r->ws.n, out, stream);
+    nvtxRangePushA("refine.stage");
+    rc = stage(r, normal, feature, hidden, B, h, w, iters, dtype, px, es, s);
+    nvtxRangePop();
+    if (rc != BVML_OK) return rc;
+    bvml::profile_mark(s, "refine.stage");
+    nvtxRangePushA("refine.ops");
+    rc = ops(r, normal, B, h, w, iters, fu, cu, fv, cv, crop_t, crop_l, out_h, out_w, dtype, px,
+             es, out, s);
+    nvtxRangePop();
+    if (rc == BVML_OK) bvml::profile_mark(s, "refine.ops");
+    return rc;
 }
 
 int bvml_refiner_status(bvml_refiner* r, void* stream) {

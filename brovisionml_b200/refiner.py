@@ -15,6 +15,8 @@ from __future__ import annotations
 
 import os
 import struct
+import sys
+import time
 from typing import Sequence
 
 import torch
@@ -50,6 +52,34 @@ def build_uv(intrins: Sequence[float], h8: int, w8: int, origH: int, origW: int,
     u = ((xs - cu) / fu).float()
     v = ((ys - cv) / fv).float()
     return torch.stack([u[None, :].expand(h8, w8), v[:, None].expand(h8, w8)]).contiguous()
+
+
+def profile_enabled() -> bool:
+    """The reference's BROVISIONML_PROFILE switch (src/profile.cpp:9-15): set
+    and not starting with '0'."""
+    v = os.environ.get("BROVISIONML_PROFILE", "")
+    return bool(v) and v[0] != "0"
+
+
+class _Marks:
+    """BROVISIONML_PROFILE marks as src/profile.cpp:17-29 has them: each mark
+    synchronises the device and prints the time since the previous one to
+    stderr (the C refiner prints the same lines)."""
+
+    def __init__(self, device) -> None:
+        self.on = profile_enabled()
+        self.device = device
+        if self.on:
+            torch.cuda.synchronize(device)
+            self.last = time.perf_counter()
+
+    def mark(self, name: str) -> None:
+        if not self.on:
+            return
+        torch.cuda.synchronize(self.device)
+        now = time.perf_counter()
+        print(f"[brovisionml-prof] {name:<28} {(now - self.last) * 1e3:9.2f} ms", file=sys.stderr)
+        self.last = now
 
 
 class Refiner:
@@ -124,12 +154,15 @@ class Refiner:
             raise RuntimeError("dsine refine: feature and hidden must be (B,64,h8,w8) like "
                                "the normal's grid")
         st = self._stage(B, h, w, out_dtype)
+        marks = _Marks(self.device)
         fu, cu, fv, cv = grid_intrinsics(intrins, h, w, origH, origW)
         st.start(hidden, feature, build_uv(intrins, h, w, origH, origW, self.device))
         outs = [st.step(up_mask=i == ITERS - 1) for i in range(ITERS)]
+        marks.mark("refine.stage")
         res = refine(normal.to(out_dtype).contiguous(), [o.prob for o in outs],
                      [o.xy for o in outs], [o.angle for o in outs], outs[-1].up_mask,
                      fu, cu, fv, cv, crop=crop, logits=True)
+        marks.mark("refine.ops")
         if check:
             st.check_pipeline()
         return res
