@@ -24,7 +24,7 @@ EXPORTS = ("bvml_last_error", "bvml_abi_version", "bvml_ray_relu", "bvml_angmf_p
            "bvml_conv2d_nhwc_f16", "bvml_conv2d_nhwc_f16_ex", "bvml_stage_inputs",
            "bvml_head_tail_1x1", "bvml_refine_status", "bvml_probe_recorded",
            "bvml_refiner_weight_name", "bvml_refiner_weight_shape", "bvml_refiner_create",
-           "bvml_refiner_forward", "bvml_refiner_status", "bvml_refiner_destroy")
+           "bvml_refiner_forward", "bvml_refiner_status", "bvml_refiner_destroy", "bvml_check_word")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(
@@ -94,6 +94,8 @@ lib.bvml_probe_events.restype = _i
 lib.bvml_probe_events.argtypes = [ctypes.POINTER(_vp), _i]
 lib.bvml_probe_recorded.restype = _i
 lib.bvml_probe_recorded.argtypes = []
+lib.bvml_check_word.restype = _i
+lib.bvml_check_word.argtypes = [_i]
 lib.bvml_refine_status.restype = _i
 lib.bvml_refine_status.argtypes = [_vp, _vp]
 REFINER_WEIGHTS = 30

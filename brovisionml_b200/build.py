@@ -27,6 +27,10 @@ CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "_lib")
 OBJ_DIR = os.path.join(HERE, "_build")
 LIB = os.path.join(LIB_DIR, "libbvml_dsine.so")
+# The same sources with -DBVML_CHECKED: every kernel tests its indices and TMA
+# coordinates before each access and records failures (bvml_check_word); the
+# GPU tests run the odd shapes through it.
+CHECKED_LIB = os.path.join(LIB_DIR, "libbvml_dsine_checked.so")
 BRIDGE = os.path.join(LIB_DIR, "libbvml_dsine_bridge.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -58,6 +62,7 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
     sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     jobs = []
     objs = []
+    cobjs = []
     for src in sources:
         obj = os.path.join(OBJ_DIR, os.path.basename(src)[:-3] + ".o")
         objs.append(obj)
@@ -65,6 +70,10 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
             cmd = [nvcc] + ARCH + NVCC_FLAGS + (["-Xptxas", "-v"] if ptxas_info else []) + \
                   ["-c", src, "-o", obj]
             jobs.append(cmd)
+        cobj = os.path.join(OBJ_DIR, "checked_" + os.path.basename(src)[:-3] + ".o")
+        cobjs.append(cobj)
+        if _stale(cobj, [src] + headers):
+            jobs.append([nvcc] + ARCH + NVCC_FLAGS + ["-DBVML_CHECKED", "-c", src, "-o", cobj])
 
     def run(cmd):
         r = subprocess.run(cmd, capture_output=True, text=True)
@@ -81,6 +90,9 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
         # handles created by THEIR CUDA runtime; one shared runtime instance
         # per process is what makes those handles valid here too.
         run([nvcc] + ARCH + ["-shared", "-cudart", "shared", "-o", LIB] + objs +
+            ["-Xlinker", "-rpath,/usr/local/cuda/lib64"])
+    if _stale(CHECKED_LIB, cobjs + [__file__]):
+        run([nvcc] + ARCH + ["-shared", "-cudart", "shared", "-o", CHECKED_LIB] + cobjs +
             ["-Xlinker", "-rpath,/usr/local/cuda/lib64"])
 
     bridge_src = os.path.join(CSRC, "dsine_ops_b200.cpp")

@@ -16,4 +16,6 @@ cudaError_t launch_angmf_iters(const AngmfItersLaunch& L, cudaStream_t s) {
     return launch_angmf_iters_act<false>(L, s);
 }
 
+BVML_CHECK_READER(check_word_angmf)
+
 }  // namespace bvml

@@ -470,7 +470,8 @@ __device__ __forceinline__ void stage_normals(const TNI* __restrict__ pnb,
         const int i = idx / SW, j = idx - i * SW;
         const int sy = clampi(y0 - R + i, 0, a.H - 1);
         const int sx = clampi(x0 - R + j, 0, a.W - 1);
-        const long sp = (long)sy * a.W + sx;
+        long sp = (long)sy * a.W + sx;
+        if (!check_ok(sp >= 0 && sp < HW, kChkNormalLoad)) sp = 0;
         float v[3] = {St<TNI>::ld(pnb + sp), St<TNI>::ld(pnb + HW + sp),
                       St<TNI>::ld(pnb + 2 * HW + sp)};
         if (FUSE_RR) ray_relu_f32(v[0], v[1], v[2], __ldg(ray + sp), __ldg(ray + HW + sp),
@@ -479,6 +480,7 @@ __device__ __forceinline__ void stage_normals(const TNI* __restrict__ pnb,
         const float tu = fmaf((float)sx, a.ifu, a.tu_c), tv = fmaf((float)sy, a.ifv, a.tv_c);
         const float u4[4] = {v[0], v[1], v[2], fmaf(tu, v[0], fmaf(tv, v[1], v[2]))};  // P.n
         const int k = j >> 1;
+        if (!check_ok(i < SH && k < T.swh, kChkHaloSmem)) continue;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             const float u = u4[c];
@@ -524,8 +526,9 @@ __device__ __forceinline__ void stage_normals_ct(const TNI* __restrict__ pnb,
         const int i = it / NP, k = it - (it / NP) * NP;
         const long row = (long)clampi(y0 - R + i, 0, a.H - 1) * a.W;
         const int sx = x0 - R + 2 * k;
-        const long q0 = row + clampi(sx, 0, a.W - 1);
-        const long q1 = row + clampi(sx + 1, 0, a.W - 1);
+        long q0 = row + clampi(sx, 0, a.W - 1);
+        long q1 = row + clampi(sx + 1, 0, a.W - 1);
+        if (!check_ok(q0 >= 0 && q0 < HW && q1 >= 0 && q1 < HW, kChkNormalLoad)) q0 = q1 = 0;
         float v0[3], v1[3];
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
@@ -546,6 +549,7 @@ __device__ __forceinline__ void stage_normals_ct(const TNI* __restrict__ pnb,
         const float tu1 = fmaf((float)clampi(sx + 1, 0, a.W - 1), a.ifu, a.tu_c);
         const float w0[4] = {v0[0], v0[1], v0[2], fmaf(tu0, v0[0], fmaf(tv, v0[1], v0[2]))};
         const float w1[4] = {v1[0], v1[1], v1[2], fmaf(tu1, v1[0], fmaf(tv, v1[1], v1[2]))};
+        if (!check_ok(i < SH && k < SWH - 1, kChkHaloSmem)) continue;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             const float u0 = w0[c], u1 = w1[c];
@@ -681,6 +685,8 @@ __device__ __forceinline__ void finish_pair(PairAcc<Mask>& A, int b, int x, int 
     const long HW = a.HW;
     const long p0 = (long)y * a.W + x;
     TNO* ob = out + (long)b * 3 * HW;
+    if (!check_ok(y >= 0 && y < a.H && x >= 0 && x < a.W && (!two || x + 1 < a.W), kChkStore))
+        return;
     if (vec) {
         St<TNO>::st2(ob + p0, ox);
         St<TNO>::st2(ob + HW + p0, oy);
@@ -872,10 +878,12 @@ __device__ __forceinline__ void angmf_tile(const TNI* __restrict__ pn,
         const TS* base = c == 0 ? prb : c == 1 ? xyb : c == 2 ? xyb + (long)P * HW : anb;
         const int gy = y0 + S::kRowsW * warp + r, gx = x0 + cc * S::kEpc;
         valid[k] = gy < a.H && gx < a.W;
+        if (!check_ok(!valid[k] || gx + S::kEpc <= a.W, kChkRing)) valid[k] = false;
         src[k] = valid[k] ? base + (long)gy * a.W + gx : base;
         dst[k] = (c * S::kRowsW + r) * kTW + cc * S::kEpc;
     }
     auto issue = [&](int slot) {
+        if (!check_ok(slot >= 0 && slot < S::kN, kChkRing)) return;
         TS* sl = ring + slot * S::kElemsW;
 #pragma unroll
         for (int k = 0; k < S::kPerLane; ++k) {
@@ -951,7 +959,8 @@ __device__ __forceinline__ void angmf_tile(const TNI* __restrict__ pn,
                 const TS* st = st_row + kx * S::kElemsW;
                 // window column offset: a constant once the kx loop is unrolled
                 const int dj = kx * DIL;
-                const int pi = prow + (dj >> 1);
+                int pi = prow + (dj >> 1);
+                if (!check_ok(pi >= 0 && pi < SH * SWH, kChkHaloSmem)) pi = 0;
                 float2 nx, ny, nz, as, tun;
                 if ((dj & 1) == 0) {
                     nx = T.e[0][pi];
@@ -1070,6 +1079,7 @@ angmf_iters_kernel(const float* __restrict__ ray, const AngmfArgs a, const Angmf
         const int ty = t % a.tiles_y;
         const int b = t / a.tiles_y;
         int* mine = J.done + ((long)b * a.tiles_y + ty) * a.tiles_x + tx;
+        if (!check_ok(b < a.B && ty < a.tiles_y && tx < a.tiles_x, kChkDep)) break;
         int next = 0;
         if (tid == kClaim) next = atomicAdd(J.counter, 1);
         auto pre = [&] {

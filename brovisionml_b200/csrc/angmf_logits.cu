@@ -15,4 +15,6 @@ cudaError_t launch_angmf_iters_logits(const AngmfItersLaunch& L, cudaStream_t s)
     return launch_angmf_iters_act<true>(L, s);
 }
 
+BVML_CHECK_READER(check_word_angmf_logits)
+
 }  // namespace bvml

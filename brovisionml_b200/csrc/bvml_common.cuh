@@ -17,6 +17,51 @@
 
 namespace bvml {
 
+// ----------------------------------------------------------- checked builds
+// With -DBVML_CHECKED (brovisionml_b200/_lib/libbvml_dsine_checked.so, built
+// beside the release library) the kernels test their index arithmetic,
+// shared-memory offsets and TMA coordinates before each access: a failed test
+// ORs its bit into this translation unit's check word and the access is
+// skipped -- never a trap, so the context stays usable. The test suite runs
+// the odd shapes and edge cases through that build and requires a zero word
+// (compute-sanitizer is not available on the GPU pool this was built on).
+// Release builds compile the tests away.
+enum CheckBit : unsigned {
+    kChkNormalLoad = 1u << 0,   // AngMF halo load outside the frame
+    kChkHaloSmem = 1u << 1,     // AngMF halo plane offset outside the plane
+    kChkRing = 1u << 2,         // AngMF ring slot or offset outside the warp's ring
+    kChkStore = 1u << 3,        // AngMF store outside the frame
+    kChkDep = 1u << 4,          // persistent AngMF counter outside the tile table
+    kChkUpTma = 1u << 5,        // upsample TMA box misaligned or outside the mask
+    kChkUpRing = 1u << 6,       // upsample ring slot outside the ring
+    kChkUpStore = 1u << 7,      // upsample store outside the output
+    kChkConvTma = 1u << 8,      // convolution TMA channel coordinate misaligned
+    kChkConvStore = 1u << 9,    // convolution epilogue pixel outside the frame
+};
+#ifdef BVML_CHECKED
+static __device__ unsigned g_check_word;
+__device__ __forceinline__ bool check_ok(bool ok, unsigned bit) {
+    if (!ok) atomicOr(&g_check_word, bit);
+    return ok;
+}
+// Host reader of this translation unit's check word (optionally reset).
+#define BVML_CHECK_READER(fn)                                                    \
+    unsigned fn(bool reset) {                                                   \
+        unsigned v = 0;                                                         \
+        if (cudaMemcpyFromSymbol(&v, g_check_word, sizeof(v)) != cudaSuccess)   \
+            return 0x80000000u;                                                 \
+        if (reset) {                                                            \
+            const unsigned z = 0;                                               \
+            cudaMemcpyToSymbol(g_check_word, &z, sizeof(z));                    \
+        }                                                                       \
+        return v;                                                               \
+    }
+#else
+__device__ __forceinline__ constexpr bool check_ok(bool, unsigned) { return true; }
+#define BVML_CHECK_READER(fn) \
+    unsigned fn(bool) { return 0; }
+#endif
+
 // ------------------------------------------------------------------ float2 ops
 __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }

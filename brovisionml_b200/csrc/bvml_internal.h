@@ -123,6 +123,13 @@ struct HeadTailLaunch {
 };
 cudaError_t launch_head_tail(const HeadTailLaunch& L, cudaStream_t s);
 
+// Checked builds: each kernel translation unit's check word (see
+// bvml_common.cuh), optionally reset; release builds return 0.
+unsigned check_word_angmf(bool reset);
+unsigned check_word_angmf_logits(bool reset);
+unsigned check_word_upsample(bool reset);
+unsigned check_word_conv(bool reset);
+
 // Encode a tiled TMA tensor map (defined in conv_tc.cu).
 bool tma_encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
                 const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapDataType dt,

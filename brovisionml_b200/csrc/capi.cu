@@ -604,6 +604,18 @@ int bvml_refine_status(const void* workspace, void* stream) {
 
 int bvml_probe_recorded(void) { return g_probe_recorded; }
 
+int bvml_check_word(int reset) {
+#ifdef BVML_CHECKED
+    const bool r = reset != 0;
+    const unsigned v = bvml::check_word_angmf(r) | bvml::check_word_angmf_logits(r) |
+                       bvml::check_word_upsample(r) | bvml::check_word_conv(r);
+    return (int)(v & 0x7fffffffu) | (v >> 31 ? (int)0x40000000 : 0);
+#else
+    (void)reset;
+    return -1;
+#endif
+}
+
 int bvml_refine(const void* normal0, const float* ray8, const void* const* prob,
                 const void* const* xy, const void* const* angle, int iters, const void* mask,
                 int B, int h, int w, int ps, int dil, double fu, double cu, double fv, double cv,

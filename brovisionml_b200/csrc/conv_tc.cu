@@ -336,7 +336,10 @@ __device__ __forceinline__ void planar_chunk_tma(const ConvArgs& a, const CUtens
     tc::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-        tc::tma_store_4d(map_o, stg_addr, px0, py0, cb, b);
+        // a TMA store's innermost coordinate must start on 16 bytes, and no
+        // store may start at a negative coordinate
+        if (check_ok((px0 * (int)sizeof(TO)) % 16 == 0 && px0 >= 0 && py0 >= 0, kChkConvTma))
+            tc::tma_store_4d(map_o, stg_addr, px0, py0, cb, b);
         tc::bulk_commit();
     }
 }
@@ -361,7 +364,8 @@ __device__ __forceinline__ void stage_f16_box(const CUtensorMap* map_o, uint8_t*
     tc::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-        tc::tma_store_4d(map_o, stg_addr, c0, px0, py0, b);
+        if (check_ok(c0 % 8 == 0 && c0 >= 0 && px0 >= 0 && py0 >= 0, kChkConvTma))
+            tc::tma_store_4d(map_o, stg_addr, c0, px0, py0, b);
         tc::bulk_commit();
     }
 }
@@ -414,7 +418,8 @@ __device__ __forceinline__ void nhwc_pair_tma(const ConvArgs& a, const CUtensorM
         tc::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-            tc::tma_store_4d(map_o, stg_addr, c0 - 32, px0, py0, b);
+            if (check_ok((c0 - 32) % 8 == 0 && c0 >= 32 && px0 >= 0 && py0 >= 0, kChkConvTma))
+                tc::tma_store_4d(map_o, stg_addr, c0 - 32, px0, py0, b);
             tc::bulk_commit();
         }
     }
@@ -516,6 +521,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     if (warp == 0 && lane == 0) {
         // ---------------------------------------------------------- producer
         int ga = 0, gb = 0;  // A and B entries issued by this CTA
+        if (!check_ok(a.cin_off % 8 == 0, kChkConvTma)) fail(8);
         if constexpr (BRES) {  // the CTA's weights, once
             tc::mbar_expect_tx(bar_bres, chunks * a.b_bytes);
             for (int ch = 0; ch < chunks; ++ch)
@@ -1488,5 +1494,7 @@ cudaError_t launch_head_tail(const HeadTailLaunch& L, cudaStream_t s) {
     }
     return cudaGetLastError();
 }
+
+BVML_CHECK_READER(check_word_conv)
 
 }  // namespace bvml

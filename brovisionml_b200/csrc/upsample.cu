@@ -207,6 +207,7 @@ __device__ __forceinline__ void collect(OutRun<TS>& run, int kx, float2 ox, floa
 template <typename TS>
 __device__ __forceinline__ void store_run(const OutRun<TS>& run, int kx, TS* __restrict__ out,
                                           const UpArgs& a, int b, int x, int Yo) {
+    if (!check_ok(Yo >= 0 && Yo < a.out_h && b >= 0 && b < a.B, kChkUpStore)) return;
     TS* orow = out + (long)b * 3 * a.out_h * a.out_w + (long)Yo * a.out_w;
     if constexpr (sizeof(TS) == 2) {
 #pragma unroll
@@ -276,6 +277,13 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
     bool failed = false;
     auto issue = [&](int k) {  // lane 0: stage k (= ky * 8 + kx) into slot k % kN
         const int s = k % U::kN;
+        // the box's innermost coordinate must start on 16 bytes
+        if (!check_ok((x0 * (int)sizeof(TS)) % 16 == 0 && x0 < a.w && y < a.h && k < 64 &&
+                          b < a.B,
+                      kChkUpTma)) {
+            tc::mbar_arrive(bar0 + 8 * s);  // completes the phase with no bytes
+            return;
+        }
         tc::mbar_expect_tx(bar0 + 8 * s, U::kBytes);
         tc::tma_load_4d(tc::smem_u32(ring + s * U::kElems), &mmap, bar0 + 8 * s, x0, y, k, b * 9);
     };
@@ -458,5 +466,7 @@ cudaError_t launch_upsample(const UpsampleLaunch& L, cudaStream_t s) {
     if (L.n_t == SType::F32) return launch_flags<float, __half>(L, a, s);
     return launch_flags<__half, __half>(L, a, s);
 }
+
+BVML_CHECK_READER(check_word_upsample)
 
 }  // namespace bvml

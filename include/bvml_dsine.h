@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define BVML_ABI_VERSION 6
+#define BVML_ABI_VERSION 7
 
 enum bvml_dtype { BVML_F32 = 0, BVML_F16 = 1 };
 
@@ -387,6 +387,17 @@ int bvml_probe_events(void* const* events, int n);
 /* How many probe events the calling thread's last bvml_refine call recorded
  * (its kernel launches + 1). */
 int bvml_probe_recorded(void);
+
+/*
+ * Checked builds only (libbvml_dsine_checked.so, compiled with BVML_CHECKED;
+ * no reference counterpart): the kernels test their indices, shared-memory
+ * offsets and TMA coordinates before each access, skip an access that fails
+ * and record it. Returns the OR of the recorded check bits since the last
+ * reset (0: every access was in bounds; bit 30: a word could not be read)
+ * and resets them when `reset` is nonzero. The release library returns -1.
+ * Synchronous: call after the work has completed.
+ */
+int bvml_check_word(int reset);
 
 #ifdef __cplusplus
 }
