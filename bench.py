@@ -892,9 +892,12 @@ def unit_bench(args, cfg, device, rank, world, barrier, max_over_ranks, torch, b
         step.ws = ws
         return step, out
 
-    def time_steps(step, clocks=False):
+    def time_steps(step, clocks=False, probes=None):
         """Device ms per step on this rank (W warm-up steps, then K timed
-        steps bracketed by a barrier and a synchronize on both sides)."""
+        steps bracketed by a barrier and a synchronize on both sides). probes:
+        one array of CUDA events per timed step, armed for that step's unit
+        (bvml_probe_events), so that every launch is timed inside the timed
+        region itself, on the launching stream."""
         with torch.cuda.stream(stream):
             for _ in range(max(3, args.warmup)):
                 step()
@@ -907,8 +910,12 @@ def unit_bench(args, cfg, device, rank, world, barrier, max_over_ranks, torch, b
             if clk:
                 clk.__enter__()
             start.record(stream)
-            for _ in range(args.steps):
+            for k in range(args.steps):
+                if probes is not None:
+                    bv.check(bv.lib.bvml_probe_events(probes[k], len(probes[k])))
                 step()
+            if probes is not None:
+                bv.lib.bvml_probe_events(None, 0)
             stop.record(stream)
             stream.synchronize()
             if clk:
@@ -917,36 +924,30 @@ def unit_bench(args, cfg, device, rank, world, barrier, max_over_ranks, torch, b
             barrier()
         return start.elapsed_time(stop) / args.steps, clk
 
-    step, out = unit(B)
-    ws_of_step = step.ws
-    ms_local, clk = time_steps(step, clocks=True)
-    ms = max_over_ranks(ms_local)
-    clocks = clk.summary()
-    out_px = cfg["B"] * cfg["H"] * cfg["W"]
-    value = out_px / (ms / 1e3) / 1e6
-
-    # per-kernel launch times: the same steps again with probe events. The
-    # unit is two launches (all AngMF iterations in one persistent launch, then
-    # the upsample) or, for shapes the persistent kernel does not take, I + 1.
+    # per-kernel launch times: probe events recorded between the unit's
+    # launches during the timed steps themselves. The unit is two launches
+    # (all AngMF iterations in one persistent launch, then the upsample) or,
+    # for shapes the persistent kernel does not take, I + 1.
     import ctypes
 
+    step, out = unit(B)
+    ws_of_step = step.ws
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(I + 2)]
            for _ in range(args.steps)]
-    n_rec = 0
     with torch.cuda.stream(stream):
         for e in evs:  # torch creates the CUDA event at its first record
             for ev in e:
                 ev.record(stream)
         stream.synchronize()
-        arrs = [(ctypes.c_void_p * len(e))(*[ev.cuda_event for ev in e]) for e in evs]
-        if B:
-            for k in range(args.steps):
-                bv.check(bv.lib.bvml_probe_events(arrs[k], len(evs[k])))
-                step()
-                n_rec = int(bv.lib.bvml_probe_recorded())
-            bv.lib.bvml_probe_events(None, 0)
-        stream.synchronize()
-        if B:
+    arrs = [(ctypes.c_void_p * len(e))(*[ev.cuda_event for ev in e]) for e in evs]
+    ms_local, clk = time_steps(step, clocks=True, probes=arrs if B else None)
+    ms = max_over_ranks(ms_local)
+    clocks = clk.summary()
+    out_px = cfg["B"] * cfg["H"] * cfg["W"]
+    value = out_px / (ms / 1e3) / 1e6
+    n_rec = int(bv.lib.bvml_probe_recorded()) if B else 0
+    if B:
+        with torch.cuda.stream(stream):
             bv.check(bv.lib.bvml_refine_status(ctypes.c_void_p(ws_of_step.data_ptr()),
                                                ctypes.c_void_p(stream.cuda_stream)))
     barrier()
