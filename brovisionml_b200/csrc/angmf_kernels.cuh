@@ -76,6 +76,8 @@ constexpr int kThreads = 256;   // one pixel pair per thread
 struct AngmfArgs {
     int B, H, W, dil, R, tiles_x, tiles_y;
     long HW;
+    float2 ifu2, ifv2;            // (1/fu, 1/fu), (1/fv, 1/fv): packed operands read from
+                                  // the kernel's parameter bank, not held in registers
     float ifu, ifv, tu_c, tv_c;   // 1/fu, 1/fv, (0.5-cu)/fu, (0.5-cv)/fv
     double fu, cu, fv, cv;        // exact values for the fp64 fix-up
 };
@@ -396,39 +398,53 @@ __device__ __forceinline__ void angmf_pair(int n, float2 xs, float2 ys, float2 t
     A.d = fma2(wm, dc, A.d);
 }
 
-// The replicate-padded halo of unit source normals in shared memory. For each
-// component an "even" and an "odd" plane of float2 pairs,
+// The replicate-padded halo of unit source normals in shared memory. Per
+// component v, an "even" and an "odd" pair of columns,
 //   E[i][k] = (v[i][2k], v[i][2k+1]),  O[i][k] = (v[i][2k+1], v[i][2k+2]),
-// so the pair starting at column j is (j even ? E : O)[i][j >> 1]: a warp's
-// pairs for one neighbour slot are consecutive float2, conflict-free. A fourth
-// pair of planes holds P.n = tu0 nx + tv0 ny + nz of each source pixel (it
-// does not depend on the output pixel, so it is formed once per tile instead
-// of once per evaluation). tu0 (with its negation) and tv0 are tabulated the
-// same way.
+// so the pair starting at column j is (j even ? E : O)[i][j >> 1]. The four
+// staged components -- nx, ny, nz and P.n = tu0 nx + tv0 ny + nz of each
+// source pixel (independent of the output pixel, so formed once per tile
+// instead of once per evaluation) -- sit two to a float4 plane, (nx pair,
+// ny pair) and (nz pair, P.n pair): a neighbour step reads its four pairs
+// with two 16-byte loads, and a warp's loads are consecutive float4,
+// conflict-free. -tu0 of each pair of columns is tabulated the same way (as
+// float2), tv0 per row.
 struct NTile {
-    float2* e[4];
-    float2* o[4];
-    float4* tue;  // (tu0, tu1, -tu0, -tu1) of the pair starting at column 2k
-    float4* tuo;  // ... at column 2k + 1
+    float4* e01;  // (nx, ny) pairs starting at column 2k
+    float4* e23;  // (nz, P.n) pairs ...
+    float4* o01;  // ... starting at column 2k + 1
+    float4* o23;
+    float2* tune; // (-tu0, -tu1) of the pair starting at column 2k
+    float2* tuno; // ... at column 2k + 1
     float* tv;
     int swh;      // pairs per plane row
 
     static constexpr __host__ __device__ int pairs_per_row(int SW) { return SW / 2 + 1; }
     static constexpr __host__ __device__ size_t bytes(int SW, int SH) {
         const int h = pairs_per_row(SW);
-        return sizeof(float4) * 2 * h + sizeof(float2) * 8 * (size_t)SH * h + sizeof(float) * SH;
+        return sizeof(float4) * 4 * (size_t)SH * h + sizeof(float2) * 2 * h + sizeof(float) * SH;
     }
+    // base: 16-byte aligned
     __device__ void carve(void* base, int SW, int SH) {
         swh = pairs_per_row(SW);
-        tue = reinterpret_cast<float4*>(base);
-        tuo = tue + swh;
-        float2* p = reinterpret_cast<float2*>(tuo + swh);
-        for (int c = 0; c < 4; ++c) {
-            e[c] = p;
-            o[c] = p + SH * swh;
-            p += 2 * SH * swh;
-        }
-        tv = reinterpret_cast<float*>(p);
+        e01 = reinterpret_cast<float4*>(base);
+        e23 = e01 + SH * swh;
+        o01 = e23 + SH * swh;
+        o23 = o01 + SH * swh;
+        tune = reinterpret_cast<float2*>(o23 + SH * swh);
+        tuno = tune + swh;
+        tv = reinterpret_cast<float*>(tuno + swh);
+    }
+    // component c (0..3) of the pair slot (first = the pair's first column)
+    // of plane entry q, as a float offset into the 01 or 23 plane
+    static __device__ __forceinline__ int slot(int q, int c, bool first) {
+        return 4 * q + 2 * (c & 1) + (first ? 0 : 1);
+    }
+    __device__ __forceinline__ float* eplane(int c) const {
+        return reinterpret_cast<float*>(c < 2 ? e01 : e23);
+    }
+    __device__ __forceinline__ float* oplane(int c) const {
+        return reinterpret_cast<float*>(c < 2 ? o01 : o23);
     }
 };
 
@@ -481,17 +497,16 @@ __device__ __forceinline__ void stage_normals(const TNI* __restrict__ pnb,
         const float u4[4] = {v[0], v[1], v[2], fmaf(tu, v[0], fmaf(tv, v[1], v[2]))};  // P.n
         const int k = j >> 1;
         if (!check_ok(i < SH && k < T.swh, kChkHaloSmem)) continue;
+        const int q = i * T.swh + k;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             const float u = u4[c];
-            float* ep = reinterpret_cast<float*>(T.e[c] + i * T.swh + k);
-            float* op = reinterpret_cast<float*>(T.o[c] + i * T.swh);
             if (j & 1) {
-                ep[1] = u;
-                op[2 * k] = u;          // O[i][k].x
+                T.eplane(c)[NTile::slot(q, c, false)] = u;   // E[i][k].y
+                T.oplane(c)[NTile::slot(q, c, true)] = u;    // O[i][k].x
             } else {
-                ep[0] = u;
-                if (k > 0) op[2 * (k - 1) + 1] = u;  // O[i][k-1].y
+                T.eplane(c)[NTile::slot(q, c, true)] = u;    // E[i][k].x
+                if (k > 0) T.oplane(c)[NTile::slot(q - 1, c, false)] = u;  // O[i][k-1].y
             }
         }
     }
@@ -500,8 +515,8 @@ __device__ __forceinline__ void stage_normals(const TNI* __restrict__ pnb,
 #pragma unroll
         for (int d = 0; d < 3; ++d)
             t[d] = fmaf((float)clampi(x0 - R + 2 * k + d, 0, a.W - 1), a.ifu, a.tu_c);
-        T.tue[k] = make_float4(t[0], t[1], -t[0], -t[1]);
-        T.tuo[k] = make_float4(t[1], t[2], -t[1], -t[2]);
+        T.tune[k] = make_float2(-t[0], -t[1]);
+        T.tuno[k] = make_float2(-t[1], -t[2]);
     }
     for (int i = threadIdx.x; i < SH; i += kThreads) {
         const int s0 = clampi(y0 - R + i, 0, a.H - 1);
@@ -550,13 +565,14 @@ __device__ __forceinline__ void stage_normals_ct(const TNI* __restrict__ pnb,
         const float w0[4] = {v0[0], v0[1], v0[2], fmaf(tu0, v0[0], fmaf(tv, v0[1], v0[2]))};
         const float w1[4] = {v1[0], v1[1], v1[2], fmaf(tu1, v1[0], fmaf(tv, v1[1], v1[2]))};
         if (!check_ok(i < SH && k < SWH - 1, kChkHaloSmem)) continue;
+        const int q = i * SWH + k;
+        T.e01[q] = make_float4(w0[0], w1[0], w0[1], w1[1]);   // E[i][k] of nx, ny
+        T.e23[q] = make_float4(w0[2], w1[2], w0[3], w1[3]);   // ... of nz, P.n
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            const float u0 = w0[c], u1 = w1[c];
-            T.e[c][i * SWH + k] = make_float2(u0, u1);     // E[i][k]
-            float* op = reinterpret_cast<float*>(T.o[c] + i * SWH);
-            op[2 * k] = u1;                                 // O[i][k].x
-            if (k > 0) op[2 * k - 1] = u0;                  // O[i][k-1].y
+            float* op = T.oplane(c);
+            op[NTile::slot(q, c, true)] = w1[c];                   // O[i][k].x
+            if (k > 0) op[NTile::slot(q - 1, c, false)] = w0[c];   // O[i][k-1].y
         }
     }
     for (int k = threadIdx.x; k < SWH; k += kThreads) {
@@ -564,8 +580,8 @@ __device__ __forceinline__ void stage_normals_ct(const TNI* __restrict__ pnb,
 #pragma unroll
         for (int d = 0; d < 3; ++d)
             t[d] = fmaf((float)clampi(x0 - R + 2 * k + d, 0, a.W - 1), a.ifu, a.tu_c);
-        T.tue[k] = make_float4(t[0], t[1], -t[0], -t[1]);
-        T.tuo[k] = make_float4(t[1], t[2], -t[1], -t[2]);
+        T.tune[k] = make_float2(-t[0], -t[1]);
+        T.tuno[k] = make_float2(-t[1], -t[2]);
     }
     for (int i = threadIdx.x; i < SH; i += kThreads)
         T.tv[i] = fmaf((float)clampi(y0 - R + i, 0, a.H - 1), a.ifv, a.tv_c);
@@ -577,22 +593,14 @@ struct NPair {
 };
 __device__ __forceinline__ NPair npair(const NTile& T, int i, int j) {
     const int k = i * T.swh + (j >> 1);
+    const float4 a = (j & 1) ? T.o01[k] : T.e01[k];
+    const float4 c = (j & 1) ? T.o23[k] : T.e23[k];
     NPair r;
-    if (j & 1) {
-        r.nx = T.o[0][k];
-        r.ny = T.o[1][k];
-        r.nz = T.o[2][k];
-        r.as = T.o[3][k];
-        const float4 t = T.tuo[j >> 1];
-        r.tun = f2(t.z, t.w);
-    } else {
-        r.nx = T.e[0][k];
-        r.ny = T.e[1][k];
-        r.nz = T.e[2][k];
-        r.as = T.e[3][k];
-        const float4 t = T.tue[j >> 1];
-        r.tun = f2(t.z, t.w);
-    }
+    r.nx = f2(a.x, a.y);
+    r.ny = f2(a.z, a.w);
+    r.nz = f2(c.x, c.y);
+    r.as = f2(c.z, c.w);
+    r.tun = (j & 1) ? T.tuno[j >> 1] : T.tune[j >> 1];
     r.tv = f2(T.tv[i]);
     return r;
 }
@@ -688,9 +696,18 @@ __device__ __forceinline__ void finish_pair(PairAcc<Mask>& A, int b, int x, int 
     if (!check_ok(y >= 0 && y < a.H && x >= 0 && x < a.W && (!two || x + 1 < a.W), kChkStore))
         return;
     if (vec) {
-        St<TNO>::st2(ob + p0, ox);
-        St<TNO>::st2(ob + HW + p0, oy);
-        St<TNO>::st2(ob + 2 * HW + p0, oz);
+        if constexpr (std::is_same<TNO, float>::value) {
+            // fp32 normals are the fused unit's intermediates (or its last
+            // iteration's output, which the upsample reads next): kept in L2
+            const uint64_t keep = l2_evict_last();
+            st2_hint(ob + p0, ox, keep);
+            st2_hint(ob + HW + p0, oy, keep);
+            st2_hint(ob + 2 * HW + p0, oz, keep);
+        } else {
+            St<TNO>::st2(ob + p0, ox);
+            St<TNO>::st2(ob + HW + p0, oy);
+            St<TNO>::st2(ob + 2 * HW + p0, oz);
+        }
     } else {
         St<TNO>::st(ob + p0, ox.x);
         St<TNO>::st(ob + HW + p0, oy.x);
@@ -759,7 +776,7 @@ angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* 
     auto ld = [&](const TS* base) -> float2 {
         return vec ? St<TS>::ld2s(base + p0) : f2(St<TS>::lds1(base + p0), St<TS>::lds1(base + p1));
     };
-    const float2 ifu2 = f2(a.ifu), ifv2 = f2(a.ifv);
+    const float2 ifu2 = a.ifu2, ifv2 = a.ifv2;
     PairAcc<Mask> A{f2(0.f), f2(0.f), f2(0.f), f2(0.f), 0, 0};
 #pragma unroll 1
     for (int ky = 0; ky < PS; ++ky) {
@@ -793,10 +810,11 @@ angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* 
 // chains interleave between barriers). With the window size, the dilation and
 // the window column compile-time constants, every shared-memory offset is an
 // immediate.
+// (evict-first in L2: every per-neighbour input is read exactly once)
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
     const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem),
-                 "r"(valid ? 16 : 0)
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;\n" ::"r"(s),
+                 "l"(gmem), "r"(valid ? 16 : 0), "l"(l2_evict_first())
                  : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
@@ -921,7 +939,7 @@ __device__ __forceinline__ void angmf_tile(const TNI* __restrict__ pn,
     const long p1 = two ? p0 + 1 : p0;
     float2 rx, ry, rz;
     pair_ray(ray, HW, p0, p1, rx, ry, rz);
-    const float2 ifu2 = f2(a.ifu), ifv2 = f2(a.ifv);
+    const float2 ifu2 = a.ifu2, ifv2 = a.ifv2;
     PairAcc<Mask> A{f2(0.f), f2(0.f), f2(0.f), f2(0.f), 0, 0};
     constexpr int kStrip = S::kRowsW * kTW;
     const TS* ring_lane = ring + (lane >> 4) * kTW + lx;   // this pair inside a slot
@@ -961,27 +979,16 @@ __device__ __forceinline__ void angmf_tile(const TNI* __restrict__ pn,
                 const int dj = kx * DIL;
                 int pi = prow + (dj >> 1);
                 if (!check_ok(pi >= 0 && pi < SH * SWH, kChkHaloSmem)) pi = 0;
-                float2 nx, ny, nz, as, tun;
-                if ((dj & 1) == 0) {
-                    nx = T.e[0][pi];
-                    ny = T.e[1][pi];
-                    nz = T.e[2][pi];
-                    as = T.e[3][pi];
-                    const float4 t4 = T.tue[(lx >> 1) + (dj >> 1)];
-                    tun = f2(t4.z, t4.w);
-                } else {
-                    nx = T.o[0][pi];
-                    ny = T.o[1][pi];
-                    nz = T.o[2][pi];
-                    as = T.o[3][pi];
-                    const float4 t4 = T.tuo[(lx >> 1) + (dj >> 1)];
-                    tun = f2(t4.z, t4.w);
-                }
+                const float4 n01 = (dj & 1) ? T.o01[pi] : T.e01[pi];
+                const float4 n23 = (dj & 1) ? T.o23[pi] : T.e23[pi];
+                const float2 tun = (dj & 1) ? T.tuno[(lx >> 1) + (dj >> 1)]
+                                            : T.tune[(lx >> 1) + (dj >> 1)];
                 float2 th = lds2<TS>(st + 3 * kStrip), wt = lds2<TS>(st);
                 if (ACT) head_activation(wt, th);
                 angmf_pair<Mask, sizeof(TS) == 4, ACT>(
-                    n, lds2<TS>(st + 1 * kStrip), lds2<TS>(st + 2 * kStrip), th, wt, nx, ny, nz,
-                    as, tun, tv, ifu2, ifv2, rx, ry, rz, A);
+                    n, lds2<TS>(st + 1 * kStrip), lds2<TS>(st + 2 * kStrip), th, wt,
+                    f2(n01.x, n01.y), f2(n01.z, n01.w), f2(n23.x, n23.y), f2(n23.z, n23.w), tun,
+                    tv, ifu2, ifv2, rx, ry, rz, A);
             }
         }
     }
@@ -1136,6 +1143,8 @@ AngmfArgs make_args(const LaunchT& L) {
     a.HW = (long)L.H * L.W;
     a.ifu = (float)(1.0 / L.fu);
     a.ifv = (float)(1.0 / L.fv);
+    a.ifu2 = make_float2(a.ifu, a.ifu);
+    a.ifv2 = make_float2(a.ifv, a.ifv);
     a.tu_c = (float)((0.5 - L.cu) / L.fu);
     a.tv_c = (float)((0.5 - L.cv) / L.fv);
     a.fu = L.fu;

@@ -116,6 +116,26 @@ __device__ __forceinline__ float rcp_ftz(float x) {
     return y;
 }
 __device__ __forceinline__ float2 rcp2_ftz(float2 a) { return make_float2(rcp_ftz(a.x), rcp_ftz(a.y)); }
+// L2 eviction priorities (PTX createpolicy, used as .L2::cache_hint operands):
+// streams read exactly once are marked evict-first so that they do not push
+// out of L2 the data that is read again soon (AngMF's intermediate normals,
+// marked evict-last when stored).
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t p;
+    asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_last() {
+    uint64_t p;
+    asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// Two floats to global memory (8-byte aligned) with an L2 policy.
+__device__ __forceinline__ void st2_hint(float* p, float2 v, uint64_t pol) {
+    asm volatile("st.global.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;" ::"l"(p), "f"(v.x),
+                 "f"(v.y), "l"(pol)
+                 : "memory");
+}
 
 // -------------------------------------------------------------- storage types
 template <typename T> struct St;
