@@ -24,7 +24,8 @@ EXPORTS = ("bvml_last_error", "bvml_abi_version", "bvml_ray_relu", "bvml_angmf_p
            "bvml_conv2d_nhwc_f16", "bvml_conv2d_nhwc_f16_ex", "bvml_stage_inputs",
            "bvml_head_tail_1x1", "bvml_refine_status", "bvml_probe_recorded",
            "bvml_refiner_weight_name", "bvml_refiner_weight_shape", "bvml_refiner_create",
-           "bvml_refiner_forward", "bvml_refiner_status", "bvml_refiner_destroy", "bvml_check_word")
+           "bvml_refiner_forward", "bvml_refiner_status", "bvml_refiner_destroy", "bvml_check_word",
+           "bvml_refine_halo_rows", "bvml_refiner_forward_banded")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(
@@ -112,6 +113,11 @@ lib.bvml_refiner_status.restype = _i
 lib.bvml_refiner_status.argtypes = [_vp, _vp]
 lib.bvml_refiner_destroy.restype = None
 lib.bvml_refiner_destroy.argtypes = [_vp]
+lib.bvml_refine_halo_rows.restype = _i
+lib.bvml_refine_halo_rows.argtypes = [_i, _i, _i]
+lib.bvml_refiner_forward_banded.restype = _i
+lib.bvml_refiner_forward_banded.argtypes = ([ctypes.POINTER(_vp), _i, _vp, _vp, _vp, _i, _i,
+                                             ctypes.POINTER(ctypes.c_float)] + [_i] * 9 + [_vp])
 
 
 def abi_version() -> int:

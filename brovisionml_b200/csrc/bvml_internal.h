@@ -12,6 +12,12 @@ namespace bvml {
 // Record `msg` as the calling thread's bvml_last_error() text; returns `code`.
 int report_error(int code, const std::string& msg);
 
+}  // namespace bvml
+struct bvml_refiner;
+namespace bvml {
+// The device a refiner handle (bvml_refiner_create) was created on.
+int refiner_device(const bvml_refiner* r);
+
 enum class SType { F32 = 0, F16 = 1 };
 
 struct AngmfLaunch {

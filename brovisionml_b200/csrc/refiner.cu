@@ -418,6 +418,12 @@ int bvml_refiner_create(const float* const* weights, int device, bvml_refiner** 
     return BVML_OK;
 }
 
+}  // extern "C"
+
+int bvml::refiner_device(const bvml_refiner* r) { return r->device; }
+
+extern "C" {
+
 void bvml_refiner_destroy(bvml_refiner* r) {
     if (!r) return;
     cudaSetDevice(r->device);

@@ -9,7 +9,8 @@
  *
  * Conventions
  *  - All pointers are DEVICE pointers of the current CUDA device, except the
- *    pointer ARRAYS of bvml_refine (host arrays of device pointers).
+ *    pointer ARRAYS of bvml_refine (host arrays of device pointers) and the
+ *    frame buffers of bvml_refiner_forward_banded (host memory).
  *  - Tensors are planar NCHW and contiguous: (B, C, H, W), W fastest. B frames
  *    of one camera share the intrinsics and the (3, H, W) fp32 ray map.
  *  - `dtype` selects the storage type of the big tensors: BVML_F32 (float) or
@@ -34,7 +35,7 @@
 extern "C" {
 #endif
 
-#define BVML_ABI_VERSION 7
+#define BVML_ABI_VERSION 8
 
 enum bvml_dtype { BVML_F32 = 0, BVML_F16 = 1 };
 
@@ -374,6 +375,36 @@ int bvml_refiner_forward(bvml_refiner* r, const float* normal, const float* feat
                          int out_w, int dtype, void* out, void* stream);
 int bvml_refiner_status(bvml_refiner* r, void* stream);
 void bvml_refiner_destroy(bvml_refiner* r);
+
+/*
+ * Large frames without the reference's resolution cap (src/dsine.cpp:117-141:
+ * downscale, refine, upsample back), for C / C++ hosts.
+ *
+ * bvml_refine_halo_rows: the grid rows of halo per side that make a row band
+ * of the whole learned refinement (`iters` iterations of the ConvGRU + heads,
+ * AngMF with a ps x ps window at dilation dil, then the upsample) equal the
+ * whole-frame result; -1 (BVML_EINVAL) for arguments outside iters 0..64,
+ * window 3/5/7, dilation 1..4. 22 for 5 iterations of 5x5 at dilation 1.
+ *
+ * bvml_refiner_forward_banded: the whole learned refinement of ONE frame from
+ * HOST memory as exact-halo row bands (bvml_refine_halo_rows(iters, 5, 1)
+ * rows of halo, clipped to the frame), dealt in turn over n_refiners handles
+ * -- one per GPU, or several on one -- each driven by its own host thread and
+ * stream. normal (3,h,w), feature and hidden (64,h,w): the decoder's fp32
+ * outputs in host memory; intrins, origH, origW, iters, the crop and dtype as
+ * for bvml_refiner_forward; out: HOST memory, (3, out_h, out_w) in dtype. Only
+ * the bands whose owned rows reach the crop run. Synchronous: returns when the
+ * frame is written. A failing band stops the others at their next band; the
+ * error names the band's grid rows and its device. The result equals
+ * bvml_refiner_forward on the whole frame up to the rounding of each band's
+ * shifted principal point (max-abs below 1e-6 in the tests).
+ */
+int bvml_refine_halo_rows(int iters, int ps, int dil);
+int bvml_refiner_forward_banded(bvml_refiner* const* refiners, int n_refiners,
+                                const float* normal, const float* feature, const float* hidden,
+                                int h, int w, const float* intrins, int origH, int origW,
+                                int iters, int n_bands, int crop_t, int crop_l, int out_h,
+                                int out_w, int dtype, void* out);
 
 /*
  * Profiling aid (no reference counterpart): arm `n` caller-created CUDA events

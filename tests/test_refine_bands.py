@@ -84,3 +84,48 @@ def test_banded_refinement_equals_whole_frame(iters, monkeypatch):
     pipeline.refine_frame_banded_full(normal, feat, hid, intr, H, W, short, n_bands=3,
                                       run_band=run, iters=iters)
     assert (short - whole).abs().max().item() > 0
+
+
+def test_c_halo_rows_match_the_python_formula():
+    """bvml_refine_halo_rows (the C entry a C++ host plans its bands with) is
+    the same formula, and rejects what the kernels do not take."""
+    from brovisionml_b200._capi import lib
+
+    for it in range(0, 9):
+        for ps in (3, 5, 7):
+            for dil in (1, 2, 3, 4):
+                assert lib.bvml_refine_halo_rows(it, ps, dil) == \
+                    sharding.refine_halo_rows(it, ps, dil), (it, ps, dil)
+    for bad in ((-1, 5, 1), (65, 5, 1), (5, 4, 1), (5, 5, 0), (5, 5, 5)):
+        assert lib.bvml_refine_halo_rows(*bad) == 1   # BVML_EINVAL
+        assert b"refine_halo_rows" in lib.bvml_last_error()
+
+
+def test_c_banded_forward_rejects_bad_arguments():
+    """Argument checks of bvml_refiner_forward_banded run before any CUDA call."""
+    import ctypes
+
+    from brovisionml_b200._capi import lib
+
+    handles = (ctypes.c_void_p * 1)(ctypes.c_void_p(1))   # never dereferenced here
+    fi = (ctypes.c_float * 4)(100.0, 100.0, 50.0, 40.0)
+    buf = (ctypes.c_float * 16)()
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    ok = dict(n=1, h=10, w=12, H=80, W=96, it=5, nb=2, ct=0, cl=0, oh=80, ow=96, dt=0)
+
+    def call(**kw):
+        a = dict(ok, **kw)
+        return lib.bvml_refiner_forward_banded(handles, a["n"], p, p, p, a["h"], a["w"], fi,
+                                               a["H"], a["W"], a["it"], a["nb"], a["ct"],
+                                               a["cl"], a["oh"], a["ow"], a["dt"], p)
+    assert call(n=0) == 1
+    assert call(h=0) == 1
+    assert call(it=0) == 1
+    assert call(nb=0) == 1
+    assert call(dt=7) == 1
+    assert call(oh=81) == 1 and b"crop window" in lib.bvml_last_error()
+    assert call(ct=1, oh=80) == 1
+    null = (ctypes.c_void_p * 1)(None)
+    assert lib.bvml_refiner_forward_banded(null, 1, p, p, p, 10, 12, fi, 80, 96, 5, 2, 0, 0, 80,
+                                           96, 0, p) == 1
+    assert b"null handle" in lib.bvml_last_error()
