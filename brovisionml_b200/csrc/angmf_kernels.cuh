@@ -649,11 +649,56 @@ __device__ __noinline__ double3 fixups(Mask m, int b, int x, int y, const TNI* _
     return make_double3(ax, ay, az);
 }
 
+// Where a tile's source normals come from. SrcFixed: one type and RayReLU
+// choice fixed at compile time (the one-tile kernels). SrcDual: chosen per
+// work item (the persistent kernel: iteration 0 stages the storage-typed
+// decoder normals with the initial RayReLU fused, later iterations the
+// previous iteration's fp32 normals), so that the kernel holds one copy of
+// the neighbour loop rather than one per variant: two copies in one body
+// raised its register spills and cost about 5 % per item.
+template <typename TNI, bool FUSE_RR>
+struct SrcFixed {
+    const TNI* pn;
+    template <int R, bool COH>
+    __device__ __forceinline__ void stage(int b, const float* ray, const NTile& T, int x0,
+                                          int y0, const AngmfArgs& a) const {
+        stage_normals_ct<R, TNI, FUSE_RR, COH>(pn + (long)b * 3 * a.HW, ray, T, x0, y0, a);
+    }
+    template <int PS, typename TS, bool ACT, bool COH, typename Mask>
+    __device__ __forceinline__ double3 fix(Mask m, int b, int x, int y, const TS* prob,
+                                           const TS* xy, const TS* ang, const float* ray,
+                                           const AngmfArgs& a) const {
+        return fixups<PS, TS, TNI, FUSE_RR, ACT, COH>(m, b, x, y, pn, prob, xy, ang, ray, a);
+    }
+};
+template <typename TS>
+struct SrcDual {
+    const TS* pn0;      // iteration 0: the decoder normals (storage type), RayReLU fused
+    const float* prev;  // later iterations: the previous iteration's fp32 normals
+    bool first;
+    template <int R, bool COH>
+    __device__ __forceinline__ void stage(int b, const float* ray, const NTile& T, int x0,
+                                          int y0, const AngmfArgs& a) const {
+        if (first)
+            stage_normals_ct<R, TS, true, COH>(pn0 + (long)b * 3 * a.HW, ray, T, x0, y0, a);
+        else
+            stage_normals_ct<R, float, false, COH>(prev + (long)b * 3 * a.HW, ray, T, x0, y0,
+                                                   a);
+    }
+    template <int PS, typename TSS, bool ACT, bool COH, typename Mask>
+    __device__ __forceinline__ double3 fix(Mask m, int b, int x, int y, const TSS* prob,
+                                           const TSS* xy, const TSS* ang, const float* ray,
+                                           const AngmfArgs& a) const {
+        if (first)
+            return fixups<PS, TSS, TS, true, ACT, COH>(m, b, x, y, pn0, prob, xy, ang, ray, a);
+        return fixups<PS, TSS, float, false, ACT, COH>(m, b, x, y, prev, prob, xy, ang, ray, a);
+    }
+};
+
 // Normalise the pair's sums (after fix-ups) and store.
-template <int PS, typename TS, typename TNI, typename TNO, bool FUSE_RR, bool ACT,
-          bool COH, typename Mask>
+template <int PS, typename TS, typename Src, typename TNO, bool ACT, bool COH, typename Mask>
 __device__ __forceinline__ void finish_pair(PairAcc<Mask>& A, int b, int x, int y, bool two,
-                                            bool vec, const TNI* pn, const TS* prob,
+                                            bool vec, const Src& src, const TS* prob,
                                             const TS* xy, const TS* ang, const float* ray,
                                             TNO* out, const AngmfArgs& a) {
     const float2 l = fma2(A.x, A.x, fma2(A.y, A.y, mul2(A.z, A.z)));
@@ -681,7 +726,7 @@ __device__ __forceinline__ void finish_pair(PairAcc<Mask>& A, int b, int x, int 
         }
         if (m == 0) return;
         const double3 f =
-            fixups<PS, TS, TNI, FUSE_RR, ACT, COH>(m, b, px, y, pn, prob, xy, ang, ray, a);
+            src.template fix<PS, TS, ACT, COH>(m, b, px, y, prob, xy, ang, ray, a);
         const double sx = (double)fx + f.x, sy = (double)fy + f.y, sz = (double)fz + f.z;
         const double sinv = 1.0 / fmax(sqrt(sx * sx + sy * sy + sz * sz), 1e-12);
         o0 = (float)(sx * sinv);
@@ -793,8 +838,8 @@ angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* 
         }
     }
     fold_ray(A, rx, ry, rz);
-    finish_pair<PS, TS, TNI, TNO, FUSE_RR, ACT, false>(A, b, x, y, two, vec, pn, prob, xy, ang, ray,
-                                                out, a);
+    finish_pair<PS, TS, SrcFixed<TNI, FUSE_RR>, TNO, ACT, false>(
+        A, b, x, y, two, vec, SrcFixed<TNI, FUSE_RR>{pn}, prob, xy, ang, ray, out, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -859,10 +904,9 @@ template <> __device__ __forceinline__ float2 lds2<__half>(const __half* p) {
 // the first ring slots are in flight and before the normal halo is staged
 // (the persistent kernel waits there for the tiles it depends on). COH: read
 // the normals with L2-coherent loads (they were written in the same launch).
-template <int PS, int DIL, typename TS, typename TNI, typename TNO, bool FUSE_RR, bool ACT,
-          bool COH, typename Pre>
-__device__ __forceinline__ void angmf_tile(const TNI* __restrict__ pn,
-                                           const TS* __restrict__ prob,
+template <int PS, int DIL, typename TS, typename Src, typename TNO, bool ACT, bool COH,
+          typename Pre>
+__device__ __forceinline__ void angmf_tile(const Src& nsrc, const TS* __restrict__ prob,
                                            const TS* __restrict__ xy, const TS* __restrict__ ang,
                                            const float* __restrict__ ray, TNO* __restrict__ out,
                                            const AngmfArgs& a, int b, int x0, int y0,
@@ -919,7 +963,7 @@ __device__ __forceinline__ void angmf_tile(const TNI* __restrict__ pn,
         cp_async_commit();
     }
     pre();
-    stage_normals_ct<R, TNI, FUSE_RR, COH>(pn + (long)b * 3 * HW, ray, T, x0, y0, a);
+    nsrc.template stage<R, COH>(b, ray, T, x0, y0, a);
     __syncthreads();  // the normal halo is shared by all warps
 
     const int lx = 2 * (lane & 15);
@@ -995,8 +1039,8 @@ __device__ __forceinline__ void angmf_tile(const TNI* __restrict__ pn,
     cp_async_wait<0>();
     if (!active) return;
     fold_ray(A, rx, ry, rz);
-    finish_pair<PS, TS, TNI, TNO, FUSE_RR, ACT, COH>(A, b, x, y, two, true, pn, prob, xy, ang,
-                                                     ray, out, a);
+    finish_pair<PS, TS, Src, TNO, ACT, COH>(A, b, x, y, two, true, nsrc, prob, xy, ang, ray,
+                                            out, a);
 }
 
 template <int PS, int DIL, typename TS, typename TNI, typename TNO, bool FUSE_RR, bool ACT>
@@ -1005,9 +1049,9 @@ angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
                     const TS* __restrict__ xy, const TS* __restrict__ ang,
                     const float* __restrict__ ray, TNO* __restrict__ out, const AngmfArgs a) {
     // grid (tiles_x, tiles_y, frames)
-    angmf_tile<PS, DIL, TS, TNI, TNO, FUSE_RR, ACT, false>(
-        pn, prob, xy, ang, ray, out, a, (int)blockIdx.z, (int)blockIdx.x * kTW,
-        (int)blockIdx.y * kTH, [] {});
+    angmf_tile<PS, DIL, TS, SrcFixed<TNI, FUSE_RR>, TNO, ACT, false>(
+        SrcFixed<TNI, FUSE_RR>{pn}, prob, xy, ang, ray, out, a, (int)blockIdx.z,
+        (int)blockIdx.x * kTW, (int)blockIdx.y * kTH, [] {});
 }
 
 // ---------------------------------------------------------------------------
@@ -1110,16 +1154,12 @@ angmf_iters_kernel(const float* __restrict__ ray, const AngmfArgs a, const Angmf
             __syncthreads();  // the neighbours' normals are visible to every thread
         };
         float* o = J.buf[it & 1];
-        if (it == 0)
-            angmf_tile<PS, DIL, TS, TS, float, true, ACT, true>(
-                static_cast<const TS*>(J.pn0), static_cast<const TS*>(J.prob[0]),
-                static_cast<const TS*>(J.xy[0]), static_cast<const TS*>(J.ang[0]), ray, o, a, b,
-                tx * kTW, ty * kTH, pre);
-        else
-            angmf_tile<PS, DIL, TS, float, float, false, ACT, true>(
-                J.buf[(it - 1) & 1], static_cast<const TS*>(J.prob[it]),
-                static_cast<const TS*>(J.xy[it]), static_cast<const TS*>(J.ang[it]), ray, o, a,
-                b, tx * kTW, ty * kTH, pre);
+        // one tile body for every iteration: iteration 0 stages the decoder
+        // normals with the initial RayReLU, later ones the previous fp32 result
+        const SrcDual<TS> src{static_cast<const TS*>(J.pn0), J.buf[(it - 1) & 1], it == 0};
+        angmf_tile<PS, DIL, TS, SrcDual<TS>, float, ACT, true>(
+            src, static_cast<const TS*>(J.prob[it]), static_cast<const TS*>(J.xy[it]),
+            static_cast<const TS*>(J.ang[it]), ray, o, a, b, tx * kTW, ty * kTH, pre);
         if (tid == kClaim) s_item[par ^ 1] = next;
         // every output of the tile stored (and the halo no longer read); the
         // release store is cumulative over the stores ordered before the barrier
