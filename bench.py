@@ -21,10 +21,9 @@ both cases, so no L2 flush is needed between steps.
 The JSON line carries, beyond the driver contract:
   roofline      the dominant kernel's algorithmic bytes per launch over its
                 average launch time (CUDA events recorded between the fused
-                unit's launches, on its stream, in a second pass of the same
-                steps right after the timed ones, so that the timed steps
-                carry no extra stream operations) against
-                MEASURED_PEAKS.json's HBM copy bandwidth;
+                unit's launches, on its stream, inside the timed steps
+                themselves, so the per-launch times add up to ms_per_step)
+                against MEASURED_PEAKS.json's HBM copy bandwidth;
   unit_roofline the same for the whole step (the fused refinement);
   weak          (N > 1) the same unit with 256 frames on EVERY rank;
   bands         config 3: one 4096^2 frame (grid 512^2, 7x7, fp32) as exact
