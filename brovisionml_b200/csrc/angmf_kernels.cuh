@@ -874,7 +874,11 @@ struct Stages {
     static constexpr int kChunksW = 4 * kRowsW * kCpr;     // per warp per slot
     static constexpr int kPerLane = kChunksW / 32;         // 1 (fp16) or 2 (fp32)
     static constexpr int kElemsW = 4 * kRowsW * kTW;       // per warp per slot
-    static constexpr int kM = (sizeof(TS) == 2 && PS < 7) ? 2 : 1;  // window rows per ring
+    // window rows per ring: one. Two rows for fp16 (10 slots, 8 ahead) were
+    // slower: the larger shared-memory carve-out left less L1 for the
+    // kernel's register spills (0.2591 against 0.2550 ms per config-4 launch,
+    // bit-identical)
+    static constexpr int kM = 1;
     static constexpr int kN = kM * PS;                     // ring depth
     static constexpr int kSP = sizeof(TS) == 2 ? 2 : 1;    // slots per warp barrier
     static constexpr int kD = kN - kSP;                    // slots issued ahead
