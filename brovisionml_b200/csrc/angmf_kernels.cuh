@@ -419,7 +419,12 @@ struct NTile {
     float* tv;
     int swh;      // pairs per plane row
 
-    static constexpr __host__ __device__ int pairs_per_row(int SW) { return SW / 2 + 1; }
+    // A pair starts at a column j <= SW - 2 (the last output pair, x = 30, at
+    // the window's far column, 2R), so SW / 2 pairs per row cover every read:
+    // E holds k <= SW/2 - 1, O (j odd, j <= SW - 3) k <= SW/2 - 2. Keeping the
+    // rows this short puts the fp16 5x5 CTA at 43.9 KB of shared memory, so
+    // three CTAs fit a 132 KB carve-out and leave more L1 for spills.
+    static constexpr __host__ __device__ int pairs_per_row(int SW) { return SW / 2; }
     static constexpr __host__ __device__ size_t bytes(int SW, int SH) {
         const int h = pairs_per_row(SW);
         return sizeof(float4) * 4 * (size_t)SH * h + sizeof(float2) * 2 * h + sizeof(float) * SH;
@@ -564,7 +569,7 @@ __device__ __forceinline__ void stage_normals_ct(const TNI* __restrict__ pnb,
         const float tu1 = fmaf((float)clampi(sx + 1, 0, a.W - 1), a.ifu, a.tu_c);
         const float w0[4] = {v0[0], v0[1], v0[2], fmaf(tu0, v0[0], fmaf(tv, v0[1], v0[2]))};
         const float w1[4] = {v1[0], v1[1], v1[2], fmaf(tu1, v1[0], fmaf(tv, v1[1], v1[2]))};
-        if (!check_ok(i < SH && k < SWH - 1, kChkHaloSmem)) continue;
+        if (!check_ok(i < SH && k < SWH, kChkHaloSmem)) continue;
         const int q = i * SWH + k;
         T.e01[q] = make_float4(w0[0], w1[0], w0[1], w1[1]);   // E[i][k] of nx, ny
         T.e23[q] = make_float4(w0[2], w1[2], w0[3], w1[3]);   // ... of nz, P.n
