@@ -58,6 +58,9 @@ struct UpRing {
     static constexpr size_t kWarpBytes = (size_t)kN * kBytes;
     static constexpr size_t kSmem = (kUThreads / 32) * (kWarpBytes + 8 * kN);
     static_assert(8 % kN == 0 && kN % kSP == 0, "slots must tile a sub-row");
+    // at least one group of stages in flight: with kN == kSP the prologue
+    // issues nothing and every wait targets a phase that was never started
+    static_assert(kN > kSP, "the ring must keep stages in flight");
     static_assert(kBytes % 128 == 0, "stage size keeps every slot 128-byte aligned");
 };
 
@@ -391,6 +394,19 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
                 }
             }
         }
+    }
+    if constexpr (TMA) {
+        // After a wait that gave up, the later waits were skipped: before the
+        // warp's shared memory can be reused, wait (bounded) for the last copy
+        // issued into each slot -- stage 64 - kN + s -- so that no copy lands
+        // after the CTA has exited. (Without a failure every copy was waited
+        // on already.)
+        if (failed && lane == 0) {
+#pragma unroll
+            for (int s = 0; s < U::kN; ++s)
+                tc::mbar_wait(bar0 + 8 * s, ((64 - U::kN + s) / U::kN) & 1, kUpWaitLimit);
+        }
+        __syncwarp();
     }
 }
 
