@@ -801,6 +801,8 @@ angmf_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob, const TS* 
              const AngmfArgs a) {
     constexpr int P = PS * PS;
     using Mask = typename std::conditional<(P <= 32), uint32_t, unsigned long long>::type;
+    pdl_trigger();
+    pdl_wait();  // (launched as a dependent: the previous iteration's normals)
     extern __shared__ float4 smem4[];
     NTile T;
     T.carve(smem4, kTW + 2 * a.R, kTH + 2 * a.R);
@@ -1057,10 +1059,15 @@ __global__ void __launch_bounds__(kThreads, (StagedCfg<PS, DIL, TS>::kMinBlocks)
 angmf_staged_kernel(const TNI* __restrict__ pn, const TS* __restrict__ prob,
                     const TS* __restrict__ xy, const TS* __restrict__ ang,
                     const float* __restrict__ ray, TNO* __restrict__ out, const AngmfArgs a) {
+    // The next iteration's launch may start its CTAs (ring prologue: its own
+    // per-neighbour inputs, written before this launch began) during this
+    // launch's last wave; a CTA launched that way waits before it stages the
+    // normals this launch writes.
+    pdl_trigger();
     // grid (tiles_x, tiles_y, frames)
     angmf_tile<PS, DIL, TS, SrcFixed<TNI, FUSE_RR>, TNO, ACT, false>(
         SrcFixed<TNI, FUSE_RR>{pn}, prob, xy, ang, ray, out, a, (int)blockIdx.z,
-        (int)blockIdx.x * kTW, (int)blockIdx.y * kTH, [] {});
+        (int)blockIdx.x * kTW, (int)blockIdx.y * kTH, [] { pdl_wait(); });
 }
 
 // ---------------------------------------------------------------------------
@@ -1123,6 +1130,7 @@ angmf_iters_kernel(const float* __restrict__ ray, const AngmfArgs a, const Angmf
     // only at the end), warp 1 polls the dependencies, warp 7 publishes the
     // completion.
     constexpr int kClaim = 64, kPoll = 32, kSignal = kThreads - 32;
+    pdl_trigger();  // the upsample's CTAs may take the slots of exiting CTAs
     __shared__ int s_item[2];
     const int tid = threadIdx.x;
     const int per_it = a.tiles_x * a.tiles_y * a.B;
@@ -1300,13 +1308,13 @@ cudaError_t launch_t(const AngmfLaunch& L, cudaStream_t s) {
             const long nb = L.B - b0 < kMaxZ ? L.B - b0 : kMaxZ;
             a.B = (int)nb;
             const dim3 grid((unsigned)a.tiles_x, (unsigned)a.tiles_y, (unsigned)nb);
-            kern<<<grid, kThreads, smem, s>>>(
-                static_cast<const TNI*>(L.pn) + b0 * 3 * a.HW,
-                static_cast<const TS*>(L.prob) + b0 * P * a.HW,
-                static_cast<const TS*>(L.xy) + b0 * 2 * P * a.HW,
-                static_cast<const TS*>(L.angle) + b0 * P * a.HW, L.ray,
-                static_cast<TNO*>(L.out) + b0 * 3 * a.HW, a);
-            e = cudaGetLastError();
+            e = launch_pdl(kern, grid, dim3(kThreads), smem, s, L.pdl && b0 == 0,
+                           static_cast<const TNI*>(L.pn) + b0 * 3 * a.HW,
+                           static_cast<const TS*>(L.prob) + b0 * P * a.HW,
+                           static_cast<const TS*>(L.xy) + b0 * 2 * P * a.HW,
+                           static_cast<const TS*>(L.angle) + b0 * P * a.HW, L.ray,
+                           static_cast<TNO*>(L.out) + b0 * 3 * a.HW, a);
+            if (e == cudaSuccess) e = cudaGetLastError();
             if (e != cudaSuccess) return e;
         }
         return cudaSuccess;
@@ -1317,11 +1325,11 @@ cudaError_t launch_t(const AngmfLaunch& L, cudaStream_t s) {
                                              (int)nsmem);
         if (e != cudaSuccess) return e;
     }
-    kern<<<(unsigned)blocks, kThreads, nsmem, s>>>(
-        static_cast<const TNI*>(L.pn), static_cast<const TS*>(L.prob),
-        static_cast<const TS*>(L.xy), static_cast<const TS*>(L.angle), L.ray,
-        static_cast<TNO*>(L.out), a);
-    return cudaGetLastError();
+    cudaError_t e = launch_pdl(kern, dim3((unsigned)blocks), dim3(kThreads), nsmem, s, L.pdl,
+                               static_cast<const TNI*>(L.pn), static_cast<const TS*>(L.prob),
+                               static_cast<const TS*>(L.xy), static_cast<const TS*>(L.angle),
+                               L.ray, static_cast<TNO*>(L.out), a);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <int PS, typename TS, bool ACT>

@@ -116,6 +116,19 @@ __device__ __forceinline__ float rcp_ftz(float x) {
     return y;
 }
 __device__ __forceinline__ float2 rcp2_ftz(float2 a) { return make_float2(rcp_ftz(a.x), rcp_ftz(a.y)); }
+// Programmatic dependent launch. A kernel launched with the programmatic
+// stream serialization attribute (launch_pdl) may be scheduled while the
+// previous kernel in its stream is still running: only once every CTA of
+// that kernel has started and executed pdl_trigger() (or exited), so a
+// waiting CTA never holds resources the previous kernel still needs.
+// pdl_wait() blocks until the previous kernel has completed and its memory
+// is visible; before it, a kernel may only read what was written before the
+// previous kernel started. Both are no-ops for a normally launched kernel.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // L2 eviction priorities (PTX createpolicy, used as .L2::cache_hint operands):
 // streams read exactly once are marked evict-first so that they do not push
 // out of L2 the data that is read again soon (AngMF's intermediate normals,
@@ -187,5 +200,24 @@ __device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? l
 
 // RayReLU eps: the CPU twin's float constant 1e-2f (src/dsine_ops.cpp:27).
 constexpr float kRayEps = 1e-2f;
+
+// Launch `kern` on `s`, as a programmatic dependent of the previous kernel in
+// the stream when `pdl` (the kernel then calls pdl_wait() before it reads
+// that kernel's results).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, bool pdl, Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl ? at : nullptr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
 
 }  // namespace bvml

@@ -32,6 +32,8 @@ struct AngmfLaunch {
     bool act;            // prob / angle are raw head outputs: activate them on load
     int B, H, W, ps, dil;
     double fu, cu, fv, cv;
+    bool pdl;            // launch as a programmatic dependent of the previous kernel
+                         // (which must not write prob / xy / angle)
 };
 cudaError_t launch_angmf(const AngmfLaunch& L, cudaStream_t s);
 cudaError_t launch_angmf_logits(const AngmfLaunch& L, cudaStream_t s);  // L.act variants
@@ -74,6 +76,8 @@ struct UpsampleLaunch {
     int crop_t, crop_l, out_h, out_w;
     double fu, cu, fv, cv;  // GRID intrinsics; the full-res ray uses 8x these
     int* status;         // optional: bit 2 set if a staging wait gave up
+    bool pdl;            // launch as a programmatic dependent of the previous kernel
+                         // (which must not write the mask)
 };
 cudaError_t launch_upsample(const UpsampleLaunch& L, cudaStream_t s);
 

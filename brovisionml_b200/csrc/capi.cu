@@ -247,6 +247,9 @@ int refine_entry(bool act, const void* normal0, const float* ray8, const void* c
             L.out_t = bvml::SType::F32;
             L.fuse_ray_relu = it == 0;
             L.act = act;
+            // iterations after the first overlap the previous one's tail: their
+            // per-neighbour inputs were written before the unit started
+            L.pdl = it > 0;
             L.B = B;
             L.H = h;
             L.W = w;
@@ -286,6 +289,7 @@ int refine_entry(bool act, const void* normal0, const float* ray8, const void* c
     U.fv = fv;
     U.cv = cv;
     U.status = sync + 1;
+    U.pdl = true;  // its mask was written before the unit started
     cudaError_t e = bvml::launch_upsample(U, s);
     if (e != cudaSuccess) return finish(e, "refine: upsample launch");
     if ((e = probe(launch_no++, s)) != cudaSuccess)

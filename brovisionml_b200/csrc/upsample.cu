@@ -304,6 +304,9 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
     const int xc = vec ? min(x, a.w - 2) : min(x, a.w - 1);
     const int x1 = min(xc + 1, a.w - 1);
 
+    // (launched as a dependent of the last AngMF launch: its mask stages are
+    // in flight above; the normals are that launch's output)
+    pdl_wait();
     // 3x3 replicate-padded neighbourhood of the pair, per channel
     const TNI* nb = nrm + (long)b * 3 * hw;
     float2 N[9][3];
@@ -431,16 +434,17 @@ cudaError_t launch_t(const UpsampleLaunch& L, const UpArgs& a, cudaStream_t s) {
             cudaError_t e =
                 cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             if (e != cudaSuccess) return e;
-            kern<<<(unsigned)blocks, kUThreads, smem, s>>>(static_cast<const TNI*>(L.n),
-                                                          static_cast<const TS*>(L.mask),
-                                                          static_cast<TS*>(L.out), a, m);
-            return cudaGetLastError();
+            e = launch_pdl(kern, dim3((unsigned)blocks), dim3(kUThreads), smem, s, L.pdl,
+                           static_cast<const TNI*>(L.n), static_cast<const TS*>(L.mask),
+                           static_cast<TS*>(L.out), a, m);
+            return e != cudaSuccess ? e : cudaGetLastError();
         }
     }
-    upsample_kernel<TNI, TS, NORM, RR, false><<<(unsigned)blocks, kUThreads, 0, s>>>(
-        static_cast<const TNI*>(L.n), static_cast<const TS*>(L.mask), static_cast<TS*>(L.out), a,
-        m);
-    return cudaGetLastError();
+    cudaError_t e = launch_pdl(upsample_kernel<TNI, TS, NORM, RR, false>,
+                               dim3((unsigned)blocks), dim3(kUThreads), 0, s, L.pdl,
+                               static_cast<const TNI*>(L.n), static_cast<const TS*>(L.mask),
+                               static_cast<TS*>(L.out), a, m);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <typename TNI, typename TS>
