@@ -29,6 +29,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <exception>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -230,7 +231,18 @@ int bvml_refiner_forward_banded(bvml_refiner* const* refiners, int n_refiners,
     if (cudaGetDevice(&caller_dev) != cudaSuccess) caller_dev = -1;
     const int nw = std::min<int>(n_refiners, (int)plan.size());
     std::vector<std::thread> threads;
-    for (int d = 1; d < nw; ++d) threads.emplace_back(work, d);
+    try {
+        for (int d = 1; d < nw; ++d) threads.emplace_back(work, d);
+    } catch (const std::exception& ex) {  // no exception crosses the C ABI
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            if (first.code == BVML_OK) {
+                first.code = BVML_EUNSUPPORTED;
+                first.msg = std::string("host thread: ") + ex.what();
+            }
+            stop = true;
+        }
+    }
     if (nw > 0) work(0);
     for (auto& t : threads) t.join();
     if (caller_dev >= 0) cudaSetDevice(caller_dev);  // work(0) ran on this thread
