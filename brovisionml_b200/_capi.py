@@ -25,7 +25,7 @@ EXPORTS = ("bvml_last_error", "bvml_abi_version", "bvml_ray_relu", "bvml_angmf_p
            "bvml_head_tail_1x1", "bvml_refine_status", "bvml_probe_recorded",
            "bvml_refiner_weight_name", "bvml_refiner_weight_shape", "bvml_refiner_create",
            "bvml_refiner_forward", "bvml_refiner_status", "bvml_refiner_destroy", "bvml_check_word",
-           "bvml_refine_halo_rows", "bvml_refiner_forward_banded")
+           "bvml_refine_halo_rows", "bvml_refiner_forward_banded", "bvml_upsample_wait_limit")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(
@@ -113,6 +113,8 @@ lib.bvml_refiner_status.restype = _i
 lib.bvml_refiner_status.argtypes = [_vp, _vp]
 lib.bvml_refiner_destroy.restype = None
 lib.bvml_refiner_destroy.argtypes = [_vp]
+lib.bvml_upsample_wait_limit.restype = ctypes.c_uint
+lib.bvml_upsample_wait_limit.argtypes = [ctypes.c_uint]
 lib.bvml_refine_halo_rows.restype = _i
 lib.bvml_refine_halo_rows.argtypes = [_i, _i, _i]
 lib.bvml_refiner_forward_banded.restype = _i

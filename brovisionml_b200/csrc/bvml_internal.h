@@ -80,6 +80,9 @@ struct UpsampleLaunch {
                          // (which must not write the mask)
 };
 cudaError_t launch_upsample(const UpsampleLaunch& L, cudaStream_t s);
+// Attempts the upsample makes at each TMA staging wait, for launches that
+// follow (0: every wait gives up at once); returns the previous value.
+uint32_t set_upsample_wait_limit(uint32_t limit);
 
 enum class ConvEpi : int {
     NHWC = 0, PLANAR16 = 1, PLANAR32 = 2, GRU_ZR = 3, GRU_Q = 4, C4_32 = 5, SPLIT16 = 6

@@ -599,11 +599,20 @@ int bvml_refine_status(const void* workspace, void* stream) {
                                     cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_fail(e, "refine_status: copy");
-    if (st != 0)
-        return fail(BVML_ECUDA, "dsine cuda: refine: a persistent AngMF dependency wait gave up "
-                                "(status " + std::to_string(st) + "); results unspecified");
+    if (st != 0) {
+        std::string what;
+        if (st & 1) what += "a persistent AngMF dependency wait";
+        if (st & 2) what += std::string(what.empty() ? "" : " and ") + "an upsample staging wait";
+        if (what.empty()) what = "a device-side wait";
+        return fail(BVML_ECUDA, "dsine cuda: refine: " + what + " gave up (status " +
+                                    std::to_string(st) + "); results unspecified");
+    }
     g_last_error.clear();
     return BVML_OK;
+}
+
+unsigned bvml_upsample_wait_limit(unsigned limit) {
+    return bvml::set_upsample_wait_limit(limit);
 }
 
 int bvml_probe_recorded(void) { return g_probe_recorded; }

@@ -40,6 +40,8 @@
 #include "bvml_internal.h"
 #include "tc_common.cuh"
 
+#include <atomic>
+
 namespace bvml {
 namespace {
 
@@ -47,6 +49,8 @@ constexpr int kUTW = 64;        // grid columns per tile (32 pairs = one warp)
 constexpr int kUTH = 8;         // grid rows per tile (one per warp)
 constexpr int kUThreads = 256;
 constexpr uint32_t kUpWaitLimit = 1u << 22;
+// Attempts per staging wait for launches that follow (bvml_upsample_wait_limit).
+std::atomic<uint32_t> g_up_wait_limit{kUpWaitLimit};
 
 // The TMA ring of one warp: kN stages of 9 x 64 logits.
 template <typename TS>
@@ -93,6 +97,8 @@ struct UpArgs {
     bool vec_out;                   // 16-byte aligned output runs
     float ifu8, ifv8, tu8_c, tv8_c; // full-res ray: ((X+0.5)-8cu)/(8fu) = X*ifu8 + tu8_c
     int* status;                    // nonzero after a staging wait gave up (may be null)
+    uint32_t wait_limit;            // attempts per staging wait; 0: give up at once
+                                    // (failure injection, bvml_upsample_wait_limit)
 };
 
 // Packs two fp32 results into one 32-bit storage word for TS = half; for
@@ -300,6 +306,7 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
         }
         __syncwarp();
     }
+    int issued_hi = U::kN - U::kSP - 1;  // last stage issued (lane 0 issues)
     const bool vec = (a.w & 1) == 0;   // pairs start at even offsets: 8/4-byte aligned
     const int xc = vec ? min(x, a.w - 2) : min(x, a.w - 1);
     const int x1 = min(xc + 1, a.w - 1);
@@ -342,19 +349,25 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
                 for (int e = 0; e < U::kSP; ++e) {
                     const int s = (kg * U::kSP + e) % U::kN;
                     const uint32_t parity = ((k + e) / U::kN) & 1;
-                    if (!failed && !tc::mbar_wait(bar0 + 8 * s, parity, kUpWaitLimit)) {
+                    if (!failed && !(a.wait_limit != 0 &&
+                                     tc::mbar_wait_pipe(bar0 + 8 * s, parity, a.wait_limit))) {
                         failed = true;
                         if (lane == 0 && a.status) atomicOr(a.status, 2);
                     }
                 }
                 __syncwarp();  // every lane done with the previous group's slots
-                if (lane == 0) {
+                if (lane == 0 && !failed) {
                     // the previous group's slots get the stages kN - kSP ahead
                     // (every lane's loads from them were consumed by the
-                    // previous group's arithmetic, so they have completed)
+                    // previous group's arithmetic, so they have completed).
+                    // After a wait gave up nothing more is issued: a slot
+                    // whose copy may still be in flight is never refilled.
 #pragma unroll
                     for (int e = 0; e < U::kSP; ++e)
-                        if (k + e + U::kN - U::kSP < 64) issue(k + e + U::kN - U::kSP);
+                        if (k + e + U::kN - U::kSP < 64) {
+                            issue(k + e + U::kN - U::kSP);
+                            issued_hi = k + e + U::kN - U::kSP;
+                        }
                 }
 #pragma unroll
                 for (int e = 0; e < U::kSP; ++e) {
@@ -399,15 +412,19 @@ upsample_kernel(const TNI* __restrict__ nrm, const TS* __restrict__ mask, TS* __
         }
     }
     if constexpr (TMA) {
-        // After a wait that gave up, the later waits were skipped: before the
-        // warp's shared memory can be reused, wait (bounded) for the last copy
-        // issued into each slot -- stage 64 - kN + s -- so that no copy lands
-        // after the CTA has exited. (Without a failure every copy was waited
-        // on already.)
+        // After a wait that gave up, the later waits were skipped and nothing
+        // more was issued: before the warp's shared memory can be reused,
+        // wait (bounded) for the last copy issued into each slot -- the
+        // largest stage j <= issued_hi with j = s mod kN, one copy per slot at
+        // most in flight -- so that no copy lands after the CTA has exited.
+        // (Without a failure every copy was waited on already.)
         if (failed && lane == 0) {
 #pragma unroll
             for (int s = 0; s < U::kN; ++s)
-                tc::mbar_wait(bar0 + 8 * s, ((64 - U::kN + s) / U::kN) & 1, kUpWaitLimit);
+                if (issued_hi >= s) {
+                    const int j = issued_hi - (issued_hi - s) % U::kN;
+                    tc::mbar_wait(bar0 + 8 * s, (j / U::kN) & 1, kUpWaitLimit);
+                }
         }
         __syncwarp();
     }
@@ -457,6 +474,8 @@ cudaError_t launch_flags(const UpsampleLaunch& L, const UpArgs& a, cudaStream_t 
 
 }  // namespace
 
+uint32_t set_upsample_wait_limit(uint32_t limit) { return g_up_wait_limit.exchange(limit); }
+
 cudaError_t launch_upsample(const UpsampleLaunch& L, cudaStream_t s) {
     if (L.B == 0 || L.h == 0 || L.w == 0 || L.out_h == 0 || L.out_w == 0) return cudaSuccess;
     UpArgs a;
@@ -479,6 +498,7 @@ cudaError_t launch_upsample(const UpsampleLaunch& L, cudaStream_t s) {
     a.tu8_c = (float)((0.5 - 8.0 * L.cu) / (8.0 * L.fu));
     a.tv8_c = (float)((0.5 - 8.0 * L.cv) / (8.0 * L.fv));
     a.status = L.status;
+    a.wait_limit = g_up_wait_limit.load(std::memory_order_relaxed);
     if (L.st == SType::F32) {
         if (L.n_t != SType::F32) return cudaErrorInvalidValue;
         return launch_flags<float, float>(L, a, s);

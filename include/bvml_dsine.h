@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define BVML_ABI_VERSION 8
+#define BVML_ABI_VERSION 9
 
 enum bvml_dtype { BVML_F32 = 0, BVML_F16 = 1 };
 
@@ -133,12 +133,28 @@ size_t bvml_refine_workspace_bytes(int B, int h, int w);
  * Status of the last bvml_refine / bvml_refine_logits call that used
  * `workspace` (no reference counterpart: the reference's per-iteration
  * launches have no device-side waits). The persistent AngMF launch lets a
- * tile wait for its neighbour tiles of the previous iteration; every such
- * wait is bounded, and one that gives up (the GPU stopped making progress)
- * records it in the workspace instead of hanging. Synchronises `stream`;
- * returns BVML_OK, or BVML_ECUDA with the reason in bvml_last_error().
+ * tile wait for its neighbour tiles of the previous iteration, and the
+ * upsample waits for its TMA-staged mask logits; every such wait is bounded,
+ * and one that gives up (the GPU stopped making progress) records it in the
+ * workspace (bit 1: an AngMF dependency wait, bit 2: an upsample staging
+ * wait) instead of hanging. Synchronises `stream`; returns BVML_OK, or
+ * BVML_ECUDA with the reason in bvml_last_error().
  */
 int bvml_refine_status(const void* workspace, void* stream);
+
+/*
+ * Failure injection for tests (no counterpart in the reference): how many
+ * attempts the fused upsample makes at each of its TMA staging waits, for the
+ * launches that follow, process-wide; returns the previous value. The default
+ * is BVML_UPSAMPLE_WAIT_DEFAULT; 0 makes every staging wait give up at once,
+ * as if a copy were stuck. A wait that gives up sets bit 2 of the unit's
+ * status word (bvml_refine_status reports it), stops the warp's staging,
+ * waits (bounded) for the copies the warp already issued and leaves that
+ * call's output unspecified; the GPU context stays usable and later calls
+ * with the default are normal.
+ */
+#define BVML_UPSAMPLE_WAIT_DEFAULT 4194304u
+unsigned bvml_upsample_wait_limit(unsigned limit);
 
 /*
  * The whole refine-ops unit of Refiner::forward (src/dsine_refine.cpp:241-292)

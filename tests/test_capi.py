@@ -23,7 +23,7 @@ def test_header_symbols_exported():
     from brovisionml_b200 import _capi
 
     syms = declared_symbols()
-    assert len(syms) == 28, syms
+    assert len(syms) == 29, syms
     assert sorted(_capi.EXPORTS) == syms
     for s in syms:
         assert hasattr(b.lib, s), s
@@ -31,7 +31,7 @@ def test_header_symbols_exported():
                          text=True, check=True).stdout
     exported = set(re.findall(r" T (bvml_\w+)", out))
     assert exported == set(syms)
-    assert b.abi_version() == 8
+    assert b.abi_version() == 9
 
 
 def test_bridge_library_exports_reference_signatures():
